@@ -1,0 +1,427 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 per-layer elementwise hot path.
+
+Workload (one "step"): Llama-3.1-8B prefill-shaped elementwise chain in BF16 —
+16 sequences x 2048 tokens (32768 tokens, positions 0..2047 per sequence),
+hidden 4096, 32/8 heads of 128, intermediate 14336, vocab 128256, 32 layers:
+embedding gather, then per layer fused residual-add+RMSNorm, RoPE on Q and K
+(llama3 scaling: factor 8, low/high freq 1/4, original context 8192), fused
+residual-add+RMSNorm, SwiGLU silu*mul; a final fused add+norm. Activations are
+synthetic N(0,1) with 0.1% of the channels scaled x20; the GEMM outputs that
+feed the chain (o_proj, down_proj, q/k, gate/up) are synthetic tensors of their
+real shapes. Every tensor the chain streams is larger than L2, so no L2 flush
+is needed between steps.
+
+Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): each rank runs
+its own 16 x 2048-token batch (weak scaling, sequences are independent: no
+data-path collective); value = all ranks' tokens / max-over-ranks time.
+
+``--impl reference`` times the reference's CPU numerical path (the PyTorch
+math of its validation scripts, ``oracle/cpu_chain.py``) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "fused-op tokens/s and achieved HBM GB/s (% of peak) at 1/2/4/8 B200"
+T_SEQ, N_SEQ = 2048, 16
+HID, NQ, NKV, HD, INTER, LAYERS, VOCAB = 4096, 32, 8, 128, 14336, 32, 128256
+ROPE = dict(theta=500000.0, factor=8.0, low=1.0, high=4.0, orig=8192)
+EPS = 1e-5
+WORKLOAD = "config3: Llama-3.1-8B prefill-shaped elementwise chain (embedding + 32 x [add+rmsnorm, rope q/k, add+rmsnorm, silu*mul] + final add+norm)"
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ── clocks sampler ───────────────────────────────────────────────────────────
+
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.dev)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ── our arm ──────────────────────────────────────────────────────────────────
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from fracture_b200 import kernels as K
+    from fracture_b200.backend import FB_BF16, CudaBackend
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    T = T_SEQ * N_SEQ
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+    def act(shape):
+        x = torch.randn(shape, generator=g, device=dev)
+        cols = torch.rand(shape[-1], generator=g, device=dev) < 0.001  # outlier channels x20
+        return torch.where(cols, x * 20.0, x).to(bf)
+
+    table = (torch.randn((VOCAB, HID), generator=g, device=dev) * 0.02).to(bf)
+    ids = torch.randint(0, VOCAB, (T,), generator=g, device=dev, dtype=torch.int32)
+    positions = (torch.arange(T, device=dev, dtype=torch.int32) % T_SEQ).contiguous()
+    h = torch.empty((T, HID), device=dev, dtype=bf)
+    normed = torch.empty_like(h)
+    attn_proj, ffn_out = act((T, HID)), act((T, HID))
+    q, k = act((T, NQ, HD)), act((T, NKV, HD))
+    gate, up = act((T, INTER)), act((T, INTER))
+    mid = torch.empty_like(gate)
+    wa = (1 + 0.02 * torch.randn((LAYERS, HID), generator=g, device=dev)).to(bf)
+    wf = (1 + 0.02 * torch.randn((LAYERS + 1, HID), generator=g, device=dev)).to(bf)
+    freqs = torch.from_numpy(K.rope_freqs_llama3(HD, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"],
+                                                 ROPE["orig"])).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    s = stream.cuda_stream
+
+    # algorithmic bytes (each input read once, each output written once; weight rows once per launch)
+    B = 2
+    by_embed = T * HID * B * 2 + T * 4
+    by_norm = T * HID * B * 2 + HID * B
+    by_addnorm = T * HID * B * 4 + HID * B
+    by_rope = T * (NQ + NKV) * HD * B * 2 + T * 4 + HD // 2 * 4
+    by_silu = T * INTER * B * 3
+    step_bytes = by_embed + by_norm + (2 * LAYERS - 1) * by_addnorm + LAYERS * by_rope + LAYERS * by_silu + by_addnorm
+    launches_per_step = 1 + 1 + (2 * LAYERS - 1) + LAYERS + LAYERS + 1
+
+    silu_events = []
+
+    def step(record_silu: bool):
+        K.embedding(h, table, ids, stream=s)
+        for l in range(LAYERS):
+            if l == 0:
+                K.rmsnorm(normed, h, wa[0], EPS, stream=s)
+            else:
+                K.add_rmsnorm(h, ffn_out, wa[l], normed, EPS, stream=s)
+            K.rope(q, k, positions, freqs, stream=s)
+            K.add_rmsnorm(h, attn_proj, wf[l], normed, EPS, stream=s)
+            if record_silu:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                K.silu_mul(mid, gate, up, stream=s)
+                e1.record(stream)
+                silu_events.append((e0, e1))
+            else:
+                K.silu_mul(mid, gate, up, stream=s)
+        K.add_rmsnorm(h, ffn_out, wf[LAYERS], normed, EPS, stream=s)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    clocks = Clocks(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(True)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    clock = clocks.stop()
+    barrier()
+    torch.cuda.synchronize(dev)
+    elapsed_ms = t0.elapsed_time(t1)
+    silu_ms = [a.elapsed_time(b) for a, b in silu_events]
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+
+    # ── e2e through the reference-facing backend API (host buffers) ──
+    be = CudaBackend(local_rank)
+    be.precompute_rope_freqs_llama3(HD, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"], ROPE["orig"])
+    reg = lambda t_, shape: be.register_external(t_.data_ptr(), shape, FB_BF16)
+    Th, Tn, Ta, Tf = reg(h, (T, HID)), reg(normed, (T, HID)), reg(attn_proj, (T, HID)), reg(ffn_out, (T, HID))
+    Tq, Tk = reg(q, (T, NQ, HD)), reg(k, (T, NKV, HD))
+    Tg, Tu, Tm = reg(gate, (T, INTER)), reg(up, (T, INTER)), reg(mid, (T, INTER))
+    Ttab = reg(table, (VOCAB, HID))
+    Twa = [reg(wa[l], (HID,)) for l in range(LAYERS)]
+    Twf = [reg(wf[l], (HID,)) for l in range(LAYERS + 1)]
+    last = be.alloc((N_SEQ, HID), FB_BF16)
+    host_ids = np.random.default_rng(rank).integers(0, VOCAB, T).astype(np.uint32)
+    pos_sets = [np.tile(np.arange(T_SEQ, dtype=np.uint32), N_SEQ), np.tile(np.arange(1, T_SEQ + 1, dtype=np.uint32), N_SEQ)]
+    out_host = np.empty(N_SEQ * HID * 2, dtype=np.uint8)
+
+    def e2e_step(i):
+        pos = pos_sets[i % 2]  # a new forward: positions change, uploaded once, reused by all 32 layers
+        be.embedding(host_ids, Ttab, Th)
+        for l in range(LAYERS):
+            if l > 0:
+                be.add(Th, Tf, Th)
+            be.rmsnorm(Th, Twa[l], EPS, Tn)
+            be.rope(Tq, Tk, pos, ROPE["theta"], HD)
+            be.add(Th, Ta, Th)
+            be.rmsnorm(Th, Twf[l], EPS, Tn)
+            be.silu_mul(Tg, Tu, Tm)
+        be.add(Th, Tf, Th)
+        be.rmsnorm(Th, Twf[LAYERS], EPS, Tn)
+        for sq in range(N_SEQ):
+            be.copy_rows(Tn, last, sq * T_SEQ + T_SEQ - 1, sq, 1)
+        be.copy_to_host(last, out_host)  # synchronous: the step's result is on the host
+
+    e2e_steps = 0 if args.no_e2e else max(3, min(args.steps, 10))
+    for i in range(0 if args.no_e2e else max(2, args.warmup)):
+        e2e_step(i)
+    barrier()
+    torch.cuda.synchronize(dev)
+    w0 = time.perf_counter()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e2e_s = time.perf_counter() - w0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    be.close()
+
+    if rank != 0:
+        return None
+    pk = peaks()
+    ms_step = elapsed_ms / args.steps
+    value = world * T / (ms_step / 1e3)
+    silu_avg = statistics.mean(silu_ms)
+    achieved = by_silu / (silu_avg / 1e3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("silu_mul_bf16_32768x14336")
+    res = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, 0.1% channels x20; random-init norm weights and embedding table)",
+        "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "sequences_per_gpu": N_SEQ, "seq_len": T_SEQ,
+                   "hidden": HID, "heads": f"{NQ}/{NKV}x{HD}", "intermediate": INTER, "layers": LAYERS,
+                   "vocab": VOCAB, "rope": "llama3 factor 8, low 1, high 4, original 8192, theta 5e5",
+                   "parallelism": f"dp{world} (sequence-sharded replicas, no collective on the data path)",
+                   "l2": "every streamed tensor > 126 MB L2 (no flush needed)"},
+        "hbm": {"algorithmic_bytes_per_step": step_bytes,
+                "achieved_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1),
+                "frac_of_peak": round(step_bytes / (ms_step / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+                "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"]},
+        "roofline": {"kernel": "silu_mul_vec_kernel<bf16> (50% of the step's bytes)", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
+                     "algorithmic_bytes_per_launch": by_silu, "avg_launch_ms": round(silu_avg, 5),
+                     "peak_source": pk["source"]},
+        "e2e": {"value": round(world * T / (e2e_s / e2e_steps), 1) if e2e_steps else None, "unit": "tokens/s",
+                "h2d_bytes_per_step": int(host_ids.nbytes + pos_sets[0].nbytes),
+                "d2h_bytes_per_step": int(out_host.nbytes),
+                "path": "fracture_b200.backend.CudaBackend (C-ABI Backend mirror): embedding/add/rmsnorm/rope/silu_mul, "
+                        "host token ids + positions uploaded each step, last-token rows read back"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clock,
+    }
+    return res
+
+
+def cpu_baseline(tokens: int, layers: int, reps: int) -> dict:
+    import torch
+
+    from oracle import cpu_chain, ops
+
+    n = cpu_chain.set_threads()
+    inv = ops.rope_freqs_llama3(HD, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"], ROPE["orig"])
+    data = cpu_chain.make_data(tokens, HID, NQ, NKV, HD, INTER, layers, 4096, torch.bfloat16)
+    cpu_chain.run_chain(data, inv)  # warm-up
+    secs = min(cpu_chain.run_chain(data, inv) for _ in range(reps))
+    tok_s = tokens / (secs * LAYERS / layers)
+    return {"value": round(tok_s, 2), "unit": "tokens/s", "cores": n, "kind": "port",
+            "sample": f"{tokens} tokens x {layers} layers of the config-3 chain (BF16 storage, f32 math, torch CPU, "
+                      f"4096-row embedding table), best of {reps}; tokens/s scaled to the 32-layer chain"}
+
+
+def run_reference(args, rank: int) -> dict | None:
+    """The reference's CPU path on the host cores; rank 0 only (other ranks exit without work)."""
+    if rank != 0:
+        return None
+    tokens, layers = 1024, 8
+    import torch
+
+    from oracle import cpu_chain, ops
+
+    n = cpu_chain.set_threads()
+    inv = ops.rope_freqs_llama3(HD, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"], ROPE["orig"])
+    data = cpu_chain.make_data(tokens, HID, NQ, NKV, HD, INTER, layers, 4096, torch.bfloat16)
+    for _ in range(args.warmup):
+        cpu_chain.run_chain(data, inv)
+    secs = [cpu_chain.run_chain(data, inv) for _ in range(args.steps)]
+    per_step = statistics.mean(secs) * LAYERS / layers  # scaled to the 32-layer chain
+    value = tokens / per_step
+    return {
+        "impl": "reference",
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": 0, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "tokens_per_step_sample": tokens, "layers_timed": layers},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": n, "kind": "port",
+                         "sample": f"{tokens} tokens x {layers} layers per step (scaled to 32 layers); the "
+                                   "reference's PyTorch-CPU numerical path (oracle/cpu_chain.py)"},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def profile_kernel(args) -> None:
+    """One kernel at its config-3 size: ``--warmup`` launches then one more (for ``ncu -s W -c 1``)."""
+    import torch
+
+    from fracture_b200 import kernels as K
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(7)
+    T, bf = T_SEQ * N_SEQ, torch.bfloat16
+    rnd = lambda *shape: torch.randn(shape, generator=g, device=dev).to(bf)
+    if args.profile_kernel == "silu_mul":
+        a, b, o = rnd(T, INTER), rnd(T, INTER), torch.empty((T, INTER), device=dev, dtype=bf)
+        fn = lambda: K.silu_mul(o, a, b)
+    elif args.profile_kernel == "add_rmsnorm":
+        h, r, w, o = rnd(T, HID), rnd(T, HID), rnd(HID), torch.empty((T, HID), device=dev, dtype=bf)
+        fn = lambda: K.add_rmsnorm(h, r, w, o, EPS)
+    elif args.profile_kernel == "rope":
+        q, k = rnd(T, NQ, HD), rnd(T, NKV, HD)
+        pos = (torch.arange(T, device=dev, dtype=torch.int32) % T_SEQ)
+        f = torch.from_numpy(K.rope_freqs_llama3(HD, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"],
+                                                 ROPE["orig"])).to(dev)
+        fn = lambda: K.rope(q, k, pos, f)
+    else:
+        tab = rnd(VOCAB, HID)
+        ids = torch.randint(0, VOCAB, (T,), generator=g, device=dev, dtype=torch.int32)
+        o = torch.empty((T, HID), device=dev, dtype=bf)
+        fn = lambda: K.embedding(o, tab, ids)
+    for _ in range(args.warmup):
+        fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    fn()
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel": args.profile_kernel, "ms": round(e0.elapsed_time(e1), 4)}))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
+    ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding"],
+                    help="run only this kernel at its config-3 size (W warm-up launches + 1), for ncu captures")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.profile_kernel:
+        profile_kernel(args)
+        return
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    res = run_ours(args, rank, world, local_rank)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if res is not None:
+        if world == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline(tokens=2048, layers=16, reps=3)
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,958 @@
+// Host-side mirror of Fracture's CUDA backend (`impl Backend for CudaBackend`,
+// backends/fracture-cuda/src/{lib,backend}.rs) over the fracture_b200 kernels.
+//
+// Same contract as the reference: opaque tensor ids resolved through a
+// registry, one stream per backend, every op enqueued on it, copies to/from the
+// host synchronous, errors mapped to the FractureError variants with the
+// reference's messages. B200-specific differences:
+//   * host slices (token ids, positions) go through pinned staging buffers with
+//     cudaMemcpyAsync instead of cudaMalloc + blocking cudaMemcpy + cudaFree per
+//     call (backend.rs:178-204, :387-410); positions identical to the previous
+//     upload are not uploaded again (the engine passes the same positions to all
+//     layers, batched.rs:320);
+//   * add(a, b, out=a) immediately followed by rmsnorm(a, ...) runs as one fused
+//     kernel (the engine always issues that pair, batched.rs:393-396);
+//   * the quantized paged KV cache writes compressed rows straight into a
+//     contiguous block pool through a device block table (one launch for K and
+//     one for V) instead of compress-to-scratch plus four copy_rows per block
+//     segment (quantized_paged_kv_cache.rs:404-500).
+
+#include <cuda_runtime.h>
+#include <string.h>
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "fracture_b200.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const std::string& msg) {
+    g_last_error = msg;
+    return status;
+}
+
+int cuda_fail(cudaError_t e) {
+    return fail(FB_ERR_BACKEND, "CUDA error (" + std::to_string((int)e) + "): " + cudaGetErrorString(e));
+}
+
+#define FB_CUDA(call)                              \
+    do {                                           \
+        cudaError_t fb_e_ = (call);                \
+        if (fb_e_ != cudaSuccess) return cuda_fail(fb_e_); \
+    } while (0)
+
+int64_t numel(const fb_tensor* t) {
+    int64_t n = 1;
+    for (int i = 0; i < t->ndim; ++i) n *= t->shape[i];
+    return n;
+}
+
+int elem_size(int dt) {
+    switch (dt) {
+        case FB_FP16: case FB_BF16: return 2;
+        case FB_FP32: return 4;
+        case FB_INT8: case FB_INT4: return 1;
+        default: return 0;
+    }
+}
+
+// DeviceTensor::size_bytes (tensor.rs:53-60): INT4 packs two per byte.
+int64_t size_bytes(const fb_tensor* t) {
+    const int64_t n = numel(t);
+    return t->dtype == FB_INT4 ? (n + 1) / 2 : n * elem_size(t->dtype);
+}
+
+std::string shape_str(const fb_tensor* t) {
+    std::string s = "[";
+    for (int i = 0; i < t->ndim; ++i) {
+        if (i) s += ", ";
+        s += std::to_string(t->shape[i]);
+    }
+    return s + "]";
+}
+
+bool same_shape(const fb_tensor* a, const fb_tensor* b) {
+    if (a->ndim != b->ndim) return false;
+    for (int i = 0; i < a->ndim; ++i)
+        if (a->shape[i] != b->shape[i]) return false;
+    return true;
+}
+
+bool float_dtype(int dt) { return dt == FB_FP16 || dt == FB_BF16 || dt == FB_FP32; }
+
+// Pinned staging buffer for host slices, reused once its last copy finished.
+struct HostStage {
+    void* host = nullptr;
+    size_t cap = 0;
+    cudaEvent_t done = nullptr;
+    bool pending = false;
+
+    cudaError_t ensure(size_t bytes) {
+        if (pending) {
+            cudaError_t e = cudaEventSynchronize(done);
+            if (e != cudaSuccess) return e;
+            pending = false;
+        }
+        if (!done) {
+            cudaError_t e = cudaEventCreateWithFlags(&done, cudaEventDisableTiming);
+            if (e != cudaSuccess) return e;
+        }
+        if (bytes <= cap) return cudaSuccess;
+        if (host) cudaFreeHost(host);
+        host = nullptr;
+        cap = 0;
+        size_t c = std::max<size_t>(bytes, 4096);
+        cudaError_t e = cudaMallocHost(&host, c);
+        if (e != cudaSuccess) return e;
+        cap = c;
+        return cudaSuccess;
+    }
+    void release() {
+        if (pending && done) cudaEventSynchronize(done);
+        if (host) cudaFreeHost(host);
+        if (done) cudaEventDestroy(done);
+        host = nullptr;
+        done = nullptr;
+        cap = 0;
+        pending = false;
+    }
+};
+
+// Device buffer that only grows.
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t cap = 0;
+    cudaError_t ensure(size_t bytes, cudaStream_t s) {
+        if (bytes <= cap) return cudaSuccess;
+        if (ptr) {
+            cudaError_t e = cudaStreamSynchronize(s);
+            if (e != cudaSuccess) return e;
+            cudaFree(ptr);
+        }
+        ptr = nullptr;
+        cap = 0;
+        size_t c = std::max<size_t>(bytes, 4096);
+        cudaError_t e = cudaMalloc(&ptr, c);
+        if (e != cudaSuccess) return e;
+        cap = c;
+        return cudaSuccess;
+    }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        cap = 0;
+    }
+};
+
+struct Entry {
+    void* ptr;
+    int64_t bytes;
+    bool owned;
+};
+
+struct PendingAdd {
+    bool active = false;
+    uint64_t a = 0, b = 0;
+    void* pa = nullptr;
+    const void* pb = nullptr;
+    int64_t n = 0;
+    int dtype = 0;
+};
+
+struct Timer {
+    cudaEvent_t start = nullptr, stop = nullptr;
+};
+
+}  // namespace
+
+struct fb_backend {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::recursive_mutex mu;
+    std::unordered_map<uint64_t, Entry> tensors;
+    uint64_t next_id = 1;
+    std::string name;
+    size_t total_mem = 0;
+    // rope
+    DevBuf freq;
+    int freq_half = 0;
+    DevBuf pos_dev;
+    HostStage pos_stage;
+    std::vector<uint32_t> pos_cache;
+    bool pos_valid = false;
+    // embedding ids
+    DevBuf ids_dev;
+    HostStage ids_stage;
+    PendingAdd pending;
+    std::map<uint64_t, Timer> timers;
+    uint64_t next_timer = 1;
+
+    int get(const fb_tensor* t, void** p) {
+        if (!t) return fail(FB_ERR_INVALID_SHAPE, "null tensor");
+        auto it = tensors.find(t->id);
+        if (it == tensors.end()) return fail(FB_ERR_TENSOR_NOT_FOUND, "tensor id " + std::to_string(t->id));
+        *p = it->second.ptr;
+        return FB_OK;
+    }
+
+    int flush() {
+        if (!pending.active) return FB_OK;
+        pending.active = false;
+        int e = fb_launch_add(pending.pa, pending.pa, pending.pb, pending.n, pending.dtype, stream);
+        if (e) return cuda_fail((cudaError_t)e);
+        return FB_OK;
+    }
+
+    // Upload a host u32 slice through the staging buffer into `dst`.
+    int upload_u32(const uint32_t* src, size_t n, HostStage& stage, DevBuf& dst) {
+        const size_t bytes = n * sizeof(uint32_t);
+        FB_CUDA(stage.ensure(bytes));
+        FB_CUDA(dst.ensure(bytes, stream));
+        memcpy(stage.host, src, bytes);
+        FB_CUDA(cudaMemcpyAsync(dst.ptr, stage.host, bytes, cudaMemcpyHostToDevice, stream));
+        FB_CUDA(cudaEventRecord(stage.done, stream));
+        stage.pending = true;
+        return FB_OK;
+    }
+};
+
+struct fb_tq_cache {
+    fb_backend* be = nullptr;
+    size_t num_blocks = 0, num_layers = 0, heads = 0, head_dim = 0;
+    fb_tq_config cfg{};
+    std::vector<int> kbits, vbits;
+    std::vector<void*> packed[2], norms[2], rot[2];
+    std::map<int, void*> centroids;  // bits -> device [2^bits] f32
+    std::vector<size_t> free_list;
+    struct Seq {
+        std::vector<int32_t> table;
+        size_t last_fill = 0, len = 0;
+        DevBuf dev_table;
+        size_t dev_len = 0;  // entries valid on the device
+    };
+    std::map<uint64_t, Seq> seqs;
+    uint64_t next_id = 0;
+    HostStage stage;
+
+    bool protected_layer(size_t l) const {
+        return cfg.protected_layers > 0 &&
+               (l < cfg.protected_layers || l >= (num_layers > cfg.protected_layers ? num_layers - cfg.protected_layers : 0));
+    }
+    size_t bytes_per_block() const {
+        size_t t = 0;
+        for (size_t l = 0; l < num_layers; ++l) {
+            t += 16 * heads * ((head_dim * kbits[l] + 7) / 8) + 16 * heads * ((head_dim * vbits[l] + 7) / 8) +
+                 2 * 16 * heads * 2;
+        }
+        return t;
+    }
+};
+
+extern "C" {
+
+const char* fb_last_error(void) { return g_last_error.c_str(); }
+
+int fb_backend_create(int device, fb_backend** out) {
+    if (!out) return fail(FB_ERR_BACKEND, "null output pointer");
+    FB_CUDA(cudaSetDevice(device));
+    auto* b = new fb_backend();
+    b->device = device;
+    cudaError_t e = cudaStreamCreate(&b->stream);
+    if (e != cudaSuccess) {
+        delete b;
+        return cuda_fail(e);
+    }
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) {
+        cudaStreamDestroy(b->stream);
+        delete b;
+        return cuda_fail(e);
+    }
+    b->name = prop.name;
+    b->total_mem = prop.totalGlobalMem;
+    *out = b;
+    return FB_OK;
+}
+
+int fb_backend_destroy(fb_backend* b) {
+    if (!b) return FB_OK;
+    {
+        std::lock_guard<std::recursive_mutex> g(b->mu);
+        b->flush();
+        cudaStreamSynchronize(b->stream);
+        for (auto& kv : b->tensors)
+            if (kv.second.owned) cudaFree(kv.second.ptr);
+        b->tensors.clear();
+        for (auto& kv : b->timers) {
+            cudaEventDestroy(kv.second.start);
+            cudaEventDestroy(kv.second.stop);
+        }
+        b->freq.release();
+        b->pos_dev.release();
+        b->ids_dev.release();
+        b->pos_stage.release();
+        b->ids_stage.release();
+        cudaStreamDestroy(b->stream);
+    }
+    delete b;
+    return FB_OK;
+}
+
+int fb_backend_stream(fb_backend* b, void** stream_out) {
+    if (!b || !stream_out) return fail(FB_ERR_BACKEND, "null argument");
+    *stream_out = b->stream;
+    return FB_OK;
+}
+
+int fb_backend_device_name(fb_backend* b, char* buf, size_t cap) {
+    if (!b || !buf || cap == 0) return fail(FB_ERR_BACKEND, "null argument");
+    snprintf(buf, cap, "%s", b->name.c_str());
+    return FB_OK;
+}
+
+int fb_backend_total_memory(fb_backend* b, size_t* out) {
+    if (!b || !out) return fail(FB_ERR_BACKEND, "null argument");
+    *out = b->total_mem;
+    return FB_OK;
+}
+
+int fb_backend_available_memory(fb_backend* b, size_t* out) {
+    if (!b || !out) return fail(FB_ERR_BACKEND, "null argument");
+    size_t f = 0, t = 0;
+    FB_CUDA(cudaMemGetInfo(&f, &t));
+    *out = f;
+    return FB_OK;
+}
+
+// ── memory ─────────────────────────────────────────────────────────────────
+
+int fb_alloc(fb_backend* b, const int64_t* shape, int ndim, int dtype, fb_tensor* out) {
+    if (!b || !out || (ndim > 0 && !shape)) return fail(FB_ERR_BACKEND, "null argument");
+    if (ndim < 1 || ndim > 4) return fail(FB_ERR_INVALID_SHAPE, "shape must have 1 to 4 dimensions");
+    if (elem_size(dtype) == 0) return fail(FB_ERR_UNSUPPORTED_DTYPE, "dtype " + std::to_string(dtype));
+    fb_tensor t{};
+    t.dtype = dtype;
+    t.ndim = ndim;
+    for (int i = 0; i < ndim; ++i) {
+        if (shape[i] < 0) return fail(FB_ERR_INVALID_SHAPE, "negative dimension");
+        t.shape[i] = shape[i];
+    }
+    const int64_t bytes = size_bytes(&t);
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    void* p = nullptr;
+    FB_CUDA(cudaSetDevice(b->device));
+    cudaError_t e = cudaMalloc(&p, (size_t)std::max<int64_t>(bytes, 1));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_fail(e);
+    }
+    t.id = b->next_id++;
+    b->tensors[t.id] = Entry{p, bytes, true};
+    *out = t;
+    return FB_OK;
+}
+
+int fb_register_external(fb_backend* b, void* dev_ptr, const int64_t* shape, int ndim, int dtype, fb_tensor* out) {
+    if (!b || !out || !dev_ptr || (ndim > 0 && !shape)) return fail(FB_ERR_BACKEND, "null argument");
+    if (ndim < 1 || ndim > 4) return fail(FB_ERR_INVALID_SHAPE, "shape must have 1 to 4 dimensions");
+    fb_tensor t{};
+    t.dtype = dtype;
+    t.ndim = ndim;
+    for (int i = 0; i < ndim; ++i) t.shape[i] = shape[i];
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    t.id = b->next_id++;
+    b->tensors[t.id] = Entry{dev_ptr, size_bytes(&t), false};
+    *out = t;
+    return FB_OK;
+}
+
+int fb_get_ptr(fb_backend* b, const fb_tensor* t, void** out) {
+    if (!b || !out) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    return b->get(t, out);
+}
+
+int fb_free(fb_backend* b, const fb_tensor* t) {
+    if (!b || !t) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    auto it = b->tensors.find(t->id);
+    if (it == b->tensors.end()) return fail(FB_ERR_TENSOR_NOT_FOUND, "tensor id " + std::to_string(t->id));
+    if (b->pending.active && (b->pending.a == t->id || b->pending.b == t->id)) {
+        int rc = b->flush();
+        if (rc) return rc;
+    }
+    Entry en = it->second;
+    b->tensors.erase(it);
+    if (en.owned) {
+        // cudaFree synchronises the device, so queued kernels that use the buffer finish first.
+        FB_CUDA(cudaFree(en.ptr));
+    }
+    return FB_OK;
+}
+
+int fb_copy_to_device(fb_backend* b, const fb_tensor* dst, const void* src, size_t src_len) {
+    if (!b || !dst || (!src && src_len)) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    void* p;
+    int rc = b->get(dst, &p);
+    if (rc) return rc;
+    const int64_t size = size_bytes(dst);
+    if ((int64_t)src_len < size)
+        return fail(FB_ERR_INVALID_SHAPE, "source buffer too small: " + std::to_string(src_len) + " < " + std::to_string(size));
+    rc = b->flush();
+    if (rc) return rc;
+    FB_CUDA(cudaMemcpyAsync(p, src, (size_t)size, cudaMemcpyHostToDevice, b->stream));
+    FB_CUDA(cudaStreamSynchronize(b->stream));
+    return FB_OK;
+}
+
+int fb_copy_to_host(fb_backend* b, const fb_tensor* src, void* dst, size_t dst_len) {
+    if (!b || !src || (!dst && dst_len)) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    void* p;
+    int rc = b->get(src, &p);
+    if (rc) return rc;
+    const int64_t size = size_bytes(src);
+    if ((int64_t)dst_len < size)
+        return fail(FB_ERR_INVALID_SHAPE,
+                    "destination buffer too small: " + std::to_string(dst_len) + " < " + std::to_string(size));
+    rc = b->flush();
+    if (rc) return rc;
+    FB_CUDA(cudaMemcpyAsync(dst, p, (size_t)size, cudaMemcpyDeviceToHost, b->stream));
+    FB_CUDA(cudaStreamSynchronize(b->stream));
+    return FB_OK;
+}
+
+// ── compute ────────────────────────────────────────────────────────────────
+
+int fb_rmsnorm(fb_backend* b, const fb_tensor* input, const fb_tensor* weight, double eps, const fb_tensor* out) {
+    if (!b || !input || !weight || !out) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    void *pi, *pw, *po;
+    int rc;
+    if ((rc = b->get(input, &pi)) || (rc = b->get(weight, &pw)) || (rc = b->get(out, &po))) return rc;
+    if (input->ndim < 2) return fail(FB_ERR_INVALID_SHAPE, "rmsnorm: input must be [rows, cols], got " + shape_str(input));
+    if (!float_dtype(input->dtype) || weight->dtype != input->dtype || out->dtype != input->dtype)
+        return fail(FB_ERR_UNSUPPORTED_DTYPE, "rmsnorm: input, weight and out must share a float dtype");
+    const int64_t rows = input->shape[0], cols = input->shape[1];
+    if (numel(weight) < cols || numel(out) < rows * cols)
+        return fail(FB_ERR_INVALID_SHAPE, "rmsnorm: weight " + shape_str(weight) + " / out " + shape_str(out) +
+                                              " too small for input " + shape_str(input));
+    if (b->pending.active && b->pending.a == input->id && b->pending.n == rows * cols &&
+        b->pending.dtype == input->dtype && b->pending.pa == pi) {
+        // add(h, r, h) then rmsnorm(h, ...): one fused launch.
+        b->pending.active = false;
+        int e = fb_launch_add_rmsnorm(pi, b->pending.pb, pw, po, (float)eps, rows, cols, input->dtype, b->stream);
+        if (e) return cuda_fail((cudaError_t)e);
+        return FB_OK;
+    }
+    if ((rc = b->flush())) return rc;
+    int e = fb_launch_rmsnorm(po, pi, pw, (float)eps, rows, cols, input->dtype, b->stream);
+    if (e) return cuda_fail((cudaError_t)e);
+    return FB_OK;
+}
+
+int fb_add(fb_backend* b, const fb_tensor* a, const fb_tensor* bb, const fb_tensor* out) {
+    if (!b || !a || !bb || !out) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    if (!same_shape(a, bb)) return fail(FB_ERR_INVALID_SHAPE, "add: a shape " + shape_str(a) + " != b shape " + shape_str(bb));
+    void *pa, *pb, *po;
+    int rc;
+    if ((rc = b->get(a, &pa)) || (rc = b->get(bb, &pb)) || (rc = b->get(out, &po))) return rc;
+    if (!float_dtype(a->dtype) || bb->dtype != a->dtype || out->dtype != a->dtype)
+        return fail(FB_ERR_UNSUPPORTED_DTYPE, "add: a, b and out must share a float dtype");
+    if ((rc = b->flush())) return rc;
+    const int64_t n = numel(a);
+    if (out->id == a->id && po == pa && bb->id != a->id) {
+        b->pending.active = true;
+        b->pending.a = a->id;
+        b->pending.b = bb->id;
+        b->pending.pa = pa;
+        b->pending.pb = pb;
+        b->pending.n = n;
+        b->pending.dtype = a->dtype;
+        return FB_OK;
+    }
+    int e = fb_launch_add(po, pa, pb, n, a->dtype, b->stream);
+    if (e) return cuda_fail((cudaError_t)e);
+    return FB_OK;
+}
+
+int fb_silu_mul(fb_backend* b, const fb_tensor* gate, const fb_tensor* up, const fb_tensor* out) {
+    if (!b || !gate || !up || !out) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    if (!same_shape(gate, up))
+        return fail(FB_ERR_INVALID_SHAPE, "silu_mul: gate shape " + shape_str(gate) + " != up shape " + shape_str(up));
+    void *pg, *pu, *po;
+    int rc;
+    if ((rc = b->get(gate, &pg)) || (rc = b->get(up, &pu)) || (rc = b->get(out, &po))) return rc;
+    if (!float_dtype(gate->dtype) || up->dtype != gate->dtype || out->dtype != gate->dtype)
+        return fail(FB_ERR_UNSUPPORTED_DTYPE, "silu_mul: gate, up and out must share a float dtype");
+    if (numel(out) < numel(gate)) return fail(FB_ERR_INVALID_SHAPE, "silu_mul: out " + shape_str(out) + " too small");
+    if ((rc = b->flush())) return rc;
+    int e = fb_launch_silu_mul(po, pg, pu, numel(gate), gate->dtype, b->stream);
+    if (e) return cuda_fail((cudaError_t)e);
+    return FB_OK;
+}
+
+int fb_embedding(fb_backend* b, const uint32_t* token_ids, size_t num_tokens, const fb_tensor* table,
+                 const fb_tensor* out) {
+    if (!b || !table || !out || (!token_ids && num_tokens)) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    void *pt, *po;
+    int rc;
+    if ((rc = b->get(table, &pt)) || (rc = b->get(out, &po))) return rc;
+    if (table->ndim < 2) return fail(FB_ERR_INVALID_SHAPE, "embedding: table must be [vocab, hidden]");
+    if (!float_dtype(table->dtype) || out->dtype != table->dtype)
+        return fail(FB_ERR_UNSUPPORTED_DTYPE, "embedding: table and out must share a float dtype");
+    const int64_t vocab = table->shape[0], hidden = table->shape[1];
+    if (numel(out) < (int64_t)num_tokens * hidden)
+        return fail(FB_ERR_INVALID_SHAPE, "embedding: out " + shape_str(out) + " too small");
+    if ((rc = b->flush())) return rc;
+    if (num_tokens == 0) return FB_OK;
+    if ((rc = b->upload_u32(token_ids, num_tokens, b->ids_stage, b->ids_dev))) return rc;
+    int e = fb_launch_embedding(po, pt, (const uint32_t*)b->ids_dev.ptr, (int64_t)num_tokens, hidden, vocab,
+                                table->dtype, b->stream);
+    if (e) return fail(FB_ERR_BACKEND, std::string("embedding kernel error: ") + cudaGetErrorString((cudaError_t)e));
+    return FB_OK;
+}
+
+int fb_precompute_rope_freqs(fb_backend* b, size_t head_dim, double theta) {
+    if (!b) return fail(FB_ERR_BACKEND, "null argument");
+    std::vector<float> f(head_dim / 2);
+    if (head_dim == 0 || fb_rope_freqs((int)head_dim, theta, f.data()))
+        return fail(FB_ERR_MODEL_CONFIG, "invalid rope parameters");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    int rc;
+    if ((rc = b->flush())) return rc;
+    FB_CUDA(b->freq.ensure(f.size() * sizeof(float), b->stream));
+    FB_CUDA(cudaMemcpyAsync(b->freq.ptr, f.data(), f.size() * sizeof(float), cudaMemcpyHostToDevice, b->stream));
+    FB_CUDA(cudaStreamSynchronize(b->stream));
+    b->freq_half = (int)f.size();
+    return FB_OK;
+}
+
+int fb_precompute_rope_freqs_llama3(fb_backend* b, size_t head_dim, double theta, double factor,
+                                    double low_freq_factor, double high_freq_factor, double original_max_position) {
+    if (!b) return fail(FB_ERR_BACKEND, "null argument");
+    std::vector<float> f(head_dim / 2);
+    if (head_dim == 0 || fb_rope_freqs_llama3((int)head_dim, theta, factor, low_freq_factor, high_freq_factor,
+                                              original_max_position, f.data()))
+        return fail(FB_ERR_MODEL_CONFIG, "invalid llama3 rope parameters");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    int rc;
+    if ((rc = b->flush())) return rc;
+    FB_CUDA(b->freq.ensure(f.size() * sizeof(float), b->stream));
+    FB_CUDA(cudaMemcpyAsync(b->freq.ptr, f.data(), f.size() * sizeof(float), cudaMemcpyHostToDevice, b->stream));
+    FB_CUDA(cudaStreamSynchronize(b->stream));
+    b->freq_half = (int)f.size();
+    return FB_OK;
+}
+
+int fb_rope(fb_backend* b, const fb_tensor* q, const fb_tensor* k, const uint32_t* positions, size_t num_positions,
+            double theta, size_t head_dim) {
+    (void)theta;  // the table comes from precompute_rope_freqs, as in the reference (backend.rs:161-172)
+    if (!b || !q || !k || (!positions && num_positions)) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    void *pq, *pk;
+    int rc;
+    if ((rc = b->get(q, &pq)) || (rc = b->get(k, &pk))) return rc;
+    if (!b->freq_half)
+        return fail(FB_ERR_BACKEND, "RoPE frequency table not initialized. Call precompute_rope_freqs() first.");
+    if (q->ndim < 2 || k->ndim < 2) return fail(FB_ERR_INVALID_SHAPE, "rope: q and k must be [tokens, heads, head_dim]");
+    if ((size_t)b->freq_half * 2 != head_dim)
+        return fail(FB_ERR_INVALID_SHAPE, "rope: head_dim " + std::to_string(head_dim) + " does not match the frequency table");
+    if (!float_dtype(q->dtype) || k->dtype != q->dtype) return fail(FB_ERR_UNSUPPORTED_DTYPE, "rope: q and k must share a float dtype");
+    const int64_t nq = q->shape[1], nkv = k->shape[1];
+    if (numel(q) < (int64_t)num_positions * nq * (int64_t)head_dim ||
+        numel(k) < (int64_t)num_positions * nkv * (int64_t)head_dim)
+        return fail(FB_ERR_INVALID_SHAPE, "rope: q " + shape_str(q) + " / k " + shape_str(k) + " too small for " +
+                                              std::to_string(num_positions) + " positions");
+    if ((rc = b->flush())) return rc;
+    if (num_positions == 0) return FB_OK;
+    const bool same = b->pos_valid && b->pos_cache.size() == num_positions &&
+                      memcmp(b->pos_cache.data(), positions, num_positions * sizeof(uint32_t)) == 0;
+    if (!same) {
+        if ((rc = b->upload_u32(positions, num_positions, b->pos_stage, b->pos_dev))) return rc;
+        b->pos_cache.assign(positions, positions + num_positions);
+        b->pos_valid = true;
+    }
+    int e = fb_launch_rope(pq, pk, (const uint32_t*)b->pos_dev.ptr, (const float*)b->freq.ptr, (int64_t)num_positions,
+                           (int)nq, (int)nkv, (int)head_dim, q->dtype, b->stream);
+    if (e) return fail(FB_ERR_BACKEND, std::string("RoPE kernel error: ") + cudaGetErrorString((cudaError_t)e));
+    return FB_OK;
+}
+
+int fb_copy_rows(fb_backend* b, const fb_tensor* src, const fb_tensor* dst, size_t src_offset, size_t dst_offset,
+                 size_t count) {
+    if (!b || !src || !dst) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    // Bounds validation messages follow backend.rs:458-486.
+    if (src->ndim < 1 || dst->ndim < 1) return fail(FB_ERR_INVALID_SHAPE, "copy_rows: empty shape");
+    if ((int64_t)(src_offset + count) > src->shape[0])
+        return fail(FB_ERR_INVALID_SHAPE, "copy_rows: src_offset(" + std::to_string(src_offset) + ") + count(" +
+                                              std::to_string(count) + ") = " + std::to_string(src_offset + count) +
+                                              " exceeds src rows(" + std::to_string(src->shape[0]) + ")");
+    if ((int64_t)(dst_offset + count) > dst->shape[0])
+        return fail(FB_ERR_INVALID_SHAPE, "copy_rows: dst_offset(" + std::to_string(dst_offset) + ") + count(" +
+                                              std::to_string(count) + ") = " + std::to_string(dst_offset + count) +
+                                              " exceeds dst rows(" + std::to_string(dst->shape[0]) + ")");
+    bool cols_same = src->ndim == dst->ndim;
+    for (int i = 1; cols_same && i < src->ndim; ++i) cols_same = src->shape[i] == dst->shape[i];
+    if (!cols_same) return fail(FB_ERR_INVALID_SHAPE, "copy_rows: src column shape != dst column shape");
+    if (src->dtype != dst->dtype) return fail(FB_ERR_INVALID_SHAPE, "copy_rows: src dtype != dst dtype");
+    void *ps, *pd;
+    int rc;
+    if ((rc = b->get(src, &ps)) || (rc = b->get(dst, &pd))) return rc;
+    if ((rc = b->flush())) return rc;
+    int64_t row = elem_size(src->dtype);
+    for (int i = 1; i < src->ndim; ++i) row *= src->shape[i];
+    if (count == 0) return FB_OK;
+    FB_CUDA(cudaMemcpyAsync((char*)pd + dst_offset * row, (const char*)ps + src_offset * row, count * row,
+                            cudaMemcpyDeviceToDevice, b->stream));
+    return FB_OK;
+}
+
+int fb_turboquant_compress(fb_backend* b, const fb_tensor* input, const fb_tensor* rotation,
+                           const fb_tensor* centroids, uint8_t bits, const fb_tensor* packed_out,
+                           const fb_tensor* norms_out) {
+    if (!b || !input || !rotation || !centroids || !packed_out || !norms_out) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    void *pi, *pr, *pc, *pp, *pn;
+    int rc;
+    if ((rc = b->get(input, &pi)) || (rc = b->get(rotation, &pr)) || (rc = b->get(centroids, &pc)) ||
+        (rc = b->get(packed_out, &pp)) || (rc = b->get(norms_out, &pn)))
+        return rc;
+    if (input->ndim != 3) return fail(FB_ERR_INVALID_SHAPE, "turboquant_compress: input must be [N, heads, head_dim]");
+    const int64_t n = input->shape[0], h = input->shape[1], d = input->shape[2];
+    const int64_t P = (d * bits + 7) / 8;
+    if (centroids->shape[0] != (1 << bits))
+        return fail(FB_ERR_INVALID_SHAPE, "turboquant_compress: centroid table has " + std::to_string(centroids->shape[0]) +
+                                              " entries for " + std::to_string(bits) + " bits");
+    if (numel(rotation) < d * d || size_bytes(packed_out) < n * h * P || numel(norms_out) < n * h)
+        return fail(FB_ERR_INVALID_SHAPE, "turboquant_compress: output or rotation too small");
+    if ((rc = b->flush())) return rc;
+    const int64_t rows = packed_out->ndim >= 1 ? packed_out->shape[0] : n;
+    int e = fb_launch_tq_compress_paged(pi, input->dtype, (const float*)pr, (const float*)pc, bits, n, (int)h, (int)d,
+                                        nullptr, 0, std::max<int64_t>(rows, n), pp, pn, nullptr, b->stream);
+    if (e) return cuda_fail((cudaError_t)e);
+    return FB_OK;
+}
+
+int fb_synchronize(fb_backend* b) {
+    if (!b) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    int rc;
+    if ((rc = b->flush())) return rc;
+    FB_CUDA(cudaStreamSynchronize(b->stream));
+    return FB_OK;
+}
+
+// ── timers (src/timers.rs) ─────────────────────────────────────────────────
+
+int fb_create_timer(fb_backend* b, uint64_t* timer) {
+    if (!b || !timer) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    Timer t;
+    FB_CUDA(cudaEventCreate(&t.start));
+    FB_CUDA(cudaEventCreate(&t.stop));
+    const uint64_t id = b->next_timer++;
+    b->timers[id] = t;
+    *timer = id;
+    return FB_OK;
+}
+
+int fb_start_timer(fb_backend* b, uint64_t timer) {
+    if (!b) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    auto it = b->timers.find(timer);
+    if (it == b->timers.end()) return fail(FB_ERR_BACKEND, "invalid timer id " + std::to_string(timer));
+    int rc;
+    if ((rc = b->flush())) return rc;
+    FB_CUDA(cudaEventRecord(it->second.start, b->stream));
+    return FB_OK;
+}
+
+int fb_stop_timer(fb_backend* b, uint64_t timer, float* ms) {
+    if (!b || !ms) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    auto it = b->timers.find(timer);
+    if (it == b->timers.end()) return fail(FB_ERR_BACKEND, "invalid timer id " + std::to_string(timer));
+    int rc;
+    if ((rc = b->flush())) return rc;
+    FB_CUDA(cudaEventRecord(it->second.stop, b->stream));
+    FB_CUDA(cudaEventSynchronize(it->second.stop));
+    FB_CUDA(cudaEventElapsedTime(ms, it->second.start, it->second.stop));
+    return FB_OK;
+}
+
+int fb_destroy_timer(fb_backend* b, uint64_t timer) {
+    if (!b) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    auto it = b->timers.find(timer);
+    if (it == b->timers.end()) return fail(FB_ERR_BACKEND, "invalid timer id " + std::to_string(timer));
+    cudaEventDestroy(it->second.start);
+    cudaEventDestroy(it->second.stop);
+    b->timers.erase(it);
+    return FB_OK;
+}
+
+// ── quantized paged KV cache ───────────────────────────────────────────────
+
+int fb_tq_cache_create(fb_backend* b, size_t num_blocks, size_t num_layers, size_t num_kv_heads, size_t head_dim,
+                       const fb_tq_config* cfg, fb_tq_cache** out) {
+    if (!b || !cfg || !out) return fail(FB_ERR_BACKEND, "null argument");
+    auto ok_bits = [](int x) { return x == 2 || x == 3 || x == 4 || x == 8; };
+    if (!ok_bits(cfg->key_bits) || !ok_bits(cfg->value_bits) || !ok_bits(cfg->protected_bits))
+        return fail(FB_ERR_MODEL_CONFIG, "TurboQuant bit widths must be 2, 3, 4 or 8");
+    if (num_layers == 0 || num_kv_heads == 0 || head_dim == 0 || head_dim > 192)
+        return fail(FB_ERR_MODEL_CONFIG, "invalid quantized cache dimensions");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    int rc;
+    if ((rc = b->flush())) return rc;
+    auto* c = new fb_tq_cache();
+    c->be = b;
+    c->num_blocks = num_blocks;
+    c->num_layers = num_layers;
+    c->heads = num_kv_heads;
+    c->head_dim = head_dim;
+    c->cfg = *cfg;
+    const size_t rows = num_blocks * 16;
+    auto cleanup = [&](int status) {
+        fb_tq_cache_destroy(c);
+        return status;
+    };
+    std::vector<float> host((size_t)head_dim * head_dim);
+    for (size_t l = 0; l < num_layers; ++l) {
+        const bool prot = c->protected_layer(l);
+        c->kbits.push_back(prot ? cfg->protected_bits : cfg->key_bits);
+        c->vbits.push_back(prot ? cfg->protected_bits : cfg->value_bits);
+        for (int kv = 0; kv < 2; ++kv) {
+            const int bits = kv == 0 ? c->kbits[l] : c->vbits[l];
+            const size_t P = (head_dim * bits + 7) / 8;
+            void *pp = nullptr, *pn = nullptr, *pr = nullptr;
+            cudaError_t e = cudaMalloc(&pp, std::max<size_t>(rows * num_kv_heads * P, 1));
+            if (e == cudaSuccess) e = cudaMalloc(&pn, std::max<size_t>(rows * num_kv_heads * 2, 1));
+            if (e == cudaSuccess) e = cudaMalloc(&pr, host.size() * sizeof(float));
+            c->packed[kv].push_back(pp);
+            c->norms[kv].push_back(pn);
+            c->rot[kv].push_back(pr);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                return cleanup(cuda_fail(e));
+            }
+            // rotation_seeds (turboquant.rs:341-345): K = base + 1000 l, V = base + 1000 l + 500.
+            const uint64_t seed = cfg->seed + (uint64_t)l * 1000 + (kv ? 500 : 0);
+            fb_tq_rotation_matrix((int)head_dim, seed, host.data());
+            e = cudaMemcpy(pr, host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) return cleanup(cuda_fail(e));
+        }
+    }
+    for (size_t l = 0; l < num_layers; ++l) {
+        for (int bits : {c->kbits[l], c->vbits[l]}) {
+            if (c->centroids.count(bits)) continue;
+            std::vector<float> cen((size_t)1 << bits);
+            fb_tq_codebook((int)head_dim, bits, cen.data(), nullptr);
+            void* pc = nullptr;
+            cudaError_t e = cudaMalloc(&pc, cen.size() * sizeof(float));
+            if (e == cudaSuccess) e = cudaMemcpy(pc, cen.data(), cen.size() * sizeof(float), cudaMemcpyHostToDevice);
+            c->centroids[bits] = pc;
+            if (e != cudaSuccess) return cleanup(cuda_fail(e));
+        }
+    }
+    for (size_t i = num_blocks; i > 0; --i) c->free_list.push_back(i - 1);
+    *out = c;
+    return FB_OK;
+}
+
+int fb_tq_cache_destroy(fb_tq_cache* c) {
+    if (!c) return FB_OK;
+    cudaStreamSynchronize(c->be->stream);
+    for (int kv = 0; kv < 2; ++kv) {
+        for (void* p : c->packed[kv]) if (p) cudaFree(p);
+        for (void* p : c->norms[kv]) if (p) cudaFree(p);
+        for (void* p : c->rot[kv]) if (p) cudaFree(p);
+    }
+    for (auto& kv : c->centroids) if (kv.second) cudaFree(kv.second);
+    for (auto& s : c->seqs) s.second.dev_table.release();
+    c->stage.release();
+    delete c;
+    return FB_OK;
+}
+
+static int tq_alloc_block(fb_tq_cache* c, int32_t* out) {
+    if (c->free_list.empty()) {
+        char buf[160];
+        snprintf(buf, sizeof(buf), "out of device memory: requested %zu bytes, available 0 bytes", c->bytes_per_block());
+        return fail(FB_ERR_OUT_OF_MEMORY, buf);
+    }
+    *out = (int32_t)c->free_list.back();
+    c->free_list.pop_back();
+    return FB_OK;
+}
+
+int fb_tq_cache_alloc(fb_tq_cache* c, uint64_t* handle) {
+    if (!c || !handle) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(c->be->mu);
+    const uint64_t id = c->next_id++;
+    int32_t blk;
+    int rc = tq_alloc_block(c, &blk);
+    if (rc) return rc;
+    c->seqs[id].table.push_back(blk);
+    *handle = id;
+    return FB_OK;
+}
+
+int fb_tq_cache_free(fb_tq_cache* c, uint64_t handle) {
+    if (!c) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(c->be->mu);
+    auto it = c->seqs.find(handle);
+    if (it == c->seqs.end()) return fail(FB_ERR_KV_CACHE, "invalid handle: " + std::to_string(handle));
+    for (int32_t blk : it->second.table) c->free_list.push_back((size_t)blk);
+    // The device copy of the table may still be read by queued kernels.
+    cudaStreamSynchronize(c->be->stream);
+    it->second.dev_table.release();
+    c->seqs.erase(it);
+    return FB_OK;
+}
+
+static int tq_sync_table(fb_tq_cache* c, fb_tq_cache::Seq& s) {
+    if (s.dev_len == s.table.size()) return FB_OK;
+    fb_backend* b = c->be;
+    const size_t bytes = s.table.size() * sizeof(int32_t);
+    FB_CUDA(s.dev_table.ensure(bytes, b->stream));
+    FB_CUDA(c->stage.ensure(bytes));
+    memcpy(c->stage.host, s.table.data(), bytes);
+    FB_CUDA(cudaMemcpyAsync(s.dev_table.ptr, c->stage.host, bytes, cudaMemcpyHostToDevice, b->stream));
+    FB_CUDA(cudaEventRecord(c->stage.done, b->stream));
+    c->stage.pending = true;
+    s.dev_len = s.table.size();
+    return FB_OK;
+}
+
+int fb_tq_cache_append_kv(fb_tq_cache* c, uint64_t handle, size_t layer, const fb_tensor* keys,
+                          const fb_tensor* values) {
+    if (!c || !keys || !values) return fail(FB_ERR_BACKEND, "null argument");
+    fb_backend* b = c->be;
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    if (layer >= c->num_layers) return fail(FB_ERR_KV_CACHE, "layer " + std::to_string(layer) + " out of range");
+    void *pk, *pv;
+    int rc;
+    if ((rc = b->get(keys, &pk)) || (rc = b->get(values, &pv))) return rc;
+    if (keys->ndim != 3 || !same_shape(keys, values) || keys->shape[1] != (int64_t)c->heads ||
+        keys->shape[2] != (int64_t)c->head_dim)
+        return fail(FB_ERR_INVALID_SHAPE, "append_kv: keys/values must be [N, " + std::to_string(c->heads) + ", " +
+                                              std::to_string(c->head_dim) + "]");
+    if (keys->dtype != values->dtype || (keys->dtype != FB_FP16 && keys->dtype != FB_BF16))
+        return fail(FB_ERR_UNSUPPORTED_DTYPE, "append_kv: keys/values must be FP16 or BF16");
+    auto it = c->seqs.find(handle);
+    if (it == c->seqs.end()) return fail(FB_ERR_KV_CACHE, "invalid handle: " + std::to_string(handle));
+    auto& s = it->second;
+    const size_t num_new = (size_t)keys->shape[0];
+    if (layer == 0) {
+        // Block growth on layer 0 (quantized_paged_kv_cache.rs:446-465); blocks taken before an
+        // out-of-blocks error stay in the table, as in the reference.
+        size_t remaining = num_new, fill = s.last_fill;
+        while (remaining > 0) {
+            const size_t slots = 16 - fill;
+            if (slots == 0) {
+                int32_t blk;
+                if ((rc = tq_alloc_block(c, &blk))) return rc;
+                s.table.push_back(blk);
+                fill = 0;
+                continue;
+            }
+            const size_t w = std::min(remaining, slots);
+            fill += w;
+            remaining -= w;
+        }
+        s.last_fill = fill;
+        s.len += num_new;
+    }
+    if (num_new == 0) return FB_OK;
+    if (s.len < num_new) return fail(FB_ERR_KV_CACHE, "append_kv on layer " + std::to_string(layer) + " before layer 0");
+    if ((rc = b->flush())) return rc;
+    if ((rc = tq_sync_table(c, s))) return rc;
+    const int64_t start = (int64_t)(s.len - num_new);
+    const int64_t rows = (int64_t)c->num_blocks * 16;
+    for (int kv = 0; kv < 2; ++kv) {
+        const int bits = kv == 0 ? c->kbits[layer] : c->vbits[layer];
+        int e = fb_launch_tq_compress_paged(kv == 0 ? pk : pv, keys->dtype, (const float*)c->rot[kv][layer],
+                                            (const float*)c->centroids[bits], bits, (int64_t)num_new, (int)c->heads,
+                                            (int)c->head_dim, (const int32_t*)s.dev_table.ptr, start, rows,
+                                            c->packed[kv][layer], c->norms[kv][layer], nullptr, b->stream);
+        if (e) return cuda_fail((cudaError_t)e);
+    }
+    return FB_OK;
+}
+
+int fb_tq_cache_block_table(fb_tq_cache* c, uint64_t handle, int32_t* out, size_t cap, size_t* len) {
+    if (!c || !len) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(c->be->mu);
+    auto it = c->seqs.find(handle);
+    if (it == c->seqs.end()) return fail(FB_ERR_KV_CACHE, "invalid handle: " + std::to_string(handle));
+    *len = it->second.table.size();
+    if (out) memcpy(out, it->second.table.data(), std::min(cap, *len) * sizeof(int32_t));
+    return FB_OK;
+}
+
+int fb_tq_cache_seq_len(fb_tq_cache* c, uint64_t handle, size_t* out) {
+    if (!c || !out) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(c->be->mu);
+    auto it = c->seqs.find(handle);
+    if (it == c->seqs.end()) return fail(FB_ERR_KV_CACHE, "invalid handle: " + std::to_string(handle));
+    *out = it->second.len;
+    return FB_OK;
+}
+
+int fb_tq_cache_num_free_blocks(fb_tq_cache* c, size_t* out) {
+    if (!c || !out) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(c->be->mu);
+    *out = c->free_list.size();
+    return FB_OK;
+}
+
+int fb_tq_cache_pool(fb_tq_cache* c, size_t layer, int kv, void** packed, void** norms, void** rotation,
+                     void** centroids, int* bits) {
+    if (!c || layer >= c->num_layers || kv < 0 || kv > 1) return fail(FB_ERR_KV_CACHE, "invalid layer or kv index");
+    const int bw = kv == 0 ? c->kbits[layer] : c->vbits[layer];
+    if (packed) *packed = c->packed[kv][layer];
+    if (norms) *norms = c->norms[kv][layer];
+    if (rotation) *rotation = c->rot[kv][layer];
+    if (centroids) *centroids = c->centroids[bw];
+    if (bits) *bits = bw;
+    return FB_OK;
+}
+
+int fb_tq_cache_dequant(fb_tq_cache* c, uint64_t handle, size_t layer, int kv, size_t count, const fb_tensor* out) {
+    if (!c || !out) return fail(FB_ERR_BACKEND, "null argument");
+    fb_backend* b = c->be;
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    if (layer >= c->num_layers || kv < 0 || kv > 1) return fail(FB_ERR_KV_CACHE, "invalid layer or kv index");
+    auto it = c->seqs.find(handle);
+    if (it == c->seqs.end()) return fail(FB_ERR_KV_CACHE, "invalid handle: " + std::to_string(handle));
+    if (count > it->second.len) return fail(FB_ERR_KV_CACHE, "dequant past the sequence length");
+    void* po;
+    int rc;
+    if ((rc = b->get(out, &po))) return rc;
+    if (numel(out) < (int64_t)(count * c->heads * c->head_dim)) return fail(FB_ERR_INVALID_SHAPE, "dequant: out too small");
+    if ((rc = b->flush())) return rc;
+    if ((rc = tq_sync_table(c, it->second))) return rc;
+    const int bits = kv == 0 ? c->kbits[layer] : c->vbits[layer];
+    int e = fb_launch_tq_dequant_paged(c->packed[kv][layer], c->norms[kv][layer], (const float*)c->rot[kv][layer],
+                                       (const float*)c->centroids[bits], bits, (int64_t)count, (int)c->heads,
+                                       (int)c->head_dim, (const int32_t*)it->second.dev_table.ptr, 0,
+                                       (int64_t)c->num_blocks * 16, po, out->dtype, b->stream);
+    if (e) return cuda_fail((cudaError_t)e);
+    return FB_OK;
+}
+
+}  // extern "C"

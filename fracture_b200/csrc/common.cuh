@@ -1,0 +1,107 @@
+// Shared device helpers for the fracture_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fracture_b200.h"
+
+namespace fb {
+
+// Storage types. The enum values are the reference's DType order
+// (crates/fracture-core/src/dtype.rs:5-11): FP16, FP32, BF16, INT8, INT4.
+template <typename T> struct dtype_of;
+template <> struct dtype_of<__half> { static constexpr int value = FB_FP16; };
+template <> struct dtype_of<float> { static constexpr int value = FB_FP32; };
+template <> struct dtype_of<__nv_bfloat16> { static constexpr int value = FB_BF16; };
+
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f32(float x) { return x; }
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+
+// A 16-byte vector of storage elements, the unit of every HBM access in the
+// streaming kernels (one 128-bit load/store per thread per step).
+template <typename T> struct Vec16 {
+    static constexpr int N = 16 / sizeof(T);
+    union {
+        uint4 u;
+        T e[N];
+    };
+};
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint4 ld_keep(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Plain coherent load (for buffers the same kernel also writes, e.g. in-place rope).
+__device__ __forceinline__ uint4 ld_rw(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_stream(void* p, uint4 v) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ void st_plain(void* p, uint4 v) {
+    asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Host-side helpers ----------------------------------------------------------
+
+int num_sms();  // SM count of the current device (cached per device)
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int dtype_size(int dt) {
+    switch (dt) {
+        case FB_FP16: return 2;
+        case FB_BF16: return 2;
+        case FB_FP32: return 4;
+        case FB_INT8: return 1;
+        default: return 0;
+    }
+}
+
+}  // namespace fb
+
+// Dispatch on the floating storage dtype; `body` sees a type alias `T`.
+#define FB_DISPATCH_FLOAT(dt, ...)                                   \
+    [&]() -> int {                                                   \
+        switch (dt) {                                                \
+            case FB_FP16: { using T = __half; __VA_ARGS__ }          \
+            case FB_BF16: { using T = __nv_bfloat16; __VA_ARGS__ }   \
+            case FB_FP32: { using T = float; __VA_ARGS__ }           \
+            default: return (int)cudaErrorInvalidValue;              \
+        }                                                            \
+    }()

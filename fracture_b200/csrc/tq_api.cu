@@ -1,0 +1,102 @@
+// C entry points of the TurboQuant kernels: argument checks and dispatch.
+//
+// Reference ABI: launch_turboquant_compress / launch_turboquant_decompress
+// (backends/fracture-cuda/src/ffi.rs:220-247) write/read the compact
+// [T, Hkv * P] layout; they are the paged entry points with no block table.
+
+#include "common.cuh"
+#include "tq_common.cuh"
+
+namespace fb {
+int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled);
+}
+
+using namespace fb;
+
+static bool tq_bits_ok(int bits) { return bits == 2 || bits == 3 || bits == 4 || bits == 8; }
+
+static int tq_check_common(int bits, int64_t num_tokens, int num_kv_heads, int head_dim, int64_t pool_rows) {
+    if (!tq_bits_ok(bits) || num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || head_dim > 192 || pool_rows < 0)
+        return (int)cudaErrorInvalidValue;
+    return 0;
+}
+
+extern "C" int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotation, const float* centroids,
+                                           int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                                           const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
+                                           void* packed_pool, void* norms_pool, unsigned int* err_count, void* stream) {
+    int rc = tq_check_common(bits, num_tokens, num_kv_heads, head_dim, num_pool_rows);
+    if (rc) return rc;
+    if (dtype != FB_FP16 && dtype != FB_BF16 && dtype != FB_FP32) return (int)cudaErrorInvalidValue;
+    if (start_pos < 0) return (int)cudaErrorInvalidValue;
+    if (num_tokens == 0) return 0;
+    if (!input || !rotation || !centroids || !packed_pool || !norms_pool) return (int)cudaErrorInvalidValue;
+    TqArgs a{};
+    a.input = input;
+    a.in_dtype = dtype;
+    a.rotation = rotation;
+    a.centroids = centroids;
+    a.bits = bits;
+    a.n_levels = 1 << bits;
+    a.num_tokens = num_tokens;
+    a.num_heads = num_kv_heads;
+    a.head_dim = head_dim;
+    a.block_table = block_table;
+    a.start_pos = start_pos;
+    a.pool_rows = num_pool_rows;
+    a.packed_pool = packed_pool;
+    a.norms_pool = norms_pool;
+    a.err_count = err_count;
+    bool handled = false;
+    rc = tq_compress_umma(a, (cudaStream_t)stream, &handled);
+    if (handled) return rc;
+    return tq_compress_exact(a, (cudaStream_t)stream);
+}
+
+extern "C" int fb_launch_tq_dequant_paged(const void* packed_pool, const void* norms_pool, const float* rotation,
+                                          const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
+                                          int head_dim, const int32_t* block_table, int64_t start_pos,
+                                          int64_t num_pool_rows, void* output, int dtype, void* stream) {
+    int rc = tq_check_common(bits, num_tokens, num_kv_heads, head_dim, num_pool_rows);
+    if (rc) return rc;
+    if (dtype != FB_FP16 && dtype != FB_BF16 && dtype != FB_FP32) return (int)cudaErrorInvalidValue;
+    if (start_pos < 0) return (int)cudaErrorInvalidValue;
+    if (num_tokens == 0) return 0;
+    if (!packed_pool || !norms_pool || !rotation || !centroids || !output) return (int)cudaErrorInvalidValue;
+    TqArgs a{};
+    a.rotation = rotation;
+    a.centroids = centroids;
+    a.bits = bits;
+    a.n_levels = 1 << bits;
+    a.num_tokens = num_tokens;
+    a.num_heads = num_kv_heads;
+    a.head_dim = head_dim;
+    a.block_table = block_table;
+    a.start_pos = start_pos;
+    a.pool_rows = num_pool_rows;
+    a.packed_pool = const_cast<void*>(packed_pool);
+    a.norms_pool = const_cast<void*>(norms_pool);
+    a.output = output;
+    a.out_dtype = dtype;
+    return tq_dequant_exact(a, (cudaStream_t)stream);
+}
+
+extern "C" int launch_turboquant_compress(const void* input, const float* rotation, const float* centroids,
+                                          void* packed_out, void* norms_out, int num_tokens, int num_kv_heads,
+                                          int head_dim, int n_levels, int bits, int packed_dim_per_head,
+                                          void* stream) {
+    if (!tq_bits_ok(bits) || n_levels != (1 << bits) || head_dim <= 0 ||
+        packed_dim_per_head != (head_dim * bits + 7) / 8)
+        return (int)cudaErrorInvalidValue;
+    return fb_launch_tq_compress_paged(input, FB_FP16, rotation, centroids, bits, num_tokens, num_kv_heads, head_dim,
+                                       nullptr, 0, num_tokens, packed_out, norms_out, nullptr, stream);
+}
+
+extern "C" int launch_turboquant_decompress(const void* packed_in, const void* norms_in, const float* rotation,
+                                            const float* centroids, void* output, int num_tokens, int num_kv_heads,
+                                            int head_dim, int bits, int packed_dim_per_head, void* stream) {
+    if (!tq_bits_ok(bits) || head_dim <= 0 || packed_dim_per_head != (head_dim * bits + 7) / 8)
+        return (int)cudaErrorInvalidValue;
+    return fb_launch_tq_dequant_paged(packed_in, norms_in, rotation, centroids, bits, num_tokens, num_kv_heads,
+                                      head_dim, nullptr, 0, num_tokens, output, FB_FP16, stream);
+}

@@ -1,0 +1,115 @@
+"""torch-facing wrappers of the raw kernel entry points (layers 1-2 of the C ABI).
+
+torch is used only for device memory and the current stream; every launch
+goes through ``libfracture_b200.so``. Each wrapper checks the returned
+cudaError_t and raises ``RuntimeError`` on failure.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import FB_BF16, FB_FP16, FB_FP32
+
+TORCH_DT = {torch.float16: FB_FP16, torch.bfloat16: FB_BF16, torch.float32: FB_FP32}
+
+
+def _stream(stream=None) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    return stream if isinstance(stream, int) else stream.cuda_stream
+
+
+def _ok(rc: int, name: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{name} failed: cudaError {rc}")
+
+
+def _dt(t: torch.Tensor) -> int:
+    return TORCH_DT[t.dtype]
+
+
+def silu_mul(out, gate, up, stream=None):
+    _ok(_lib.load().fb_launch_silu_mul(out.data_ptr(), gate.data_ptr(), up.data_ptr(), gate.numel(), _dt(gate),
+                                       _stream(stream)), "silu_mul")
+
+
+def add(out, a, b, stream=None):
+    _ok(_lib.load().fb_launch_add(out.data_ptr(), a.data_ptr(), b.data_ptr(), a.numel(), _dt(a), _stream(stream)), "add")
+
+
+def rmsnorm(out, x, w, eps, stream=None):
+    rows, cols = x.shape[0], x.shape[-1]
+    _ok(_lib.load().fb_launch_rmsnorm(out.data_ptr(), x.data_ptr(), w.data_ptr(), float(eps), rows, cols, _dt(x),
+                                      _stream(stream)), "rmsnorm")
+
+
+def add_rmsnorm(h, residual, w, normed, eps, stream=None):
+    rows, cols = h.shape[0], h.shape[-1]
+    _ok(_lib.load().fb_launch_add_rmsnorm(h.data_ptr(), residual.data_ptr(), w.data_ptr(), normed.data_ptr(),
+                                          float(eps), rows, cols, _dt(h), _stream(stream)), "add_rmsnorm")
+
+
+def embedding(out, table, ids, stream=None):
+    _ok(_lib.load().fb_launch_embedding(out.data_ptr(), table.data_ptr(), ids.data_ptr(), ids.numel(),
+                                        table.shape[1], table.shape[0], _dt(table), _stream(stream)), "embedding")
+
+
+def rope(q, k, positions, freqs, stream=None):
+    T, nq, hd = q.shape
+    nkv = k.shape[1]
+    _ok(_lib.load().fb_launch_rope(q.data_ptr(), k.data_ptr(), positions.data_ptr(), freqs.data_ptr(), T, nq, nkv,
+                                   hd, _dt(q), _stream(stream)), "rope")
+
+
+def tq_compress_paged(x, rotation, centroids, bits, packed_pool, norms_pool, block_table=None, start_pos=0,
+                      err=None, stream=None):
+    T, H, d = x.shape
+    rows = norms_pool.shape[0]
+    _ok(_lib.load().fb_launch_tq_compress_paged(
+        x.data_ptr(), _dt(x), rotation.data_ptr(), centroids.data_ptr(), bits, T, H, d,
+        block_table.data_ptr() if block_table is not None else None, start_pos, rows, packed_pool.data_ptr(),
+        norms_pool.data_ptr(), err.data_ptr() if err is not None else None, _stream(stream)), "tq_compress_paged")
+
+
+def tq_dequant_paged(packed_pool, norms_pool, rotation, centroids, bits, out, block_table=None, start_pos=0,
+                     stream=None):
+    T, H, d = out.shape
+    rows = norms_pool.shape[0]
+    _ok(_lib.load().fb_launch_tq_dequant_paged(
+        packed_pool.data_ptr(), norms_pool.data_ptr(), rotation.data_ptr(), centroids.data_ptr(), bits, T, H, d,
+        block_table.data_ptr() if block_table is not None else None, start_pos, rows, out.data_ptr(), _dt(out),
+        _stream(stream)), "tq_dequant_paged")
+
+
+# host tables -------------------------------------------------------------------
+
+def rope_freqs(head_dim: int, theta: float) -> np.ndarray:
+    out = np.zeros(head_dim // 2, dtype=np.float32)
+    _ok(_lib.load().fb_rope_freqs(head_dim, theta, out.ctypes.data_as(_lib.f32p)), "fb_rope_freqs")
+    return out
+
+
+def rope_freqs_llama3(head_dim, theta, factor, low, high, original_max_position) -> np.ndarray:
+    out = np.zeros(head_dim // 2, dtype=np.float32)
+    _ok(_lib.load().fb_rope_freqs_llama3(head_dim, theta, factor, low, high, original_max_position,
+                                         out.ctypes.data_as(_lib.f32p)), "fb_rope_freqs_llama3")
+    return out
+
+
+def tq_codebook(dim: int, bits: int):
+    c = np.zeros(1 << bits, dtype=np.float32)
+    b = np.zeros((1 << bits) - 1, dtype=np.float32)
+    _ok(_lib.load().fb_tq_codebook(dim, bits, c.ctypes.data_as(_lib.f32p), b.ctypes.data_as(_lib.f32p)),
+        "fb_tq_codebook")
+    return c, b
+
+
+def tq_rotation_matrix(d: int, seed: int) -> np.ndarray:
+    out = np.zeros((d, d), dtype=np.float32)
+    _ok(_lib.load().fb_tq_rotation_matrix(d, seed, out.ctypes.data_as(_lib.f32p)), "fb_tq_rotation_matrix")
+    return out

@@ -1,0 +1,248 @@
+/*
+ * fracture_b200 — C ABI of the B200 (sm_100a) implementation of Fracture's
+ * per-layer elementwise hot path and TurboQuant KV compression.
+ *
+ * Three layers of entry points, all plain C (pointers, sizes, ints):
+ *
+ *  1. The reference kernel ABI. Same names, argument lists and meaning as the
+ *     `extern "C"` kernels Fracture's CUDA backend links today
+ *     (backends/fracture-cuda/src/ffi.rs:141-249, implemented by
+ *     backends/fracture-cuda/kernels/*.cu). FP16 tensors, cudaError_t return,
+ *     enqueued on `stream`. Linking this library instead of
+ *     libfracture_kernels.a changes nothing above the FFI.
+ *
+ *  2. New kernel entry points: dtype-generic (FP16 / BF16 / FP32) versions,
+ *     the fused residual-add + RMSNorm, one-launch Q+K RoPE, and TurboQuant
+ *     compress / dequantize straight into a paged pool. Host-table builders
+ *     (RoPE frequencies incl. llama3 scaling, Lloyd-Max codebook, Haar
+ *     rotation) restate crates/fracture-core on the host.
+ *
+ *  3. A backend object that mirrors `trait Backend`
+ *     (crates/fracture-core/src/backend.rs:8-223) over opaque tensor handles,
+ *     so the Rust `CudaBackend` can be replaced by a thin shim, plus the
+ *     quantized paged KV cache of crates/fracture-engine/src/
+ *     quantized_paged_kv_cache.rs with its append_kv fused into one launch.
+ *
+ * Return values: layer 1 and 2 return a cudaError_t value (0 = success;
+ * cudaErrorInvalidValue = 1 for arguments rejected by the host-side checks,
+ * before anything is enqueued). Layer 3 returns an fb_status and records a
+ * message retrievable with fb_last_error().
+ */
+#ifndef FRACTURE_B200_H
+#define FRACTURE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Storage dtypes, in the reference's DType order (crates/fracture-core/src/dtype.rs:5-11). */
+enum fb_dtype { FB_FP16 = 0, FB_FP32 = 1, FB_BF16 = 2, FB_INT8 = 3, FB_INT4 = 4 };
+
+/* ======================================================================== */
+/* 1. Reference kernel ABI (backends/fracture-cuda/src/ffi.rs:141-249)       */
+/* ======================================================================== */
+
+/* ffi.rs:142-150; kernels/rmsnorm.cu:69-85. output = x * rsqrt(mean(x^2)+eps) * w, FP16 [rows, cols]. */
+int launch_rmsnorm(void* output, const void* input, const void* weight, float eps, int rows, int cols,
+                   void* stream);
+
+/* ffi.rs:152-162; kernels/rope.cu:51-82. In-place split-half RoPE on Q [T,Hq,d] and K [T,Hkv,d] FP16.
+ * positions: device u32 [T]; freq_table: device f32 [d/2]. One launch covers Q and K. */
+int launch_rope(void* q, void* k, const uint32_t* positions, const float* freq_table, int num_tokens,
+                int num_q_heads, int num_kv_heads, int head_dim, void* stream);
+
+/* ffi.rs:164-170; kernels/silu_mul.cu:25-38. output = silu(gate) * up, FP16 [n]. */
+int launch_silu_mul(void* output, const void* gate, const void* up, int n, void* stream);
+
+/* ffi.rs:200-208; kernels/embedding.cu:30-47. output[t] = table[ids[t]] (zero row when id >= vocab). */
+int launch_embedding(void* output, const void* table, const uint32_t* token_ids, int num_tokens,
+                     int hidden_dim, int vocab_size, void* stream);
+
+/* ffi.rs:210-216; kernels/add.cu:16-29. output = a + b, FP16 [n] (output may alias a or b). */
+int launch_add(void* output, const void* a, const void* b, int n, void* stream);
+
+/* ffi.rs:220-233; kernels/turboquant_compress.cu:189-222. input FP16 [T,Hkv,d]; rotation f32 [d,d];
+ * centroids f32 [n_levels]; packed_out u8 [T, Hkv*packed_dim_per_head]; norms_out FP16 [T,Hkv].
+ * bits: 2, 3, 4 or 8 (3 is an extension: MSB-first bit stream). */
+int launch_turboquant_compress(const void* input, const float* rotation, const float* centroids,
+                               void* packed_out, void* norms_out, int num_tokens, int num_kv_heads,
+                               int head_dim, int n_levels, int bits, int packed_dim_per_head,
+                               void* stream);
+
+/* ffi.rs:235-247; kernels/turboquant_decompress.cu:96-127. Inverse of the above into FP16 [T,Hkv,d]. */
+int launch_turboquant_decompress(const void* packed_in, const void* norms_in, const float* rotation,
+                                 const float* centroids, void* output, int num_tokens, int num_kv_heads,
+                                 int head_dim, int bits, int packed_dim_per_head, void* stream);
+
+/* ======================================================================== */
+/* 2. New kernel entry points                                               */
+/* ======================================================================== */
+
+/* Embedding gather for any storage dtype (replaces embedding.cu:7-28). */
+int fb_launch_embedding(void* output, const void* table, const uint32_t* token_ids, int64_t num_tokens,
+                        int64_t hidden_dim, int64_t vocab_size, int dtype, void* stream);
+
+/* out = a + b with one rounding to dtype (replaces add.cu:5-14). */
+int fb_launch_add(void* output, const void* a, const void* b, int64_t n, int dtype, void* stream);
+
+/* RMSNorm for any storage dtype (replaces rmsnorm.cu:10-67). */
+int fb_launch_rmsnorm(void* output, const void* input, const void* weight, float eps, int64_t rows,
+                      int64_t cols, int dtype, void* stream);
+
+/* Fused residual add + RMSNorm: h <- round(h + residual); normed <- round(h * rsqrt(mean(h^2)+eps) * w).
+ * Replaces the engine's back-to-back add(h, r, h); rmsnorm(h, w, eps, normed)
+ * (crates/fracture-engine/src/batched.rs:393-396, engine.rs:364-371). No reference counterpart. */
+int fb_launch_add_rmsnorm(void* h_inout, const void* residual, const void* weight, void* normed_out,
+                          float eps, int64_t rows, int64_t cols, int dtype, void* stream);
+
+/* In-place RoPE on Q and K in one launch, any storage dtype (replaces rope.cu:20-82). */
+int fb_launch_rope(void* q, void* k, const uint32_t* positions, const float* freq_table, int64_t num_tokens,
+                   int num_q_heads, int num_kv_heads, int head_dim, int dtype, void* stream);
+
+/* silu(gate) * up for any storage dtype (replaces silu_mul.cu:8-23). */
+int fb_launch_silu_mul(void* output, const void* gate, const void* up, int64_t n, int dtype, void* stream);
+
+/* TurboQuant compress written straight into a paged pool.
+ * input: [num_tokens, Hkv, d] (FP16 or BF16, `dtype`); rotation f32 [d,d] row-major; centroids f32 [2^bits].
+ * Token t (position start_pos + t of the sequence) lands in pool row
+ *   slot = block_table[(start_pos+t)/16]*16 + (start_pos+t)%16
+ * i.e. packed_pool[slot, h*P .. h*P+P) and norms_pool[slot, h] (FP16), P = ceil(d*bits/8), which is
+ * the per-block layout of the reference's block tensors (quantized_paged_kv_cache.rs:82-133) placed
+ * back to back. block_table == NULL means slot = t (the reference's compress-to-scratch layout).
+ * num_pool_rows bounds every slot (rejected on device: the token is skipped and *err_count bumped
+ * when err_count != NULL). Replaces turboquant_compress + 4x copy_rows per block segment
+ * (quantized_paged_kv_cache.rs:417-497). Index results equal the exact float32 statement
+ * (sequential sums, true division) bit for bit. */
+int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotation, const float* centroids,
+                                int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                                const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
+                                void* packed_pool, void* norms_pool, unsigned int* err_count, void* stream);
+
+/* TurboQuant dequantize from a paged pool into [num_tokens, Hkv, d] (`dtype` FP16/BF16/FP32):
+ * x = (Pi^T @ centroids[idx]) * norm (replaces turboquant_decompress.cu:21-94). Same slot rule. */
+int fb_launch_tq_dequant_paged(const void* packed_pool, const void* norms_pool, const float* rotation,
+                               const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
+                               int head_dim, const int32_t* block_table, int64_t start_pos,
+                               int64_t num_pool_rows, void* output, int dtype, void* stream);
+
+/* Host tables. */
+/* CudaBackend::precompute_rope_freqs (backends/fracture-cuda/src/lib.rs:133-138): out[d/2] f32. */
+int fb_rope_freqs(int head_dim, double theta, float* out);
+/* Same, then the Llama 3.1 frequency scaling rule (no reference counterpart; the reference ignores
+ * rope scaling). */
+int fb_rope_freqs_llama3(int head_dim, double theta, double factor, double low_freq_factor,
+                         double high_freq_factor, double original_max_position, float* out);
+/* LloydMaxCodebook::compute (crates/fracture-core/src/turboquant.rs:186-250): centroids[2^bits],
+ * boundaries[2^bits - 1] (either may be NULL). */
+int fb_tq_codebook(int dim, int bits, float* centroids, float* boundaries);
+/* generate_rotation_matrix (turboquant.rs:306-338): out[d*d] row-major f32. */
+int fb_tq_rotation_matrix(int d, uint64_t seed, float* out);
+
+/* ======================================================================== */
+/* 3. Backend object (mirror of trait Backend)                              */
+/* ======================================================================== */
+
+/* Status codes, one per FractureError variant the backend can raise (crates/fracture-core/src/error.rs:7-50). */
+enum fb_status {
+    FB_OK = 0,
+    FB_ERR_BACKEND = 1,          /* FractureError::Backend("CUDA error (N): msg" ...) */
+    FB_ERR_OUT_OF_MEMORY = 2,    /* FractureError::OutOfMemory */
+    FB_ERR_INVALID_SHAPE = 3,    /* FractureError::InvalidShape */
+    FB_ERR_TENSOR_NOT_FOUND = 4, /* FractureError::TensorNotFound("tensor id N") */
+    FB_ERR_UNSUPPORTED_DTYPE = 5,/* FractureError::UnsupportedDType */
+    FB_ERR_KV_CACHE = 6,         /* FractureError::KvCache */
+    FB_ERR_MODEL_CONFIG = 7      /* FractureError::ModelConfig */
+};
+
+/* DeviceTensor {id, shape, dtype} (crates/fracture-core/src/tensor.rs:14-18). Views share the id. */
+typedef struct fb_tensor {
+    uint64_t id;
+    int32_t dtype;
+    int32_t ndim;
+    int64_t shape[4];
+} fb_tensor;
+
+typedef struct fb_backend fb_backend;
+
+/* Message of the last failing fb_* call on the calling thread ("" if none). */
+const char* fb_last_error(void);
+
+/* CudaBackend::new (src/lib.rs:76-114): device, own stream. */
+int fb_backend_create(int device, fb_backend** out);
+int fb_backend_destroy(fb_backend* b);
+int fb_backend_stream(fb_backend* b, void** stream_out);
+int fb_backend_device_name(fb_backend* b, char* buf, size_t cap);
+int fb_backend_total_memory(fb_backend* b, size_t* out);
+int fb_backend_available_memory(fb_backend* b, size_t* out);
+
+/* Memory (backend.rs:11-20). */
+int fb_alloc(fb_backend* b, const int64_t* shape, int ndim, int dtype, fb_tensor* out);
+int fb_free(fb_backend* b, const fb_tensor* t);
+int fb_copy_to_device(fb_backend* b, const fb_tensor* dst, const void* src, size_t src_len);
+int fb_copy_to_host(fb_backend* b, const fb_tensor* src, void* dst, size_t dst_len);
+/* Register memory owned by the caller (not freed by the backend). */
+int fb_register_external(fb_backend* b, void* dev_ptr, const int64_t* shape, int ndim, int dtype, fb_tensor* out);
+int fb_get_ptr(fb_backend* b, const fb_tensor* t, void** out);
+
+/* Compute (backend.rs:30-117, 166-178). */
+int fb_rmsnorm(fb_backend* b, const fb_tensor* input, const fb_tensor* weight, double eps, const fb_tensor* out);
+int fb_rope(fb_backend* b, const fb_tensor* q, const fb_tensor* k, const uint32_t* positions, size_t num_positions,
+            double theta, size_t head_dim);
+int fb_silu_mul(fb_backend* b, const fb_tensor* gate, const fb_tensor* up, const fb_tensor* out);
+int fb_embedding(fb_backend* b, const uint32_t* token_ids, size_t num_tokens, const fb_tensor* table,
+                 const fb_tensor* out);
+/* add(a, b, out). When out aliases a and the next op is rmsnorm(a, ...), the two run as one fused
+ * launch (deferred add; any other use of a or b first runs the pending add). */
+int fb_add(fb_backend* b, const fb_tensor* a, const fb_tensor* bb, const fb_tensor* out);
+int fb_copy_rows(fb_backend* b, const fb_tensor* src, const fb_tensor* dst, size_t src_offset, size_t dst_offset,
+                 size_t count);
+int fb_turboquant_compress(fb_backend* b, const fb_tensor* input, const fb_tensor* rotation,
+                           const fb_tensor* centroids, uint8_t bits, const fb_tensor* packed_out,
+                           const fb_tensor* norms_out);
+int fb_synchronize(fb_backend* b);
+/* precompute_rope_freqs (src/lib.rs:133) and its llama3 variant. */
+int fb_precompute_rope_freqs(fb_backend* b, size_t head_dim, double theta);
+int fb_precompute_rope_freqs_llama3(fb_backend* b, size_t head_dim, double theta, double factor,
+                                    double low_freq_factor, double high_freq_factor, double original_max_position);
+
+/* Timers (backend.rs:132-143; src/timers.rs). */
+int fb_create_timer(fb_backend* b, uint64_t* timer);
+int fb_start_timer(fb_backend* b, uint64_t timer);
+int fb_stop_timer(fb_backend* b, uint64_t timer, float* ms);
+int fb_destroy_timer(fb_backend* b, uint64_t timer);
+
+/* Quantized paged KV cache (crates/fracture-engine/src/quantized_paged_kv_cache.rs). */
+typedef struct fb_tq_config {
+    uint8_t key_bits, value_bits, protected_bits, pad0;
+    uint32_t protected_layers;
+    uint32_t residual_tokens;
+    uint64_t seed;
+} fb_tq_config;
+
+typedef struct fb_tq_cache fb_tq_cache;
+
+int fb_tq_cache_create(fb_backend* b, size_t num_blocks, size_t num_layers, size_t num_kv_heads, size_t head_dim,
+                       const fb_tq_config* cfg, fb_tq_cache** out);
+int fb_tq_cache_destroy(fb_tq_cache* c);
+int fb_tq_cache_alloc(fb_tq_cache* c, uint64_t* handle);
+int fb_tq_cache_free(fb_tq_cache* c, uint64_t handle);
+/* keys / values: [N, Hkv, d] FP16 or BF16 tensors of the backend. One launch per K and per V. */
+int fb_tq_cache_append_kv(fb_tq_cache* c, uint64_t handle, size_t layer, const fb_tensor* keys,
+                          const fb_tensor* values);
+int fb_tq_cache_block_table(fb_tq_cache* c, uint64_t handle, int32_t* out, size_t cap, size_t* len);
+int fb_tq_cache_seq_len(fb_tq_cache* c, uint64_t handle, size_t* out);
+int fb_tq_cache_num_free_blocks(fb_tq_cache* c, size_t* out);
+/* Device pointers of one layer's pool (kv: 0 = K, 1 = V) and of its tables, for attention kernels. */
+int fb_tq_cache_pool(fb_tq_cache* c, size_t layer, int kv, void** packed, void** norms, void** rotation,
+                     void** centroids, int* bits);
+/* Dequantize a sequence's first `count` tokens of one layer into `out` ([count, Hkv, d]). */
+int fb_tq_cache_dequant(fb_tq_cache* c, uint64_t handle, size_t layer, int kv, size_t count, const fb_tensor* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FRACTURE_B200_H */

@@ -1,0 +1,200 @@
+"""GPU parity of TurboQuant compress / dequantize against the exact CPU oracle.
+
+Bar (north star): codebook indices and packed bytes bit-exact — every
+coordinate, not just all but 1e-6 of them — and the fp16 norms bit-exact;
+dequantized outputs within the FP tolerance of the float32 oracle (here they
+are bit-exact in float32 output, since the dequant kernel evaluates the same
+sequential sum). The pool placement (block table, start position) is
+bit-exact by construction and checked byte for byte.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from fracture_b200 import kernels as K
+from oracle import ops, turboquant as tq
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+TDT = {"f16": torch.float16, "bf16": torch.bfloat16}
+KIND = {"f16": tq.INPUT_F16, "bf16": tq.INPUT_BF16}
+
+
+def make_input(T, H, d, dt, seed, outliers=0.005):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, H, d)).astype(np.float32)
+    x[rng.random(x.shape) < outliers] *= 10.0
+    x = ops.round_to(x, dt)
+    return x, ops.to_storage_bytes(x, dt).reshape(x.shape)
+
+
+def dev(x, dt):
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(DEV).to(TDT[dt])
+
+
+def tables(d, bits, seed):
+    c, _ = K.tq_codebook(d, bits)
+    return K.tq_rotation_matrix(d, seed), c
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+@pytest.mark.parametrize("T,H,d", [(64, 8, 128), (4, 2, 16), (7, 3, 32), (33, 8, 128)])
+def test_compress_bit_exact_compact_layout(dt, bits, T, H, d):
+    x, raw = make_input(T, H, d, dt, seed=bits * 100 + T)
+    pi, c = tables(d, bits, 42)
+    P = tq.TurboQuantConfig.packed_dim_per_head(d, bits)
+    packed = torch.zeros((T, H * P), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((T, H), dtype=torch.float16, device=DEV)
+    K.tq_compress_paged(dev(x, dt), torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed, norms)
+    torch.cuda.synchronize()
+    pc, nc, _ = tq.compress_c(raw, KIND[dt], pi, c, bits, num_threads=4)
+    assert np.array_equal(packed.cpu().numpy(), pc)
+    assert np.array_equal(norms.cpu().numpy().view(np.uint16), nc)
+
+
+def test_reference_abi_compress_decompress_fp16():
+    """launch_turboquant_compress / _decompress with the reference's argument lists."""
+    from fracture_b200 import _lib
+
+    lib = _lib.load()
+    T, H, d, bits = 16, 8, 128, 4
+    x, raw = make_input(T, H, d, "f16", 5)
+    pi, c = tables(d, bits, 542)
+    P = d * bits // 8
+    tx = dev(x, "f16")
+    tpi, tc = torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV)
+    packed = torch.zeros((T, H * P), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((T, H), dtype=torch.float16, device=DEV)
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.launch_turboquant_compress(tx.data_ptr(), tpi.data_ptr(), tc.data_ptr(), packed.data_ptr(),
+                                          norms.data_ptr(), T, H, d, 16, bits, P, s) == 0
+    out = torch.zeros((T, H, d), dtype=torch.float16, device=DEV)
+    assert lib.launch_turboquant_decompress(packed.data_ptr(), norms.data_ptr(), tpi.data_ptr(), tc.data_ptr(),
+                                            out.data_ptr(), T, H, d, bits, P, s) == 0
+    torch.cuda.synchronize()
+    pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits)
+    assert np.array_equal(packed.cpu().numpy(), pc)
+    ref = tq.decompress_c(pc, nc, pi, c, bits, H, d)
+    ops.assert_close_fp(out.float().cpu().numpy(), ref, label="decompress fp16")
+
+
+@pytest.mark.parametrize("bits", [3, 4])
+@pytest.mark.parametrize("start_pos", [0, 5, 16])
+def test_compress_into_paged_pool(bits, start_pos):
+    """Random block table, unaligned start: every token lands in block_table[pos/16]*16 + pos%16."""
+    T, H, d, nblocks = 70, 8, 128, 40
+    x, raw = make_input(T, H, d, "f16", 11 + bits)
+    pi, c = tables(d, bits, 1042)
+    rng = np.random.default_rng(3)
+    table = rng.permutation(nblocks).astype(np.int32)
+    P = d * bits // 8
+    rows = nblocks * 16
+    packed = torch.full((rows, H * P), 0xAB, dtype=torch.uint8, device=DEV)
+    norms = torch.full((rows, H), 0x5555, dtype=torch.int16, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    K.tq_compress_paged(dev(x, "f16"), torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed,
+                        norms, block_table=torch.from_numpy(table).to(DEV), start_pos=start_pos, err=err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits)
+    exp_p = np.full((rows, H * P), 0xAB, np.uint8)
+    exp_n = np.full((rows, H), 0x5555, np.uint16)
+    pos = start_pos + np.arange(T)
+    slots = table[pos // 16] * 16 + pos % 16
+    exp_p[slots] = pc
+    exp_n[slots] = nc
+    assert np.array_equal(packed.cpu().numpy(), exp_p)
+    assert np.array_equal(norms.cpu().numpy().view(np.uint16), exp_n)
+    # dequantize back out of the pool
+    out = torch.zeros((T, H, d), dtype=torch.float32, device=DEV)
+    K.tq_dequant_paged(packed, norms, torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, out,
+                       block_table=torch.from_numpy(table).to(DEV), start_pos=start_pos)
+    torch.cuda.synchronize()
+    ref = tq.decompress_c(pc, nc, pi, c, bits, H, d)
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+def test_out_of_range_slots_are_skipped_and_counted():
+    T, H, d, bits = 20, 2, 16, 4
+    x, _ = make_input(T, H, d, "f16", 1)
+    pi, c = tables(d, bits, 42)
+    table = np.array([0, -1], dtype=np.int32)  # second block missing
+    packed = torch.zeros((16, H * 8), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((16, H), dtype=torch.float16, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    K.tq_compress_paged(dev(x, "f16"), torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed,
+                        norms, block_table=torch.from_numpy(table).to(DEV), err=err)
+    torch.cuda.synchronize()
+    assert err.item() > 0  # tokens 16..19 have no block; nothing was written for them
+    assert packed.cpu().numpy().any()
+
+
+@pytest.mark.parametrize("bits,min_cos", [(4, 0.95), (2, 0.80), (8, 0.999)])
+def test_reference_gpu_roundtrip_thresholds(bits, min_cos):
+    """turboquant_gpu.rs:87-430: head_dim 16, 2 heads, 4 tokens, rotation-matrix entries as data."""
+    d, H, T = 16, 2, 4
+    numel = T * H * d
+    side = max(int(np.ceil(np.sqrt(numel))), 2)
+    x = K.tq_rotation_matrix(side, 12345).ravel()[:numel].astype(np.float16).astype(np.float32).reshape(T, H, d)
+    pi, c = tables(d, bits, 42)
+    P = tq.TurboQuantConfig.packed_dim_per_head(d, bits)
+    packed = torch.zeros((T, H * P), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((T, H), dtype=torch.float16, device=DEV)
+    tpi, tc = torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV)
+    K.tq_compress_paged(dev(x, "f16"), tpi, tc, bits, packed, norms)
+    out = torch.zeros((T, H, d), dtype=torch.float16, device=DEV)
+    K.tq_dequant_paged(packed, norms, tpi, tc, bits, out)
+    torch.cuda.synchronize()
+    o = out.float().cpu().numpy()
+    n = norms.float().cpu().numpy()
+    for t in range(T):
+        for h in range(H):
+            a, b = x[t, h], o[t, h]
+            assert a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-10) > min_cos
+            assert abs(n[t, h] - np.linalg.norm(a)) / np.linalg.norm(a) < 0.02
+
+
+def test_zero_vectors():
+    T, H, d, bits = 3, 8, 128, 4
+    x = np.zeros((T, H, d), np.float32)
+    pi, c = tables(d, bits, 42)
+    packed = torch.zeros((T, H * 64), dtype=torch.uint8, device=DEV)
+    norms = torch.ones((T, H), dtype=torch.float16, device=DEV)
+    K.tq_compress_paged(dev(x, "f16"), torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed, norms)
+    out = torch.ones((T, H, d), dtype=torch.float16, device=DEV)
+    K.tq_dequant_paged(packed, norms, torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, out)
+    torch.cuda.synchronize()
+    assert not norms.float().cpu().numpy().any()
+    assert np.all(np.isfinite(out.float().cpu().numpy())) and np.abs(out.float().cpu().numpy()).max() < 1e-6
+    pc, nc, _ = tq.compress_c(np.zeros((T, H, d), np.uint16), tq.INPUT_F16, pi, c, bits)
+    assert np.array_equal(packed.cpu().numpy(), pc)
+
+
+@pytest.mark.parametrize("bits", [3, 4])
+def test_config4_scale_bit_exact_sample(bits):
+    """BASELINE config 4 shape (65536 x 8 x 128, 0.5% outliers x10) on the GPU; the C oracle
+    checks a 4096-token sample bit for bit, and the pool round trip is checked everywhere."""
+    T, H, d = 65536, 8, 128
+    g = torch.Generator(device=DEV).manual_seed(4)
+    x = torch.randn((T, H, d), generator=g, device=DEV)
+    x = torch.where(torch.rand((T, H, d), generator=g, device=DEV) < 0.005, x * 10.0, x).to(torch.float16)
+    pi, c = tables(d, bits, 42)
+    tpi, tc = torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV)
+    P = d * bits // 8
+    packed = torch.zeros((T, H * P), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((T, H), dtype=torch.float16, device=DEV)
+    K.tq_compress_paged(x, tpi, tc, bits, packed, norms)
+    torch.cuda.synchronize()
+    sl = slice(T - 4096, T)
+    raw = x[sl].cpu().numpy().view(np.uint16)
+    pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits, num_threads=8)
+    assert np.array_equal(packed[sl].cpu().numpy(), pc)
+    assert np.array_equal(norms[sl].cpu().numpy().view(np.uint16), nc)
+    out = torch.empty((T, H, d), dtype=torch.float16, device=DEV)
+    K.tq_dequant_paged(packed, norms, tpi, tc, bits, out)
+    torch.cuda.synchronize()
+    xf, of = x.float(), out.float()
+    cos = (xf * of).sum(-1) / (xf.norm(dim=-1) * of.norm(dim=-1) + 1e-10)
+    assert cos.min().item() > (0.97 if bits == 4 else 0.93)
