@@ -254,10 +254,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     value = world * T / (ms_step / 1e3)
     silu_avg = statistics.mean(silu_ms)
     achieved = by_silu / (silu_avg / 1e3) / 1e9
-    traffic = None
-    tf = ROOT / "profiles" / "traffic.json"
+    traffic = None  # DRAM bytes per launch from the committed ncu capture of this kernel at this size
+    tf = ROOT / "profiles" / "silu_mul_bf16_config3.md"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get("silu_mul_bf16_32768x14336")
+        import re
+
+        m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", tf.read_text())
+        traffic = int(m.group(1)) if m else None
     res = {
         "metric": METRIC,
         "value": round(value, 1),

@@ -41,9 +41,11 @@ __device__ __forceinline__ uint4 ld_stream_rw(const void* p) {
     return v;
 }
 
-// silu(g) * u in float32: g * (1 / (1 + e^-g)), reciprocal rounded to nearest.
+// silu(g) * u in float32: g / (1 + e^-g) * u with the hardware exp2 and
+// reciprocal (a few ulp of float32, far below the FP16/BF16 output rounding;
+// for g < -87 the quotient flushes to zero instead of ~1e-37).
 __device__ __forceinline__ float silu_mul_f32(float g, float u) {
-    return g * __frcp_rn(1.0f + __expf(-g)) * u;
+    return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
 // ─── silu_mul ────────────────────────────────────────────────────────────────

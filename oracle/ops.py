@@ -192,20 +192,36 @@ def silu_mul(gate: np.ndarray, up: np.ndarray, dtype: str) -> np.ndarray:
 
 # ── tolerance helpers (the north-star parity bar) ───────────────────────────
 
-def parity_report(actual: np.ndarray, expected: np.ndarray) -> dict:
-    """max-abs error relative to the reference magnitude, and cosine similarity."""
+def half_ulp(x: np.ndarray, dtype: str) -> np.ndarray:
+    """Half a unit in the last place of the storage dtype at each value (its rounding bound)."""
+    mant = {"f16": 10, "bf16": 7, "f32": 23}[dtype]
+    ax = np.maximum(np.abs(np.asarray(x, np.float64)), 2.0 ** (-14 if dtype == "f16" else -126))
+    return np.ldexp(1.0, np.floor(np.log2(ax)).astype(np.int64) - mant - 1)
+
+
+def parity_report(actual: np.ndarray, expected: np.ndarray, dtype: str | None = None) -> dict:
+    """max-abs error relative to the reference magnitude, and cosine similarity.
+
+    With ``dtype``, each element's own storage rounding (half an ulp of that
+    dtype at the expected value) is not counted as error: an output stored in
+    BF16 cannot be closer than that to a float32 reference.
+    """
     a = np.asarray(actual, np.float64).ravel()
     e = np.asarray(expected, np.float64).ravel()
     mag = float(np.max(np.abs(e))) if e.size else 0.0
-    err = float(np.max(np.abs(a - e))) if e.size else 0.0
+    diff = np.abs(a - e)
+    if dtype is not None and e.size:
+        diff = np.maximum(diff - half_ulp(e, dtype), 0.0)
+    err = float(np.max(diff)) if e.size else 0.0
     na, ne = float(np.linalg.norm(a)), float(np.linalg.norm(e))
     cos = float(np.dot(a, e) / (na * ne)) if na > 0 and ne > 0 else (1.0 if na == ne else 0.0)
     return {"max_abs": err, "rel_max_abs": err / mag if mag > 0 else err, "cosine": cos}
 
 
-def assert_close_fp(actual, expected, rel=2e-3, min_cos=0.9999, label=""):
-    """North-star FP bar: max-abs within ``rel`` x max|expected| and cosine >= ``min_cos``."""
-    r = parity_report(actual, expected)
+def assert_close_fp(actual, expected, rel=2e-3, min_cos=0.9999, label="", dtype=None):
+    """North-star FP bar against a float32-or-better computation: max-abs error within
+    ``rel`` x max|expected| beyond the output dtype's own rounding, and cosine >= ``min_cos``."""
+    r = parity_report(actual, expected, dtype)
     assert r["rel_max_abs"] <= rel, f"{label}: max-abs {r['max_abs']:.3e} = {r['rel_max_abs']:.3e} of magnitude > {rel}"
     assert r["cosine"] >= min_cos, f"{label}: cosine {r['cosine']:.7f} < {min_cos}"
     return r

@@ -88,7 +88,7 @@ def test_add_then_rmsnorm_fuses_and_matches_separate_ops(be, dt):
     be.rmsnorm(th, tw, 1e-5, tn)  # fused launch
     h_ref, _ = ops.add_rmsnorm(h0, r, w, 1e-5, npdt)
     assert np.array_equal(download(be, th), h_ref)
-    ops.assert_close_fp(download(be, tn), ops.rmsnorm(h_ref, w, 1e-5, "f32"))
+    ops.assert_close_fp(download(be, tn), ops.rmsnorm(h_ref, w, 1e-5, "f32"), dtype=npdt)
     # a pending add is flushed by any other use of the tensor
     be.add(th, tr, th)
     got = download(be, th)  # copy_to_host flushes
@@ -96,7 +96,7 @@ def test_add_then_rmsnorm_fuses_and_matches_separate_ops(be, dt):
     be.add(th, tr, th)
     be.silu_mul(th, tr, tn)  # flushes, then silu
     h2 = ops.add(ops.add(h_ref, r, npdt), r, npdt)
-    ops.assert_close_fp(download(be, tn), ops.silu_mul(h2, r, "f32"))
+    ops.assert_close_fp(download(be, tn), ops.silu_mul(h2, r, "f32"), dtype=npdt)
     for t in (th, tr, tw, tn):
         be.free(t)
 
@@ -144,8 +144,8 @@ def test_rope_requires_freq_table_then_matches_oracle():
     ref_q, ref_k = qx, kx
     for _ in range(3):
         ref_q, ref_k = ops.rope(ref_q, pos, f, "bf16"), ops.rope(ref_k, pos, f, "bf16")
-    ops.assert_close_fp(download(b, tq_), ref_q, rel=6e-3)
-    ops.assert_close_fp(download(b, tk), ref_k, rel=6e-3)
+    ops.assert_close_fp(download(b, tq_), ref_q, rel=6e-3, dtype="bf16")
+    ops.assert_close_fp(download(b, tk), ref_k, rel=6e-3, dtype="bf16")
     b.close()
 
 

@@ -1,8 +1,9 @@
 """GPU parity of the elementwise kernels against the CPU oracle (and the fixture goldens).
 
 Tolerances: the north-star bar for FP16/BF16 outputs — max-abs error within
-2e-3 of the reference magnitude and cosine >= 0.9999 against a float64
-computation (``oracle.ops.assert_close_fp``); bit-exact for the embedding
+2e-3 of the reference magnitude, beyond the output dtype's own rounding (half
+an ulp, which for BF16 alone can reach 3.9e-3 of a value), and cosine >= 0.9999
+against a float64 computation (``oracle.ops.assert_close_fp``); bit-exact for the embedding
 gather and for the residual add's stored sum. The fixture tests additionally
 apply the reference harness's own rule ``|a-e| <= atol + rtol*|e|``
 (tests/model-validation/tests/kernels.rs:118-123, :1551-1552).
@@ -47,7 +48,7 @@ def test_silu_mul(dt, n):
     out = torch.empty(n, dtype=TDT[dt], device=DEV)
     K.silu_mul(out, to_dev(g, dt), to_dev(u, dt))
     torch.cuda.synchronize()
-    ops.assert_close_fp(to_np(out), ops.silu_mul(g, u, "f32"), label=f"silu {dt} {n}")
+    ops.assert_close_fp(to_np(out), ops.silu_mul(g, u, "f32"), label=f"silu {dt} {n}", dtype=dt)
 
 
 def test_silu_mul_unaligned_and_extremes():
@@ -105,7 +106,7 @@ def test_rmsnorm(dt, rows, cols):
     out = torch.empty((rows, cols), dtype=TDT[dt], device=DEV)
     K.rmsnorm(out, to_dev(x, dt), to_dev(w, dt), 1e-5)
     torch.cuda.synchronize()
-    ops.assert_close_fp(to_np(out), ops.rmsnorm(x, w, 1e-5, "f32"), label=f"rmsnorm {dt} {rows}x{cols}")
+    ops.assert_close_fp(to_np(out), ops.rmsnorm(x, w, 1e-5, "f32"), label=f"rmsnorm {dt} {rows}x{cols}", dtype=dt)
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
@@ -120,7 +121,7 @@ def test_add_rmsnorm_fused(dt, rows, cols):
     torch.cuda.synchronize()
     h_ref, _ = ops.add_rmsnorm(h, r, w, 1e-5, dt)
     assert np.array_equal(to_np(th), h_ref)  # the stored residual is bit-exact
-    ops.assert_close_fp(to_np(normed), ops.rmsnorm(h_ref, w, 1e-5, "f32"), label=f"add_rmsnorm {dt}")
+    ops.assert_close_fp(to_np(normed), ops.rmsnorm(h_ref, w, 1e-5, "f32"), label=f"add_rmsnorm {dt}", dtype=dt)
 
 
 def test_rmsnorm_zero_rows():
@@ -150,8 +151,8 @@ def test_rope(dt, T, nq, nkv, hd, maxpos, llama3):
     tq_, tk = to_dev(q, dt), to_dev(k, dt)
     K.rope(tq_, tk, torch.from_numpy(pos.view(np.int32)).to(DEV), torch.from_numpy(f).to(DEV))
     torch.cuda.synchronize()
-    ops.assert_close_fp(to_np(tq_), ops.rope(q, pos, f, "f32"), label="rope q")
-    ops.assert_close_fp(to_np(tk), ops.rope(k, pos, f, "f32"), label="rope k")
+    ops.assert_close_fp(to_np(tq_), ops.rope(q, pos, f, "f32"), label="rope q", dtype=dt)
+    ops.assert_close_fp(to_np(tk), ops.rope(k, pos, f, "f32"), label="rope k", dtype=dt)
 
 
 # ── reference fixture goldens through the raw kernels ───────────────────────
