@@ -128,6 +128,10 @@ int fb_launch_tq_dequant_paged(const void* packed_pool, const void* norms_pool, 
                                int head_dim, const int32_t* block_table, int64_t start_pos,
                                int64_t num_pool_rows, void* output, int dtype, void* stream);
 
+/* Number of bounded waits that timed out inside the tensor-core TurboQuant kernel since the library
+ * was loaded (0 in normal operation; a timeout abandons the launch's remaining tiles). */
+unsigned int fb_tq_timeouts(void);
+
 /* Host tables. */
 /* CudaBackend::precompute_rope_freqs (backends/fracture-cuda/src/lib.rs:133-138): out[d/2] f32. */
 int fb_rope_freqs(int head_dim, double theta, float* out);

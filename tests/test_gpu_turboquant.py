@@ -198,3 +198,56 @@ def test_config4_scale_bit_exact_sample(bits):
     xf, of = x.float(), out.float()
     cos = (xf * of).sum(-1) / (xf.norm(dim=-1) * of.norm(dim=-1) + 1e-10)
     assert cos.min().item() > (0.97 if bits == 4 else 0.93)
+
+
+# ── tensor-core path (head_dim 128, 2/3/4 bits, FP16/BF16): full-size bit-exactness ──
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("bits", [2, 3, 4])
+def test_tensor_core_path_bit_exact_many_tiles(dt, bits):
+    """8219 tokens x 8 heads = 513+ tiles (last one partial), every vector checked against
+    the exact C statement; the kernel must not have timed out."""
+    from fracture_b200 import _lib
+
+    T, H, d = 8219, 8, 128
+    x, raw = make_input(T, H, d, dt, seed=77 + bits)
+    pi, c = tables(d, bits, 5042)
+    P = d * bits // 8
+    packed = torch.zeros((T, H * P), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((T, H), dtype=torch.float16, device=DEV)
+    before = _lib.load().fb_tq_timeouts()
+    K.tq_compress_paged(dev(x, dt), torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed, norms)
+    torch.cuda.synchronize()
+    assert _lib.load().fb_tq_timeouts() == before
+    pc, nc, _ = tq.compress_c(raw, KIND[dt], pi, c, bits, num_threads=8)
+    got_p, got_n = packed.cpu().numpy(), norms.cpu().numpy().view(np.uint16)
+    bad_rows = np.nonzero(np.any(got_p != pc, axis=1) | np.any(got_n != nc, axis=1))[0]
+    assert bad_rows.size == 0, f"{bad_rows.size} token rows differ, first {bad_rows[:5]}"
+
+
+def test_tensor_core_path_adversarial_vectors():
+    """Vectors aligned with rows of Pi (|y_i| = 1), zero vectors, tiny and huge fp16 values,
+    and vectors placed exactly on decision boundaries."""
+    T, H, d, bits = 40, 8, 128, 4
+    pi, c = tables(d, bits, 42)
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((T, H, d)).astype(np.float32)
+    x[0, :] = pi[:H, :]            # x = row i of Pi  ->  y = e_i
+    x[1, :] = 0.0
+    x[2, :] = 6e-8                 # fp16 subnormal
+    x[3, :] = 60000.0
+    x[4, :, :] = 0.0
+    x[4, :, 0] = 1.0               # y = Pi[:, 0]
+    mids = (c[:-1] + c[1:]) / 2
+    for h in range(H):             # y lands on a boundary (to fp16 rounding of x)
+        y = rng.choice(mids, d)
+        x[5, h] = pi.T.astype(np.float64) @ y
+    x = ops.round_to(x, "f16")
+    raw = ops.to_storage_bytes(x, "f16").reshape(x.shape)
+    packed = torch.zeros((T, H * 64), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((T, H), dtype=torch.float16, device=DEV)
+    K.tq_compress_paged(dev(x, "f16"), torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed, norms)
+    torch.cuda.synchronize()
+    pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits)
+    assert np.array_equal(packed.cpu().numpy(), pc)
+    assert np.array_equal(norms.cpu().numpy().view(np.uint16), nc)
