@@ -53,6 +53,16 @@ constexpr float kWindowPad = 1e-4f; // a bin owns the boundaries within this dis
 constexpr int THREADS = 320;
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
+// Rows whose fast-path result is not certain (a coordinate within kRiskBand of a
+// decision boundary, or a norm within kNormBand of an fp16 rounding tie) are
+// queued here and settled by tq_fixup_kernel with the exact float32 sequence.
+struct FixEntry {
+    uint32_t vi;       // vector index (token * heads + head) of the call
+    uint32_t flags;    // kFixNorm: rewrite the norm; kFixAll: every coordinate
+    uint32_t mask[4];  // coordinates to recompute
+};
+constexpr uint32_t kFixNorm = 1u, kFixAll = 2u;
+
 struct Misc {
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
@@ -60,6 +70,7 @@ struct Misc {
     uint64_t tempty[2];
     uint32_t tmem_base;
     int use_exact;  // table could not be built: every row takes the exact path
+    uint32_t zero_word; // packing word of a zero vector (every code = nearest centroid of 0)
     float cen[256];
 };
 
@@ -180,7 +191,8 @@ __device__ __forceinline__ int sw128_offset(int n, int k) {
 
 template <typename TIn, int NPARTS, int BITS>
 __global__ void __launch_bounds__(THREADS, 1)
-    tq_compress_umma_kernel(const __grid_constant__ CUtensorMap tmap, TqArgs a, int num_tiles) {
+    tq_compress_umma_kernel(const __grid_constant__ CUtensorMap tmap, TqArgs a, int num_tiles, FixEntry* fix,
+                            unsigned int* fix_count, unsigned int fix_cap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sB = base;
@@ -273,12 +285,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             en.hi = __uint_as_float(((__float_as_uint(en.hi) + 16u) & ~15u) | code_lo);
             lut[e] = en;
         }
-        if (!ok && threadIdx.x == 0) misc->use_exact = 1;
+        if (threadIdx.x == 0) {
+            if (!ok) misc->use_exact = 1;
+            const uint32_t cz = (uint32_t)nearest_centroid(0.0f, misc->cen, nlev);
+            misc->zero_word = BITS == 4 ? cz * 0x11111111u : BITS == 2 ? cz * 0x55555555u : (cz * 0x249249u) << 8;
+        }
     }
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = misc->tmem_base;
     const int use_exact = misc->use_exact;
+    const uint32_t zero_word = misc->zero_word;
     const int ntiles_cta = num_tiles > (int)blockIdx.x ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     unsigned int* err = a.err_count;
 
@@ -397,7 +414,30 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int64_t slot = tq_slot(a, vi / a.num_heads);
             if (slot < 0) continue;
             __half nh = __float2half_rn(norm_f);
+            if (ss == 0.0f) {
+                // zero vector: y = 0 for every coordinate in both statements
+#pragma unroll
+                for (int w2 = 0; w2 < 16; ++w2) pk[w2] = zero_word;
+                mask[0] = mask[1] = mask[2] = mask[3] = 0;
+                norm_amb = false;
+            }
+            bool inline_exact = false;
             if (use_exact || norm_amb || (mask[0] | mask[1] | mask[2] | mask[3])) {
+                const uint32_t qi = atomicAdd(fix_count, 1u);
+                if (qi < fix_cap) {
+                    FixEntry en;
+                    en.vi = (uint32_t)vi;
+                    en.flags = (norm_amb ? kFixNorm : 0u) | (use_exact ? kFixAll | kFixNorm : 0u);
+                    en.mask[0] = mask[0];
+                    en.mask[1] = mask[1];
+                    en.mask[2] = mask[2];
+                    en.mask[3] = mask[3];
+                    fix[qi] = en;
+                } else {
+                    inline_exact = true;  // queue full: settle here
+                }
+            }
+            if (inline_exact) {
                 // exact float32 statement for this row
                 const TIn* xr = (const TIn*)a.input + vi * D;
                 float s = 0.0f;
@@ -468,6 +508,80 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+
+// Settles queued rows with the exact float32 statement, one row per thread:
+// sequential sum of squares, norm, true division by (norm + 1e-8), and for each
+// queued coordinate the sequential dot product with its rotation row and the
+// first-minimum nearest centroid; the code is patched into the stored bit
+// stream (the row belongs to this thread alone) and the norm rewritten.
+template <typename TIn, int BITS>
+__global__ void __launch_bounds__(128) tq_fixup_kernel(TqArgs a, const FixEntry* __restrict__ fix,
+                                                       const unsigned int* __restrict__ fix_count,
+                                                       unsigned int fix_cap) {
+    __shared__ float cen[256];
+    const int nlev = 1 << BITS;
+    for (int e = threadIdx.x; e < nlev; e += blockDim.x) cen[e] = __ldg(a.centroids + e);
+    __syncthreads();
+    const unsigned int n = min(*fix_count, fix_cap);
+    const int P = (D * BITS) >> 3;
+    for (unsigned int q = blockIdx.x * blockDim.x + threadIdx.x; q < n; q += gridDim.x * blockDim.x) {
+        const FixEntry en = fix[q];
+        const int64_t vi = en.vi;
+        const int64_t slot = tq_slot(a, vi / a.num_heads);
+        if (slot < 0) continue;
+        const TIn* xr = (const TIn*)a.input + vi * D;
+        float x[D];
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) {
+            Vec16<TIn> v;
+            v.u = __ldg((const uint4*)(xr + 8 * c));
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[8 * c + e] = to_f32(v.e[e]);
+        }
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < D; ++j) s = __fadd_rn(s, __fmul_rn(x[j], x[j]));
+        const float norm = __fsqrt_rn(s);
+        if (en.flags & kFixNorm) ((__half*)a.norms_pool)[slot * a.num_heads + vi % a.num_heads] = __float2half_rn(norm);
+        const float den = __fadd_rn(norm, 1e-8f);
+#pragma unroll
+        for (int j = 0; j < D; ++j) x[j] = __fdiv_rn(x[j], den);
+        uint8_t* row = (uint8_t*)a.packed_pool + (slot * a.num_heads + vi % a.num_heads) * P;
+        for (int c = 0; c < 4; ++c) {
+            uint32_t m = (en.flags & kFixAll) ? 0xffffffffu : en.mask[c];
+            while (m) {
+                const int i = c * 32 + __ffs(m) - 1;
+                m &= m - 1;
+                const float4* prow = (const float4*)(a.rotation + i * D);
+                float y = 0.0f;
+#pragma unroll
+                for (int jb = 0; jb < 4; ++jb) {
+                    float4 p[8];
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) p[t] = __ldg(prow + jb * 8 + t);
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) {
+                        y = __fadd_rn(y, __fmul_rn(p[t].x, x[jb * 32 + 4 * t + 0]));
+                        y = __fadd_rn(y, __fmul_rn(p[t].y, x[jb * 32 + 4 * t + 1]));
+                        y = __fadd_rn(y, __fmul_rn(p[t].z, x[jb * 32 + 4 * t + 2]));
+                        y = __fadd_rn(y, __fmul_rn(p[t].w, x[jb * 32 + 4 * t + 3]));
+                    }
+                }
+                const uint32_t code = (uint32_t)nearest_centroid(y, cen, nlev);
+                // MSB-first: bit b of the code (from its top) is stream bit i*BITS + b
+#pragma unroll
+                for (int b = 0; b < BITS; ++b) {
+                    const int bp = i * BITS + b;
+                    const uint8_t bit = (uint8_t)(0x80u >> (bp & 7));
+                    uint8_t byte = row[bp >> 3];
+                    byte = ((code >> (BITS - 1 - b)) & 1u) ? (uint8_t)(byte | bit) : (uint8_t)(byte & ~bit);
+                    row[bp >> 3] = byte;
+                }
+            }
+        }
+    }
+}
+
 }  // namespace umma
 
 // ── host side ───────────────────────────────────────────────────────────────
@@ -493,6 +607,41 @@ static bool device_is_sm100() {
     return major == 10 && minor == 0;
 }
 
+// Fixup queue: one per device, grown to the largest call (24 bytes per vector), kept for the
+// life of the process. The queue is consumed by the fixup kernel of the same launch sequence on
+// the same stream; calls on different streams of one device must not overlap.
+struct FixWorkspace {
+    void* ptr = nullptr;
+    size_t cap = 0;  // entries
+};
+
+static int fix_workspace(int64_t nvec, umma::FixEntry** entries, unsigned int** count, unsigned int* cap) {
+    static FixWorkspace ws[64];
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(mu);
+    FixWorkspace& w = ws[dev];
+    const size_t want = (size_t)std::max<int64_t>(nvec, 4096);
+    if (w.cap < want) {
+        if (w.ptr) {
+            e = cudaFree(w.ptr);
+            if (e != cudaSuccess) return (int)e;
+        }
+        w.ptr = nullptr;
+        w.cap = 0;
+        e = cudaMalloc(&w.ptr, 256 + want * sizeof(umma::FixEntry));
+        if (e != cudaSuccess) return (int)e;
+        w.cap = want;
+    }
+    *count = (unsigned int*)w.ptr;
+    *entries = (umma::FixEntry*)((char*)w.ptr + 256);
+    *cap = (unsigned int)std::min<size_t>(w.cap, 0xffffffffu);
+    return 0;
+}
+
 template <typename TIn, int NPARTS, int BITS>
 static int launch_umma(const TqArgs& a, cudaStream_t s) {
     auto encode = get_encode();
@@ -508,13 +657,23 @@ static int launch_umma(const TqArgs& a, cudaStream_t s) {
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return (int)cudaErrorInvalidValue;
-    const int smem = umma::Smem::bytes(NPARTS);
+    umma::FixEntry* fix;
+    unsigned int* fix_count;
+    unsigned int fix_cap;
+    int rc = fix_workspace(nvec, &fix, &fix_count, &fix_cap);
+    if (rc) return rc;
+    cudaError_t e = cudaMemsetAsync(fix_count, 0, sizeof(unsigned int), s);
+    if (e != cudaSuccess) return (int)e;
+    constexpr int smem = umma::Smem::bytes(NPARTS);
     auto kern = umma::tq_compress_umma_kernel<TIn, NPARTS, BITS>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
     const int num_tiles = (int)((nvec + umma::TILE - 1) / umma::TILE);
     const int grid = std::max(1, std::min(num_tiles, num_sms()));
-    kern<<<grid, umma::THREADS, smem, s>>>(map, a, num_tiles);
+    kern<<<grid, umma::THREADS, smem, s>>>(map, a, num_tiles, fix, fix_count, fix_cap);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+    umma::tq_fixup_kernel<TIn, BITS><<<num_sms() * 2, 128, 0, s>>>(a, fix, fix_count, fix_cap);
     return (int)cudaGetLastError();
 }
 

@@ -197,7 +197,7 @@ def test_config4_scale_bit_exact_sample(bits):
     torch.cuda.synchronize()
     xf, of = x.float(), out.float()
     cos = (xf * of).sum(-1) / (xf.norm(dim=-1) * of.norm(dim=-1) + 1e-10)
-    assert cos.min().item() > (0.97 if bits == 4 else 0.93)
+    assert cos.min().item() > (0.95 if bits == 4 else 0.90)  # turboquant_gpu.rs: >0.95 at 4 bits
 
 
 # ── tensor-core path (head_dim 128, 2/3/4 bits, FP16/BF16): full-size bit-exactness ──
