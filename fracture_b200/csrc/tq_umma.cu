@@ -47,8 +47,8 @@ constexpr int KBLK_BYTES = TILE * 128;    // one K-block (64 elements) of a 128-
 constexpr int TILE_BYTES = 2 * KBLK_BYTES;  // 32 KB
 constexpr int NB = 64;              // decision-table bins over [-kRange, kRange]
 constexpr float kRange = 0.54f;
-constexpr float kRiskBand = 4e-6f;  // |y - boundary| below this: settle with the exact sequence
-constexpr float kNormBand = 1e-5f;  // relative band around fp16 rounding ties of the norm
+constexpr float kRiskBand = 2.5e-6f;  // |y - boundary| below this: settle with the exact sequence
+constexpr float kNormBand = 2e-6f;  // relative band around fp16 rounding ties of the norm
 constexpr float kWindowPad = 1e-4f; // a bin owns the boundaries within this distance of its edges
 constexpr int THREADS = 320;
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
@@ -168,6 +168,23 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t set_ge(float a, float b) {
     uint32_t r;
@@ -360,24 +377,29 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!mbar_wait(&misc->tfull[eg], (i >> 1) & 1, err)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + (uint32_t)(eg * D) + ((uint32_t)(quarter * 32) << 16);
-            float v[32];
-            // pass 1: |Pi x|^2 = |x|^2
-            float ss = 0.0f;
+            // The whole accumulator row (128 fp32) in registers: 4 TMEM loads, one wait,
+            // then the buffer goes back to the MMA warp before any arithmetic.
+            float v[D];
+            tmem_ld32_nowait(taddr + 0, v + 0);
+            tmem_ld32_nowait(taddr + 32, v + 32);
+            tmem_ld32_nowait(taddr + 64, v + 64);
+            tmem_ld32_nowait(taddr + 96, v + 96);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&misc->tempty[eg]);
+            // |Pi x|^2 = |x|^2 (four partial sums for ILP; the exact norm is settled later when needed)
+            float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                tmem_ld32(taddr + c * 32, v);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
-            }
+            for (int j = 0; j < D; ++j) s4[j & 3] = fmaf(v[j], v[j], s4[j & 3]);
+            const float ss = (s4[0] + s4[1]) + (s4[2] + s4[3]);
             const float norm_f = sqrtf(ss);
             const float kr = __frcp_rn(norm_f + 1e-8f) * inv2r;
             bool norm_amb = __float2half_rn(norm_f * (1.0f - kNormBand)) != __float2half_rn(norm_f * (1.0f + kNormBand));
-            // pass 2: codes
             uint32_t pk[16];
             uint32_t mask[4];
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-                tmem_ld32(taddr + c * 32, v);
                 uint32_t m = 0;
                 constexpr int G = (BITS == 2) ? 16 : 8;  // codes per packing word
 #pragma unroll
@@ -390,7 +412,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         if constexpr (BITS == 4) j = g * G + (q ^ 1);
                         else if constexpr (BITS == 2) j = g * G + ((q & ~3) | (3 - (q & 3)));
                         else j = g * G + (G - 1 - q);
-                        const float t = __saturatef(fmaf(v[j], kr, 0.5f));
+                        const float t = __saturatef(fmaf(v[c * 32 + j], kr, 0.5f));
                         const float u = fmaf(t, (float)(NB - 1), magic);
                         const uint32_t addr = __float_as_uint(u) * 256u + lut_lane;
                         float lo, hi;
@@ -404,9 +426,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 mask[c] = m;
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&misc->tempty[eg]);
 
             const int64_t vi = (int64_t)tile * TILE + row;
             const int64_t nvec = a.num_tokens * a.num_heads;
@@ -543,10 +562,19 @@ __global__ void __launch_bounds__(128) tq_fixup_kernel(TqArgs a, const FixEntry*
         for (int j = 0; j < D; ++j) s = __fadd_rn(s, __fmul_rn(x[j], x[j]));
         const float norm = __fsqrt_rn(s);
         if (en.flags & kFixNorm) ((__half*)a.norms_pool)[slot * a.num_heads + vi % a.num_heads] = __float2half_rn(norm);
+        const bool any = (en.flags & kFixAll) || (en.mask[0] | en.mask[1] | en.mask[2] | en.mask[3]);
+        if (!any) continue;
         const float den = __fadd_rn(norm, 1e-8f);
 #pragma unroll
         for (int j = 0; j < D; ++j) x[j] = __fdiv_rn(x[j], den);
-        uint8_t* row = (uint8_t*)a.packed_pool + (slot * a.num_heads + vi % a.num_heads) * P;
+        // the row's packed bytes, patched in registers and written back once
+        uint4* rowp = (uint4*)((uint8_t*)a.packed_pool + (slot * a.num_heads + vi % a.num_heads) * P);
+        uint32_t wds[16];
+#pragma unroll
+        for (int q4 = 0; q4 < P / 16; ++q4) {
+            const uint4 t4 = rowp[q4];
+            wds[4 * q4] = t4.x; wds[4 * q4 + 1] = t4.y; wds[4 * q4 + 2] = t4.z; wds[4 * q4 + 3] = t4.w;
+        }
         for (int c = 0; c < 4; ++c) {
             uint32_t m = (en.flags & kFixAll) ? 0xffffffffu : en.mask[c];
             while (m) {
@@ -568,17 +596,22 @@ __global__ void __launch_bounds__(128) tq_fixup_kernel(TqArgs a, const FixEntry*
                     }
                 }
                 const uint32_t code = (uint32_t)nearest_centroid(y, cen, nlev);
-                // MSB-first: bit b of the code (from its top) is stream bit i*BITS + b
+                // MSB-first stream bit bp lives in byte bp>>3 at bit 7-(bp&7); bytes are little-endian in words
 #pragma unroll
                 for (int b = 0; b < BITS; ++b) {
                     const int bp = i * BITS + b;
-                    const uint8_t bit = (uint8_t)(0x80u >> (bp & 7));
-                    uint8_t byte = row[bp >> 3];
-                    byte = ((code >> (BITS - 1 - b)) & 1u) ? (uint8_t)(byte | bit) : (uint8_t)(byte & ~bit);
-                    row[bp >> 3] = byte;
+                    const int byte = bp >> 3;
+                    const uint32_t bit = 1u << (8 * (byte & 3) + 7 - (bp & 7));
+                    const uint32_t on = (code >> (BITS - 1 - b)) & 1u;
+#pragma unroll
+                    for (int w2 = 0; w2 < 16; ++w2)
+                        if (w2 == (byte >> 2)) wds[w2] = on ? (wds[w2] | bit) : (wds[w2] & ~bit);
                 }
             }
         }
+#pragma unroll
+        for (int q4 = 0; q4 < P / 16; ++q4)
+            rowp[q4] = make_uint4(wds[4 * q4], wds[4 * q4 + 1], wds[4 * q4 + 2], wds[4 * q4 + 3]);
     }
 }
 
