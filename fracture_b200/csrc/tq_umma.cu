@@ -196,7 +196,8 @@ __device__ __forceinline__ uint32_t set_ge(float a, float b) {
 // warp on 32 different banks. lo/hi are in t units (t = y / (2 R) + 0.5);
 // hi's low 4 mantissa bits hold the code of the lower side of the bin's boundary.
 struct LutEntry {
-    float lo, hi;
+    float mid;      // boundary in t units (4.0: the bin holds no boundary)
+    uint32_t base;  // code below the boundary (the code of the whole bin when mid = 4.0)
 };
 
 // Byte offset in the SW128 K-major image of element (row n, column k) of a
@@ -207,7 +208,7 @@ __device__ __forceinline__ int sw128_offset(int n, int k) {
 }
 
 template <typename TIn, int NPARTS, int BITS>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __maxnreg__(200)
     tq_compress_umma_kernel(const __grid_constant__ CUtensorMap tmap, TqArgs a, int num_tiles, FixEntry* fix,
                             unsigned int* fix_count, unsigned int fix_cap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -287,25 +288,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (m >= ylo - kWindowPad && m <= yhi + kWindowPad) owner = k;
             }
             LutEntry en;
-            uint32_t code_lo;
             if (owner >= 0) {
                 const float m = 0.5f * (misc->cen[owner] + misc->cen[owner + 1]);
-                en.lo = (m - kRiskBand) * inv2r + 0.5f;
-                en.hi = (m + kRiskBand) * inv2r + 0.5f;
-                code_lo = (uint32_t)owner;
+                en.mid = m * inv2r + 0.5f;
+                en.base = (uint32_t)owner;
             } else {
-                en.lo = 4.0f;
-                en.hi = 4.0f;
-                code_lo = (uint32_t)below;
+                en.mid = 4.0f;
+                en.base = (uint32_t)below;
             }
-            // hi moves up by 16 ulps, then carries the code in its low 4 bits.
-            en.hi = __uint_as_float(((__float_as_uint(en.hi) + 16u) & ~15u) | code_lo);
             lut[e] = en;
         }
         if (threadIdx.x == 0) {
             if (!ok) misc->use_exact = 1;
             const uint32_t cz = (uint32_t)nearest_centroid(0.0f, misc->cen, nlev);
-            misc->zero_word = BITS == 4 ? cz * 0x11111111u : BITS == 2 ? cz * 0x55555555u : (cz * 0x249249u) << 8;
+            misc->zero_word = BITS == 4 ? cz * 0x11111111u : BITS == 2 ? cz * 0x55555555u : cz * 0x249249u;
         }
     }
     __syncthreads();
@@ -396,35 +392,47 @@ __global__ void __launch_bounds__(THREADS, 1)
             const float norm_f = sqrtf(ss);
             const float kr = __frcp_rn(norm_f + 1e-8f) * inv2r;
             bool norm_amb = __float2half_rn(norm_f * (1.0f - kNormBand)) != __float2half_rn(norm_f * (1.0f + kNormBand));
+            // Codes. Per coordinate: t = y/(2R) + 0.5 (saturated), its table bin, the bin's
+            // boundary `mid`; code = base + (t > mid) from the sign of mid - t; packed
+            // big-endian by integer multiply-add (first code in the top bits).
+            constexpr int G = (BITS == 2) ? 16 : 8;  // codes per packing word
+            const float band_t = kRiskBand * inv2r;
             uint32_t pk[16];
-            uint32_t mask[4];
+            float dmin = 1.0f;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t m = 0;
-                constexpr int G = (BITS == 2) ? 16 : 8;  // codes per packing word
+            for (int w2 = 0; w2 < D / G; ++w2) {
+                uint32_t wd = 0;
 #pragma unroll
-                for (int g = 0; g < 32 / G; ++g) {
-                    uint32_t wd = 0;
-#pragma unroll
-                    for (int q = 0; q < G; ++q) {
-                        // processing order makes the funnel-shifted word the MSB-first byte stream
-                        int j;
-                        if constexpr (BITS == 4) j = g * G + (q ^ 1);
-                        else if constexpr (BITS == 2) j = g * G + ((q & ~3) | (3 - (q & 3)));
-                        else j = g * G + (G - 1 - q);
-                        const float t = __saturatef(fmaf(v[c * 32 + j], kr, 0.5f));
-                        const float u = fmaf(t, (float)(NB - 1), magic);
-                        const uint32_t addr = __float_as_uint(u) * 256u + lut_lane;
-                        float lo, hi;
-                        asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(lo), "=f"(hi) : "r"(addr));
-                        const uint32_t r = set_ge(t, lo);
-                        if (t < hi) m |= r & (1u << j);
-                        const uint32_t code = __float_as_uint(hi) - r;
-                        wd = __funnelshift_r(wd, code, BITS);
-                    }
-                    pk[c * (32 / G) + g] = wd;
+                for (int q = 0; q < G; ++q) {
+                    const int j = w2 * G + q;
+                    float t;
+                    asm("fma.rn.sat.f32 %0, %1, %2, 0f3F000000;" : "=f"(t) : "f"(v[j]), "f"(kr));
+                    const float u = fmaf(t, (float)(NB - 1), magic);
+                    const uint32_t addr = __float_as_uint(u) * 256u + lut_lane;
+                    float mid;
+                    uint32_t base;
+                    asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
+                    const float dd = mid - t;
+                    dmin = fminf(dmin, fabsf(dd));
+                    const uint32_t code = base + (__float_as_uint(dd) >> 31);
+                    wd = wd * (1u << BITS) + code;
                 }
-                mask[c] = m;
+                pk[w2] = wd;
+            }
+            uint32_t mask[4] = {0u, 0u, 0u, 0u};
+            if (dmin < band_t) {
+                // rare: list the coordinates within the band
+#pragma unroll
+                for (int j = 0; j < D; ++j) {
+                    float t;
+                    asm("fma.rn.sat.f32 %0, %1, %2, 0f3F000000;" : "=f"(t) : "f"(v[j]), "f"(kr));
+                    const float u = fmaf(t, (float)(NB - 1), magic);
+                    const uint32_t addr = __float_as_uint(u) * 256u + lut_lane;
+                    float mid;
+                    uint32_t base;
+                    asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
+                    if (fabsf(mid - t) < band_t) mask[j >> 5] |= 1u << (j & 31);
+                }
             }
 
             const int64_t vi = (int64_t)tile * TILE + row;
@@ -477,14 +485,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                         float y = 0.0f;
                         for (int j = 0; j < D; ++j) y = __fadd_rn(y, __fmul_rn(__ldg(prow + j), __fdiv_rn(to_f32(xr[j]), den)));
                         const uint32_t code = (uint32_t)nearest_centroid(y, misc->cen, nlev);
-                        // patch the code into its packing word
+                        // patch the code into its packing word (first code in the top bits)
                         constexpr int G = (BITS == 2) ? 16 : 8;
                         const int widx = i_coord / G, q = i_coord % G;
-                        int pos;  // processing position of coordinate q within its word
-                        if constexpr (BITS == 4) pos = q ^ 1;
-                        else if constexpr (BITS == 2) pos = (q & ~3) | (3 - (q & 3));
-                        else pos = G - 1 - q;
-                        const int sh = 32 - BITS * (G - pos);
+                        const int sh = BITS * (G - 1 - q);
                         const uint32_t clr = ~(((1u << BITS) - 1u) << sh);
 #pragma unroll
                         for (int w2 = 0; w2 < 16; ++w2)
@@ -494,24 +498,23 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             ((__half*)a.norms_pool)[slot * a.num_heads + vi % a.num_heads] = nh;
             uint8_t* dst = (uint8_t*)a.packed_pool + (slot * a.num_heads + vi % a.num_heads) * P;
-            if constexpr (BITS == 4) {
+            if constexpr (BITS == 4 || BITS == 2) {
+                // big-endian words -> byte stream
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4)
-                    *(uint4*)(dst + 16 * q4) = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-            } else if constexpr (BITS == 2) {
-#pragma unroll
-                for (int q4 = 0; q4 < 2; ++q4)
-                    *(uint4*)(dst + 16 * q4) = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+                for (int q4 = 0; q4 < P / 16; ++q4)
+                    *(uint4*)(dst + 16 * q4) =
+                        make_uint4(__byte_perm(pk[4 * q4], 0, 0x0123), __byte_perm(pk[4 * q4 + 1], 0, 0x0123),
+                                   __byte_perm(pk[4 * q4 + 2], 0, 0x0123), __byte_perm(pk[4 * q4 + 3], 0, 0x0123));
             } else {
-                // 3-bit: each word holds 24 stream bits in its top three bytes (big-endian);
+                // 3-bit: each word holds 24 stream bits (bits 23..0, first code on top);
                 // four words -> three little-endian output words.
                 uint32_t o[12];
 #pragma unroll
                 for (int q4 = 0; q4 < 4; ++q4) {
                     const uint32_t w0 = pk[4 * q4], w1 = pk[4 * q4 + 1], w2 = pk[4 * q4 + 2], w3 = pk[4 * q4 + 3];
-                    o[3 * q4 + 0] = __byte_perm(w0, w1, 0x7123);  // w0.b3 w0.b2 w0.b1 w1.b3
-                    o[3 * q4 + 1] = __byte_perm(w1, w2, 0x6712);  // w1.b2 w1.b1 w2.b3 w2.b2
-                    o[3 * q4 + 2] = __byte_perm(w2, w3, 0x5671);  // w2.b1 w3.b3 w3.b2 w3.b1
+                    o[3 * q4 + 0] = __byte_perm(w0, w1, 0x6012);  // w0.b2 w0.b1 w0.b0 w1.b2
+                    o[3 * q4 + 1] = __byte_perm(w1, w2, 0x5601);  // w1.b1 w1.b0 w2.b2 w2.b1
+                    o[3 * q4 + 2] = __byte_perm(w2, w3, 0x4560);  // w2.b0 w3.b2 w3.b1 w3.b0
                 }
 #pragma unroll
                 for (int q4 = 0; q4 < 3; ++q4)
