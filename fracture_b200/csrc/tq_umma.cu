@@ -208,7 +208,7 @@ __device__ __forceinline__ int sw128_offset(int n, int k) {
 }
 
 template <typename TIn, int NPARTS, int BITS>
-__global__ void __maxnreg__(200)
+__global__ void __maxnreg__(184)
     tq_compress_umma_kernel(const __grid_constant__ CUtensorMap tmap, TqArgs a, int num_tiles, FixEntry* fix,
                             unsigned int* fix_count, unsigned int fix_cap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
