@@ -208,7 +208,7 @@ __device__ __forceinline__ int sw128_offset(int n, int k) {
 }
 
 template <typename TIn, int NPARTS, int BITS>
-__global__ void __maxnreg__(184)
+__global__ void __launch_bounds__(THREADS, 1)
     tq_compress_umma_kernel(const __grid_constant__ CUtensorMap tmap, TqArgs a, int num_tiles, FixEntry* fix,
                             unsigned int* fix_count, unsigned int fix_cap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -373,68 +373,77 @@ __global__ void __maxnreg__(184)
             if (!mbar_wait(&misc->tfull[eg], (i >> 1) & 1, err)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + (uint32_t)(eg * D) + ((uint32_t)(quarter * 32) << 16);
-            // The whole accumulator row (128 fp32) in registers: 4 TMEM loads, one wait,
-            // then the buffer goes back to the MMA warp before any arithmetic.
-            float v[D];
-            tmem_ld32_nowait(taddr + 0, v + 0);
-            tmem_ld32_nowait(taddr + 32, v + 32);
-            tmem_ld32_nowait(taddr + 64, v + 64);
-            tmem_ld32_nowait(taddr + 96, v + 96);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&misc->tempty[eg]);
-            // |Pi x|^2 = |x|^2 (four partial sums for ILP; the exact norm is settled later when needed)
+            // Pass 1: |Pi x|^2 = |x|^2 from the accumulator row (four partial sums for ILP;
+            // the exact norm is settled later when needed).
+            float v[64];
             float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int j = 0; j < D; ++j) s4[j & 3] = fmaf(v[j], v[j], s4[j & 3]);
+            for (int h = 0; h < 2; ++h) {
+                tmem_ld32_nowait(taddr + h * 64, v);
+                tmem_ld32_nowait(taddr + h * 64 + 32, v + 32);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 64; ++j) s4[j & 3] = fmaf(v[j], v[j], s4[j & 3]);
+            }
             const float ss = (s4[0] + s4[1]) + (s4[2] + s4[3]);
             const float norm_f = sqrtf(ss);
             const float kr = __frcp_rn(norm_f + 1e-8f) * inv2r;
             bool norm_amb = __float2half_rn(norm_f * (1.0f - kNormBand)) != __float2half_rn(norm_f * (1.0f + kNormBand));
-            // Codes. Per coordinate: t = y/(2R) + 0.5 (saturated), its table bin, the bin's
-            // boundary `mid`; code = base + (t > mid) from the sign of mid - t; packed
-            // big-endian by integer multiply-add (first code in the top bits).
+            // Pass 2, codes, half a row at a time. Per coordinate: t = y/(2R) + 0.5
+            // (saturated), its table bin, the bin's boundary `mid`; code = base + (t > mid)
+            // from the sign of mid - t; packed big-endian by integer multiply-add (first
+            // code in the top bits). The accumulator goes back to the MMA warp as soon as
+            // the last half is in registers.
             constexpr int G = (BITS == 2) ? 16 : 8;  // codes per packing word
             const float band_t = kRiskBand * inv2r;
             uint32_t pk[16];
-            float dmin = 1.0f;
-#pragma unroll
-            for (int w2 = 0; w2 < D / G; ++w2) {
-                uint32_t wd = 0;
-#pragma unroll
-                for (int q = 0; q < G; ++q) {
-                    const int j = w2 * G + q;
-                    float t;
-                    asm("fma.rn.sat.f32 %0, %1, %2, 0f3F000000;" : "=f"(t) : "f"(v[j]), "f"(kr));
-                    const float u = fmaf(t, (float)(NB - 1), magic);
-                    const uint32_t addr = __float_as_uint(u) * 256u + lut_lane;
-                    float mid;
-                    uint32_t base;
-                    asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
-                    const float dd = mid - t;
-                    dmin = fminf(dmin, fabsf(dd));
-                    const uint32_t code = base + (__float_as_uint(dd) >> 31);
-                    wd = wd * (1u << BITS) + code;
-                }
-                pk[w2] = wd;
-            }
             uint32_t mask[4] = {0u, 0u, 0u, 0u};
-            if (dmin < band_t) {
-                // rare: list the coordinates within the band
 #pragma unroll
-                for (int j = 0; j < D; ++j) {
-                    float t;
-                    asm("fma.rn.sat.f32 %0, %1, %2, 0f3F000000;" : "=f"(t) : "f"(v[j]), "f"(kr));
-                    const float u = fmaf(t, (float)(NB - 1), magic);
-                    const uint32_t addr = __float_as_uint(u) * 256u + lut_lane;
-                    float mid;
-                    uint32_t base;
-                    asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
-                    if (fabsf(mid - t) < band_t) mask[j >> 5] |= 1u << (j & 31);
+            for (int h = 0; h < 2; ++h) {
+                float dmin = 1.0f;
+                tmem_ld32_nowait(taddr + h * 64, v);
+                tmem_ld32_nowait(taddr + h * 64 + 32, v + 32);
+                tmem_wait_ld();
+                if (h == 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&misc->tempty[eg]);
+                }
+#pragma unroll
+                for (int w2 = 0; w2 < 64 / G; ++w2) {
+                    uint32_t wd = 0;
+#pragma unroll
+                    for (int q = 0; q < G; ++q) {
+                        const int j = w2 * G + q;
+                        float t;
+                        asm("fma.rn.sat.f32 %0, %1, %2, 0f3F000000;" : "=f"(t) : "f"(v[j]), "f"(kr));
+                        const float u = fmaf(t, (float)(NB - 1), magic);
+                        const uint32_t addr = __float_as_uint(u) * 256u + lut_lane;
+                        float mid;
+                        uint32_t base;
+                        asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
+                        const float dd = mid - t;
+                        dmin = fminf(dmin, fabsf(dd));
+                        const uint32_t code = base + (__float_as_uint(dd) >> 31);
+                        wd = wd * (1u << BITS) + code;
+                    }
+                    pk[h * (64 / G) + w2] = wd;
+                }
+                if (dmin < band_t) {
+                    // rare: list this half's coordinates within the band
+#pragma unroll
+                    for (int j = 0; j < 64; ++j) {
+                        float t;
+                        asm("fma.rn.sat.f32 %0, %1, %2, 0f3F000000;" : "=f"(t) : "f"(v[j]), "f"(kr));
+                        const float u = fmaf(t, (float)(NB - 1), magic);
+                        const uint32_t addr = __float_as_uint(u) * 256u + lut_lane;
+                        float mid;
+                        uint32_t base;
+                        asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
+                        if (fabsf(mid - t) < band_t) mask[2 * h + (j >> 5)] |= 1u << (j & 31);
+                    }
                 }
             }
-
             const int64_t vi = (int64_t)tile * TILE + row;
             const int64_t nvec = a.num_tokens * a.num_heads;
             if (vi >= nvec) continue;
