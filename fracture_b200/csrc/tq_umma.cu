@@ -47,8 +47,8 @@ constexpr int KBLK_BYTES = TILE * 128;    // one K-block (64 elements) of a 128-
 constexpr int TILE_BYTES = 2 * KBLK_BYTES;  // 32 KB
 constexpr int NB = 64;              // decision-table bins over [-kRange, kRange]
 constexpr float kRange = 0.54f;
-constexpr float kRiskBand = 2.5e-6f;  // |y - boundary| below this: settle with the exact sequence
-constexpr float kNormBand = 2e-6f;  // relative band around fp16 rounding ties of the norm
+constexpr float kRiskBand = 1e-6f;   // |y - boundary| below this: settle with the exact sequence
+constexpr float kNormBand = 1e-6f;  // relative band around fp16 rounding ties of the norm
 constexpr float kWindowPad = 1e-4f; // a bin owns the boundaries within this distance of its edges
 constexpr int THREADS = 320;
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
@@ -540,90 +540,103 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 
-// Settles queued rows with the exact float32 statement, one row per thread:
-// sequential sum of squares, norm, true division by (norm + 1e-8), and for each
-// queued coordinate the sequential dot product with its rotation row and the
-// first-minimum nearest centroid; the code is patched into the stored bit
-// stream (the row belongs to this thread alone) and the norm rewritten.
+// Settles queued rows with the exact float32 statement, one row per warp: the
+// lanes form the squares, quotients x_j / (norm + 1e-8) and products in
+// parallel (4 coordinates each) and lane 0 adds them up in index order, so
+// every sum is the sequential float32 sum; then the first-minimum nearest
+// centroid, patched into the stored bit stream, and the norm rewritten.
+constexpr int FIX_WARPS = 4;
+
 template <typename TIn, int BITS>
-__global__ void __launch_bounds__(128) tq_fixup_kernel(TqArgs a, const FixEntry* __restrict__ fix,
-                                                       const unsigned int* __restrict__ fix_count,
-                                                       unsigned int fix_cap) {
+__global__ void __launch_bounds__(FIX_WARPS * 32) tq_fixup_kernel(TqArgs a, const FixEntry* __restrict__ fix,
+                                                                  const unsigned int* __restrict__ fix_count,
+                                                                  unsigned int fix_cap) {
     __shared__ float cen[256];
+    __shared__ float terms[FIX_WARPS][D];
     const int nlev = 1 << BITS;
     for (int e = threadIdx.x; e < nlev; e += blockDim.x) cen[e] = __ldg(a.centroids + e);
     __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* tw = terms[warp];
     const unsigned int n = min(*fix_count, fix_cap);
     const int P = (D * BITS) >> 3;
-    for (unsigned int q = blockIdx.x * blockDim.x + threadIdx.x; q < n; q += gridDim.x * blockDim.x) {
+    for (unsigned int q = blockIdx.x * FIX_WARPS + warp; q < n; q += gridDim.x * FIX_WARPS) {
         const FixEntry en = fix[q];
         const int64_t vi = en.vi;
         const int64_t slot = tq_slot(a, vi / a.num_heads);
         if (slot < 0) continue;
-        const TIn* xr = (const TIn*)a.input + vi * D;
-        float x[D];
+        const TIn* xr = (const TIn*)a.input + vi * D + 4 * lane;
+        float x[4];
 #pragma unroll
-        for (int c = 0; c < D / 8; ++c) {
-            Vec16<TIn> v;
-            v.u = __ldg((const uint4*)(xr + 8 * c));
+        for (int k = 0; k < 4; ++k) x[k] = to_f32(xr[k]);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) x[8 * c + e] = to_f32(v.e[e]);
+        for (int k = 0; k < 4; ++k) tw[4 * lane + k] = __fmul_rn(x[k], x[k]);
+        __syncwarp();
+        float den = 0.0f;
+        if (lane == 0) {
+            float s = 0.0f;
+#pragma unroll 16
+            for (int j = 0; j < D; ++j) s = __fadd_rn(s, tw[j]);
+            const float norm = __fsqrt_rn(s);
+            if (en.flags & kFixNorm)
+                ((__half*)a.norms_pool)[slot * a.num_heads + vi % a.num_heads] = __float2half_rn(norm);
+            den = __fadd_rn(norm, 1e-8f);
         }
-        float s = 0.0f;
-#pragma unroll
-        for (int j = 0; j < D; ++j) s = __fadd_rn(s, __fmul_rn(x[j], x[j]));
-        const float norm = __fsqrt_rn(s);
-        if (en.flags & kFixNorm) ((__half*)a.norms_pool)[slot * a.num_heads + vi % a.num_heads] = __float2half_rn(norm);
+        den = __shfl_sync(0xffffffffu, den, 0);
         const bool any = (en.flags & kFixAll) || (en.mask[0] | en.mask[1] | en.mask[2] | en.mask[3]);
-        if (!any) continue;
-        const float den = __fadd_rn(norm, 1e-8f);
+        if (!any) {
+            __syncwarp();
+            continue;
+        }
+        float xn[4];
 #pragma unroll
-        for (int j = 0; j < D; ++j) x[j] = __fdiv_rn(x[j], den);
-        // the row's packed bytes, patched in registers and written back once
+        for (int k = 0; k < 4; ++k) xn[k] = __fdiv_rn(x[k], den);
         uint4* rowp = (uint4*)((uint8_t*)a.packed_pool + (slot * a.num_heads + vi % a.num_heads) * P);
         uint32_t wds[16];
+        if (lane == 0) {
 #pragma unroll
-        for (int q4 = 0; q4 < P / 16; ++q4) {
-            const uint4 t4 = rowp[q4];
-            wds[4 * q4] = t4.x; wds[4 * q4 + 1] = t4.y; wds[4 * q4 + 2] = t4.z; wds[4 * q4 + 3] = t4.w;
+            for (int q4 = 0; q4 < P / 16; ++q4) {
+                const uint4 t4 = rowp[q4];
+                wds[4 * q4] = t4.x; wds[4 * q4 + 1] = t4.y; wds[4 * q4 + 2] = t4.z; wds[4 * q4 + 3] = t4.w;
+            }
         }
         for (int c = 0; c < 4; ++c) {
             uint32_t m = (en.flags & kFixAll) ? 0xffffffffu : en.mask[c];
             while (m) {
                 const int i = c * 32 + __ffs(m) - 1;
                 m &= m - 1;
-                const float4* prow = (const float4*)(a.rotation + i * D);
-                float y = 0.0f;
+                const float4 p = __ldg((const float4*)(a.rotation + i * D) + lane);
+                __syncwarp();
+                tw[4 * lane + 0] = __fmul_rn(p.x, xn[0]);
+                tw[4 * lane + 1] = __fmul_rn(p.y, xn[1]);
+                tw[4 * lane + 2] = __fmul_rn(p.z, xn[2]);
+                tw[4 * lane + 3] = __fmul_rn(p.w, xn[3]);
+                __syncwarp();
+                if (lane == 0) {
+                    float y = 0.0f;
+#pragma unroll 16
+                    for (int j = 0; j < D; ++j) y = __fadd_rn(y, tw[j]);
+                    const uint32_t code = (uint32_t)nearest_centroid(y, cen, nlev);
+                    // MSB-first stream bit bp lives in byte bp>>3 at bit 7-(bp&7); bytes little-endian in words
 #pragma unroll
-                for (int jb = 0; jb < 4; ++jb) {
-                    float4 p[8];
+                    for (int b = 0; b < BITS; ++b) {
+                        const int bp = i * BITS + b;
+                        const int byte = bp >> 3;
+                        const uint32_t bit = 1u << (8 * (byte & 3) + 7 - (bp & 7));
+                        const uint32_t on = (code >> (BITS - 1 - b)) & 1u;
 #pragma unroll
-                    for (int t = 0; t < 8; ++t) p[t] = __ldg(prow + jb * 8 + t);
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) {
-                        y = __fadd_rn(y, __fmul_rn(p[t].x, x[jb * 32 + 4 * t + 0]));
-                        y = __fadd_rn(y, __fmul_rn(p[t].y, x[jb * 32 + 4 * t + 1]));
-                        y = __fadd_rn(y, __fmul_rn(p[t].z, x[jb * 32 + 4 * t + 2]));
-                        y = __fadd_rn(y, __fmul_rn(p[t].w, x[jb * 32 + 4 * t + 3]));
+                        for (int w2 = 0; w2 < 16; ++w2)
+                            if (w2 == (byte >> 2)) wds[w2] = on ? (wds[w2] | bit) : (wds[w2] & ~bit);
                     }
-                }
-                const uint32_t code = (uint32_t)nearest_centroid(y, cen, nlev);
-                // MSB-first stream bit bp lives in byte bp>>3 at bit 7-(bp&7); bytes are little-endian in words
-#pragma unroll
-                for (int b = 0; b < BITS; ++b) {
-                    const int bp = i * BITS + b;
-                    const int byte = bp >> 3;
-                    const uint32_t bit = 1u << (8 * (byte & 3) + 7 - (bp & 7));
-                    const uint32_t on = (code >> (BITS - 1 - b)) & 1u;
-#pragma unroll
-                    for (int w2 = 0; w2 < 16; ++w2)
-                        if (w2 == (byte >> 2)) wds[w2] = on ? (wds[w2] | bit) : (wds[w2] & ~bit);
                 }
             }
         }
+        if (lane == 0) {
 #pragma unroll
-        for (int q4 = 0; q4 < P / 16; ++q4)
-            rowp[q4] = make_uint4(wds[4 * q4], wds[4 * q4 + 1], wds[4 * q4 + 2], wds[4 * q4 + 3]);
+            for (int q4 = 0; q4 < P / 16; ++q4)
+                rowp[q4] = make_uint4(wds[4 * q4], wds[4 * q4 + 1], wds[4 * q4 + 2], wds[4 * q4 + 3]);
+        }
+        __syncwarp();
     }
 }
 
@@ -718,7 +731,7 @@ static int launch_umma(const TqArgs& a, cudaStream_t s) {
     kern<<<grid, umma::THREADS, smem, s>>>(map, a, num_tiles, fix, fix_count, fix_cap);
     e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
-    umma::tq_fixup_kernel<TIn, BITS><<<num_sms() * 2, 128, 0, s>>>(a, fix, fix_count, fix_cap);
+    umma::tq_fixup_kernel<TIn, BITS><<<num_sms() * 16, umma::FIX_WARPS * 32, 0, s>>>(a, fix, fix_count, fix_cap);
     return (int)cudaGetLastError();
 }
 
