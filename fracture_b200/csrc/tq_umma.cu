@@ -50,7 +50,10 @@ constexpr float kRange = 0.54f;
 constexpr float kRiskBand = 1e-6f;   // |y - boundary| below this: settle with the exact sequence
 constexpr float kNormBand = 1e-6f;  // relative band around fp16 rounding ties of the norm
 constexpr float kWindowPad = 1e-4f; // a bin owns the boundaries within this distance of its edges
-constexpr int THREADS = 320;
+constexpr int EPI_WGS = 4;                 // epilogue warpgroups, one TMEM accumulator each
+constexpr int THREADS = 64 + EPI_WGS * 128;  // warp 0 TMA, warp 1 MMA, then the epilogue
+constexpr int VCH = 32;                    // accumulator values per thread per TMEM load round
+constexpr int MAX_REGS = 96;               // 18 warps: at most 5 per scheduler, 16K registers each
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 // Rows whose fast-path result is not certain (a coordinate within kRiskBand of a
@@ -66,8 +69,8 @@ constexpr uint32_t kFixNorm = 1u, kFixAll = 2u;
 struct Misc {
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
-    uint64_t tfull[2];
-    uint64_t tempty[2];
+    uint64_t tfull[EPI_WGS];
+    uint64_t tempty[EPI_WGS];
     uint32_t tmem_base;
     int use_exact;  // table could not be built: every row takes the exact path
     uint32_t zero_word; // packing word of a zero vector (every code = nearest centroid of 0)
@@ -208,7 +211,7 @@ __device__ __forceinline__ int sw128_offset(int n, int k) {
 }
 
 template <typename TIn, int NPARTS, int BITS>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __maxnreg__(MAX_REGS)
     tq_compress_umma_kernel(const __grid_constant__ CUtensorMap tmap, TqArgs a, int num_tiles, FixEntry* fix,
                             unsigned int* fix_count, unsigned int fix_cap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -228,7 +231,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&misc->full[s], 1);
             mbar_init(&misc->empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < EPI_WGS; ++b) {
             mbar_init(&misc->tfull[b], 1);
             mbar_init(&misc->tempty[b], 4);
         }
@@ -236,7 +239,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         misc->use_exact = 0;
     }
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
                          smem_u32(&misc->tmem_base))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -336,9 +339,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
             int done = 0;
             for (int i = 0; i < ntiles_cta; ++i) {
-                const int s = i % STAGES, buf = i & 1;
+                const int s = i % STAGES, buf = i % EPI_WGS;
                 if (!mbar_wait(&misc->full[s], (i / STAGES) & 1, err)) break;
-                if (!mbar_wait(&misc->tempty[buf], ((i >> 1) + 1) & 1, err)) break;
+                if (!mbar_wait(&misc->tempty[buf], ((i / EPI_WGS) + 1) & 1, err)) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(buf * D);
                 uint32_t acc = 0;
@@ -358,59 +361,57 @@ __global__ void __launch_bounds__(THREADS, 1)
                 done = i + 1;
             }
             // The last accumulations finish before TMEM is released.
-            if (done > 0) mbar_wait(&misc->tfull[(done - 1) & 1], ((done - 1) >> 1) & 1, err);
+            if (done > 0) mbar_wait(&misc->tfull[(done - 1) % EPI_WGS], ((done - 1) / EPI_WGS) & 1, err);
         }
     } else {
-        // ── epilogue: warps 2..9, warpgroup eg handles tiles i with i % 2 == eg ──
+        // ── epilogue: warps 2.., warpgroup eg handles tiles i with i % EPI_WGS == eg ──
         const int eg = (warp - 2) >> 2;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const int P = (D * BITS) >> 3;
         const float magic = 12582912.0f;  // 1.5 * 2^23: fma(t, NB-1, magic) holds round(t*(NB-1)) in its low bits
         const uint32_t lut_lane = smem_u32(lut) + lane * 8 - (uint32_t)__float_as_uint(magic) * 256u;
-        for (int i = eg; i < ntiles_cta; i += 2) {
+        for (int i = eg; i < ntiles_cta; i += EPI_WGS) {
             const int tile = (int)blockIdx.x + i * (int)gridDim.x;
-            if (!mbar_wait(&misc->tfull[eg], (i >> 1) & 1, err)) break;
+            if (!mbar_wait(&misc->tfull[eg], (i / EPI_WGS) & 1, err)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + (uint32_t)(eg * D) + ((uint32_t)(quarter * 32) << 16);
             // Pass 1: |Pi x|^2 = |x|^2 from the accumulator row (four partial sums for ILP;
             // the exact norm is settled later when needed).
-            float v[64];
+            float v[VCH];
             float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                tmem_ld32_nowait(taddr + h * 64, v);
-                tmem_ld32_nowait(taddr + h * 64 + 32, v + 32);
+            for (int h = 0; h < D / VCH; ++h) {
+                tmem_ld32_nowait(taddr + h * VCH, v);
                 tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 64; ++j) s4[j & 3] = fmaf(v[j], v[j], s4[j & 3]);
+                for (int j = 0; j < VCH; ++j) s4[j & 3] = fmaf(v[j], v[j], s4[j & 3]);
             }
             const float ss = (s4[0] + s4[1]) + (s4[2] + s4[3]);
             const float norm_f = sqrtf(ss);
             const float kr = __frcp_rn(norm_f + 1e-8f) * inv2r;
             bool norm_amb = __float2half_rn(norm_f * (1.0f - kNormBand)) != __float2half_rn(norm_f * (1.0f + kNormBand));
-            // Pass 2, codes, half a row at a time. Per coordinate: t = y/(2R) + 0.5
+            // Pass 2, codes, VCH coordinates per round. Per coordinate: t = y/(2R) + 0.5
             // (saturated), its table bin, the bin's boundary `mid`; code = base + (t > mid)
             // from the sign of mid - t; packed big-endian by integer multiply-add (first
             // code in the top bits). The accumulator goes back to the MMA warp as soon as
-            // the last half is in registers.
+            // the last round is in registers.
             constexpr int G = (BITS == 2) ? 16 : 8;  // codes per packing word
             const float band_t = kRiskBand * inv2r;
             uint32_t pk[16];
             uint32_t mask[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
+            for (int h = 0; h < D / VCH; ++h) {
                 float dmin = 1.0f;
-                tmem_ld32_nowait(taddr + h * 64, v);
-                tmem_ld32_nowait(taddr + h * 64 + 32, v + 32);
+                tmem_ld32_nowait(taddr + h * VCH, v);
                 tmem_wait_ld();
-                if (h == 1) {
+                if (h == D / VCH - 1) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&misc->tempty[eg]);
                 }
 #pragma unroll
-                for (int w2 = 0; w2 < 64 / G; ++w2) {
+                for (int w2 = 0; w2 < VCH / G; ++w2) {
                     uint32_t wd = 0;
 #pragma unroll
                     for (int q = 0; q < G; ++q) {
@@ -427,12 +428,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint32_t code = base + (__float_as_uint(dd) >> 31);
                         wd = wd * (1u << BITS) + code;
                     }
-                    pk[h * (64 / G) + w2] = wd;
+                    pk[h * (VCH / G) + w2] = wd;
                 }
                 if (dmin < band_t) {
-                    // rare: list this half's coordinates within the band
+                    // rare: list this round's coordinates within the band
 #pragma unroll
-                    for (int j = 0; j < 64; ++j) {
+                    for (int j = 0; j < VCH; ++j) {
                         float t;
                         asm("fma.rn.sat.f32 %0, %1, %2, 0f3F000000;" : "=f"(t) : "f"(v[j]), "f"(kr));
                         const float u = fmaf(t, (float)(NB - 1), magic);
@@ -440,10 +441,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                         float mid;
                         uint32_t base;
                         asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
-                        if (fabsf(mid - t) < band_t) mask[2 * h + (j >> 5)] |= 1u << (j & 31);
+                        const int jj = h * VCH + j;
+                        if (fabsf(mid - t) < band_t) mask[jj >> 5] |= 1u << (jj & 31);
                     }
                 }
             }
+
             const int64_t vi = (int64_t)tile * TILE + row;
             const int64_t nvec = a.num_tokens * a.num_heads;
             if (vi >= nvec) continue;
@@ -535,7 +538,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem_base) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem_base) : "memory");
     }
 }
 
