@@ -210,6 +210,40 @@ __device__ __forceinline__ int sw128_offset(int n, int k) {
     return kb * KBLK_BYTES + n * 128 + ((((kk >> 3) ^ (n & 7))) << 4) + ((kk & 7) << 1);
 }
 
+// Exact float32 statement for one queued row, by one thread, on the stored
+// bytes (used when the fixup queue is full).
+template <typename TIn, int BITS>
+__device__ __forceinline__ void settle_row_inline(const TqArgs& a, int64_t vi, int64_t prow, uint32_t flags,
+                                               uint32_t m0, uint32_t m1, uint32_t m2, uint32_t m3, const float* cen) {
+    const int nlev = 1 << BITS;
+    const int P = (D * BITS) >> 3;
+    const TIn* xr = (const TIn*)a.input + vi * D;
+    float s = 0.0f;
+    for (int j = 0; j < D; ++j) {
+        const float x = to_f32(xr[j]);
+        s = __fadd_rn(s, __fmul_rn(x, x));
+    }
+    const float norm = __fsqrt_rn(s);
+    if (flags & kFixNorm) ((__half*)a.norms_pool)[prow] = __float2half_rn(norm);
+    const float den = __fadd_rn(norm, 1e-8f);
+    uint8_t* row = (uint8_t*)a.packed_pool + prow * P;
+    for (int c = 0; c < 4; ++c) {
+        uint32_t m = (flags & kFixAll) ? 0xffffffffu : (c == 0 ? m0 : c == 1 ? m1 : c == 2 ? m2 : m3);
+        while (m) {
+            const int i = c * 32 + __ffs(m) - 1;
+            m &= m - 1;
+            float y = 0.0f;
+            for (int j = 0; j < D; ++j) y = __fadd_rn(y, __fmul_rn(a.rotation[i * D + j], __fdiv_rn(to_f32(xr[j]), den)));
+            const uint32_t code = (uint32_t)nearest_centroid(y, cen, nlev);
+            for (int b = 0; b < BITS; ++b) {
+                const int bp = i * BITS + b;
+                const uint8_t bit = (uint8_t)(0x80u >> (bp & 7));
+                row[bp >> 3] = ((code >> (BITS - 1 - b)) & 1u) ? (uint8_t)(row[bp >> 3] | bit) : (uint8_t)(row[bp >> 3] & ~bit);
+            }
+        }
+    }
+}
+
 template <typename TIn, int NPARTS, int BITS>
 __global__ void __maxnreg__(MAX_REGS)
     tq_compress_umma_kernel(const __grid_constant__ CUtensorMap tmap, TqArgs a, int num_tiles, FixEntry* fix,
@@ -371,8 +405,18 @@ __global__ void __maxnreg__(MAX_REGS)
         const int P = (D * BITS) >> 3;
         const float magic = 12582912.0f;  // 1.5 * 2^23: fma(t, NB-1, magic) holds round(t*(NB-1)) in its low bits
         const uint32_t lut_lane = smem_u32(lut) + lane * 8 - (uint32_t)__float_as_uint(magic) * 256u;
+        const int64_t nvec = a.num_tokens * a.num_heads;
+        constexpr int G = (BITS == 2) ? 16 : 8;  // codes per packing word
+        constexpr int WPR = VCH / G;              // packing words per round
+        const float band_t = kRiskBand * inv2r;
         for (int i = eg; i < ntiles_cta; i += EPI_WGS) {
             const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+            const int64_t vi = (int64_t)tile * TILE + row;
+            // Pool row: the block-table lookup is issued before the accumulator wait.
+            int64_t slot = -1;
+            if (vi < nvec) slot = tq_slot(a, vi / a.num_heads);
+            const int64_t prow = slot >= 0 ? slot * a.num_heads + vi % a.num_heads : -1;
+            uint8_t* dst = prow >= 0 ? (uint8_t*)a.packed_pool + prow * P : nullptr;
             if (!mbar_wait(&misc->tfull[eg], (i / EPI_WGS) & 1, err)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + (uint32_t)(eg * D) + ((uint32_t)(quarter * 32) << 16);
@@ -380,7 +424,7 @@ __global__ void __maxnreg__(MAX_REGS)
             // the exact norm is settled later when needed).
             float v[VCH];
             float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
+#pragma unroll 1
             for (int h = 0; h < D / VCH; ++h) {
                 tmem_ld32_nowait(taddr + h * VCH, v);
                 tmem_wait_ld();
@@ -388,19 +432,18 @@ __global__ void __maxnreg__(MAX_REGS)
                 for (int j = 0; j < VCH; ++j) s4[j & 3] = fmaf(v[j], v[j], s4[j & 3]);
             }
             const float ss = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+            const bool zero = ss == 0.0f;  // zero vector: y = 0 for every coordinate in both statements
             const float norm_f = sqrtf(ss);
             const float kr = __frcp_rn(norm_f + 1e-8f) * inv2r;
-            bool norm_amb = __float2half_rn(norm_f * (1.0f - kNormBand)) != __float2half_rn(norm_f * (1.0f + kNormBand));
-            // Pass 2, codes, VCH coordinates per round. Per coordinate: t = y/(2R) + 0.5
-            // (saturated), its table bin, the bin's boundary `mid`; code = base + (t > mid)
-            // from the sign of mid - t; packed big-endian by integer multiply-add (first
-            // code in the top bits). The accumulator goes back to the MMA warp as soon as
-            // the last round is in registers.
-            constexpr int G = (BITS == 2) ? 16 : 8;  // codes per packing word
-            const float band_t = kRiskBand * inv2r;
-            uint32_t pk[16];
+            const bool norm_amb =
+                __float2half_rn(norm_f * (1.0f - kNormBand)) != __float2half_rn(norm_f * (1.0f + kNormBand));
+            // Pass 2, codes, VCH coordinates per round, stored as soon as a round is done.
+            // Per coordinate: t = y/(2R) + 0.5 (saturated), its table bin, the bin's boundary
+            // `mid`; code = base + (t > mid) from the sign of mid - t; packed big-endian by
+            // integer multiply-add (first code in the top bits). The accumulator goes back
+            // to the MMA warp as soon as the last round is in registers.
             uint32_t mask[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
+#pragma unroll 1
             for (int h = 0; h < D / VCH; ++h) {
                 float dmin = 1.0f;
                 tmem_ld32_nowait(taddr + h * VCH, v);
@@ -410,8 +453,9 @@ __global__ void __maxnreg__(MAX_REGS)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&misc->tempty[eg]);
                 }
+                uint32_t w[WPR];
 #pragma unroll
-                for (int w2 = 0; w2 < VCH / G; ++w2) {
+                for (int w2 = 0; w2 < WPR; ++w2) {
                     uint32_t wd = 0;
 #pragma unroll
                     for (int q = 0; q < G; ++q) {
@@ -428,10 +472,25 @@ __global__ void __maxnreg__(MAX_REGS)
                         const uint32_t code = base + (__float_as_uint(dd) >> 31);
                         wd = wd * (1u << BITS) + code;
                     }
-                    pk[h * (VCH / G) + w2] = wd;
+                    w[w2] = zero ? zero_word : wd;
                 }
-                if (dmin < band_t) {
+                if (dst) {
+                    if constexpr (BITS == 4) {
+                        *(uint4*)(dst + 16 * h) = make_uint4(__byte_perm(w[0], 0, 0x0123), __byte_perm(w[1], 0, 0x0123),
+                                                             __byte_perm(w[2], 0, 0x0123), __byte_perm(w[3], 0, 0x0123));
+                    } else if constexpr (BITS == 2) {
+                        *(uint2*)(dst + 8 * h) = make_uint2(__byte_perm(w[0], 0, 0x0123), __byte_perm(w[1], 0, 0x0123));
+                    } else {
+                        // 3-bit: each word holds 24 stream bits (bits 23..0, first code on top)
+                        uint32_t* d3 = (uint32_t*)(dst + 12 * h);
+                        d3[0] = __byte_perm(w[0], w[1], 0x6012);  // w0.b2 w0.b1 w0.b0 w1.b2
+                        d3[1] = __byte_perm(w[1], w[2], 0x5601);  // w1.b1 w1.b0 w2.b2 w2.b1
+                        d3[2] = __byte_perm(w[2], w[3], 0x4560);  // w2.b0 w3.b2 w3.b1 w3.b0
+                    }
+                }
+                if (dmin < band_t && !zero) {
                     // rare: list this round's coordinates within the band
+                    uint32_t m = 0;
 #pragma unroll
                     for (int j = 0; j < VCH; ++j) {
                         float t;
@@ -441,96 +500,32 @@ __global__ void __maxnreg__(MAX_REGS)
                         float mid;
                         uint32_t base;
                         asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
-                        const int jj = h * VCH + j;
-                        if (fabsf(mid - t) < band_t) mask[jj >> 5] |= 1u << (jj & 31);
+                        if (fabsf(mid - t) < band_t) m |= 1u << j;
                     }
+                    if (h == 0) mask[0] = m;
+                    else if (h == 1) mask[1] = m;
+                    else if (h == 2) mask[2] = m;
+                    else mask[3] = m;
                 }
             }
-
-            const int64_t vi = (int64_t)tile * TILE + row;
-            const int64_t nvec = a.num_tokens * a.num_heads;
-            if (vi >= nvec) continue;
-            const int64_t slot = tq_slot(a, vi / a.num_heads);
-            if (slot < 0) continue;
-            __half nh = __float2half_rn(norm_f);
-            if (ss == 0.0f) {
-                // zero vector: y = 0 for every coordinate in both statements
-#pragma unroll
-                for (int w2 = 0; w2 < 16; ++w2) pk[w2] = zero_word;
-                mask[0] = mask[1] = mask[2] = mask[3] = 0;
-                norm_amb = false;
-            }
-            bool inline_exact = false;
-            if (use_exact || norm_amb || (mask[0] | mask[1] | mask[2] | mask[3])) {
+            if (prow < 0) continue;
+            ((__half*)a.norms_pool)[prow] = __float2half_rn(norm_f);
+            const uint32_t flags = ((norm_amb && !zero) ? kFixNorm : 0u) | (use_exact ? kFixAll | kFixNorm : 0u);
+            if (flags || (mask[0] | mask[1] | mask[2] | mask[3])) {
                 const uint32_t qi = atomicAdd(fix_count, 1u);
                 if (qi < fix_cap) {
                     FixEntry en;
                     en.vi = (uint32_t)vi;
-                    en.flags = (norm_amb ? kFixNorm : 0u) | (use_exact ? kFixAll | kFixNorm : 0u);
+                    en.flags = flags;
                     en.mask[0] = mask[0];
                     en.mask[1] = mask[1];
                     en.mask[2] = mask[2];
                     en.mask[3] = mask[3];
                     fix[qi] = en;
                 } else {
-                    inline_exact = true;  // queue full: settle here
+                    // queue full: settle the row here
+                    settle_row_inline<TIn, BITS>(a, vi, prow, flags, mask[0], mask[1], mask[2], mask[3], misc->cen);
                 }
-            }
-            if (inline_exact) {
-                // exact float32 statement for this row
-                const TIn* xr = (const TIn*)a.input + vi * D;
-                float s = 0.0f;
-                for (int j = 0; j < D; ++j) {
-                    const float x = to_f32(xr[j]);
-                    s = __fadd_rn(s, __fmul_rn(x, x));
-                }
-                const float norm = __fsqrt_rn(s);
-                nh = __float2half_rn(norm);
-                const float den = __fadd_rn(norm, 1e-8f);
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t m = use_exact ? 0xffffffffu : mask[c];
-                    while (m) {
-                        const int jj = __ffs(m) - 1;
-                        m &= m - 1;
-                        const int i_coord = c * 32 + jj;
-                        const float* prow = a.rotation + i_coord * D;
-                        float y = 0.0f;
-                        for (int j = 0; j < D; ++j) y = __fadd_rn(y, __fmul_rn(__ldg(prow + j), __fdiv_rn(to_f32(xr[j]), den)));
-                        const uint32_t code = (uint32_t)nearest_centroid(y, misc->cen, nlev);
-                        // patch the code into its packing word (first code in the top bits)
-                        constexpr int G = (BITS == 2) ? 16 : 8;
-                        const int widx = i_coord / G, q = i_coord % G;
-                        const int sh = BITS * (G - 1 - q);
-                        const uint32_t clr = ~(((1u << BITS) - 1u) << sh);
-#pragma unroll
-                        for (int w2 = 0; w2 < 16; ++w2)
-                            if (w2 == widx) pk[w2] = (pk[w2] & clr) | (code << sh);
-                    }
-                }
-            }
-            ((__half*)a.norms_pool)[slot * a.num_heads + vi % a.num_heads] = nh;
-            uint8_t* dst = (uint8_t*)a.packed_pool + (slot * a.num_heads + vi % a.num_heads) * P;
-            if constexpr (BITS == 4 || BITS == 2) {
-                // big-endian words -> byte stream
-#pragma unroll
-                for (int q4 = 0; q4 < P / 16; ++q4)
-                    *(uint4*)(dst + 16 * q4) =
-                        make_uint4(__byte_perm(pk[4 * q4], 0, 0x0123), __byte_perm(pk[4 * q4 + 1], 0, 0x0123),
-                                   __byte_perm(pk[4 * q4 + 2], 0, 0x0123), __byte_perm(pk[4 * q4 + 3], 0, 0x0123));
-            } else {
-                // 3-bit: each word holds 24 stream bits (bits 23..0, first code on top);
-                // four words -> three little-endian output words.
-                uint32_t o[12];
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    const uint32_t w0 = pk[4 * q4], w1 = pk[4 * q4 + 1], w2 = pk[4 * q4 + 2], w3 = pk[4 * q4 + 3];
-                    o[3 * q4 + 0] = __byte_perm(w0, w1, 0x6012);  // w0.b2 w0.b1 w0.b0 w1.b2
-                    o[3 * q4 + 1] = __byte_perm(w1, w2, 0x5601);  // w1.b1 w1.b0 w2.b2 w2.b1
-                    o[3 * q4 + 2] = __byte_perm(w2, w3, 0x4560);  // w2.b0 w3.b2 w3.b1 w3.b0
-                }
-#pragma unroll
-                for (int q4 = 0; q4 < 3; ++q4)
-                    *(uint4*)(dst + 16 * q4) = make_uint4(o[4 * q4], o[4 * q4 + 1], o[4 * q4 + 2], o[4 * q4 + 3]);
             }
         }
     }
