@@ -172,6 +172,11 @@ struct Timer {
 
 }  // namespace
 
+namespace fb {
+// Lets the kernel entry points of other translation units report a message through fb_last_error.
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+}  // namespace fb
+
 struct fb_backend {
     int device = 0;
     cudaStream_t stream = nullptr;

@@ -4,11 +4,15 @@
 // (backends/fracture-cuda/src/ffi.rs:220-247) write/read the compact
 // [T, Hkv * P] layout; they are the paged entry points with no block table.
 
+#include <cstdio>
+
 #include "common.cuh"
 #include "tq_common.cuh"
 
 namespace fb {
 int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled);
+int tq_compress_umma_noalloc(const TqArgs& a, cudaStream_t s, bool* handled);
+void set_last_error(const char* msg);
 }
 
 using namespace fb;
@@ -49,6 +53,52 @@ extern "C" int fb_launch_tq_compress_paged(const void* input, int dtype, const f
     a.err_count = err_count;
     bool handled = false;
     rc = tq_compress_umma(a, (cudaStream_t)stream, &handled);
+    if (handled) return rc;
+    return tq_compress_exact(a, (cudaStream_t)stream);
+}
+
+// Same contract as fb_launch_tq_compress_paged, but the call allocates no device memory: the
+// fixup queue of the tensor-core path is a static device array sized for kTqNoAllocMaxVectors
+// vectors (tq_umma.cu), and larger calls are rejected before anything is launched. The first
+// call on a device looks up that array's address (set-up), later calls only launch.
+extern "C" int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype, const float* rotation,
+                                                   const float* centroids, int bits, int64_t num_tokens,
+                                                   int num_kv_heads, int head_dim, const int32_t* block_table,
+                                                   int64_t start_pos, int64_t num_pool_rows, void* packed_pool,
+                                                   void* norms_pool, unsigned int* err_count, void* stream) {
+    int rc = tq_check_common(bits, num_tokens, num_kv_heads, head_dim, num_pool_rows);
+    if (rc) return rc;
+    if (dtype != FB_FP16 && dtype != FB_BF16 && dtype != FB_FP32) return (int)cudaErrorInvalidValue;
+    if (start_pos < 0) return (int)cudaErrorInvalidValue;
+    if (num_tokens > kTqNoAllocMaxVectors / num_kv_heads) {
+        char msg[200];
+        snprintf(msg, sizeof msg,
+                 "fb_launch_tq_compress_paged_noalloc: %lld tokens x %d KV heads exceed the static scratch "
+                 "limit of %lld vectors per call",
+                 (long long)num_tokens, num_kv_heads, (long long)kTqNoAllocMaxVectors);
+        set_last_error(msg);
+        return (int)cudaErrorInvalidValue;
+    }
+    if (num_tokens == 0) return 0;
+    if (!input || !rotation || !centroids || !packed_pool || !norms_pool) return (int)cudaErrorInvalidValue;
+    TqArgs a{};
+    a.input = input;
+    a.in_dtype = dtype;
+    a.rotation = rotation;
+    a.centroids = centroids;
+    a.bits = bits;
+    a.n_levels = 1 << bits;
+    a.num_tokens = num_tokens;
+    a.num_heads = num_kv_heads;
+    a.head_dim = head_dim;
+    a.block_table = block_table;
+    a.start_pos = start_pos;
+    a.pool_rows = num_pool_rows;
+    a.packed_pool = packed_pool;
+    a.norms_pool = norms_pool;
+    a.err_count = err_count;
+    bool handled = false;
+    rc = tq_compress_umma_noalloc(a, (cudaStream_t)stream, &handled);
     if (handled) return rc;
     return tq_compress_exact(a, (cudaStream_t)stream);
 }

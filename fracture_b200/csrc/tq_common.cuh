@@ -6,6 +6,10 @@
 
 namespace fb {
 
+// Largest call (num_tokens * num_kv_heads) of the no-allocation compress entry point; its
+// fixup queue is a static device array of this many entries.
+constexpr int64_t kTqNoAllocMaxVectors = (int64_t)1 << 19;
+
 struct TqArgs {
     const void* input;         // compress: [T, H, d] fp16/bf16
     int in_dtype;

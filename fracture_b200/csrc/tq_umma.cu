@@ -698,8 +698,42 @@ static int fix_workspace(int64_t nvec, umma::FixEntry** entries, unsigned int** 
     return 0;
 }
 
+// Fixup queue of the no-allocation entry point: a file-scope device array, so that a call
+// allocates nothing. It holds the queue header (256 bytes) and one entry per vector of the
+// largest call accepted, kTqNoAllocMaxVectors (524288 vectors, e.g. 65536 tokens x 8 KV heads):
+// 12 MiB + 256 bytes per device, reserved when the module loads. One array per device serves
+// every call on that device, so calls that overlap in time (two streams, two host threads)
+// race on it.
+static __device__ __align__(256) unsigned char
+    g_tq_fix_scratch[256 + (size_t)kTqNoAllocMaxVectors * sizeof(umma::FixEntry)];
+
+// Set-up, once per device with that device current: the device address of g_tq_fix_scratch.
+// The first call on a device does this set-up (it may load the module), so it belongs before
+// any stream capture; later calls only read the cached address.
+static int static_fix_scratch(int64_t nvec, umma::FixEntry** entries, unsigned int** count, unsigned int* cap) {
+    static void* addr[64];
+    static std::mutex mu;
+    if (nvec > kTqNoAllocMaxVectors) return (int)cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_tq_fix_scratch);
+        if (e != cudaSuccess) return (int)e;
+        if (!p) return (int)cudaErrorInvalidSymbol;
+        addr[dev] = p;
+    }
+    *count = (unsigned int*)addr[dev];
+    *entries = (umma::FixEntry*)((char*)addr[dev] + 256);
+    *cap = (unsigned int)kTqNoAllocMaxVectors;
+    return 0;
+}
+
 template <typename TIn, int NPARTS, int BITS>
-static int launch_umma(const TqArgs& a, cudaStream_t s) {
+static int launch_umma(const TqArgs& a, cudaStream_t s, bool static_scratch) {
     auto encode = get_encode();
     if (!encode) return (int)cudaErrorNotSupported;
     const int64_t nvec = a.num_tokens * a.num_heads;
@@ -716,8 +750,10 @@ static int launch_umma(const TqArgs& a, cudaStream_t s) {
     umma::FixEntry* fix;
     unsigned int* fix_count;
     unsigned int fix_cap;
-    int rc = fix_workspace(nvec, &fix, &fix_count, &fix_cap);
+    int rc = static_scratch ? static_fix_scratch(nvec, &fix, &fix_count, &fix_cap)
+                            : fix_workspace(nvec, &fix, &fix_count, &fix_cap);
     if (rc) return rc;
+    // the queue counter must start at zero; the entries are written before they are read
     cudaError_t e = cudaMemsetAsync(fix_count, 0, sizeof(unsigned int), s);
     if (e != cudaSuccess) return (int)e;
     constexpr int smem = umma::Smem::bytes(NPARTS);
@@ -733,7 +769,7 @@ static int launch_umma(const TqArgs& a, cudaStream_t s) {
     return (int)cudaGetLastError();
 }
 
-int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled) {
+static int umma_dispatch(const TqArgs& a, cudaStream_t s, bool* handled, bool static_scratch) {
     *handled = false;
     if (a.head_dim != umma::D || !(a.bits == 2 || a.bits == 3 || a.bits == 4)) return 0;
     if (a.in_dtype != FB_FP16 && a.in_dtype != FB_BF16) return 0;
@@ -745,13 +781,21 @@ int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled) {
     if (!sm100) return 0;
     *handled = true;
     if (a.in_dtype == FB_FP16) {
-        if (a.bits == 4) return launch_umma<__half, 2, 4>(a, s);
-        if (a.bits == 3) return launch_umma<__half, 2, 3>(a, s);
-        return launch_umma<__half, 2, 2>(a, s);
+        if (a.bits == 4) return launch_umma<__half, 2, 4>(a, s, static_scratch);
+        if (a.bits == 3) return launch_umma<__half, 2, 3>(a, s, static_scratch);
+        return launch_umma<__half, 2, 2>(a, s, static_scratch);
     }
-    if (a.bits == 4) return launch_umma<__nv_bfloat16, 3, 4>(a, s);
-    if (a.bits == 3) return launch_umma<__nv_bfloat16, 3, 3>(a, s);
-    return launch_umma<__nv_bfloat16, 3, 2>(a, s);
+    if (a.bits == 4) return launch_umma<__nv_bfloat16, 3, 4>(a, s, static_scratch);
+    if (a.bits == 3) return launch_umma<__nv_bfloat16, 3, 3>(a, s, static_scratch);
+    return launch_umma<__nv_bfloat16, 3, 2>(a, s, static_scratch);
+}
+
+int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled) {
+    return umma_dispatch(a, s, handled, false);
+}
+
+int tq_compress_umma_noalloc(const TqArgs& a, cudaStream_t s, bool* handled) {
+    return umma_dispatch(a, s, handled, true);
 }
 
 }  // namespace fb

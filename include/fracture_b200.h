@@ -121,6 +121,20 @@ int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotat
                                 const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
                                 void* packed_pool, void* norms_pool, unsigned int* err_count, void* stream);
 
+/* fb_launch_tq_compress_paged that allocates no device memory (no reference counterpart; the
+ * reference allocates per call). Results are identical to fb_launch_tq_compress_paged. The fixup
+ * queue of the tensor-core path is a static device array (12 MiB + 256 B per device) sized for at
+ * most 524288 vectors per call (num_tokens * num_kv_heads); larger calls return
+ * cudaErrorInvalidValue with the reason in fb_last_error(), before anything is launched. The first
+ * call on a device does set-up (looks up the array's device address), so make it before any
+ * stream capture. One array per device serves every call: calls that overlap in time on one
+ * device (two streams, two host threads) race and must be serialised by the caller. */
+int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype, const float* rotation,
+                                        const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
+                                        int head_dim, const int32_t* block_table, int64_t start_pos,
+                                        int64_t num_pool_rows, void* packed_pool, void* norms_pool,
+                                        unsigned int* err_count, void* stream);
+
 /* TurboQuant dequantize from a paged pool into [num_tokens, Hkv, d] (`dtype` FP16/BF16/FP32):
  * x = (Pi^T @ centroids[idx]) * norm (replaces turboquant_decompress.cu:21-94). Same slot rule. */
 int fb_launch_tq_dequant_paged(const void* packed_pool, const void* norms_pool, const float* rotation,
