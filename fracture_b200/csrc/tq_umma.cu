@@ -45,8 +45,10 @@ constexpr int TILE = 128;           // vectors per tile
 constexpr int STAGES = 3;           // A-tile pipeline depth
 constexpr int KBLK_BYTES = TILE * 128;    // one K-block (64 elements) of a 128-row tile, SW128
 constexpr int TILE_BYTES = 2 * KBLK_BYTES;  // 32 KB
-constexpr int NB = 64;              // decision-table bins over [-kRange, kRange]
-constexpr float kRange = 0.54f;
+constexpr int NB = 128;             // decision-table bins; bin b covers y in [(b - kBin0 -+ 1/2) w]
+constexpr int kBin0 = 64;           // the bin centred on y = 0
+constexpr float kInvW = 63.5f / 1.02f;  // 1 / bin width: bins span [-1.036, 1.02), and |y| <= 1
+constexpr int LUT_COPIES = 16;      // copies per bin; lanes l and l + 16 share one
 constexpr float kRiskBand = 1e-6f;   // |y - boundary| below this: settle with the exact sequence
 constexpr float kNormBand = 1e-6f;  // relative band around fp16 rounding ties of the norm
 constexpr float kWindowPad = 1e-4f; // a bin owns the boundaries within this distance of its edges
@@ -54,17 +56,19 @@ constexpr int EPI_WGS = 3;                 // epilogue warpgroups, one TMEM accu
 constexpr int THREADS = 64 + EPI_WGS * 128;  // warp 0 TMA, warp 1 MMA, then the epilogue
 constexpr int VCH = 32;                    // accumulator values per thread per TMEM load round
 constexpr int MAX_REGS = 128;              // 14 warps: at most 4 per scheduler, 16K registers each
+static_assert(THREADS > NB, "one thread per table bin plus one for the checks");
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 // Rows whose fast-path result is not certain (a coordinate within kRiskBand of a
 // decision boundary, or a norm within kNormBand of an fp16 rounding tie) are
-// queued here and settled by tq_fixup_kernel with the exact float32 sequence.
+// queued here, one entry per uncertain coordinate (or one norm-only entry), and
+// settled by tq_fixup_kernel with the exact float32 sequence.
 struct FixEntry {
-    uint32_t vi;       // vector index (token * heads + head) of the call
-    uint32_t flags;    // kFixNorm: rewrite the norm; kFixAll: every coordinate
-    uint32_t mask[4];  // coordinates to recompute
+    uint32_t vi;    // vector index (token * heads + head) of the call
+    uint32_t info;  // bits 0-6: coordinate; kHasCoord, kFixNorm, kFixAll, kSkip
+    int64_t prow;   // pool row (slot * heads + head)
 };
-constexpr uint32_t kFixNorm = 1u, kFixAll = 2u;
+constexpr uint32_t kHasCoord = 1u << 8, kFixNorm = 1u << 9, kFixAll = 1u << 10, kSkip = 1u << 11;
 
 struct Misc {
     uint64_t full[STAGES];
@@ -75,13 +79,15 @@ struct Misc {
     int use_exact;  // table could not be built: every row takes the exact path
     uint32_t zero_word; // packing word of a zero vector (every code = nearest centroid of 0)
     float cen[256];
+    float bin_mid[NB];      // per-bin table entry before it is copied LUT_COPIES times
+    uint32_t bin_base[NB];
 };
 
 // Byte offsets from the 1024-aligned base of dynamic shared memory.
 struct Smem {
     static constexpr int a_off(int nparts) { return nparts * TILE_BYTES; }
     static constexpr int lut_off(int nparts) { return a_off(nparts) + STAGES * TILE_BYTES; }
-    static constexpr int misc_off(int nparts) { return lut_off(nparts) + NB * 32 * 8; }
+    static constexpr int misc_off(int nparts) { return lut_off(nparts) + NB * LUT_COPIES * 8; }
     static constexpr int bytes(int nparts) { return misc_off(nparts) + (int)sizeof(Misc) + 1024; }
 };
 
@@ -156,8 +162,9 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-    uint32_t r[32];
+// Issues a 32-column TMEM load of this thread's accumulator row into r; the values are
+// valid only after tmem_wait_tie(r).
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -167,40 +174,45 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float* v) {
-    uint32_t r[32];
+// Waits for this thread's TMEM loads. The registers of the load are in-out operands, so
+// no use of them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_tie(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+
+// 16-column variants of the two helpers above.
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-__device__ __forceinline__ uint32_t set_ge(float a, float b) {
-    uint32_t r;
-    asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(r) : "f"(a), "f"(b));
-    return r;  // 0xffffffff or 0
+__device__ __forceinline__ void tmem_wait_tie(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
 }
 
-// One table entry per (bin, lane): lane-private copies keep the 32 lanes of a
-// warp on 32 different banks. lo/hi are in t units (t = y / (2 R) + 0.5);
-// hi's low 4 mantissa bits hold the code of the lower side of the bin's boundary.
+// One table entry per (bin, copy). The 16 copies of a bin sit side by side, so the
+// 16 lanes of each half-warp read 16 different bank pairs with one 64-bit load.
 struct LutEntry {
-    float mid;      // boundary in t units (4.0: the bin holds no boundary)
-    uint32_t base;  // code below the boundary (the code of the whole bin when mid = 4.0)
+    float mid;      // the bin's decision boundary in y units (8.0: the bin holds none)
+    uint32_t base;  // code below the boundary (the code of the whole bin when it holds none)
 };
 
 // Byte offset in the SW128 K-major image of element (row n, column k) of a
@@ -210,30 +222,53 @@ __device__ __forceinline__ int sw128_offset(int n, int k) {
     return kb * KBLK_BYTES + n * 128 + ((((kk >> 3) ^ (n & 7))) << 4) + ((kk & 7) << 1);
 }
 
-// Exact float32 statement for one queued row, by one thread, on the stored
-// bytes (used when the fixup queue is full).
+// Exact float32 statement for one queued row, by one thread, on the stored bytes:
+// the sequential sum of the squares (norm), then for each listed coordinate the
+// sequential sum of Pi[i][j] * (x_j / (norm + 1e-8)) and the first-minimum nearest
+// centroid, patched into the row's bit stream. Loads are 16-byte vectors; the
+// input row stays in L1 across the coordinates.
 template <typename TIn, int BITS>
 __device__ __forceinline__ void settle_row_inline(const TqArgs& a, int64_t vi, int64_t prow, uint32_t flags,
                                                uint32_t m0, uint32_t m1, uint32_t m2, uint32_t m3, const float* cen) {
+    constexpr int EPV = 16 / sizeof(TIn);  // elements per 16-byte vector
     const int nlev = 1 << BITS;
     const int P = (D * BITS) >> 3;
-    const TIn* xr = (const TIn*)a.input + vi * D;
+    const uint4* xr = (const uint4*)((const TIn*)a.input + vi * D);
     float s = 0.0f;
-    for (int j = 0; j < D; ++j) {
-        const float x = to_f32(xr[j]);
-        s = __fadd_rn(s, __fmul_rn(x, x));
+#pragma unroll 4
+    for (int c = 0; c < D / EPV; ++c) {
+        Vec16<TIn> u;
+        u.u = __ldg(xr + c);
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) {
+            const float x = to_f32(u.e[e]);
+            s = __fadd_rn(s, __fmul_rn(x, x));
+        }
     }
     const float norm = __fsqrt_rn(s);
     if (flags & kFixNorm) ((__half*)a.norms_pool)[prow] = __float2half_rn(norm);
     const float den = __fadd_rn(norm, 1e-8f);
     uint8_t* row = (uint8_t*)a.packed_pool + prow * P;
-    for (int c = 0; c < 4; ++c) {
-        uint32_t m = (flags & kFixAll) ? 0xffffffffu : (c == 0 ? m0 : c == 1 ? m1 : c == 2 ? m2 : m3);
+    for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t m = (flags & kFixAll) ? 0xffffffffu : (c4 == 0 ? m0 : c4 == 1 ? m1 : c4 == 2 ? m2 : m3);
         while (m) {
-            const int i = c * 32 + __ffs(m) - 1;
+            const int i = c4 * 32 + __ffs(m) - 1;
             m &= m - 1;
+            const float4* pr = (const float4*)(a.rotation + i * D);
             float y = 0.0f;
-            for (int j = 0; j < D; ++j) y = __fadd_rn(y, __fmul_rn(a.rotation[i * D + j], __fdiv_rn(to_f32(xr[j]), den)));
+#pragma unroll 2
+            for (int c = 0; c < D / EPV; ++c) {
+                Vec16<TIn> u;
+                u.u = __ldg(xr + c);
+#pragma unroll
+                for (int e4 = 0; e4 < EPV / 4; ++e4) {
+                    const float4 p = __ldg(pr + c * (EPV / 4) + e4);
+                    y = __fadd_rn(y, __fmul_rn(p.x, __fdiv_rn(to_f32(u.e[4 * e4 + 0]), den)));
+                    y = __fadd_rn(y, __fmul_rn(p.y, __fdiv_rn(to_f32(u.e[4 * e4 + 1]), den)));
+                    y = __fadd_rn(y, __fmul_rn(p.z, __fdiv_rn(to_f32(u.e[4 * e4 + 2]), den)));
+                    y = __fadd_rn(y, __fmul_rn(p.w, __fdiv_rn(to_f32(u.e[4 * e4 + 3]), den)));
+                }
+            }
             const uint32_t code = (uint32_t)nearest_centroid(y, cen, nlev);
             for (int b = 0; b < BITS; ++b) {
                 const int bp = i * BITS + b;
@@ -247,7 +282,7 @@ __device__ __forceinline__ void settle_row_inline(const TqArgs& a, int64_t vi, i
 template <typename TIn, int NPARTS, int BITS>
 __global__ void __maxnreg__(MAX_REGS)
     tq_compress_umma_kernel(const __grid_constant__ CUtensorMap tmap, TqArgs a, int num_tiles, FixEntry* fix,
-                            unsigned int* fix_count, unsigned int fix_cap) {
+                            unsigned long long* fix_count, unsigned int fix_cap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sB = base;
@@ -257,9 +292,18 @@ __global__ void __maxnreg__(MAX_REGS)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nlev = 1 << BITS;
-    const float inv2r = 1.0f / (2.0f * kRange);
+
+    const int ntiles_cta = num_tiles > (int)blockIdx.x ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int prefetched = ntiles_cta < STAGES ? ntiles_cta : STAGES;
 
     // ── prologue ─────────────────────────────────────────────────────────────
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                         smem_u32(&misc->tmem_base))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        tc_fence_before();
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&misc->full[s], 1);
@@ -271,13 +315,13 @@ __global__ void __maxnreg__(MAX_REGS)
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         misc->use_exact = 0;
-    }
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
-                         smem_u32(&misc->tmem_base))
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-        tc_fence_before();
+        // The first tiles are requested now, so their loads overlap the set-up below.
+        for (int i = 0; i < prefetched; ++i) {
+            const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+            mbar_expect_tx(&misc->full[i], TILE_BYTES);
+            tma_load_2d(sA + i * TILE_BYTES, &tmap, &misc->full[i], 0, tile * TILE);
+            tma_load_2d(sA + i * TILE_BYTES + KBLK_BYTES, &tmap, &misc->full[i], 64, tile * TILE);
+        }
     }
     for (int e = threadIdx.x; e < nlev; e += THREADS) misc->cen[e] = __ldg(a.centroids + e);
     // B operand: Pi split into NPARTS parts (hi + lo [+ lo2]) in the SW128 K-major image.
@@ -302,43 +346,45 @@ __global__ void __maxnreg__(MAX_REGS)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
 
-    // Decision table (all threads): boundaries m_k = (c_k + c_{k+1}) / 2, must be
-    // increasing, inside the table range and farther apart than one bin plus the bands.
+    // Decision table: boundaries m_k = (c_k + c_{k+1}) / 2, must be increasing, inside
+    // the table range and farther apart than one bin plus the bands (thread NB checks).
+    // Bin b covers y in [(b - kBin0 - 1/2) w, (b - kBin0 + 1/2) w) and owns the one
+    // boundary within kWindowPad of that interval, if any (threads 0..NB-1, one bin
+    // each); then every thread copies entries into the LUT_COPIES copies.
     {
-        const float w = 2.0f * kRange / (float)(NB - 1);
-        bool ok = true;
-        for (int k = 0; k + 1 < nlev; ++k) {
-            const float m = 0.5f * (misc->cen[k] + misc->cen[k + 1]);
-            if (!(misc->cen[k + 1] > misc->cen[k]) || !(fabsf(m) < kRange - 2.0f * w)) ok = false;
-            if (k > 0) {
-                const float mp = 0.5f * (misc->cen[k - 1] + misc->cen[k]);
-                if (!(m - mp > w + 2.0f * kWindowPad + 4.0f * kRiskBand)) ok = false;
+        const float w = 1.0f / kInvW;
+        if (threadIdx.x == NB) {
+            bool ok = true;
+            for (int k = 0; k + 1 < nlev; ++k) {
+                const float m = 0.5f * (misc->cen[k] + misc->cen[k + 1]);
+                if (!(misc->cen[k + 1] > misc->cen[k]) || !(fabsf(m) < 0.9f)) ok = false;
+                if (k > 0) {
+                    const float mp = 0.5f * (misc->cen[k - 1] + misc->cen[k]);
+                    if (!(m - mp > w + 2.0f * kWindowPad + 4.0f * kRiskBand)) ok = false;
+                }
             }
+            if (!ok) misc->use_exact = 1;
+            const uint32_t cz = (uint32_t)nearest_centroid(0.0f, misc->cen, nlev);
+            misc->zero_word = BITS == 4 ? cz * 0x11111111u : BITS == 2 ? cz * 0x55555555u : cz * 0x249249u;
         }
-        for (int e = threadIdx.x; e < NB * 32; e += THREADS) {
-            const int bin = e >> 5;
-            const float ylo = -kRange + ((float)bin - 0.5f) * w, yhi = -kRange + ((float)bin + 0.5f) * w;
+        if (threadIdx.x < NB) {
+            const int bin = threadIdx.x;
+            const float ylo = ((float)(bin - kBin0) - 0.5f) * w, yhi = ((float)(bin - kBin0) + 0.5f) * w;
             int below = 0, owner = -1;
             for (int k = 0; k + 1 < nlev; ++k) {
                 const float m = 0.5f * (misc->cen[k] + misc->cen[k + 1]);
                 if (m < ylo - kWindowPad) below = k + 1;
                 if (m >= ylo - kWindowPad && m <= yhi + kWindowPad) owner = k;
             }
-            LutEntry en;
-            if (owner >= 0) {
-                const float m = 0.5f * (misc->cen[owner] + misc->cen[owner + 1]);
-                en.mid = m * inv2r + 0.5f;
-                en.base = (uint32_t)owner;
-            } else {
-                en.mid = 4.0f;
-                en.base = (uint32_t)below;
-            }
-            lut[e] = en;
+            misc->bin_mid[bin] = owner >= 0 ? 0.5f * (misc->cen[owner] + misc->cen[owner + 1]) : 8.0f;
+            misc->bin_base[bin] = owner >= 0 ? (uint32_t)owner : (uint32_t)below;
         }
-        if (threadIdx.x == 0) {
-            if (!ok) misc->use_exact = 1;
-            const uint32_t cz = (uint32_t)nearest_centroid(0.0f, misc->cen, nlev);
-            misc->zero_word = BITS == 4 ? cz * 0x11111111u : BITS == 2 ? cz * 0x55555555u : cz * 0x249249u;
+        __syncthreads();
+        for (int e = threadIdx.x; e < NB * LUT_COPIES; e += THREADS) {
+            LutEntry en;
+            en.mid = misc->bin_mid[e / LUT_COPIES];
+            en.base = misc->bin_base[e / LUT_COPIES];
+            lut[e] = en;
         }
     }
     __syncthreads();
@@ -346,14 +392,13 @@ __global__ void __maxnreg__(MAX_REGS)
     const uint32_t tmem_base = misc->tmem_base;
     const int use_exact = misc->use_exact;
     const uint32_t zero_word = misc->zero_word;
-    const int ntiles_cta = num_tiles > (int)blockIdx.x ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     unsigned int* err = a.err_count;
 
     if (warp == 0) {
         // ── TMA producer ────────────────────────────────────────────────────
         if (lane == 0) {
-            int issued = 0;
-            for (int i = 0; i < ntiles_cta; ++i) {
+            int issued = prefetched;
+            for (int i = prefetched; i < ntiles_cta; ++i) {
                 const int s = i % STAGES;
                 if (!mbar_wait(&misc->empty[s], ((i / STAGES) + 1) & 1, err)) break;
                 const int tile = (int)blockIdx.x + i * (int)gridDim.x;
@@ -403,12 +448,15 @@ __global__ void __maxnreg__(MAX_REGS)
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const int P = (D * BITS) >> 3;
-        const float magic = 12582912.0f;  // 1.5 * 2^23: fma(t, NB-1, magic) holds round(t*(NB-1)) in its low bits
-        const uint32_t lut_lane = smem_u32(lut) + lane * 8 - (uint32_t)__float_as_uint(magic) * 256u;
+        const float magic = 12582912.0f;  // 1.5 * 2^23: fma(y, 1/w, magic + kBin0) holds the bin in its low bits
+        const float ubias = magic + (float)kBin0;
+        const uint32_t lut_lane =
+            smem_u32(lut) + (lane & (LUT_COPIES - 1)) * 8 - (uint32_t)__float_as_uint(magic) * (LUT_COPIES * 8u);
         const int64_t nvec = a.num_tokens * a.num_heads;
         constexpr int G = (BITS == 2) ? 16 : 8;  // codes per packing word
         constexpr int WPR = VCH / G;              // packing words per round
-        const float band_t = kRiskBand * inv2r;
+        constexpr int CW = 16;                    // accumulator columns per TMEM load (one chunk)
+        constexpr int NCH = D / CW;               // chunks per row
         for (int i = eg; i < ntiles_cta; i += EPI_WGS) {
             const int tile = (int)blockIdx.x + i * (int)gridDim.x;
             const int64_t vi = (int64_t)tile * TILE + row;
@@ -420,110 +468,146 @@ __global__ void __maxnreg__(MAX_REGS)
             if (!mbar_wait(&misc->tfull[eg], (i / EPI_WGS) & 1, err)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + (uint32_t)(eg * D) + ((uint32_t)(quarter * 32) << 16);
-            // Pass 1: |Pi x|^2 = |x|^2 from the accumulator row (four partial sums for ILP;
-            // the exact norm is settled later when needed).
-            float v[VCH];
+            // Pass 1: |Pi x|^2 = |x|^2 from the accumulator row, in 16-column chunks 0..NCH-1
+            // with the next chunk's load in flight while the current one is summed (four
+            // partial sums for ILP; the exact norm is settled later when needed). The last
+            // chunk stays in registers.
+            uint32_t ra[CW], rb[CW];
             float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 1
-            for (int h = 0; h < D / VCH; ++h) {
-                tmem_ld32_nowait(taddr + h * VCH, v);
-                tmem_wait_ld();
+            tmem_ld16_issue(taddr, ra);
 #pragma unroll
-                for (int j = 0; j < VCH; ++j) s4[j & 3] = fmaf(v[j], v[j], s4[j & 3]);
+            for (int h = 0; h < NCH; ++h) {
+                uint32_t(&cur)[CW] = (h & 1) ? rb : ra;
+                uint32_t(&nxt)[CW] = (h & 1) ? ra : rb;
+                tmem_wait_tie(cur);
+                if (h + 1 < NCH) tmem_ld16_issue(taddr + (h + 1) * CW, nxt);
+#pragma unroll
+                for (int j = 0; j < CW; ++j) {
+                    const float v = __uint_as_float(cur[j]);
+                    s4[j & 3] = fmaf(v, v, s4[j & 3]);
+                }
             }
             const float ss = (s4[0] + s4[1]) + (s4[2] + s4[3]);
             const bool zero = ss == 0.0f;  // zero vector: y = 0 for every coordinate in both statements
+            const bool finite = ss <= 3.402823466e38f;  // NaN or inf: the row takes the exact path
             const float norm_f = sqrtf(ss);
-            const float kr = __frcp_rn(norm_f + 1e-8f) * inv2r;
+            const float kr = finite ? __frcp_rn(norm_f + 1e-8f) : 0.0f;  // y = acc * kr
+            const float ku = kr * kInvW;
             const bool norm_amb =
                 __float2half_rn(norm_f * (1.0f - kNormBand)) != __float2half_rn(norm_f * (1.0f + kNormBand));
-            // Pass 2, codes, VCH coordinates per round, stored as soon as a round is done.
-            // Per coordinate: t = y/(2R) + 0.5 (saturated), its table bin, the bin's boundary
-            // `mid`; code = base + (t > mid) from the sign of mid - t; packed big-endian by
-            // integer multiply-add (first code in the top bits). The accumulator goes back
-            // to the MMA warp as soon as the last round is in registers.
+            // Pass 2, codes, chunks NCH-1..0 (the last one is still in registers; the next
+            // load is in flight while a chunk is coded); a round of VCH coordinates (two
+            // chunks) is stored as soon as both are coded. Per coordinate: its table bin from
+            // the rounded fma(acc, ku, ubias), the bin's boundary m and lower code; dd = m - y;
+            // code = base + (y > m) from the sign of dd, packed big-endian by integer
+            // multiply-add (first code in the top bits). The accumulator goes back to the MMA
+            // warp once the last chunk is in registers.
             uint32_t mask[4] = {0u, 0u, 0u, 0u};
-#pragma unroll 1
-            for (int h = 0; h < D / VCH; ++h) {
-                float dmin = 1.0f;
-                tmem_ld32_nowait(taddr + h * VCH, v);
-                tmem_wait_ld();
-                if (h == D / VCH - 1) {
+            uint32_t w[WPR];
+#pragma unroll
+            for (int c = NCH - 1; c >= 0; --c) {
+                // chunk NCH-1 is in the buffer pass 1 used last; the chunks below alternate
+                constexpr bool last_in_b = ((NCH - 1) & 1) != 0;
+                const bool in_b = (((NCH - 1 - c) & 1) == 0) ? last_in_b : !last_in_b;
+                uint32_t(&cur)[CW] = in_b ? rb : ra;
+                uint32_t(&nxt)[CW] = in_b ? ra : rb;
+                if (c < NCH - 1) tmem_wait_tie(cur);
+                if (c > 0) {
+                    tmem_ld16_issue(taddr + (c - 1) * CW, nxt);
+                } else {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&misc->tempty[eg]);
                 }
-                uint32_t w[WPR];
+                // four running minima and a pairwise packing tree keep the dependency chains short
+                float dm[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+                constexpr int WPC = CW / G;  // packing words per chunk
 #pragma unroll
-                for (int w2 = 0; w2 < WPR; ++w2) {
-                    uint32_t wd = 0;
+                for (int w2 = 0; w2 < WPC; ++w2) {
+                    uint32_t code[G];
 #pragma unroll
                     for (int q = 0; q < G; ++q) {
-                        const int j = w2 * G + q;
-                        float t;
-                        asm("fma.rn.sat.f32 %0, %1, %2, 0f3F000000;" : "=f"(t) : "f"(v[j]), "f"(kr));
-                        const float u = fmaf(t, (float)(NB - 1), magic);
-                        const uint32_t addr = __float_as_uint(u) * 256u + lut_lane;
+                        const float v = __uint_as_float(cur[w2 * G + q]);
+                        const float u = fmaf(v, ku, ubias);
+                        const uint32_t addr = __float_as_uint(u) * (LUT_COPIES * 8u) + lut_lane;
                         float mid;
                         uint32_t base;
                         asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
-                        const float dd = mid - t;
-                        dmin = fminf(dmin, fabsf(dd));
-                        const uint32_t code = base + (__float_as_uint(dd) >> 31);
-                        wd = wd * (1u << BITS) + code;
+                        const float dd = fmaf(-v, kr, mid);
+                        dm[q & 3] = fminf(dm[q & 3], fabsf(dd));
+                        code[q] = base + (__float_as_uint(dd) >> 31);
                     }
-                    w[w2] = zero ? zero_word : wd;
+                    // big-endian: code 0 in the top bits
+#pragma unroll
+                    for (int span = 1; span < G; span *= 2)
+#pragma unroll
+                        for (int q = 0; q < G; q += 2 * span) code[q] = code[q] * (1u << (BITS * span)) + code[q + span];
+                    w[(c & 1) * WPC + w2] = zero ? zero_word : code[0];
                 }
-                if (dst) {
+                const float dmin = fminf(fminf(dm[0], dm[1]), fminf(dm[2], dm[3]));
+                if (dmin < kRiskBand && !zero) {
+                    // rare: list this chunk's coordinates within the band
+                    uint32_t m = 0;
+#pragma unroll
+                    for (int j = 0; j < CW; ++j) {
+                        const float v = __uint_as_float(cur[j]);
+                        const float u = fmaf(v, ku, ubias);
+                        const uint32_t addr = __float_as_uint(u) * (LUT_COPIES * 8u) + lut_lane;
+                        float mid;
+                        uint32_t base;
+                        asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
+                        if (fabsf(fmaf(-v, kr, mid)) < kRiskBand) m |= 1u << j;
+                    }
+                    mask[c >> 1] |= m << ((c & 1) * CW);
+                }
+                if ((c & 1) == 0 && dst) {
+                    const int g = c >> 1;  // both chunks of round g are coded
                     if constexpr (BITS == 4) {
-                        *(uint4*)(dst + 16 * h) = make_uint4(__byte_perm(w[0], 0, 0x0123), __byte_perm(w[1], 0, 0x0123),
+                        *(uint4*)(dst + 16 * g) = make_uint4(__byte_perm(w[0], 0, 0x0123), __byte_perm(w[1], 0, 0x0123),
                                                              __byte_perm(w[2], 0, 0x0123), __byte_perm(w[3], 0, 0x0123));
                     } else if constexpr (BITS == 2) {
-                        *(uint2*)(dst + 8 * h) = make_uint2(__byte_perm(w[0], 0, 0x0123), __byte_perm(w[1], 0, 0x0123));
+                        *(uint2*)(dst + 8 * g) = make_uint2(__byte_perm(w[0], 0, 0x0123), __byte_perm(w[1], 0, 0x0123));
                     } else {
                         // 3-bit: each word holds 24 stream bits (bits 23..0, first code on top)
-                        uint32_t* d3 = (uint32_t*)(dst + 12 * h);
+                        uint32_t* d3 = (uint32_t*)(dst + 12 * g);
                         d3[0] = __byte_perm(w[0], w[1], 0x6012);  // w0.b2 w0.b1 w0.b0 w1.b2
                         d3[1] = __byte_perm(w[1], w[2], 0x5601);  // w1.b1 w1.b0 w2.b2 w2.b1
                         d3[2] = __byte_perm(w[2], w[3], 0x4560);  // w2.b0 w3.b2 w3.b1 w3.b0
                     }
                 }
-                if (dmin < band_t && !zero) {
-                    // rare: list this round's coordinates within the band
-                    uint32_t m = 0;
-#pragma unroll
-                    for (int j = 0; j < VCH; ++j) {
-                        float t;
-                        asm("fma.rn.sat.f32 %0, %1, %2, 0f3F000000;" : "=f"(t) : "f"(v[j]), "f"(kr));
-                        const float u = fmaf(t, (float)(NB - 1), magic);
-                        const uint32_t addr = __float_as_uint(u) * 256u + lut_lane;
-                        float mid;
-                        uint32_t base;
-                        asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
-                        if (fabsf(mid - t) < band_t) m |= 1u << j;
-                    }
-                    if (h == 0) mask[0] = m;
-                    else if (h == 1) mask[1] = m;
-                    else if (h == 2) mask[2] = m;
-                    else mask[3] = m;
-                }
             }
             if (prow < 0) continue;
             ((__half*)a.norms_pool)[prow] = __float2half_rn(norm_f);
-            const uint32_t flags = ((norm_amb && !zero) ? kFixNorm : 0u) | (use_exact ? kFixAll | kFixNorm : 0u);
-            if (flags || (mask[0] | mask[1] | mask[2] | mask[3])) {
-                const uint32_t qi = atomicAdd(fix_count, 1u);
-                if (qi < fix_cap) {
-                    FixEntry en;
-                    en.vi = (uint32_t)vi;
-                    en.flags = flags;
-                    en.mask[0] = mask[0];
-                    en.mask[1] = mask[1];
-                    en.mask[2] = mask[2];
-                    en.mask[3] = mask[3];
-                    fix[qi] = en;
+            const uint32_t flags = ((norm_amb && !zero) ? kFixNorm : 0u) |
+                                   ((use_exact || !finite) ? kFixAll | kFixNorm : 0u);
+            if (!finite) mask[0] = mask[1] = mask[2] = mask[3] = 0u;
+            const uint32_t ncoord = __popc(mask[0]) + __popc(mask[1]) + __popc(mask[2]) + __popc(mask[3]);
+            if (flags || ncoord) {
+                // one entry per listed coordinate (the first also carries the norm), a
+                // norm-only entry, or one whole-row entry when the table is not in use
+                const bool whole = (flags & kFixAll) != 0;
+                const uint32_t nent = (whole || ncoord == 0) ? 1u : ncoord;
+                const unsigned long long qi = atomicAdd(fix_count, (unsigned long long)nent);
+                if (qi + nent <= fix_cap) {
+                    if (whole || ncoord == 0) {
+                        fix[qi] = FixEntry{(uint32_t)vi, flags, prow};
+                    } else {
+                        uint32_t k = 0, nf = flags;
+#pragma unroll 1
+                        for (int c4 = 0; c4 < 4; ++c4) {
+                            uint32_t m = mask[c4];
+                            while (m) {
+                                const uint32_t i = (uint32_t)(c4 * 32 + __ffs(m) - 1);
+                                m &= m - 1;
+                                fix[qi + k] = FixEntry{(uint32_t)vi, i | kHasCoord | nf, prow};
+                                nf = 0;
+                                ++k;
+                            }
+                        }
+                    }
                 } else {
-                    // queue full: settle the row here
+                    // queue full: mark the reserved entries void and settle the row here
+                    for (unsigned long long t = qi; t < fix_cap; ++t) fix[t] = FixEntry{0u, kSkip, 0};
                     settle_row_inline<TIn, BITS>(a, vi, prow, flags, mask[0], mask[1], mask[2], mask[3], misc->cen);
                 }
             }
@@ -538,103 +622,99 @@ __global__ void __maxnreg__(MAX_REGS)
 }
 
 
-// Settles queued rows with the exact float32 statement, one row per warp: the
-// lanes form the squares, quotients x_j / (norm + 1e-8) and products in
-// parallel (4 coordinates each) and lane 0 adds them up in index order, so
-// every sum is the sequential float32 sum; then the first-minimum nearest
-// centroid, patched into the stored bit stream, and the norm rewritten.
-constexpr int FIX_WARPS = 4;
+// Correctly rounded x / den for fp16 x with |x| <= den, den in [1e-8, 2^20]: from the
+// correctly rounded reciprocal r, two FMA corrections of the quotient (P. Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000 processor", IBM J.
+// Res. Dev. 34(1), 1990): q1 = q0 + (x - den q0) r is faithful, the remainder x - den q1
+// is then exact and q1 + (x - den q1) r is the rounded quotient. Branch-free, so the
+// quotients of a row pipeline. (Checked against exact rational arithmetic on the domain.)
+__device__ __forceinline__ float quot_rn(float x, float den, float r) {
+    const float q0 = __fmul_rn(x, r);
+    const float q1 = __fmaf_rn(__fmaf_rn(-q0, den, x), r, q0);
+    return __fmaf_rn(__fmaf_rn(-q1, den, x), r, q1);
+}
+
+// Settles queued entries with the exact float32 statement, one entry per thread: the
+// sequential sum of the row's squares (norm, rewritten when flagged), then for the
+// entry's coordinate the sequential sum of Pi[i][j] * (x_j / (norm + 1e-8)) and the
+// first-minimum nearest centroid, whose bits are patched into the pool row with word
+// atomics (entries of one row patch disjoint bits). Whole-row entries (table not in
+// use) run settle_row_inline.
+constexpr int FIX_THREADS = 128;
 
 template <typename TIn, int BITS>
-__global__ void __launch_bounds__(FIX_WARPS * 32) tq_fixup_kernel(TqArgs a, const FixEntry* __restrict__ fix,
-                                                                  const unsigned int* __restrict__ fix_count,
-                                                                  unsigned int fix_cap) {
+__global__ void __launch_bounds__(FIX_THREADS) tq_fixup_kernel(TqArgs a, const FixEntry* __restrict__ fix,
+                                                               unsigned long long* fix_count, unsigned int* fix_done,
+                                                               unsigned int fix_cap) {
     __shared__ float cen[256];
-    __shared__ float terms[FIX_WARPS][D];
+    constexpr int EPV = 16 / sizeof(TIn);  // elements per 16-byte vector
+    constexpr int NV = D / EPV;
     const int nlev = 1 << BITS;
+    const int P = (D * BITS) >> 3;
     for (int e = threadIdx.x; e < nlev; e += blockDim.x) cen[e] = __ldg(a.centroids + e);
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* tw = terms[warp];
-    const unsigned int n = min(*fix_count, fix_cap);
-    const int P = (D * BITS) >> 3;
-    for (unsigned int q = blockIdx.x * FIX_WARPS + warp; q < n; q += gridDim.x * FIX_WARPS) {
+    const unsigned long long n = min(*(volatile unsigned long long*)fix_count, (unsigned long long)fix_cap);
+    for (unsigned long long q = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; q < n;
+         q += (unsigned long long)gridDim.x * blockDim.x) {
         const FixEntry en = fix[q];
-        const int64_t vi = en.vi;
-        const int64_t slot = tq_slot(a, vi / a.num_heads);
-        if (slot < 0) continue;
-        const TIn* xr = (const TIn*)a.input + vi * D + 4 * lane;
-        float x[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) x[k] = to_f32(xr[k]);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) tw[4 * lane + k] = __fmul_rn(x[k], x[k]);
-        __syncwarp();
-        float den = 0.0f;
-        if (lane == 0) {
-            float s = 0.0f;
-#pragma unroll 16
-            for (int j = 0; j < D; ++j) s = __fadd_rn(s, tw[j]);
-            const float norm = __fsqrt_rn(s);
-            if (en.flags & kFixNorm)
-                ((__half*)a.norms_pool)[slot * a.num_heads + vi % a.num_heads] = __float2half_rn(norm);
-            den = __fadd_rn(norm, 1e-8f);
-        }
-        den = __shfl_sync(0xffffffffu, den, 0);
-        const bool any = (en.flags & kFixAll) || (en.mask[0] | en.mask[1] | en.mask[2] | en.mask[3]);
-        if (!any) {
-            __syncwarp();
+        if (en.info & kSkip) continue;
+        if (en.info & kFixAll) {
+            settle_row_inline<TIn, BITS>(a, en.vi, en.prow, kFixAll | kFixNorm, 0u, 0u, 0u, 0u, cen);
             continue;
         }
-        float xn[4];
+        const uint4* xr = (const uint4*)((const TIn*)a.input + (int64_t)en.vi * D);
+        Vec16<TIn> xv[NV];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) xn[k] = __fdiv_rn(x[k], den);
-        uint4* rowp = (uint4*)((uint8_t*)a.packed_pool + (slot * a.num_heads + vi % a.num_heads) * P);
-        uint32_t wds[16];
-        if (lane == 0) {
+        for (int c = 0; c < NV; ++c) xv[c].u = __ldg(xr + c);
+        float s = 0.0f;
 #pragma unroll
-            for (int q4 = 0; q4 < P / 16; ++q4) {
-                const uint4 t4 = rowp[q4];
-                wds[4 * q4] = t4.x; wds[4 * q4 + 1] = t4.y; wds[4 * q4 + 2] = t4.z; wds[4 * q4 + 3] = t4.w;
+        for (int c = 0; c < NV; ++c)
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) {
+                const float x = to_f32(xv[c].e[e]);
+                s = __fadd_rn(s, __fmul_rn(x, x));
+            }
+        const float norm = __fsqrt_rn(s);
+        if (en.info & kFixNorm) ((__half*)a.norms_pool)[en.prow] = __float2half_rn(norm);
+        if (!(en.info & kHasCoord)) continue;
+        const float den = __fadd_rn(norm, 1e-8f);
+        const float r = __frcp_rn(den);
+        const int i = (int)(en.info & 127u);
+        const float4* pr = (const float4*)(a.rotation + i * D);
+        float y = 0.0f;
+#pragma unroll
+        for (int c = 0; c < D / 4; ++c) {
+            const float4 p = __ldg(pr + c);
+            const float pv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int j = 4 * c + k;
+                const float x = to_f32(xv[j / EPV].e[j % EPV]);
+                const float qn = dtype_of<TIn>::value == FB_FP16 ? quot_rn(x, den, r) : __fdiv_rn(x, den);
+                y = __fadd_rn(y, __fmul_rn(pv[k], qn));
             }
         }
-        for (int c = 0; c < 4; ++c) {
-            uint32_t m = (en.flags & kFixAll) ? 0xffffffffu : en.mask[c];
-            while (m) {
-                const int i = c * 32 + __ffs(m) - 1;
-                m &= m - 1;
-                const float4 p = __ldg((const float4*)(a.rotation + i * D) + lane);
-                __syncwarp();
-                tw[4 * lane + 0] = __fmul_rn(p.x, xn[0]);
-                tw[4 * lane + 1] = __fmul_rn(p.y, xn[1]);
-                tw[4 * lane + 2] = __fmul_rn(p.z, xn[2]);
-                tw[4 * lane + 3] = __fmul_rn(p.w, xn[3]);
-                __syncwarp();
-                if (lane == 0) {
-                    float y = 0.0f;
-#pragma unroll 16
-                    for (int j = 0; j < D; ++j) y = __fadd_rn(y, tw[j]);
-                    const uint32_t code = (uint32_t)nearest_centroid(y, cen, nlev);
-                    // MSB-first stream bit bp lives in byte bp>>3 at bit 7-(bp&7); bytes little-endian in words
-#pragma unroll
-                    for (int b = 0; b < BITS; ++b) {
-                        const int bp = i * BITS + b;
-                        const int byte = bp >> 3;
-                        const uint32_t bit = 1u << (8 * (byte & 3) + 7 - (bp & 7));
-                        const uint32_t on = (code >> (BITS - 1 - b)) & 1u;
-#pragma unroll
-                        for (int w2 = 0; w2 < 16; ++w2)
-                            if (w2 == (byte >> 2)) wds[w2] = on ? (wds[w2] | bit) : (wds[w2] & ~bit);
-                    }
-                }
-            }
+        const uint32_t code = (uint32_t)nearest_centroid(y, cen, nlev);
+        uint32_t* roww = (uint32_t*)((uint8_t*)a.packed_pool + en.prow * P);
+        for (int b = 0; b < BITS; ++b) {
+            // MSB-first stream bit bp lives in byte bp >> 3 at bit 7 - (bp & 7); bytes little-endian in words
+            const int bp = i * BITS + b;
+            const int byte = bp >> 3;
+            const uint32_t bit = 1u << (8 * (byte & 3) + 7 - (bp & 7));
+            if ((code >> (BITS - 1 - b)) & 1u) atomicOr(roww + (byte >> 2), bit);
+            else atomicAnd(roww + (byte >> 2), ~bit);
         }
-        if (lane == 0) {
-#pragma unroll
-            for (int q4 = 0; q4 < P / 16; ++q4)
-                rowp[q4] = make_uint4(wds[4 * q4], wds[4 * q4 + 1], wds[4 * q4 + 2], wds[4 * q4 + 3]);
+    }
+    // The last block to finish clears the queue header for the next call (every block
+    // read the count before it arrived here).
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(fix_done, 1u) == gridDim.x - 1) {
+            *fix_count = 0ull;
+            *fix_done = 0u;
+            __threadfence();
         }
-        __syncwarp();
     }
 }
 
@@ -663,15 +743,18 @@ static bool device_is_sm100() {
     return major == 10 && minor == 0;
 }
 
-// Fixup queue: one per device, grown to the largest call (24 bytes per vector), kept for the
-// life of the process. The queue is consumed by the fixup kernel of the same launch sequence on
-// the same stream; calls on different streams of one device must not overlap.
+// Fixup queue: one per device, grown to one 16-byte entry per vector of the largest call, kept for the
+// life of the process. Its 256-byte header holds the entry count (u64 at 0) and the fixup kernel's
+// block counter (u32 at 8): zeroed when the queue is allocated, and zeroed again by the fixup kernel
+// once it has consumed the queue. The queue is consumed by the fixup kernel of the same launch
+// sequence on the same stream; calls on different streams of one device must not overlap.
 struct FixWorkspace {
     void* ptr = nullptr;
     size_t cap = 0;  // entries
 };
 
-static int fix_workspace(int64_t nvec, umma::FixEntry** entries, unsigned int** count, unsigned int* cap) {
+static int fix_workspace(int64_t nvec, cudaStream_t s, umma::FixEntry** entries, unsigned long long** count,
+                         unsigned int* cap) {
     static FixWorkspace ws[64];
     static std::mutex mu;
     int dev = 0;
@@ -690,9 +773,11 @@ static int fix_workspace(int64_t nvec, umma::FixEntry** entries, unsigned int** 
         w.cap = 0;
         e = cudaMalloc(&w.ptr, 256 + want * sizeof(umma::FixEntry));
         if (e != cudaSuccess) return (int)e;
+        e = cudaMemsetAsync(w.ptr, 0, 256, s);
+        if (e != cudaSuccess) return (int)e;
         w.cap = want;
     }
-    *count = (unsigned int*)w.ptr;
+    *count = (unsigned long long*)w.ptr;
     *entries = (umma::FixEntry*)((char*)w.ptr + 256);
     *cap = (unsigned int)std::min<size_t>(w.cap, 0xffffffffu);
     return 0;
@@ -701,16 +786,18 @@ static int fix_workspace(int64_t nvec, umma::FixEntry** entries, unsigned int** 
 // Fixup queue of the no-allocation entry point: a file-scope device array, so that a call
 // allocates nothing. It holds the queue header (256 bytes) and one entry per vector of the
 // largest call accepted, kTqNoAllocMaxVectors (524288 vectors, e.g. 65536 tokens x 8 KV heads):
-// 12 MiB + 256 bytes per device, reserved when the module loads. One array per device serves
+// 8 MiB + 256 bytes per device, reserved when the module loads. One array per device serves
 // every call on that device, so calls that overlap in time (two streams, two host threads)
 // race on it.
 static __device__ __align__(256) unsigned char
     g_tq_fix_scratch[256 + (size_t)kTqNoAllocMaxVectors * sizeof(umma::FixEntry)];
 
-// Set-up, once per device with that device current: the device address of g_tq_fix_scratch.
-// The first call on a device does this set-up (it may load the module), so it belongs before
-// any stream capture; later calls only read the cached address.
-static int static_fix_scratch(int64_t nvec, umma::FixEntry** entries, unsigned int** count, unsigned int* cap) {
+// Set-up, once per device with that device current: the device address of g_tq_fix_scratch,
+// and its queue header cleared on the call's stream. The first call on a device does this set-up
+// (it may load the module), so it belongs before any stream capture; later calls only read the
+// cached address (the fixup kernel leaves the header cleared).
+static int static_fix_scratch(int64_t nvec, cudaStream_t s, umma::FixEntry** entries, unsigned long long** count,
+                              unsigned int* cap) {
     static void* addr[64];
     static std::mutex mu;
     if (nvec > kTqNoAllocMaxVectors) return (int)cudaErrorInvalidValue;
@@ -724,9 +811,11 @@ static int static_fix_scratch(int64_t nvec, umma::FixEntry** entries, unsigned i
         e = cudaGetSymbolAddress(&p, g_tq_fix_scratch);
         if (e != cudaSuccess) return (int)e;
         if (!p) return (int)cudaErrorInvalidSymbol;
+        e = cudaMemsetAsync(p, 0, 256, s);  // the queue header starts at zero
+        if (e != cudaSuccess) return (int)e;
         addr[dev] = p;
     }
-    *count = (unsigned int*)addr[dev];
+    *count = (unsigned long long*)addr[dev];
     *entries = (umma::FixEntry*)((char*)addr[dev] + 256);
     *cap = (unsigned int)kTqNoAllocMaxVectors;
     return 0;
@@ -748,25 +837,28 @@ static int launch_umma(const TqArgs& a, cudaStream_t s, bool static_scratch) {
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return (int)cudaErrorInvalidValue;
     umma::FixEntry* fix;
-    unsigned int* fix_count;
+    unsigned long long* fix_count;
     unsigned int fix_cap;
-    int rc = static_scratch ? static_fix_scratch(nvec, &fix, &fix_count, &fix_cap)
-                            : fix_workspace(nvec, &fix, &fix_count, &fix_cap);
+    int rc = static_scratch ? static_fix_scratch(nvec, s, &fix, &fix_count, &fix_cap)
+                            : fix_workspace(nvec, s, &fix, &fix_count, &fix_cap);
     if (rc) return rc;
-    // the queue counter must start at zero; the entries are written before they are read
-    cudaError_t e = cudaMemsetAsync(fix_count, 0, sizeof(unsigned int), s);
-    if (e != cudaSuccess) return (int)e;
+    unsigned int* fix_done = (unsigned int*)((char*)fix_count + 8);
     constexpr int smem = umma::Smem::bytes(NPARTS);
     auto kern = umma::tq_compress_umma_kernel<TIn, NPARTS, BITS>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
     const int num_tiles = (int)((nvec + umma::TILE - 1) / umma::TILE);
     const int grid = std::max(1, std::min(num_tiles, num_sms()));
     kern<<<grid, umma::THREADS, smem, s>>>(map, a, num_tiles, fix, fix_count, fix_cap);
     e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
-    umma::tq_fixup_kernel<TIn, BITS><<<num_sms() * 16, umma::FIX_WARPS * 32, 0, s>>>(a, fix, fix_count, fix_cap);
-    return (int)cudaGetLastError();
+    umma::tq_fixup_kernel<TIn, BITS><<<num_sms() * 2, umma::FIX_THREADS, 0, s>>>(a, fix, fix_count, fix_done, fix_cap);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        cudaMemsetAsync(fix_count, 0, 16, s);  // the header must be clear for the next call
+        return (int)e;
+    }
+    return 0;
 }
 
 static int umma_dispatch(const TqArgs& a, cudaStream_t s, bool* handled, bool static_scratch) {

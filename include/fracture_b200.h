@@ -123,7 +123,7 @@ int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotat
 
 /* fb_launch_tq_compress_paged that allocates no device memory (no reference counterpart; the
  * reference allocates per call). Results are identical to fb_launch_tq_compress_paged. The fixup
- * queue of the tensor-core path is a static device array (12 MiB + 256 B per device) sized for at
+ * queue of the tensor-core path is a static device array (8 MiB + 256 B per device) sized for at
  * most 524288 vectors per call (num_tokens * num_kv_heads); larger calls return
  * cudaErrorInvalidValue with the reason in fb_last_error(), before anything is launched. The first
  * call on a device does set-up (looks up the array's device address), so make it before any

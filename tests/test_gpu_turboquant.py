@@ -251,3 +251,48 @@ def test_tensor_core_path_adversarial_vectors():
     pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits)
     assert np.array_equal(packed.cpu().numpy(), pc)
     assert np.array_equal(norms.cpu().numpy().view(np.uint16), nc)
+
+
+def _boundary_codebook(values, n_levels):
+    """Centroids whose decision boundaries (c_k + c_{k+1}) / 2 sit on chosen y values.
+
+    Walks upwards from c_0 (just below the smallest value): the next boundary is the smallest
+    of ``values`` between 0.012 and 0.03 above the current centroid (else a synthetic one 0.015 above), and the next
+    centroid mirrors the current one across it, so centroids increase by at least 0.024
+    and boundaries are at least 0.024 apart."""
+    vals = np.sort(np.asarray(values, np.float64))
+    c = [max(-0.42, float(vals[0]) - 0.013)]
+    mids = []
+    while len(c) < n_levels:
+        lo, hi = c[-1] + 0.012, c[-1] + 0.03
+        pick = vals[(vals > lo) & (vals <= hi)]
+        if mids:
+            pick = pick[pick - mids[-1] >= 0.025]
+        v = float(pick[0]) if pick.size else c[-1] + 0.015
+        mids.append(v)
+        c.append(2.0 * v - c[-1])
+    return np.array(c, dtype=np.float32), np.array(mids)
+
+
+def test_tensor_core_path_queue_overflow():
+    """Every row has 15 coordinates on a decision boundary, so the exact-settle queue overflows:
+    rows beyond its capacity are settled inside the main kernel, and the partly reserved
+    entries are voided. The result still equals the exact statement bit for bit."""
+    T, H, d, bits = 300, 8, 128, 4
+    pi = K.tq_rotation_matrix(d, 42)
+    rng = np.random.default_rng(11)
+    c, m = _boundary_codebook(pi[:, 0], 1 << bits)
+    assert np.all(np.diff(c) > 0)
+    # x = v * e_0 with v + 1e-8 == v in float32: x / (norm + 1e-8) = e_0 and y = Pi[:, 0] exactly
+    x = np.zeros((T, H, d), np.float32)
+    x[:, :, 0] = rng.choice([0.5, 1.0, 3.0, 100.0, -2.0], size=(T, H))
+    raw = ops.to_storage_bytes(x, "f16").reshape(x.shape)
+    y = pi[:, 0]
+    assert np.sum(np.min(np.abs(y[:, None] - m[None, :]), axis=1) < 1e-6) >= 10
+    packed = torch.zeros((T, H * 64), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((T, H), dtype=torch.float16, device=DEV)
+    K.tq_compress_paged(dev(x, "f16"), torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed, norms)
+    torch.cuda.synchronize()
+    pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits)
+    assert np.array_equal(packed.cpu().numpy(), pc)
+    assert np.array_equal(norms.cpu().numpy().view(np.uint16), nc)
