@@ -30,6 +30,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "tq_common.cuh"
@@ -504,6 +505,11 @@ __global__ void __maxnreg__(MAX_REGS)
             // warp once the last chunk is in registers.
             uint32_t mask[4] = {0u, 0u, 0u, 0u};
             uint32_t w[WPR];
+            // SAFE: a row of this warp is not finite (NaN/inf in the input); its accumulator
+            // values are replaced by 0 so every table index stays in range (the row is
+            // settled whole by the exact path).
+            auto pass2 = [&](auto safe_tag) {
+            constexpr bool SAFE = decltype(safe_tag)::value;
 #pragma unroll
             for (int c = NCH - 1; c >= 0; --c) {
                 // chunk NCH-1 is in the buffer pass 1 used last; the chunks below alternate
@@ -527,7 +533,7 @@ __global__ void __maxnreg__(MAX_REGS)
                     uint32_t code[G];
 #pragma unroll
                     for (int q = 0; q < G; ++q) {
-                        const float v = __uint_as_float(cur[w2 * G + q]);
+                        const float v = (SAFE && !finite) ? 0.0f : __uint_as_float(cur[w2 * G + q]);
                         const float u = fmaf(v, ku, ubias);
                         const uint32_t addr = __float_as_uint(u) * (LUT_COPIES * 8u) + lut_lane;
                         float mid;
@@ -550,7 +556,7 @@ __global__ void __maxnreg__(MAX_REGS)
                     uint32_t m = 0;
 #pragma unroll
                     for (int j = 0; j < CW; ++j) {
-                        const float v = __uint_as_float(cur[j]);
+                        const float v = (SAFE && !finite) ? 0.0f : __uint_as_float(cur[j]);
                         const float u = fmaf(v, ku, ubias);
                         const uint32_t addr = __float_as_uint(u) * (LUT_COPIES * 8u) + lut_lane;
                         float mid;
@@ -576,6 +582,9 @@ __global__ void __maxnreg__(MAX_REGS)
                     }
                 }
             }
+            };
+            if (__any_sync(0xffffffffu, !finite)) pass2(std::true_type{});
+            else pass2(std::false_type{});
             if (prow < 0) continue;
             ((__half*)a.norms_pool)[prow] = __float2half_rn(norm_f);
             const uint32_t flags = ((norm_amb && !zero) ? kFixNorm : 0u) |

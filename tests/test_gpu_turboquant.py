@@ -296,3 +296,34 @@ def test_tensor_core_path_queue_overflow():
     pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits)
     assert np.array_equal(packed.cpu().numpy(), pc)
     assert np.array_equal(norms.cpu().numpy().view(np.uint16), nc)
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_tensor_core_path_non_finite_rows(dt):
+    """Rows holding NaN or +-inf (and, for BF16, values whose squares overflow float32) next to
+    ordinary rows of the same warp: the tensor-core path keeps every table index in range, and
+    every row equals the exact statement (NaN rows code to index 0; NaN norms compared as NaN)."""
+    T, H, d, bits = 64, 8, 128, 4
+    x, _ = make_input(T, H, d, dt, seed=21)
+    x[0, 1, 5] = np.nan
+    x[1, 2, 0] = np.inf
+    x[2, 3, 7] = -np.inf
+    x[3, 4, 9], x[3, 4, 10] = np.inf, -np.inf
+    x[9, 0, :] = np.nan
+    if dt == "bf16":
+        x[5, 6, :] = 1e30  # |x|^2 overflows float32: norm = inf, y = 0
+        x[6, 7, 3] = -3e38
+    x = ops.round_to(x, dt)
+    raw = ops.to_storage_bytes(x, dt).reshape(x.shape)
+    pi, c = tables(d, bits, 42)
+    packed = torch.zeros((T, H * 64), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((T, H), dtype=torch.float16, device=DEV)
+    K.tq_compress_paged(dev(x, dt), torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed, norms)
+    torch.cuda.synchronize()
+    pc, nc, _ = tq.compress_c(raw, KIND[dt], pi, c, bits)
+    assert np.array_equal(packed.cpu().numpy(), pc)
+    got = norms.cpu().numpy()
+    exp = nc.view(np.float16)
+    both_nan = np.isnan(got) & np.isnan(exp)
+    assert np.array_equal(got.view(np.uint16)[~both_nan], nc[~both_nan])
+    assert np.array_equal(np.isnan(got), np.isnan(exp))
