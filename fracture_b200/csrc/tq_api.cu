@@ -12,6 +12,7 @@
 namespace fb {
 int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled);
 int tq_compress_umma_noalloc(const TqArgs& a, cudaStream_t s, bool* handled);
+int tq_dequant_umma(const TqArgs& a, cudaStream_t s, bool* handled);
 void set_last_error(const char* msg);
 }
 
@@ -128,6 +129,9 @@ extern "C" int fb_launch_tq_dequant_paged(const void* packed_pool, const void* n
     a.norms_pool = const_cast<void*>(norms_pool);
     a.output = output;
     a.out_dtype = dtype;
+    bool handled = false;
+    rc = tq_dequant_umma(a, (cudaStream_t)stream, &handled);
+    if (handled) return rc;
     return tq_dequant_exact(a, (cudaStream_t)stream);
 }
 

@@ -34,6 +34,7 @@
 
 #include "common.cuh"
 #include "tq_common.cuh"
+#include "tq_sm100.cuh"
 
 namespace fb {
 
@@ -41,11 +42,9 @@ __device__ unsigned int g_tq_umma_timeouts = 0;
 
 namespace umma {
 
-constexpr int D = 128;              // head_dim
-constexpr int TILE = 128;           // vectors per tile
+using namespace sm100;
+
 constexpr int STAGES = 3;           // A-tile pipeline depth
-constexpr int KBLK_BYTES = TILE * 128;    // one K-block (64 elements) of a 128-row tile, SW128
-constexpr int TILE_BYTES = 2 * KBLK_BYTES;  // 32 KB
 constexpr int NB = 128;             // decision-table bins; bin b covers y in [(b - kBin0 -+ 1/2) w]
 constexpr int kBin0 = 64;           // the bin centred on y = 0
 constexpr float kInvW = 63.5f / 1.02f;  // 1 / bin width: bins span [-1.036, 1.02), and |y| <= 1
@@ -92,28 +91,6 @@ struct Smem {
     static constexpr int bytes(int nparts) { return misc_off(nparts) + (int)sizeof(Misc) + 1024; }
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
 // Bounded wait for the phase with parity `parity`; false (and a counted timeout) if it never completes.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -128,87 +105,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     return true;
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
-        : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    return (uint64_t)((saddr & 0x3FFFF) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-// Instruction descriptor: D f32, A/B fp16 (fmt 0) or bf16 (fmt 1), both K-major, M=128, N=128.
-__host__ __device__ constexpr uint32_t idesc_f16(uint32_t fmt) {
-    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(D >> 3) << 17) | ((uint32_t)(TILE >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Issues a 32-column TMEM load of this thread's accumulator row into r; the values are
-// valid only after tmem_wait_tie(r).
-__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-
-// Waits for this thread's TMEM loads. The registers of the load are in-out operands, so
-// no use of them can be scheduled before the wait.
-__device__ __forceinline__ void tmem_wait_tie(uint32_t (&r)[32]) {
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
-                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
-                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
-                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
-                 :
-                 : "memory");
-}
-
-// 16-column variants of the two helpers above.
-__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_wait_tie(uint32_t (&r)[16]) {
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
-                   "+r"(r[15])
-                 :
-                 : "memory");
-}
-
 // One table entry per (bin, copy). The 16 copies of a bin sit side by side, so the
 // 16 lanes of each half-warp read 16 different bank pairs with one 64-bit load.
 struct LutEntry {
@@ -216,12 +112,6 @@ struct LutEntry {
     uint32_t base;  // code below the boundary (the code of the whole bin when it holds none)
 };
 
-// Byte offset in the SW128 K-major image of element (row n, column k) of a
-// 128 x 128 tile stored as two 64-column K-blocks.
-__device__ __forceinline__ int sw128_offset(int n, int k) {
-    const int kb = k >> 6, kk = k & 63;
-    return kb * KBLK_BYTES + n * 128 + ((((kk >> 3) ^ (n & 7))) << 4) + ((kk & 7) << 1);
-}
 
 // Exact float32 statement for one queued row, by one thread, on the stored bytes:
 // the sequential sum of the squares (norm), then for each listed coordinate the
@@ -432,7 +322,7 @@ __global__ void __maxnreg__(MAX_REGS)
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
                             const uint32_t off = kb * KBLK_BYTES + k * 32;
-                            umma(d, sw128_desc(a0 + s * TILE_BYTES + off), sw128_desc(b0 + p * TILE_BYTES + off), idesc,
+                            mma_f16(d, sw128_desc(a0 + s * TILE_BYTES + off), sw128_desc(b0 + p * TILE_BYTES + off), idesc,
                                  acc);
                             acc = 1;
                         }
@@ -901,8 +791,12 @@ int tq_compress_umma_noalloc(const TqArgs& a, cudaStream_t s, bool* handled) {
 
 }  // namespace fb
 
+namespace fb {
+unsigned int tq_dequant_timeouts();
+}
+
 extern "C" unsigned int fb_tq_timeouts(void) {
     unsigned int v = 0;
     cudaMemcpyFromSymbol(&v, fb::g_tq_umma_timeouts, sizeof(v));
-    return v;
+    return v + fb::tq_dequant_timeouts();
 }

@@ -136,14 +136,18 @@ int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype, const floa
                                         unsigned int* err_count, void* stream);
 
 /* TurboQuant dequantize from a paged pool into [num_tokens, Hkv, d] (`dtype` FP16/BF16/FP32):
- * x = (Pi^T @ centroids[idx]) * norm (replaces turboquant_decompress.cu:21-94). Same slot rule. */
+ * x = (Pi^T @ centroids[idx]) * norm (replaces turboquant_decompress.cu:21-94). Same slot rule; a
+ * token without a valid slot dequantizes to zeros. head_dim 128 with 2/3/4-bit codes and FP16/BF16
+ * output runs on the tensor cores (one fp16 pass: within about 1e-4 of the output's magnitude of
+ * the float32 statement); every other case evaluates the float32 statement exactly. */
 int fb_launch_tq_dequant_paged(const void* packed_pool, const void* norms_pool, const float* rotation,
                                const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
                                int head_dim, const int32_t* block_table, int64_t start_pos,
                                int64_t num_pool_rows, void* output, int dtype, void* stream);
 
-/* Number of bounded waits that timed out inside the tensor-core TurboQuant kernel since the library
- * was loaded (0 in normal operation; a timeout abandons the launch's remaining tiles). */
+/* Number of bounded waits that timed out inside the tensor-core TurboQuant kernels (compress and
+ * dequantize) since the library was loaded (0 in normal operation; a timeout abandons the launch's
+ * remaining tiles). */
 unsigned int fb_tq_timeouts(void);
 
 /* Host tables. */

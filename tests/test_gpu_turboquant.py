@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 import torch
 
+from fracture_b200 import _lib
 from fracture_b200 import kernels as K
 from oracle import ops, turboquant as tq
 
@@ -327,3 +328,61 @@ def test_tensor_core_path_non_finite_rows(dt):
     both_nan = np.isnan(got) & np.isnan(exp)
     assert np.array_equal(got.view(np.uint16)[~both_nan], nc[~both_nan])
     assert np.array_equal(np.isnan(got), np.isnan(exp))
+
+
+# ── tensor-core dequantize (head_dim 128, 2/3/4 bits, FP16/BF16 output) ──
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("bits", [2, 3, 4])
+def test_tensor_core_dequant_paged_many_tiles(dt, bits):
+    """4099 tokens x 8 heads (257 tiles, the last one partial) from a shuffled paged pool with an
+    unaligned start; against the float32 statement: within 3e-4 of the magnitude beyond the output
+    dtype's rounding (the north-star bar is 2e-3) and cosine >= 0.9999."""
+    T, H, d, start = 4099, 8, 128, 21
+    x, raw = make_input(T, H, d, "f16", seed=300 + bits)
+    pi, c = tables(d, bits, 4242)
+    P = d * bits // 8
+    nblk = (start + T + 15) // 16 + 3
+    table = np.random.default_rng(bits).permutation(nblk).astype(np.int32)
+    rows = nblk * 16
+    tpi, tc, tt = torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), torch.from_numpy(table).to(DEV)
+    packed = torch.zeros((rows, H * P), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((rows, H), dtype=torch.float16, device=DEV)
+    K.tq_compress_paged(dev(x, "f16"), tpi, tc, bits, packed, norms, block_table=tt, start_pos=start)
+    out = torch.full((T, H, d), 7.0, dtype=TDT[dt], device=DEV)
+    before = _lib.load().fb_tq_timeouts()
+    K.tq_dequant_paged(packed, norms, tpi, tc, bits, out, block_table=tt, start_pos=start)
+    torch.cuda.synchronize()
+    assert _lib.load().fb_tq_timeouts() == before
+    pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits, num_threads=8)
+    ref = tq.decompress_c(pc, nc, pi, c, bits, H, d).reshape(T, H, d)
+    got = out.float().cpu().numpy()
+    ops.assert_close_fp(got, ref, rel=3e-4, min_cos=0.9999, label=f"tensor-core dequant {dt}/{bits}", dtype=dt)
+    # every vector on its own
+    num = (got * ref).sum(-1)
+    den = np.linalg.norm(got, axis=-1) * np.linalg.norm(ref, axis=-1) + 1e-30
+    assert (num / den).min() > 0.9999
+
+
+def test_tensor_core_dequant_missing_blocks_give_zeros():
+    """Tokens whose block-table entry is -1 dequantize to zeros, like the CUDA-core kernel."""
+    T, H, d, bits = 300, 8, 128, 4
+    x, _ = make_input(T, H, d, "f16", seed=5)
+    pi, c = tables(d, bits, 42)
+    nblk = (T + 15) // 16
+    table = np.arange(nblk, dtype=np.int32)
+    tpi, tc = torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV)
+    packed = torch.zeros((nblk * 16, H * 64), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((nblk * 16, H), dtype=torch.float16, device=DEV)
+    K.tq_compress_paged(dev(x, "f16"), tpi, tc, bits, packed, norms, block_table=torch.from_numpy(table).to(DEV))
+    table[[3, 7]] = -1
+    out16 = torch.full((T, H, d), 5.0, dtype=torch.float16, device=DEV)
+    out32 = torch.full((T, H, d), 5.0, dtype=torch.float32, device=DEV)
+    tt = torch.from_numpy(table).to(DEV)
+    K.tq_dequant_paged(packed, norms, tpi, tc, bits, out16, block_table=tt)
+    K.tq_dequant_paged(packed, norms, tpi, tc, bits, out32, block_table=tt)  # CUDA-core kernel
+    torch.cuda.synchronize()
+    g16, g32 = out16.float().cpu().numpy(), out32.cpu().numpy()
+    for b in (3, 7):
+        assert not g16[16 * b:16 * b + 16].any() and not g32[16 * b:16 * b + 16].any()
+    ops.assert_close_fp(g16, g32, rel=3e-4, label="tensor-core vs CUDA-core dequant", dtype="f16")
