@@ -378,6 +378,19 @@ def profile_kernel(args) -> None:
         packed = torch.empty((Tk, NKV * 64), dtype=torch.uint8, device=dev)
         norms = torch.empty((Tk, NKV), dtype=torch.float16, device=dev)
         fn = lambda: K.tq_compress_paged(x, rot, cen, 4, packed, norms, block_table=table)
+    elif args.profile_kernel == "tq_dequant":
+        # BASELINE config 4 dequantize: the K pool of 65536 tokens x 8 KV heads x 128 back to FP16
+        Tk = 65536
+        x = torch.randn((Tk, NKV, HD), generator=g, device=dev)
+        x = torch.where(torch.rand((Tk, NKV, HD), generator=g, device=dev) < 0.005, x * 10, x).to(torch.float16)
+        rot = torch.from_numpy(K.tq_rotation_matrix(HD, 42)).to(dev)
+        cen = torch.from_numpy(K.tq_codebook(HD, 4)[0]).to(dev)
+        table = torch.randperm(Tk // 16, generator=g, device=dev).to(torch.int32)
+        packed = torch.empty((Tk, NKV * 64), dtype=torch.uint8, device=dev)
+        norms = torch.empty((Tk, NKV), dtype=torch.float16, device=dev)
+        K.tq_compress_paged(x, rot, cen, 4, packed, norms, block_table=table)
+        out = torch.empty((Tk, NKV, HD), dtype=torch.float16, device=dev)
+        fn = lambda: K.tq_dequant_paged(packed, norms, rot, cen, 4, out, block_table=table)
     else:
         tab = rnd(VOCAB, HID)
         ids = torch.randint(0, VOCAB, (T,), generator=g, device=dev, dtype=torch.int32)
@@ -401,7 +414,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
-    ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding", "tq_compress"],
+    ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding", "tq_compress",
+                                                                   "tq_dequant"],
                     help="run only this kernel at its config-3 size (W warm-up launches + 1), for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

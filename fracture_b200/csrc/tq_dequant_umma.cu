@@ -14,7 +14,7 @@
 //                of the row through the block table and write fp16 centroid values
 //                straight into the 128-byte-swizzled A tile, through lane-private
 //                lookup tables (two 4-bit, four 2-bit or two 3-bit codes per lookup)
-//   warps 9-16   epilogue, two warpgroups on alternating TMEM buffers: one thread per
+//   warps 9-16   epilogue, two warpgroups on alternating tiles (four TMEM accumulators): one thread per
 //                vector scales its accumulator row by the stored fp16 norm, converts,
 //                stages the tile in swizzled shared memory, and one thread writes it out
 //                with two TMA tensor stores
@@ -43,21 +43,30 @@ namespace dq {
 using namespace sm100;
 
 constexpr int A_STAGES = 2;  // A tiles in flight
-constexpr int TBUF = 2;      // TMEM accumulators = epilogue warpgroups = staging tiles
+constexpr int NACC = 4;      // TMEM accumulators (4 x 128 columns: all of TMEM)
+constexpr int TBUF = 2;      // epilogue warpgroups = output staging tiles
 constexpr int DEC_WARPS = 8;
 constexpr int EPI_WARPS = 4 * TBUF;
 constexpr int THREADS = 32 * (1 + DEC_WARPS + EPI_WARPS);
 constexpr int MAX_REGS = 96;  // 17 warps: up to 5 on one scheduler, 16K registers each
+// Norms travel from the decoders to the epilogue through shared memory, one row of 128 per
+// tile, NORM_BUF rows deep: the decoder of tile i + NORM_BUF can only start after the MMA of
+// tile i + NACC, which waits for the epilogue of tile i to release its accumulator.
+constexpr int NORM_BUF = A_STAGES + NACC;
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 struct Misc {
     uint64_t a_full[A_STAGES];
     uint64_t a_empty[A_STAGES];
-    uint64_t tfull[TBUF];
-    uint64_t tempty[TBUF];
+    uint64_t tfull[NACC];
+    uint64_t tempty[NACC];
     uint64_t st_free[TBUF];  // staging tile may be overwritten (its last TMA store has read it)
     uint64_t st_full[TBUF];  // staging tile written by all four warps of the warpgroup
+    uint64_t pi_full;        // Pi (fp32) copied into the staging area for the set-up
     uint32_t tmem_base;
+    float cen[16];
+    uint64_t norm_full[NORM_BUF];  // the decoders have written norm[k] for the tile
+    float norm[NORM_BUF][TILE];    // written by the decoders (h == 0), read by the epilogue
 };
 
 // Lookup tables of the decoders, lane-private so the 32 lanes of a warp hit 32 banks:
@@ -128,7 +137,7 @@ __global__ void __maxnreg__(MAX_REGS)
 
     // ── prologue ─────────────────────────────────────────────────────────────
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
                          smem_u32(&misc->tmem_base))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -139,32 +148,49 @@ __global__ void __maxnreg__(MAX_REGS)
             mbar_init(&misc->a_full[s], DEC_WARPS);
             mbar_init(&misc->a_empty[s], 1);
         }
-        for (int b = 0; b < TBUF; ++b) {
+        for (int b = 0; b < NACC; ++b) {
             mbar_init(&misc->tfull[b], 1);
             mbar_init(&misc->tempty[b], 4);
+        }
+        for (int b = 0; b < TBUF; ++b) {
             mbar_init(&misc->st_free[b], 1);
             mbar_init(&misc->st_full[b], 4);
         }
+        mbar_init(&misc->pi_full, 1);
+        for (int k = 0; k < NORM_BUF; ++k) mbar_init(&misc->norm_full[k], DEC_WARPS);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // Pi (64 KB fp32) lands in the output staging area, which is free until the first tile
+        mbar_expect_tx(&misc->pi_full, D * D * 4);
+        bulk_load(sST, a.rotation, D * D * 4, &misc->pi_full);
     }
-    // B operand: B[i][j] = Pi[j][i] in fp16 (K-major: the contraction index j is contiguous).
-    for (int e = threadIdx.x; e < D * D; e += THREADS) {
-        const int j = e >> 7, i = e & (D - 1);
-        *(__half*)(sB + sw128_offset(i, j)) = __float2half_rn(__ldg(a.rotation + e));
-    }
+    if (threadIdx.x < nlev) misc->cen[threadIdx.x] = __ldg(a.centroids + threadIdx.x);
+    __syncthreads();
     // Decode tables (codes in MSB-first order: the first code of a byte is its high bits).
     for (int e = threadIdx.x; e < TB::entries * TB::copies; e += THREADS) {
         const int ent = e / TB::copies;
+        const float* cen = misc->cen;
         if constexpr (BITS == 4) {
-            const __half2 h = __floats2half2_rn(__ldg(a.centroids + (ent >> 4)), __ldg(a.centroids + (ent & 15)));
-            ((uint32_t*)tab)[e] = h2_bits(h);
+            ((uint32_t*)tab)[e] = h2_bits(__floats2half2_rn(cen[ent >> 4], cen[ent & 15]));
         } else if constexpr (BITS == 3) {
-            const __half2 h = __floats2half2_rn(__ldg(a.centroids + (ent >> 3)), __ldg(a.centroids + (ent & 7)));
-            ((uint32_t*)tab)[e] = h2_bits(h);
+            ((uint32_t*)tab)[e] = h2_bits(__floats2half2_rn(cen[ent >> 3], cen[ent & 7]));
         } else {
-            const __half2 h0 = __floats2half2_rn(__ldg(a.centroids + (ent >> 6)), __ldg(a.centroids + ((ent >> 4) & 3)));
-            const __half2 h1 = __floats2half2_rn(__ldg(a.centroids + ((ent >> 2) & 3)), __ldg(a.centroids + (ent & 3)));
+            const __half2 h0 = __floats2half2_rn(cen[ent >> 6], cen[(ent >> 4) & 3]);
+            const __half2 h1 = __floats2half2_rn(cen[(ent >> 2) & 3], cen[ent & 3]);
             ((uint2*)tab)[e] = make_uint2(h2_bits(h0), h2_bits(h1));
+        }
+    }
+    // B operand: B[i][j] = Pi[j][i] in fp16 (K-major: the contraction index j is contiguous);
+    // item (i, j0) packs Pi[j0..j0+7][i] into one 16-byte chunk.
+    mbar_wait(&misc->pi_full, 0);  // a timeout is counted (B would then be garbage)
+    {
+        const float* pis = (const float*)sST;
+        for (int it = threadIdx.x; it < D * D / 8; it += THREADS) {
+            const int i = it & (D - 1), j0 = (it >> 7) * 8;
+            uint32_t o[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                o[k] = h2_bits(__floats2half2_rn(pis[(j0 + 2 * k) * D + i], pis[(j0 + 2 * k + 1) * D + i]));
+            *(uint4*)(sB + sw128_offset(i, j0)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
     }
     (void)nlev;
@@ -180,9 +206,9 @@ __global__ void __maxnreg__(MAX_REGS)
             const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
             int done = 0;
             for (int i = 0; i < ntiles_cta; ++i) {
-                const int s = i % A_STAGES, buf = i % TBUF;
+                const int s = i % A_STAGES, buf = i % NACC;
                 if (!mbar_wait(&misc->a_full[s], (i / A_STAGES) & 1)) break;
-                if (!mbar_wait(&misc->tempty[buf], ((i / TBUF) + 1) & 1)) break;
+                if (!mbar_wait(&misc->tempty[buf], ((i / NACC) + 1) & 1)) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(buf * D);
 #pragma unroll
@@ -198,46 +224,67 @@ __global__ void __maxnreg__(MAX_REGS)
                 done = i + 1;
             }
             // The last accumulations finish before TMEM is released.
-            if (done > 0) mbar_wait(&misc->tfull[(done - 1) % TBUF], ((done - 1) / TBUF) & 1);
+            if (done > 0) mbar_wait(&misc->tfull[(done - 1) % NACC], ((done - 1) / NACC) & 1);
         }
     } else if (warp <= DEC_WARPS) {
         // ── decoders: thread dt handles half h of row r ─────────────────────
+        // The packed codes of tile i+1 and the block-table entry of tile i+2 are requested
+        // while tile i is decoded, so the two dependent global loads overlap the pipeline.
         const int dt = threadIdx.x - 32;
         const int r = dt >> 1, h = dt & 1;
         const uint32_t tlane = smem_u32(tab) + (uint32_t)(lane & (TB::copies - 1)) * TB::entry_bytes;
-        for (int i = 0; i < ntiles_cta; ++i) {
-            const int s = i % A_STAGES;
-            const int tile = (int)blockIdx.x + i * (int)gridDim.x;
-            const int64_t vi = (int64_t)tile * TILE + r;
-            int64_t slot = -1;
-            if (vi < nvec) slot = tq_slot(a, vi / a.num_heads);
-            const uint8_t* src =
-                slot >= 0 ? (const uint8_t*)a.packed_pool + (slot * a.num_heads + vi % a.num_heads) * P + h * (P / 2)
-                          : nullptr;
-            // this half-row's packed bytes (zeros when the vector has no slot)
-            uint32_t wv[BITS * 2];
+        constexpr int NW = BITS * 2;  // 32-bit words of packed codes per half-row
+        // Pool row of this thread's vector in tile i, in two steps so that no branch waits on
+        // a load: bt_of issues the block-table read (-1: no vector; 0 without a table), row_of
+        // applies the slot rule of tq_slot to it two steps later (-1: no row).
+        // (32-bit division: the host keeps the vector count below 2^31.)
+        // Prefetched values stay raw (int32 table entry, fp16 norm bits) until they are used,
+        // so no conversion waits on a load that is still in flight.
+        auto bt_of = [&](int i) -> int32_t {
+            const uint32_t vi = (uint32_t)((int)blockIdx.x + i * (int)gridDim.x) * TILE + r;
+            if (i >= ntiles_cta || (int64_t)vi >= nvec) return -1;
+            const int64_t pos = a.start_pos + vi / (uint32_t)a.num_heads;
+            return a.block_table ? __ldg(a.block_table + (pos >> 4)) : (int32_t)0;
+        };
+        auto row_of = [&](int i, int32_t bt) -> int64_t {
+            if (bt < 0) return -1;
+            const uint32_t vi = (uint32_t)((int)blockIdx.x + i * (int)gridDim.x) * TILE + r;
+            const uint32_t tok = vi / (uint32_t)a.num_heads, head = vi - tok * (uint32_t)a.num_heads;
+            const int64_t pos = a.start_pos + tok;
+            const int64_t slot = a.block_table ? (int64_t)bt * 16 + (pos & 15) : pos;
+            return slot < a.pool_rows ? slot * a.num_heads + head : -1;
+        };
+        auto load_codes = [&](int64_t prow, uint32_t (&wv)[NW]) {  // zeros when there is no row
 #pragma unroll
-            for (int k = 0; k < BITS * 2; ++k) wv[k] = 0u;
-            if (src) {
-                if constexpr (BITS == 3) {
+            for (int k = 0; k < NW; ++k) wv[k] = 0u;
+            if (prow < 0) return;
+            const uint8_t* src = (const uint8_t*)a.packed_pool + prow * P + h * (P / 2);
+            if constexpr (BITS == 3) {
 #pragma unroll
-                    for (int k = 0; k < 3; ++k) {
-                        const uint2 t = __ldg((const uint2*)src + k);
-                        wv[2 * k] = t.x;
-                        wv[2 * k + 1] = t.y;
-                    }
-                } else {
+                for (int k = 0; k < 3; ++k) {
+                    const uint2 t = __ldg((const uint2*)src + k);
+                    wv[2 * k] = t.x;
+                    wv[2 * k + 1] = t.y;
+                }
+            } else {
 #pragma unroll
-                    for (int k = 0; k < BITS / 2; ++k) {
-                        const uint4 t = __ldg((const uint4*)src + k);
-                        wv[4 * k] = t.x;
-                        wv[4 * k + 1] = t.y;
-                        wv[4 * k + 2] = t.z;
-                        wv[4 * k + 3] = t.w;
-                    }
+                for (int k = 0; k < BITS / 2; ++k) {
+                    const uint4 t = __ldg((const uint4*)src + k);
+                    wv[4 * k] = t.x;
+                    wv[4 * k + 1] = t.y;
+                    wv[4 * k + 2] = t.z;
+                    wv[4 * k + 3] = t.w;
                 }
             }
-            if (!mbar_wait(&misc->a_empty[s], ((i / A_STAGES) + 1) & 1)) break;
+        };
+        auto load_norm = [&](int64_t prow) -> unsigned short {
+            return (prow >= 0 && h == 0) ? __ldg((const unsigned short*)a.norms_pool + prow) : (unsigned short)0;
+        };
+        // One tile: wait for the stage, publish the norm, decode `wv` into the A tile, signal.
+        auto decode_tile = [&](int i, const uint32_t (&wv)[NW], unsigned short nbits) -> bool {
+            const int s = i % A_STAGES;
+            if (!mbar_wait(&misc->a_empty[s], ((i / A_STAGES) + 1) & 1)) return false;
+            if (h == 0) misc->norm[i % NORM_BUF][r] = __half2float(__ushort_as_half(nbits));
             uint8_t* dstrow = sA + s * TILE_BYTES;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 values: columns 64h + 8c ..
@@ -275,10 +322,48 @@ __global__ void __maxnreg__(MAX_REGS)
             }
             fence_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&misc->a_full[s]);
+            if (lane == 0) {
+                mbar_arrive(&misc->norm_full[i % NORM_BUF]);
+                mbar_arrive(&misc->a_full[s]);
+            }
+            return true;
+        };
+        // Register rings, no copies between iterations: at step t the codes and norm of tile
+        // t + 2 are requested (ring slot (t + 2) % 3) and the block-table entry of tile t + 4
+        // (slot (t + 1) % 3, freed at step t - 1), then tile t is decoded; every load has two
+        // steps to arrive before it is used.
+        uint32_t w[3][NW];
+        unsigned short nr[3];
+        int32_t bt[3];
+        bt[0] = bt_of(0);
+        bt[1] = bt_of(1);
+        bt[2] = bt_of(2);
+        {
+            const int64_t q0 = row_of(0, bt[0]), q1 = row_of(1, bt[1]);
+            load_codes(q0, w[0]);
+            nr[0] = load_norm(q0);
+            load_codes(q1, w[1]);
+            nr[1] = load_norm(q1);
+        }
+        bt[0] = bt_of(3);
+        bool ok = true;
+        for (int i = 0; i < ntiles_cta && ok; i += 3) {
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                const int t = i + k;
+                if (t >= ntiles_cta) break;
+                const int64_t q = row_of(t + 2, bt[(k + 2) % 3]);
+                load_codes(q, w[(k + 2) % 3]);
+                nr[(k + 2) % 3] = load_norm(q);
+                bt[(k + 1) % 3] = bt_of(t + 4);
+                if (!decode_tile(t, w[k], nr[k])) {
+                    ok = false;
+                    break;
+                }
+            }
         }
     } else {
-        // ── epilogue: warpgroup e takes the tiles i with i % TBUF == e ──────
+        // ── epilogue: warpgroup e takes the tiles i with i % TBUF == e (accumulator i % NACC) ──
         const int e = (warp - 1 - DEC_WARPS) >> 2;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
@@ -287,38 +372,40 @@ __global__ void __maxnreg__(MAX_REGS)
         int n = 0;
         for (int i = e; i < ntiles_cta; i += TBUF, ++n) {
             const int tile = (int)blockIdx.x + i * (int)gridDim.x;
-            const int64_t vi = (int64_t)tile * TILE + row;
-            float nrm = 0.0f;
-            if (vi < nvec) {
-                const int64_t slot = tq_slot(a, vi / a.num_heads);
-                if (slot >= 0) nrm = __half2float(((const __half*)a.norms_pool)[slot * a.num_heads + vi % a.num_heads]);
-            }
             if (leader) {
                 bulk_wait_read_all();  // the previous store from this staging tile has read it
                 mbar_arrive(&misc->st_free[e]);
             }
-            if (!mbar_wait(&misc->tfull[e], n & 1)) break;
+            const int acc = i % NACC;
+            if (!mbar_wait(&misc->tfull[acc], (i / NACC) & 1)) break;
             if (!mbar_wait(&misc->st_free[e], n & 1)) break;
             tc_fence_after();
-            const uint32_t taddr = tmem_base + (uint32_t)(e * D) + ((uint32_t)(quarter * 32) << 16);
+            if (!mbar_wait(&misc->norm_full[i % NORM_BUF], (i / NORM_BUF) & 1)) break;
+            const float nrm = misc->norm[i % NORM_BUF][row];
+            const uint32_t taddr = tmem_base + (uint32_t)(acc * D) + ((uint32_t)(quarter * 32) << 16);
+            // 16-column chunks, the next load in flight while the current chunk is stored
+            uint32_t va[16], vb[16];
+            tmem_ld16_issue(taddr, va);
 #pragma unroll
-            for (int cchunk = 0; cchunk < D / 32; ++cchunk) {
-                uint32_t v[32];
-                tmem_ld32_issue(taddr + cchunk * 32, v);
+            for (int cchunk = 0; cchunk < D / 16; ++cchunk) {
+                uint32_t(&v)[16] = (cchunk & 1) ? vb : va;
+                uint32_t(&vn)[16] = (cchunk & 1) ? va : vb;
                 tmem_wait_tie(v);
-                if (cchunk == D / 32 - 1) {
+                if (cchunk + 1 < D / 16) {
+                    tmem_ld16_issue(taddr + (cchunk + 1) * 16, vn);
+                } else {
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&misc->tempty[e]);
+                    if (lane == 0) mbar_arrive(&misc->tempty[acc]);
                 }
 #pragma unroll
-                for (int g = 0; g < 4; ++g) {
+                for (int g = 0; g < 2; ++g) {
                     uint32_t o[4];
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
                         o[k] = pack_out<TOut>(__uint_as_float(v[8 * g + 2 * k]) * nrm,
                                               __uint_as_float(v[8 * g + 2 * k + 1]) * nrm);
-                    *(uint4*)(st + sw128_offset(row, 32 * cchunk + 8 * g)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    *(uint4*)(st + sw128_offset(row, 16 * cchunk + 8 * g)) = make_uint4(o[0], o[1], o[2], o[3]);
                 }
             }
             fence_async_smem();
@@ -337,7 +424,7 @@ __global__ void __maxnreg__(MAX_REGS)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem_base) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem_base) : "memory");
     }
 }
 
@@ -388,7 +475,7 @@ int tq_dequant_umma(const TqArgs& a, cudaStream_t s, bool* handled) {
     if (a.head_dim != dq::D || !(a.bits == 2 || a.bits == 3 || a.bits == 4)) return 0;
     if (a.out_dtype != FB_FP16 && a.out_dtype != FB_BF16) return 0;
     if (!aligned16(a.output) || !aligned16(a.packed_pool) || (((uintptr_t)a.norms_pool) & 1)) return 0;
-    if (((uintptr_t)a.rotation & 3) != 0) return 0;
+    if (!aligned16(a.rotation)) return 0;
     if (a.num_tokens * a.num_heads > ((int64_t)1 << 31) - dq::TILE) return 0;
     int dev = 0, major = 0, minor = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;

@@ -124,6 +124,15 @@ __device__ __forceinline__ int sw128_offset(int n, int k) {
     return kb * KBLK_BYTES + n * 128 + ((((kk >> 3) ^ (n & 7))) << 4) + ((kk & 7) << 1);
 }
 
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from global to shared
+// memory, completing on `bar` (the caller has added the bytes to its transaction count).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // TMA tensor store of a 2D box from shared memory (bulk async-group completion).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),

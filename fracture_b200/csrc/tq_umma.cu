@@ -353,8 +353,11 @@ __global__ void __maxnreg__(MAX_REGS)
             const int64_t vi = (int64_t)tile * TILE + row;
             // Pool row: the block-table lookup is issued before the accumulator wait.
             int64_t slot = -1;
-            if (vi < nvec) slot = tq_slot(a, vi / a.num_heads);
-            const int64_t prow = slot >= 0 ? slot * a.num_heads + vi % a.num_heads : -1;
+            // 32-bit division: the host keeps the vector count below 2^31
+            const uint32_t tok = (uint32_t)vi / (uint32_t)a.num_heads;
+            const uint32_t head = (uint32_t)vi - tok * (uint32_t)a.num_heads;
+            if (vi < nvec) slot = tq_slot(a, (int64_t)tok);
+            const int64_t prow = slot >= 0 ? slot * a.num_heads + head : -1;
             uint8_t* dst = prow >= 0 ? (uint8_t*)a.packed_pool + prow * P : nullptr;
             if (!mbar_wait(&misc->tfull[eg], (i / EPI_WGS) & 1, err)) break;
             tc_fence_after();
