@@ -16,6 +16,11 @@ Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): each rank runs
 its own 16 x 2048-token batch (weak scaling, sequences are independent: no
 data-path collective); value = all ranks' tokens / max-over-ranks time.
 
+The same line carries ``tq_config4``: BASELINE config 4 (TurboQuant K+V of
+65536 tokens x 8 KV heads x 128 quantized into a paged cache and dequantized
+back, 3 and 4 bits), timed per step with CUDA events, the token range split by
+16-token blocks across the ranks (strong scaling, max-over-ranks time).
+
 ``--impl reference`` times the reference's CPU numerical path (the PyTorch
 math of its validation scripts, ``oracle/cpu_chain.py``) on the host cores.
 """
@@ -299,6 +304,85 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     return res
 
 
+def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """TurboQuant K and V of [65536 tokens, 8 KV heads, 128] FP16 (N(0,1), 0.5% of
+    elements x10) quantized into a paged cache (block 16, random block table) and dequantized back,
+    at 3 and 4 bits. The 65536 tokens are split by 16-token blocks across the ranks (each rank owns
+    a disjoint pool shard; strong scaling, no collective on the data path). One step = K and V."""
+    import torch
+    import torch.distributed as dist
+
+    from fracture_b200 import kernels as K
+
+    dev = torch.device("cuda", local_rank)
+    T_all, H, D = 65536, NKV, HD
+    T = T_all // world
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    kv = []
+    for _ in range(2):
+        x = torch.randn((T, H, D), generator=g, device=dev)
+        kv.append(torch.where(torch.rand((T, H, D), generator=g, device=dev) < 0.005, x * 10.0, x).to(torch.float16))
+    rot = [torch.from_numpy(K.tq_rotation_matrix(D, sd)).to(dev) for sd in (42, 542)]
+    table = torch.randperm(T // 16, generator=g, device=dev).to(torch.int32)
+    outs = [torch.empty((T, H, D), dtype=torch.float16, device=dev) for _ in range(2)]
+    stream = torch.cuda.current_stream(dev)
+    pk = peaks()
+    res = {}
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    for bits in (4, 3):
+        P = D * bits // 8
+        cen = torch.from_numpy(K.tq_codebook(D, bits)[0]).to(dev)
+        pools = [(torch.empty((T, H * P), dtype=torch.uint8, device=dev),
+                  torch.empty((T, H), dtype=torch.float16, device=dev)) for _ in range(2)]
+
+        def quant():
+            for j in range(2):
+                K.tq_compress_paged(kv[j], rot[j], cen, bits, pools[j][0], pools[j][1], block_table=table)
+
+        def dequant():
+            for j in range(2):
+                K.tq_dequant_paged(pools[j][0], pools[j][1], rot[j], cen, bits, outs[j], block_table=table)
+
+        ms_q, ms_d = timed(quant), timed(dequant)
+        vec = 2 * T_all * H  # K and V vectors of the whole job
+        by_q = vec * (D * 2 + P + 2) + 2 * (T_all // 16) * 4  # read fp16, write codes + fp16 norm (+ block tables)
+        by_d = vec * (P + 2 + D * 2) + 2 * (T_all // 16) * 4
+        for name, ms, by in (("quantize", ms_q, by_q), ("dequantize", ms_d, by_d)):
+            gbs = by / (ms / 1e3) / 1e9
+            res.setdefault(name, {})[f"{bits}bit"] = {
+                "ms_per_step": round(ms, 4), "vectors_per_s": round(vec / (ms / 1e3), 1),
+                "algorithmic_bytes_per_step": by, "achieved_gbs": round(gbs, 1),
+                "frac_of_peak": round(gbs / pk["hbm_gbs"], 4)}
+    if rank != 0:
+        return None
+    return {"workload": "config4: TurboQuant K+V [65536, 8, 128] FP16 -> paged cache (block 16, random table) "
+                        "and back, Lloyd-Max 3/4-bit, per-vector FP16 norms",
+            "tokens": T_all, "tokens_per_gpu": T, "scaling": "strong" if world > 1 else None,
+            "parallelism": f"token shards of 16-token blocks over {world} GPU(s), no collective on the data path",
+            "output_dtype": "fp16", "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"],
+            "bound": "hbm", **res}
+
+
 def cpu_baseline(tokens: int, layers: int, reps: int) -> dict:
     import torch
 
@@ -414,6 +498,7 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
+    ap.add_argument("--no-tq", action="store_true", help="skip the config-4 TurboQuant measurement")
     ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding", "tq_compress",
                                                                    "tq_dequant"],
                     help="run only this kernel at its config-3 size (W warm-up launches + 1), for ncu captures")
@@ -442,9 +527,12 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     res = run_ours(args, rank, world, local_rank)
+    tq = None if args.no_tq else run_tq_config4(args, rank, world, local_rank)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if res is not None and tq is not None:
+        res["tq_config4"] = tq
     if res is not None:
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(tokens=2048, layers=16, reps=3)
