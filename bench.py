@@ -304,6 +304,84 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     return res
 
 
+def run_config2(args, local_rank: int) -> dict:
+    """Llama-3.1-8B decode-shaped fused ops in FP16 on one GPU — 64 single tokens
+    at positions uniform in [0, 8192): embedding gather, then 32 x [add+RMSNorm, RoPE (llama3),
+    add+RMSNorm, silu*mul] and a final add+RMSNorm (130 launches). Every tensor but the embedding
+    table fits in L2, so this shape is bound by launch latency, not HBM: it is timed both as eager
+    launches and as one captured CUDA graph per step."""
+    import torch
+
+    from fracture_b200 import kernels as K
+
+    dev = torch.device("cuda", local_rank)
+    T, f16 = 64, torch.float16
+    g = torch.Generator(device=dev).manual_seed(2)
+    table = (torch.randn((VOCAB, HID), generator=g, device=dev) * 0.02).to(f16)
+    ids = torch.randint(0, VOCAB, (T,), generator=g, device=dev, dtype=torch.int32)
+    positions = torch.randint(0, 8192, (T,), generator=g, device=dev, dtype=torch.int32)
+    h, normed = torch.empty((T, HID), device=dev, dtype=f16), torch.empty((T, HID), device=dev, dtype=f16)
+    attn_proj, ffn_out = (torch.randn((T, HID), generator=g, device=dev).to(f16) for _ in range(2))
+    q = torch.randn((T, NQ, HD), generator=g, device=dev).to(f16)
+    k = torch.randn((T, NKV, HD), generator=g, device=dev).to(f16)
+    gate, up = (torch.randn((T, INTER), generator=g, device=dev).to(f16) for _ in range(2))
+    mid = torch.empty_like(gate)
+    wa = (1 + 0.02 * torch.randn((LAYERS, HID), generator=g, device=dev)).to(f16)
+    wf = (1 + 0.02 * torch.randn((LAYERS + 1, HID), generator=g, device=dev)).to(f16)
+    freqs = torch.from_numpy(K.rope_freqs_llama3(HD, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"],
+                                                 ROPE["orig"])).to(dev)
+    B = 2
+    by = (T * HID * B * 2 + T * 4) + (T * HID * B * 2 + HID * B) + (2 * LAYERS - 1 + 1) * (T * HID * B * 4 + HID * B) \
+        + LAYERS * (T * (NQ + NKV) * HD * B * 2 + T * 4 + HD // 2 * 4) + LAYERS * T * INTER * B * 3
+    launches = 1 + 1 + (2 * LAYERS - 1) + LAYERS + LAYERS + 1
+
+    def chain():
+        K.embedding(h, table, ids)
+        for l in range(LAYERS):
+            if l == 0:
+                K.rmsnorm(normed, h, wa[0], EPS)
+            else:
+                K.add_rmsnorm(h, ffn_out, wa[l], normed, EPS)
+            K.rope(q, k, positions, freqs)
+            K.add_rmsnorm(h, attn_proj, wf[l], normed, EPS)
+            K.silu_mul(mid, gate, up)
+        K.add_rmsnorm(h, ffn_out, wf[LAYERS], normed, EPS)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / args.steps
+
+    ms_eager = timed(chain)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        chain()  # one eager pass on the capture stream before capture
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        chain()
+    ms_graph = timed(graph.replay)
+    del graph
+    out = {"workload": "config2: Llama-3.1-8B decode-shaped fused ops, FP16, 64 tokens at positions U[0,8192), "
+                       "32 layers of [add+rmsnorm, rope q/k (llama3), add+rmsnorm, silu*mul] + embedding + final norm",
+           "tokens": T, "launches_per_step": launches, "algorithmic_bytes_per_step": by,
+           "bound": "launch latency (every tensor but the embedding table stays in the 126 MB L2)"}
+    for name, ms in (("eager", ms_eager), ("cuda_graph", ms_graph)):
+        out[name] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(T / (ms / 1e3), 1),
+                     "us_per_launch": round(ms * 1e3 / launches, 3),
+                     "effective_gbs": round(by / (ms / 1e3) / 1e9, 1)}
+    return out
+
+
 def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
     """TurboQuant K and V of [65536 tokens, 8 KV heads, 128] FP16 (N(0,1), 0.5% of
     elements x10) quantized into a paged cache (block 16, random block table) and dequantized back,
@@ -499,6 +577,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
     ap.add_argument("--no-tq", action="store_true", help="skip the config-4 TurboQuant measurement")
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode-shaped measurement")
     ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding", "tq_compress",
                                                                    "tq_dequant"],
                     help="run only this kernel at its config-3 size (W warm-up launches + 1), for ncu captures")
@@ -533,6 +612,8 @@ def main() -> None:
         dist.destroy_process_group()
     if res is not None and tq is not None:
         res["tq_config4"] = tq
+    if res is not None and world == 1 and not args.no_decode:
+        res["decode_config2"] = run_config2(args, local_rank)
     if res is not None:
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(tokens=2048, layers=16, reps=3)
