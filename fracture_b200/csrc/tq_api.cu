@@ -26,10 +26,10 @@ static int tq_check_common(int bits, int64_t num_tokens, int num_kv_heads, int h
     return 0;
 }
 
-extern "C" int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotation, const float* centroids,
-                                           int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
-                                           const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
-                                           void* packed_pool, void* norms_pool, unsigned int* err_count, void* stream) {
+static int tq_compress_any(const void* input, int dtype, const float* rotation, const float* centroids, int bits,
+                           int64_t num_tokens, int num_kv_heads, int head_dim, const int32_t* block_table,
+                           const int64_t* slot_map, int64_t start_pos, int64_t num_pool_rows, void* packed_pool,
+                           void* norms_pool, unsigned int* err_count, void* stream) {
     int rc = tq_check_common(bits, num_tokens, num_kv_heads, head_dim, num_pool_rows);
     if (rc) return rc;
     if (dtype != FB_FP16 && dtype != FB_BF16 && dtype != FB_FP32) return (int)cudaErrorInvalidValue;
@@ -47,6 +47,7 @@ extern "C" int fb_launch_tq_compress_paged(const void* input, int dtype, const f
     a.num_heads = num_kv_heads;
     a.head_dim = head_dim;
     a.block_table = block_table;
+    a.slot_map = slot_map;
     a.start_pos = start_pos;
     a.pool_rows = num_pool_rows;
     a.packed_pool = packed_pool;
@@ -56,6 +57,25 @@ extern "C" int fb_launch_tq_compress_paged(const void* input, int dtype, const f
     rc = tq_compress_umma(a, (cudaStream_t)stream, &handled);
     if (handled) return rc;
     return tq_compress_exact(a, (cudaStream_t)stream);
+}
+
+extern "C" int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotation, const float* centroids,
+                                           int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                                           const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
+                                           void* packed_pool, void* norms_pool, unsigned int* err_count, void* stream) {
+    return tq_compress_any(input, dtype, rotation, centroids, bits, num_tokens, num_kv_heads, head_dim, block_table,
+                           nullptr, start_pos, num_pool_rows, packed_pool, norms_pool, err_count, stream);
+}
+
+// Batched append: token t of the call goes to pool row slot_map[t] (negative or out of range:
+// skipped and counted in err_count); one launch for the new tokens of many sequences.
+extern "C" int fb_launch_tq_compress_slots(const void* input, int dtype, const float* rotation, const float* centroids,
+                                           int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                                           const int64_t* slot_map, int64_t num_pool_rows, void* packed_pool,
+                                           void* norms_pool, unsigned int* err_count, void* stream) {
+    if (!slot_map && num_tokens > 0) return (int)cudaErrorInvalidValue;
+    return tq_compress_any(input, dtype, rotation, centroids, bits, num_tokens, num_kv_heads, head_dim, nullptr,
+                           slot_map, 0, num_pool_rows, packed_pool, norms_pool, err_count, stream);
 }
 
 // Same contract as fb_launch_tq_compress_paged, but the call allocates no device memory: the
@@ -104,10 +124,10 @@ extern "C" int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype,
     return tq_compress_exact(a, (cudaStream_t)stream);
 }
 
-extern "C" int fb_launch_tq_dequant_paged(const void* packed_pool, const void* norms_pool, const float* rotation,
-                                          const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
-                                          int head_dim, const int32_t* block_table, int64_t start_pos,
-                                          int64_t num_pool_rows, void* output, int dtype, void* stream) {
+static int tq_dequant_any(const void* packed_pool, const void* norms_pool, const float* rotation,
+                          const float* centroids, int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                          const int32_t* block_table, const int64_t* slot_map, int64_t start_pos,
+                          int64_t num_pool_rows, void* output, int dtype, void* stream) {
     int rc = tq_check_common(bits, num_tokens, num_kv_heads, head_dim, num_pool_rows);
     if (rc) return rc;
     if (dtype != FB_FP16 && dtype != FB_BF16 && dtype != FB_FP32) return (int)cudaErrorInvalidValue;
@@ -123,6 +143,7 @@ extern "C" int fb_launch_tq_dequant_paged(const void* packed_pool, const void* n
     a.num_heads = num_kv_heads;
     a.head_dim = head_dim;
     a.block_table = block_table;
+    a.slot_map = slot_map;
     a.start_pos = start_pos;
     a.pool_rows = num_pool_rows;
     a.packed_pool = const_cast<void*>(packed_pool);
@@ -133,6 +154,24 @@ extern "C" int fb_launch_tq_dequant_paged(const void* packed_pool, const void* n
     rc = tq_dequant_umma(a, (cudaStream_t)stream, &handled);
     if (handled) return rc;
     return tq_dequant_exact(a, (cudaStream_t)stream);
+}
+
+extern "C" int fb_launch_tq_dequant_paged(const void* packed_pool, const void* norms_pool, const float* rotation,
+                                          const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
+                                          int head_dim, const int32_t* block_table, int64_t start_pos,
+                                          int64_t num_pool_rows, void* output, int dtype, void* stream) {
+    return tq_dequant_any(packed_pool, norms_pool, rotation, centroids, bits, num_tokens, num_kv_heads, head_dim,
+                          block_table, nullptr, start_pos, num_pool_rows, output, dtype, stream);
+}
+
+// Gather by slot map: output token t from pool row slot_map[t] (no row: zeros).
+extern "C" int fb_launch_tq_dequant_slots(const void* packed_pool, const void* norms_pool, const float* rotation,
+                                          const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
+                                          int head_dim, const int64_t* slot_map, int64_t num_pool_rows, void* output,
+                                          int dtype, void* stream) {
+    if (!slot_map && num_tokens > 0) return (int)cudaErrorInvalidValue;
+    return tq_dequant_any(packed_pool, norms_pool, rotation, centroids, bits, num_tokens, num_kv_heads, head_dim,
+                          nullptr, slot_map, 0, num_pool_rows, output, dtype, stream);
 }
 
 extern "C" int launch_turboquant_compress(const void* input, const float* rotation, const float* centroids,

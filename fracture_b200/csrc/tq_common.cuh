@@ -21,6 +21,7 @@ struct TqArgs {
     int num_heads;
     int head_dim;
     const int32_t* block_table;  // nullptr: slot = position
+    const int64_t* slot_map;     // when set: pool row of call token t = slot_map[t] (block_table unused)
     int64_t start_pos;
     int64_t pool_rows;
     void* packed_pool;         // [pool_rows, H * P] u8
@@ -34,7 +35,9 @@ struct TqArgs {
 __device__ __forceinline__ int64_t tq_slot(const TqArgs& a, int64_t t) {
     const int64_t pos = a.start_pos + t;
     int64_t slot;
-    if (a.block_table) {
+    if (a.slot_map) {
+        slot = __ldg(a.slot_map + t);
+    } else if (a.block_table) {
         const int32_t b = __ldg(a.block_table + (pos >> 4));
         slot = b < 0 ? -1 : (int64_t)b * 16 + (pos & 15);
     } else {

@@ -235,24 +235,32 @@ __global__ void __maxnreg__(MAX_REGS)
         const uint32_t tlane = smem_u32(tab) + (uint32_t)(lane & (TB::copies - 1)) * TB::entry_bytes;
         constexpr int NW = BITS * 2;  // 32-bit words of packed codes per half-row
         // Pool row of this thread's vector in tile i, in two steps so that no branch waits on
-        // a load: bt_of issues the block-table read (-1: no vector; 0 without a table), row_of
-        // applies the slot rule of tq_slot to it two steps later (-1: no row).
+        // a load: bt_of issues the slot-map or block-table read (-1: no vector; 0 without
+        // either), row_of applies the slot rule of tq_slot to it two steps later (-1: no row).
         // (32-bit division: the host keeps the vector count below 2^31.)
-        // Prefetched values stay raw (int32 table entry, fp16 norm bits) until they are used,
-        // so no conversion waits on a load that is still in flight.
-        auto bt_of = [&](int i) -> int32_t {
+        // Prefetched values stay raw (the slot-map entry, or the int32 table entry zero-extended;
+        // fp16 norm bits) until they are used, so no conversion waits on a load still in flight.
+        auto bt_of = [&](int i) -> int64_t {
             const uint32_t vi = (uint32_t)((int)blockIdx.x + i * (int)gridDim.x) * TILE + r;
             if (i >= ntiles_cta || (int64_t)vi >= nvec) return -1;
-            const int64_t pos = a.start_pos + vi / (uint32_t)a.num_heads;
-            return a.block_table ? __ldg(a.block_table + (pos >> 4)) : (int32_t)0;
+            const uint32_t tok = vi / (uint32_t)a.num_heads;
+            if (a.slot_map) return __ldg(a.slot_map + tok);
+            if (!a.block_table) return 0;
+            return (int64_t)(uint32_t)__ldg(a.block_table + ((a.start_pos + tok) >> 4));
         };
-        auto row_of = [&](int i, int32_t bt) -> int64_t {
-            if (bt < 0) return -1;
+        auto row_of = [&](int i, int64_t raw) -> int64_t {
+            if (raw == -1) return -1;
             const uint32_t vi = (uint32_t)((int)blockIdx.x + i * (int)gridDim.x) * TILE + r;
             const uint32_t tok = vi / (uint32_t)a.num_heads, head = vi - tok * (uint32_t)a.num_heads;
             const int64_t pos = a.start_pos + tok;
-            const int64_t slot = a.block_table ? (int64_t)bt * 16 + (pos & 15) : pos;
-            return slot < a.pool_rows ? slot * a.num_heads + head : -1;
+            int64_t slot = pos;
+            if (a.slot_map) {
+                slot = raw;
+            } else if (a.block_table) {
+                const int32_t b = (int32_t)(uint32_t)raw;
+                slot = b < 0 ? -1 : (int64_t)b * 16 + (pos & 15);
+            }
+            return (slot >= 0 && slot < a.pool_rows) ? slot * a.num_heads + head : -1;
         };
         auto load_codes = [&](int64_t prow, uint32_t (&wv)[NW]) {  // zeros when there is no row
 #pragma unroll
@@ -334,7 +342,7 @@ __global__ void __maxnreg__(MAX_REGS)
         // steps to arrive before it is used.
         uint32_t w[3][NW];
         unsigned short nr[3];
-        int32_t bt[3];
+        int64_t bt[3];
         bt[0] = bt_of(0);
         bt[1] = bt_of(1);
         bt[2] = bt_of(2);

@@ -34,7 +34,8 @@ __global__ void __launch_bounds__(256) tq_compress_exact_kernel(TqArgs a) {
     float* xs = piT + d * d;            // [EX_V][d] input as float, then xn
     float* cen = xs + EX_V * d;         // [256]
     float* scal = cen + 256;            // [EX_V] denominators
-    uint8_t* idx = (uint8_t*)(scal + EX_V);  // [EX_V][d]
+    int64_t* prow_s = (int64_t*)(((uintptr_t)(scal + EX_V) + 7) & ~(uintptr_t)7);  // [EX_V] pool rows (-1: none)
+    uint8_t* idx = (uint8_t*)(prow_s + EX_V);   // [EX_V][d]
 
     for (int e = threadIdx.x; e < d * d; e += blockDim.x) {
         const int i = e / d, j = e % d;
@@ -56,8 +57,9 @@ __global__ void __launch_bounds__(256) tq_compress_exact_kernel(TqArgs a) {
             const int v = threadIdx.x;
             const float norm = exact_norm(xs + v * d, d);
             const int64_t vi = v0 + v;
-            const int64_t slot = tq_slot(a, vi / a.num_heads);
-            if (slot >= 0) ((__half*)a.norms_pool)[slot * a.num_heads + vi % a.num_heads] = __float2half_rn(norm);
+            const int64_t slot = tq_slot(a, vi / a.num_heads);  // once per vector (counts a miss once)
+            prow_s[v] = slot >= 0 ? slot * a.num_heads + vi % a.num_heads : -1;
+            if (slot >= 0) ((__half*)a.norms_pool)[prow_s[v]] = __float2half_rn(norm);
             scal[v] = __fadd_rn(norm, 1e-8f);
         }
         __syncthreads();
@@ -81,11 +83,8 @@ __global__ void __launch_bounds__(256) tq_compress_exact_kernel(TqArgs a) {
         __syncthreads();
         for (int e = threadIdx.x; e < nv * P; e += blockDim.x) {
             const int v = e / P, byte = e % P;
-            const int64_t vi = v0 + v;
-            const int64_t slot = tq_slot(a, vi / a.num_heads);
-            if (slot < 0) continue;
-            ((uint8_t*)a.packed_pool)[(slot * a.num_heads + vi % a.num_heads) * P + byte] =
-                pack_byte(idx + v * d, d, a.bits, byte);
+            if (prow_s[v] < 0) continue;
+            ((uint8_t*)a.packed_pool)[prow_s[v] * P + byte] = pack_byte(idx + v * d, d, a.bits, byte);
         }
         __syncthreads();
     }
@@ -132,7 +131,7 @@ __global__ void __launch_bounds__(256) tq_dequant_exact_kernel(TqArgs a) {
 }
 
 static size_t exact_compress_smem(int d) {
-    return sizeof(float) * ((size_t)d * d + EX_V * d + 256 + EX_V) + EX_V * d;
+    return sizeof(float) * ((size_t)d * d + EX_V * d + 256 + EX_V) + 8 + sizeof(int64_t) * EX_V + EX_V * d;
 }
 
 int tq_compress_exact(const TqArgs& a, cudaStream_t s) {

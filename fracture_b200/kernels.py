@@ -86,6 +86,25 @@ def tq_dequant_paged(packed_pool, norms_pool, rotation, centroids, bits, out, bl
         _stream(stream)), "tq_dequant_paged")
 
 
+def tq_compress_slots(x, rotation, centroids, bits, packed_pool, norms_pool, slot_map, err=None, stream=None):
+    """Batched append: token t of ``x [T, H, d]`` into pool row ``slot_map[t]`` (int64 tensor)."""
+    T, H, d = x.shape
+    rows = norms_pool.shape[0]
+    _ok(_lib.load().fb_launch_tq_compress_slots(
+        x.data_ptr(), _dt(x), rotation.data_ptr(), centroids.data_ptr(), bits, T, H, d, slot_map.data_ptr(), rows,
+        packed_pool.data_ptr(), norms_pool.data_ptr(), err.data_ptr() if err is not None else None, _stream(stream)),
+        "tq_compress_slots")
+
+
+def tq_dequant_slots(packed_pool, norms_pool, rotation, centroids, bits, out, slot_map, stream=None):
+    """Gather: ``out[t]`` dequantized from pool row ``slot_map[t]`` (int64 tensor)."""
+    T, H, d = out.shape
+    rows = norms_pool.shape[0]
+    _ok(_lib.load().fb_launch_tq_dequant_slots(
+        packed_pool.data_ptr(), norms_pool.data_ptr(), rotation.data_ptr(), centroids.data_ptr(), bits, T, H, d,
+        slot_map.data_ptr(), rows, out.data_ptr(), _dt(out), _stream(stream)), "tq_dequant_slots")
+
+
 # host tables -------------------------------------------------------------------
 
 def rope_freqs(head_dim: int, theta: float) -> np.ndarray:

@@ -135,6 +135,16 @@ int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype, const floa
                                         int64_t num_pool_rows, void* packed_pool, void* norms_pool,
                                         unsigned int* err_count, void* stream);
 
+/* Batched append (no reference counterpart; the reference appends one sequence at a time,
+ * quantized_paged_kv_cache.rs:404-500, called per sequence from batched.rs:324-350): as
+ * fb_launch_tq_compress_paged, but call token t goes to pool row slot_map[t] (int64; negative or
+ * >= num_pool_rows: skipped and counted in err_count once per head vector), so one launch writes the
+ * new tokens of many sequences. */
+int fb_launch_tq_compress_slots(const void* input, int dtype, const float* rotation, const float* centroids,
+                                int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                                const int64_t* slot_map, int64_t num_pool_rows, void* packed_pool,
+                                void* norms_pool, unsigned int* err_count, void* stream);
+
 /* TurboQuant dequantize from a paged pool into [num_tokens, Hkv, d] (`dtype` FP16/BF16/FP32):
  * x = (Pi^T @ centroids[idx]) * norm (replaces turboquant_decompress.cu:21-94). Same slot rule; a
  * token without a valid slot dequantizes to zeros. head_dim 128 with 2/3/4-bit codes and FP16/BF16
@@ -144,6 +154,14 @@ int fb_launch_tq_dequant_paged(const void* packed_pool, const void* norms_pool, 
                                const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
                                int head_dim, const int32_t* block_table, int64_t start_pos,
                                int64_t num_pool_rows, void* output, int dtype, void* stream);
+
+/* Gather counterpart of fb_launch_tq_compress_slots (no reference counterpart): output token t is
+ * dequantized from pool row slot_map[t] (no row: zeros). Same kernels and tolerance as
+ * fb_launch_tq_dequant_paged. */
+int fb_launch_tq_dequant_slots(const void* packed_pool, const void* norms_pool, const float* rotation,
+                               const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
+                               int head_dim, const int64_t* slot_map, int64_t num_pool_rows, void* output,
+                               int dtype, void* stream);
 
 /* Number of bounded waits that timed out inside the tensor-core TurboQuant kernels (compress and
  * dequantize) since the library was loaded (0 in normal operation; a timeout abandons the launch's

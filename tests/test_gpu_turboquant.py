@@ -41,7 +41,7 @@ def tables(d, bits, seed):
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 @pytest.mark.parametrize("bits", [2, 3, 4, 8])
-@pytest.mark.parametrize("T,H,d", [(64, 8, 128), (4, 2, 16), (7, 3, 32), (33, 8, 128)])
+@pytest.mark.parametrize("T,H,d", [(64, 8, 128), (4, 2, 16), (7, 3, 32), (33, 8, 128), (5, 3, 33)])
 def test_compress_bit_exact_compact_layout(dt, bits, T, H, d):
     x, raw = make_input(T, H, d, dt, seed=bits * 100 + T)
     pi, c = tables(d, bits, 42)
@@ -386,3 +386,51 @@ def test_tensor_core_dequant_missing_blocks_give_zeros():
     for b in (3, 7):
         assert not g16[16 * b:16 * b + 16].any() and not g32[16 * b:16 * b + 16].any()
     ops.assert_close_fp(g16, g32, rel=3e-4, label="tensor-core vs CUDA-core dequant", dtype="f16")
+
+
+# ── batched append / gather by slot map ──
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("bits,d", [(4, 128), (3, 128), (2, 128), (4, 64)])
+def test_slot_map_append_equals_per_sequence_appends(dt, bits, d):
+    """Decode-style batch: 300 sequences each append one token at their own position (own block
+    table) — one slot-mapped launch equals 300 per-sequence block-table launches byte for byte;
+    slot -1 is skipped and counted; the slot-mapped gather returns the same values."""
+    H, nseq, nblk_per = 8, 300, 4
+    rng = np.random.default_rng(bits + d)
+    pos = rng.integers(0, nblk_per * 16, nseq)
+    tables_ = rng.permutation(nseq * nblk_per).astype(np.int32).reshape(nseq, nblk_per)
+    slots = (tables_[np.arange(nseq), pos // 16].astype(np.int64) * 16 + pos % 16)
+    slots[[7, 150]] = -1
+    x, raw = make_input(nseq, H, d, dt, seed=9)
+    pi, c = tables(d, bits, 777)
+    tpi, tc = torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV)
+    P = tq.TurboQuantConfig.packed_dim_per_head(d, bits)
+    rows = nseq * nblk_per * 16
+    pk1 = torch.full((rows, H * P), 0x3C, dtype=torch.uint8, device=DEV)
+    nr1 = torch.full((rows, H), 0x1234, dtype=torch.int16, device=DEV)
+    pk2, nr2 = pk1.clone(), nr1.clone()
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    xd = dev(x, dt)
+    K.tq_compress_slots(xd, tpi, tc, bits, pk1, nr1, torch.from_numpy(slots).to(DEV), err=err)
+    for sq in range(nseq):
+        if slots[sq] < 0:
+            continue
+        K.tq_compress_paged(xd[sq:sq + 1], tpi, tc, bits, pk2, nr2,
+                            block_table=torch.from_numpy(tables_[sq]).to(DEV), start_pos=int(pos[sq]))
+    torch.cuda.synchronize()
+    assert err.item() == 2 * H  # counted once per head vector
+    assert torch.equal(pk1, pk2) and torch.equal(nr1, nr2)
+    # against the exact statement, row by row
+    pc, nc, _ = tq.compress_c(raw, KIND[dt], pi, c, bits)
+    ok = slots >= 0
+    assert np.array_equal(pk1.cpu().numpy()[slots[ok]], pc[ok])
+    assert np.array_equal(nr1.cpu().numpy().view(np.uint16)[slots[ok]], nc[ok])
+    # gather back
+    out = torch.full((nseq, H, d), 3.0, dtype=torch.float16, device=DEV)
+    K.tq_dequant_slots(pk1, nr1, tpi, tc, bits, out, torch.from_numpy(slots).to(DEV))
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    assert not got[~ok].any()
+    ref = tq.decompress_c(pc[ok], nc[ok], pi, c, bits, H, d).reshape(-1, H, d)
+    ops.assert_close_fp(got[ok], ref, rel=3e-4, label="slot-mapped dequant", dtype="f16")
