@@ -382,6 +382,180 @@ def run_config2(args, local_rank: int) -> dict:
     return out
 
 
+C5 = dict(hidden=8192, nq=64, nkv=8, hd=128, inter=28672, vocab=128256, layers=80, seqs=256, prompt=1024,
+          decode=128, mb_seqs=8, bits=4)
+
+
+def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """Llama-3-70B-shaped pipeline, BF16, 80 layers split over the N ranks
+    (stage s = rank s). Prefill: 256 sequences x 1024 tokens in micro-batches of 8 sequences,
+    hidden states [8192 tokens, 8192] handed stage to stage by NCCL send/recv (fracture_b200.shards).
+    Decode: 128 steps for the 256 sequences in N groups, as a ring (the last stage hands each group's
+    next tokens back to stage 0). Per layer: fused add+RMSNorm, RoPE q/k (64/8 heads), fused
+    add+RMSNorm, silu*mul (I = 28672) and a 4-bit TurboQuant write of K and V into this stage's
+    paged cache (slot-mapped, one launch each). The GEMMs between these ops are outside the path:
+    synthetic tensors of their shapes stand in for their outputs."""
+    import torch
+
+    from fracture_b200 import kernels as K
+    from fracture_b200 import shards
+
+    c = C5
+    dev = torch.device("cuda", local_rank)
+    bf = torch.bfloat16
+    H, NQ5, NKV5, HD5, I5 = c["hidden"], c["nq"], c["nkv"], c["hd"], c["inter"]
+    my_layers = shards.stage_layers(c["layers"], world, rank)
+    nl = len(my_layers)
+    g = torch.Generator(device=dev).manual_seed(500 + rank)
+    mb_tokens = c["mb_seqs"] * c["prompt"]
+    n_mb = c["seqs"] // c["mb_seqs"]
+    seq_rows = c["prompt"] + c["decode"]  # pool rows per sequence (blocks of 16, contiguous per sequence)
+    bits = c["bits"]
+    P = HD5 * bits // 8
+
+    def act(shape):
+        return torch.randn(shape, generator=g, device=dev).to(bf)
+
+    # stand-ins for the GEMM outputs, shared by all layers of this stage
+    attn_out, ffn_out = act((mb_tokens, H)), act((mb_tokens, H))
+    q, k, v = act((mb_tokens, NQ5, HD5)), act((mb_tokens, NKV5, HD5)), act((mb_tokens, NKV5, HD5))
+    gate, up = act((mb_tokens, I5)), act((mb_tokens, I5))
+    mid = torch.empty_like(gate)
+    normed = torch.empty((mb_tokens, H), device=dev, dtype=bf)
+    wa = (1 + 0.02 * torch.randn((nl, H), generator=g, device=dev)).to(bf)
+    wf = (1 + 0.02 * torch.randn((nl + 1, H), generator=g, device=dev)).to(bf)
+    table = (torch.randn((c["vocab"], H), generator=g, device=dev) * 0.02).to(bf) if rank == 0 else None
+    freqs = torch.from_numpy(K.rope_freqs_llama3(HD5, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"],
+                                                 ROPE["orig"])).to(dev)
+    rots = [torch.from_numpy(K.tq_rotation_matrix(HD5, sd)).to(dev) for sd in (42, 542)]
+    cen = torch.from_numpy(K.tq_codebook(HD5, bits)[0]).to(dev)
+    rows = c["seqs"] * seq_rows
+    pools = [[(torch.empty((rows, NKV5 * P), dtype=torch.uint8, device=dev),
+               torch.empty((rows, NKV5), dtype=torch.float16, device=dev)) for _ in range(2)] for _ in range(nl)]
+    pos_prefill = (torch.arange(mb_tokens, device=dev, dtype=torch.int32) % c["prompt"]).contiguous()
+    ids_prefill = torch.randint(0, c["vocab"], (n_mb, mb_tokens), generator=g, device=dev, dtype=torch.int32)
+    # slot of token t of prefill micro-batch m: sequence (m * mb_seqs + t // prompt), position t % prompt
+    tt = torch.arange(mb_tokens, device=dev, dtype=torch.int64)
+    slots_prefill = [((m * c["mb_seqs"] + tt // c["prompt"]) * seq_rows + tt % c["prompt"]).contiguous()
+                     for m in range(n_mb)]
+    hbuf = [torch.empty((mb_tokens, H), device=dev, dtype=bf) for _ in range(2)]
+    # the layers work in place on the received buffer, which is then sent on: three receive
+    # buffers keep the receive of m + 1 off the buffer whose send (m - 1) may still be in flight
+    rbuf = [torch.empty((mb_tokens, H), device=dev, dtype=bf) for _ in range(3)]
+
+    def layers(h, T, pos, slots, li0=0):
+        for j in range(nl):
+            K.add_rmsnorm(h, attn_out[:T], wa[j], normed[:T], EPS)
+            K.rope(q[:T], k[:T], pos, freqs)
+            for kv, src in ((0, k), (1, v)):
+                K.tq_compress_slots(src[:T], rots[kv], cen, bits, pools[j][kv][0], pools[j][kv][1], slots)
+            K.add_rmsnorm(h, ffn_out[:T], wf[j], normed[:T], EPS)
+            K.silu_mul(mid[:T], gate[:T], up[:T])
+
+    link = shards.StageLink(rank, world)
+
+    def prefill():
+        def first_input(m):
+            K.embedding(hbuf[m % 2], table, ids_prefill[m])
+            return hbuf[m % 2]
+
+        def stage(m, x):
+            layers(x, mb_tokens, pos_prefill, slots_prefill[m])
+            if rank == world - 1:
+                K.add_rmsnorm(x, ffn_out, wf[nl], normed, EPS)
+            return x
+
+        shards.run_pipeline(n_mb, link, first_input, stage, rbuf)
+
+    # decode: G groups of sequences in flight around the ring
+    G = max(world, 1)
+    gs = c["seqs"] // G
+    ring = shards.StageLink(rank, world, ring=True)
+    ids_dec = [torch.randint(0, c["vocab"], (gs,), generator=g, device=dev, dtype=torch.int32) for _ in range(G)]
+    hdec = [torch.empty((gs, H), device=dev, dtype=bf) for _ in range(G)]
+    pos_dec = torch.empty((gs,), device=dev, dtype=torch.int32)
+    seq_idx = [torch.arange(gr * gs, (gr + 1) * gs, device=dev, dtype=torch.int64) for gr in range(G)]
+
+    def decode():
+        import torch.distributed as dist
+
+        h_send = [None] * G    # send of hdec[gr] to the next stage still in flight
+        ids_send = [None] * G  # ring send of ids_dec[gr] still in flight
+        for t in range(c["decode"]):
+            pos_dec.fill_(c["prompt"] + t)
+            for gr in range(G):
+                slots = seq_idx[gr] * seq_rows + (c["prompt"] + t)
+                h = hdec[gr]
+                if h_send[gr] is not None:  # hdec[gr] is about to be overwritten
+                    h_send[gr].wait()
+                    h_send[gr] = None
+                if rank == 0:
+                    if t > 0 and world > 1:
+                        ring.irecv(ids_dec[gr]).wait()
+                    K.embedding(h, table, ids_dec[gr])
+                else:
+                    link.irecv(h).wait()
+                layers(h, gs, pos_dec, slots)
+                if rank < world - 1:
+                    h_send[gr] = link.isend(h)
+                else:
+                    K.add_rmsnorm(h, ffn_out[:gs], wf[nl], normed[:gs], EPS)
+                    if ids_send[gr] is not None:
+                        ids_send[gr].wait()
+                        ids_send[gr] = None
+                    # next tokens of the group (a deterministic stand-in for sampling)
+                    ids_dec[gr].add_(1).remainder_(c["vocab"])
+                    if world > 1 and t + 1 < c["decode"]:
+                        ids_send[gr] = ring.isend(ids_dec[gr])
+        for w_ in h_send + ids_send:
+            if w_ is not None:
+                w_.wait()
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, reps):
+        fn()  # warm-up pass
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return shards.max_over_ranks(e0.elapsed_time(e1) / reps, dev)
+
+    reps = max(1, min(args.steps, 2))
+    ms_pre = timed(prefill, reps)
+    ms_dec = timed(decode, 1)
+    # algorithmic bytes per token per layer (BF16 activations; 4-bit K and V into the pool)
+    by_tok_layer = 2 * (4 * H * 2) + (NQ5 + NKV5) * HD5 * 2 * 2 + 4 + 3 * I5 * 2 \
+        + 2 * (NKV5 * HD5 * 2 + NKV5 * (P + 2) + 8)
+    pre_tokens = c["seqs"] * c["prompt"]
+    dec_tokens = c["seqs"] * c["decode"]
+    stage_bytes_pre = by_tok_layer * nl * pre_tokens
+    if rank != 0:
+        return None
+    pk = peaks()
+    return {"workload": "config5: Llama-3-70B-shaped pipeline, BF16, 80 layers split over the GPUs; per layer "
+                        "add+rmsnorm, rope q/k (64/8 heads), add+rmsnorm, silu*mul (I=28672) and 4-bit TurboQuant "
+                        "K+V writes into a paged cache; 256 x 1024 prefill in micro-batches of 8 sequences, "
+                        "then 128 decode steps in groups around a ring",
+            "stages": world, "layers_per_stage": nl, "micro_batch_tokens": mb_tokens,
+            "handoff": "NCCL send/recv of BF16 hidden states between neighbouring stages (decode: next tokens "
+                       "from the last stage back to stage 0)" if world > 1 else "none (one stage)",
+            "prefill": {"ms": round(ms_pre, 3), "tokens_per_s": round(pre_tokens / (ms_pre / 1e3), 1),
+                        "stage_algorithmic_bytes": stage_bytes_pre,
+                        "stage_achieved_gbs": round(stage_bytes_pre / (ms_pre / 1e3) / 1e9, 1),
+                        "stage_frac_of_peak": round(stage_bytes_pre / (ms_pre / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+                        "handoff_bytes_per_boundary": pre_tokens * H * 2},
+            "decode": {"ms": round(ms_dec, 3), "tokens_per_s": round(dec_tokens / (ms_dec / 1e3), 1),
+                       "groups": G, "group_sequences": gs},
+            "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"]}
+
+
 def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
     """TurboQuant K and V of [65536 tokens, 8 KV heads, 128] FP16 (N(0,1), 0.5% of
     elements x10) quantized into a paged cache (block 16, random block table) and dequantized back,
@@ -578,6 +752,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
     ap.add_argument("--no-tq", action="store_true", help="skip the config-4 TurboQuant measurement")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode-shaped measurement")
+    ap.add_argument("--pipeline", action="store_true",
+                    help="also run config 5 (70B-shaped pipeline over the ranks, NCCL stage handoff)")
     ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding", "tq_compress",
                                                                    "tq_dequant"],
                     help="run only this kernel at its config-3 size (W warm-up launches + 1), for ncu captures")
@@ -607,11 +783,14 @@ def main() -> None:
                                 device_id=torch.device("cuda", local_rank))
     res = run_ours(args, rank, world, local_rank)
     tq = None if args.no_tq else run_tq_config4(args, rank, world, local_rank)
+    c5 = run_config5(args, rank, world, local_rank) if (args.pipeline or world > 1) else None
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if res is not None and tq is not None:
         res["tq_config4"] = tq
+    if res is not None and c5 is not None:
+        res["pipeline_config5"] = c5
     if res is not None and world == 1 and not args.no_decode:
         res["decode_config2"] = run_config2(args, local_rank)
     if res is not None:

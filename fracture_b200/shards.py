@@ -107,7 +107,9 @@ def run_pipeline(n_micro: int, link: StageLink, first_input, stage_fn, recv_buff
     previous stage into ``recv_buffers[m % len(recv_buffers)]`` (the receive of ``m + 1`` is
     posted before ``m`` is computed). ``stage_fn(m, x)`` runs this stage's layers and returns the
     tensor to hand on; the send of ``m`` overlaps the compute of ``m + 1`` (at most one send in
-    flight, so a result buffer may be reused two micro-batches later). The last stage passes its
+    flight, so a result buffer may be reused two micro-batches later). A ``stage_fn`` that works in
+    place and returns its input needs three receive buffers, so the receive of ``m + 1`` never
+    lands in the buffer whose send (``m - 1``) may still be in flight. The last stage passes its
     results to ``on_output(m, y)``. Every stage posts the same sends and receives in the same
     order, so the links cannot deadlock.
     """

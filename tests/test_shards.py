@@ -89,6 +89,22 @@ def _worker(rank, world, port, n_micro, errq):
                     x = _stage_fn(s)(m, x)
                 assert torch.equal(outs[m], x), (m, outs[m], x)
             assert sorted(outs) == list(range(n_micro))
+        # stages that work in place on the received buffer and send it on (three buffers)
+        outs2 = {}
+
+        def stage_inplace(m, x):
+            if rank == 0:
+                x = x.clone()
+            x.mul_(rank + 2).add_((m + 1) * (rank + 1))
+            return x
+
+        shards.run_pipeline(n_micro, link,
+                            first_input=lambda m: torch.full(shape, float(m)),
+                            stage_fn=stage_inplace,
+                            recv_buffers=[torch.empty(shape) for _ in range(3)],
+                            on_output=lambda m, y: outs2.__setitem__(m, y.clone()))
+        if rank == world - 1:
+            assert all(torch.equal(outs2[m], outs[m]) for m in range(n_micro))
         # timing aggregate
         assert shards.max_over_ranks(float(rank) * 1.5) == (world - 1) * 1.5
         # ring: the last stage hands a tensor back to stage 0
