@@ -16,6 +16,9 @@ Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): each rank runs
 its own 16 x 2048-token batch (weak scaling, sequences are independent: no
 data-path collective); value = all ranks' tokens / max-over-ranks time.
 
+With ``--pipeline`` the line also carries ``pipeline_config5``
+(70B shapes, 80 layers split into N pipeline stages, NCCL handoff between stages).
+
 The same line carries ``tq_config4``: BASELINE config 4 (TurboQuant K+V of
 65536 tokens x 8 KV heads x 128 quantized into a paged cache and dequantized
 back, 3 and 4 bits), timed per step with CUDA events, the token range split by
@@ -467,14 +470,22 @@ def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
 
         shards.run_pipeline(n_mb, link, first_input, stage, rbuf)
 
-    # decode: G groups of sequences in flight around the ring
+    # decode: G groups of sequences in flight around the ring; each group's layer stack on this
+    # stage is one captured CUDA graph (positions and slots live in static tensors updated per step)
     G = max(world, 1)
     gs = c["seqs"] // G
     ring = shards.StageLink(rank, world, ring=True)
     ids_dec = [torch.randint(0, c["vocab"], (gs,), generator=g, device=dev, dtype=torch.int32) for _ in range(G)]
     hdec = [torch.empty((gs, H), device=dev, dtype=bf) for _ in range(G)]
     pos_dec = torch.empty((gs,), device=dev, dtype=torch.int32)
-    seq_idx = [torch.arange(gr * gs, (gr + 1) * gs, device=dev, dtype=torch.int64) for gr in range(G)]
+    slot_base = torch.arange(c["seqs"], device=dev, dtype=torch.int64).view(G, gs) * seq_rows
+    slots_dec = torch.empty((G, gs), device=dev, dtype=torch.int64)
+    graphs = []
+
+    def group_body(gr):
+        layers(hdec[gr], gs, pos_dec, slots_dec[gr])
+        if rank == world - 1:
+            K.add_rmsnorm(hdec[gr], ffn_out[:gs], wf[nl], normed[:gs], EPS)
 
     def decode():
         import torch.distributed as dist
@@ -483,8 +494,8 @@ def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
         ids_send = [None] * G  # ring send of ids_dec[gr] still in flight
         for t in range(c["decode"]):
             pos_dec.fill_(c["prompt"] + t)
+            torch.add(slot_base, c["prompt"] + t, out=slots_dec)
             for gr in range(G):
-                slots = seq_idx[gr] * seq_rows + (c["prompt"] + t)
                 h = hdec[gr]
                 if h_send[gr] is not None:  # hdec[gr] is about to be overwritten
                     h_send[gr].wait()
@@ -495,11 +506,13 @@ def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
                     K.embedding(h, table, ids_dec[gr])
                 else:
                     link.irecv(h).wait()
-                layers(h, gs, pos_dec, slots)
+                if graphs:
+                    graphs[gr].replay()
+                else:
+                    group_body(gr)
                 if rank < world - 1:
                     h_send[gr] = link.isend(h)
                 else:
-                    K.add_rmsnorm(h, ffn_out[:gs], wf[nl], normed[:gs], EPS)
                     if ids_send[gr] is not None:
                         ids_send[gr].wait()
                         ids_send[gr] = None
@@ -512,6 +525,15 @@ def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
                 w_.wait()
         if world > 1:
             dist.barrier()
+
+    def capture_decode_graphs():
+        torch.cuda.synchronize(dev)
+        for gr in range(G):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                group_body(gr)
+            graphs.append(graph)
+        torch.cuda.synchronize(dev)
 
     def timed(fn, reps):
         fn()  # warm-up pass
@@ -529,7 +551,10 @@ def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     reps = max(1, min(args.steps, 2))
     ms_pre = timed(prefill, reps)
+    decode()  # eager pass: sizes every workspace before capture
+    capture_decode_graphs()
     ms_dec = timed(decode, 1)
+    graphs.clear()
     # algorithmic bytes per token per layer (BF16 activations; 4-bit K and V into the pool)
     by_tok_layer = 2 * (4 * H * 2) + (NQ5 + NKV5) * HD5 * 2 * 2 + 4 + 3 * I5 * 2 \
         + 2 * (NKV5 * HD5 * 2 + NKV5 * (P + 2) + 8)
@@ -552,7 +577,9 @@ def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
                         "stage_frac_of_peak": round(stage_bytes_pre / (ms_pre / 1e3) / 1e9 / pk["hbm_gbs"], 4),
                         "handoff_bytes_per_boundary": pre_tokens * H * 2},
             "decode": {"ms": round(ms_dec, 3), "tokens_per_s": round(dec_tokens / (ms_dec / 1e3), 1),
-                       "groups": G, "group_sequences": gs},
+                       "groups": G, "group_sequences": gs,
+                       "launch": "one CUDA graph per group and stage per step (layers of the stage); NCCL "
+                                 "handoffs and the embedding outside the graphs"},
             "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"]}
 
 
@@ -567,8 +594,10 @@ def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
     from fracture_b200 import kernels as K
 
     dev = torch.device("cuda", local_rank)
+    from fracture_b200 import shards
+
     T_all, H, D = 65536, NKV, HD
-    T = T_all // world
+    T = len(shards.block_shard(T_all, world, rank))
     g = torch.Generator(device=dev).manual_seed(99 + rank)
     kv = []
     for _ in range(2):
@@ -581,6 +610,10 @@ def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
     pk = peaks()
     res = {}
 
+    # A shard can fit in the 126 MB L2 (2 x 67 MB at 2 GPUs, less beyond): every timed step starts
+    # after a 256 MB write that evicts it, and only the step itself is inside the events.
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
     def timed(fn):
         for _ in range(args.warmup):
             fn()
@@ -588,13 +621,14 @@ def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for e0, e1 in ev:
+            flush.fill_(1)
+            e0.record(stream)
             fn()
-        e1.record(stream)
+            e1.record(stream)
         torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / args.steps
+        ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / args.steps
         if world > 1:
             t = torch.tensor([ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -632,6 +666,7 @@ def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
             "tokens": T_all, "tokens_per_gpu": T, "scaling": "strong" if world > 1 else None,
             "parallelism": f"token shards of 16-token blocks over {world} GPU(s), no collective on the data path",
             "output_dtype": "fp16", "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"],
+            "l2": "256 MB written before every timed step (a shard can fit in L2); the flush is outside the timed events",
             "bound": "hbm", **res}
 
 
@@ -783,7 +818,7 @@ def main() -> None:
                                 device_id=torch.device("cuda", local_rank))
     res = run_ours(args, rank, world, local_rank)
     tq = None if args.no_tq else run_tq_config4(args, rank, world, local_rank)
-    c5 = run_config5(args, rank, world, local_rank) if (args.pipeline or world > 1) else None
+    c5 = run_config5(args, rank, world, local_rank) if args.pipeline else None
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
