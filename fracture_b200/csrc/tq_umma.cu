@@ -52,10 +52,10 @@ constexpr int LUT_COPIES = 16;      // copies per bin; lanes l and l + 16 share 
 constexpr float kRiskBand = 1e-6f;   // |y - boundary| below this: settle with the exact sequence
 constexpr float kNormBand = 1e-6f;  // relative band around fp16 rounding ties of the norm
 constexpr float kWindowPad = 1e-4f; // a bin owns the boundaries within this distance of its edges
-constexpr int EPI_WGS = 3;                 // epilogue warpgroups, one TMEM accumulator each
+constexpr int EPI_WGS = 4;                 // epilogue warpgroups, one TMEM accumulator each
 constexpr int THREADS = 64 + EPI_WGS * 128;  // warp 0 TMA, warp 1 MMA, then the epilogue
 constexpr int VCH = 32;                    // accumulator values per thread per TMEM load round
-constexpr int MAX_REGS = 128;              // 14 warps: at most 4 per scheduler, 16K registers each
+constexpr int MAX_REGS = 96;               // 18 warps: up to 5 per scheduler, 16K registers each
 static_assert(THREADS > NB, "one thread per table bin plus one for the checks");
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
