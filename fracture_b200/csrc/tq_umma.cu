@@ -8,11 +8,11 @@
 //   warp 1      MMA issuer:   acc[v][i] = sum_j x[v][j] * Pi[i][j] on tcgen05,
 //               Pi split into 2 fp16 (or 3 bf16) parts so the product is
 //               float32-accurate while x stays exact; accumulator in TMEM
-//   warps 2-9   epilogue, two warpgroups on alternating TMEM buffers: one
+//   warps 2-17  epilogue, four warpgroups on their own TMEM accumulators: one
 //               thread per vector reads its row of acc from TMEM, derives the
 //               norm (|Pi x| = |x|), maps each coordinate to its code through
-//               a lane-private boundary table, packs the MSB-first bit stream
-//               and writes it straight into its paged-pool row.
+//               a decision table in shared memory, packs the MSB-first bit
+//               stream and writes it straight into its paged-pool row.
 //
 // Bit-exactness. The reference result is the exact float32 statement
 // (sequential sums, true division, first-minimum nearest centroid). The fast
