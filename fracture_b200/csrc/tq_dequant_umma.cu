@@ -10,14 +10,14 @@
 //   warp 0       MMA issuer: acc[v][i] = sum_j Y[v][j] * PiT[i][j] on tcgen05 with
 //                Y[v][j] = c[idx[v][j]]; one fp16 pass (fp16 centroids and Pi keep the
 //                output within about 1e-4 of its magnitude of the float32 statement)
-//   warps 1-8    decoders: two threads per vector gather the packed codes of their half
-//                of the row through the block table and write fp16 centroid values
-//                straight into the 128-byte-swizzled A tile, through lane-private
+//   warps 1-16   decoders: four threads per vector gather the packed codes of their
+//                quarter of the row through the block table and write fp16 centroid
+//                values straight into the 128-byte-swizzled A tile, through lane-private
 //                lookup tables (two 4-bit, four 2-bit or two 3-bit codes per lookup)
-//   warps 9-16   epilogue, two warpgroups on alternating tiles (four TMEM accumulators): one thread per
-//                vector scales its accumulator row by the stored fp16 norm, converts,
-//                stages the tile in swizzled shared memory, and one thread writes it out
-//                with two TMA tensor stores
+//   warps 17-20  epilogue warpgroup: one thread per vector scales its accumulator row
+//                (one of four TMEM accumulators) by the stored fp16 norm, converts,
+//                stages the tile in swizzled shared memory (two staging tiles in turn),
+//                and one thread writes it out with two TMA tensor stores
 //
 // Pool rows follow the slot rule of tq_common.cuh; a token without a valid slot
 // dequantizes to zeros (norm 0), as the CUDA-core kernel does. Every barrier wait is
@@ -44,11 +44,13 @@ using namespace sm100;
 
 constexpr int A_STAGES = 2;  // A tiles in flight
 constexpr int NACC = 4;      // TMEM accumulators (4 x 128 columns: all of TMEM)
-constexpr int TBUF = 2;      // epilogue warpgroups = output staging tiles
-constexpr int DEC_WARPS = 8;
-constexpr int EPI_WARPS = 4 * TBUF;
+constexpr int STG = 2;       // output staging tiles (the epilogue alternates between them)
+constexpr int DEC_WARPS = 16;
+constexpr int TPR = DEC_WARPS * 32 / TILE;  // decoder threads per vector
+constexpr int EPI_WGS = 1;                 // epilogue warpgroups (2: one staging tile each)
+constexpr int EPI_WARPS = 4 * EPI_WGS;
 constexpr int THREADS = 32 * (1 + DEC_WARPS + EPI_WARPS);
-constexpr int MAX_REGS = 96;  // 17 warps: up to 5 on one scheduler, 16K registers each
+constexpr int MAX_REGS = 80;  // 21 warps: up to 6 on one scheduler, 16K registers each
 // Norms travel from the decoders to the epilogue through shared memory, one row of 128 per
 // tile, NORM_BUF rows deep: the decoder of tile i + NORM_BUF can only start after the MMA of
 // tile i + NACC, which waits for the epilogue of tile i to release its accumulator.
@@ -60,8 +62,8 @@ struct Misc {
     uint64_t a_empty[A_STAGES];
     uint64_t tfull[NACC];
     uint64_t tempty[NACC];
-    uint64_t st_free[TBUF];  // staging tile may be overwritten (its last TMA store has read it)
-    uint64_t st_full[TBUF];  // staging tile written by all four warps of the warpgroup
+    uint64_t st_free[STG];  // staging tile may be overwritten (its last TMA store has read it)
+    uint64_t st_full[STG];  // staging tile written by all four warps of the warpgroup
     uint64_t pi_full;        // Pi (fp32) copied into the staging area for the set-up
     uint32_t tmem_base;
     float cen[16];
@@ -84,8 +86,8 @@ template <int BITS>
 struct Smem {
     static constexpr int b_off = 0;                                   // Pi^T, fp16, SW128
     static constexpr int a_off = TILE_BYTES;                          // A_STAGES decoded tiles
-    static constexpr int st_off = a_off + A_STAGES * TILE_BYTES;      // TBUF output staging tiles
-    static constexpr int tab_off = st_off + TBUF * TILE_BYTES;
+    static constexpr int st_off = a_off + A_STAGES * TILE_BYTES;      // STG output staging tiles
+    static constexpr int tab_off = st_off + STG * TILE_BYTES;
     static constexpr int misc_off = tab_off + Table<BITS>::bytes;
     static constexpr int bytes = misc_off + (int)sizeof(Misc) + 1024;
 };
@@ -152,7 +154,7 @@ __global__ void __maxnreg__(MAX_REGS)
             mbar_init(&misc->tfull[b], 1);
             mbar_init(&misc->tempty[b], 4);
         }
-        for (int b = 0; b < TBUF; ++b) {
+        for (int b = 0; b < STG; ++b) {
             mbar_init(&misc->st_free[b], 1);
             mbar_init(&misc->st_full[b], 4);
         }
@@ -231,9 +233,10 @@ __global__ void __maxnreg__(MAX_REGS)
         // The packed codes of tile i+1 and the block-table entry of tile i+2 are requested
         // while tile i is decoded, so the two dependent global loads overlap the pipeline.
         const int dt = threadIdx.x - 32;
-        const int r = dt >> 1, h = dt & 1;
+        const int r = dt / TPR, h = dt % TPR;  // part h of row r: codes CPT*h .. CPT*h + CPT - 1
+        constexpr int CPT = D / TPR;
         const uint32_t tlane = smem_u32(tab) + (uint32_t)(lane & (TB::copies - 1)) * TB::entry_bytes;
-        constexpr int NW = BITS * 2;  // 32-bit words of packed codes per half-row
+        constexpr int NW = BITS * CPT / 32;  // 32-bit words of packed codes per part
         // Pool row of this thread's vector in tile i, in two steps so that no branch waits on
         // a load: bt_of issues the slot-map or block-table read (-1: no vector; 0 without
         // either), row_of applies the slot rule of tq_slot to it two steps later (-1: no row).
@@ -266,23 +269,26 @@ __global__ void __maxnreg__(MAX_REGS)
 #pragma unroll
             for (int k = 0; k < NW; ++k) wv[k] = 0u;
             if (prow < 0) return;
-            const uint8_t* src = (const uint8_t*)a.packed_pool + prow * P + h * (P / 2);
-            if constexpr (BITS == 3) {
+            const uint8_t* src = (const uint8_t*)a.packed_pool + prow * P + h * (P / TPR);
+            if constexpr (NW % 4 == 0) {
 #pragma unroll
-                for (int k = 0; k < 3; ++k) {
-                    const uint2 t = __ldg((const uint2*)src + k);
-                    wv[2 * k] = t.x;
-                    wv[2 * k + 1] = t.y;
-                }
-            } else {
-#pragma unroll
-                for (int k = 0; k < BITS / 2; ++k) {
+                for (int k = 0; k < NW / 4; ++k) {
                     const uint4 t = __ldg((const uint4*)src + k);
                     wv[4 * k] = t.x;
                     wv[4 * k + 1] = t.y;
                     wv[4 * k + 2] = t.z;
                     wv[4 * k + 3] = t.w;
                 }
+            } else if constexpr (NW % 2 == 0) {
+#pragma unroll
+                for (int k = 0; k < NW / 2; ++k) {
+                    const uint2 t = __ldg((const uint2*)src + k);
+                    wv[2 * k] = t.x;
+                    wv[2 * k + 1] = t.y;
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < NW; ++k) wv[k] = __ldg((const uint32_t*)src + k);
             }
         };
         auto load_norm = [&](int64_t prow) -> unsigned short {
@@ -295,7 +301,7 @@ __global__ void __maxnreg__(MAX_REGS)
             if (h == 0) misc->norm[i % NORM_BUF][r] = __half2float(__ushort_as_half(nbits));
             uint8_t* dstrow = sA + s * TILE_BYTES;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 values: columns 64h + 8c ..
+            for (int c = 0; c < CPT / 8; ++c) {  // chunks of 8 values: columns CPT*h + 8c ..
                 uint32_t o[4];
                 if constexpr (BITS == 4) {
                     const uint32_t w = wv[c];  // 4 bytes = 8 codes, byte 0 first
@@ -326,7 +332,7 @@ __global__ void __maxnreg__(MAX_REGS)
                         asm("ld.shared.b32 %0, [%1];" : "=r"(o[k]) : "r"(tlane + six * (TB::copies * 4u)));
                     }
                 }
-                *(uint4*)(dstrow + sw128_offset(r, 64 * h + 8 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
+                *(uint4*)(dstrow + sw128_offset(r, CPT * h + 8 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
             }
             fence_async_smem();
             __syncwarp();
@@ -371,22 +377,26 @@ __global__ void __maxnreg__(MAX_REGS)
             }
         }
     } else {
-        // ── epilogue: warpgroup e takes the tiles i with i % TBUF == e (accumulator i % NACC) ──
+        // ── epilogue: warpgroup e takes the tiles i with i % EPI_WGS == e (accumulator i % NACC);
+        // with one warpgroup the two staging tiles alternate, with two each has its own ──
+        static_assert(EPI_WGS == 1 || EPI_WGS == STG, "one warpgroup per staging tile, or one for both");
         const int e = (warp - 1 - DEC_WARPS) >> 2;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const bool leader = ((warp - 1 - DEC_WARPS) & 3) == 0 && lane == 0;
-        uint8_t* st = sST + e * TILE_BYTES;
-        int n = 0;
-        for (int i = e; i < ntiles_cta; i += TBUF, ++n) {
+        for (int i = e, k = 0; i < ntiles_cta; i += EPI_WGS, ++k) {
             const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+            const int sb = EPI_WGS == 1 ? (k % STG) : e, n = EPI_WGS == 1 ? k / STG : k;
+            uint8_t* st = sST + sb * TILE_BYTES;
             if (leader) {
-                bulk_wait_read_all();  // the previous store from this staging tile has read it
-                mbar_arrive(&misc->st_free[e]);
+                // the store that last read this staging tile is done with it
+                if constexpr (EPI_WGS == 1) bulk_wait_read_newest_pending();
+                else bulk_wait_read_all();
+                mbar_arrive(&misc->st_free[sb]);
             }
             const int acc = i % NACC;
             if (!mbar_wait(&misc->tfull[acc], (i / NACC) & 1)) break;
-            if (!mbar_wait(&misc->st_free[e], n & 1)) break;
+            if (!mbar_wait(&misc->st_free[sb], n & 1)) break;
             tc_fence_after();
             if (!mbar_wait(&misc->norm_full[i % NORM_BUF], (i / NORM_BUF) & 1)) break;
             const float nrm = misc->norm[i % NORM_BUF][row];
@@ -418,9 +428,9 @@ __global__ void __maxnreg__(MAX_REGS)
             }
             fence_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&misc->st_full[e]);
+            if (lane == 0) mbar_arrive(&misc->st_full[sb]);
             if (leader) {
-                if (!mbar_wait(&misc->st_full[e], n & 1)) break;
+                if (!mbar_wait(&misc->st_full[sb], n & 1)) break;
                 tma_store_2d(&omap, st, 0, tile * TILE);
                 tma_store_2d(&omap, st + KBLK_BYTES, 64, tile * TILE);
                 bulk_commit();

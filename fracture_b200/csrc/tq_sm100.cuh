@@ -142,6 +142,10 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Waits until the committed bulk stores no longer read their shared-memory source.
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until all but the newest committed bulk-store group no longer read shared memory.
+__device__ __forceinline__ void bulk_wait_read_newest_pending() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 // Waits until the committed bulk stores are complete.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Orders this thread's generic-proxy shared-memory writes before later async-proxy reads.
