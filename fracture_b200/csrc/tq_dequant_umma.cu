@@ -120,7 +120,7 @@ __device__ __forceinline__ uint32_t pack_out(float a, float b) {
 
 template <typename TOut, int BITS>
 __global__ void __maxnreg__(MAX_REGS)
-    tq_dequant_umma_kernel(const __grid_constant__ CUtensorMap omap, TqArgs a, int num_tiles) {
+    tq_dequant_umma_kernel(const __grid_constant__ CUtensorMap omap, TqArgs a, int num_tiles, DivU32 hdiv) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     using L = Smem<BITS>;
@@ -229,24 +229,28 @@ __global__ void __maxnreg__(MAX_REGS)
             if (done > 0) mbar_wait(&misc->tfull[(done - 1) % NACC], ((done - 1) / NACC) & 1);
         }
     } else if (warp <= DEC_WARPS) {
-        // ── decoders: thread dt handles half h of row r ─────────────────────
+        // ── decoders: thread dt handles part h of row r ─────────────────────
         // The packed codes of tile i+1 and the block-table entry of tile i+2 are requested
         // while tile i is decoded, so the two dependent global loads overlap the pipeline.
+        // A warp covers RPW rows; quarter-warp q (8 lanes) takes part q of 8 consecutive rows,
+        // so its 16-byte stores into the swizzled A tile fall in 8 distinct bank groups.
+        constexpr int RPW = 32 / TPR;
+        static_assert(RPW == 8, "one 16-byte chunk column per quarter-warp");
         const int dt = threadIdx.x - 32;
-        const int r = dt / TPR, h = dt % TPR;  // part h of row r: codes CPT*h .. CPT*h + CPT - 1
+        const int r = (dt >> 5) * RPW + lane % RPW, h = lane / RPW;  // part h of row r: codes CPT*h ..
         constexpr int CPT = D / TPR;
         const uint32_t tlane = smem_u32(tab) + (uint32_t)(lane & (TB::copies - 1)) * TB::entry_bytes;
         constexpr int NW = BITS * CPT / 32;  // 32-bit words of packed codes per part
         // Pool row of this thread's vector in tile i, in two steps so that no branch waits on
         // a load: bt_of issues the slot-map or block-table read (-1: no vector; 0 without
         // either), row_of applies the slot rule of tq_slot to it two steps later (-1: no row).
-        // (32-bit division: the host keeps the vector count below 2^31.)
+        // (32-bit division by the head count: the host keeps the vector count below 2^31.)
         // Prefetched values stay raw (the slot-map entry, or the int32 table entry zero-extended;
         // fp16 norm bits) until they are used, so no conversion waits on a load still in flight.
         auto bt_of = [&](int i) -> int64_t {
             const uint32_t vi = (uint32_t)((int)blockIdx.x + i * (int)gridDim.x) * TILE + r;
             if (i >= ntiles_cta || (int64_t)vi >= nvec) return -1;
-            const uint32_t tok = vi / (uint32_t)a.num_heads;
+            const uint32_t tok = divu32(vi, hdiv);
             if (a.slot_map) return __ldg(a.slot_map + tok);
             if (!a.block_table) return 0;
             return (int64_t)(uint32_t)__ldg(a.block_table + ((a.start_pos + tok) >> 4));
@@ -254,7 +258,7 @@ __global__ void __maxnreg__(MAX_REGS)
         auto row_of = [&](int i, int64_t raw) -> int64_t {
             if (raw == -1) return -1;
             const uint32_t vi = (uint32_t)((int)blockIdx.x + i * (int)gridDim.x) * TILE + r;
-            const uint32_t tok = vi / (uint32_t)a.num_heads, head = vi - tok * (uint32_t)a.num_heads;
+            const uint32_t tok = divu32(vi, hdiv), head = vi - tok * (uint32_t)a.num_heads;
             const int64_t pos = a.start_pos + tok;
             int64_t slot = pos;
             if (a.slot_map) {
@@ -484,7 +488,7 @@ static int launch_dequant(const TqArgs& a, cudaStream_t s) {
     if (e != cudaSuccess) return (int)e;
     const int num_tiles = (int)((nvec + dq::TILE - 1) / dq::TILE);
     const int grid = std::max(1, std::min(num_tiles, num_sms()));
-    kern<<<grid, dq::THREADS, smem, s>>>(map, a, num_tiles);
+    kern<<<grid, dq::THREADS, smem, s>>>(map, a, num_tiles, sm100::make_divu32((uint32_t)a.num_heads));
     return (int)cudaGetLastError();
 }
 

@@ -14,6 +14,30 @@ constexpr int TILE = 128;                   // vectors per tile (MMA M)
 constexpr int KBLK_BYTES = TILE * 128;      // one 64-element K-block of a 128-row 16-bit tile, SW128
 constexpr int TILE_BYTES = 2 * KBLK_BYTES;  // 32 KB: a 128 x 128 16-bit tile
 
+// Unsigned 32-bit division by a divisor fixed for a launch, as one multiply-high and two
+// shifts: the round-up method of Granlund and Montgomery, "Division by invariant integers
+// using multiplication" (PLDI 1994, section 4). With l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1 (which fits in 32 bits), t = mulhi(m, n) gives
+// n / d = (t + ((n - t) >> min(l, 1))) >> max(l - 1, 0) for every 32-bit n.
+struct DivU32 {
+    uint32_t m, s1, s2;
+};
+
+inline DivU32 make_divu32(uint32_t d) {  // d >= 1
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;
+    DivU32 v;
+    v.m = (uint32_t)((((uint64_t)1 << 32) * (((uint64_t)1 << l) - d)) / d + 1);
+    v.s1 = l < 1 ? l : 1;
+    v.s2 = l > 1 ? l - 1 : 0;
+    return v;
+}
+
+__device__ __forceinline__ uint32_t divu32(uint32_t n, const DivU32& v) {
+    const uint32_t t = __umulhi(v.m, n);
+    return (t + ((n - t) >> v.s1)) >> v.s2;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -364,6 +364,30 @@ def test_tensor_core_dequant_paged_many_tiles(dt, bits):
     assert (num / den).min() > 0.9999
 
 
+@pytest.mark.parametrize("H", [1, 3, 5, 7])
+def test_tensor_core_dequant_odd_head_counts(H):
+    """Token and head of each vector come from a division by the head count done by
+    multiply-high and shifts; head counts that are not powers of two, over several waves of
+    tiles, against the float32 statement."""
+    T, d, bits, start = 160 * 128 // H + 7, 128, 4, 9
+    x, raw = make_input(T, H, d, "f16", seed=40 + H)
+    pi, c = tables(d, bits, 77)
+    P = d * bits // 8
+    nblk = (start + T + 15) // 16
+    table = np.random.default_rng(H).permutation(nblk).astype(np.int32)
+    tpi, tc, tt = torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), torch.from_numpy(table).to(DEV)
+    packed = torch.zeros((nblk * 16, H * P), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((nblk * 16, H), dtype=torch.float16, device=DEV)
+    K.tq_compress_paged(dev(x, "f16"), tpi, tc, bits, packed, norms, block_table=tt, start_pos=start)
+    out = torch.full((T, H, d), 7.0, dtype=torch.float16, device=DEV)
+    K.tq_dequant_paged(packed, norms, tpi, tc, bits, out, block_table=tt, start_pos=start)
+    torch.cuda.synchronize()
+    pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits, num_threads=8)
+    ref = tq.decompress_c(pc, nc, pi, c, bits, H, d).reshape(T, H, d)
+    ops.assert_close_fp(out.float().cpu().numpy(), ref, rel=3e-4, min_cos=0.9999,
+                        label=f"tensor-core dequant H={H}", dtype="f16")
+
+
 def test_tensor_core_dequant_missing_blocks_give_zeros():
     """Tokens whose block-table entry is -1 dequantize to zeros, like the CUDA-core kernel."""
     T, H, d, bits = 300, 8, 128, 4

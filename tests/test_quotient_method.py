@@ -65,3 +65,37 @@ def test_corrected_reciprocal_quotient_is_correctly_rounded():
         rem = A - q1 * B
         assert _rn32(rem) == rem, (a, b)
         assert _rn32(q1 + rem * r) == _rn32(A / B), (a, b)
+
+
+def _divu32_params(d):
+    """Multiplier and shifts of the round-up method (``make_divu32`` in
+    ``fracture_b200/csrc/tq_sm100.cuh``): Granlund and Montgomery, PLDI 1994, section 4."""
+    l = 0
+    while (1 << l) < d:
+        l += 1
+    m = ((1 << 32) * ((1 << l) - d)) // d + 1
+    assert 0 < m < (1 << 32)
+    return m, min(l, 1), max(l - 1, 0)
+
+
+def _divu32(n, params):
+    m, s1, s2 = params
+    t = (m * n) >> 32
+    return (t + ((n - t) >> s1)) >> s2
+
+
+def test_invariant_divisor_quotient_is_exact():
+    """n / d by multiply-high and shifts equals floor division for every divisor tried, at the
+    dividends where a wrong multiplier would show first (around multiples of d and at 2^32 - 1)."""
+    rng = np.random.default_rng(7)
+    divisors = list(range(1, 300)) + [2 ** k for k in range(32)] + [2 ** k - 1 for k in range(2, 33)] + \
+        [2 ** k + 1 for k in range(2, 32)] + [int(x) for x in rng.integers(1, 2 ** 32, 200)]
+    for d in divisors:
+        p = _divu32_params(d)
+        ns = [0, 1, d - 1, d, d + 1, 2 ** 31 - 1, 2 ** 31, 2 ** 32 - 1] + \
+            [int(x) for x in rng.integers(0, 2 ** 32, 64)]
+        q = (2 ** 32 - 1) // d
+        ns += [q * d, q * d - 1, min(q * d + d - 1, 2 ** 32 - 1)]
+        for n in ns:
+            if 0 <= n < 2 ** 32:
+                assert _divu32(n, p) == n // d, (d, n)
