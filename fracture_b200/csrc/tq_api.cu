@@ -11,7 +11,6 @@
 
 namespace fb {
 int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled);
-int tq_compress_umma_noalloc(const TqArgs& a, cudaStream_t s, bool* handled);
 int tq_dequant_umma(const TqArgs& a, cudaStream_t s, bool* handled);
 void set_last_error(const char* msg);
 }
@@ -78,10 +77,9 @@ extern "C" int fb_launch_tq_compress_slots(const void* input, int dtype, const f
                            slot_map, 0, num_pool_rows, packed_pool, norms_pool, err_count, stream);
 }
 
-// Same contract as fb_launch_tq_compress_paged, but the call allocates no device memory: the
-// fixup queue of the tensor-core path is a static device array sized for kTqNoAllocMaxVectors
-// vectors (tq_umma.cu), and larger calls are rejected before anything is launched. The first
-// call on a device looks up that array's address (set-up), later calls only launch.
+// Same contract as fb_launch_tq_compress_paged, which allocates no device memory (the settle
+// queue of the tensor-core path is in shared memory), with a per-call limit of
+// kTqNoAllocMaxVectors vectors: larger calls are rejected before anything is launched.
 extern "C" int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype, const float* rotation,
                                                    const float* centroids, int bits, int64_t num_tokens,
                                                    int num_kv_heads, int head_dim, const int32_t* block_table,
@@ -94,8 +92,8 @@ extern "C" int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype,
     if (num_tokens > kTqNoAllocMaxVectors / num_kv_heads) {
         char msg[200];
         snprintf(msg, sizeof msg,
-                 "fb_launch_tq_compress_paged_noalloc: %lld tokens x %d KV heads exceed the static scratch "
-                 "limit of %lld vectors per call",
+                 "fb_launch_tq_compress_paged_noalloc: %lld tokens x %d KV heads exceed the per-call "
+                 "limit of %lld vectors",
                  (long long)num_tokens, num_kv_heads, (long long)kTqNoAllocMaxVectors);
         set_last_error(msg);
         return (int)cudaErrorInvalidValue;
@@ -119,7 +117,7 @@ extern "C" int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype,
     a.norms_pool = norms_pool;
     a.err_count = err_count;
     bool handled = false;
-    rc = tq_compress_umma_noalloc(a, (cudaStream_t)stream, &handled);
+    rc = tq_compress_umma(a, (cudaStream_t)stream, &handled);
     if (handled) return rc;
     return tq_compress_exact(a, (cudaStream_t)stream);
 }

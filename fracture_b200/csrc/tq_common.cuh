@@ -6,8 +6,7 @@
 
 namespace fb {
 
-// Largest call (num_tokens * num_kv_heads) of the no-allocation compress entry point; its
-// fixup queue is a static device array of this many entries.
+// Largest call (num_tokens * num_kv_heads) accepted by the no-allocation compress entry point.
 constexpr int64_t kTqNoAllocMaxVectors = (int64_t)1 << 19;
 
 struct TqArgs {

@@ -56,13 +56,17 @@ constexpr int EPI_WGS = 4;                 // epilogue warpgroups, one TMEM accu
 constexpr int THREADS = 64 + EPI_WGS * 128;  // warp 0 TMA, warp 1 MMA, then the epilogue
 constexpr int VCH = 32;                    // accumulator values per thread per TMEM load round
 constexpr int MAX_REGS = 96;               // 18 warps: up to 5 per scheduler, 16K registers each
+constexpr int SQ = 512;                    // settle queue entries per CTA (shared memory)
 static_assert(THREADS > NB, "one thread per table bin plus one for the checks");
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 // Rows whose fast-path result is not certain (a coordinate within kRiskBand of a
 // decision boundary, or a norm within kNormBand of an fp16 rounding tie) are
-// queued here, one entry per uncertain coordinate (or one norm-only entry), and
-// settled by tq_fixup_kernel with the exact float32 sequence.
+// queued in shared memory, one entry per uncertain coordinate (or one norm-only
+// entry), and settled with the exact float32 sequence by the whole CTA, one entry
+// per thread, once its last tile is coded. Rows that need every coordinate settled
+// (non-finite input, or no decision table), and rows that find the queue full, are
+// settled whole by their epilogue thread at once.
 struct FixEntry {
     uint32_t vi;    // vector index (token * heads + head) of the call
     uint32_t info;  // bits 0-6: coordinate; kHasCoord, kFixNorm, kFixAll, kSkip
@@ -81,6 +85,8 @@ struct Misc {
     float cen[256];
     float bin_mid[NB];      // per-bin table entry before it is copied LUT_COPIES times
     uint32_t bin_base[NB];
+    uint32_t sq_tail;  // settle queue: positions reserved (entries at or past SQ are not stored)
+    FixEntry sq[SQ];
 };
 
 // Byte offsets from the 1024-aligned base of dynamic shared memory.
@@ -112,6 +118,18 @@ struct LutEntry {
     uint32_t base;  // code below the boundary (the code of the whole bin when it holds none)
 };
 
+
+// Correctly rounded x / den for fp16 x with |x| <= den, den in [1e-8, 2^20]: from the
+// correctly rounded reciprocal r, two FMA corrections of the quotient (P. Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000 processor", IBM J.
+// Res. Dev. 34(1), 1990): q1 = q0 + (x - den q0) r is faithful, the remainder x - den q1
+// is then exact and q1 + (x - den q1) r is the rounded quotient. Branch-free, so the
+// quotients of a row pipeline. (Checked against exact rational arithmetic on the domain.)
+__device__ __forceinline__ float quot_rn(float x, float den, float r) {
+    const float q0 = __fmul_rn(x, r);
+    const float q1 = __fmaf_rn(__fmaf_rn(-q0, den, x), r, q0);
+    return __fmaf_rn(__fmaf_rn(-q1, den, x), r, q1);
+}
 
 // Exact float32 statement for one queued row, by one thread, on the stored bytes:
 // the sequential sum of the squares (norm), then for each listed coordinate the
@@ -170,10 +188,76 @@ __device__ __forceinline__ void settle_row_inline(const TqArgs& a, int64_t vi, i
     }
 }
 
+// One queued entry, by one thread: the sequential sum of the row's
+// squares (norm, rewritten when flagged), then for the entry's coordinate i the sequential
+// sum of Pi[i][j] * (x_j / (norm + 1e-8)) and the first-minimum nearest centroid, whose bits
+// are patched into the pool row with word atomics (entries of one row patch disjoint bits;
+// threads may hold entries of the same row). FP16 inputs take the corrected-reciprocal quotient.
+template <typename TIn, int BITS>
+__device__ __forceinline__ void settle_entry(const TqArgs& a, const FixEntry& en, const float* cen) {
+    constexpr int EPV = 16 / sizeof(TIn);  // elements per 16-byte vector
+    const int nlev = 1 << BITS;
+    const int P = (D * BITS) >> 3;
+    const uint4* xr = (const uint4*)((const TIn*)a.input + (int64_t)en.vi * D);
+    const int i = (int)(en.info & 127u);
+    const float4* pr = (const float4*)(a.rotation + i * D);
+    // the row and, for a coordinate, its rotation row into L1 at once: the sums below then
+    // wait on one memory round trip instead of one per load
+#pragma unroll
+    for (int l = 0; l < D * (int)sizeof(TIn) / 128; ++l)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"((const char*)xr + 128 * l));
+    if (en.info & kHasCoord) {
+#pragma unroll
+        for (int l = 0; l < D * 4 / 128; ++l) asm volatile("prefetch.global.L1 [%0];" ::"l"((const char*)pr + 128 * l));
+    }
+    float s = 0.0f;
+#pragma unroll 4
+    for (int c = 0; c < D / EPV; ++c) {
+        Vec16<TIn> u;
+        u.u = __ldg(xr + c);
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) {
+            const float x = to_f32(u.e[e]);
+            s = __fadd_rn(s, __fmul_rn(x, x));
+        }
+    }
+    const float norm = __fsqrt_rn(s);
+    if (en.info & kFixNorm) ((__half*)a.norms_pool)[en.prow] = __float2half_rn(norm);
+    if (!(en.info & kHasCoord)) return;
+    const float den = __fadd_rn(norm, 1e-8f);
+    const float r = __frcp_rn(den);
+    float y = 0.0f;
+#pragma unroll 2
+    for (int c = 0; c < D / EPV; ++c) {
+        Vec16<TIn> u;
+        u.u = __ldg(xr + c);
+#pragma unroll
+        for (int e4 = 0; e4 < EPV / 4; ++e4) {
+            const float4 p = __ldg(pr + c * (EPV / 4) + e4);
+            const float pv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float x = to_f32(u.e[4 * e4 + k]);
+                const float qn = dtype_of<TIn>::value == FB_FP16 ? quot_rn(x, den, r) : __fdiv_rn(x, den);
+                y = __fadd_rn(y, __fmul_rn(pv[k], qn));
+            }
+        }
+    }
+    const uint32_t code = (uint32_t)nearest_centroid(y, cen, nlev);
+    uint32_t* roww = (uint32_t*)((uint8_t*)a.packed_pool + en.prow * P);
+    for (int b = 0; b < BITS; ++b) {
+        // MSB-first stream bit bp lives in byte bp >> 3 at bit 7 - (bp & 7); bytes little-endian in words
+        const int bp = i * BITS + b;
+        const int byte = bp >> 3;
+        const uint32_t bit = 1u << (8 * (byte & 3) + 7 - (bp & 7));
+        if ((code >> (BITS - 1 - b)) & 1u) atomicOr(roww + (byte >> 2), bit);
+        else atomicAnd(roww + (byte >> 2), ~bit);
+    }
+}
+
 template <typename TIn, int NPARTS, int BITS>
 __global__ void __maxnreg__(MAX_REGS)
-    tq_compress_umma_kernel(const __grid_constant__ CUtensorMap tmap, TqArgs a, int num_tiles, FixEntry* fix,
-                            unsigned long long* fix_count, unsigned int fix_cap) {
+    tq_compress_umma_kernel(const __grid_constant__ CUtensorMap tmap, TqArgs a, int num_tiles) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sB = base;
@@ -206,6 +290,7 @@ __global__ void __maxnreg__(MAX_REGS)
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         misc->use_exact = 0;
+        misc->sq_tail = 0u;
         // The first tiles are requested now, so their loads overlap the set-up below.
         for (int i = 0; i < prefetched; ++i) {
             const int tile = (int)blockIdx.x + i * (int)gridDim.x;
@@ -484,38 +569,47 @@ __global__ void __maxnreg__(MAX_REGS)
                                    ((use_exact || !finite) ? kFixAll | kFixNorm : 0u);
             if (!finite) mask[0] = mask[1] = mask[2] = mask[3] = 0u;
             const uint32_t ncoord = __popc(mask[0]) + __popc(mask[1]) + __popc(mask[2]) + __popc(mask[3]);
-            if (flags || ncoord) {
-                // one entry per listed coordinate (the first also carries the norm), a
-                // norm-only entry, or one whole-row entry when the table is not in use
-                const bool whole = (flags & kFixAll) != 0;
-                const uint32_t nent = (whole || ncoord == 0) ? 1u : ncoord;
-                const unsigned long long qi = atomicAdd(fix_count, (unsigned long long)nent);
-                if (qi + nent <= fix_cap) {
-                    if (whole || ncoord == 0) {
-                        fix[qi] = FixEntry{(uint32_t)vi, flags, prow};
-                    } else {
-                        uint32_t k = 0, nf = flags;
+            if (flags & kFixAll) {
+                // rare: a non-finite row, or no decision table; settled whole here
+                settle_row_inline<TIn, BITS>(a, vi, prow, flags, 0u, 0u, 0u, 0u, misc->cen);
+            } else if (flags || ncoord) {
+                // one entry per listed coordinate (the first also carries the norm flag), or a
+                // norm-only entry; settled after the last tile (the row's stores above stay first)
+                const uint32_t nent = ncoord == 0 ? 1u : ncoord;
+                const uint32_t q0 = atomicAdd(&misc->sq_tail, nent);
+                if (q0 + nent > (uint32_t)SQ) {
+                    // queue full: void the slots reserved below SQ and settle the row here
+                    for (uint32_t q = q0; q < (uint32_t)SQ; ++q) misc->sq[q] = FixEntry{0u, kSkip, 0};
+                    settle_row_inline<TIn, BITS>(a, vi, prow, flags, mask[0], mask[1], mask[2], mask[3], misc->cen);
+                } else if (ncoord == 0) {
+                    misc->sq[q0] = FixEntry{(uint32_t)vi, flags, prow};
+                } else {
+                    uint32_t k = 0, nf = flags;
 #pragma unroll 1
-                        for (int c4 = 0; c4 < 4; ++c4) {
-                            uint32_t m = mask[c4];
-                            while (m) {
-                                const uint32_t i = (uint32_t)(c4 * 32 + __ffs(m) - 1);
-                                m &= m - 1;
-                                fix[qi + k] = FixEntry{(uint32_t)vi, i | kHasCoord | nf, prow};
-                                nf = 0;
-                                ++k;
-                            }
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        uint32_t m = mask[c4];
+                        while (m) {
+                            const uint32_t i = (uint32_t)(c4 * 32 + __ffs(m) - 1);
+                            m &= m - 1;
+                            misc->sq[q0 + k] = FixEntry{(uint32_t)vi, i | kHasCoord | nf, prow};
+                            nf = 0;
+                            ++k;
                         }
                     }
-                } else {
-                    // queue full: mark the reserved entries void and settle the row here
-                    for (unsigned long long t = qi; t < fix_cap; ++t) fix[t] = FixEntry{0u, kSkip, 0};
-                    settle_row_inline<TIn, BITS>(a, vi, prow, flags, mask[0], mask[1], mask[2], mask[3], misc->cen);
                 }
             }
         }
     }
 
+    // Every tile is coded and stored: the queued entries, one per thread.
+    __syncthreads();
+    {
+        const uint32_t nq = min(misc->sq_tail, (uint32_t)SQ);
+        for (uint32_t e = threadIdx.x; e < nq; e += THREADS) {
+            const FixEntry en = misc->sq[e];
+            if (!(en.info & kSkip)) settle_entry<TIn, BITS>(a, en, misc->cen);
+        }
+    }
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
@@ -523,102 +617,6 @@ __global__ void __maxnreg__(MAX_REGS)
     }
 }
 
-
-// Correctly rounded x / den for fp16 x with |x| <= den, den in [1e-8, 2^20]: from the
-// correctly rounded reciprocal r, two FMA corrections of the quotient (P. Markstein,
-// "Computation of elementary functions on the IBM RISC System/6000 processor", IBM J.
-// Res. Dev. 34(1), 1990): q1 = q0 + (x - den q0) r is faithful, the remainder x - den q1
-// is then exact and q1 + (x - den q1) r is the rounded quotient. Branch-free, so the
-// quotients of a row pipeline. (Checked against exact rational arithmetic on the domain.)
-__device__ __forceinline__ float quot_rn(float x, float den, float r) {
-    const float q0 = __fmul_rn(x, r);
-    const float q1 = __fmaf_rn(__fmaf_rn(-q0, den, x), r, q0);
-    return __fmaf_rn(__fmaf_rn(-q1, den, x), r, q1);
-}
-
-// Settles queued entries with the exact float32 statement, one entry per thread: the
-// sequential sum of the row's squares (norm, rewritten when flagged), then for the
-// entry's coordinate the sequential sum of Pi[i][j] * (x_j / (norm + 1e-8)) and the
-// first-minimum nearest centroid, whose bits are patched into the pool row with word
-// atomics (entries of one row patch disjoint bits). Whole-row entries (table not in
-// use) run settle_row_inline.
-constexpr int FIX_THREADS = 128;
-
-template <typename TIn, int BITS>
-__global__ void __launch_bounds__(FIX_THREADS) tq_fixup_kernel(TqArgs a, const FixEntry* __restrict__ fix,
-                                                               unsigned long long* fix_count, unsigned int* fix_done,
-                                                               unsigned int fix_cap) {
-    __shared__ float cen[256];
-    constexpr int EPV = 16 / sizeof(TIn);  // elements per 16-byte vector
-    constexpr int NV = D / EPV;
-    const int nlev = 1 << BITS;
-    const int P = (D * BITS) >> 3;
-    for (int e = threadIdx.x; e < nlev; e += blockDim.x) cen[e] = __ldg(a.centroids + e);
-    __syncthreads();
-    const unsigned long long n = min(*(volatile unsigned long long*)fix_count, (unsigned long long)fix_cap);
-    for (unsigned long long q = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; q < n;
-         q += (unsigned long long)gridDim.x * blockDim.x) {
-        const FixEntry en = fix[q];
-        if (en.info & kSkip) continue;
-        if (en.info & kFixAll) {
-            settle_row_inline<TIn, BITS>(a, en.vi, en.prow, kFixAll | kFixNorm, 0u, 0u, 0u, 0u, cen);
-            continue;
-        }
-        const uint4* xr = (const uint4*)((const TIn*)a.input + (int64_t)en.vi * D);
-        Vec16<TIn> xv[NV];
-#pragma unroll
-        for (int c = 0; c < NV; ++c) xv[c].u = __ldg(xr + c);
-        float s = 0.0f;
-#pragma unroll
-        for (int c = 0; c < NV; ++c)
-#pragma unroll
-            for (int e = 0; e < EPV; ++e) {
-                const float x = to_f32(xv[c].e[e]);
-                s = __fadd_rn(s, __fmul_rn(x, x));
-            }
-        const float norm = __fsqrt_rn(s);
-        if (en.info & kFixNorm) ((__half*)a.norms_pool)[en.prow] = __float2half_rn(norm);
-        if (!(en.info & kHasCoord)) continue;
-        const float den = __fadd_rn(norm, 1e-8f);
-        const float r = __frcp_rn(den);
-        const int i = (int)(en.info & 127u);
-        const float4* pr = (const float4*)(a.rotation + i * D);
-        float y = 0.0f;
-#pragma unroll
-        for (int c = 0; c < D / 4; ++c) {
-            const float4 p = __ldg(pr + c);
-            const float pv[4] = {p.x, p.y, p.z, p.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int j = 4 * c + k;
-                const float x = to_f32(xv[j / EPV].e[j % EPV]);
-                const float qn = dtype_of<TIn>::value == FB_FP16 ? quot_rn(x, den, r) : __fdiv_rn(x, den);
-                y = __fadd_rn(y, __fmul_rn(pv[k], qn));
-            }
-        }
-        const uint32_t code = (uint32_t)nearest_centroid(y, cen, nlev);
-        uint32_t* roww = (uint32_t*)((uint8_t*)a.packed_pool + en.prow * P);
-        for (int b = 0; b < BITS; ++b) {
-            // MSB-first stream bit bp lives in byte bp >> 3 at bit 7 - (bp & 7); bytes little-endian in words
-            const int bp = i * BITS + b;
-            const int byte = bp >> 3;
-            const uint32_t bit = 1u << (8 * (byte & 3) + 7 - (bp & 7));
-            if ((code >> (BITS - 1 - b)) & 1u) atomicOr(roww + (byte >> 2), bit);
-            else atomicAnd(roww + (byte >> 2), ~bit);
-        }
-    }
-    // The last block to finish clears the queue header for the next call (every block
-    // read the count before it arrived here).
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        if (atomicAdd(fix_done, 1u) == gridDim.x - 1) {
-            *fix_count = 0ull;
-            *fix_done = 0u;
-            __threadfence();
-        }
-    }
-}
 
 }  // namespace umma
 
@@ -645,86 +643,8 @@ static bool device_is_sm100() {
     return major == 10 && minor == 0;
 }
 
-// Fixup queue: one per device, grown to one 16-byte entry per vector of the largest call, kept for the
-// life of the process. Its 256-byte header holds the entry count (u64 at 0) and the fixup kernel's
-// block counter (u32 at 8): zeroed when the queue is allocated, and zeroed again by the fixup kernel
-// once it has consumed the queue. The queue is consumed by the fixup kernel of the same launch
-// sequence on the same stream; calls on different streams of one device must not overlap.
-struct FixWorkspace {
-    void* ptr = nullptr;
-    size_t cap = 0;  // entries
-};
-
-static int fix_workspace(int64_t nvec, cudaStream_t s, umma::FixEntry** entries, unsigned long long** count,
-                         unsigned int* cap) {
-    static FixWorkspace ws[64];
-    static std::mutex mu;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return (int)e;
-    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> g(mu);
-    FixWorkspace& w = ws[dev];
-    const size_t want = (size_t)std::max<int64_t>(nvec, 4096);
-    if (w.cap < want) {
-        if (w.ptr) {
-            e = cudaFree(w.ptr);
-            if (e != cudaSuccess) return (int)e;
-        }
-        w.ptr = nullptr;
-        w.cap = 0;
-        e = cudaMalloc(&w.ptr, 256 + want * sizeof(umma::FixEntry));
-        if (e != cudaSuccess) return (int)e;
-        e = cudaMemsetAsync(w.ptr, 0, 256, s);
-        if (e != cudaSuccess) return (int)e;
-        w.cap = want;
-    }
-    *count = (unsigned long long*)w.ptr;
-    *entries = (umma::FixEntry*)((char*)w.ptr + 256);
-    *cap = (unsigned int)std::min<size_t>(w.cap, 0xffffffffu);
-    return 0;
-}
-
-// Fixup queue of the no-allocation entry point: a file-scope device array, so that a call
-// allocates nothing. It holds the queue header (256 bytes) and one entry per vector of the
-// largest call accepted, kTqNoAllocMaxVectors (524288 vectors, e.g. 65536 tokens x 8 KV heads):
-// 8 MiB + 256 bytes per device, reserved when the module loads. One array per device serves
-// every call on that device, so calls that overlap in time (two streams, two host threads)
-// race on it.
-static __device__ __align__(256) unsigned char
-    g_tq_fix_scratch[256 + (size_t)kTqNoAllocMaxVectors * sizeof(umma::FixEntry)];
-
-// Set-up, once per device with that device current: the device address of g_tq_fix_scratch,
-// and its queue header cleared on the call's stream. The first call on a device does this set-up
-// (it may load the module), so it belongs before any stream capture; later calls only read the
-// cached address (the fixup kernel leaves the header cleared).
-static int static_fix_scratch(int64_t nvec, cudaStream_t s, umma::FixEntry** entries, unsigned long long** count,
-                              unsigned int* cap) {
-    static void* addr[64];
-    static std::mutex mu;
-    if (nvec > kTqNoAllocMaxVectors) return (int)cudaErrorInvalidValue;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return (int)e;
-    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> g(mu);
-    if (!addr[dev]) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_tq_fix_scratch);
-        if (e != cudaSuccess) return (int)e;
-        if (!p) return (int)cudaErrorInvalidSymbol;
-        e = cudaMemsetAsync(p, 0, 256, s);  // the queue header starts at zero
-        if (e != cudaSuccess) return (int)e;
-        addr[dev] = p;
-    }
-    *count = (unsigned long long*)addr[dev];
-    *entries = (umma::FixEntry*)((char*)addr[dev] + 256);
-    *cap = (unsigned int)kTqNoAllocMaxVectors;
-    return 0;
-}
-
 template <typename TIn, int NPARTS, int BITS>
-static int launch_umma(const TqArgs& a, cudaStream_t s, bool static_scratch) {
+static int launch_umma(const TqArgs& a, cudaStream_t s) {
     auto encode = get_encode();
     if (!encode) return (int)cudaErrorNotSupported;
     const int64_t nvec = a.num_tokens * a.num_heads;
@@ -738,32 +658,17 @@ static int launch_umma(const TqArgs& a, cudaStream_t s, bool static_scratch) {
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return (int)cudaErrorInvalidValue;
-    umma::FixEntry* fix;
-    unsigned long long* fix_count;
-    unsigned int fix_cap;
-    int rc = static_scratch ? static_fix_scratch(nvec, s, &fix, &fix_count, &fix_cap)
-                            : fix_workspace(nvec, s, &fix, &fix_count, &fix_cap);
-    if (rc) return rc;
-    unsigned int* fix_done = (unsigned int*)((char*)fix_count + 8);
     constexpr int smem = umma::Smem::bytes(NPARTS);
     auto kern = umma::tq_compress_umma_kernel<TIn, NPARTS, BITS>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
     const int num_tiles = (int)((nvec + umma::TILE - 1) / umma::TILE);
     const int grid = std::max(1, std::min(num_tiles, num_sms()));
-    kern<<<grid, umma::THREADS, smem, s>>>(map, a, num_tiles, fix, fix_count, fix_cap);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return (int)e;
-    umma::tq_fixup_kernel<TIn, BITS><<<num_sms() * 2, umma::FIX_THREADS, 0, s>>>(a, fix, fix_count, fix_done, fix_cap);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        cudaMemsetAsync(fix_count, 0, 16, s);  // the header must be clear for the next call
-        return (int)e;
-    }
-    return 0;
+    kern<<<grid, umma::THREADS, smem, s>>>(map, a, num_tiles);
+    return (int)cudaGetLastError();
 }
 
-static int umma_dispatch(const TqArgs& a, cudaStream_t s, bool* handled, bool static_scratch) {
+int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled) {
     *handled = false;
     if (a.head_dim != umma::D || !(a.bits == 2 || a.bits == 3 || a.bits == 4)) return 0;
     if (a.in_dtype != FB_FP16 && a.in_dtype != FB_BF16) return 0;
@@ -775,22 +680,15 @@ static int umma_dispatch(const TqArgs& a, cudaStream_t s, bool* handled, bool st
     if (!sm100) return 0;
     *handled = true;
     if (a.in_dtype == FB_FP16) {
-        if (a.bits == 4) return launch_umma<__half, 2, 4>(a, s, static_scratch);
-        if (a.bits == 3) return launch_umma<__half, 2, 3>(a, s, static_scratch);
-        return launch_umma<__half, 2, 2>(a, s, static_scratch);
+        if (a.bits == 4) return launch_umma<__half, 2, 4>(a, s);
+        if (a.bits == 3) return launch_umma<__half, 2, 3>(a, s);
+        return launch_umma<__half, 2, 2>(a, s);
     }
-    if (a.bits == 4) return launch_umma<__nv_bfloat16, 3, 4>(a, s, static_scratch);
-    if (a.bits == 3) return launch_umma<__nv_bfloat16, 3, 3>(a, s, static_scratch);
-    return launch_umma<__nv_bfloat16, 3, 2>(a, s, static_scratch);
+    if (a.bits == 4) return launch_umma<__nv_bfloat16, 3, 4>(a, s);
+    if (a.bits == 3) return launch_umma<__nv_bfloat16, 3, 3>(a, s);
+    return launch_umma<__nv_bfloat16, 3, 2>(a, s);
 }
 
-int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled) {
-    return umma_dispatch(a, s, handled, false);
-}
-
-int tq_compress_umma_noalloc(const TqArgs& a, cudaStream_t s, bool* handled) {
-    return umma_dispatch(a, s, handled, true);
-}
 
 }  // namespace fb
 

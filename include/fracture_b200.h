@@ -122,13 +122,12 @@ int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotat
                                 void* packed_pool, void* norms_pool, unsigned int* err_count, void* stream);
 
 /* fb_launch_tq_compress_paged that allocates no device memory (no reference counterpart; the
- * reference allocates per call). Results are identical to fb_launch_tq_compress_paged. The fixup
- * queue of the tensor-core path is a static device array (8 MiB + 256 B per device) sized for at
- * most 524288 vectors per call (num_tokens * num_kv_heads); larger calls return
- * cudaErrorInvalidValue with the reason in fb_last_error(), before anything is launched. The first
- * call on a device does set-up (looks up the array's device address), so make it before any
- * stream capture. One array per device serves every call: calls that overlap in time on one
- * device (two streams, two host threads) race and must be serialised by the caller. */
+ * reference allocates per call). Results are identical to fb_launch_tq_compress_paged, which
+ * itself now allocates nothing either: the exact-settle queue of the tensor-core path lives in
+ * each CTA's shared memory, so there is no device scratch and no state shared between calls.
+ * This entry point keeps its per-call limit of 524288 vectors (num_tokens * num_kv_heads):
+ * larger calls return cudaErrorInvalidValue with the reason in fb_last_error(), before anything
+ * is launched. */
 int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype, const float* rotation,
                                         const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
                                         int head_dim, const int32_t* block_table, int64_t start_pos,

@@ -1,11 +1,11 @@
 """fb_launch_tq_compress_paged_noalloc against fb_launch_tq_compress_paged, through the C ABI.
 
-The no-allocation entry point keeps the tensor-core path's fixup queue in a
-static device array; everything else is the same launch sequence, so its pool
-bytes and norms must equal the allocating entry point's bit for bit. Two calls
-in a row with different inputs check that the queue counter is cleared between
-calls. The file sorts last so that it also runs after every other GPU test in
-one process.
+The no-allocation entry point runs the same launch sequence as the paged entry
+point (whose exact-settle queue lives in each CTA's shared memory), with a
+per-call vector limit, so its pool bytes and norms must equal the paged entry
+point's bit for bit. Two calls in a row with different inputs check that no
+state carries over between calls. The file sorts last so that it also runs
+after every other GPU test in one process.
 """
 
 import numpy as np
@@ -80,13 +80,13 @@ def test_noalloc_matches_allocating_entry_two_calls(dt, bits):
 
 
 def test_noalloc_max_size_and_no_device_allocation():
-    """A call at the limit matches the allocating path; calls after set-up leave free device memory unchanged."""
+    """A call at the limit matches the paged entry point; calls after the first leave free device memory unchanged."""
     H, d, bits, dt = 8, 128, 4, "f16"
     T = MAX_VECTORS // H
     pi, c = _tables(d, bits, 7)
     x = _inputs(T, H, d, dt, seed=3)
     outs = [_outputs(T, H, d, bits) for _ in range(2)]
-    _call("fb_launch_tq_compress_paged_noalloc", x, dt, pi, c, bits, None, 0, T, out=outs[1])  # set-up call
+    _call("fb_launch_tq_compress_paged_noalloc", x, dt, pi, c, bits, None, 0, T, out=outs[1])  # loads the module
     torch.cuda.synchronize()
     free0 = torch.cuda.mem_get_info()[0]
     for o in outs:
@@ -112,12 +112,12 @@ def test_noalloc_rejects_oversize_before_launch():
                                                  torch.cuda.current_stream().cuda_stream)
     assert rc != 0
     msg = lib.fb_last_error().decode()
-    assert "static scratch limit" in msg and str(MAX_VECTORS) in msg
+    assert "per-call limit" in msg and str(MAX_VECTORS) in msg
     torch.cuda.synchronize()
 
 
 def test_noalloc_exact_path_shapes_match():
-    """head_dim other than 128 and 8-bit codes take the CUDA-core path, which uses no scratch."""
+    """head_dim other than 128 and 8-bit codes take the CUDA-core path."""
     for (T, H, d, bits) in [(33, 8, 64, 4), (40, 4, 128, 8)]:
         pi, c = _tables(d, bits, 11)
         x = _inputs(T, H, d, "f16", seed=T)
