@@ -488,11 +488,16 @@ __global__ void __maxnreg__(MAX_REGS)
             // settled whole by the exact path).
             auto pass2 = [&](auto safe_tag) {
             constexpr bool SAFE = decltype(safe_tag)::value;
+            // rounds g = NCH/2-1 .. 0 of two chunks each, kept rolled so the hot loop stays small
+            // in the instruction cache; within a round everything is unrolled
+#pragma unroll 1
+            for (int g = NCH / 2 - 1; g >= 0; --g)
 #pragma unroll
-            for (int c = NCH - 1; c >= 0; --c) {
+            for (int hc = 1; hc >= 0; --hc) {
+                const int c = 2 * g + hc;
                 // chunk NCH-1 is in the buffer pass 1 used last; the chunks below alternate
                 constexpr bool last_in_b = ((NCH - 1) & 1) != 0;
-                const bool in_b = (((NCH - 1 - c) & 1) == 0) ? last_in_b : !last_in_b;
+                const bool in_b = hc == 1 ? last_in_b : !last_in_b;
                 uint32_t(&cur)[CW] = in_b ? rb : ra;
                 uint32_t(&nxt)[CW] = in_b ? ra : rb;
                 if (c < NCH - 1) tmem_wait_tie(cur);
@@ -526,7 +531,7 @@ __global__ void __maxnreg__(MAX_REGS)
                     for (int span = 1; span < G; span *= 2)
 #pragma unroll
                         for (int q = 0; q < G; q += 2 * span) code[q] = code[q] * (1u << (BITS * span)) + code[q + span];
-                    w[(c & 1) * WPC + w2] = zero ? zero_word : code[0];
+                    w[hc * WPC + w2] = zero ? zero_word : code[0];
                 }
                 const float dmin = fminf(fminf(dm[0], dm[1]), fminf(dm[2], dm[3]));
                 if (dmin < kRiskBand && !zero) {
@@ -542,10 +547,13 @@ __global__ void __maxnreg__(MAX_REGS)
                         asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
                         if (fabsf(fmaf(-v, kr, mid)) < kRiskBand) m |= 1u << j;
                     }
-                    mask[c >> 1] |= m << ((c & 1) * CW);
+                    const uint32_t mm = m << (hc * CW);
+                    if (g == 0) mask[0] |= mm;
+                    else if (g == 1) mask[1] |= mm;
+                    else if (g == 2) mask[2] |= mm;
+                    else mask[3] |= mm;
                 }
-                if ((c & 1) == 0 && dst) {
-                    const int g = c >> 1;  // both chunks of round g are coded
+                if (hc == 0 && dst) {  // both chunks of round g are coded
                     if constexpr (BITS == 4) {
                         *(uint4*)(dst + 16 * g) = make_uint4(__byte_perm(w[0], 0, 0x0123), __byte_perm(w[1], 0, 0x0123),
                                                              __byte_perm(w[2], 0, 0x0123), __byte_perm(w[3], 0, 0x0123));
