@@ -658,7 +658,7 @@ def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
             res.setdefault(name, {})[f"{bits}bit"] = {
                 "ms_per_step": round(ms, 4), "vectors_per_s": round(vec / (ms / 1e3), 1),
                 "algorithmic_bytes_per_step": by, "achieved_gbs": round(gbs, 1),
-                "frac_of_peak": round(gbs / pk["hbm_gbs"], 4)}
+                "frac_of_peak": round(gbs / (world * pk["hbm_gbs"]), 4)}  # of all GPUs' peak
     if rank != 0:
         return None
     return {"workload": "config4: TurboQuant K+V [65536, 8, 128] FP16 -> paged cache (block 16, random table) "
@@ -666,6 +666,7 @@ def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
             "tokens": T_all, "tokens_per_gpu": T, "scaling": "strong" if world > 1 else None,
             "parallelism": f"token shards of 16-token blocks over {world} GPU(s), no collective on the data path",
             "output_dtype": "fp16", "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"],
+            "frac_of": f"{world} x peak_gbs (whole job)",
             "l2": "256 MB written before every timed step (a shard can fit in L2); the flush is outside the timed events",
             "bound": "hbm", **res}
 
