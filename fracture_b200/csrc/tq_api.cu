@@ -52,6 +52,7 @@ static int tq_compress_any(const void* input, int dtype, const float* rotation, 
     a.packed_pool = packed_pool;
     a.norms_pool = norms_pool;
     a.err_count = err_count;
+    if (tq_small_compress_call(a)) return tq_compress_small(a, (cudaStream_t)stream);
     bool handled = false;
     rc = tq_compress_umma(a, (cudaStream_t)stream, &handled);
     if (handled) return rc;
@@ -116,6 +117,7 @@ extern "C" int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype,
     a.packed_pool = packed_pool;
     a.norms_pool = norms_pool;
     a.err_count = err_count;
+    if (tq_small_compress_call(a)) return tq_compress_small(a, (cudaStream_t)stream);
     bool handled = false;
     rc = tq_compress_umma(a, (cudaStream_t)stream, &handled);
     if (handled) return rc;
@@ -148,6 +150,7 @@ static int tq_dequant_any(const void* packed_pool, const void* norms_pool, const
     a.norms_pool = const_cast<void*>(norms_pool);
     a.output = output;
     a.out_dtype = dtype;
+    if (tq_small_dequant_call(a)) return tq_dequant_small(a, (cudaStream_t)stream);
     bool handled = false;
     rc = tq_dequant_umma(a, (cudaStream_t)stream, &handled);
     if (handled) return rc;

@@ -9,6 +9,14 @@ namespace fb {
 // Largest call (num_tokens * num_kv_heads) accepted by the no-allocation compress entry point.
 constexpr int64_t kTqNoAllocMaxVectors = (int64_t)1 << 19;
 
+// Calls of at most this many head vectors (num_tokens * num_kv_heads) take the small-call exact
+// kernels of tq_small.cu (a few vectors per CTA, none of the tensor-core kernels' set-up):
+// where they beat the tensor-core kernels on B200 (GPU time of graph-replayed calls, head_dim
+// 128: compress 6.1 vs 10.0 us at 32 vectors, 7.3 vs 10.5 at 256, 10.5 vs 11.0 at 1024;
+// dequantize 5.8 vs 6.7 us at 32 vectors, even at 256).
+constexpr int64_t kTqSmallCompressVectors = 1024;
+constexpr int64_t kTqSmallDequantVectors = 192;
+
 struct TqArgs {
     const void* input;         // compress: [T, H, d] fp16/bf16
     int in_dtype;
@@ -100,5 +108,9 @@ __device__ __forceinline__ int unpack_code(const uint8_t* row, int i, int bits) 
 
 int tq_compress_exact(const TqArgs& a, cudaStream_t s);
 int tq_dequant_exact(const TqArgs& a, cudaStream_t s);
+bool tq_small_compress_call(const TqArgs& a);
+bool tq_small_dequant_call(const TqArgs& a);
+int tq_compress_small(const TqArgs& a, cudaStream_t s);
+int tq_dequant_small(const TqArgs& a, cudaStream_t s);
 
 }  // namespace fb

@@ -132,6 +132,83 @@ def test_out_of_range_slots_are_skipped_and_counted():
     assert packed.cpu().numpy().any()
 
 
+# ── small calls (decode steps): the few-vectors-per-CTA exact kernels ──
+
+@pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
+@pytest.mark.parametrize("T,H,d,bits", [(1, 8, 128, 4), (37, 8, 128, 4), (77, 8, 128, 3), (125, 8, 128, 2),
+                                        (9, 3, 64, 8), (5, 3, 33, 4), (40, 2, 192, 4)])
+def test_small_call_compress_bit_exact(dt, T, H, d, bits):
+    """Calls of up to 1024 head vectors (1, 2 or 4 vectors per CTA, the last CTA partial) into a
+    paged pool with an unaligned start and one missing block: pool bytes and norms bit-exact
+    against the oracle, tokens of the missing block untouched and counted once per vector."""
+    start = 3
+    x, raw = make_input(T, H, d, "f16" if dt == "f32" else dt, 900 + T * H + d)
+    if dt == "f32":
+        x = x.astype(np.float32) * np.float32(1.0 + 2.0 ** -13)  # values off the fp16 grid
+        raw = x
+    pi, c = tables(d, bits, 5 + d)
+    P = (d * bits + 7) // 8
+    nblk = (start + T + 15) // 16 + 2
+    table = np.random.default_rng(T).permutation(nblk).astype(np.int32)
+    missing = (start + T - 1) // 16 if T > 20 else -1
+    if missing >= 0:
+        table[missing] = -1
+    rows = nblk * 16
+    packed = torch.full((rows, H * P), 0xAB, dtype=torch.uint8, device=DEV)
+    norms = torch.full((rows, H), 0x5555, dtype=torch.int16, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    xin = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(DEV)
+    if dt != "f32":
+        xin = xin.to(TDT[dt])
+    K.tq_compress_paged(xin, torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed, norms,
+                        block_table=torch.from_numpy(table).to(DEV), start_pos=start, err=err)
+    torch.cuda.synchronize()
+    kind = {"f16": tq.INPUT_F16, "bf16": tq.INPUT_BF16, "f32": tq.INPUT_F32}[dt]
+    pc, nc, _ = tq.compress_c(raw, kind, pi, c, bits)
+    pos = start + np.arange(T)
+    have = table[pos // 16] >= 0
+    slots = table[pos // 16] * 16 + pos % 16
+    exp_p = np.full((rows, H * P), 0xAB, np.uint8)
+    exp_n = np.full((rows, H), 0x5555, np.uint16)
+    exp_p[slots[have]] = pc[have]
+    exp_n[slots[have]] = nc[have]
+    assert np.array_equal(packed.cpu().numpy(), exp_p)
+    assert np.array_equal(norms.cpu().numpy().view(np.uint16), exp_n)
+    assert err.item() == int((~have).sum()) * H
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
+@pytest.mark.parametrize("T,H,d,bits", [(1, 8, 128, 4), (24, 8, 128, 4), (19, 3, 64, 3), (7, 3, 33, 2)])
+def test_small_call_dequant_bit_exact(dt, T, H, d, bits):
+    """Calls of up to 192 head vectors take the exact small-call kernel: the float32 statement,
+    rounded once to the output type; a token whose block is missing gives zeros."""
+    start = 5
+    x, raw = make_input(T, H, d, "f16", 300 + T + d)
+    pi, c = tables(d, bits, 77)
+    P = (d * bits + 7) // 8
+    nblk = (start + T + 15) // 16
+    table = np.random.default_rng(d).permutation(nblk).astype(np.int32)
+    rows = nblk * 16
+    tt = torch.from_numpy(table).to(DEV)
+    tpi, tc = torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV)
+    packed = torch.zeros((rows, H * P), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((rows, H), dtype=torch.float16, device=DEV)
+    K.tq_compress_paged(dev(x, "f16"), tpi, tc, bits, packed, norms, block_table=tt, start_pos=start)
+    if T > 4:
+        tt[(start + T - 1) // 16] = -1
+    odt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[dt]
+    out = torch.full((T, H, d), 7.0, dtype=odt, device=DEV)
+    K.tq_dequant_paged(packed, norms, tpi, tc, bits, out, block_table=tt, start_pos=start)
+    torch.cuda.synchronize()
+    pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits)
+    ref = tq.decompress_c(pc, nc, pi, c, bits, H, d).reshape(T, H, d)
+    if T > 4:
+        pos = start + np.arange(T)
+        ref[pos // 16 == (start + T - 1) // 16] = 0.0
+    exp = torch.from_numpy(ref).to(odt).float().numpy()
+    assert np.array_equal(out.float().cpu().numpy(), exp)
+
+
 @pytest.mark.parametrize("bits,min_cos", [(4, 0.95), (2, 0.80), (8, 0.999)])
 def test_reference_gpu_roundtrip_thresholds(bits, min_cos):
     """turboquant_gpu.rs:87-430: head_dim 16, 2 heads, 4 tokens, rotation-matrix entries as data."""
