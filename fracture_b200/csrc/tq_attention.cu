@@ -1,0 +1,597 @@
+// Attention of query tokens over the TurboQuant-compressed paged KV cache, sm_100a.
+//
+// Replaces backends/fracture-cuda/kernels/attention_paged_tq.cu:56-309 (one CTA per query
+// token and Q head, the whole causal range in one CTA, every Q head of a GQA group re-reading
+// its KV head's codes). The math is the reference's (attention_paged_tq.cu:12-17): scores in
+// K's rotated space, (Pi_k q) . c_k[idx] * k_norm / sqrt(d); softmax over the causal range;
+// values accumulated in V's rotated space, sum p * c_v[idx] * v_norm, and rotated back once,
+// Pi_v^T acc. Here, in float32 throughout:
+//
+//   tqa_rotate_q    q_rot = Pi_k q for every query token and Q head (one warp per 32 rows
+//                   of Pi_k, lanes along the row), into the workspace
+//   tqa_chunk       one CTA per (256-position chunk, KV head, query token): thread p scores
+//                   position p for all Q heads of the group from the position's packed K
+//                   row (pair-of-codes lookup tables, lane-private), the CTA takes the
+//                   chunk's softmax maximum and sum, and then warp w accumulates its 32
+//                   positions' values (lane l: coordinates 4l..4l+3, every head of the
+//                   group) from the V rows staged in shared memory; the chunk's (max, sum,
+//                   acc) go to the workspace (split-K over the causal range)
+//   tqa_combine     rescales and sums the chunks of each query token and head, divides by
+//                   the softmax sum and rotates back with Pi_v^T (thread i: output i, column
+//                   i of Pi_v read once for the whole group)
+//
+// Each KV head's codes are read once per query token for its whole group of Q heads. A
+// position whose block-table entry is negative, or whose pool row is out of range, is left
+// out; a query token with no position gives zeros.
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "tq_common.cuh"
+
+namespace fb {
+
+namespace tqa {
+
+constexpr int D = 128;
+constexpr int CH = 256;       // positions per chunk: one per thread of tqa_chunk
+constexpr int THREADS = 256;
+constexpr int NWARPS = THREADS / 32;
+constexpr int MAXG = 8;
+constexpr int PART = D + 2;   // floats per chunk partial: max, sum, acc[D]
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+struct AttnArgs {
+    const void* q;
+    int dtype;  // of q and out: FB_FP16 or FB_BF16
+    int num_seqs, q_per_seq, hq, hkv;
+    const int32_t* block_tables;  // [num_seqs, max_blocks]
+    int max_blocks;
+    const int32_t* kv_lens;    // [num_seqs] (null: kv_len for every sequence)
+    const int32_t* start_pos;  // [num_seqs] (null: start for every sequence)
+    int kv_len, start;
+    const float* pik;
+    const float* piv;
+    const float* ck;
+    const float* cv;
+    float* qrot;  // [rows, hq, D]
+    float* part;  // [rows, hq, nch, PART]
+    int nch;
+    void* out;
+};
+
+// K/V rows in this library's contiguous pools: pool row = block * 16 + offset, head g at
+// g * P within it.
+struct PoolAddr {
+    const uint8_t* kp;
+    const __half* kn;
+    const uint8_t* vp;
+    const __half* vn;
+    int64_t pool_rows;
+    __device__ bool locate(int32_t blk, int off, int g, int hkv, int pk, int pv, const uint8_t*& krow,
+                           const uint8_t*& vrow, float& knorm, float& vnorm) const {
+        const int64_t row = (int64_t)blk * 16 + off;
+        if (row >= pool_rows) return false;
+        const int64_t hr = row * hkv + g;
+        krow = kp + hr * pk;
+        vrow = vp + hr * pv;
+        knorm = __half2float(kn[hr]);
+        vnorm = __half2float(vn[hr]);
+        return true;
+    }
+};
+
+// The reference's per-block tensors (attention_paged_tq.cu:123-129): block b's packed K rows
+// at kp[b] ([16, hkv * P]), its norms at kn[b] ([16, hkv]); the same for V.
+struct BlockPtrAddr {
+    const uint8_t* const* kp;
+    const __half* const* kn;
+    const uint8_t* const* vp;
+    const __half* const* vn;
+    __device__ bool locate(int32_t blk, int off, int g, int hkv, int pk, int pv, const uint8_t*& krow,
+                           const uint8_t*& vrow, float& knorm, float& vnorm) const {
+        const int hr = off * hkv + g;
+        krow = kp[blk] + hr * pk;
+        vrow = vp[blk] + hr * pv;
+        knorm = __half2float(kn[blk][hr]);
+        vnorm = __half2float(vn[blk][hr]);
+        return true;
+    }
+};
+
+__device__ __forceinline__ int causal_len(const AttnArgs& a, int s, int t) {
+    const int kv = a.kv_lens ? a.kv_lens[s] : a.kv_len;
+    const int st = a.start_pos ? a.start_pos[s] : a.start;
+    return max(0, min(st + t + 1, kv));
+}
+
+__device__ __forceinline__ float load_q(const AttnArgs& a, int64_t i) {
+    return a.dtype == FB_BF16 ? __bfloat162float(((const __nv_bfloat16*)a.q)[i]) : __half2float(((const __half*)a.q)[i]);
+}
+
+// q_rot[row][h][i] = sum_j Pi_k[i][j] q[row][h][j] for the heads of KV group blockIdx.y.
+__global__ void __launch_bounds__(128) tqa_rotate_q(AttnArgs a) {
+    __shared__ float qs[MAXG][D];
+    const int row = blockIdx.x, g = blockIdx.y, G = a.hq / a.hkv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = threadIdx.x; e < G * D; e += blockDim.x)
+        qs[e / D][e % D] = load_q(a, ((int64_t)row * a.hq + g * G) * D + e);
+    __syncthreads();
+    for (int i = warp; i < D; i += 4) {
+        const float4 p = __ldg((const float4*)(a.pik + i * D) + lane);
+        for (int h = 0; h < G; ++h) {
+            const float4 x = *(const float4*)&qs[h][4 * lane];
+            float v = p.x * x.x + p.y * x.y + p.z * x.z + p.w * x.w;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) a.qrot[((int64_t)row * a.hq + g * G + h) * D + i] = v;
+        }
+    }
+}
+
+// Decoding tables. Pair tables (2-, 3- and 4-bit codes): the 2*BITS bits of two adjacent
+// codes -> float2 (first code, second code), 16 copies side by side so a half-warp reads 16
+// different bank pairs. 8-bit codes: code -> float, 32 copies.
+template <int BITS>
+struct Lut {
+    static constexpr bool pair = BITS <= 4;
+    static constexpr int entries = pair ? (1 << (2 * BITS)) : 256;
+    static constexpr int copies = pair ? 16 : 32;
+    static constexpr int entry_bytes = pair ? 8 : 4;
+    static constexpr int bytes = entries * copies * entry_bytes;
+};
+
+template <int BITS>
+__device__ __forceinline__ void build_lut(uint8_t* lut, const float* cen) {
+    using L = Lut<BITS>;
+    for (int e = threadIdx.x; e < L::entries * L::copies; e += blockDim.x) {
+        const int ent = e / L::copies;
+        if constexpr (L::pair)
+            ((float2*)lut)[e] = make_float2(__ldg(cen + (ent >> BITS)), __ldg(cen + (ent & ((1 << BITS) - 1))));
+        else
+            ((float*)lut)[e] = __ldg(cen + ent);
+    }
+}
+
+template <int BITS>
+__device__ __forceinline__ float2 lut_pair(uint32_t lane_base, uint32_t idx) {
+    float2 v;
+    asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(lane_base + idx * (Lut<BITS>::copies * 8u)));
+    return v;
+}
+__device__ __forceinline__ float lut_one(uint32_t lane_base, uint32_t idx) {
+    float v;
+    asm("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(lane_base + idx * (32u * 4u)));
+    return v;
+}
+
+// Code pair m (coordinates 2m, 2m+1) of a row held as 32-bit little-endian words of its
+// MSB-first bit stream, as a table index (2-, 3-, 4-bit codes).
+template <int BITS>
+__device__ __forceinline__ uint32_t pair_index(const uint32_t* w, int m) {
+    if constexpr (BITS == 4) {
+        return (w[m >> 2] >> (8 * (m & 3))) & 0xffu;  // byte m
+    } else if constexpr (BITS == 2) {
+        const uint32_t byte = (w[m >> 3] >> (8 * ((m >> 1) & 3))) & 0xffu;  // byte m/2, high nibble first
+        return (m & 1) ? (byte & 15u) : (byte >> 4);
+    } else {
+        // 3-bit: 8 codes per 3 bytes; pair m is bits 18 - 6 (m & 3) of the big-endian 24-bit
+        // value of bytes 3c, 3c+1, 3c+2, c = m / 4
+        const int c = m >> 2, b0 = 3 * c;
+        const uint32_t x0 = (w[b0 >> 2] >> (8 * (b0 & 3))) & 0xffu;
+        const uint32_t x1 = (w[(b0 + 1) >> 2] >> (8 * ((b0 + 1) & 3))) & 0xffu;
+        const uint32_t x2 = (w[(b0 + 2) >> 2] >> (8 * ((b0 + 2) & 3))) & 0xffu;
+        const uint32_t v24 = (x0 << 16) | (x1 << 8) | x2;
+        return (v24 >> (18 - 6 * (m & 3))) & 63u;
+    }
+}
+
+template <int KB, int VB, int G>
+struct ChunkSmem {
+    static constexpr int PV = D * VB / 8;
+    static constexpr int qr_off = 0;                                   // [G][D] f32
+    static constexpr int lutk_off = qr_off + G * D * 4;
+    static constexpr int lutv_off = lutk_off + Lut<KB>::bytes;
+    static constexpr int vs_bytes = CH * PV > NWARPS * G * D * 4 ? CH * PV : NWARPS * G * D * 4;
+    static constexpr int vs_off = lutv_off + Lut<VB>::bytes;           // V rows, then the warps' acc
+    static constexpr int w_off = vs_off + vs_bytes;                    // [G][CH] f32 weights
+    static constexpr int red_off = w_off + G * CH * 4;                 // [NWARPS][G] f32
+    static constexpr int bytes = red_off + NWARPS * G * 4 + 16;
+};
+
+template <int KB, int VB, int G, typename Addr>
+__global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
+    using S = ChunkSmem<KB, VB, G>;
+    constexpr int PK = D * KB / 8, PV = D * VB / 8;
+    extern __shared__ __align__(16) uint8_t sm[];
+    float* qr = (float*)(sm + S::qr_off);
+    uint8_t* lutk = sm + S::lutk_off;
+    uint8_t* lutv = sm + S::lutv_off;
+    uint8_t* vs = sm + S::vs_off;
+    float* ws = (float*)(sm + S::w_off);
+    float* red = (float*)(sm + S::red_off);
+
+    const int row = blockIdx.z, g = blockIdx.y, c = blockIdx.x;
+    const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
+    const int L = causal_len(a, s, t);
+    const int p0 = c * CH;
+    if (p0 >= L) return;  // the whole CTA: chunk past the causal range
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    const int GA = a.hq / a.hkv;  // heads of the group (<= G; the others are computed on zeros)
+    build_lut<KB>(lutk, a.ck);
+    build_lut<VB>(lutv, a.cv);
+    for (int e = tid; e < G * D; e += THREADS) qr[e] = e < GA * D ? a.qrot[((int64_t)row * a.hq + g * GA) * D + e] : 0.0f;
+    __syncthreads();
+
+    // ── scores: thread tid takes position p0 + tid ──
+    const int p = p0 + tid;
+    bool valid = p < L && (p >> 4) < a.max_blocks;
+    const uint8_t* krow = nullptr;
+    const uint8_t* vrow = nullptr;
+    float knorm = 0.0f, vnorm = 0.0f;
+    if (valid) {
+        const int32_t blk = a.block_tables[(int64_t)s * a.max_blocks + (p >> 4)];
+        valid = blk >= 0 && ad.locate(blk, p & 15, g, a.hkv, PK, PV, krow, vrow, knorm, vnorm);
+    }
+    float sc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) sc[h] = 0.0f;
+    if (valid) {
+        uint32_t kw[PK / 4];
+#pragma unroll
+        for (int k = 0; k < PK / 16; ++k) {
+            const uint4 u = __ldg((const uint4*)krow + k);
+            kw[4 * k] = u.x;
+            kw[4 * k + 1] = u.y;
+            kw[4 * k + 2] = u.z;
+            kw[4 * k + 3] = u.w;
+        }
+#pragma unroll
+        for (int k = 0; k < PV / 16; ++k) ((uint4*)(vs + tid * PV))[k] = __ldg((const uint4*)vrow + k);
+        if constexpr (Lut<KB>::pair) {
+            const uint32_t lb = smem_addr(lutk) + (lane & 15) * 8u;
+#pragma unroll
+            for (int m = 0; m < D / 2; ++m) {  // unrolled: the code words stay in registers
+                const float2 cc = lut_pair<KB>(lb, pair_index<KB>(kw, m));
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float2 qq = *(const float2*)&qr[h * D + 2 * m];
+                    sc[h] = fmaf(qq.x, cc.x, sc[h]);
+                    sc[h] = fmaf(qq.y, cc.y, sc[h]);
+                }
+            }
+        } else {
+            const uint32_t lb = smem_addr(lutk) + lane * 4u;
+#pragma unroll
+            for (int j = 0; j < D; ++j) {
+                const float cc = lut_one(lb, (kw[j >> 2] >> (8 * (j & 3))) & 0xffu);
+#pragma unroll
+                for (int h = 0; h < G; ++h) sc[h] = fmaf(qr[h * D + j], cc, sc[h]);
+            }
+        }
+        const float f = knorm * rsqrtf((float)D);
+#pragma unroll
+        for (int h = 0; h < G; ++h) sc[h] *= f;
+    }
+
+    // ── softmax over the chunk: maximum, then weights exp(s - max) * v_norm and their sum ──
+    float mx[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        float v = valid ? sc[h] : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) red[warp * G + h] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        float v = red[h];
+        for (int w = 1; w < NWARPS; ++w) v = fmaxf(v, red[w * G + h]);
+        mx[h] = v;  // finite: the chunk holds at least position p0 < L, unless every block is missing
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        const float e = valid ? expf(sc[h] - mx[h]) : 0.0f;
+        ws[h * CH + tid] = e * vnorm;
+        float v = e;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[warp * G + h] = v;
+    }
+    __syncthreads();
+
+    // ── values: warp w takes its 32 positions, lane l coordinates 4l..4l+3 of every head ──
+    float acc[G][4];
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[h][k] = 0.0f;
+    {
+        const uint32_t lb = smem_addr(lutv) + (Lut<VB>::pair ? (lane & 15) * 8u : lane * 4u);
+        const int jn = min(32, L - (p0 + warp * 32));
+        for (int j = 0; j < jn; ++j) {
+            const int pl = warp * 32 + j;
+            const uint8_t* r = vs + pl * PV;
+            float v[4];
+            if constexpr (VB == 4) {
+                const uint32_t b2 = *(const uint16_t*)(r + 2 * lane);  // bytes 2l, 2l+1
+                const float2 a0 = lut_pair<4>(lb, b2 & 0xffu), a1 = lut_pair<4>(lb, b2 >> 8);
+                v[0] = a0.x; v[1] = a0.y; v[2] = a1.x; v[3] = a1.y;
+            } else if constexpr (VB == 2) {
+                const uint32_t byte = r[lane];
+                const float2 a0 = lut_pair<2>(lb, byte >> 4), a1 = lut_pair<2>(lb, byte & 15u);
+                v[0] = a0.x; v[1] = a0.y; v[2] = a1.x; v[3] = a1.y;
+            } else if constexpr (VB == 3) {
+                const int bit = 12 * lane, b = bit >> 3;
+                const uint32_t v16 = ((uint32_t)r[b] << 8) | r[b + 1];
+                const uint32_t v12 = (bit & 7) ? (v16 & 0xfffu) : (v16 >> 4);
+                const float2 a0 = lut_pair<3>(lb, v12 >> 6), a1 = lut_pair<3>(lb, v12 & 63u);
+                v[0] = a0.x; v[1] = a0.y; v[2] = a1.x; v[3] = a1.y;
+            } else {
+                const uint32_t w4 = *(const uint32_t*)(r + 4 * lane);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[k] = lut_one(lb, (w4 >> (8 * k)) & 0xffu);
+            }
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                const float wt = ws[h * CH + pl];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) acc[h][k] = fmaf(wt, v[k], acc[h][k]);
+            }
+        }
+    }
+    __syncthreads();  // every warp is done with the staged V rows
+    float* accs = (float*)vs;  // [NWARPS][G][D]
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+        *(float4*)&accs[(warp * G + h) * D + 4 * lane] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+    __syncthreads();
+    float* part = a.part + (((int64_t)row * a.hq + g * GA) * a.nch + c) * PART;
+    for (int e = tid; e < GA * D; e += THREADS) {
+        const int h = e / D, i = e - h * D;
+        float v = 0.0f;
+        for (int w = 0; w < NWARPS; ++w) v += accs[(w * G + h) * D + i];
+        part[(int64_t)h * a.nch * PART + 2 + i] = v;
+    }
+    if (tid < GA) {
+        float l = 0.0f;
+        for (int w = 0; w < NWARPS; ++w) l += red[w * G + tid];
+        float* ph = part + (int64_t)tid * a.nch * PART;
+        ph[0] = mx[tid];
+        ph[1] = l;
+    }
+}
+
+// out[row][h][i] = sum_j Pi_v[j][i] * (sum_c acc_c[j] e^(m_c - M)) / (sum_c l_c e^(m_c - M)).
+__global__ void __launch_bounds__(128) tqa_combine(AttnArgs a) {
+    __shared__ float accs[MAXG][D];
+    const int row = blockIdx.x, g = blockIdx.y, G = a.hq / a.hkv, i = threadIdx.x;
+    const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
+    const int L = causal_len(a, s, t);
+    const int nc = (L + CH - 1) / CH;
+    for (int h = 0; h < G; ++h) {
+        const float* ph = a.part + ((int64_t)row * a.hq + g * G + h) * a.nch * PART;
+        float M = -INFINITY;
+        for (int c = 0; c < nc; ++c) M = fmaxf(M, ph[c * PART]);
+        float l = 0.0f, v = 0.0f;
+        if (M > -INFINITY) {
+            for (int c = 0; c < nc; ++c) {
+                const float m = ph[c * PART];
+                if (m == -INFINITY) continue;
+                const float f = expf(m - M);
+                l = fmaf(ph[c * PART + 1], f, l);
+                v = fmaf(ph[c * PART + 2 + i], f, v);
+            }
+        }
+        accs[h][i] = l > 0.0f ? v / l : 0.0f;
+    }
+    __syncthreads();
+    float o[MAXG];
+    for (int h = 0; h < G; ++h) o[h] = 0.0f;
+    for (int j = 0; j < D; ++j) {
+        const float p = __ldg(a.piv + j * D + i);
+        for (int h = 0; h < G; ++h) o[h] = fmaf(p, accs[h][j], o[h]);
+    }
+    for (int h = 0; h < G; ++h) {
+        const int64_t e = ((int64_t)row * a.hq + g * G + h) * D + i;
+        if (a.dtype == FB_BF16) ((__nv_bfloat16*)a.out)[e] = __float2bfloat16_rn(o[h]);
+        else ((__half*)a.out)[e] = __float2half_rn(o[h]);
+    }
+}
+
+size_t workspace_bytes(int64_t rows, int hq, int nch) {
+    return (size_t)rows * hq * D * 4 + (size_t)rows * hq * nch * PART * 4;
+}
+
+template <int KB, int VB, int G, typename Addr>
+int launch_chunk(const AttnArgs& a, const Addr& ad, cudaStream_t s) {
+    constexpr int smem = ChunkSmem<KB, VB, G>::bytes;
+    auto kern = tqa_chunk<KB, VB, G, Addr>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return (int)e;
+    const int rows = a.num_seqs * a.q_per_seq;
+    kern<<<dim3(a.nch, a.hkv, rows), THREADS, smem, s>>>(a, ad);
+    return (int)cudaGetLastError();
+}
+
+template <int KB, int VB, typename Addr>
+int dispatch_g(const AttnArgs& a, const Addr& ad, cudaStream_t s) {
+    // groups of 1, 2 or 4 Q heads share the 4-head kernel
+    return a.hq / a.hkv <= 4 ? launch_chunk<KB, VB, 4>(a, ad, s) : launch_chunk<KB, VB, 8>(a, ad, s);
+}
+
+template <int KB, typename Addr>
+int dispatch_vb(const AttnArgs& a, int vb, const Addr& ad, cudaStream_t s) {
+    switch (vb) {
+        case 2: return dispatch_g<KB, 2>(a, ad, s);
+        case 3: return dispatch_g<KB, 3>(a, ad, s);
+        case 4: return dispatch_g<KB, 4>(a, ad, s);
+        default: return dispatch_g<KB, 8>(a, ad, s);
+    }
+}
+
+template <typename Addr>
+int run(const AttnArgs& a, int kb, int vb, const Addr& ad, cudaStream_t s) {
+    const int rows = a.num_seqs * a.q_per_seq;
+    if (rows == 0) return 0;
+    tqa_rotate_q<<<dim3(rows, a.hkv), 128, 0, s>>>(a);
+    int rc = (int)cudaGetLastError();
+    if (rc) return rc;
+    if (a.nch > 0) {
+        switch (kb) {
+            case 2: rc = dispatch_vb<2>(a, vb, ad, s); break;
+            case 3: rc = dispatch_vb<3>(a, vb, ad, s); break;
+            case 4: rc = dispatch_vb<4>(a, vb, ad, s); break;
+            default: rc = dispatch_vb<8>(a, vb, ad, s); break;
+        }
+        if (rc) return rc;
+    }
+    tqa_combine<<<dim3(rows, a.hkv), 128, 0, s>>>(a);
+    return (int)cudaGetLastError();
+}
+
+bool bits_ok(int b) { return b == 2 || b == 3 || b == 4 || b == 8; }
+
+bool shape_ok(int hq, int hkv, int head_dim) {
+    if (head_dim != D || hkv <= 0 || hq <= 0 || hq % hkv) return false;
+    const int G = hq / hkv;
+    return G == 1 || G == 2 || G == 4 || G == 8;
+}
+
+}  // namespace tqa
+
+void set_last_error(const char* msg);
+
+}  // namespace fb
+
+using namespace fb;
+
+extern "C" size_t fb_tq_attention_workspace_bytes(int num_seqs, int q_per_seq, int num_q_heads, int max_kv_len) {
+    if (num_seqs < 0 || q_per_seq < 0 || num_q_heads <= 0 || max_kv_len < 0) return 0;
+    const int nch = (max_kv_len + tqa::CH - 1) / tqa::CH;
+    return tqa::workspace_bytes((int64_t)num_seqs * q_per_seq, num_q_heads, nch);
+}
+
+extern "C" int fb_launch_tq_attention_paged(const void* q, int dtype, int num_seqs, int q_per_seq, int num_q_heads,
+                                            int num_kv_heads, int head_dim, const void* k_packed_pool,
+                                            const void* k_norms_pool, const void* v_packed_pool,
+                                            const void* v_norms_pool, int64_t num_pool_rows,
+                                            const int32_t* block_tables, int max_blocks_per_seq,
+                                            const int32_t* kv_lens, const int32_t* start_pos, int max_kv_len,
+                                            const float* k_rotation, const float* v_rotation,
+                                            const float* k_centroids, const float* v_centroids, int key_bits,
+                                            int value_bits, void* workspace, size_t workspace_bytes, void* output,
+                                            void* stream) {
+    if (dtype != FB_FP16 && dtype != FB_BF16) return (int)cudaErrorInvalidValue;
+    if (!tqa::shape_ok(num_q_heads, num_kv_heads, head_dim) || !tqa::bits_ok(key_bits) || !tqa::bits_ok(value_bits))
+        return (int)cudaErrorInvalidValue;
+    if (num_seqs < 0 || q_per_seq < 0 || max_blocks_per_seq < 0 || max_kv_len < 0 || num_pool_rows < 0)
+        return (int)cudaErrorInvalidValue;
+    if ((int64_t)num_seqs * q_per_seq == 0) return 0;
+    if (!q || !output || !k_rotation || !v_rotation || !k_centroids || !v_centroids || !kv_lens || !start_pos)
+        return (int)cudaErrorInvalidValue;
+    if (max_kv_len > 0 && (!block_tables || !k_packed_pool || !k_norms_pool || !v_packed_pool || !v_norms_pool))
+        return (int)cudaErrorInvalidValue;
+    if (!aligned16(k_packed_pool) || !aligned16(v_packed_pool) || !aligned16(k_rotation) || !aligned16(workspace))
+        return (int)cudaErrorInvalidValue;
+    const int nch = (max_kv_len + tqa::CH - 1) / tqa::CH;
+    const int64_t rows = (int64_t)num_seqs * q_per_seq;
+    if (rows > 65535 || nch > (1 << 30) || !workspace ||
+        workspace_bytes < tqa::workspace_bytes(rows, num_q_heads, nch)) {
+        set_last_error("fb_launch_tq_attention_paged: workspace missing or smaller than "
+                       "fb_tq_attention_workspace_bytes(), or more than 65535 query rows");
+        return (int)cudaErrorInvalidValue;
+    }
+    tqa::AttnArgs a{};
+    a.q = q;
+    a.dtype = dtype;
+    a.num_seqs = num_seqs;
+    a.q_per_seq = q_per_seq;
+    a.hq = num_q_heads;
+    a.hkv = num_kv_heads;
+    a.block_tables = block_tables;
+    a.max_blocks = max_blocks_per_seq;
+    a.kv_lens = kv_lens;
+    a.start_pos = start_pos;
+    a.pik = k_rotation;
+    a.piv = v_rotation;
+    a.ck = k_centroids;
+    a.cv = v_centroids;
+    a.qrot = (float*)workspace;
+    a.part = a.qrot + rows * num_q_heads * tqa::D;
+    a.nch = nch;
+    a.out = output;
+    tqa::PoolAddr ad{(const uint8_t*)k_packed_pool, (const __half*)k_norms_pool, (const uint8_t*)v_packed_pool,
+                     (const __half*)v_norms_pool, num_pool_rows};
+    return tqa::run(a, key_bits, value_bits, ad, (cudaStream_t)stream);
+}
+
+// The reference ABI (ffi.rs:251-274, attention_paged_tq.cu:261-309): one sequence, FP16, a
+// device block table and per-block pointer arrays. The workspace is this library's, one
+// per device, grown to the largest call and kept (calls on one device are serialised by it).
+extern "C" int launch_attention_paged_tq(void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
+                                         const void** k_norms_ptrs, const void** v_packed_ptrs,
+                                         const void** v_norms_ptrs, const float* k_rotation, const float* v_rotation,
+                                         const float* k_centroids, const float* v_centroids, int num_tokens,
+                                         int num_q_heads, int num_kv_heads, int head_dim, int kv_len, int start_pos,
+                                         int key_bits, int value_bits, int k_packed_dim_per_head,
+                                         int v_packed_dim_per_head, void* stream) {
+    if (!tqa::shape_ok(num_q_heads, num_kv_heads, head_dim) || !tqa::bits_ok(key_bits) || !tqa::bits_ok(value_bits))
+        return (int)cudaErrorInvalidValue;
+    if (k_packed_dim_per_head != (head_dim * key_bits + 7) / 8 ||
+        v_packed_dim_per_head != (head_dim * value_bits + 7) / 8)
+        return (int)cudaErrorInvalidValue;
+    if (num_tokens < 0 || kv_len < 0 || start_pos < 0 || num_tokens > 65535) return (int)cudaErrorInvalidValue;
+    if (num_tokens == 0) return 0;
+    if (!output || !q || !k_rotation || !v_rotation || !k_centroids || !v_centroids) return (int)cudaErrorInvalidValue;
+    if (kv_len > 0 && (!block_table || !k_packed_ptrs || !k_norms_ptrs || !v_packed_ptrs || !v_norms_ptrs))
+        return (int)cudaErrorInvalidValue;
+    const int nch = (kv_len + tqa::CH - 1) / tqa::CH;
+    const size_t need = tqa::workspace_bytes(num_tokens, num_q_heads, nch);
+    static void* ws[64];
+    static size_t cap[64];
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(mu);
+    if (cap[dev] < need) {
+        if (ws[dev]) {
+            e = cudaFree(ws[dev]);
+            if (e != cudaSuccess) return (int)e;
+        }
+        ws[dev] = nullptr;
+        cap[dev] = 0;
+        e = cudaMalloc(&ws[dev], need);
+        if (e != cudaSuccess) return (int)e;
+        cap[dev] = need;
+    }
+    tqa::AttnArgs a{};
+    a.q = q;
+    a.dtype = FB_FP16;
+    a.num_seqs = 1;
+    a.q_per_seq = num_tokens;
+    a.hq = num_q_heads;
+    a.hkv = num_kv_heads;
+    a.block_tables = block_table;
+    a.max_blocks = (kv_len + 15) / 16;
+    a.kv_len = kv_len;
+    a.start = start_pos;
+    a.pik = k_rotation;
+    a.piv = v_rotation;
+    a.ck = k_centroids;
+    a.cv = v_centroids;
+    a.qrot = (float*)ws[dev];
+    a.part = a.qrot + (int64_t)num_tokens * num_q_heads * tqa::D;
+    a.nch = nch;
+    a.out = output;
+    tqa::BlockPtrAddr ad{(const uint8_t* const*)k_packed_ptrs, (const __half* const*)k_norms_ptrs,
+                         (const uint8_t* const*)v_packed_ptrs, (const __half* const*)v_norms_ptrs};
+    return tqa::run(a, key_bits, value_bits, ad, (cudaStream_t)stream);
+}

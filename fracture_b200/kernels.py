@@ -105,6 +105,33 @@ def tq_dequant_slots(packed_pool, norms_pool, rotation, centroids, bits, out, sl
         slot_map.data_ptr(), rows, out.data_ptr(), _dt(out), _stream(stream)), "tq_dequant_slots")
 
 
+def tq_attention_workspace_bytes(num_seqs, q_per_seq, num_q_heads, max_kv_len) -> int:
+    return int(_lib.load().fb_tq_attention_workspace_bytes(num_seqs, q_per_seq, num_q_heads, max_kv_len))
+
+
+def tq_attention_paged(q, k_pool, k_norms, v_pool, v_norms, block_tables, kv_lens, start_pos, k_rotation,
+                       v_rotation, k_centroids, v_centroids, key_bits, value_bits, out, max_kv_len=None,
+                       workspace=None, stream=None):
+    """Attention of ``q [S, Tq, Hq, 128]`` over the compressed paged cache of S sequences.
+
+    ``block_tables [S, max_blocks]`` int32, ``kv_lens`` / ``start_pos`` ``[S]`` int32 (device);
+    pools as ``tq_compress_paged`` writes them (``[rows, Hkv * P]`` uint8, norms ``[rows, Hkv]``
+    fp16). ``out`` like ``q``. A workspace is allocated when none is given."""
+    S, Tq, Hq, d = q.shape
+    Hkv = k_norms.shape[1]
+    if max_kv_len is None:
+        max_kv_len = int(kv_lens.max().item()) if kv_lens.numel() else 0
+    need = tq_attention_workspace_bytes(S, Tq, Hq, max_kv_len)
+    if workspace is None:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+    _ok(_lib.load().fb_launch_tq_attention_paged(
+        q.data_ptr(), _dt(q), S, Tq, Hq, Hkv, d, k_pool.data_ptr(), k_norms.data_ptr(), v_pool.data_ptr(),
+        v_norms.data_ptr(), k_norms.shape[0], block_tables.data_ptr(), block_tables.shape[1], kv_lens.data_ptr(),
+        start_pos.data_ptr(), max_kv_len, k_rotation.data_ptr(), v_rotation.data_ptr(), k_centroids.data_ptr(),
+        v_centroids.data_ptr(), key_bits, value_bits, workspace.data_ptr(), workspace.numel(), out.data_ptr(),
+        _stream(stream)), "tq_attention_paged")
+
+
 # host tables -------------------------------------------------------------------
 
 def rope_freqs(head_dim: int, theta: float) -> np.ndarray:

@@ -76,6 +76,20 @@ int launch_turboquant_compress(const void* input, const float* rotation, const f
 int launch_turboquant_decompress(const void* packed_in, const void* norms_in, const float* rotation,
                                  const float* centroids, void* output, int num_tokens, int num_kv_heads,
                                  int head_dim, int bits, int packed_dim_per_head, void* stream);
+/* ffi.rs:251-274 (attention_paged_tq.cu:261-309): attention of num_tokens FP16 query tokens of one
+ * sequence over its TurboQuant-compressed paged cache; block_table (device int32) maps logical
+ * block pos/16 to a physical block whose packed K/V rows and norms sit at k_packed_ptrs[b],
+ * k_norms_ptrs[b], ... (device arrays of device pointers, [16, Hkv*P] and [16, Hkv]). Token t
+ * attends positions [0, min(start_pos + t + 1, kv_len)). head_dim 128, Hq/Hkv in {1, 2, 4, 8},
+ * 2/3/4/8-bit codes. Float32 throughout (the reference's math in another summation order: within
+ * FP16 rounding plus ~1e-6 of the output's magnitude). Uses a device workspace owned by this
+ * library, one per device, grown to the largest call. */
+int launch_attention_paged_tq(void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
+                              const void** k_norms_ptrs, const void** v_packed_ptrs, const void** v_norms_ptrs,
+                              const float* k_rotation, const float* v_rotation, const float* k_centroids,
+                              const float* v_centroids, int num_tokens, int num_q_heads, int num_kv_heads,
+                              int head_dim, int kv_len, int start_pos, int key_bits, int value_bits,
+                              int k_packed_dim_per_head, int v_packed_dim_per_head, void* stream);
 
 /* ======================================================================== */
 /* 2. New kernel entry points                                               */
@@ -161,6 +175,26 @@ int fb_launch_tq_dequant_slots(const void* packed_pool, const void* norms_pool, 
                                const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
                                int head_dim, const int64_t* slot_map, int64_t num_pool_rows, void* output,
                                int dtype, void* stream);
+
+/* TurboQuant paged attention over this library's pools, batched over sequences (no reference
+ * counterpart for the batching; the math is attention_paged_tq.cu:56-259, called per sequence
+ * from batched.rs:156-193). Queries [num_seqs * q_per_seq, Hq, 128] FP16/BF16 (`dtype`, also the
+ * output's), sequence-major; sequence s reads its blocks from block_tables[s * max_blocks_per_seq
+ * ...] (device int32; a negative entry leaves its 16 positions out) in the K/V pools laid out as
+ * fb_launch_tq_compress_paged writes them; query t of sequence s attends positions
+ * [0, min(start_pos[s] + t + 1, kv_lens[s])) (device int32 arrays; max_kv_len bounds kv_lens).
+ * Hq/Hkv in {1, 2, 4, 8}; key_bits/value_bits 2, 3, 4 or 8. `workspace` (16-byte aligned, at
+ * least fb_tq_attention_workspace_bytes(num_seqs, q_per_seq, num_q_heads, max_kv_len) bytes)
+ * holds the rotated queries and the per-256-position partial results. */
+size_t fb_tq_attention_workspace_bytes(int num_seqs, int q_per_seq, int num_q_heads, int max_kv_len);
+int fb_launch_tq_attention_paged(const void* q, int dtype, int num_seqs, int q_per_seq, int num_q_heads,
+                                 int num_kv_heads, int head_dim, const void* k_packed_pool, const void* k_norms_pool,
+                                 const void* v_packed_pool, const void* v_norms_pool, int64_t num_pool_rows,
+                                 const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
+                                 const int32_t* start_pos, int max_kv_len, const float* k_rotation,
+                                 const float* v_rotation, const float* k_centroids, const float* v_centroids,
+                                 int key_bits, int value_bits, void* workspace, size_t workspace_bytes, void* output,
+                                 void* stream);
 
 /* Number of bounded waits that timed out inside the tensor-core TurboQuant kernels (compress and
  * dequantize) since the library was loaded (0 in normal operation; a timeout abandons the launch's

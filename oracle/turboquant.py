@@ -532,3 +532,55 @@ class QuantizedKvCache:
         self.pool_norms[layer][0][rows] = k_norms
         self.pool_packed[layer][1][rows] = v_packed
         self.pool_norms[layer][1][rows] = v_norms
+
+
+# ── paged attention over the compressed cache ───────────────────────────────
+
+def attention_paged_tq(q: np.ndarray, k_packed: np.ndarray, k_norms: np.ndarray, v_packed: np.ndarray,
+                       v_norms: np.ndarray, block_table: np.ndarray, kv_len: int, start_pos: int,
+                       k_rotation: np.ndarray, v_rotation: np.ndarray, k_centroids: np.ndarray,
+                       v_centroids: np.ndarray, key_bits: int, value_bits: int, num_kv_heads: int) -> np.ndarray:
+    """The statement of ``attention_paged_tq_kernel`` (``backends/fracture-cuda/kernels/
+    attention_paged_tq.cu:56-280``) in float64, for one sequence.
+
+    ``q [N, Hq, d]`` (values); pools ``[rows, Hkv * P]`` uint8 with norms ``[rows, Hkv]`` (values)
+    addressed by ``block_table[pos // 16] * 16 + pos % 16``. Query token t attends positions
+    ``[0, min(start_pos + t + 1, kv_len))`` (``:86-87``); q head h reads KV head
+    ``h // (Hq / Hkv)`` (``:83-84``). Scores in K's rotated space,
+    ``(Pi_k q) . c_k[idx] * k_norm / sqrt(d)`` (``:102-140``); softmax (``:145-206``); values
+    accumulated in V's rotated space, ``sum p * c_v[idx] * v_norm``, then ``Pi_v^T @ acc``
+    (``:208-280``). A position whose block-table entry is negative is left out (the reference
+    has no such case). A query with no position gives zeros.
+    """
+    q = np.asarray(q, np.float64)
+    N, Hq, d = q.shape
+    G = Hq // num_kv_heads
+    Pk, Pv = (d * key_bits + 7) // 8, (d * value_bits + 7) // 8
+    kp = np.asarray(k_packed, np.uint8).reshape(-1, num_kv_heads, Pk)
+    vp = np.asarray(v_packed, np.uint8).reshape(-1, num_kv_heads, Pv)
+    kn = np.asarray(k_norms, np.float64).reshape(-1, num_kv_heads)
+    vn = np.asarray(v_norms, np.float64).reshape(-1, num_kv_heads)
+    pik, piv = np.asarray(k_rotation, np.float64), np.asarray(v_rotation, np.float64)
+    ck, cv = np.asarray(k_centroids, np.float64), np.asarray(v_centroids, np.float64)
+    table = np.asarray(block_table, np.int64)
+    out = np.zeros((N, Hq, d), np.float64)
+    scale = 1.0 / np.sqrt(d)
+    for t in range(N):
+        L = min(start_pos + t + 1, kv_len)
+        pos = np.arange(L)
+        blk = table[pos // 16]
+        keep = blk >= 0
+        rows = (blk * 16 + pos % 16)[keep]
+        for g in range(num_kv_heads):
+            if rows.size == 0:
+                continue
+            yk = ck[unpack_indices(kp[rows, g], key_bits, d)]      # [L', d]
+            yv = cv[unpack_indices(vp[rows, g], value_bits, d)]
+            for h in range(g * G, (g + 1) * G):
+                qr = pik @ q[t, h]
+                s = (yk @ qr) * kn[rows, g] * scale
+                p = np.exp(s - s.max())
+                p /= p.sum()
+                acc = (p * vn[rows, g]) @ yv
+                out[t, h] = piv.T @ acc
+    return out

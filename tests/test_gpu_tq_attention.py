@@ -1,0 +1,187 @@
+"""TurboQuant paged attention against the float64 statement of the reference kernel
+(``oracle.turboquant.attention_paged_tq``, ``attention_paged_tq.cu:56-259``) and against the
+reference kernel itself (``oracle/_ref``), on caches written by this library's compress.
+
+Bar (north star, FP16/BF16 outputs): max-abs error within 2e-3 of the output's magnitude
+beyond the output dtype's rounding, cosine >= 0.9999. Both entry points run the same float32
+kernels, so they agree bit for bit with each other.
+"""
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from fracture_b200 import _lib
+from fracture_b200 import kernels as K
+from oracle import ops, turboquant as tq
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+D = 128
+TDT = {"f16": torch.float16, "bf16": torch.bfloat16}
+REF_SO = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libfracture_ref_kernels.so"
+
+
+def build_cache(kv_lens, Hkv, kb, vb, seed):
+    """Pools shared by the sequences; sequence s owns ceil(kv_lens[s] / 16) shuffled blocks,
+    filled by fb_launch_tq_compress_paged with random keys and values."""
+    rng = np.random.default_rng(seed)
+    nblk = [(L + 15) // 16 for L in kv_lens]
+    total = sum(nblk) + 3
+    perm = rng.permutation(total).astype(np.int32)
+    max_blocks = max(nblk + [1])
+    tables = np.full((len(kv_lens), max_blocks), -1, np.int32)
+    k = 0
+    for s, n in enumerate(nblk):
+        tables[s, :n] = perm[k:k + n]
+        k += n
+    rows = total * 16
+    Pk, Pv = D * kb // 8, D * vb // 8
+    c = {"kp": torch.zeros((rows, Hkv * Pk), dtype=torch.uint8, device=DEV),
+         "vp": torch.zeros((rows, Hkv * Pv), dtype=torch.uint8, device=DEV),
+         "kn": torch.zeros((rows, Hkv), dtype=torch.float16, device=DEV),
+         "vn": torch.zeros((rows, Hkv), dtype=torch.float16, device=DEV)}
+    pik, piv = K.tq_rotation_matrix(D, seed), K.tq_rotation_matrix(D, seed + 500)
+    ck, cv = K.tq_codebook(D, kb)[0], K.tq_codebook(D, vb)[0]
+    dev = {n: torch.from_numpy(np.ascontiguousarray(x)).to(DEV) for n, x in
+           (("pik", pik), ("piv", piv), ("ck", ck), ("cv", cv))}
+    for s, L in enumerate(kv_lens):
+        if L == 0:
+            continue
+        kx = torch.from_numpy((rng.standard_normal((L, Hkv, D)) * 1.5).astype(np.float32)).to(DEV).half()
+        vx = torch.from_numpy(rng.standard_normal((L, Hkv, D)).astype(np.float32)).to(DEV).half()
+        bt = torch.from_numpy(tables[s]).to(DEV)
+        K.tq_compress_paged(kx, dev["pik"], dev["ck"], kb, c["kp"], c["kn"], block_table=bt)
+        K.tq_compress_paged(vx, dev["piv"], dev["cv"], vb, c["vp"], c["vn"], block_table=bt)
+    torch.cuda.synchronize()
+    c.update(dev)
+    c.update({"tables": tables, "pik_h": pik, "piv_h": piv, "ck_h": ck, "cv_h": cv, "kb": kb, "vb": vb,
+              "Hkv": Hkv})
+    return c
+
+
+def statement(c, q, s, kv_len, start):
+    """The oracle for sequence s (q: [Tq, Hq, D] values)."""
+    return tq.attention_paged_tq(q, c["kp"].cpu().numpy(), c["kn"].float().cpu().numpy(), c["vp"].cpu().numpy(),
+                                 c["vn"].float().cpu().numpy(), c["tables"][s], kv_len, start, c["pik_h"],
+                                 c["piv_h"], c["ck_h"], c["cv_h"], c["kb"], c["vb"], c["Hkv"])
+
+
+def run_ours(c, q, kv_lens, starts, dt):
+    S, Tq, Hq, _ = q.shape
+    out = torch.full(q.shape, 7.0, dtype=TDT[dt], device=DEV)
+    K.tq_attention_paged(q, c["kp"], c["kn"], c["vp"], c["vn"], torch.from_numpy(c["tables"]).to(DEV),
+                         torch.tensor(kv_lens, dtype=torch.int32, device=DEV),
+                         torch.tensor(starts, dtype=torch.int32, device=DEV), c["pik"], c["piv"], c["ck"], c["cv"],
+                         c["kb"], c["vb"], out)
+    torch.cuda.synchronize()
+    return out
+
+
+def make_q(S, Tq, Hq, dt, seed):
+    x = np.random.default_rng(seed).standard_normal((S, Tq, Hq, D)).astype(np.float32)
+    x = ops.round_to(x, dt)
+    return x, torch.from_numpy(x).to(DEV).to(TDT[dt])
+
+
+@pytest.mark.parametrize("G,kb,vb,dt", [(4, 4, 2, "f16"), (1, 4, 4, "f16"), (2, 3, 3, "bf16"), (8, 8, 8, "f16"),
+                                        (4, 2, 4, "bf16"), (8, 4, 2, "bf16")])
+def test_decode_matches_statement(G, kb, vb, dt):
+    """One query token per sequence at the end of its context (decode), contexts of 1 to 777
+    positions (one to four 256-position chunks), GQA groups of 1 to 8."""
+    Hkv = 2
+    kv_lens = [1, 300, 777]
+    c = build_cache(kv_lens, Hkv, kb, vb, seed=10 * G + kb)
+    qh, q = make_q(len(kv_lens), 1, G * Hkv, dt, seed=G + vb)
+    starts = [L - 1 for L in kv_lens]
+    got = run_ours(c, q, kv_lens, starts, dt).float().cpu().numpy()
+    for s, L in enumerate(kv_lens):
+        ref = statement(c, qh[s], s, L, starts[s])
+        ops.assert_close_fp(got[s], ref, rel=2e-3, min_cos=0.9999, label=f"seq {s} (kv {L})", dtype=dt)
+
+
+def test_prefill_chunk_causal():
+    """Seven query tokens per sequence appended at the end: token t sees start + t + 1 positions."""
+    kv_lens, Tq, Hkv, G = [40, 600], 7, 2, 4
+    c = build_cache(kv_lens, Hkv, 4, 2, seed=3)
+    qh, q = make_q(2, Tq, G * Hkv, "f16", seed=4)
+    starts = [L - Tq for L in kv_lens]
+    got = run_ours(c, q, kv_lens, starts, "f16").float().cpu().numpy()
+    for s, L in enumerate(kv_lens):
+        ops.assert_close_fp(got[s], statement(c, qh[s], s, L, starts[s]), rel=2e-3, min_cos=0.9999,
+                            label=f"seq {s}", dtype="f16")
+
+
+def test_missing_block_and_empty_sequence():
+    """A negative block-table entry leaves its 16 positions out; a sequence with no positions
+    gives zeros."""
+    kv_lens, Hkv, G = [0, 90, 513], 2, 4
+    c = build_cache(kv_lens, Hkv, 4, 2, seed=8)
+    c["tables"][2, 3] = -1
+    c["tables"][1, 0] = -1
+    qh, q = make_q(3, 1, G * Hkv, "f16", seed=9)
+    starts = [max(L - 1, 0) for L in kv_lens]
+    got = run_ours(c, q, kv_lens, starts, "f16").float().cpu().numpy()
+    assert not np.any(got[0])
+    for s in (1, 2):
+        ops.assert_close_fp(got[s], statement(c, qh[s], s, kv_lens[s], starts[s]), rel=2e-3, min_cos=0.9999,
+                            label=f"seq {s}", dtype="f16")
+
+
+def _block_pointer_arrays(c, nblocks):
+    Hkv = c["Hkv"]
+    Pk, Pv = D * c["kb"] // 8, D * c["vb"] // 8
+    arr = lambda base, stride: torch.tensor([base + b * 16 * stride for b in range(nblocks)], dtype=torch.int64,
+                                            device=DEV)
+    return (arr(c["kp"].data_ptr(), Hkv * Pk), arr(c["kn"].data_ptr(), Hkv * 2), arr(c["vp"].data_ptr(), Hkv * Pv),
+            arr(c["vn"].data_ptr(), Hkv * 2))
+
+
+def _reference_abi_call(lib, c, q, kv_len, start):
+    Tq, Hq, _ = q.shape
+    nblocks = int(c["tables"].max()) + 1
+    kp, kn, vp, vn = _block_pointer_arrays(c, nblocks)
+    bt = torch.from_numpy(np.ascontiguousarray(c["tables"][0])).to(DEV)
+    out = torch.full((Tq, Hq, D), 7.0, dtype=torch.float16, device=DEV)
+    Pk, Pv = D * c["kb"] // 8, D * c["vb"] // 8
+    rc = lib.launch_attention_paged_tq(out.data_ptr(), q.data_ptr(), bt.data_ptr(), kp.data_ptr(), kn.data_ptr(),
+                                       vp.data_ptr(), vn.data_ptr(), c["pik"].data_ptr(), c["piv"].data_ptr(),
+                                       c["ck"].data_ptr(), c["cv"].data_ptr(), Tq, Hq, c["Hkv"], D, kv_len, start,
+                                       c["kb"], c["vb"], Pk, Pv, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == 0
+    return out
+
+
+@pytest.mark.parametrize("kb,vb", [(4, 2), (8, 8), (2, 4)])
+def test_reference_abi_equals_batched_entry(kb, vb):
+    """launch_attention_paged_tq (per-block pointer arrays, ffi.rs:251-274) gives the batched entry
+    point's result bit for bit, and both meet the bar against the statement."""
+    kv_len, Tq, Hkv, G = 700, 3, 2, 4
+    c = build_cache([kv_len], Hkv, kb, vb, seed=20 + kb)
+    qh, q = make_q(1, Tq, G * Hkv, "f16", seed=21)
+    ours = run_ours(c, q, [kv_len], [kv_len - Tq], "f16")
+    abi = _reference_abi_call(_lib.load(), c, q[0], kv_len, kv_len - Tq)
+    assert torch.equal(abi, ours[0])
+    ops.assert_close_fp(abi.float().cpu().numpy(), statement(c, qh[0], 0, kv_len, kv_len - Tq), rel=2e-3,
+                        min_cos=0.9999, label="reference ABI", dtype="f16")
+
+
+@pytest.mark.parametrize("kb,vb", [(4, 2), (4, 4), (2, 2), (8, 8)])
+def test_reference_kernel_meets_the_bar_against_the_statement(kb, vb):
+    """The reference's own kernel (oracle/_ref, fast-math) on the same cache and queries: within
+    the bar of the float64 statement, which pins the oracle to the reference implementation."""
+    if not REF_SO.exists():
+        pytest.skip("oracle/_ref not built (make -C oracle ref needs the reference sources)")
+    ref = C.CDLL(str(REF_SO))
+    ref.launch_attention_paged_tq.argtypes = [C.c_void_p] * 11 + [C.c_int] * 10 + [C.c_void_p]
+    ref.launch_attention_paged_tq.restype = C.c_int
+    kv_len, Tq, Hkv, G = 400, 2, 2, 4
+    c = build_cache([kv_len], Hkv, kb, vb, seed=40 + kb + vb)
+    qh, q = make_q(1, Tq, G * Hkv, "f16", seed=41)
+    got = _reference_abi_call(ref, c, q[0], kv_len, kv_len - Tq).float().cpu().numpy()
+    ops.assert_close_fp(got, statement(c, qh[0], 0, kv_len, kv_len - Tq), rel=2e-3, min_cos=0.9999,
+                        label="reference kernel", dtype="f16")

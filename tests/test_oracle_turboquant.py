@@ -269,3 +269,45 @@ def test_paged_cache_block_accounting():
     assert c.free_list[-2:] == [0, 2]
     d_ = c.alloc()
     assert c.seqs[d_].block_table == [2]
+
+
+def test_attention_statement_equals_dense_attention_over_the_dequantized_cache():
+    """Scores in K's rotated space and values accumulated in V's rotated space
+    (attention_paged_tq.cu:12-17) equal plain causal attention over the dequantized keys and
+    values, Pi^T c[idx] * norm, to float64 rounding; a missing block drops its positions."""
+    rng = np.random.default_rng(0)
+    d, Hkv, Hq, T = 128, 2, 4, 40
+    c = np.asarray(tq.get_codebook(d, 4).centroids, np.float32)
+    c2 = np.asarray(tq.get_codebook(d, 2).centroids, np.float32)
+    pik, piv = tq.generate_rotation_matrix(d, 1), tq.generate_rotation_matrix(d, 2)
+    x = rng.standard_normal((T, Hkv, d)).astype(np.float32)
+    pk, nk, _, _ = tq.compress(x, pik, c, 4)
+    pv, nv, _, _ = tq.compress(x * 0.5 + 1, piv, c2, 2)
+    table = np.array([2, 0, 1], np.int32)
+    rows = 48
+    KP = np.zeros((rows, Hkv * 64), np.uint8)
+    VP = np.zeros((rows, Hkv * 32), np.uint8)
+    KN, VN = np.zeros((rows, Hkv)), np.zeros((rows, Hkv))
+    pos = np.arange(T)
+    sl = table[pos // 16] * 16 + pos % 16
+    KP[sl], VP[sl], KN[sl], VN[sl] = pk, pv, nk, nv
+    q = rng.standard_normal((3, Hq, d))
+    dk = np.stack([(c[tq.unpack_indices(pk.reshape(T, Hkv, 64)[:, g], 4, d)] @ pik.astype(np.float64))
+                   * nk[:, g, None] for g in range(Hkv)], 1)
+    dv = np.stack([(c2[tq.unpack_indices(pv.reshape(T, Hkv, 32)[:, g], 2, d)] @ piv.astype(np.float64))
+                   * nv[:, g, None] for g in range(Hkv)], 1)
+    for missing in (None, 1):
+        tab = table.copy()
+        if missing is not None:
+            tab[missing] = -1
+        got = tq.attention_paged_tq(q, KP, KN, VP, VN, tab, T, T - 3, pik, piv, c, c2, 4, 2, Hkv)
+        keep = np.ones(T, bool) if missing is None else (pos // 16 != missing)
+        for t in range(3):
+            L = T - 3 + t + 1
+            m = keep[:L]
+            for h in range(Hq):
+                g = h // 2
+                s = dk[:L][m, g] @ q[t, h] / np.sqrt(d)
+                p = np.exp(s - s.max())
+                p /= p.sum()
+                assert np.abs(got[t, h] - p @ dv[:L][m, g]).max() < 1e-12
