@@ -671,6 +671,68 @@ def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
             "bound": "hbm", **res}
 
 
+def run_tq_attention(args, local_rank: int) -> dict:
+    """Decode attention over the TurboQuant cache (the consumer of config 4's format): 64
+    sequences, one query token each at the end of an 8192-token context, Llama-3.1-8B heads
+    (32 Q / 8 KV x 128), keys 4-bit and values 2-bit (the reference's default TurboQuantConfig,
+    turboquant.rs:20-30), random block tables over one shared pool. One step = one
+    fb_launch_tq_attention_paged call for all 64 sequences. The cache (420 MB) is larger than
+    L2, so no flush is needed."""
+    import torch
+
+    from fracture_b200 import kernels as K
+
+    dev = torch.device("cuda", local_rank)
+    S, L, HQ, HKV, D, KB, VB = 64, 8192, NQ, NKV, HD, 4, 2
+    nblk = L // 16
+    g = torch.Generator(device=dev).manual_seed(7)
+    rows = S * L
+    kp = torch.empty((rows, HKV * D * KB // 8), dtype=torch.uint8, device=dev)
+    vp = torch.empty((rows, HKV * D * VB // 8), dtype=torch.uint8, device=dev)
+    kn = torch.empty((rows, HKV), dtype=torch.float16, device=dev)
+    vn = torch.empty((rows, HKV), dtype=torch.float16, device=dev)
+    tables = torch.randperm(S * nblk, generator=g, device=dev).to(torch.int32).view(S, nblk)
+    pik, piv = (torch.from_numpy(K.tq_rotation_matrix(D, sd)).to(dev) for sd in (42, 542))
+    ck, cv = (torch.from_numpy(K.tq_codebook(D, b)[0]).to(dev) for b in (KB, VB))
+    for s in range(S):  # fill the cache through the compress kernels
+        x = torch.randn((L, HKV, D), generator=g, device=dev).half()
+        K.tq_compress_paged(x, pik, ck, KB, kp, kn, block_table=tables[s])
+        K.tq_compress_paged(x, piv, cv, VB, vp, vn, block_table=tables[s])
+    q = torch.randn((S, 1, HQ, D), generator=g, device=dev).half()
+    out = torch.empty_like(q)
+    kv_lens = torch.full((S,), L, dtype=torch.int32, device=dev)
+    starts = torch.full((S,), L - 1, dtype=torch.int32, device=dev)
+    ws = torch.empty(K.tq_attention_workspace_bytes(S, 1, HQ, L), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        K.tq_attention_paged(q, kp, kn, vp, vn, tables, kv_lens, starts, pik, piv, ck, cv, KB, VB, out,
+                             max_kv_len=L, workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for e0, e1 in ev:
+        e0.record(stream)
+        step()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / args.steps
+    kv_bytes = S * L * HKV * (D * KB // 8 + 2 + D * VB // 8 + 2)
+    by = kv_bytes + 2 * S * HQ * D * 2 + S * nblk * 4 + 2 * D * D * 4
+    gbs = by / (ms / 1e3) / 1e9
+    pk = peaks()
+    return {"workload": "TurboQuant paged attention (decode): 64 sequences x 1 query token, context 8192, "
+                        "32 Q / 8 KV heads x 128, K 4-bit / V 2-bit, FP16 queries and output",
+            "kernels": "tqa_rotate_q + tqa_chunk (256-position split-K) + tqa_combine, CUDA cores, float32",
+            "ms_per_step": round(ms, 4), "query_tokens_per_s": round(S / (ms / 1e3), 1),
+            "kv_positions_per_s": round(S * L / (ms / 1e3), 1), "algorithmic_bytes_per_step": by,
+            "achieved_gbs": round(gbs, 1), "frac_of_peak": round(gbs / pk["hbm_gbs"], 4),
+            "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"],
+            "l2": "the 420 MB cache is larger than L2 (no flush)"}
+
+
 def cpu_baseline(tokens: int, layers: int, reps: int) -> dict:
     import torch
 
@@ -722,6 +784,11 @@ def profile_kernel(args) -> None:
     import torch
 
     from fracture_b200 import kernels as K
+
+    if args.profile_kernel == "tq_attention":  # the bench's attention workload, W warm-up steps + 1
+        args.steps = 1
+        print(json.dumps({"kernel": "tq_attention", "ms": run_tq_attention(args, 0)["ms_per_step"]}))
+        return
 
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(7)
@@ -788,10 +855,11 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
     ap.add_argument("--no-tq", action="store_true", help="skip the config-4 TurboQuant measurement")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode-shaped measurement")
+    ap.add_argument("--no-attention", action="store_true", help="skip the TurboQuant paged-attention measurement")
     ap.add_argument("--pipeline", action="store_true",
                     help="also run config 5 (70B-shaped pipeline over the ranks, NCCL stage handoff)")
     ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding", "tq_compress",
-                                                                   "tq_dequant"],
+                                                                   "tq_dequant", "tq_attention"],
                     help="run only this kernel at its config-3 size (W warm-up launches + 1), for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -829,6 +897,8 @@ def main() -> None:
         res["pipeline_config5"] = c5
     if res is not None and world == 1 and not args.no_decode:
         res["decode_config2"] = run_config2(args, local_rank)
+    if res is not None and world == 1 and not args.no_attention:
+        res["tq_attention"] = run_tq_attention(args, local_rank)
     if res is not None:
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(tokens=2048, layers=16, reps=3)

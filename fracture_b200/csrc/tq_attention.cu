@@ -119,14 +119,20 @@ __global__ void __launch_bounds__(128) tqa_rotate_q(AttnArgs a) {
     for (int e = threadIdx.x; e < G * D; e += blockDim.x)
         qs[e / D][e % D] = load_q(a, ((int64_t)row * a.hq + g * G) * D + e);
     __syncthreads();
-    for (int i = warp; i < D; i += 4) {
-        const float4 p = __ldg((const float4*)(a.pik + i * D) + lane);
+    // warp w: rows w, w + 4, ...; eight rows' loads in flight at a time
+    for (int i0 = warp; i0 < D; i0 += 32) {
+        float4 p[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) p[k] = __ldg((const float4*)(a.pik + (i0 + 4 * k) * D) + lane);
         for (int h = 0; h < G; ++h) {
             const float4 x = *(const float4*)&qs[h][4 * lane];
-            float v = p.x * x.x + p.y * x.y + p.z * x.z + p.w * x.w;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) a.qrot[((int64_t)row * a.hq + g * G + h) * D + i] = v;
+            for (int k = 0; k < 8; ++k) {
+                float v = p[k].x * x.x + p[k].y * x.y + p[k].z * x.z + p[k].w * x.w;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0) a.qrot[((int64_t)row * a.hq + g * G + h) * D + i0 + 4 * k] = v;
+            }
         }
     }
 }
@@ -143,15 +149,24 @@ struct Lut {
     static constexpr int bytes = entries * copies * entry_bytes;
 };
 
+// One thread per entry writes its 128 bytes of copies as eight 16-byte stores, starting at a
+// thread-dependent chunk so a quarter-warp's stores fall in eight different bank groups.
 template <int BITS>
 __device__ __forceinline__ void build_lut(uint8_t* lut, const float* cen) {
     using L = Lut<BITS>;
-    for (int e = threadIdx.x; e < L::entries * L::copies; e += blockDim.x) {
-        const int ent = e / L::copies;
-        if constexpr (L::pair)
-            ((float2*)lut)[e] = make_float2(__ldg(cen + (ent >> BITS)), __ldg(cen + (ent & ((1 << BITS) - 1))));
-        else
-            ((float*)lut)[e] = __ldg(cen + ent);
+    static_assert(L::copies * L::entry_bytes == 128, "one 128-byte row of copies per entry");
+    for (int ent = threadIdx.x; ent < L::entries; ent += blockDim.x) {
+        float4 v;
+        if constexpr (L::pair) {
+            const float a = __ldg(cen + (ent >> BITS)), b = __ldg(cen + (ent & ((1 << BITS) - 1)));
+            v = make_float4(a, b, a, b);
+        } else {
+            const float a = __ldg(cen + ent);
+            v = make_float4(a, a, a, a);
+        }
+        float4* row = (float4*)(lut + ent * 128);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) row[(k + threadIdx.x) & 7] = v;
     }
 }
 
@@ -192,11 +207,12 @@ template <int KB, int VB, int G>
 struct ChunkSmem {
     static constexpr int PV = D * VB / 8;
     static constexpr int qr_off = 0;                                   // [G][D] f32
-    static constexpr int lutk_off = qr_off + G * D * 4;
-    static constexpr int lutv_off = lutk_off + Lut<KB>::bytes;
-    static constexpr int vs_bytes = CH * PV > NWARPS * G * D * 4 ? CH * PV : NWARPS * G * D * 4;
-    static constexpr int vs_off = lutv_off + Lut<VB>::bytes;           // V rows, then the warps' acc
-    static constexpr int w_off = vs_off + vs_bytes;                    // [G][CH] f32 weights
+    static constexpr int lutk_off = qr_off + G * D * 4;  // K table, then the warps' sums [NWARPS][G][D]
+    static constexpr int lutk_bytes = Lut<KB>::bytes > NWARPS * G * D * 4 ? Lut<KB>::bytes : NWARPS * G * D * 4;
+    static constexpr int lutv_off = lutk_off + lutk_bytes;
+    static constexpr int vs_bytes = CH * PV;
+    static constexpr int vs_off = lutv_off + Lut<VB>::bytes;           // V rows of the chunk
+    static constexpr int w_off = vs_off + vs_bytes;                    // [CH][G] f32 weights
     static constexpr int red_off = w_off + G * CH * 4;                 // [NWARPS][G] f32
     static constexpr int bytes = red_off + NWARPS * G * 4 + 16;
 };
@@ -211,6 +227,7 @@ __global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
     uint8_t* lutv = sm + S::lutv_off;
     uint8_t* vs = sm + S::vs_off;
     float* ws = (float*)(sm + S::w_off);
+    static_assert(G % 4 == 0, "weights are read four heads at a time");
     float* red = (float*)(sm + S::red_off);
 
     const int row = blockIdx.z, g = blockIdx.y, c = blockIdx.x;
@@ -252,25 +269,39 @@ __global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
 #pragma unroll
         for (int k = 0; k < PV / 16; ++k) ((uint4*)(vs + tid * PV))[k] = __ldg((const uint4*)vrow + k);
         if constexpr (Lut<KB>::pair) {
+            // two running sums per head (even and odd coordinates) in one packed register pair:
+            // one two-wide FMA per code pair and head; q_rot four coordinates per load
             const uint32_t lb = smem_addr(lutk) + (lane & 15) * 8u;
+            float2 s2[G];
 #pragma unroll
-            for (int m = 0; m < D / 2; ++m) {  // unrolled: the code words stay in registers
-                const float2 cc = lut_pair<KB>(lb, pair_index<KB>(kw, m));
+            for (int h = 0; h < G; ++h) s2[h] = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int m = 0; m < D / 2; m += 2) {  // unrolled: the code words stay in registers
+                const float2 c0 = lut_pair<KB>(lb, pair_index<KB>(kw, m));
+                const float2 c1 = lut_pair<KB>(lb, pair_index<KB>(kw, m + 1));
 #pragma unroll
                 for (int h = 0; h < G; ++h) {
-                    const float2 qq = *(const float2*)&qr[h * D + 2 * m];
-                    sc[h] = fmaf(qq.x, cc.x, sc[h]);
-                    sc[h] = fmaf(qq.y, cc.y, sc[h]);
+                    const float4 qq = *(const float4*)&qr[h * D + 2 * m];
+                    s2[h] = __ffma2_rn(make_float2(qq.x, qq.y), c0, s2[h]);
+                    s2[h] = __ffma2_rn(make_float2(qq.z, qq.w), c1, s2[h]);
                 }
             }
+#pragma unroll
+            for (int h = 0; h < G; ++h) sc[h] = s2[h].x + s2[h].y;
         } else {
             const uint32_t lb = smem_addr(lutk) + lane * 4u;
+            float2 s2[G];
 #pragma unroll
-            for (int j = 0; j < D; ++j) {
-                const float cc = lut_one(lb, (kw[j >> 2] >> (8 * (j & 3))) & 0xffu);
+            for (int h = 0; h < G; ++h) s2[h] = make_float2(0.0f, 0.0f);
 #pragma unroll
-                for (int h = 0; h < G; ++h) sc[h] = fmaf(qr[h * D + j], cc, sc[h]);
+            for (int j = 0; j < D; j += 2) {
+                const float2 cc = make_float2(lut_one(lb, (kw[j >> 2] >> (8 * (j & 3))) & 0xffu),
+                                              lut_one(lb, (kw[j >> 2] >> (8 * ((j + 1) & 3))) & 0xffu));
+#pragma unroll
+                for (int h = 0; h < G; ++h) s2[h] = __ffma2_rn(*(const float2*)&qr[h * D + j], cc, s2[h]);
             }
+#pragma unroll
+            for (int h = 0; h < G; ++h) sc[h] = s2[h].x + s2[h].y;
         }
         const float f = knorm * rsqrtf((float)D);
 #pragma unroll
@@ -297,7 +328,7 @@ __global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
 #pragma unroll
     for (int h = 0; h < G; ++h) {
         const float e = valid ? expf(sc[h] - mx[h]) : 0.0f;
-        ws[h * CH + tid] = e * vnorm;
+        ws[tid * G + h] = e * vnorm;
         float v = e;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -306,50 +337,55 @@ __global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
     __syncthreads();
 
     // ── values: warp w takes its 32 positions, lane l coordinates 4l..4l+3 of every head ──
-    float acc[G][4];
+    float2 acc[G][2];  // coordinates (4l, 4l+1) and (4l+2, 4l+3) of each head
 #pragma unroll
-    for (int h = 0; h < G; ++h)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) acc[h][k] = 0.0f;
+    for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = make_float2(0.0f, 0.0f);
     {
         const uint32_t lb = smem_addr(lutv) + (Lut<VB>::pair ? (lane & 15) * 8u : lane * 4u);
         const int jn = min(32, L - (p0 + warp * 32));
         for (int j = 0; j < jn; ++j) {
             const int pl = warp * 32 + j;
             const uint8_t* r = vs + pl * PV;
-            float v[4];
+            float2 a0, a1;  // values of coordinates (4l, 4l+1) and (4l+2, 4l+3)
             if constexpr (VB == 4) {
                 const uint32_t b2 = *(const uint16_t*)(r + 2 * lane);  // bytes 2l, 2l+1
-                const float2 a0 = lut_pair<4>(lb, b2 & 0xffu), a1 = lut_pair<4>(lb, b2 >> 8);
-                v[0] = a0.x; v[1] = a0.y; v[2] = a1.x; v[3] = a1.y;
+                a0 = lut_pair<4>(lb, b2 & 0xffu);
+                a1 = lut_pair<4>(lb, b2 >> 8);
             } else if constexpr (VB == 2) {
                 const uint32_t byte = r[lane];
-                const float2 a0 = lut_pair<2>(lb, byte >> 4), a1 = lut_pair<2>(lb, byte & 15u);
-                v[0] = a0.x; v[1] = a0.y; v[2] = a1.x; v[3] = a1.y;
+                a0 = lut_pair<2>(lb, byte >> 4);
+                a1 = lut_pair<2>(lb, byte & 15u);
             } else if constexpr (VB == 3) {
                 const int bit = 12 * lane, b = bit >> 3;
                 const uint32_t v16 = ((uint32_t)r[b] << 8) | r[b + 1];
                 const uint32_t v12 = (bit & 7) ? (v16 & 0xfffu) : (v16 >> 4);
-                const float2 a0 = lut_pair<3>(lb, v12 >> 6), a1 = lut_pair<3>(lb, v12 & 63u);
-                v[0] = a0.x; v[1] = a0.y; v[2] = a1.x; v[3] = a1.y;
+                a0 = lut_pair<3>(lb, v12 >> 6);
+                a1 = lut_pair<3>(lb, v12 & 63u);
             } else {
                 const uint32_t w4 = *(const uint32_t*)(r + 4 * lane);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) v[k] = lut_one(lb, (w4 >> (8 * k)) & 0xffu);
+                a0 = make_float2(lut_one(lb, w4 & 0xffu), lut_one(lb, (w4 >> 8) & 0xffu));
+                a1 = make_float2(lut_one(lb, (w4 >> 16) & 0xffu), lut_one(lb, w4 >> 24));
             }
+            const float* wp = ws + pl * G;  // this position's weights, G consecutive floats
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
-                const float wt = ws[h * CH + pl];
+            for (int h4 = 0; h4 < G; h4 += 4) {
+                const float4 w4 = *(const float4*)(wp + h4);
+                const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-                for (int k = 0; k < 4; ++k) acc[h][k] = fmaf(wt, v[k], acc[h][k]);
+                for (int k = 0; k < 4; ++k) {
+                    const float2 w2 = make_float2(wv[k], wv[k]);
+                    acc[h4 + k][0] = __ffma2_rn(w2, a0, acc[h4 + k][0]);
+                    acc[h4 + k][1] = __ffma2_rn(w2, a1, acc[h4 + k][1]);
+                }
             }
         }
     }
-    __syncthreads();  // every warp is done with the staged V rows
-    float* accs = (float*)vs;  // [NWARPS][G][D]
+    // the warps' sums, added in warp order (the K table is no longer read: several barriers
+    // separate its last use from here)
+    float* accs = (float*)lutk;
 #pragma unroll
     for (int h = 0; h < G; ++h)
-        *(float4*)&accs[(warp * G + h) * D + 4 * lane] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+        *(float4*)&accs[(warp * G + h) * D + 4 * lane] = make_float4(acc[h][0].x, acc[h][0].y, acc[h][1].x, acc[h][1].y);
     __syncthreads();
     float* part = a.part + (((int64_t)row * a.hq + g * GA) * a.nch + c) * PART;
     for (int e = tid; e < GA * D; e += THREADS) {
@@ -377,9 +413,11 @@ __global__ void __launch_bounds__(128) tqa_combine(AttnArgs a) {
     for (int h = 0; h < G; ++h) {
         const float* ph = a.part + ((int64_t)row * a.hq + g * G + h) * a.nch * PART;
         float M = -INFINITY;
+#pragma unroll 8
         for (int c = 0; c < nc; ++c) M = fmaxf(M, ph[c * PART]);
         float l = 0.0f, v = 0.0f;
         if (M > -INFINITY) {
+#pragma unroll 4
             for (int c = 0; c < nc; ++c) {
                 const float m = ph[c * PART];
                 if (m == -INFINITY) continue;
@@ -393,9 +431,13 @@ __global__ void __launch_bounds__(128) tqa_combine(AttnArgs a) {
     __syncthreads();
     float o[MAXG];
     for (int h = 0; h < G; ++h) o[h] = 0.0f;
-    for (int j = 0; j < D; ++j) {
-        const float p = __ldg(a.piv + j * D + i);
-        for (int h = 0; h < G; ++h) o[h] = fmaf(p, accs[h][j], o[h]);
+    for (int j0 = 0; j0 < D; j0 += 16) {  // sixteen loads of column i in flight at a time
+        float p[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) p[k] = __ldg(a.piv + (j0 + k) * D + i);
+        for (int h = 0; h < G; ++h)
+#pragma unroll
+            for (int k = 0; k < 16; ++k) o[h] = fmaf(p[k], accs[h][j0 + k], o[h]);
     }
     for (int h = 0; h < G; ++h) {
         const int64_t e = ((int64_t)row * a.hq + g * G + h) * D + i;
