@@ -104,6 +104,7 @@ SIGNATURES = {
     "fb_tq_cache_pool": (i32, [vp, szt, i32, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp),
                                 C.POINTER(i32)]),
     "fb_tq_cache_dequant": (i32, [vp, C.c_uint64, szt, i32, szt, TP]),
+    "fb_tq_cache_attention": (i32, [vp, C.c_uint64, szt, TP, szt, szt, TP]),
 }
 
 _LIB = None

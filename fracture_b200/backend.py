@@ -310,3 +310,8 @@ class QuantizedKvCache:
 
     def dequant(self, handle: int, layer: int, kv: int, count: int, out: DeviceTensor) -> None:
         _check(self._lib.fb_tq_cache_dequant(self._h, handle, layer, kv, count, _ref(out)))
+
+    def attention(self, handle: int, layer: int, q: DeviceTensor, kv_len: int, start_pos: int,
+                  out: DeviceTensor) -> None:
+        """``attention_paged_tq`` of the sequence's cached layer (``batched.rs:143-193``)."""
+        _check(self._lib.fb_tq_cache_attention(self._h, handle, layer, _ref(q), kv_len, start_pos, _ref(out)))

@@ -228,6 +228,15 @@ struct fb_backend {
     }
 };
 
+namespace fb {
+size_t tq_attention_ws_bytes(int64_t rows, int hq, int max_kv_len);
+int tq_attention_one_seq(const void* q, int dtype, int num_tokens, int hq, int hkv, int head_dim, const void* kp,
+                         const void* kn, const void* vp, const void* vn, int64_t pool_rows, const int32_t* block_table,
+                         int num_blocks, int kv_len, int start_pos, const float* pik, const float* piv,
+                         const float* ck, const float* cv, int kb, int vb, void* workspace, size_t ws_bytes,
+                         void* out, cudaStream_t s);
+}  // namespace fb
+
 struct fb_tq_cache {
     fb_backend* be = nullptr;
     size_t num_blocks = 0, num_layers = 0, heads = 0, head_dim = 0;
@@ -245,6 +254,7 @@ struct fb_tq_cache {
     std::map<uint64_t, Seq> seqs;
     uint64_t next_id = 0;
     HostStage stage;
+    DevBuf attn_ws;  // rotated queries and chunk partials of attention, grown to the largest call
 
     bool protected_layer(size_t l) const {
         return cfg.protected_layers > 0 &&
@@ -788,6 +798,7 @@ int fb_tq_cache_destroy(fb_tq_cache* c) {
     }
     for (auto& kv : c->centroids) if (kv.second) cudaFree(kv.second);
     for (auto& s : c->seqs) s.second.dev_table.release();
+    c->attn_ws.release();
     c->stage.release();
     delete c;
     return FB_OK;
@@ -956,6 +967,43 @@ int fb_tq_cache_dequant(fb_tq_cache* c, uint64_t handle, size_t layer, int kv, s
                                        (const float*)c->centroids[bits], bits, (int64_t)count, (int)c->heads,
                                        (int)c->head_dim, (const int32_t*)it->second.dev_table.ptr, 0,
                                        (int64_t)c->num_blocks * 16, po, out->dtype, b->stream);
+    if (e) return cuda_fail((cudaError_t)e);
+    return FB_OK;
+}
+
+// QuantizedKvCacheManager's attention (batched.rs:143-193 -> Backend::attention_paged_tq,
+// backend.rs:180-222): q [N, Hq, d] FP16/BF16 tokens of the sequence at positions start_pos..,
+// attending its first kv_len cached positions of `layer`; out like q.
+int fb_tq_cache_attention(fb_tq_cache* c, uint64_t handle, size_t layer, const fb_tensor* q, size_t kv_len,
+                          size_t start_pos, const fb_tensor* out) {
+    if (!c || !q || !out) return fail(FB_ERR_BACKEND, "null argument");
+    fb_backend* b = c->be;
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    if (layer >= c->num_layers) return fail(FB_ERR_KV_CACHE, "layer " + std::to_string(layer) + " out of range");
+    auto it = c->seqs.find(handle);
+    if (it == c->seqs.end()) return fail(FB_ERR_KV_CACHE, "invalid handle: " + std::to_string(handle));
+    if (kv_len > it->second.len) return fail(FB_ERR_KV_CACHE, "attention past the sequence length");
+    void *pq, *po;
+    int rc;
+    if ((rc = b->get(q, &pq)) || (rc = b->get(out, &po))) return rc;
+    if (q->ndim != 3 || !same_shape(q, out) || q->shape[2] != (int64_t)c->head_dim ||
+        q->shape[1] % (int64_t)c->heads != 0)
+        return fail(FB_ERR_INVALID_SHAPE, "attention: q and out must be [N, Hq, " + std::to_string(c->head_dim) +
+                                              "] with Hq a multiple of " + std::to_string(c->heads));
+    if (q->dtype != out->dtype || (q->dtype != FB_FP16 && q->dtype != FB_BF16))
+        return fail(FB_ERR_UNSUPPORTED_DTYPE, "attention: q and out must be FP16 or BF16 of one type");
+    if ((rc = b->flush())) return rc;
+    if ((rc = tq_sync_table(c, it->second))) return rc;
+    const size_t ws = fb::tq_attention_ws_bytes(q->shape[0], (int)q->shape[1], (int)kv_len);
+    FB_CUDA(c->attn_ws.ensure(std::max<size_t>(ws, 16), b->stream));
+    const int kb = c->kbits[layer], vb = c->vbits[layer];
+    int e = fb::tq_attention_one_seq(pq, q->dtype, (int)q->shape[0], (int)q->shape[1], (int)c->heads, (int)c->head_dim,
+                                     c->packed[0][layer], c->norms[0][layer], c->packed[1][layer], c->norms[1][layer],
+                                     (int64_t)c->num_blocks * 16, (const int32_t*)it->second.dev_table.ptr,
+                                     (int)it->second.table.size(), (int)kv_len, (int)start_pos,
+                                     (const float*)c->rot[0][layer], (const float*)c->rot[1][layer],
+                                     (const float*)c->centroids[kb], (const float*)c->centroids[vb], kb, vb,
+                                     c->attn_ws.ptr, c->attn_ws.cap, po, b->stream);
     if (e) return cuda_fail((cudaError_t)e);
     return FB_OK;
 }

@@ -509,6 +509,47 @@ bool shape_ok(int hq, int hkv, int head_dim) {
 
 void set_last_error(const char* msg);
 
+size_t tq_attention_ws_bytes(int64_t rows, int hq, int max_kv_len) {
+    return tqa::workspace_bytes(rows, hq, (max_kv_len + tqa::CH - 1) / tqa::CH);
+}
+
+// One sequence over the contiguous pools, with host scalars for its length and start (the
+// backend object's cache manager).
+int tq_attention_one_seq(const void* q, int dtype, int num_tokens, int hq, int hkv, int head_dim, const void* kp,
+                         const void* kn, const void* vp, const void* vn, int64_t pool_rows, const int32_t* block_table,
+                         int num_blocks, int kv_len, int start_pos, const float* pik, const float* piv,
+                         const float* ck, const float* cv, int kb, int vb, void* workspace, size_t ws_bytes,
+                         void* out, cudaStream_t s) {
+    if ((dtype != FB_FP16 && dtype != FB_BF16) || !tqa::shape_ok(hq, hkv, head_dim) || !tqa::bits_ok(kb) ||
+        !tqa::bits_ok(vb) || num_tokens < 0 || num_tokens > 65535 || kv_len < 0 || start_pos < 0)
+        return (int)cudaErrorInvalidValue;
+    if (num_tokens == 0) return 0;
+    if (ws_bytes < tq_attention_ws_bytes(num_tokens, hq, kv_len) || !aligned16(workspace) || !aligned16(kp) ||
+        !aligned16(vp))
+        return (int)cudaErrorInvalidValue;
+    tqa::AttnArgs a{};
+    a.q = q;
+    a.dtype = dtype;
+    a.num_seqs = 1;
+    a.q_per_seq = num_tokens;
+    a.hq = hq;
+    a.hkv = hkv;
+    a.block_tables = block_table;
+    a.max_blocks = num_blocks;
+    a.kv_len = kv_len;
+    a.start = start_pos;
+    a.pik = pik;
+    a.piv = piv;
+    a.ck = ck;
+    a.cv = cv;
+    a.qrot = (float*)workspace;
+    a.part = a.qrot + (int64_t)num_tokens * hq * tqa::D;
+    a.nch = (kv_len + tqa::CH - 1) / tqa::CH;
+    a.out = out;
+    tqa::PoolAddr ad{(const uint8_t*)kp, (const __half*)kn, (const uint8_t*)vp, (const __half*)vn, pool_rows};
+    return tqa::run(a, kb, vb, ad, s);
+}
+
 }  // namespace fb
 
 using namespace fb;

@@ -313,6 +313,13 @@ int fb_tq_cache_pool(fb_tq_cache* c, size_t layer, int kv, void** packed, void**
                      void** centroids, int* bits);
 /* Dequantize a sequence's first `count` tokens of one layer into `out` ([count, Hkv, d]). */
 int fb_tq_cache_dequant(fb_tq_cache* c, uint64_t handle, size_t layer, int kv, size_t count, const fb_tensor* out);
+/* QuantizedKvCacheManager's attention (batched.rs:143-193 -> Backend::attention_paged_tq,
+ * backend.rs:180-222): q [N, Hq, d] FP16/BF16 (Hq a multiple of Hkv, Hq/Hkv in {1, 2, 4, 8}, d 128),
+ * tokens of the sequence at positions start_pos.., attending the sequence's first kv_len cached
+ * positions of `layer` (token t: positions [0, min(start_pos + t + 1, kv_len))); out like q. The
+ * workspace is the cache's, grown to the largest call. */
+int fb_tq_cache_attention(fb_tq_cache* c, uint64_t handle, size_t layer, const fb_tensor* q, size_t kv_len,
+                          size_t start_pos, const fb_tensor* out);
 
 #ifdef __cplusplus
 }

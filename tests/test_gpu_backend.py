@@ -249,6 +249,49 @@ def test_quantized_cache_append_matches_reference_placement(be):
     cache.destroy()
 
 
+def test_quantized_cache_attention_matches_statement(be):
+    """Attention through the cache manager (batched.rs:143-193): a sequence grown by uneven appends
+    over three layers (the first and last protected: 8-bit codes), then three query tokens at its end
+    against the float64 statement of attention_paged_tq.cu on the cache's own pools."""
+    H, d, L, NB, Hq = 8, 128, 3, 20, 32
+    cfg = TurboQuantConfig(key_bits=4, value_bits=2, protected_bits=8, protected_layers=1)
+    cache = QuantizedKvCache(be, NB, L, H, d, cfg)
+    a = cache.alloc()
+    rng = np.random.default_rng(12)
+    for n in (37, 1, 90, 5):
+        for layer in range(L):
+            cache.append_kv(a, layer, upload(be, rng.standard_normal((n, H, d)) * 1.5),
+                            upload(be, rng.standard_normal((n, H, d))))
+    T = cache.seq_len(a)
+    table = np.array(cache.block_table(a), np.int32)
+    be.synchronize()
+    for layer in range(L):
+        q = ops.round_to(rng.standard_normal((3, Hq, d)), "f16")
+        out = be.alloc([3, Hq, d], FB_FP16)
+        cache.attention(a, layer, upload(be, q), T, T - 3, out)
+        got = download(be, out)
+        pools = []
+        for kv in range(2):
+            p = cache.pool(layer, kv)
+            P = d * p["bits"] // 8
+            rows = NB * 16
+            tp = be.register_external(p["packed"], [rows, H * P], FB_INT8)
+            tn = be.register_external(p["norms"], [rows, H], FB_FP16)
+            tr = be.register_external(p["rotation"], [d, d], FB_FP32)
+            tc = be.register_external(p["centroids"], [1 << p["bits"]], FB_FP32)
+            pools.append((be.copy_to_host(tp).reshape(rows, H * P),
+                          be.copy_to_host(tn).view(np.float16).astype(np.float64).reshape(rows, H),
+                          be.copy_to_host(tr).view(np.float32).reshape(d, d),
+                          be.copy_to_host(tc).view(np.float32), p["bits"]))
+        (kp, kn, kr, kc, kb), (vp, vn, vr, vc, vb) = pools
+        assert (kb, vb) == ((4, 2) if layer == 1 else (8, 8))
+        ref = tq.attention_paged_tq(q, kp, kn, vp, vn, table, T, T - 3, kr, vr, kc, vc, kb, vb, H)
+        ops.assert_close_fp(got, ref, rel=2e-3, min_cos=0.9999, label=f"layer {layer}", dtype="f16")
+    with pytest.raises(KvCacheError, match="past the sequence length"):
+        cache.attention(a, 0, upload(be, np.zeros((1, Hq, d))), T + 1, T, be.alloc([1, Hq, d], FB_FP16))
+    cache.destroy()
+
+
 def test_quantized_cache_out_of_blocks(be):
     cache = QuantizedKvCache(be, 2, 1, 2, 16, TurboQuantConfig())
     h = cache.alloc()
