@@ -44,6 +44,7 @@ SIGNATURES = {
     "launch_turboquant_compress": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
     "launch_turboquant_decompress": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "launch_attention_paged_tq": (i32, [vp] * 11 + [i32] * 10 + [vp]),
+    "launch_paged_attention": (i32, [vp] * 5 + [i32] * 7 + [vp]),
     # 2. new kernel entry points
     "fb_launch_embedding": (i32, [vp, vp, vp, i64, i64, i64, i32, vp]),
     "fb_launch_add": (i32, [vp, vp, vp, i64, i32, vp]),
@@ -60,6 +61,10 @@ SIGNATURES = {
     "fb_tq_attention_workspace_bytes": (C.c_size_t, [i32, i32, i32, i32]),
     "fb_launch_tq_attention_paged": (i32, [vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, i64, vp, i32, vp, vp,
                                            i32, vp, vp, vp, vp, i32, i32, vp, C.c_size_t, vp, vp]),
+    "fb_attention_workspace_bytes": (C.c_size_t, [i32, i32, i32, i32]),
+    "fb_launch_attention_paged": (i32, [vp, i32, i32, i32, i32, i32, i32, vp, vp, i64, vp, i32, vp, vp, i32, vp,
+                                        C.c_size_t, vp, vp]),
+    "fb_launch_kv_append_paged": (i32, [vp, vp, i32, i64, i32, i32, vp, i64, i64, vp, vp, vp, vp]),
     "fb_tq_timeouts": (C.c_uint, []),
     "fb_rope_freqs": (i32, [i32, C.c_double, f32p]),
     "fb_rope_freqs_llama3": (i32, [i32, C.c_double, C.c_double, C.c_double, C.c_double, C.c_double, f32p]),

@@ -1,0 +1,446 @@
+// Paged attention over the FP16/BF16 KV cache and the paged append, sm_100a.
+//
+// Replaces backends/fracture-cuda/kernels/attention_paged.cu:25-185 (one CTA per query token
+// and Q head over the whole causal range, every Q head of a GQA group re-reading its KV head's
+// rows, the value phase one thread per coordinate walking every position) and the per-block row
+// copies of PagedKvCacheManager::append_kv (crates/fracture-engine/src/paged_kv_cache.rs:253-315).
+// The math is the reference kernel's: scores q . k / sqrt(d) in float32, softmax over
+// [0, min(start_pos + t + 1, kv_len)), out = sum p v. Here, split-K over 256-position chunks:
+//
+//   kvp_chunk    one CTA per (chunk, KV head, query token): thread p scores position p for
+//                every Q head of the group from the position's key row (16-byte loads,
+//                two-wide FP32 FMAs against the queries in shared memory), the CTA takes the
+//                chunk's softmax maximum and sum, then warp w accumulates its 32 positions'
+//                value rows (lane l: coordinates 4l..4l+3, one coalesced 8-byte load per
+//                position) for every head; the chunk's (max, sum, acc) go to the workspace
+//   kvp_combine  rescales and sums the chunks of each query token and head and divides
+//   kvp_append   writes new key/value rows into the pool through the block table
+//
+// Each KV head's rows are read once per query token for its whole group of Q heads. A position
+// whose block-table entry is negative, or whose pool row is out of range, is left out; a query
+// token with no position gives zeros.
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace fb {
+
+namespace kvp {
+
+constexpr int D = 128;
+constexpr int CH = 256;
+constexpr int THREADS = 256;
+constexpr int NWARPS = THREADS / 32;
+constexpr int MAXG = 8;
+constexpr int PART = D + 2;  // max, sum, acc[D]
+
+struct Args {
+    const void* q;
+    int dtype;  // FB_FP16 / FB_BF16: q, cache rows and out
+    int num_seqs, q_per_seq, hq, hkv;
+    const int32_t* block_tables;
+    int max_blocks;
+    const int32_t* kv_lens;    // null: kv_len for every sequence
+    const int32_t* start_pos;  // null: start for every sequence
+    int kv_len, start;
+    float* part;  // [rows, hq, nch, PART]
+    int nch;
+    void* out;
+};
+
+// Rows of the contiguous pools ([blocks * 16, hkv, D]) or of the reference's per-block tensors.
+struct PoolRows {
+    const uint8_t* k;
+    const uint8_t* v;
+    int64_t pool_rows;
+    __device__ bool locate(int32_t blk, int off, int g, int hkv, int esz, const uint8_t*& kr, const uint8_t*& vr) const {
+        const int64_t row = (int64_t)blk * 16 + off;
+        if (row >= pool_rows) return false;
+        const int64_t o = (row * hkv + g) * (int64_t)D * esz;
+        kr = k + o;
+        vr = v + o;
+        return true;
+    }
+};
+struct BlockPtrRows {
+    const uint8_t* const* k;
+    const uint8_t* const* v;
+    __device__ bool locate(int32_t blk, int off, int g, int hkv, int esz, const uint8_t*& kr, const uint8_t*& vr) const {
+        const int64_t o = ((int64_t)off * hkv + g) * D * esz;
+        kr = k[blk] + o;
+        vr = v[blk] + o;
+        return true;
+    }
+};
+
+__device__ __forceinline__ int causal_len(const Args& a, int s, int t) {
+    const int kv = a.kv_lens ? a.kv_lens[s] : a.kv_len;
+    const int st = a.start_pos ? a.start_pos[s] : a.start;
+    return max(0, min(st + t + 1, kv));
+}
+
+template <typename T>
+__device__ __forceinline__ float2 to_f2(uint32_t w) {
+    if constexpr (dtype_of<T>::value == FB_BF16) {
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+    } else {
+        return __half22float2(*reinterpret_cast<const __half2*>(&w));
+    }
+}
+
+template <typename T, int G>
+struct ChunkSmem {
+    static constexpr int q_off = 0;                              // [G][D] f32 (scaled queries)
+    static constexpr int acc_off = q_off + G * D * 4;            // [NWARPS][G][D] f32
+    static constexpr int w_off = acc_off + NWARPS * G * D * 4;   // [CH][G] f32 weights
+    static constexpr int red_off = w_off + CH * G * 4;           // [NWARPS][G]
+    static constexpr int bytes = red_off + NWARPS * G * 4 + 16;
+};
+
+template <typename T, int G, typename Rows>
+__global__ void __launch_bounds__(THREADS) kvp_chunk(Args a, Rows rw) {
+    using S = ChunkSmem<T, G>;
+    extern __shared__ __align__(16) uint8_t sm[];
+    float* qs = (float*)(sm + S::q_off);
+    float* accs = (float*)(sm + S::acc_off);
+    float* ws = (float*)(sm + S::w_off);
+    float* red = (float*)(sm + S::red_off);
+    const int row = blockIdx.z, g = blockIdx.y, c = blockIdx.x;
+    const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
+    const int L = causal_len(a, s, t);
+    const int p0 = c * CH;
+    if (p0 >= L) return;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int GA = a.hq / a.hkv;
+    const float scale = rsqrtf((float)D);
+    for (int e = tid; e < G * D; e += THREADS) {
+        float v = 0.0f;
+        if (e < GA * D) {
+            const int64_t qi = ((int64_t)row * a.hq + g * GA) * D + e;
+            v = dtype_of<T>::value == FB_BF16 ? __bfloat162float(((const __nv_bfloat16*)a.q)[qi])
+                                              : __half2float(((const __half*)a.q)[qi]);
+        }
+        qs[e] = v * scale;
+    }
+    __syncthreads();
+
+    // ── scores: thread tid takes position p0 + tid ──
+    const int p = p0 + tid;
+    bool valid = p < L && (p >> 4) < a.max_blocks;
+    const uint8_t* kr = nullptr;
+    const uint8_t* vr = nullptr;
+    if (valid) {
+        const int32_t blk = a.block_tables[(int64_t)s * a.max_blocks + (p >> 4)];
+        valid = blk >= 0 && rw.locate(blk, p & 15, g, a.hkv, (int)sizeof(T), kr, vr);
+    }
+    float sc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) sc[h] = 0.0f;
+    if (valid) {
+        float2 s2[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) s2[h] = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int k = 0; k < D / 8; ++k) {  // 8 coordinates per 16-byte load (all loads issued first)
+            const uint4 u = __ldg((const uint4*)kr + k);
+            const float2 x0 = to_f2<T>(u.x), x1 = to_f2<T>(u.y), x2 = to_f2<T>(u.z), x3 = to_f2<T>(u.w);
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                const float4 qa = *(const float4*)&qs[h * D + 8 * k];
+                const float4 qb = *(const float4*)&qs[h * D + 8 * k + 4];
+                s2[h] = __ffma2_rn(make_float2(qa.x, qa.y), x0, s2[h]);
+                s2[h] = __ffma2_rn(make_float2(qa.z, qa.w), x1, s2[h]);
+                s2[h] = __ffma2_rn(make_float2(qb.x, qb.y), x2, s2[h]);
+                s2[h] = __ffma2_rn(make_float2(qb.z, qb.w), x3, s2[h]);
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) sc[h] = s2[h].x + s2[h].y;
+    }
+
+    // ── softmax over the chunk ──
+    float mx[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        float v = valid ? sc[h] : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) red[warp * G + h] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        float v = red[h];
+        for (int w = 1; w < NWARPS; ++w) v = fmaxf(v, red[w * G + h]);
+        mx[h] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        const float e = valid ? expf(sc[h] - mx[h]) : 0.0f;
+        ws[tid * G + h] = e;
+        float v = e;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[warp * G + h] = v;
+    }
+    __syncthreads();
+
+    // ── values: warp w takes its 32 positions, lane l coordinates 4l..4l+3 of every head ──
+    float2 acc[G][2];
+#pragma unroll
+    for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = make_float2(0.0f, 0.0f);
+    // warp w scored the same 32 positions it now accumulates: lane j's value-row pointer
+    // travels by shuffle (0: position left out)
+    const unsigned long long vrow = valid ? (unsigned long long)vr : 0ull;
+    const int jn = min(32, L - (p0 + warp * 32));
+#pragma unroll 4
+    for (int j = 0; j < jn; ++j) {
+        const unsigned long long rp = __shfl_sync(0xffffffffu, vrow, j);
+        if (rp == 0ull) continue;  // position left out (weight 0)
+        const uint2 u = __ldg((const uint2*)rp + lane);
+        const float2 a0 = to_f2<T>(u.x), a1 = to_f2<T>(u.y);
+        const float* wp = ws + (warp * 32 + j) * G;
+#pragma unroll
+        for (int h4 = 0; h4 < G; h4 += 4) {
+            const float4 w4 = *(const float4*)(wp + h4);
+            const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 w2 = make_float2(wv[k], wv[k]);
+                acc[h4 + k][0] = __ffma2_rn(w2, a0, acc[h4 + k][0]);
+                acc[h4 + k][1] = __ffma2_rn(w2, a1, acc[h4 + k][1]);
+            }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+        *(float4*)&accs[(warp * G + h) * D + 4 * lane] = make_float4(acc[h][0].x, acc[h][0].y, acc[h][1].x, acc[h][1].y);
+    __syncthreads();
+    float* part = a.part + (((int64_t)row * a.hq + g * GA) * a.nch + c) * PART;
+    for (int e = tid; e < GA * D; e += THREADS) {
+        const int h = e / D, i = e - h * D;
+        float v = 0.0f;
+        for (int w = 0; w < NWARPS; ++w) v += accs[(w * G + h) * D + i];
+        part[(int64_t)h * a.nch * PART + 2 + i] = v;
+    }
+    if (tid < GA) {
+        float l = 0.0f;
+        for (int w = 0; w < NWARPS; ++w) l += red[w * G + tid];
+        float* ph = part + (int64_t)tid * a.nch * PART;
+        ph[0] = mx[tid];
+        ph[1] = l;
+    }
+}
+
+// out = (sum_c acc_c e^(m_c - M)) / (sum_c l_c e^(m_c - M)); thread i: coordinate i of every head.
+template <typename T>
+__global__ void __launch_bounds__(128) kvp_combine(Args a) {
+    const int row = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
+    const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
+    const int L = causal_len(a, s, t);
+    const int nc = (L + CH - 1) / CH;
+    const float* ph = a.part + ((int64_t)row * a.hq + h) * a.nch * PART;
+    float M = -INFINITY;
+#pragma unroll 8
+    for (int c = 0; c < nc; ++c) M = fmaxf(M, ph[c * PART]);
+    float l = 0.0f, v = 0.0f;
+    if (M > -INFINITY) {
+#pragma unroll 4
+        for (int c = 0; c < nc; ++c) {
+            const float m = ph[c * PART];
+            if (m == -INFINITY) continue;
+            const float f = expf(m - M);
+            l = fmaf(ph[c * PART + 1], f, l);
+            v = fmaf(ph[c * PART + 2 + i], f, v);
+        }
+    }
+    const float o = l > 0.0f ? v / l : 0.0f;
+    ((T*)a.out)[((int64_t)row * a.hq + h) * D + i] = from_f32<T>(o);
+}
+
+// Token t of the call goes to pool row block_table[(start + t) / 16] * 16 + (start + t) % 16 (a
+// negative entry or a row past the pool: skipped and counted in err_count); each thread copies
+// one 16-byte piece of one token's K and V rows ([Hkv * head_dim] elements).
+__global__ void kvp_append(const uint4* __restrict__ keys, const uint4* __restrict__ values, int64_t num_tokens,
+                           int row_vecs, const int32_t* __restrict__ block_table, int64_t start_pos,
+                           int64_t pool_rows, uint4* __restrict__ k_pool, uint4* __restrict__ v_pool,
+                           unsigned int* err_count) {
+    const int64_t n = num_tokens * row_vecs;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = e / row_vecs, k = e - t * row_vecs;
+        const int64_t pos = start_pos + t;
+        const int32_t b = block_table[pos >> 4];
+        const int64_t slot = b < 0 ? -1 : (int64_t)b * 16 + (pos & 15);
+        if (slot < 0 || slot >= pool_rows) {
+            if (k == 0 && err_count) atomicAdd(err_count, 1u);
+            continue;
+        }
+        k_pool[slot * row_vecs + k] = __ldg(keys + e);
+        v_pool[slot * row_vecs + k] = __ldg(values + e);
+    }
+}
+
+size_t workspace_bytes(int64_t rows, int hq, int nch) { return (size_t)rows * hq * nch * PART * 4; }
+
+template <typename T, int G, typename Rows>
+int launch_chunk(const Args& a, const Rows& rw, cudaStream_t s) {
+    constexpr int smem = ChunkSmem<T, G>::bytes;
+    auto kern = kvp_chunk<T, G, Rows>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return (int)e;
+    kern<<<dim3(a.nch, a.hkv, a.num_seqs * a.q_per_seq), THREADS, smem, s>>>(a, rw);
+    return (int)cudaGetLastError();
+}
+
+template <typename T, typename Rows>
+int run_t(const Args& a, const Rows& rw, cudaStream_t s) {
+    const int rows = a.num_seqs * a.q_per_seq;
+    if (rows == 0) return 0;
+    if (a.nch > 0) {
+        const int rc = a.hq / a.hkv <= 4 ? launch_chunk<T, 4>(a, rw, s) : launch_chunk<T, 8>(a, rw, s);
+        if (rc) return rc;
+    }
+    kvp_combine<T><<<dim3(rows, a.hq), 128, 0, s>>>(a);
+    return (int)cudaGetLastError();
+}
+
+template <typename Rows>
+int run(const Args& a, const Rows& rw, cudaStream_t s) {
+    return a.dtype == FB_BF16 ? run_t<__nv_bfloat16>(a, rw, s) : run_t<__half>(a, rw, s);
+}
+
+bool shape_ok(int hq, int hkv, int head_dim) {
+    if (head_dim != D || hkv <= 0 || hq <= 0 || hq % hkv) return false;
+    const int G = hq / hkv;
+    return G == 1 || G == 2 || G == 4 || G == 8;
+}
+
+}  // namespace kvp
+
+void set_last_error(const char* msg);
+
+}  // namespace fb
+
+using namespace fb;
+
+extern "C" size_t fb_attention_workspace_bytes(int num_seqs, int q_per_seq, int num_q_heads, int max_kv_len) {
+    if (num_seqs < 0 || q_per_seq < 0 || num_q_heads <= 0 || max_kv_len < 0) return 0;
+    return kvp::workspace_bytes((int64_t)num_seqs * q_per_seq, num_q_heads, (max_kv_len + kvp::CH - 1) / kvp::CH);
+}
+
+extern "C" int fb_launch_attention_paged(const void* q, int dtype, int num_seqs, int q_per_seq, int num_q_heads,
+                                         int num_kv_heads, int head_dim, const void* k_pool, const void* v_pool,
+                                         int64_t num_pool_rows, const int32_t* block_tables, int max_blocks_per_seq,
+                                         const int32_t* kv_lens, const int32_t* start_pos, int max_kv_len,
+                                         void* workspace, size_t workspace_bytes, void* output, void* stream) {
+    if ((dtype != FB_FP16 && dtype != FB_BF16) || !kvp::shape_ok(num_q_heads, num_kv_heads, head_dim))
+        return (int)cudaErrorInvalidValue;
+    if (num_seqs < 0 || q_per_seq < 0 || max_blocks_per_seq < 0 || max_kv_len < 0 || num_pool_rows < 0)
+        return (int)cudaErrorInvalidValue;
+    const int64_t rows = (int64_t)num_seqs * q_per_seq;
+    if (rows == 0) return 0;
+    if (!q || !output || !kv_lens || !start_pos) return (int)cudaErrorInvalidValue;
+    if (max_kv_len > 0 && (!block_tables || !k_pool || !v_pool)) return (int)cudaErrorInvalidValue;
+    if (!aligned16(k_pool) || !aligned16(v_pool) || !aligned16(workspace)) return (int)cudaErrorInvalidValue;
+    const int nch = (max_kv_len + kvp::CH - 1) / kvp::CH;
+    if (rows > 65535 || !workspace || workspace_bytes < kvp::workspace_bytes(rows, num_q_heads, nch)) {
+        set_last_error("fb_launch_attention_paged: workspace missing or smaller than fb_attention_workspace_bytes(), "
+                       "or more than 65535 query rows");
+        return (int)cudaErrorInvalidValue;
+    }
+    kvp::Args a{};
+    a.q = q;
+    a.dtype = dtype;
+    a.num_seqs = num_seqs;
+    a.q_per_seq = q_per_seq;
+    a.hq = num_q_heads;
+    a.hkv = num_kv_heads;
+    a.block_tables = block_tables;
+    a.max_blocks = max_blocks_per_seq;
+    a.kv_lens = kv_lens;
+    a.start_pos = start_pos;
+    a.part = (float*)workspace;
+    a.nch = nch;
+    a.out = output;
+    kvp::PoolRows rw{(const uint8_t*)k_pool, (const uint8_t*)v_pool, num_pool_rows};
+    return kvp::run(a, rw, (cudaStream_t)stream);
+}
+
+// ffi.rs:186-200 (attention_paged.cu:161-185): one sequence, FP16, per-block pointer arrays
+// (block b's K rows at k_block_ptrs[b], [16, Hkv, d]). Workspace: this library's, one per device,
+// grown to the largest call.
+extern "C" int launch_paged_attention(void* output, const void* q, const int* block_table, const void** k_block_ptrs,
+                                      const void** v_block_ptrs, int num_tokens, int num_q_heads, int num_kv_heads,
+                                      int head_dim, int kv_len, int start_pos, int num_blocks_in_seq, void* stream) {
+    if (!kvp::shape_ok(num_q_heads, num_kv_heads, head_dim) || num_tokens < 0 || num_tokens > 65535 || kv_len < 0 ||
+        start_pos < 0 || num_blocks_in_seq < 0)
+        return (int)cudaErrorInvalidValue;
+    if (num_tokens == 0) return 0;
+    if (!output || !q) return (int)cudaErrorInvalidValue;
+    if (kv_len > 0 && (!block_table || !k_block_ptrs || !v_block_ptrs)) return (int)cudaErrorInvalidValue;
+    const int nch = (kv_len + kvp::CH - 1) / kvp::CH;
+    const size_t need = std::max<size_t>(kvp::workspace_bytes(num_tokens, num_q_heads, nch), 16);
+    static void* ws[64];
+    static size_t cap[64];
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(mu);
+    if (cap[dev] < need) {
+        if (ws[dev]) {
+            e = cudaFree(ws[dev]);
+            if (e != cudaSuccess) return (int)e;
+        }
+        ws[dev] = nullptr;
+        cap[dev] = 0;
+        e = cudaMalloc(&ws[dev], need);
+        if (e != cudaSuccess) return (int)e;
+        cap[dev] = need;
+    }
+    kvp::Args a{};
+    a.q = q;
+    a.dtype = FB_FP16;
+    a.num_seqs = 1;
+    a.q_per_seq = num_tokens;
+    a.hq = num_q_heads;
+    a.hkv = num_kv_heads;
+    a.block_tables = block_table;
+    a.max_blocks = num_blocks_in_seq;
+    a.kv_len = kv_len;
+    a.start = start_pos;
+    a.part = (float*)ws[dev];
+    a.nch = nch;
+    a.out = output;
+    kvp::BlockPtrRows rw{(const uint8_t* const*)k_block_ptrs, (const uint8_t* const*)v_block_ptrs};
+    return kvp::run(a, rw, (cudaStream_t)stream);
+}
+
+// PagedKvCacheManager::append_kv's writes (paged_kv_cache.rs:290-315) in one launch: keys/values
+// [num_tokens, Hkv, d] (dtype FP16/BF16/FP32, the pool's), token t at sequence position
+// start_pos + t.
+extern "C" int fb_launch_kv_append_paged(const void* keys, const void* values, int dtype, int64_t num_tokens,
+                                         int num_kv_heads, int head_dim, const int32_t* block_table, int64_t start_pos,
+                                         int64_t num_pool_rows, void* k_pool, void* v_pool, unsigned int* err_count,
+                                         void* stream) {
+    const int esz = dtype == FB_FP32 ? 4 : (dtype == FB_FP16 || dtype == FB_BF16) ? 2 : 0;
+    if (!esz || num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || start_pos < 0 || num_pool_rows < 0)
+        return (int)cudaErrorInvalidValue;
+    if (num_tokens == 0) return 0;
+    const int64_t row_bytes = (int64_t)num_kv_heads * head_dim * esz;
+    if (row_bytes % 16 || !keys || !values || !block_table || !k_pool || !v_pool)
+        return (int)cudaErrorInvalidValue;
+    if (!aligned16(keys) || !aligned16(values) || !aligned16(k_pool) || !aligned16(v_pool))
+        return (int)cudaErrorInvalidValue;
+    const int row_vecs = (int)(row_bytes / 16);
+    const int64_t n = num_tokens * row_vecs;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 16));
+    kvp::kvp_append<<<grid, 256, 0, (cudaStream_t)stream>>>((const uint4*)keys, (const uint4*)values, num_tokens,
+                                                            row_vecs, block_table, start_pos, num_pool_rows,
+                                                            (uint4*)k_pool, (uint4*)v_pool, err_count);
+    return (int)cudaGetLastError();
+}

@@ -132,6 +132,35 @@ def tq_attention_paged(q, k_pool, k_norms, v_pool, v_norms, block_tables, kv_len
         _stream(stream)), "tq_attention_paged")
 
 
+def kv_append_paged(keys, values, k_pool, v_pool, block_table, start_pos=0, err=None, stream=None):
+    """Write ``keys``/``values [T, Hkv, d]`` into the pools ``[rows, Hkv, d]`` through the block table."""
+    T, H, d = keys.shape
+    _ok(_lib.load().fb_launch_kv_append_paged(
+        keys.data_ptr(), values.data_ptr(), _dt(keys), T, H, d, block_table.data_ptr(), start_pos, k_pool.shape[0],
+        k_pool.data_ptr(), v_pool.data_ptr(), err.data_ptr() if err is not None else None, _stream(stream)),
+        "kv_append_paged")
+
+
+def attention_workspace_bytes(num_seqs, q_per_seq, num_q_heads, max_kv_len) -> int:
+    return int(_lib.load().fb_attention_workspace_bytes(num_seqs, q_per_seq, num_q_heads, max_kv_len))
+
+
+def attention_paged(q, k_pool, v_pool, block_tables, kv_lens, start_pos, out, max_kv_len=None, workspace=None,
+                    stream=None):
+    """Attention of ``q [S, Tq, Hq, 128]`` over the FP16/BF16 paged cache (pools ``[rows, Hkv, 128]``)."""
+    S, Tq, Hq, d = q.shape
+    Hkv = k_pool.shape[1]
+    if max_kv_len is None:
+        max_kv_len = int(kv_lens.max().item()) if kv_lens.numel() else 0
+    need = attention_workspace_bytes(S, Tq, Hq, max_kv_len)
+    if workspace is None:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+    _ok(_lib.load().fb_launch_attention_paged(
+        q.data_ptr(), _dt(q), S, Tq, Hq, Hkv, d, k_pool.data_ptr(), v_pool.data_ptr(), k_pool.shape[0],
+        block_tables.data_ptr(), block_tables.shape[1], kv_lens.data_ptr(), start_pos.data_ptr(), max_kv_len,
+        workspace.data_ptr(), workspace.numel(), out.data_ptr(), _stream(stream)), "attention_paged")
+
+
 # host tables -------------------------------------------------------------------
 
 def rope_freqs(head_dim: int, theta: float) -> np.ndarray:

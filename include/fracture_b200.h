@@ -76,6 +76,16 @@ int launch_turboquant_compress(const void* input, const float* rotation, const f
 int launch_turboquant_decompress(const void* packed_in, const void* norms_in, const float* rotation,
                                  const float* centroids, void* output, int num_tokens, int num_kv_heads,
                                  int head_dim, int bits, int packed_dim_per_head, void* stream);
+/* ffi.rs:186-200 (attention_paged.cu:161-185): GQA attention of num_tokens FP16 query tokens of one
+ * sequence over its FP16 paged KV cache; block_table (device int32, num_blocks_in_seq entries)
+ * maps logical block pos/16 to a physical block whose K and V rows sit at k_block_ptrs[b],
+ * v_block_ptrs[b] (device arrays of device pointers, [16, Hkv, d] each). Token t attends positions
+ * [0, min(start_pos + t + 1, kv_len)). head_dim 128, Hq/Hkv in {1, 2, 4, 8}; float32 math. Uses a
+ * device workspace owned by this library, one per device, grown to the largest call. */
+int launch_paged_attention(void* output, const void* q, const int* block_table, const void** k_block_ptrs,
+                           const void** v_block_ptrs, int num_tokens, int num_q_heads, int num_kv_heads,
+                           int head_dim, int kv_len, int start_pos, int num_blocks_in_seq, void* stream);
+
 /* ffi.rs:251-274 (attention_paged_tq.cu:261-309): attention of num_tokens FP16 query tokens of one
  * sequence over its TurboQuant-compressed paged cache; block_table (device int32) maps logical
  * block pos/16 to a physical block whose packed K/V rows and norms sit at k_packed_ptrs[b],
@@ -195,6 +205,28 @@ int fb_launch_tq_attention_paged(const void* q, int dtype, int num_seqs, int q_p
                                  const float* v_rotation, const float* k_centroids, const float* v_centroids,
                                  int key_bits, int value_bits, void* workspace, size_t workspace_bytes, void* output,
                                  void* stream);
+
+/* Paged attention over an FP16/BF16 KV cache, batched over sequences (no reference counterpart for
+ * the batching; the math is attention_paged.cu:25-159, called per sequence). Pools
+ * [num_pool_rows, Hkv, 128] of `dtype` (the reference's per-block tensors [16, Hkv, d] back to back,
+ * pool row = block * 16 + offset); queries and output [num_seqs * q_per_seq, Hq, 128] of `dtype`;
+ * block tables, kv_lens, start_pos and the workspace as for fb_launch_tq_attention_paged
+ * (fb_attention_workspace_bytes). */
+size_t fb_attention_workspace_bytes(int num_seqs, int q_per_seq, int num_q_heads, int max_kv_len);
+int fb_launch_attention_paged(const void* q, int dtype, int num_seqs, int q_per_seq, int num_q_heads, int num_kv_heads,
+                              int head_dim, const void* k_pool, const void* v_pool, int64_t num_pool_rows,
+                              const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
+                              const int32_t* start_pos, int max_kv_len, void* workspace, size_t workspace_bytes,
+                              void* output, void* stream);
+/* PagedKvCacheManager::append_kv's row writes (paged_kv_cache.rs:290-315) in one launch: keys and
+ * values [num_tokens, Hkv, d] of `dtype` (FP16/BF16/FP32, the pools'), token t written at pool row
+ * block_table[(start_pos + t) / 16] * 16 + (start_pos + t) % 16 of k_pool / v_pool
+ * ([num_pool_rows, Hkv, d]); a negative block entry or a row past the pool is skipped and counted
+ * in err_count (device uint32, optional) once per token. Hkv * d * element size must be a multiple
+ * of 16 bytes. */
+int fb_launch_kv_append_paged(const void* keys, const void* values, int dtype, int64_t num_tokens, int num_kv_heads,
+                              int head_dim, const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
+                              void* k_pool, void* v_pool, unsigned int* err_count, void* stream);
 
 /* Number of bounded waits that timed out inside the tensor-core TurboQuant kernels (compress and
  * dequantize) since the library was loaded (0 in normal operation; a timeout abandons the launch's

@@ -192,6 +192,35 @@ def silu_mul(gate: np.ndarray, up: np.ndarray, dtype: str) -> np.ndarray:
 
 # ── tolerance helpers (the north-star parity bar) ───────────────────────────
 
+def attention_paged(q: np.ndarray, k_pool: np.ndarray, v_pool: np.ndarray, block_table: np.ndarray, kv_len: int,
+                    start_pos: int) -> np.ndarray:
+    """The statement of ``paged_attention_kernel`` (``backends/fracture-cuda/kernels/attention_paged.cu:25-159``)
+    in float64 for one sequence: ``q [N, Hq, d]`` (values), pools ``[rows, Hkv, d]`` (values) addressed by
+    ``block_table[pos // 16] * 16 + pos % 16``; token t attends ``[0, min(start_pos + t + 1, kv_len))``
+    (``:45-46``), Q head h reads KV head ``h // (Hq / Hkv)`` (``:42-43``); scores ``q . k / sqrt(d)``
+    (``:54-76``), softmax (``:78-135``), ``sum p v`` (``:137-157``). A negative block-table entry
+    leaves its positions out; a query with no position gives zeros."""
+    q = np.asarray(q, np.float64)
+    kp, vp = np.asarray(k_pool, np.float64), np.asarray(v_pool, np.float64)
+    N, Hq, d = q.shape
+    G = Hq // kp.shape[1]
+    table = np.asarray(block_table, np.int64)
+    out = np.zeros((N, Hq, d))
+    for t in range(N):
+        L = min(start_pos + t + 1, kv_len)
+        pos = np.arange(L)
+        blk = table[pos // 16]
+        rows = (blk * 16 + pos % 16)[blk >= 0]
+        if rows.size == 0:
+            continue
+        for h in range(Hq):
+            k, v = kp[rows, h // G], vp[rows, h // G]
+            s = k @ q[t, h] / np.sqrt(d)
+            p = np.exp(s - s.max())
+            out[t, h] = (p / p.sum()) @ v
+    return out
+
+
 def half_ulp(x: np.ndarray, dtype: str) -> np.ndarray:
     """Half a unit in the last place of the storage dtype at each value (its rounding bound)."""
     mant = {"f16": 10, "bf16": 7, "f32": 23}[dtype]
