@@ -733,6 +733,57 @@ def run_tq_attention(args, local_rank: int) -> dict:
             "l2": "the 420 MB cache is larger than L2 (no flush)"}
 
 
+def run_attention_fp16(args, local_rank: int) -> dict:
+    """The same decode attention over the uncompressed FP16 paged cache (PagedKvCacheManager's
+    path): 64 sequences x 1 query token at the end of an 8192-token context, 32 Q / 8 KV heads x
+    128, one fb_launch_attention_paged call per step. The 2.1 GB cache is larger than L2."""
+    import torch
+
+    from fracture_b200 import kernels as K
+
+    dev = torch.device("cuda", local_rank)
+    S, L, HQ, HKV, D = 64, 8192, NQ, NKV, HD
+    nblk = L // 16
+    g = torch.Generator(device=dev).manual_seed(8)
+    kp = torch.empty((S * L, HKV, D), dtype=torch.float16, device=dev)
+    vp = torch.empty_like(kp)
+    tables = torch.randperm(S * nblk, generator=g, device=dev).to(torch.int32).view(S, nblk)
+    for s in range(S):
+        x = torch.randn((L, HKV, D), generator=g, device=dev).half()
+        K.kv_append_paged(x, x, kp, vp, tables[s])
+    q = torch.randn((S, 1, HQ, D), generator=g, device=dev).half()
+    out = torch.empty_like(q)
+    kv_lens = torch.full((S,), L, dtype=torch.int32, device=dev)
+    starts = torch.full((S,), L - 1, dtype=torch.int32, device=dev)
+    ws = torch.empty(K.attention_workspace_bytes(S, 1, HQ, L), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        K.attention_paged(q, kp, vp, tables, kv_lens, starts, out, max_kv_len=L, workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for e0, e1 in ev:
+        e0.record(stream)
+        step()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / args.steps
+    by = S * L * HKV * D * 2 * 2 + 2 * S * HQ * D * 2 + S * nblk * 4
+    gbs = by / (ms / 1e3) / 1e9
+    pk = peaks()
+    return {"workload": "paged attention (decode) over the FP16 cache: 64 sequences x 1 query token, context 8192, "
+                        "32 Q / 8 KV heads x 128",
+            "kernels": "kvp_chunk (256-position split-K) + kvp_combine, CUDA cores, float32",
+            "ms_per_step": round(ms, 4), "query_tokens_per_s": round(S / (ms / 1e3), 1),
+            "kv_positions_per_s": round(S * L / (ms / 1e3), 1), "algorithmic_bytes_per_step": by,
+            "achieved_gbs": round(gbs, 1), "frac_of_peak": round(gbs / pk["hbm_gbs"], 4),
+            "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"],
+            "l2": "the 2.1 GB cache is larger than L2 (no flush)"}
+
+
 def cpu_baseline(tokens: int, layers: int, reps: int) -> dict:
     import torch
 
@@ -785,9 +836,10 @@ def profile_kernel(args) -> None:
 
     from fracture_b200 import kernels as K
 
-    if args.profile_kernel == "tq_attention":  # the bench's attention workload, W warm-up steps + 1
+    if args.profile_kernel in ("tq_attention", "attention_fp16"):  # the bench's workload, W warm-ups + 1
         args.steps = 1
-        print(json.dumps({"kernel": "tq_attention", "ms": run_tq_attention(args, 0)["ms_per_step"]}))
+        fn = run_tq_attention if args.profile_kernel == "tq_attention" else run_attention_fp16
+        print(json.dumps({"kernel": args.profile_kernel, "ms": fn(args, 0)["ms_per_step"]}))
         return
 
     dev = torch.device("cuda", 0)
@@ -859,7 +911,7 @@ def main() -> None:
     ap.add_argument("--pipeline", action="store_true",
                     help="also run config 5 (70B-shaped pipeline over the ranks, NCCL stage handoff)")
     ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding", "tq_compress",
-                                                                   "tq_dequant", "tq_attention"],
+                                                                   "tq_dequant", "tq_attention", "attention_fp16"],
                     help="run only this kernel at its config-3 size (W warm-up launches + 1), for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -899,6 +951,7 @@ def main() -> None:
         res["decode_config2"] = run_config2(args, local_rank)
     if res is not None and world == 1 and not args.no_attention:
         res["tq_attention"] = run_tq_attention(args, local_rank)
+        res["attention_fp16"] = run_attention_fp16(args, local_rank)
     if res is not None:
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline(tokens=2048, layers=16, reps=3)

@@ -196,22 +196,30 @@ __global__ void __launch_bounds__(THREADS) kvp_chunk(Args a, Rows rw) {
     // travels by shuffle (0: position left out)
     const unsigned long long vrow = valid ? (unsigned long long)vr : 0ull;
     const int jn = min(32, L - (p0 + warp * 32));
-#pragma unroll 4
-    for (int j = 0; j < jn; ++j) {
-        const unsigned long long rp = __shfl_sync(0xffffffffu, vrow, j);
-        if (rp == 0ull) continue;  // position left out (weight 0)
-        const uint2 u = __ldg((const uint2*)rp + lane);
-        const float2 a0 = to_f2<T>(u.x), a1 = to_f2<T>(u.y);
-        const float* wp = ws + (warp * 32 + j) * G;
+    for (int j0 = 0; j0 < jn; j0 += 8) {
+        // eight positions' value rows requested before any is used (a position left out, or past
+        // the causal range, loads nothing and has weight 0)
+        uint2 u[8];
 #pragma unroll
-        for (int h4 = 0; h4 < G; h4 += 4) {
-            const float4 w4 = *(const float4*)(wp + h4);
-            const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+        for (int k = 0; k < 8; ++k) {
+            const unsigned long long rp = __shfl_sync(0xffffffffu, vrow, j0 + k);
+            u[k] = make_uint2(0u, 0u);
+            if (j0 + k < jn && rp != 0ull) u[k] = __ldg((const uint2*)rp + lane);
+        }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float2 w2 = make_float2(wv[k], wv[k]);
-                acc[h4 + k][0] = __ffma2_rn(w2, a0, acc[h4 + k][0]);
-                acc[h4 + k][1] = __ffma2_rn(w2, a1, acc[h4 + k][1]);
+        for (int k = 0; k < 8; ++k) {
+            const float2 a0 = to_f2<T>(u[k].x), a1 = to_f2<T>(u[k].y);
+            const float* wp = ws + (warp * 32 + j0 + k) * G;
+#pragma unroll
+            for (int h4 = 0; h4 < G; h4 += 4) {
+                const float4 w4 = *(const float4*)(wp + h4);
+                const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float2 w2 = make_float2(wv[q], wv[q]);
+                    acc[h4 + q][0] = __ffma2_rn(w2, a0, acc[h4 + q][0]);
+                    acc[h4 + q][1] = __ffma2_rn(w2, a1, acc[h4 + q][1]);
+                }
             }
         }
     }
