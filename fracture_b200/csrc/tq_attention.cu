@@ -5,7 +5,8 @@
 // its KV head's codes). The math is the reference's (attention_paged_tq.cu:12-17): scores in
 // K's rotated space, (Pi_k q) . c_k[idx] * k_norm / sqrt(d); softmax over the causal range;
 // values accumulated in V's rotated space, sum p * c_v[idx] * v_norm, and rotated back once,
-// Pi_v^T acc. Here, in float32 throughout:
+// Pi_v^T acc. Here, with the centroid values read as fp16 (2^-11 relative) and everything else
+// in float32:
 //
 //   tqa_rotate_q    q_rot = Pi_k q for every query token and Q head (one warp per 32 rows
 //                   of Pi_k, lanes along the row), into the workspace
@@ -137,15 +138,16 @@ __global__ void __launch_bounds__(128) tqa_rotate_q(AttnArgs a) {
     }
 }
 
-// Decoding tables. Pair tables (2-, 3- and 4-bit codes): the 2*BITS bits of two adjacent
-// codes -> float2 (first code, second code), 16 copies side by side so a half-warp reads 16
-// different bank pairs. 8-bit codes: code -> float, 32 copies.
+// Decoding tables, 32 lane-private copies side by side (a warp's lookups hit 32 banks). Pair
+// tables (2-, 3- and 4-bit codes): the 2*BITS bits of two adjacent codes -> half2 (first code,
+// second code; the centroids rounded to fp16, 2^-11 relative, one shared-memory wavefront per
+// lookup). 8-bit codes: code -> float.
 template <int BITS>
 struct Lut {
     static constexpr bool pair = BITS <= 4;
     static constexpr int entries = pair ? (1 << (2 * BITS)) : 256;
-    static constexpr int copies = pair ? 16 : 32;
-    static constexpr int entry_bytes = pair ? 8 : 4;
+    static constexpr int copies = 32;
+    static constexpr int entry_bytes = 4;
     static constexpr int bytes = entries * copies * entry_bytes;
 };
 
@@ -158,8 +160,9 @@ __device__ __forceinline__ void build_lut(uint8_t* lut, const float* cen) {
     for (int ent = threadIdx.x; ent < L::entries; ent += blockDim.x) {
         float4 v;
         if constexpr (L::pair) {
-            const float a = __ldg(cen + (ent >> BITS)), b = __ldg(cen + (ent & ((1 << BITS) - 1)));
-            v = make_float4(a, b, a, b);
+            const __half2 h = __floats2half2_rn(__ldg(cen + (ent >> BITS)), __ldg(cen + (ent & ((1 << BITS) - 1))));
+            const float f = *reinterpret_cast<const float*>(&h);
+            v = make_float4(f, f, f, f);
         } else {
             const float a = __ldg(cen + ent);
             v = make_float4(a, a, a, a);
@@ -172,9 +175,9 @@ __device__ __forceinline__ void build_lut(uint8_t* lut, const float* cen) {
 
 template <int BITS>
 __device__ __forceinline__ float2 lut_pair(uint32_t lane_base, uint32_t idx) {
-    float2 v;
-    asm("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(lane_base + idx * (Lut<BITS>::copies * 8u)));
-    return v;
+    uint32_t w;
+    asm("ld.shared.b32 %0, [%1];" : "=r"(w) : "r"(lane_base + idx * 128u));
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
 }
 __device__ __forceinline__ float lut_one(uint32_t lane_base, uint32_t idx) {
     float v;
@@ -271,7 +274,7 @@ __global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
         if constexpr (Lut<KB>::pair) {
             // two running sums per head (even and odd coordinates) in one packed register pair:
             // one two-wide FMA per code pair and head; q_rot four coordinates per load
-            const uint32_t lb = smem_addr(lutk) + (lane & 15) * 8u;
+            const uint32_t lb = smem_addr(lutk) + lane * 4u;
             float2 s2[G];
 #pragma unroll
             for (int h = 0; h < G; ++h) s2[h] = make_float2(0.0f, 0.0f);
@@ -341,7 +344,7 @@ __global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
 #pragma unroll
     for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = make_float2(0.0f, 0.0f);
     {
-        const uint32_t lb = smem_addr(lutv) + (Lut<VB>::pair ? (lane & 15) * 8u : lane * 4u);
+        const uint32_t lb = smem_addr(lutv) + lane * 4u;
         const int jn = min(32, L - (p0 + warp * 32));
         for (int j = 0; j < jn; ++j) {
             const int pl = warp * 32 + j;

@@ -91,8 +91,8 @@ int launch_paged_attention(void* output, const void* q, const int* block_table, 
  * block pos/16 to a physical block whose packed K/V rows and norms sit at k_packed_ptrs[b],
  * k_norms_ptrs[b], ... (device arrays of device pointers, [16, Hkv*P] and [16, Hkv]). Token t
  * attends positions [0, min(start_pos + t + 1, kv_len)). head_dim 128, Hq/Hkv in {1, 2, 4, 8},
- * 2/3/4/8-bit codes. Float32 throughout (the reference's math in another summation order: within
- * FP16 rounding plus ~1e-6 of the output's magnitude). Uses a device workspace owned by this
+ * 2/3/4/8-bit codes. The reference's math in float32 with the 2/3/4-bit centroid values read as
+ * fp16 (within the 2e-3 FP bar of the float32 statement). Uses a device workspace owned by this
  * library, one per device, grown to the largest call. */
 int launch_attention_paged_tq(void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
                               const void** k_norms_ptrs, const void** v_packed_ptrs, const void** v_norms_ptrs,
