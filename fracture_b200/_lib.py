@@ -110,6 +110,16 @@ SIGNATURES = {
                                 C.POINTER(i32)]),
     "fb_tq_cache_dequant": (i32, [vp, C.c_uint64, szt, i32, szt, TP]),
     "fb_tq_cache_attention": (i32, [vp, C.c_uint64, szt, TP, szt, szt, TP]),
+    "fb_kv_cache_create": (i32, [vp, szt, szt, szt, szt, i32, C.POINTER(vp)]),
+    "fb_kv_cache_destroy": (i32, [vp]),
+    "fb_kv_cache_alloc": (i32, [vp, C.POINTER(C.c_uint64)]),
+    "fb_kv_cache_free": (i32, [vp, C.c_uint64]),
+    "fb_kv_cache_append_kv": (i32, [vp, C.c_uint64, szt, TP, TP]),
+    "fb_kv_cache_block_table": (i32, [vp, C.c_uint64, C.POINTER(C.c_int32), szt, C.POINTER(szt)]),
+    "fb_kv_cache_seq_len": (i32, [vp, C.c_uint64, C.POINTER(szt), C.POINTER(szt)]),
+    "fb_kv_cache_num_free_blocks": (i32, [vp, C.POINTER(szt)]),
+    "fb_kv_cache_pool": (i32, [vp, szt, C.POINTER(vp), C.POINTER(vp)]),
+    "fb_kv_cache_attention": (i32, [vp, C.c_uint64, szt, TP, szt, szt, TP]),
 }
 
 _LIB = None

@@ -236,6 +236,67 @@ class CudaBackend:
         _check(self._lib.fb_destroy_timer(self._h, t))
 
 
+class PagedKvCache:
+    """``PagedKvCacheManager`` (paged_kv_cache.rs:207-370) for the uncompressed FP16/BF16 cache."""
+
+    def __init__(self, backend: CudaBackend, num_blocks: int, num_layers: int, num_kv_heads: int, head_dim: int,
+                 dtype: int = FB_FP16):
+        self._lib = backend._lib
+        self.backend = backend
+        self.num_blocks, self.num_layers, self.num_kv_heads, self.head_dim = num_blocks, num_layers, num_kv_heads, head_dim
+        h = C.c_void_p()
+        _check(self._lib.fb_kv_cache_create(backend.handle, num_blocks, num_layers, num_kv_heads, head_dim, dtype,
+                                            C.byref(h)))
+        self._h = h
+
+    def destroy(self) -> None:
+        if self._h:
+            self._lib.fb_kv_cache_destroy(self._h)
+            self._h = None
+
+    def alloc(self) -> int:
+        v = C.c_uint64()
+        _check(self._lib.fb_kv_cache_alloc(self._h, C.byref(v)))
+        return v.value
+
+    def free(self, handle: int) -> None:
+        _check(self._lib.fb_kv_cache_free(self._h, handle))
+
+    def append_kv(self, handle: int, layer: int, keys: DeviceTensor, values: DeviceTensor) -> None:
+        _check(self._lib.fb_kv_cache_append_kv(self._h, handle, layer, _ref(keys), _ref(values)))
+
+    def block_table(self, handle: int) -> list[int]:
+        n = C.c_size_t()
+        _check(self._lib.fb_kv_cache_block_table(self._h, handle, None, 0, C.byref(n)))
+        arr = (C.c_int32 * max(n.value, 1))()
+        _check(self._lib.fb_kv_cache_block_table(self._h, handle, arr, n.value, C.byref(n)))
+        return list(arr[: n.value])
+
+    def seq_len(self, handle: int) -> int:
+        v, f = C.c_size_t(), C.c_size_t()
+        _check(self._lib.fb_kv_cache_seq_len(self._h, handle, C.byref(v), C.byref(f)))
+        return v.value
+
+    def last_block_tokens(self, handle: int) -> int:
+        v, f = C.c_size_t(), C.c_size_t()
+        _check(self._lib.fb_kv_cache_seq_len(self._h, handle, C.byref(v), C.byref(f)))
+        return f.value
+
+    def num_free_blocks(self) -> int:
+        v = C.c_size_t()
+        _check(self._lib.fb_kv_cache_num_free_blocks(self._h, C.byref(v)))
+        return v.value
+
+    def pool(self, layer: int) -> dict:
+        k, v = C.c_void_p(), C.c_void_p()
+        _check(self._lib.fb_kv_cache_pool(self._h, layer, C.byref(k), C.byref(v)))
+        return {"k": k.value, "v": v.value}
+
+    def attention(self, handle: int, layer: int, q: DeviceTensor, kv_len: int, start_pos: int,
+                  out: DeviceTensor) -> None:
+        _check(self._lib.fb_kv_cache_attention(self._h, handle, layer, _ref(q), kv_len, start_pos, _ref(out)))
+
+
 @dataclass
 class TurboQuantConfig:
     """``TurboQuantConfig`` (crates/fracture-core/src/turboquant.rs:7-33); 3 bits is accepted here."""

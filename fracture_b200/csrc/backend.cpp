@@ -228,6 +228,18 @@ struct fb_backend {
     }
 };
 
+extern "C" {
+size_t fb_attention_workspace_bytes(int num_seqs, int q_per_seq, int num_q_heads, int max_kv_len);
+int fb_launch_attention_paged(const void* q, int dtype, int num_seqs, int q_per_seq, int num_q_heads, int num_kv_heads,
+                              int head_dim, const void* k_pool, const void* v_pool, int64_t num_pool_rows,
+                              const int32_t* block_tables, int max_blocks_per_seq, const int32_t* kv_lens,
+                              const int32_t* start_pos, int max_kv_len, void* workspace, size_t workspace_bytes,
+                              void* output, void* stream);
+int fb_launch_kv_append_paged(const void* keys, const void* values, int dtype, int64_t num_tokens, int num_kv_heads,
+                              int head_dim, const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
+                              void* k_pool, void* v_pool, unsigned int* err_count, void* stream);
+}
+
 namespace fb {
 size_t tq_attention_ws_bytes(int64_t rows, int hq, int max_kv_len);
 int tq_attention_one_seq(const void* q, int dtype, int num_tokens, int hq, int hkv, int head_dim, const void* kp,
@@ -268,6 +280,29 @@ struct fb_tq_cache {
         }
         return t;
     }
+};
+
+// PagedKvCacheManager (crates/fracture-engine/src/paged_kv_cache.rs:207-370) over contiguous
+// per-layer K and V pools [num_blocks * 16, heads, head_dim] of one dtype (the BlockPool's
+// per-block tensors back to back, paged_kv_cache.rs:35-205).
+struct fb_kv_cache {
+    fb_backend* be = nullptr;
+    size_t num_blocks = 0, num_layers = 0, heads = 0, head_dim = 0;
+    int dtype = FB_FP16;
+    std::vector<void*> k, v;  // per layer
+    std::vector<size_t> free_list;
+    struct Seq {
+        std::vector<int32_t> table;
+        size_t last_fill = 0, len = 0;
+        DevBuf dev_table;
+        size_t dev_len = 0;
+        DevBuf one;  // kv_len and start_pos of an attention call (2 x int32)
+    };
+    std::map<uint64_t, Seq> seqs;
+    uint64_t next_id = 0;
+    HostStage stage;
+    DevBuf attn_ws;
+    size_t bytes_per_block() const { return num_layers * 2 * 16 * heads * head_dim * 2; }  // FP16 or BF16
 };
 
 extern "C" {
@@ -967,6 +1002,234 @@ int fb_tq_cache_dequant(fb_tq_cache* c, uint64_t handle, size_t layer, int kv, s
                                        (const float*)c->centroids[bits], bits, (int64_t)count, (int)c->heads,
                                        (int)c->head_dim, (const int32_t*)it->second.dev_table.ptr, 0,
                                        (int64_t)c->num_blocks * 16, po, out->dtype, b->stream);
+    if (e) return cuda_fail((cudaError_t)e);
+    return FB_OK;
+}
+
+// ── FP16 / BF16 paged KV cache ────────────────────────────────────────────
+
+int fb_kv_cache_create(fb_backend* b, size_t num_blocks, size_t num_layers, size_t num_kv_heads, size_t head_dim,
+                       int dtype, fb_kv_cache** out) {
+    if (!b || !out) return fail(FB_ERR_BACKEND, "null argument");
+    if (dtype != FB_FP16 && dtype != FB_BF16) return fail(FB_ERR_UNSUPPORTED_DTYPE, "paged KV cache: FP16 or BF16");
+    if (num_layers == 0 || num_kv_heads == 0 || head_dim == 0 || (num_kv_heads * head_dim * 2) % 16)
+        return fail(FB_ERR_MODEL_CONFIG, "invalid paged cache dimensions");
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    int rc;
+    if ((rc = b->flush())) return rc;
+    auto* c = new fb_kv_cache();
+    c->be = b;
+    c->num_blocks = num_blocks;
+    c->num_layers = num_layers;
+    c->heads = num_kv_heads;
+    c->head_dim = head_dim;
+    c->dtype = dtype;
+    const size_t bytes = std::max<size_t>(num_blocks * 16 * num_kv_heads * head_dim * 2, 1);
+    for (size_t l = 0; l < num_layers; ++l) {
+        void *pk = nullptr, *pv = nullptr;
+        cudaError_t e = cudaMalloc(&pk, bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&pv, bytes);
+        c->k.push_back(pk);
+        c->v.push_back(pv);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            fb_kv_cache_destroy(c);
+            return cuda_fail(e);
+        }
+    }
+    for (size_t i = num_blocks; i > 0; --i) c->free_list.push_back(i - 1);
+    *out = c;
+    return FB_OK;
+}
+
+int fb_kv_cache_destroy(fb_kv_cache* c) {
+    if (!c) return FB_OK;
+    cudaStreamSynchronize(c->be->stream);
+    for (void* p : c->k) if (p) cudaFree(p);
+    for (void* p : c->v) if (p) cudaFree(p);
+    for (auto& s : c->seqs) {
+        s.second.dev_table.release();
+        s.second.one.release();
+    }
+    c->attn_ws.release();
+    c->stage.release();
+    delete c;
+    return FB_OK;
+}
+
+static int kv_alloc_block(fb_kv_cache* c, int32_t* out) {
+    if (c->free_list.empty()) {
+        char buf[160];
+        snprintf(buf, sizeof(buf), "out of device memory: requested %zu bytes, available 0 bytes", c->bytes_per_block());
+        return fail(FB_ERR_OUT_OF_MEMORY, buf);
+    }
+    *out = (int32_t)c->free_list.back();
+    c->free_list.pop_back();
+    return FB_OK;
+}
+
+// alloc: one initial block (paged_kv_cache.rs:231-249).
+int fb_kv_cache_alloc(fb_kv_cache* c, uint64_t* handle) {
+    if (!c || !handle) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(c->be->mu);
+    const uint64_t id = c->next_id++;
+    int32_t blk;
+    int rc = kv_alloc_block(c, &blk);
+    if (rc) return rc;
+    c->seqs[id].table.push_back(blk);
+    *handle = id;
+    return FB_OK;
+}
+
+int fb_kv_cache_free(fb_kv_cache* c, uint64_t handle) {
+    if (!c) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(c->be->mu);
+    auto it = c->seqs.find(handle);
+    if (it == c->seqs.end()) return fail(FB_ERR_KV_CACHE, "invalid handle: " + std::to_string(handle));
+    for (int32_t blk : it->second.table) c->free_list.push_back((size_t)blk);
+    cudaStreamSynchronize(c->be->stream);  // queued kernels may still read the device table
+    it->second.dev_table.release();
+    it->second.one.release();
+    c->seqs.erase(it);
+    return FB_OK;
+}
+
+static int kv_sync_table(fb_kv_cache* c, fb_kv_cache::Seq& s) {
+    if (s.dev_len == s.table.size()) return FB_OK;
+    fb_backend* b = c->be;
+    const size_t bytes = s.table.size() * sizeof(int32_t);
+    FB_CUDA(s.dev_table.ensure(bytes, b->stream));
+    FB_CUDA(c->stage.ensure(bytes));
+    memcpy(c->stage.host, s.table.data(), bytes);
+    FB_CUDA(cudaMemcpyAsync(s.dev_table.ptr, c->stage.host, bytes, cudaMemcpyHostToDevice, b->stream));
+    FB_CUDA(cudaEventRecord(c->stage.done, b->stream));
+    c->stage.pending = true;
+    s.dev_len = s.table.size();
+    return FB_OK;
+}
+
+// append_kv (paged_kv_cache.rs:253-315): blocks are taken on layer 0; every layer's rows are
+// written by one launch for K and V.
+int fb_kv_cache_append_kv(fb_kv_cache* c, uint64_t handle, size_t layer, const fb_tensor* keys,
+                          const fb_tensor* values) {
+    if (!c || !keys || !values) return fail(FB_ERR_BACKEND, "null argument");
+    fb_backend* b = c->be;
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    if (layer >= c->num_layers) return fail(FB_ERR_KV_CACHE, "layer " + std::to_string(layer) + " out of range");
+    void *pk, *pv;
+    int rc;
+    if ((rc = b->get(keys, &pk)) || (rc = b->get(values, &pv))) return rc;
+    if (keys->ndim != 3 || !same_shape(keys, values) || keys->shape[1] != (int64_t)c->heads ||
+        keys->shape[2] != (int64_t)c->head_dim)
+        return fail(FB_ERR_INVALID_SHAPE, "append_kv: keys/values must be [N, " + std::to_string(c->heads) + ", " +
+                                              std::to_string(c->head_dim) + "]");
+    if (keys->dtype != c->dtype || values->dtype != c->dtype)
+        return fail(FB_ERR_UNSUPPORTED_DTYPE, "append_kv: keys/values must have the cache's dtype");
+    auto it = c->seqs.find(handle);
+    if (it == c->seqs.end()) return fail(FB_ERR_KV_CACHE, "invalid handle: " + std::to_string(handle));
+    auto& s = it->second;
+    const size_t num_new = (size_t)keys->shape[0];
+    if (layer == 0) {
+        size_t remaining = num_new, fill = s.last_fill;
+        while (remaining > 0) {
+            const size_t slots = 16 - fill;
+            if (slots == 0) {
+                int32_t blk;
+                if ((rc = kv_alloc_block(c, &blk))) return rc;
+                s.table.push_back(blk);
+                fill = 0;
+                continue;
+            }
+            const size_t w = std::min(remaining, slots);
+            fill += w;
+            remaining -= w;
+        }
+        s.last_fill = fill;
+        s.len += num_new;
+    }
+    if (num_new == 0) return FB_OK;
+    if (s.len < num_new) return fail(FB_ERR_KV_CACHE, "append_kv on layer " + std::to_string(layer) + " before layer 0");
+    if ((rc = b->flush())) return rc;
+    if ((rc = kv_sync_table(c, s))) return rc;
+    int e = fb_launch_kv_append_paged(pk, pv, c->dtype, (int64_t)num_new, (int)c->heads, (int)c->head_dim,
+                                      (const int32_t*)s.dev_table.ptr, (int64_t)(s.len - num_new),
+                                      (int64_t)c->num_blocks * 16, c->k[layer], c->v[layer], nullptr, b->stream);
+    if (e) return cuda_fail((cudaError_t)e);
+    return FB_OK;
+}
+
+int fb_kv_cache_block_table(fb_kv_cache* c, uint64_t handle, int32_t* out, size_t cap, size_t* len) {
+    if (!c || !len) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(c->be->mu);
+    auto it = c->seqs.find(handle);
+    if (it == c->seqs.end()) return fail(FB_ERR_KV_CACHE, "invalid handle: " + std::to_string(handle));
+    *len = it->second.table.size();
+    if (out) memcpy(out, it->second.table.data(), std::min(cap, *len) * sizeof(int32_t));
+    return FB_OK;
+}
+
+int fb_kv_cache_seq_len(fb_kv_cache* c, uint64_t handle, size_t* len, size_t* last_block_tokens) {
+    if (!c || !len) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(c->be->mu);
+    auto it = c->seqs.find(handle);
+    if (it == c->seqs.end()) return fail(FB_ERR_KV_CACHE, "invalid handle: " + std::to_string(handle));
+    *len = it->second.len;
+    if (last_block_tokens) *last_block_tokens = it->second.last_fill;
+    return FB_OK;
+}
+
+int fb_kv_cache_num_free_blocks(fb_kv_cache* c, size_t* out) {
+    if (!c || !out) return fail(FB_ERR_BACKEND, "null argument");
+    std::lock_guard<std::recursive_mutex> g(c->be->mu);
+    *out = c->free_list.size();
+    return FB_OK;
+}
+
+int fb_kv_cache_pool(fb_kv_cache* c, size_t layer, void** k_pool, void** v_pool) {
+    if (!c || layer >= c->num_layers) return fail(FB_ERR_KV_CACHE, "invalid layer");
+    if (k_pool) *k_pool = c->k[layer];
+    if (v_pool) *v_pool = c->v[layer];
+    return FB_OK;
+}
+
+// The manager's attention (batched.rs -> Backend::attention_paged, backend.rs:66-88): q [N, Hq, d]
+// of the cache's dtype, tokens at positions start_pos.., over the first kv_len cached positions.
+int fb_kv_cache_attention(fb_kv_cache* c, uint64_t handle, size_t layer, const fb_tensor* q, size_t kv_len,
+                          size_t start_pos, const fb_tensor* out) {
+    if (!c || !q || !out) return fail(FB_ERR_BACKEND, "null argument");
+    fb_backend* b = c->be;
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    if (layer >= c->num_layers) return fail(FB_ERR_KV_CACHE, "layer " + std::to_string(layer) + " out of range");
+    auto it = c->seqs.find(handle);
+    if (it == c->seqs.end()) return fail(FB_ERR_KV_CACHE, "invalid handle: " + std::to_string(handle));
+    auto& s = it->second;
+    if (kv_len > s.len) return fail(FB_ERR_KV_CACHE, "attention past the sequence length");
+    void *pq, *po;
+    int rc;
+    if ((rc = b->get(q, &pq)) || (rc = b->get(out, &po))) return rc;
+    if (q->ndim != 3 || !same_shape(q, out) || q->shape[2] != (int64_t)c->head_dim ||
+        q->shape[1] % (int64_t)c->heads != 0)
+        return fail(FB_ERR_INVALID_SHAPE, "attention: q and out must be [N, Hq, " + std::to_string(c->head_dim) +
+                                              "] with Hq a multiple of " + std::to_string(c->heads));
+    if (q->dtype != c->dtype || out->dtype != c->dtype)
+        return fail(FB_ERR_UNSUPPORTED_DTYPE, "attention: q and out must have the cache's dtype");
+    if ((rc = b->flush())) return rc;
+    if ((rc = kv_sync_table(c, s))) return rc;
+    // kv_len and start_pos as device scalars for the batched entry point (one sequence)
+    FB_CUDA(s.one.ensure(8, b->stream));
+    FB_CUDA(c->stage.ensure(8));
+    const int32_t hv[2] = {(int32_t)kv_len, (int32_t)start_pos};
+    memcpy(c->stage.host, hv, 8);
+    FB_CUDA(cudaMemcpyAsync(s.one.ptr, c->stage.host, 8, cudaMemcpyHostToDevice, b->stream));
+    FB_CUDA(cudaEventRecord(c->stage.done, b->stream));
+    c->stage.pending = true;
+    const size_t ws = std::max<size_t>(fb_attention_workspace_bytes(1, (int)q->shape[0], (int)q->shape[1], (int)kv_len), 16);
+    FB_CUDA(c->attn_ws.ensure(ws, b->stream));
+    const int32_t* one = (const int32_t*)s.one.ptr;
+    int e = fb_launch_attention_paged(pq, c->dtype, 1, (int)q->shape[0], (int)q->shape[1], (int)c->heads,
+                                      (int)c->head_dim, c->k[layer], c->v[layer], (int64_t)c->num_blocks * 16,
+                                      (const int32_t*)s.dev_table.ptr, (int)s.table.size(), one, one + 1,
+                                      (int)kv_len, c->attn_ws.ptr, c->attn_ws.cap, po, b->stream);
     if (e) return cuda_fail((cudaError_t)e);
     return FB_OK;
 }

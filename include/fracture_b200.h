@@ -353,6 +353,28 @@ int fb_tq_cache_dequant(fb_tq_cache* c, uint64_t handle, size_t layer, int kv, s
 int fb_tq_cache_attention(fb_tq_cache* c, uint64_t handle, size_t layer, const fb_tensor* q, size_t kv_len,
                           size_t start_pos, const fb_tensor* out);
 
+/* PagedKvCacheManager (crates/fracture-engine/src/paged_kv_cache.rs:207-370) for the uncompressed
+ * cache: per-layer K and V pools [num_blocks * 16, Hkv, d] of `dtype` (FP16/BF16), blocks of 16
+ * tokens from a free list. alloc takes one initial block (:231-249); append_kv takes blocks on
+ * layer 0 and writes every layer's rows with one launch for K and V (:253-315); out of blocks is
+ * FB_ERR_OUT_OF_MEMORY as in the reference's BlockPool. attention: q and out [N, Hq, d] of the
+ * cache's dtype, tokens at positions start_pos.. attending the first kv_len cached positions
+ * (Backend::attention_paged, backend.rs:66-88). */
+typedef struct fb_kv_cache fb_kv_cache;
+int fb_kv_cache_create(fb_backend* b, size_t num_blocks, size_t num_layers, size_t num_kv_heads, size_t head_dim,
+                       int dtype, fb_kv_cache** out);
+int fb_kv_cache_destroy(fb_kv_cache* c);
+int fb_kv_cache_alloc(fb_kv_cache* c, uint64_t* handle);
+int fb_kv_cache_free(fb_kv_cache* c, uint64_t handle);
+int fb_kv_cache_append_kv(fb_kv_cache* c, uint64_t handle, size_t layer, const fb_tensor* keys,
+                          const fb_tensor* values);
+int fb_kv_cache_block_table(fb_kv_cache* c, uint64_t handle, int32_t* out, size_t cap, size_t* len);
+int fb_kv_cache_seq_len(fb_kv_cache* c, uint64_t handle, size_t* len, size_t* last_block_tokens);
+int fb_kv_cache_num_free_blocks(fb_kv_cache* c, size_t* out);
+int fb_kv_cache_pool(fb_kv_cache* c, size_t layer, void** k_pool, void** v_pool);
+int fb_kv_cache_attention(fb_kv_cache* c, uint64_t handle, size_t layer, const fb_tensor* q, size_t kv_len,
+                          size_t start_pos, const fb_tensor* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 from fracture_b200.backend import (FB_BF16, FB_FP16, FB_FP32, FB_INT8, BackendError, CudaBackend, InvalidShape,
-                                   KvCacheError, OutOfMemory, QuantizedKvCache, TensorNotFound, TurboQuantConfig)
+                                   KvCacheError, OutOfMemory, PagedKvCache, QuantizedKvCache, TensorNotFound, TurboQuantConfig)
 from fracture_b200 import kernels as K
 from oracle import ops, turboquant as tq
 
@@ -289,6 +289,57 @@ def test_quantized_cache_attention_matches_statement(be):
         ops.assert_close_fp(got, ref, rel=2e-3, min_cos=0.9999, label=f"layer {layer}", dtype="f16")
     with pytest.raises(KvCacheError, match="past the sequence length"):
         cache.attention(a, 0, upload(be, np.zeros((1, Hq, d))), T + 1, T, be.alloc([1, Hq, d], FB_FP16))
+    cache.destroy()
+
+
+def test_paged_cache_append_and_attention(be):
+    """PagedKvCacheManager: uneven appends over two layers place rows through the block table
+    (one block up front, new blocks on layer 0), the manager's attention meets the FP bar of
+    attention_paged.cu's statement, and running out of blocks is OutOfMemory."""
+    H, d, L, NB, Hq = 8, 128, 2, 12, 32
+    cache = PagedKvCache(be, NB, L, H, d, FB_FP16)
+    a = cache.alloc()
+    assert cache.num_free_blocks() == NB - 1 and cache.block_table(a) != []
+    rng = np.random.default_rng(13)
+    keys = {l: [] for l in range(L)}
+    vals = {l: [] for l in range(L)}
+    for n in (10, 6, 1, 40):
+        for layer in range(L):
+            kx = ops.round_to(rng.standard_normal((n, H, d)), "f16")
+            vx = ops.round_to(rng.standard_normal((n, H, d)), "f16")
+            keys[layer].append(kx)
+            vals[layer].append(vx)
+            cache.append_kv(a, layer, upload(be, kx), upload(be, vx))
+    T = cache.seq_len(a)
+    assert T == 57 and cache.last_block_tokens(a) == 57 - 48
+    table = np.array(cache.block_table(a), np.int32)
+    assert len(table) == 4
+    be.synchronize()
+    pos = np.arange(T)
+    rows = table[pos // 16] * 16 + pos % 16
+    for layer in range(L):
+        p = cache.pool(layer)
+        tk = be.register_external(p["k"], [NB * 16, H, d], FB_FP16)
+        tv = be.register_external(p["v"], [NB * 16, H, d], FB_FP16)
+        kpool = be.copy_to_host(tk).view(np.float16).astype(np.float32).reshape(NB * 16, H, d)
+        vpool = be.copy_to_host(tv).view(np.float16).astype(np.float32).reshape(NB * 16, H, d)
+        assert np.array_equal(kpool[rows], np.concatenate(keys[layer]))
+        assert np.array_equal(vpool[rows], np.concatenate(vals[layer]))
+        q = ops.round_to(rng.standard_normal((2, Hq, d)), "f16")
+        out = be.alloc([2, Hq, d], FB_FP16)
+        cache.attention(a, layer, upload(be, q), T, T - 2, out)
+        ref = ops.attention_paged(q, kpool, vpool, table, T, T - 2)
+        ops.assert_close_fp(download(be, out), ref, rel=2e-3, min_cos=0.9999, label=f"layer {layer}", dtype="f16")
+    b_ = cache.alloc()
+    with pytest.raises(OutOfMemory):
+        for _ in range(20):
+            for layer in range(L):
+                cache.append_kv(b_, layer, upload(be, np.zeros((16, H, d))), upload(be, np.zeros((16, H, d))))
+    free_before = cache.num_free_blocks()
+    cache.free(a)
+    assert cache.num_free_blocks() == free_before + len(table)
+    with pytest.raises(KvCacheError, match="invalid handle"):
+        cache.free(a)
     cache.destroy()
 
 
