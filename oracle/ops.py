@@ -194,7 +194,7 @@ def silu_mul(gate: np.ndarray, up: np.ndarray, dtype: str) -> np.ndarray:
 
 def attention_paged(q: np.ndarray, k_pool: np.ndarray, v_pool: np.ndarray, block_table: np.ndarray, kv_len: int,
                     start_pos: int) -> np.ndarray:
-    """The statement of ``paged_attention_kernel`` (``backends/fracture-cuda/kernels/attention_paged.cu:25-159``)
+    """The statement of ``paged_attention_kernel`` (``backends/fracture-cuda/kernels/attention_paged.cu:25-155``)
     in float64 for one sequence: ``q [N, Hq, d]`` (values), pools ``[rows, Hkv, d]`` (values) addressed by
     ``block_table[pos // 16] * 16 + pos % 16``; token t attends ``[0, min(start_pos + t + 1, kv_len))``
     (``:45-46``), Q head h reads KV head ``h // (Hq / Hkv)`` (``:42-43``); scores ``q . k / sqrt(d)``

@@ -541,7 +541,7 @@ def attention_paged_tq(q: np.ndarray, k_packed: np.ndarray, k_norms: np.ndarray,
                        k_rotation: np.ndarray, v_rotation: np.ndarray, k_centroids: np.ndarray,
                        v_centroids: np.ndarray, key_bits: int, value_bits: int, num_kv_heads: int) -> np.ndarray:
     """The statement of ``attention_paged_tq_kernel`` (``backends/fracture-cuda/kernels/
-    attention_paged_tq.cu:56-280``) in float64, for one sequence.
+    attention_paged_tq.cu:56-257``) in float64, for one sequence.
 
     ``q [N, Hq, d]`` (values); pools ``[rows, Hkv * P]`` uint8 with norms ``[rows, Hkv]`` (values)
     addressed by ``block_table[pos // 16] * 16 + pos % 16``. Query token t attends positions
