@@ -13,6 +13,8 @@
 //                chunk's softmax maximum and sum, then warp w accumulates its 32 positions'
 //                value rows (lane l: coordinates 4l..4l+3, one coalesced 8-byte load per
 //                position) for every head; the chunk's (max, sum, acc) go to the workspace
+//   kvp_mma      (queries 16-byte aligned, i.e. always through the Python and backend layers)
+//                replaces kvp_chunk: tensor cores, persistent CTAs, 512-position chunks; see below
 //   kvp_combine  rescales and sums the chunks of each query token and head and divides
 //   kvp_append   writes new key/value rows into the pool through the block table
 //
@@ -47,6 +49,7 @@ struct Args {
     int kv_len, start;
     float* part;  // [rows, hq, nch, PART]
     int nch;
+    int ch;  // positions per chunk
     void* out;
 };
 
@@ -63,6 +66,16 @@ struct PoolRows {
         vr = v + o;
         return true;
     }
+    // Rows of block blk inside the pool (16 unless the pool ends inside the block).
+    __device__ int block_rows(int32_t blk) const {
+        return (int)max((int64_t)0, min((int64_t)16, pool_rows - (int64_t)blk * 16));
+    }
+    // KV head g of row `off` of block blk: at kb + off * hkv * D * esz (the same for V).
+    __device__ void block_base(int32_t blk, int g, int hkv, int esz, const uint8_t*& kb, const uint8_t*& vb) const {
+        const int64_t o = ((int64_t)blk * 16 * hkv + g) * (int64_t)D * esz;
+        kb = k + o;
+        vb = v + o;
+    }
 };
 struct BlockPtrRows {
     const uint8_t* const* k;
@@ -72,6 +85,11 @@ struct BlockPtrRows {
         kr = k[blk] + o;
         vr = v[blk] + o;
         return true;
+    }
+    __device__ int block_rows(int32_t) const { return 16; }
+    __device__ void block_base(int32_t blk, int g, int, int esz, const uint8_t*& kb, const uint8_t*& vb) const {
+        kb = k[blk] + (int64_t)g * D * esz;
+        vb = v[blk] + (int64_t)g * D * esz;
     }
 };
 
@@ -249,7 +267,7 @@ __global__ void __launch_bounds__(128) kvp_combine(Args a) {
     const int row = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
     const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
     const int L = causal_len(a, s, t);
-    const int nc = (L + CH - 1) / CH;
+    const int nc = min((L + a.ch - 1) / a.ch, a.nch);  // kv_lens past max_kv_len: the chunks computed
     const float* ph = a.part + ((int64_t)row * a.hq + h) * a.nch * PART;
     float M = -INFINITY;
 #pragma unroll 8
@@ -267,6 +285,274 @@ __global__ void __launch_bounds__(128) kvp_combine(Args a) {
     }
     const float o = l > 0.0f ? v / l : 0.0f;
     ((T*)a.out)[((int64_t)row * a.hq + h) * D + i] = from_f32<T>(o);
+}
+
+// ── tensor-core path ──
+//
+// One work item = (512-position chunk, KV head, query token); persistent CTAs take items in
+// turn. Warp w takes positions 64w..64w+63 of the chunk as four 16-position tiles, one after the
+// other with its own running softmax (maximum, sum, accumulator) per head, and does both
+// contractions with mma.sync m16n8k16 (16-bit operands, FP32 accumulators) on operands loaded
+// straight into registers:
+//
+//   scores   S[16 positions x 8 heads] = K_tile . Q^T: lane (r, t) = (lane / 4, lane % 4) loads
+//            coordinates 32t..32t+31 of key rows r and r + 8 (four 16-byte loads each); the k
+//            index 2t+e of step kk stands for coordinate 32t + 4kk + e (+2 for the upper half),
+//            and the B registers hold the query of head r at the same coordinates.
+//   values   acc^T[128 dims x 8 heads] += V_tile^T . P: lane (r, t) loads coordinates
+//            16r..16r+15 of value rows 2t, 2t+1, 2t+8, 2t+9 and pairs the two positions of one
+//            coordinate into an A register with a byte permute; the weights P go through shared
+//            memory and come back transposed (ldmatrix .trans) as B registers. BF16 weights are
+//            split into a high and a low part (two MMAs), which keeps them to FP32 accuracy.
+//
+// At the end of an item the warps' (maximum, sum, accumulator) are rescaled to the item's
+// maximum and added in warp order.
+
+namespace tc {
+constexpr int TILE = 16, TPW = 4, CHM = NWARPS * TPW * TILE;  // 512 positions per item
+
+struct Smem {
+    static constexpr int acc_off = 0;                                  // [NWARPS][8][D] f32
+    static constexpr int p_off = acc_off + NWARPS * 8 * D * 4;         // [NWARPS][2][16][8] 16-bit
+    static constexpr int mx_off = p_off + NWARPS * 2 * TILE * 8 * 2;   // [NWARPS][8] f32
+    static constexpr int l_off = mx_off + NWARPS * 8 * 4;              // [NWARPS][8] f32
+    static constexpr int bytes = l_off + NWARPS * 8 * 4;
+};
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    if constexpr (dtype_of<T>::value == FB_BF16) {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    } else {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
+}
+
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t& r0, uint32_t& r1, uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr)
+                 : "memory");
+}
+
+// Two floats as a 16-bit pair of type T (x in the low half), and what rounding left over.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float x, float y, float& rx, float& ry) {
+    if constexpr (dtype_of<T>::value == FB_BF16) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+        const float2 back = __bfloat1622float2(h);
+        rx = x - back.x;
+        ry = y - back.y;
+        return *reinterpret_cast<const uint32_t*>(&h);
+    } else {
+        const __half2 h = __floats2half2_rn(x, y);
+        rx = ry = 0.0f;
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float x, float y) {
+    float rx, ry;
+    return pack2<T>(x, y, rx, ry);
+}
+
+}  // namespace tc
+
+template <typename T, typename Rows>
+__global__ void __launch_bounds__(THREADS, 2) kvp_mma(Args a, Rows rw, int items) {
+    using namespace tc;
+    constexpr bool SPLIT = dtype_of<T>::value == FB_BF16;
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, r = lane >> 2, t = lane & 3;
+    const int GA = a.hq / a.hkv;
+    float* accs = (float*)(sm + Smem::acc_off);
+    uint16_t* pb = (uint16_t*)(sm + Smem::p_off) + warp * 2 * TILE * 8;
+    float* rmx = (float*)(sm + Smem::mx_off);
+    float* rl = (float*)(sm + Smem::l_off);
+    const float scale = rsqrtf((float)D);
+    const int64_t rst = (int64_t)a.hkv * D * (int64_t)sizeof(T);  // bytes between a block's rows
+
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int c = item % a.nch, rest = item / a.nch, g = rest % a.hkv, row = rest / a.hkv;
+        const int s = row / a.q_per_seq, tq = row - s * a.q_per_seq;
+        const int L = causal_len(a, s, tq);
+        const int p0 = c * CHM;
+        if (p0 >= L) continue;  // the whole CTA
+
+        // B registers of the score MMA: the query of head r (zeros past the group),
+        // coordinates 32t + 2j, 32t + 2j + 1 in register j
+        uint32_t qh[16];
+        {
+            const uint4* qp = (const uint4*)((const T*)a.q + ((int64_t)row * a.hq + g * GA + min(r, GA - 1)) * D + 32 * t);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint4 u = r < GA ? __ldg(qp + j) : make_uint4(0, 0, 0, 0);
+                qh[4 * j] = u.x;
+                qh[4 * j + 1] = u.y;
+                qh[4 * j + 2] = u.z;
+                qh[4 * j + 3] = u.w;
+            }
+        }
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // heads 2t, 2t + 1
+        float acc[8][4];
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
+
+        const int pw = p0 + warp * TPW * TILE;
+#pragma unroll 1
+        for (int i = 0; i < TPW; ++i) {
+            const int ps = pw + i * TILE;
+            if (ps >= L || (ps >> 4) >= a.max_blocks) break;
+            const int32_t blk = a.block_tables[(int64_t)s * a.max_blocks + (ps >> 4)];
+            if (blk < 0) continue;
+            const int n = min(min(TILE, L - ps), rw.block_rows(blk));
+            if (n <= 0) continue;
+            const uint8_t *kb, *vb;
+            rw.block_base(blk, g, a.hkv, (int)sizeof(T), kb, vb);
+
+            uint32_t kw[2][16], vw[4][8];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int off = r + 8 * h;
+                const uint4* p = (const uint4*)(kb + off * rst + 64 * t);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint4 u = off < n ? __ldg(p + j) : make_uint4(0, 0, 0, 0);
+                    kw[h][4 * j] = u.x;
+                    kw[h][4 * j + 1] = u.y;
+                    kw[h][4 * j + 2] = u.z;
+                    kw[h][4 * j + 3] = u.w;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int off = 2 * t + (u & 1) + 8 * (u >> 1);
+                const uint4* p = (const uint4*)(vb + off * rst + 32 * r);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const uint4 x = off < n ? __ldg(p + j) : make_uint4(0, 0, 0, 0);
+                    vw[u][4 * j] = x.x;
+                    vw[u][4 * j + 1] = x.y;
+                    vw[u][4 * j + 2] = x.z;
+                    vw[u][4 * j + 3] = x.w;
+                }
+            }
+
+            // scores of the tile
+            float c4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+                mma16816<T>(c4, kw[0][2 * kk], kw[1][2 * kk], kw[0][2 * kk + 1], kw[1][2 * kk + 1], qh[2 * kk],
+                            qh[2 * kk + 1]);
+            const float s0 = r < n ? c4[0] * scale : -INFINITY, s1 = r < n ? c4[1] * scale : -INFINITY;
+            const float s2 = r + 8 < n ? c4[2] * scale : -INFINITY, s3 = r + 8 < n ? c4[3] * scale : -INFINITY;
+
+            // running softmax: the tile's maximum per head (row 0 of the tile is in range)
+            float t0 = fmaxf(s0, s2), t1 = fmaxf(s1, s3);
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
+                t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
+            }
+            if (t0 > m0 || t1 > m1) {
+                const float f0 = t0 > m0 ? __expf(m0 - t0) : 1.0f, f1 = t1 > m1 ? __expf(m1 - t1) : 1.0f;
+                m0 = fmaxf(m0, t0);
+                m1 = fmaxf(m1, t1);
+                l0 *= f0;
+                l1 *= f1;
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    acc[mt][0] *= f0;
+                    acc[mt][2] *= f0;
+                    acc[mt][1] *= f1;
+                    acc[mt][3] *= f1;
+                }
+            }
+            const float e0 = __expf(s0 - m0), e1 = __expf(s1 - m1), e2 = __expf(s2 - m0), e3 = __expf(s3 - m1);
+            l0 += e0 + e2;
+            l1 += e1 + e3;
+
+            // weights -> B registers (transposed through shared memory)
+            __syncwarp();
+            {
+                uint32_t* pr = (uint32_t*)(pb + r * 8 + 2 * t);
+                float x0, x1, x2, x3;
+                pr[0] = pack2<T>(e0, e1, x0, x1);
+                pr[32] = pack2<T>(e2, e3, x2, x3);  // row r + 8
+                if constexpr (SPLIT) {
+                    pr[64] = pack2<T>(x0, x1);  // the low parts, rows 16..31
+                    pr[96] = pack2<T>(x2, x3);
+                }
+            }
+            __syncwarp();
+            uint32_t b0, b1, b2 = 0u, b3 = 0u;
+            ldsm_x2_trans(b0, b1, (uint32_t)__cvta_generic_to_shared(pb + (lane & 15) * 8));
+            if constexpr (SPLIT) ldsm_x2_trans(b2, b3, (uint32_t)__cvta_generic_to_shared(pb + (16 + (lane & 15)) * 8));
+
+            // values: A register = one coordinate at two adjacent positions
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                const uint32_t a0 = __byte_perm(vw[0][mt], vw[1][mt], 0x5410u);
+                const uint32_t a1 = __byte_perm(vw[0][mt], vw[1][mt], 0x7632u);
+                const uint32_t a2 = __byte_perm(vw[2][mt], vw[3][mt], 0x5410u);
+                const uint32_t a3 = __byte_perm(vw[2][mt], vw[3][mt], 0x7632u);
+                mma16816<T>(acc[mt], a0, a1, a2, a3, b0, b1);
+                if constexpr (SPLIT) mma16816<T>(acc[mt], a0, a1, a2, a3, b2, b3);
+            }
+        }
+
+        // ── the warps' results, rescaled to the item's maximum and added in warp order ──
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+        }
+        if (r == 0) {
+            rmx[warp * 8 + 2 * t] = m0;
+            rmx[warp * 8 + 2 * t + 1] = m1;
+            rl[warp * 8 + 2 * t] = l0;
+            rl[warp * 8 + 2 * t + 1] = l1;
+        }
+        {
+            float* a0 = accs + (warp * 8 + 2 * t) * D + 16 * r;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                *(float2*)(a0 + 2 * mt) = make_float2(acc[mt][0], acc[mt][2]);
+                *(float2*)(a0 + D + 2 * mt) = make_float2(acc[mt][1], acc[mt][3]);
+            }
+        }
+        __syncthreads();
+        float* part = a.part + (((int64_t)row * a.hq + g * GA) * a.nch + c) * PART;
+        for (int e = tid; e < GA * D; e += THREADS) {
+            const int h = e / D, i = e - h * D;
+            float M = rmx[h];
+#pragma unroll
+            for (int w = 1; w < NWARPS; ++w) M = fmaxf(M, rmx[w * 8 + h]);
+            float v = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NWARPS; ++w) {
+                const float mw = rmx[w * 8 + h];
+                if (mw > -INFINITY) v = fmaf(accs[(w * 8 + h) * D + i], __expf(mw - M), v);
+            }
+            part[(int64_t)h * a.nch * PART + 2 + i] = v;
+            if (i == 0) {
+                float l = 0.0f;
+#pragma unroll
+                for (int w = 0; w < NWARPS; ++w) {
+                    const float mw = rmx[w * 8 + h];
+                    if (mw > -INFINITY) l = fmaf(rl[w * 8 + h], __expf(mw - M), l);
+                }
+                part[(int64_t)h * a.nch * PART] = M;
+                part[(int64_t)h * a.nch * PART + 1] = l;
+            }
+        }
+        __syncthreads();  // the next item rewrites the shared sums
+    }
 }
 
 // Token t of the call goes to pool row block_table[(start + t) / 16] * 16 + (start + t) % 16 (a
@@ -304,10 +590,46 @@ int launch_chunk(const Args& a, const Rows& rw, cudaStream_t s) {
 }
 
 template <typename T, typename Rows>
-int run_t(const Args& a, const Rows& rw, cudaStream_t s) {
+int launch_tc(const Args& a, const Rows& rw, cudaStream_t s) {
+    constexpr int smem = tc::Smem::bytes;
+    auto kern = kvp_mma<T, Rows>;
+    static int slots[64];  // CTAs per device, found on the first launch on that device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    if (slots[dev] == 0) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return (int)e;
+        int per_sm = 0, sms = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, THREADS, smem);
+        if (e != cudaSuccess) return (int)e;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return (int)e;
+        if (per_sm < 1) return (int)cudaErrorInvalidConfiguration;
+        slots[dev] = per_sm * sms;
+    }
+    const int64_t items = (int64_t)a.nch * a.hkv * a.num_seqs * a.q_per_seq;
+    if (items > INT32_MAX) return (int)cudaErrorInvalidValue;
+    kern<<<(int)std::min<int64_t>(items, slots[dev]), THREADS, smem, s>>>(a, rw, (int)items);
+    return (int)cudaGetLastError();
+}
+
+template <typename T, typename Rows>
+int run_t(Args a, const Rows& rw, cudaStream_t s) {
     const int rows = a.num_seqs * a.q_per_seq;
     if (rows == 0) return 0;
-    if (a.nch > 0) {
+    a.ch = CH;
+    // the tensor-core kernel reads the queries 16 bytes at a time; a.nch counts CH-position
+    // chunks (the workspace is sized for them), the tensor-core kernel takes CHM-position ones
+    if (aligned16(a.q)) {
+        a.ch = tc::CHM;
+        a.nch = (int)(((int64_t)a.nch * CH + tc::CHM - 1) / tc::CHM);
+        if (a.nch > 0) {
+            const int rc = launch_tc<T>(a, rw, s);
+            if (rc) return rc;
+        }
+    } else if (a.nch > 0) {
         const int rc = a.hq / a.hkv <= 4 ? launch_chunk<T, 4>(a, rw, s) : launch_chunk<T, 8>(a, rw, s);
         if (rc) return rc;
     }

@@ -21,6 +21,9 @@
 //                   the softmax sum and rotates back with Pi_v^T (thread i: output i, column
 //                   i of Pi_v read once for the whole group)
 //
+// With 2- or 4-bit keys and values, tqa_mma (tensor cores, below) replaces tqa_chunk: same
+// split-K partials, 512-position chunks. 3- and 8-bit codes take tqa_chunk.
+//
 // Each KV head's codes are read once per query token for its whole group of Q heads. A
 // position whose block-table entry is negative, or whose pool row is out of range, is left
 // out; a query token with no position gives zeros.
@@ -60,6 +63,7 @@ struct AttnArgs {
     float* qrot;  // [rows, hq, D]
     float* part;  // [rows, hq, nch, PART]
     int nch;
+    int ch;  // positions per chunk
     void* out;
 };
 
@@ -82,6 +86,20 @@ struct PoolAddr {
         vnorm = __half2float(vn[hr]);
         return true;
     }
+    // Rows of block blk that lie inside the pool (16 unless the pool ends inside the block).
+    __device__ int block_rows(int32_t blk) const {
+        return (int)max((int64_t)0, min((int64_t)16, pool_rows - (int64_t)blk * 16));
+    }
+    // KV head g of row `off` of block blk: K codes at kb + off * hkv * pk, its norm at
+    // knb[off * hkv]; the same for V.
+    __device__ void block_base(int32_t blk, int g, int hkv, int pk, int pv, const uint8_t*& kb, const uint8_t*& vb,
+                               const __half*& knb, const __half*& vnb) const {
+        const int64_t hr = (int64_t)blk * 16 * hkv + g;
+        kb = kp + hr * pk;
+        vb = vp + hr * pv;
+        knb = kn + hr;
+        vnb = vn + hr;
+    }
 };
 
 // The reference's per-block tensors (attention_paged_tq.cu:123-129): block b's packed K rows
@@ -99,6 +117,14 @@ struct BlockPtrAddr {
         knorm = __half2float(kn[blk][hr]);
         vnorm = __half2float(vn[blk][hr]);
         return true;
+    }
+    __device__ int block_rows(int32_t) const { return 16; }
+    __device__ void block_base(int32_t blk, int g, int hkv, int pk, int pv, const uint8_t*& kb, const uint8_t*& vb,
+                               const __half*& knb, const __half*& vnb) const {
+        kb = kp[blk] + g * pk;
+        vb = vp[blk] + g * pv;
+        knb = kn[blk] + g;
+        vnb = vn[blk] + g;
     }
 };
 
@@ -412,7 +438,7 @@ __global__ void __launch_bounds__(128) tqa_combine(AttnArgs a) {
     const int row = blockIdx.x, g = blockIdx.y, G = a.hq / a.hkv, i = threadIdx.x;
     const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
     const int L = causal_len(a, s, t);
-    const int nc = (L + CH - 1) / CH;
+    const int nc = min((L + a.ch - 1) / a.ch, a.nch);  // kv_lens past max_kv_len: the chunks computed
     for (int h = 0; h < G; ++h) {
         const float* ph = a.part + ((int64_t)row * a.hq + g * G + h) * a.nch * PART;
         float M = -INFINITY;
@@ -449,6 +475,324 @@ __global__ void __launch_bounds__(128) tqa_combine(AttnArgs a) {
     }
 }
 
+// ── tensor-core path: 2- and 4-bit keys and values ──
+//
+// One work item = (512-position chunk, KV head, query token); a persistent CTA takes items
+// in turn and builds its decoding tables once. Warp w takes positions 64w..64w+63 of the
+// chunk as four 16-position tiles and does both contractions with mma.sync m16n8k16 (FP16
+// operands, FP32 accumulators), the operands decoded in registers:
+//
+//   scores   S[16 positions x 8 heads] = K_tile[16 x 128] . Q^T: lane (r, t) = (lane / 4,
+//            lane % 4) reads bytes of rows r and r + 8 holding code pairs 16t..16t+15 and
+//            turns each pair into an A register with one table lookup (pair -> half2); the
+//            MMA's k index 2t+e of step kk stands for coordinate 32t + 4kk + e (+2 for the
+//            upper half), and the B registers hold q_rot of head r at the same coordinates.
+//   values   acc^T[128 dims x 8 heads] += V_tile^T[128 x 16 positions] . P[16 x 8]: lane
+//            (r, t) owns dims 16r..16r+15 (MMA m-tile mt: rows r and r + 8 are dims 16r + 2mt
+//            and 16r + 2mt + 1) and positions 2t, 2t+1, 2t+8, 2t+9; an A register holds one
+//            dim at two adjacent positions, so the V table is indexed by the codes of the two
+//            positions (cross-position pairs). The weights P go through shared memory and come
+//            back transposed (ldmatrix .trans) as B registers.
+//
+// Table lookups: entry e at byte 256e, 32 lane-private copies of the K pair value at
+// 256e + 4 lane and of the V pair value at 256e + 128 + 4 lane, so the address is one byte
+// permute of the code byte and the lane offset, and a warp's lookups hit 32 banks.
+
+namespace tc {
+constexpr int TILE = 16, TPW = 4, CHM = NWARPS * TPW * TILE;  // 512 positions per item
+
+template <int KB, int VB>
+struct Smem {
+    static constexpr int ke = 1 << (2 * KB), ve = 1 << (2 * VB);
+    static constexpr int entries = ke > ve ? ke : ve;
+    static constexpr int acc_off = entries * 256;                       // [NWARPS][8][D] f32
+    static constexpr int p_off = acc_off + NWARPS * 8 * D * 4;          // [NWARPS][TPW][16][8] f16
+    static constexpr int mx_off = p_off + NWARPS * TPW * TILE * 8 * 2;  // [NWARPS][8] f32
+    static constexpr int l_off = mx_off + NWARPS * 8 * 4;               // [NWARPS][8] f32
+    static constexpr int bytes = l_off + NWARPS * 8 * 4;
+};
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t& r0, uint32_t& r1, uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float x, float y) {
+    const __half2 h = __floats2half2_rn(x, y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Table address of the code byte b of word w: (byte << 8) | off, off = lane offset (< 256).
+__device__ __forceinline__ uint32_t taddr(uint32_t w, uint32_t off, int b) {
+    return __byte_perm(w, off, 0x5504u | ((uint32_t)b << 4));
+}
+
+}  // namespace tc
+
+template <int KB, int VB, typename Addr>
+__global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int items) {
+    using namespace tc;
+    using S = Smem<KB, VB>;
+    constexpr int PK = D * KB / 8, PV = D * VB / 8;
+    constexpr int KW = PK / 16;  // 32-bit words of a K row per lane (rows are split in four)
+    constexpr int VW = PV / 32;  // 32-bit words of a V row per lane (rows are split in eight)
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, r = lane >> 2, t = lane & 3;
+
+    for (int j = tid; j < S::ke + S::ve; j += THREADS) {
+        const bool key = j < S::ke;
+        const int e = key ? j : j - S::ke, bits = key ? KB : VB;
+        const float* cen = key ? a.ck : a.cv;
+        const uint32_t w = pack_half2(__ldg(cen + (e >> bits)), __ldg(cen + (e & ((1 << bits) - 1))));
+        uint4* row = (uint4*)(sm + e * 256 + (key ? 0 : 128));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) row[(k + j) & 7] = make_uint4(w, w, w, w);
+    }
+    __syncthreads();
+    auto lut = [&](uint32_t addr) { return *reinterpret_cast<const uint32_t*>(sm + addr); };
+
+    const int GA = a.hq / a.hkv;
+    float* accs = (float*)(sm + S::acc_off);
+    __half* pb = (__half*)(sm + S::p_off) + warp * TPW * TILE * 8;
+    float* rmx = (float*)(sm + S::mx_off);
+    float* rl = (float*)(sm + S::l_off);
+    const uint32_t kof = 4u * lane, vof = 128u + 4u * lane;
+    const float rs = rsqrtf((float)D);
+    const int64_t kst = (int64_t)a.hkv * PK, vst = (int64_t)a.hkv * PV;
+
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int c = item % a.nch, rest = item / a.nch, g = rest % a.hkv, row = rest / a.hkv;
+        const int s = row / a.q_per_seq, tq = row - s * a.q_per_seq;
+        const int L = causal_len(a, s, tq);
+        const int p0 = c * CHM;
+        if (p0 >= L) continue;  // the whole CTA
+
+        // B registers of the score MMA: q_rot of head r (zeros past the group), coordinates
+        // 32t + 2j, 32t + 2j + 1 in register j
+        uint32_t qh[16];
+        {
+            const float4* qp = (const float4*)(a.qrot + ((int64_t)row * a.hq + g * GA + min(r, GA - 1)) * D + 32 * t);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 f = __ldg(qp + j);
+                qh[2 * j] = r < GA ? pack_half2(f.x, f.y) : 0u;
+                qh[2 * j + 1] = r < GA ? pack_half2(f.z, f.w) : 0u;
+            }
+        }
+
+        // codes and norms of the warp's four tiles, all requested before any is used
+        const int pw = p0 + warp * TPW * TILE;
+        uint32_t kw[TPW][2][KW], vw[TPW][4][VW];
+        float kn[TPW][2], vn[TPW][2];
+        int nv[TPW];
+#pragma unroll
+        for (int i = 0; i < TPW; ++i) {
+            const int ps = pw + i * TILE;
+            const uint8_t *kb = nullptr, *vb = nullptr;
+            const __half *knb = nullptr, *vnb = nullptr;
+            int n = 0;
+            if (ps < L && (ps >> 4) < a.max_blocks) {
+                const int32_t blk = a.block_tables[(int64_t)s * a.max_blocks + (ps >> 4)];
+                if (blk >= 0) n = min(min(TILE, L - ps), ad.block_rows(blk));
+                if (n > 0) ad.block_base(blk, g, a.hkv, PK, PV, kb, vb, knb, vnb);
+            }
+            nv[i] = n;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int off = r + 8 * h;
+                const bool ok = off < n;
+                if constexpr (KW == 4) {
+                    const uint4 u = ok ? __ldg((const uint4*)(kb + off * kst + 16 * t)) : make_uint4(0, 0, 0, 0);
+                    kw[i][h][0] = u.x;
+                    kw[i][h][1] = u.y;
+                    kw[i][h][2] = u.z;
+                    kw[i][h][3] = u.w;
+                } else {
+                    const uint2 u = ok ? __ldg((const uint2*)(kb + off * kst + 8 * t)) : make_uint2(0, 0);
+                    kw[i][h][0] = u.x;
+                    kw[i][h][1] = u.y;
+                }
+                kn[i][h] = ok ? __half2float(knb[off * a.hkv]) : 0.0f;
+                vn[i][h] = ok ? __half2float(vnb[off * a.hkv]) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int off = 2 * t + (u & 1) + 8 * (u >> 1);
+                const bool ok = off < n;
+                if constexpr (VW == 1) {
+                    vw[i][u][0] = ok ? __ldg((const uint32_t*)(vb + off * vst + 4 * r)) : 0u;
+                } else {
+                    const uint2 x = ok ? __ldg((const uint2*)(vb + off * vst + 8 * r)) : make_uint2(0, 0);
+                    vw[i][u][0] = x.x;
+                    vw[i][u][1] = x.y;
+                }
+            }
+        }
+
+        // ── scores ──
+        float sc[TPW][4];
+#pragma unroll
+        for (int i = 0; i < TPW; ++i) {
+            float c4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (nv[i] > 0) {
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    uint32_t a0, a1, a2, a3;
+                    if constexpr (KB == 4) {  // pair 2kk: byte 2kk of the lane's 16; pair 2kk + 1: the next
+                        const uint32_t w0 = kw[i][0][kk >> 1], w1 = kw[i][1][kk >> 1];
+                        const int b = 2 * (kk & 1);
+                        a0 = lut(taddr(w0, kof, b));
+                        a1 = lut(taddr(w1, kof, b));
+                        a2 = lut(taddr(w0, kof, b + 1));
+                        a3 = lut(taddr(w1, kof, b + 1));
+                    } else {  // pair 2kk: high nibble of byte kk of the lane's 8; pair 2kk + 1: low nibble
+                        const uint32_t w0 = kw[i][0][kk >> 2], w1 = kw[i][1][kk >> 2];
+                        const int b = kk & 3;
+                        a0 = lut(taddr((w0 >> 4) & 0x0f0f0f0fu, kof, b));
+                        a1 = lut(taddr((w1 >> 4) & 0x0f0f0f0fu, kof, b));
+                        a2 = lut(taddr(w0 & 0x0f0f0f0fu, kof, b));
+                        a3 = lut(taddr(w1 & 0x0f0f0f0fu, kof, b));
+                    }
+                    mma16816(c4, a0, a1, a2, a3, qh[2 * kk], qh[2 * kk + 1]);
+                }
+            }
+            const float f0 = kn[i][0] * rs, f1 = kn[i][1] * rs;
+            sc[i][0] = r < nv[i] ? c4[0] * f0 : -INFINITY;
+            sc[i][1] = r < nv[i] ? c4[1] * f0 : -INFINITY;
+            sc[i][2] = r + 8 < nv[i] ? c4[2] * f1 : -INFINITY;
+            sc[i][3] = r + 8 < nv[i] ? c4[3] * f1 : -INFINITY;
+        }
+
+        // ── softmax over the item: maximum per head, weights exp(s - max) * v_norm ──
+        float m0 = -INFINITY, m1 = -INFINITY;  // heads 2t, 2t + 1
+#pragma unroll
+        for (int i = 0; i < TPW; ++i) {
+            m0 = fmaxf(m0, fmaxf(sc[i][0], sc[i][2]));
+            m1 = fmaxf(m1, fmaxf(sc[i][1], sc[i][3]));
+        }
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+            m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+        }
+        if (r == 0) {
+            rmx[warp * 8 + 2 * t] = m0;
+            rmx[warp * 8 + 2 * t + 1] = m1;
+        }
+        __syncthreads();
+        float M0 = rmx[2 * t], M1 = rmx[2 * t + 1];
+#pragma unroll
+        for (int w = 1; w < NWARPS; ++w) {
+            M0 = fmaxf(M0, rmx[w * 8 + 2 * t]);
+            M1 = fmaxf(M1, rmx[w * 8 + 2 * t + 1]);
+        }
+        const bool any = M0 > -INFINITY;  // some position of the item is in the cache
+        float l0 = 0.0f, l1 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < TPW; ++i) {
+            const float e0 = any ? __expf(sc[i][0] - M0) : 0.0f, e1 = any ? __expf(sc[i][1] - M1) : 0.0f;
+            const float e2 = any ? __expf(sc[i][2] - M0) : 0.0f, e3 = any ? __expf(sc[i][3] - M1) : 0.0f;
+            l0 += e0 + e2;
+            l1 += e1 + e3;
+            uint32_t* pr = (uint32_t*)(pb + (i * TILE + r) * 8 + 2 * t);
+            pr[0] = pack_half2(e0 * vn[i][0], e1 * vn[i][0]);
+            pr[8 * 4] = pack_half2(e2 * vn[i][1], e3 * vn[i][1]);  // row r + 8
+        }
+        __syncwarp();
+
+        // ── values ──
+        float acc[8][4];
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < TPW; ++i) {
+            if (nv[i] == 0) continue;
+            uint32_t b0, b1;
+            ldsm_x2_trans(b0, b1, (uint32_t)__cvta_generic_to_shared(pb + (i * TILE + (lane & 15)) * 8));
+            if constexpr (VB == 2) {
+                // X[j] byte q: (code of dim 4q + j at position 2t) << 2 | (same dim at 2t + 1);
+                // Y[j]: positions 2t + 8, 2t + 9
+                uint32_t X[4], Y[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int sh = 6 - 2 * j;
+                    X[j] = ((vw[i][0][0] >> sh << 2) & 0x0c0c0c0cu) | ((vw[i][1][0] >> sh) & 0x03030303u);
+                    Y[j] = ((vw[i][2][0] >> sh << 2) & 0x0c0c0c0cu) | ((vw[i][3][0] >> sh) & 0x03030303u);
+                }
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    const int b = mt >> 1, j0 = 2 * (mt & 1);
+                    mma16816(acc[mt], lut(taddr(X[j0], vof, b)), lut(taddr(X[j0 + 1], vof, b)),
+                             lut(taddr(Y[j0], vof, b)), lut(taddr(Y[j0 + 1], vof, b)), b0, b1);
+                }
+            } else {
+                // H[u] byte q: (high nibble of byte 4u + q at position 2t) << 4 | (same at 2t + 1),
+                // the dim 2(4u + q); L[u]: low nibbles, dim 2(4u + q) + 1; H2/L2: positions 2t + 8, 2t + 9
+                uint32_t H[2], Lo[2], H2[2], L2[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    H[u] = (vw[i][0][u] & 0xf0f0f0f0u) | ((vw[i][1][u] >> 4) & 0x0f0f0f0fu);
+                    Lo[u] = ((vw[i][0][u] << 4) & 0xf0f0f0f0u) | (vw[i][1][u] & 0x0f0f0f0fu);
+                    H2[u] = (vw[i][2][u] & 0xf0f0f0f0u) | ((vw[i][3][u] >> 4) & 0x0f0f0f0fu);
+                    L2[u] = ((vw[i][2][u] << 4) & 0xf0f0f0f0u) | (vw[i][3][u] & 0x0f0f0f0fu);
+                }
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    const int u = mt >> 2, b = mt & 3;
+                    mma16816(acc[mt], lut(taddr(H[u], vof, b)), lut(taddr(Lo[u], vof, b)), lut(taddr(H2[u], vof, b)),
+                             lut(taddr(L2[u], vof, b)), b0, b1);
+                }
+            }
+        }
+
+        // ── the warps' sums, added in warp order ──
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+        }
+        if (r == 0) {
+            rl[warp * 8 + 2 * t] = l0;
+            rl[warp * 8 + 2 * t + 1] = l1;
+        }
+        {
+            float* a0 = accs + (warp * 8 + 2 * t) * D + 16 * r;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                *(float2*)(a0 + 2 * mt) = make_float2(acc[mt][0], acc[mt][2]);
+                *(float2*)(a0 + D + 2 * mt) = make_float2(acc[mt][1], acc[mt][3]);
+            }
+        }
+        __syncthreads();
+        float* part = a.part + (((int64_t)row * a.hq + g * GA) * a.nch + c) * PART;
+        for (int e = tid; e < GA * D; e += THREADS) {
+            const int h = e / D, i = e - h * D;
+            float v = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NWARPS; ++w) v += accs[(w * 8 + h) * D + i];
+            part[(int64_t)h * a.nch * PART + 2 + i] = v;
+        }
+        if (tid < GA) {
+            float m = rmx[tid], l = rl[tid];
+            for (int w = 1; w < NWARPS; ++w) {
+                m = fmaxf(m, rmx[w * 8 + tid]);
+                l += rl[w * 8 + tid];
+            }
+            float* ph = part + (int64_t)tid * a.nch * PART;
+            ph[0] = m;
+            ph[1] = l;
+        }
+        __syncthreads();  // the next item rewrites the maxima and sums
+    }
+}
+
 size_t workspace_bytes(int64_t rows, int hq, int nch) {
     return (size_t)rows * hq * D * 4 + (size_t)rows * hq * nch * PART * 4;
 }
@@ -480,14 +824,59 @@ int dispatch_vb(const AttnArgs& a, int vb, const Addr& ad, cudaStream_t s) {
     }
 }
 
+// One CTA per SM slot, each walking the items (chunk, KV head, query token) in turn.
+template <int KB, int VB, typename Addr>
+int launch_tc(const AttnArgs& a, const Addr& ad, cudaStream_t s) {
+    constexpr int smem = tc::Smem<KB, VB>::bytes;
+    auto kern = tqa_mma<KB, VB, Addr>;
+    static int slots[64];  // CTAs per device, found on the first launch on that device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    if (slots[dev] == 0) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return (int)e;
+        int per_sm = 0, sms = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, THREADS, smem);
+        if (e != cudaSuccess) return (int)e;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return (int)e;
+        if (per_sm < 1) return (int)cudaErrorInvalidConfiguration;
+        slots[dev] = per_sm * sms;
+    }
+    const int64_t items = (int64_t)a.nch * a.hkv * a.num_seqs * a.q_per_seq;
+    if (items > INT32_MAX) return (int)cudaErrorInvalidValue;
+    const int grid = (int)std::min<int64_t>(items, slots[dev]);
+    kern<<<grid, THREADS, smem, s>>>(a, ad, (int)items);
+    return (int)cudaGetLastError();
+}
+
+template <int KB, typename Addr>
+int dispatch_tc(const AttnArgs& a, int vb, const Addr& ad, cudaStream_t s) {
+    return vb == 2 ? launch_tc<KB, 2>(a, ad, s) : launch_tc<KB, 4>(a, ad, s);
+}
+
+bool tc_ok(int kb, int vb) { return (kb == 2 || kb == 4) && (vb == 2 || vb == 4); }
+
 template <typename Addr>
-int run(const AttnArgs& a, int kb, int vb, const Addr& ad, cudaStream_t s) {
+int run(AttnArgs a, int kb, int vb, const Addr& ad, cudaStream_t s) {
     const int rows = a.num_seqs * a.q_per_seq;
     if (rows == 0) return 0;
     tqa_rotate_q<<<dim3(rows, a.hkv), 128, 0, s>>>(a);
     int rc = (int)cudaGetLastError();
     if (rc) return rc;
-    if (a.nch > 0) {
+    // a.nch counts CH-position chunks (the workspace is sized for them); the tensor-core
+    // path takes CHM-position chunks, so it uses fewer of the same partial slots
+    a.ch = CH;
+    if (tc_ok(kb, vb)) {
+        a.ch = tc::CHM;
+        a.nch = (int)(((int64_t)a.nch * CH + tc::CHM - 1) / tc::CHM);
+        if (a.nch > 0) {
+            rc = kb == 2 ? dispatch_tc<2>(a, vb, ad, s) : dispatch_tc<4>(a, vb, ad, s);
+            if (rc) return rc;
+        }
+    } else if (a.nch > 0) {
         switch (kb) {
             case 2: rc = dispatch_vb<2>(a, vb, ad, s); break;
             case 3: rc = dispatch_vb<3>(a, vb, ad, s); break;

@@ -156,3 +156,35 @@ def test_reference_kernel_meets_the_bar_against_the_statement():
     got = _reference_abi(ref, c, q[0], kv_len, kv_len - Tq).float().cpu().numpy()
     ops.assert_close_fp(got, ops.attention_paged(qh[0], c["hk"], c["hv"], c["tables"][0], kv_len, kv_len - Tq),
                         rel=2e-3, min_cos=0.9999, label="reference kernel", dtype="f16")
+
+
+def test_chunk_boundaries_and_more_items_than_ctas():
+    """Contexts at and around the 512-position chunk edge and several chunks long, 40 prefill
+    query tokens per sequence: more (chunk, KV head, token) items than the persistent grid has
+    CTAs."""
+    kv_lens, Tq, Hkv, G = [511, 512, 513, 1537], 40, 2, 4
+    c = build_cache(kv_lens, Hkv, "bf16", seed=11)
+    qh, q = make_q(len(kv_lens), Tq, G * Hkv, "bf16", seed=12)
+    starts = [L - Tq for L in kv_lens]
+    got = run_ours(c, q, kv_lens, starts).float().cpu().numpy()
+    for s, L in enumerate(kv_lens):
+        ref = ops.attention_paged(qh[s], c["hk"], c["hv"], c["tables"][s], L, starts[s])
+        ops.assert_close_fp(got[s], ref, rel=2e-3, min_cos=0.9999, label=f"seq {s} (kv {L})", dtype="bf16")
+
+
+def test_unaligned_queries_take_the_cuda_core_kernel():
+    """Queries that do not start on a 16-byte boundary go through the CUDA-core kernel (the
+    tensor-core kernel reads them 16 bytes at a time); both meet the bar."""
+    kv_lens, Hkv, G = [300, 700], 2, 4
+    c = build_cache(kv_lens, Hkv, "f16", seed=13)
+    qh, q = make_q(2, 1, G * Hkv, "f16", seed=14)
+    buf = torch.empty(q.numel() + 1, dtype=q.dtype, device=DEV)
+    q_odd = buf[1:].view(q.shape)
+    q_odd.copy_(q)
+    assert q_odd.data_ptr() % 16 != 0
+    starts = [L - 1 for L in kv_lens]
+    for qq in (q, q_odd):
+        got = run_ours(c, qq, kv_lens, starts).float().cpu().numpy()
+        for s, L in enumerate(kv_lens):
+            ref = ops.attention_paged(qh[s], c["hk"], c["hv"], c["tables"][s], L, starts[s])
+            ops.assert_close_fp(got[s], ref, rel=2e-3, min_cos=0.9999, label=f"seq {s}", dtype="f16")
