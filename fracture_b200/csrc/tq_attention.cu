@@ -18,8 +18,8 @@
 //                   group) from the V rows staged in shared memory; the chunk's (max, sum,
 //                   acc) go to the workspace (split-K over the causal range)
 //   tqa_combine     rescales and sums the chunks of each query token and head, divides by
-//                   the softmax sum and rotates back with Pi_v^T (thread i: output i, column
-//                   i of Pi_v read once for the whole group)
+//                   the softmax sum and rotates back with Pi_v^T (thread (h, i): output i of
+//                   head h, column i of Pi_v shared by the group's heads through L1)
 //
 // With 2- or 4-bit keys and values, tqa_mma (tensor cores, below) replaces tqa_chunk: same
 // split-K partials, 512-position chunks. 3- and 8-bit codes take tqa_chunk.
@@ -432,14 +432,16 @@ __global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
     }
 }
 
-// out[row][h][i] = sum_j Pi_v[j][i] * (sum_c acc_c[j] e^(m_c - M)) / (sum_c l_c e^(m_c - M)).
-__global__ void __launch_bounds__(128) tqa_combine(AttnArgs a) {
+// out[row][h][i] = sum_j Pi_v[j][i] * (sum_c acc_c[j] e^(m_c - M)) / (sum_c l_c e^(m_c - M)):
+// thread (h, i), 128 per head of KV group blockIdx.y.
+__global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a) {
     __shared__ float accs[MAXG][D];
-    const int row = blockIdx.x, g = blockIdx.y, G = a.hq / a.hkv, i = threadIdx.x;
+    const int row = blockIdx.x, g = blockIdx.y, G = a.hq / a.hkv;
+    const int h = threadIdx.x / D, i = threadIdx.x - h * D;
     const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
     const int L = causal_len(a, s, t);
     const int nc = min((L + a.ch - 1) / a.ch, a.nch);  // kv_lens past max_kv_len: the chunks computed
-    for (int h = 0; h < G; ++h) {
+    {
         const float* ph = a.part + ((int64_t)row * a.hq + g * G + h) * a.nch * PART;
         float M = -INFINITY;
 #pragma unroll 8
@@ -458,21 +460,17 @@ __global__ void __launch_bounds__(128) tqa_combine(AttnArgs a) {
         accs[h][i] = l > 0.0f ? v / l : 0.0f;
     }
     __syncthreads();
-    float o[MAXG];
-    for (int h = 0; h < G; ++h) o[h] = 0.0f;
+    float o = 0.0f;
     for (int j0 = 0; j0 < D; j0 += 16) {  // sixteen loads of column i in flight at a time
         float p[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k) p[k] = __ldg(a.piv + (j0 + k) * D + i);
-        for (int h = 0; h < G; ++h)
 #pragma unroll
-            for (int k = 0; k < 16; ++k) o[h] = fmaf(p[k], accs[h][j0 + k], o[h]);
+        for (int k = 0; k < 16; ++k) o = fmaf(p[k], accs[h][j0 + k], o);
     }
-    for (int h = 0; h < G; ++h) {
-        const int64_t e = ((int64_t)row * a.hq + g * G + h) * D + i;
-        if (a.dtype == FB_BF16) ((__nv_bfloat16*)a.out)[e] = __float2bfloat16_rn(o[h]);
-        else ((__half*)a.out)[e] = __float2half_rn(o[h]);
-    }
+    const int64_t e = ((int64_t)row * a.hq + g * G + h) * D + i;
+    if (a.dtype == FB_BF16) ((__nv_bfloat16*)a.out)[e] = __float2bfloat16_rn(o);
+    else ((__half*)a.out)[e] = __float2half_rn(o);
 }
 
 // ── tensor-core path: 2- and 4-bit keys and values ──
@@ -885,7 +883,7 @@ int run(AttnArgs a, int kb, int vb, const Addr& ad, cudaStream_t s) {
         }
         if (rc) return rc;
     }
-    tqa_combine<<<dim3(rows, a.hkv), 128, 0, s>>>(a);
+    tqa_combine<<<dim3(rows, a.hkv), (a.hq / a.hkv) * D, 0, s>>>(a);
     return (int)cudaGetLastError();
 }
 
