@@ -291,7 +291,8 @@ __global__ void __launch_bounds__(128) kvp_combine(Args a) {
 //
 // One work item = (512-position chunk, KV head, query token); persistent CTAs take items in
 // turn. Warp w takes positions 64w..64w+63 of the chunk as four 16-position tiles, one after the
-// other with its own running softmax (maximum, sum, accumulator) per head, and does both
+// other (the next tile's rows requested into the registers the current one has finished with)
+// with its own running softmax (maximum, sum, accumulator) per head, and does both
 // contractions with mma.sync m16n8k16 (16-bit operands, FP32 accumulators) on operands loaded
 // straight into registers:
 //
@@ -316,7 +317,8 @@ struct Smem {
     static constexpr int p_off = acc_off + NWARPS * 8 * D * 4;         // [NWARPS][2][16][8] 16-bit
     static constexpr int mx_off = p_off + NWARPS * 2 * TILE * 8 * 2;   // [NWARPS][8] f32
     static constexpr int l_off = mx_off + NWARPS * 8 * 4;              // [NWARPS][8] f32
-    static constexpr int bytes = l_off + NWARPS * 8 * 4;
+    static constexpr int q_off = l_off + NWARPS * 8 * 4;               // [8 steps][32 lanes] uint2
+    static constexpr int bytes = q_off + 8 * 32 * 8;
 };
 
 template <typename T>
@@ -374,6 +376,7 @@ __global__ void __launch_bounds__(THREADS, 2) kvp_mma(Args a, Rows rw, int items
     uint16_t* pb = (uint16_t*)(sm + Smem::p_off) + warp * 2 * TILE * 8;
     float* rmx = (float*)(sm + Smem::mx_off);
     float* rl = (float*)(sm + Smem::l_off);
+    uint2* qf = (uint2*)(sm + Smem::q_off);
     const float scale = rsqrtf((float)D);
     const int64_t rst = (int64_t)a.hkv * D * (int64_t)sizeof(T);  // bytes between a block's rows
 
@@ -384,38 +387,40 @@ __global__ void __launch_bounds__(THREADS, 2) kvp_mma(Args a, Rows rw, int items
         const int p0 = c * CHM;
         if (p0 >= L) continue;  // the whole CTA
 
-        // B registers of the score MMA: the query of head r (zeros past the group),
-        // coordinates 32t + 2j, 32t + 2j + 1 in register j
-        uint32_t qh[16];
+        // B registers of the score MMA, step kk, lane (r, t): the query of head r (zeros past
+        // the group) at coordinates 32t + 4kk .. 32t + 4kk + 3, staged in shared memory in that
+        // order (one conflict-free 8-byte load per lane and step); thread (kk, lane) = (warp, lane)
         {
-            const uint4* qp = (const uint4*)((const T*)a.q + ((int64_t)row * a.hq + g * GA + min(r, GA - 1)) * D + 32 * t);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint4 u = r < GA ? __ldg(qp + j) : make_uint4(0, 0, 0, 0);
-                qh[4 * j] = u.x;
-                qh[4 * j + 1] = u.y;
-                qh[4 * j + 2] = u.z;
-                qh[4 * j + 3] = u.w;
-            }
+            const uint2 u = r < GA ? __ldg((const uint2*)((const T*)a.q + ((int64_t)row * a.hq + g * GA + r) * D +
+                                                          32 * t + 4 * warp))
+                                   : make_uint2(0u, 0u);
+            qf[warp * 32 + lane] = u;
         }
+        __syncthreads();
         float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // heads 2t, 2t + 1
         float acc[8][4];
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
 
         const int pw = p0 + warp * TPW * TILE;
-#pragma unroll 1
+        const int lim = min(L, a.max_blocks * 16);
+        // the warp's tiles: block entry and positions in the cache (a prefix of the 16)
+        int32_t bk[TPW];
+        int nv[TPW];
+#pragma unroll
         for (int i = 0; i < TPW; ++i) {
             const int ps = pw + i * TILE;
-            if (ps >= L || (ps >> 4) >= a.max_blocks) break;
-            const int32_t blk = a.block_tables[(int64_t)s * a.max_blocks + (ps >> 4)];
-            if (blk < 0) continue;
-            const int n = min(min(TILE, L - ps), rw.block_rows(blk));
-            if (n <= 0) continue;
-            const uint8_t *kb, *vb;
-            rw.block_base(blk, g, a.hkv, (int)sizeof(T), kb, vb);
-
-            uint32_t kw[2][16], vw[4][8];
+            const int32_t blk = ps < lim ? __ldg(a.block_tables + (int64_t)s * a.max_blocks + (ps >> 4)) : -1;
+            nv[i] = blk >= 0 ? min(min(TILE, L - ps), rw.block_rows(blk)) : 0;
+            bk[i] = blk;
+        }
+        // Tile i + 1's keys are requested as soon as tile i's scores are done with the key
+        // registers, its values as soon as tile i's values are done with the value registers.
+        uint32_t kw[2][16], vw[4][8];
+        auto load_k = [&](int i) {
+            const int n = nv[i];
+            const uint8_t *kb = nullptr, *vb = nullptr;
+            if (n > 0) rw.block_base(bk[i], g, a.hkv, (int)sizeof(T), kb, vb);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int off = r + 8 * h;
@@ -429,6 +434,11 @@ __global__ void __launch_bounds__(THREADS, 2) kvp_mma(Args a, Rows rw, int items
                     kw[h][4 * j + 3] = u.w;
                 }
             }
+        };
+        auto load_v = [&](int i) {
+            const int n = nv[i];
+            const uint8_t *kb = nullptr, *vb = nullptr;
+            if (n > 0) rw.block_base(bk[i], g, a.hkv, (int)sizeof(T), kb, vb);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int off = 2 * t + (u & 1) + 8 * (u >> 1);
@@ -442,68 +452,80 @@ __global__ void __launch_bounds__(THREADS, 2) kvp_mma(Args a, Rows rw, int items
                     vw[u][4 * j + 3] = x.w;
                 }
             }
-
+        };
+        load_k(0);
+        load_v(0);
+#pragma unroll
+        for (int i = 0; i < TPW; ++i) {
+            const int n = nv[i];
             // scores of the tile
             float c4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (n > 0) {
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-                mma16816<T>(c4, kw[0][2 * kk], kw[1][2 * kk], kw[0][2 * kk + 1], kw[1][2 * kk + 1], qh[2 * kk],
-                            qh[2 * kk + 1]);
-            const float s0 = r < n ? c4[0] * scale : -INFINITY, s1 = r < n ? c4[1] * scale : -INFINITY;
-            const float s2 = r + 8 < n ? c4[2] * scale : -INFINITY, s3 = r + 8 < n ? c4[3] * scale : -INFINITY;
-
-            // running softmax: the tile's maximum per head (row 0 of the tile is in range)
-            float t0 = fmaxf(s0, s2), t1 = fmaxf(s1, s3);
-#pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-                t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
-                t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint2 b = qf[kk * 32 + lane];
+                    mma16816<T>(c4, kw[0][2 * kk], kw[1][2 * kk], kw[0][2 * kk + 1], kw[1][2 * kk + 1], b.x, b.y);
+                }
             }
-            if (t0 > m0 || t1 > m1) {
-                const float f0 = t0 > m0 ? __expf(m0 - t0) : 1.0f, f1 = t1 > m1 ? __expf(m1 - t1) : 1.0f;
-                m0 = fmaxf(m0, t0);
-                m1 = fmaxf(m1, t1);
-                l0 *= f0;
-                l1 *= f1;
+            if (i + 1 < TPW) load_k(i + 1);
+            if (n > 0) {
+                const float s0 = r < n ? c4[0] * scale : -INFINITY, s1 = r < n ? c4[1] * scale : -INFINITY;
+                const float s2 = r + 8 < n ? c4[2] * scale : -INFINITY, s3 = r + 8 < n ? c4[3] * scale : -INFINITY;
+
+                // running softmax: the tile's maximum per head (row 0 of the tile is in range)
+                float t0 = fmaxf(s0, s2), t1 = fmaxf(s1, s3);
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                    t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
+                    t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
+                }
+                if (t0 > m0 || t1 > m1) {
+                    const float f0 = t0 > m0 ? __expf(m0 - t0) : 1.0f, f1 = t1 > m1 ? __expf(m1 - t1) : 1.0f;
+                    m0 = fmaxf(m0, t0);
+                    m1 = fmaxf(m1, t1);
+                    l0 *= f0;
+                    l1 *= f1;
+#pragma unroll
+                    for (int mt = 0; mt < 8; ++mt) {
+                        acc[mt][0] *= f0;
+                        acc[mt][2] *= f0;
+                        acc[mt][1] *= f1;
+                        acc[mt][3] *= f1;
+                    }
+                }
+                const float e0 = __expf(s0 - m0), e1 = __expf(s1 - m1), e2 = __expf(s2 - m0), e3 = __expf(s3 - m1);
+                l0 += e0 + e2;
+                l1 += e1 + e3;
+
+                // weights -> B registers (transposed through shared memory)
+                __syncwarp();
+                {
+                    uint32_t* pr = (uint32_t*)(pb + r * 8 + 2 * t);
+                    float x0, x1, x2, x3;
+                    pr[0] = pack2<T>(e0, e1, x0, x1);
+                    pr[32] = pack2<T>(e2, e3, x2, x3);  // row r + 8
+                    if constexpr (SPLIT) {
+                        pr[64] = pack2<T>(x0, x1);  // the low parts, rows 16..31
+                        pr[96] = pack2<T>(x2, x3);
+                    }
+                }
+                __syncwarp();
+                uint32_t b0, b1, b2 = 0u, b3 = 0u;
+                ldsm_x2_trans(b0, b1, (uint32_t)__cvta_generic_to_shared(pb + (lane & 15) * 8));
+                if constexpr (SPLIT) ldsm_x2_trans(b2, b3, (uint32_t)__cvta_generic_to_shared(pb + (16 + (lane & 15)) * 8));
+
+                // values: A register = one coordinate at two adjacent positions
 #pragma unroll
                 for (int mt = 0; mt < 8; ++mt) {
-                    acc[mt][0] *= f0;
-                    acc[mt][2] *= f0;
-                    acc[mt][1] *= f1;
-                    acc[mt][3] *= f1;
+                    const uint32_t a0 = __byte_perm(vw[0][mt], vw[1][mt], 0x5410u);
+                    const uint32_t a1 = __byte_perm(vw[0][mt], vw[1][mt], 0x7632u);
+                    const uint32_t a2 = __byte_perm(vw[2][mt], vw[3][mt], 0x5410u);
+                    const uint32_t a3 = __byte_perm(vw[2][mt], vw[3][mt], 0x7632u);
+                    mma16816<T>(acc[mt], a0, a1, a2, a3, b0, b1);
+                    if constexpr (SPLIT) mma16816<T>(acc[mt], a0, a1, a2, a3, b2, b3);
                 }
             }
-            const float e0 = __expf(s0 - m0), e1 = __expf(s1 - m1), e2 = __expf(s2 - m0), e3 = __expf(s3 - m1);
-            l0 += e0 + e2;
-            l1 += e1 + e3;
-
-            // weights -> B registers (transposed through shared memory)
-            __syncwarp();
-            {
-                uint32_t* pr = (uint32_t*)(pb + r * 8 + 2 * t);
-                float x0, x1, x2, x3;
-                pr[0] = pack2<T>(e0, e1, x0, x1);
-                pr[32] = pack2<T>(e2, e3, x2, x3);  // row r + 8
-                if constexpr (SPLIT) {
-                    pr[64] = pack2<T>(x0, x1);  // the low parts, rows 16..31
-                    pr[96] = pack2<T>(x2, x3);
-                }
-            }
-            __syncwarp();
-            uint32_t b0, b1, b2 = 0u, b3 = 0u;
-            ldsm_x2_trans(b0, b1, (uint32_t)__cvta_generic_to_shared(pb + (lane & 15) * 8));
-            if constexpr (SPLIT) ldsm_x2_trans(b2, b3, (uint32_t)__cvta_generic_to_shared(pb + (16 + (lane & 15)) * 8));
-
-            // values: A register = one coordinate at two adjacent positions
-#pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
-                const uint32_t a0 = __byte_perm(vw[0][mt], vw[1][mt], 0x5410u);
-                const uint32_t a1 = __byte_perm(vw[0][mt], vw[1][mt], 0x7632u);
-                const uint32_t a2 = __byte_perm(vw[2][mt], vw[3][mt], 0x5410u);
-                const uint32_t a3 = __byte_perm(vw[2][mt], vw[3][mt], 0x7632u);
-                mma16816<T>(acc[mt], a0, a1, a2, a3, b0, b1);
-                if constexpr (SPLIT) mma16816<T>(acc[mt], a0, a1, a2, a3, b2, b3);
-            }
+            if (i + 1 < TPW) load_v(i + 1);
         }
 
         // ── the warps' results, rescaled to the item's maximum and added in warp order ──
