@@ -507,7 +507,8 @@ struct Smem {
     static constexpr int p_off = acc_off + NWARPS * 8 * D * 4;          // [NWARPS][TPW][16][8] f16
     static constexpr int mx_off = p_off + NWARPS * TPW * TILE * 8 * 2;  // [NWARPS][8] f32
     static constexpr int l_off = mx_off + NWARPS * 8 * 4;               // [NWARPS][8] f32
-    static constexpr int bytes = l_off + NWARPS * 8 * 4;
+    static constexpr int q_off = l_off + NWARPS * 8 * 4;              // [8 steps][32 lanes] uint2
+    static constexpr int bytes = q_off + 8 * 32 * 8;
 };
 
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -561,6 +562,7 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
     __half* pb = (__half*)(sm + S::p_off) + warp * TPW * TILE * 8;
     float* rmx = (float*)(sm + S::mx_off);
     float* rl = (float*)(sm + S::l_off);
+    uint2* qf = (uint2*)(sm + S::q_off);
     const uint32_t kof = 4u * lane, vof = 128u + 4u * lane;
     const float rs = rsqrtf((float)D);
     const int64_t kst = (int64_t)a.hkv * PK, vst = (int64_t)a.hkv * PV;
@@ -572,17 +574,15 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
         const int p0 = c * CHM;
         if (p0 >= L) continue;  // the whole CTA
 
-        // B registers of the score MMA: q_rot of head r (zeros past the group), coordinates
-        // 32t + 2j, 32t + 2j + 1 in register j
-        uint32_t qh[16];
+        // B registers of the score MMA, step kk, lane (r, t): q_rot of head r (zeros past the
+        // group) at coordinates 32t + 4kk .. 32t + 4kk + 3 as two half2, staged in shared memory
+        // in that order (one conflict-free 8-byte load per lane and step; the barrier below the
+        // code loads publishes them); thread (kk, lane) = (warp, lane)
         {
-            const float4* qp = (const float4*)(a.qrot + ((int64_t)row * a.hq + g * GA + min(r, GA - 1)) * D + 32 * t);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float4 f = __ldg(qp + j);
-                qh[2 * j] = r < GA ? pack_half2(f.x, f.y) : 0u;
-                qh[2 * j + 1] = r < GA ? pack_half2(f.z, f.w) : 0u;
-            }
+            const float4 f = r < GA ? __ldg((const float4*)(a.qrot + ((int64_t)row * a.hq + g * GA + r) * D + 32 * t +
+                                                            4 * warp))
+                                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            qf[warp * 32 + lane] = make_uint2(pack_half2(f.x, f.y), pack_half2(f.z, f.w));
         }
 
         // codes and norms of the warp's four tiles, all requested before any is used
@@ -634,6 +634,8 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
             }
         }
 
+        __syncthreads();  // the staged query fragments
+
         // ── scores ──
         float sc[TPW][4];
 #pragma unroll
@@ -658,7 +660,8 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
                         a2 = lut(taddr(w0 & 0x0f0f0f0fu, kof, b));
                         a3 = lut(taddr(w1 & 0x0f0f0f0fu, kof, b));
                     }
-                    mma16816(c4, a0, a1, a2, a3, qh[2 * kk], qh[2 * kk + 1]);
+                    const uint2 qb = qf[kk * 32 + lane];
+                    mma16816(c4, a0, a1, a2, a3, qb.x, qb.y);
                 }
             }
             const float f0 = kn[i][0] * rs, f1 = kn[i][1] * rs;
