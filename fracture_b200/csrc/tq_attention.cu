@@ -918,7 +918,7 @@ int tq_attention_one_seq(const void* q, int dtype, int num_tokens, int hq, int h
         return (int)cudaErrorInvalidValue;
     if (num_tokens == 0) return 0;
     if (ws_bytes < tq_attention_ws_bytes(num_tokens, hq, kv_len) || !aligned16(workspace) || !aligned16(kp) ||
-        !aligned16(vp))
+        !aligned16(vp) || !aligned16(pik))
         return (int)cudaErrorInvalidValue;
     tqa::AttnArgs a{};
     a.q = q;
@@ -1025,6 +1025,7 @@ extern "C" int launch_attention_paged_tq(void* output, const void* q, const int*
     if (num_tokens < 0 || kv_len < 0 || start_pos < 0 || num_tokens > 65535) return (int)cudaErrorInvalidValue;
     if (num_tokens == 0) return 0;
     if (!output || !q || !k_rotation || !v_rotation || !k_centroids || !v_centroids) return (int)cudaErrorInvalidValue;
+    if (!aligned16(k_rotation)) return (int)cudaErrorInvalidValue;  // read 16 bytes at a time
     if (kv_len > 0 && (!block_table || !k_packed_ptrs || !k_norms_ptrs || !v_packed_ptrs || !v_norms_ptrs))
         return (int)cudaErrorInvalidValue;
     const int nch = (kv_len + tqa::CH - 1) / tqa::CH;

@@ -91,9 +91,11 @@ int launch_paged_attention(void* output, const void* q, const int* block_table, 
  * block pos/16 to a physical block whose packed K/V rows and norms sit at k_packed_ptrs[b],
  * k_norms_ptrs[b], ... (device arrays of device pointers, [16, Hkv*P] and [16, Hkv]). Token t
  * attends positions [0, min(start_pos + t + 1, kv_len)). head_dim 128, Hq/Hkv in {1, 2, 4, 8},
- * 2/3/4/8-bit codes. The reference's math in float32 with the 2/3/4-bit centroid values read as
- * fp16 (within the 2e-3 FP bar of the float32 statement). Uses a device workspace owned by this
- * library, one per device, grown to the largest call. */
+ * 2/3/4/8-bit codes; k_rotation 16-byte aligned. The reference's math with FP32 accumulation:
+ * 2- and 4-bit codes on the tensor cores (centroid values, rotated queries and softmax weights as
+ * fp16 operands), 3- and 8-bit codes on CUDA cores in float32 with the 3-bit centroid values read
+ * as fp16; all within the 2e-3 FP bar of the float32 statement. Uses a device workspace owned by
+ * this library, one per device, grown to the largest call. */
 int launch_attention_paged_tq(void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
                               const void** k_norms_ptrs, const void** v_packed_ptrs, const void** v_norms_ptrs,
                               const float* k_rotation, const float* v_rotation, const float* k_centroids,
@@ -195,7 +197,8 @@ int fb_launch_tq_dequant_slots(const void* packed_pool, const void* norms_pool, 
  * [0, min(start_pos[s] + t + 1, kv_lens[s])) (device int32 arrays; max_kv_len bounds kv_lens).
  * Hq/Hkv in {1, 2, 4, 8}; key_bits/value_bits 2, 3, 4 or 8. `workspace` (16-byte aligned, at
  * least fb_tq_attention_workspace_bytes(num_seqs, q_per_seq, num_q_heads, max_kv_len) bytes)
- * holds the rotated queries and the per-256-position partial results. */
+ * holds the rotated queries and the split-K partial results (sized for 256-position chunks).
+ * k_rotation 16-byte aligned. Numerics as for launch_attention_paged_tq. */
 size_t fb_tq_attention_workspace_bytes(int num_seqs, int q_per_seq, int num_q_heads, int max_kv_len);
 int fb_launch_tq_attention_paged(const void* q, int dtype, int num_seqs, int q_per_seq, int num_q_heads,
                                  int num_kv_heads, int head_dim, const void* k_packed_pool, const void* k_norms_pool,
@@ -211,7 +214,9 @@ int fb_launch_tq_attention_paged(const void* q, int dtype, int num_seqs, int q_p
  * [num_pool_rows, Hkv, 128] of `dtype` (the reference's per-block tensors [16, Hkv, d] back to back,
  * pool row = block * 16 + offset); queries and output [num_seqs * q_per_seq, Hq, 128] of `dtype`;
  * block tables, kv_lens, start_pos and the workspace as for fb_launch_tq_attention_paged
- * (fb_attention_workspace_bytes). */
+ * (fb_attention_workspace_bytes). Queries on a 16-byte boundary take the tensor-core kernel
+ * (FP32 accumulation; the softmax weights as the cache's 16-bit type, BF16 ones split into a high
+ * and a low part), others the CUDA-core kernel (float32); both within the 2e-3 FP bar. */
 size_t fb_attention_workspace_bytes(int num_seqs, int q_per_seq, int num_q_heads, int max_kv_len);
 int fb_launch_attention_paged(const void* q, int dtype, int num_seqs, int q_per_seq, int num_q_heads, int num_kv_heads,
                               int head_dim, const void* k_pool, const void* v_pool, int64_t num_pool_rows,
