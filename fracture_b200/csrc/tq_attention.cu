@@ -32,6 +32,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tq_sm100.cuh"
 #include "tq_common.cuh"
 
 namespace fb {
@@ -64,6 +65,7 @@ struct AttnArgs {
     float* part;  // [rows, hq, nch, PART]
     int nch;
     int ch;  // positions per chunk
+    sm100::DivU32 dnch, dhkv, dqps;  // nch, hkv, q_per_seq as multiply-high divisors (tensor-core kernel)
     void* out;
 };
 
@@ -568,8 +570,9 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
     const int64_t kst = (int64_t)a.hkv * PK, vst = (int64_t)a.hkv * PV;
 
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
-        const int c = item % a.nch, rest = item / a.nch, g = rest % a.hkv, row = rest / a.hkv;
-        const int s = row / a.q_per_seq, tq = row - s * a.q_per_seq;
+        const uint32_t rest = sm100::divu32((uint32_t)item, a.dnch), rw_ = sm100::divu32(rest, a.dhkv);
+        const int c = item - (int)rest * a.nch, g = (int)rest - (int)rw_ * a.hkv, row = (int)rw_;
+        const int s = (int)sm100::divu32(rw_, a.dqps), tq = row - s * a.q_per_seq;
         const int L = causal_len(a, s, tq);
         const int p0 = c * CHM;
         if (p0 >= L) continue;  // the whole CTA
@@ -849,7 +852,11 @@ int launch_tc(const AttnArgs& a, const Addr& ad, cudaStream_t s) {
     const int64_t items = (int64_t)a.nch * a.hkv * a.num_seqs * a.q_per_seq;
     if (items > INT32_MAX) return (int)cudaErrorInvalidValue;
     const int grid = (int)std::min<int64_t>(items, slots[dev]);
-    kern<<<grid, THREADS, smem, s>>>(a, ad, (int)items);
+    AttnArgs b = a;
+    b.dnch = sm100::make_divu32((uint32_t)a.nch);
+    b.dhkv = sm100::make_divu32((uint32_t)a.hkv);
+    b.dqps = sm100::make_divu32((uint32_t)a.q_per_seq);
+    kern<<<grid, THREADS, smem, s>>>(b, ad, (int)items);
     return (int)cudaGetLastError();
 }
 
