@@ -53,6 +53,7 @@ __device__ __forceinline__ float silu_mul_f32(float g, float u) {
 template <typename T, int UNROLL>
 __global__ void __launch_bounds__(256) silu_mul_vec_kernel(T* __restrict__ out, const T* __restrict__ gate,
                                                            const T* __restrict__ up, int64_t nvec) {
+    pdl_begin();
     using V = Vec16<T>;
     const int64_t base = (int64_t)blockIdx.x * (blockDim.x * UNROLL) + threadIdx.x;
     V g[UNROLL], u[UNROLL];
@@ -78,6 +79,7 @@ __global__ void __launch_bounds__(256) silu_mul_vec_kernel(T* __restrict__ out, 
 
 template <typename T>
 __global__ void silu_mul_scalar_kernel(T* out, const T* gate, const T* up, int64_t begin, int64_t n) {
+    pdl_begin();
     for (int64_t i = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         out[i] = from_f32<T>(silu_mul_f32(to_f32(gate[i]), to_f32(up[i])));
 }
@@ -86,6 +88,7 @@ __global__ void silu_mul_scalar_kernel(T* out, const T* gate, const T* up, int64
 
 template <typename T, int UNROLL>
 __global__ void __launch_bounds__(256) add_vec_kernel(T* out, const T* a, const T* b, int64_t nvec) {
+    pdl_begin();
     using V = Vec16<T>;
     const int64_t base = (int64_t)blockIdx.x * (blockDim.x * UNROLL) + threadIdx.x;
     V x[UNROLL], y[UNROLL];
@@ -111,6 +114,7 @@ __global__ void __launch_bounds__(256) add_vec_kernel(T* out, const T* a, const 
 
 template <typename T>
 __global__ void add_scalar_kernel(T* out, const T* a, const T* b, int64_t begin, int64_t n) {
+    pdl_begin();
     for (int64_t i = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         out[i] = from_f32<T>(to_f32(a[i]) + to_f32(b[i]));
 }
@@ -122,6 +126,7 @@ template <typename T>
 __global__ void embedding_vec_kernel(T* __restrict__ out, const T* __restrict__ table,
                                      const uint32_t* __restrict__ ids, int64_t hidden, int64_t hvec,
                                      uint32_t vocab) {
+    pdl_begin();
     using V = Vec16<T>;
     const int64_t t = blockIdx.x;
     const uint32_t id = __ldg(ids + t);
@@ -136,6 +141,7 @@ __global__ void embedding_vec_kernel(T* __restrict__ out, const T* __restrict__ 
 
 template <typename T>
 __global__ void embedding_scalar_kernel(T* out, const T* table, const uint32_t* ids, int64_t hidden, uint32_t vocab) {
+    pdl_begin();
     const int64_t t = blockIdx.x;
     const uint32_t id = ids[t];
     for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x)
@@ -167,6 +173,7 @@ template <typename T, int VPT, bool ADD>
 __global__ void __launch_bounds__(256) norm_rows_vec_kernel(const T* x, const T* __restrict__ r, T* h_out,
                                                              const T* __restrict__ w, T* out, float eps,
                                                              int64_t cols, int cols_vec) {
+    pdl_begin();
     using V = Vec16<T>;
     __shared__ float red[33];
     const int64_t row = blockIdx.x;
@@ -219,6 +226,7 @@ __global__ void __launch_bounds__(256) norm_rows_vec_kernel(const T* x, const T*
 
 template <typename T, bool ADD>
 __global__ void norm_rows_scalar_kernel(const T* x, const T* r, T* h_out, const T* w, T* out, float eps, int64_t cols) {
+    pdl_begin();
     __shared__ float red[33];
     const int64_t row = blockIdx.x;
     float ss = 0.0f;
@@ -256,10 +264,10 @@ static int silu_mul_impl(T* out, const T* gate, const T* up, int64_t n, cudaStre
     if (aligned16(out) && aligned16(gate) && aligned16(up)) {
         const int64_t nvec = n / N;
         vec_elems = nvec * N;
-        if (nvec > 0) silu_mul_vec_kernel<T, UNROLL><<<grid_for(nvec, TPB * UNROLL), TPB, 0, s>>>(out, gate, up, nvec);
+        if (nvec > 0) launch_pdl(silu_mul_vec_kernel<T, UNROLL>, dim3(grid_for(nvec, TPB * UNROLL)), dim3(TPB), s, out, gate, up, nvec);
     }
     if (vec_elems < n)
-        silu_mul_scalar_kernel<T><<<(int)stride_grid(n - vec_elems, 256), 256, 0, s>>>(out, gate, up, vec_elems, n);
+        launch_pdl(silu_mul_scalar_kernel<T>, dim3((int)stride_grid(n - vec_elems, 256)), dim3(256), s, out, gate, up, vec_elems, n);
     return (int)cudaGetLastError();
 }
 
@@ -270,9 +278,9 @@ static int add_impl(T* out, const T* a, const T* b, int64_t n, cudaStream_t s) {
     if (aligned16(out) && aligned16(a) && aligned16(b)) {
         const int64_t nvec = n / N;
         vec_elems = nvec * N;
-        if (nvec > 0) add_vec_kernel<T, UNROLL><<<grid_for(nvec, TPB * UNROLL), TPB, 0, s>>>(out, a, b, nvec);
+        if (nvec > 0) launch_pdl(add_vec_kernel<T, UNROLL>, dim3(grid_for(nvec, TPB * UNROLL)), dim3(TPB), s, out, a, b, nvec);
     }
-    if (vec_elems < n) add_scalar_kernel<T><<<(int)stride_grid(n - vec_elems, 256), 256, 0, s>>>(out, a, b, vec_elems, n);
+    if (vec_elems < n) launch_pdl(add_scalar_kernel<T>, dim3((int)stride_grid(n - vec_elems, 256)), dim3(256), s, out, a, b, vec_elems, n);
     return (int)cudaGetLastError();
 }
 
@@ -284,10 +292,10 @@ static int embedding_impl(T* out, const T* table, const uint32_t* ids, int64_t n
     if (aligned16(out) && aligned16(table) && hidden % N == 0) {
         const int64_t hvec = hidden / N;
         const int tpb = (int)std::min<int64_t>(256, ((hvec + 31) / 32) * 32);
-        embedding_vec_kernel<T><<<(unsigned)ntok, tpb, 0, s>>>(out, table, ids, hidden, hvec, v32);
+        launch_pdl(embedding_vec_kernel<T>, dim3((unsigned)ntok), dim3(tpb), s, out, table, ids, hidden, hvec, v32);
     } else {
         const int tpb = (int)std::min<int64_t>(256, ((hidden + 31) / 32) * 32);
-        embedding_scalar_kernel<T><<<(unsigned)ntok, tpb, 0, s>>>(out, table, ids, hidden, v32);
+        launch_pdl(embedding_scalar_kernel<T>, dim3((unsigned)ntok), dim3(tpb), s, out, table, ids, hidden, v32);
     }
     return (int)cudaGetLastError();
 }
@@ -297,7 +305,7 @@ static void launch_norm_vec(const T* x, const T* r, T* h, const T* w, T* out, fl
                             int cols_vec, cudaStream_t s) {
     int tpb = (cols_vec + VPT - 1) / VPT;
     tpb = ((tpb + 31) / 32) * 32;
-    norm_rows_vec_kernel<T, VPT, ADD><<<(unsigned)rows, tpb, 0, s>>>(x, r, h, w, out, eps, cols, cols_vec);
+    launch_pdl(norm_rows_vec_kernel<T, VPT, ADD>, dim3((unsigned)rows), dim3(tpb), s, x, r, h, w, out, eps, cols, cols_vec);
 }
 
 template <typename T, bool ADD>
@@ -314,7 +322,7 @@ static int norm_impl(const T* x, const T* r, T* h, const T* w, T* out, float eps
         else if (cols_vec <= 1024) launch_norm_vec<T, ADD, 4>(x, r, h, w, out, eps, rows, cols, cols_vec, s);
         else launch_norm_vec<T, ADD, 8>(x, r, h, w, out, eps, rows, cols, cols_vec, s);
     } else {
-        norm_rows_scalar_kernel<T, ADD><<<(unsigned)rows, 256, 0, s>>>(x, r, h, w, out, eps, cols);
+        launch_pdl(norm_rows_scalar_kernel<T, ADD>, dim3((unsigned)rows), dim3(256), s, x, r, h, w, out, eps, cols);
     }
     return (int)cudaGetLastError();
 }

@@ -32,6 +32,7 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(T* q, T* k, const uint32_
                                                        const float* __restrict__ freqs, int64_t num_tokens,
                                                        int nq, int nkv, int head_dim, int ngv, int qgroups,
                                                        int kgroups) {
+    pdl_begin();
     using V = Vec16<T>;
     constexpr int N = V::N;
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -94,6 +95,7 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(T* q, T* k, const uint32_
 template <typename T>
 __global__ void rope_scalar_kernel(T* q, T* k, const uint32_t* positions, const float* freqs, int64_t num_tokens,
                                    int nq, int nkv, int head_dim) {
+    pdl_begin();
     const int half = head_dim >> 1;
     const int64_t per_tok = (int64_t)(nq + nkv) * half;
     const int64_t total = num_tokens * per_tok;
@@ -124,11 +126,12 @@ static int rope_impl(T* q, T* k, const uint32_t* pos, const float* freqs, int64_
         const int64_t threads = ntok * (int64_t)(qg + kg) * ngv;
         const int64_t blocks = (threads + 255) / 256;
         if (blocks > 0x7fffffffLL) return (int)cudaErrorInvalidValue;
-        rope_vec_kernel<T, HG><<<(unsigned)blocks, 256, 0, s>>>(q, k, pos, freqs, ntok, nq, nkv, hd, ngv, qg, kg);
+        launch_pdl(rope_vec_kernel<T, HG>, dim3((unsigned)blocks), dim3(256), s, q, k, pos, freqs, ntok, nq, nkv, hd, ngv, qg, kg);
     } else {
         const int64_t total = ntok * (int64_t)(nq + nkv) * half;
         const int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 32);
-        rope_scalar_kernel<T><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, s>>>(q, k, pos, freqs, ntok, nq, nkv, hd);
+        launch_pdl(rope_scalar_kernel<T>, dim3((unsigned)std::max<int64_t>(blocks, 1)), dim3(256), s, q, k, pos, freqs,
+                   ntok, nq, nkv, hd);
     }
     return (int)cudaGetLastError();
 }
