@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "fracture_b200.h"
 
 namespace fb {
@@ -98,11 +100,12 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // more than two CTAs per SM launch normally, so waiting CTAs never hold slots a large kernel
 // still needs. Launch errors are left for cudaGetLastError(), as with <<<>>>.
 template <typename... KArgs, typename... Args>
-inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args&&... args) {
+inline void launch_pdl_smem(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            Args&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -111,6 +114,10 @@ inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream
     cfg.attrs = &attr;
     cfg.numAttrs = blocks <= 2ull * (uint64_t)num_sms() ? 1 : 0;
     (void)cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args&&... args) {
+    launch_pdl_smem(kern, grid, block, 0, s, std::forward<Args>(args)...);
 }
 
 inline int dtype_size(int dt) {

@@ -69,6 +69,7 @@ __device__ __forceinline__ float norm_seq(const float* x, int d) {
 
 template <int V>
 __global__ void __launch_bounds__(256) tq_compress_small_kernel(TqArgs a) {
+    pdl_begin();
     extern __shared__ __align__(16) float sm[];
     const int d = a.head_dim, ld = d + 4, i = threadIdx.x;
     float* pis = sm;                 // pis[r * ld + j] = Pi[r][j]
@@ -148,6 +149,7 @@ __global__ void __launch_bounds__(256) tq_compress_small_kernel(TqArgs a) {
 // x_i = (sum_j Pi[j][i] * c[idx_j] in order) * norm; a vector without a slot gives zeros.
 template <typename Tout, int V>
 __global__ void __launch_bounds__(256) tq_dequant_small_kernel(TqArgs a) {
+    pdl_begin();
     extern __shared__ __align__(16) float sm[];
     const int d = a.head_dim, i = threadIdx.x;
     const int ld = d + 4;
@@ -209,7 +211,7 @@ int launch_small(K kern, const TqArgs& a, int V, cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;
     const int64_t nvec = a.num_tokens * a.num_heads;
-    kern<<<(unsigned)((nvec + V - 1) / V), small_threads(a.head_dim), smem, s>>>(a);
+    launch_pdl_smem(kern, dim3((unsigned)((nvec + V - 1) / V)), dim3(small_threads(a.head_dim)), smem, s, a);
     return (int)cudaGetLastError();
 }
 
