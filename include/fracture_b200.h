@@ -12,8 +12,9 @@
  *     libfracture_kernels.a changes nothing above the FFI.
  *
  *  2. New kernel entry points: dtype-generic (FP16 / BF16 / FP32) versions,
- *     the fused residual-add + RMSNorm, one-launch Q+K RoPE, and TurboQuant
- *     compress / dequantize straight into a paged pool. Host-table builders
+ *     the fused residual-add + RMSNorm, one-launch Q+K RoPE, TurboQuant
+ *     compress / dequantize straight into a paged pool, and paged attention
+ *     over the TurboQuant and the FP16/BF16 caches. Host-table builders
  *     (RoPE frequencies incl. llama3 scaling, Lloyd-Max codebook, Haar
  *     rotation) restate crates/fracture-core on the host.
  *
@@ -21,7 +22,14 @@
  *     (crates/fracture-core/src/backend.rs:8-223) over opaque tensor handles,
  *     so the Rust `CudaBackend` can be replaced by a thin shim, plus the
  *     quantized paged KV cache of crates/fracture-engine/src/
- *     quantized_paged_kv_cache.rs with its append_kv fused into one launch.
+ *     quantized_paged_kv_cache.rs with its append_kv fused into one launch,
+ *     and the FP16/BF16 paged KV cache of paged_kv_cache.rs.
+ *
+ * Stream order: every call is ordered after the work already on its stream.
+ * Decode-sized elementwise, RoPE and small TurboQuant launches are
+ * programmatic dependent launches: they may be scheduled while the previous
+ * kernel on the stream drains, and wait for it to complete (its writes
+ * visible) before they touch memory, so the ordering is the same.
  *
  * Return values: layer 1 and 2 return a cudaError_t value (0 = success;
  * cudaErrorInvalidValue = 1 for arguments rejected by the host-side checks,
