@@ -188,3 +188,33 @@ def test_unaligned_queries_take_the_cuda_core_kernel():
         for s, L in enumerate(kv_lens):
             ref = ops.attention_paged(qh[s], c["hk"], c["hv"], c["tables"][s], L, starts[s])
             ops.assert_close_fp(got[s], ref, rel=2e-3, min_cos=0.9999, label=f"seq {s}", dtype="f16")
+
+
+def test_pool_ending_inside_a_block_leaves_the_missing_rows_out():
+    """Pools cut 5 rows into the last block a sequence uses: positions whose pool row lies past
+    the pool are left out (as a missing block's are), on the tensor-core and CUDA-core kernels."""
+    kv_lens, Hkv, G = [200], 2, 4
+    c = build_cache(kv_lens, Hkv, "f16", seed=15)
+    table = c["tables"][0]
+    last = int(table.max())
+    cut = last * 16 + 11  # rows last*16 + 11 .. last*16 + 15 are outside the pool
+    qh, q = make_q(1, 1, G * Hkv, "f16", seed=16)
+    pos = np.arange(kv_lens[0])
+    rows = table[pos // 16] * 16 + pos % 16
+    keep = rows < cut
+    assert 0 < (~keep).sum() < len(pos)
+    # expected: plain attention over the kept positions
+    k, v = c["hk"][rows][keep], c["hv"][rows][keep]
+    exp = np.zeros((1, G * Hkv, D))
+    for h in range(G * Hkv):
+        sc = k[:, h // G] @ qh[0, 0, h] / np.sqrt(D)
+        p = np.exp(sc - sc.max())
+        exp[0, h] = (p / p.sum()) @ v[:, h // G]
+    for qq in (q, torch.empty(q.numel() + 1, dtype=q.dtype, device=DEV)[1:].view(q.shape).copy_(q)):
+        out = torch.full(qq.shape, 7.0, dtype=qq.dtype, device=DEV)
+        K.attention_paged(qq, c["kp"][:cut], c["vp"][:cut], torch.from_numpy(c["tables"]).to(DEV),
+                          torch.tensor(kv_lens, dtype=torch.int32, device=DEV),
+                          torch.tensor([kv_lens[0] - 1], dtype=torch.int32, device=DEV), out)
+        torch.cuda.synchronize()
+        ops.assert_close_fp(out[0].float().cpu().numpy(), exp, rel=2e-3, min_cos=0.9999, label="cut pool",
+                            dtype="f16")

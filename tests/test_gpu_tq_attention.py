@@ -201,3 +201,43 @@ def test_chunk_boundaries_and_more_items_than_ctas(kb, vb):
     for s, L in enumerate(kv_lens):
         ops.assert_close_fp(got[s], statement(c, qh[s], s, L, starts[s]), rel=2e-3, min_cos=0.9999,
                             label=f"seq {s} (kv {L})", dtype="f16")
+
+
+@pytest.mark.parametrize("kb,vb", [(4, 2), (3, 3)])
+def test_pool_ending_inside_a_block_leaves_the_missing_rows_out(kb, vb):
+    """Pools cut 5 rows into the last block the sequence uses: positions whose pool row lies past
+    the pool are left out (the tensor-core kernel for 4/2 bits, the CUDA-core one for 3/3)."""
+    kv_len, Hkv, G = 200, 2, 4
+    c = build_cache([kv_len], Hkv, kb, vb, seed=70 + kb)
+    table = c["tables"][0]
+    last = int(table.max())
+    cut = last * 16 + 11
+    qh, q = make_q(1, 1, G * Hkv, "f16", seed=71)
+    # expected: the statement over a cache whose cut rows hold no block (their block entry
+    # stays, but the statement sees the kept positions only through a per-position table)
+    pos = np.arange(kv_len)
+    rows = table[pos // 16] * 16 + pos % 16
+    keep = rows < cut
+    assert 0 < (~keep).sum() < kv_len
+    d = D
+    Pk, Pv = d * kb // 8, d * vb // 8
+    kp = c["kp"].cpu().numpy().reshape(-1, Hkv, Pk)[rows[keep]]
+    vp = c["vp"].cpu().numpy().reshape(-1, Hkv, Pv)[rows[keep]]
+    kn = c["kn"].float().cpu().numpy()[rows[keep]]
+    vn = c["vn"].float().cpu().numpy()[rows[keep]]
+    n = int(keep.sum())
+    nb = (n + 15) // 16
+    pad = nb * 16 - n
+    kp = np.concatenate([kp, np.zeros((pad, Hkv, Pk), np.uint8)]).reshape(nb * 16, Hkv * Pk)
+    vp = np.concatenate([vp, np.zeros((pad, Hkv, Pv), np.uint8)]).reshape(nb * 16, Hkv * Pv)
+    kn = np.concatenate([kn, np.zeros((pad, Hkv))])
+    vn = np.concatenate([vn, np.zeros((pad, Hkv))])
+    exp = tq.attention_paged_tq(qh[0], kp, kn, vp, vn, np.arange(nb), n, n - 1, c["pik_h"], c["piv_h"], c["ck_h"],
+                                c["cv_h"], kb, vb, Hkv)
+    out = torch.full(q.shape, 7.0, dtype=torch.float16, device=DEV)
+    K.tq_attention_paged(q, c["kp"][:cut], c["kn"][:cut], c["vp"][:cut], c["vn"][:cut],
+                         torch.from_numpy(c["tables"]).to(DEV), torch.tensor([kv_len], dtype=torch.int32, device=DEV),
+                         torch.tensor([kv_len - 1], dtype=torch.int32, device=DEV), c["pik"], c["piv"], c["ck"],
+                         c["cv"], kb, vb, out)
+    torch.cuda.synchronize()
+    ops.assert_close_fp(out[0].float().cpu().numpy(), exp, rel=2e-3, min_cos=0.9999, label="cut pool", dtype="f16")
