@@ -23,7 +23,6 @@
 // token with no position gives zeros.
 
 #include <algorithm>
-#include <mutex>
 
 #include "common.cuh"
 
@@ -722,8 +721,8 @@ extern "C" int fb_launch_attention_paged(const void* q, int dtype, int num_seqs,
 }
 
 // ffi.rs:186-200 (attention_paged.cu:161-185): one sequence, FP16, per-block pointer arrays
-// (block b's K rows at k_block_ptrs[b], [16, Hkv, d]). Workspace: this library's, one per device,
-// grown to the largest call.
+// (block b's K rows at k_block_ptrs[b], [16, Hkv, d]). Workspace: this library's, one per device
+// and stream, grown to the largest call on that stream.
 extern "C" int launch_paged_attention(void* output, const void* q, const int* block_table, const void** k_block_ptrs,
                                       const void** v_block_ptrs, int num_tokens, int num_q_heads, int num_kv_heads,
                                       int head_dim, int kv_len, int start_pos, int num_blocks_in_seq, void* stream) {
@@ -735,41 +734,24 @@ extern "C" int launch_paged_attention(void* output, const void* q, const int* bl
     if (kv_len > 0 && (!block_table || !k_block_ptrs || !v_block_ptrs)) return (int)cudaErrorInvalidValue;
     const int nch = (kv_len + kvp::CH - 1) / kvp::CH;
     const size_t need = std::max<size_t>(kvp::workspace_bytes(num_tokens, num_q_heads, nch), 16);
-    static void* ws[64];
-    static size_t cap[64];
-    static std::mutex mu;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return (int)e;
-    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> g(mu);
-    if (cap[dev] < need) {
-        if (ws[dev]) {
-            e = cudaFree(ws[dev]);
-            if (e != cudaSuccess) return (int)e;
-        }
-        ws[dev] = nullptr;
-        cap[dev] = 0;
-        e = cudaMalloc(&ws[dev], need);
-        if (e != cudaSuccess) return (int)e;
-        cap[dev] = need;
-    }
-    kvp::Args a{};
-    a.q = q;
-    a.dtype = FB_FP16;
-    a.num_seqs = 1;
-    a.q_per_seq = num_tokens;
-    a.hq = num_q_heads;
-    a.hkv = num_kv_heads;
-    a.block_tables = block_table;
-    a.max_blocks = num_blocks_in_seq;
-    a.kv_len = kv_len;
-    a.start = start_pos;
-    a.part = (float*)ws[dev];
-    a.nch = nch;
-    a.out = output;
-    kvp::BlockPtrRows rw{(const uint8_t* const*)k_block_ptrs, (const uint8_t* const*)v_block_ptrs};
-    return kvp::run(a, rw, (cudaStream_t)stream);
+    return with_stream_workspace(stream, need, [&](void* ws) {
+        kvp::Args a{};
+        a.q = q;
+        a.dtype = FB_FP16;
+        a.num_seqs = 1;
+        a.q_per_seq = num_tokens;
+        a.hq = num_q_heads;
+        a.hkv = num_kv_heads;
+        a.block_tables = block_table;
+        a.max_blocks = num_blocks_in_seq;
+        a.kv_len = kv_len;
+        a.start = start_pos;
+        a.part = (float*)ws;
+        a.nch = nch;
+        a.out = output;
+        kvp::BlockPtrRows rw{(const uint8_t* const*)k_block_ptrs, (const uint8_t* const*)v_block_ptrs};
+        return kvp::run(a, rw, (cudaStream_t)stream);
+    });
 }
 
 // PagedKvCacheManager::append_kv's writes (paged_kv_cache.rs:290-315) in one launch: keys/values

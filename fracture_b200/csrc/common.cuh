@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <utility>
 
 #include "fracture_b200.h"
@@ -91,6 +92,40 @@ __device__ __forceinline__ void pdl_begin() {
 // Host-side helpers ----------------------------------------------------------
 
 int num_sms();  // SM count of the current device (cached per device)
+
+// Library-owned device workspace for the reference-ABI entry points that take none: one buffer per
+// (device, stream), grown to the largest call on that stream and kept until exit. Calls on one
+// stream run in order and share it; calls on different streams get different buffers, so they
+// may overlap on the GPU. Growing frees the old buffer (cudaFree waits for the device first).
+struct StreamWorkspace {
+    void* ptr = nullptr;
+    size_t cap = 0;
+};
+std::mutex& stream_workspace_mutex();
+StreamWorkspace& stream_workspace(int device, const void* stream);  // with the mutex held
+
+// Runs enqueue(ptr) with a workspace of at least `need` bytes for the current device and
+// `stream`, holding the lock so that no other call regrows that buffer before the work is queued.
+template <typename F>
+int with_stream_workspace(const void* stream, size_t need, F&& enqueue) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    std::lock_guard<std::mutex> g(stream_workspace_mutex());
+    StreamWorkspace& w = stream_workspace(dev, stream);
+    if (w.cap < need) {
+        if (w.ptr) {
+            e = cudaFree(w.ptr);
+            if (e != cudaSuccess) return (int)e;
+        }
+        w.ptr = nullptr;
+        w.cap = 0;
+        e = cudaMalloc(&w.ptr, need);
+        if (e != cudaSuccess) return (int)e;
+        w.cap = need;
+    }
+    return enqueue(w.ptr);
+}
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -13,6 +13,7 @@
 //   add+rmsnorm has no reference kernel (the engine issues add then rmsnorm).
 
 #include <algorithm>
+#include <map>
 
 #include "common.cuh"
 
@@ -28,6 +29,16 @@ int num_sms() {
         cached[dev] = n > 0 ? n : 148;
     }
     return cached[dev];
+}
+
+std::mutex& stream_workspace_mutex() {
+    static std::mutex m;
+    return m;
+}
+
+StreamWorkspace& stream_workspace(int device, const void* stream) {
+    static std::map<std::pair<int, uintptr_t>, StreamWorkspace> buffers;
+    return buffers[{device, reinterpret_cast<uintptr_t>(stream)}];
 }
 
 // Coherent streaming load: used where the same kernel writes the buffer it

@@ -29,7 +29,6 @@
 // out; a query token with no position gives zeros.
 
 #include <algorithm>
-#include <mutex>
 
 #include "common.cuh"
 #include "tq_sm100.cuh"
@@ -1015,8 +1014,8 @@ extern "C" int fb_launch_tq_attention_paged(const void* q, int dtype, int num_se
 }
 
 // The reference ABI (ffi.rs:251-274, attention_paged_tq.cu:261-309): one sequence, FP16, a
-// device block table and per-block pointer arrays. The workspace is this library's, one
-// per device, grown to the largest call and kept (calls on one device are serialised by it).
+// device block table and per-block pointer arrays. The workspace is this library's, one per
+// device and stream, grown to the largest call on that stream and kept.
 extern "C" int launch_attention_paged_tq(void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
                                          const void** k_norms_ptrs, const void** v_packed_ptrs,
                                          const void** v_norms_ptrs, const float* k_rotation, const float* v_rotation,
@@ -1037,45 +1036,28 @@ extern "C" int launch_attention_paged_tq(void* output, const void* q, const int*
         return (int)cudaErrorInvalidValue;
     const int nch = (kv_len + tqa::CH - 1) / tqa::CH;
     const size_t need = tqa::workspace_bytes(num_tokens, num_q_heads, nch);
-    static void* ws[64];
-    static size_t cap[64];
-    static std::mutex mu;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return (int)e;
-    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> g(mu);
-    if (cap[dev] < need) {
-        if (ws[dev]) {
-            e = cudaFree(ws[dev]);
-            if (e != cudaSuccess) return (int)e;
-        }
-        ws[dev] = nullptr;
-        cap[dev] = 0;
-        e = cudaMalloc(&ws[dev], need);
-        if (e != cudaSuccess) return (int)e;
-        cap[dev] = need;
-    }
-    tqa::AttnArgs a{};
-    a.q = q;
-    a.dtype = FB_FP16;
-    a.num_seqs = 1;
-    a.q_per_seq = num_tokens;
-    a.hq = num_q_heads;
-    a.hkv = num_kv_heads;
-    a.block_tables = block_table;
-    a.max_blocks = (kv_len + 15) / 16;
-    a.kv_len = kv_len;
-    a.start = start_pos;
-    a.pik = k_rotation;
-    a.piv = v_rotation;
-    a.ck = k_centroids;
-    a.cv = v_centroids;
-    a.qrot = (float*)ws[dev];
-    a.part = a.qrot + (int64_t)num_tokens * num_q_heads * tqa::D;
-    a.nch = nch;
-    a.out = output;
-    tqa::BlockPtrAddr ad{(const uint8_t* const*)k_packed_ptrs, (const __half* const*)k_norms_ptrs,
-                         (const uint8_t* const*)v_packed_ptrs, (const __half* const*)v_norms_ptrs};
-    return tqa::run(a, key_bits, value_bits, ad, (cudaStream_t)stream);
+    return with_stream_workspace(stream, need, [&](void* ws) {
+        tqa::AttnArgs a{};
+        a.q = q;
+        a.dtype = FB_FP16;
+        a.num_seqs = 1;
+        a.q_per_seq = num_tokens;
+        a.hq = num_q_heads;
+        a.hkv = num_kv_heads;
+        a.block_tables = block_table;
+        a.max_blocks = (kv_len + 15) / 16;
+        a.kv_len = kv_len;
+        a.start = start_pos;
+        a.pik = k_rotation;
+        a.piv = v_rotation;
+        a.ck = k_centroids;
+        a.cv = v_centroids;
+        a.qrot = (float*)ws;
+        a.part = a.qrot + (int64_t)num_tokens * num_q_heads * tqa::D;
+        a.nch = nch;
+        a.out = output;
+        tqa::BlockPtrAddr ad{(const uint8_t* const*)k_packed_ptrs, (const __half* const*)k_norms_ptrs,
+                             (const uint8_t* const*)v_packed_ptrs, (const __half* const*)v_norms_ptrs};
+        return tqa::run(a, key_bits, value_bits, ad, (cudaStream_t)stream);
+    });
 }

@@ -89,7 +89,8 @@ int launch_turboquant_decompress(const void* packed_in, const void* norms_in, co
  * maps logical block pos/16 to a physical block whose K and V rows sit at k_block_ptrs[b],
  * v_block_ptrs[b] (device arrays of device pointers, [16, Hkv, d] each). Token t attends positions
  * [0, min(start_pos + t + 1, kv_len)). head_dim 128, Hq/Hkv in {1, 2, 4, 8}; float32 math. Uses a
- * device workspace owned by this library, one per device, grown to the largest call. */
+ * device workspace owned by this library, one per device and stream, grown to the largest call on
+ * that stream and kept until exit (calls on different streams may run at the same time). */
 int launch_paged_attention(void* output, const void* q, const int* block_table, const void** k_block_ptrs,
                            const void** v_block_ptrs, int num_tokens, int num_q_heads, int num_kv_heads,
                            int head_dim, int kv_len, int start_pos, int num_blocks_in_seq, void* stream);
@@ -103,7 +104,8 @@ int launch_paged_attention(void* output, const void* q, const int* block_table, 
  * 2- and 4-bit codes on the tensor cores (centroid values, rotated queries and softmax weights as
  * fp16 operands), 3- and 8-bit codes on CUDA cores in float32 with the 3-bit centroid values read
  * as fp16; all within the 2e-3 FP bar of the float32 statement. Uses a device workspace owned by
- * this library, one per device, grown to the largest call. */
+ * this library, one per device and stream, grown to the largest call on that stream and kept until
+ * exit (calls on different streams may run at the same time). */
 int launch_attention_paged_tq(void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
                               const void** k_norms_ptrs, const void** v_packed_ptrs, const void** v_norms_ptrs,
                               const float* k_rotation, const float* v_rotation, const float* k_centroids,

@@ -241,3 +241,32 @@ def test_pool_ending_inside_a_block_leaves_the_missing_rows_out(kb, vb):
                          c["cv"], kb, vb, out)
     torch.cuda.synchronize()
     ops.assert_close_fp(out[0].float().cpu().numpy(), exp, rel=2e-3, min_cos=0.9999, label="cut pool", dtype="f16")
+
+
+def test_reference_abi_calls_on_two_streams_at_once():
+    """launch_attention_paged_tq keeps one library workspace per device and stream: calls queued
+    alternately on two streams (free to overlap on the GPU) give the same bytes as calls made
+    one after the other."""
+    kv_len, Tq, Hkv, G = 3000, 4, 2, 4
+    c = build_cache([kv_len], Hkv, 4, 2, seed=80)
+    lib = _lib.load()
+    qs = [make_q(1, Tq, G * Hkv, "f16", seed=81 + i)[1][0] for i in range(4)]
+    ref = [_reference_abi_call(lib, c, qq, kv_len, kv_len - Tq) for qq in qs]
+    nblocks = int(c["tables"].max()) + 1
+    kp, kn, vp, vn = _block_pointer_arrays(c, nblocks)
+    bt = torch.from_numpy(np.ascontiguousarray(c["tables"][0])).to(DEV)
+    outs = [torch.full_like(r, 7.0) for r in ref]
+    torch.cuda.synchronize()  # everything above is ready before the streams start
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    Hq = G * Hkv
+    for _ in range(3):
+        for i, qq in enumerate(qs):
+            rc = lib.launch_attention_paged_tq(outs[i].data_ptr(), qq.data_ptr(), bt.data_ptr(), kp.data_ptr(),
+                                               kn.data_ptr(), vp.data_ptr(), vn.data_ptr(), c["pik"].data_ptr(),
+                                               c["piv"].data_ptr(), c["ck"].data_ptr(), c["cv"].data_ptr(), Tq, Hq,
+                                               Hkv, D, kv_len, kv_len - Tq, 4, 2, D // 2, D // 4,
+                                               streams[i % 2].cuda_stream)
+            assert rc == 0
+    torch.cuda.synchronize()
+    for o, r in zip(outs, ref):
+        assert torch.equal(o, r)
