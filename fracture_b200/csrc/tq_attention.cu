@@ -22,7 +22,7 @@
 //                   head h, column i of Pi_v shared by the group's heads through L1)
 //
 // With 2- or 4-bit keys and values, tqa_mma (tensor cores, below) replaces tqa_chunk: same
-// split-K partials, 512-position chunks. 3- and 8-bit codes take tqa_chunk.
+// split-K partials, 1024-position chunks. 3- and 8-bit codes take tqa_chunk.
 //
 // Each KV head's codes are read once per query token for its whole group of Q heads. A
 // position whose block-table entry is negative, or whose pool row is out of range, is left
@@ -476,10 +476,12 @@ __global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a) {
 
 // ── tensor-core path: 2- and 4-bit keys and values ──
 //
-// One work item = (512-position chunk, KV head, query token); a persistent CTA takes items
-// in turn and builds its decoding tables once. Warp w takes positions 64w..64w+63 of the
-// chunk as four 16-position tiles and does both contractions with mma.sync m16n8k16 (FP16
-// operands, FP32 accumulators), the operands decoded in registers:
+// One work item = (1024-position chunk, KV head, query token); a persistent CTA takes items
+// in turn and builds its decoding tables once. Warp w takes positions 128w..128w+127 of the
+// chunk in two rounds of four 16-position tiles (a round's codes all requested before any is
+// used), keeps a running softmax (maximum, sum, accumulator) per head across the rounds, and
+// does both contractions with mma.sync m16n8k16 (FP16 operands, FP32 accumulators), the
+// operands decoded in registers:
 //
 //   scores   S[16 positions x 8 heads] = K_tile[16 x 128] . Q^T: lane (r, t) = (lane / 4,
 //            lane % 4) reads bytes of rows r and r + 8 holding code pairs 16t..16t+15 and
@@ -495,10 +497,11 @@ __global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a) {
 //
 // Table lookups: entry e at byte 256e, 32 lane-private copies of the K pair value at
 // 256e + 4 lane and of the V pair value at 256e + 128 + 4 lane, so the address is one byte
-// permute of the code byte and the lane offset, and a warp's lookups hit 32 banks.
+// permute of the code byte and the lane offset, and a warp's lookups hit 32 banks. At the end
+// of an item the warps' results are rescaled to the item's maximum and added in warp order.
 
 namespace tc {
-constexpr int TILE = 16, TPW = 4, CHM = NWARPS * TPW * TILE;  // 512 positions per item
+constexpr int TILE = 16, TPW = 4, RND = 2, CHM = NWARPS * RND * TPW * TILE;  // 1024 positions per item
 
 template <int KB, int VB>
 struct Smem {
@@ -587,8 +590,14 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
             qf[warp * 32 + lane] = make_uint2(pack_half2(f.x, f.y), pack_half2(f.z, f.w));
         }
 
-        // codes and norms of the warp's four tiles, all requested before any is used
-        const int pw = p0 + warp * TPW * TILE;
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // heads 2t, 2t + 1: running softmax
+        float acc[8][4];
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
+#pragma unroll 1
+        for (int rd = 0; rd < RND; ++rd) {
+        // codes and norms of the round's four tiles of the warp, all requested before any is used
+        const int pw = p0 + (warp * RND + rd) * TPW * TILE;
         uint32_t kw[TPW][2][KW], vw[TPW][4][VW];
         float kn[TPW][2], vn[TPW][2];
         int nv[TPW];
@@ -636,7 +645,7 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
             }
         }
 
-        __syncthreads();  // the staged query fragments
+        if (rd == 0) __syncthreads();  // the staged query fragments
 
         // ── scores ──
         float sc[TPW][4];
@@ -673,35 +682,39 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
             sc[i][3] = r + 8 < nv[i] ? c4[3] * f1 : -INFINITY;
         }
 
-        // ── softmax over the item: maximum per head, weights exp(s - max) * v_norm ──
-        float m0 = -INFINITY, m1 = -INFINITY;  // heads 2t, 2t + 1
+        // ── running softmax of the warp: the round's maximum per head, the sums so far rescaled
+        // when it grows, weights exp(s - max) * v_norm ──
+        float t0 = -INFINITY, t1 = -INFINITY;
 #pragma unroll
         for (int i = 0; i < TPW; ++i) {
-            m0 = fmaxf(m0, fmaxf(sc[i][0], sc[i][2]));
-            m1 = fmaxf(m1, fmaxf(sc[i][1], sc[i][3]));
+            t0 = fmaxf(t0, fmaxf(sc[i][0], sc[i][2]));
+            t1 = fmaxf(t1, fmaxf(sc[i][1], sc[i][3]));
         }
 #pragma unroll
         for (int o = 4; o < 32; o <<= 1) {
-            m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
-            m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+            t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
+            t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
         }
-        if (r == 0) {
-            rmx[warp * 8 + 2 * t] = m0;
-            rmx[warp * 8 + 2 * t + 1] = m1;
-        }
-        __syncthreads();
-        float M0 = rmx[2 * t], M1 = rmx[2 * t + 1];
+        if (t0 > m0 || t1 > m1) {
+            const float g0 = t0 > m0 ? __expf(m0 - t0) : 1.0f, g1 = t1 > m1 ? __expf(m1 - t1) : 1.0f;
+            m0 = fmaxf(m0, t0);
+            m1 = fmaxf(m1, t1);
+            l0 *= g0;
+            l1 *= g1;
 #pragma unroll
-        for (int w = 1; w < NWARPS; ++w) {
-            M0 = fmaxf(M0, rmx[w * 8 + 2 * t]);
-            M1 = fmaxf(M1, rmx[w * 8 + 2 * t + 1]);
+            for (int mt = 0; mt < 8; ++mt) {
+                acc[mt][0] *= g0;
+                acc[mt][2] *= g0;
+                acc[mt][1] *= g1;
+                acc[mt][3] *= g1;
+            }
         }
-        const bool any = M0 > -INFINITY;  // some position of the item is in the cache
-        float l0 = 0.0f, l1 = 0.0f;
+        const bool any = m0 > -INFINITY;  // some position of the warp's rounds so far is in the cache
+        __syncwarp();  // the previous round's weights have been read
 #pragma unroll
         for (int i = 0; i < TPW; ++i) {
-            const float e0 = any ? __expf(sc[i][0] - M0) : 0.0f, e1 = any ? __expf(sc[i][1] - M1) : 0.0f;
-            const float e2 = any ? __expf(sc[i][2] - M0) : 0.0f, e3 = any ? __expf(sc[i][3] - M1) : 0.0f;
+            const float e0 = any ? __expf(sc[i][0] - m0) : 0.0f, e1 = any ? __expf(sc[i][1] - m1) : 0.0f;
+            const float e2 = any ? __expf(sc[i][2] - m0) : 0.0f, e3 = any ? __expf(sc[i][3] - m1) : 0.0f;
             l0 += e0 + e2;
             l1 += e1 + e3;
             uint32_t* pr = (uint32_t*)(pb + (i * TILE + r) * 8 + 2 * t);
@@ -711,9 +724,6 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
         __syncwarp();
 
         // ── values ──
-        float acc[8][4];
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
 #pragma unroll
         for (int i = 0; i < TPW; ++i) {
             if (nv[i] == 0) continue;
@@ -755,13 +765,17 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
             }
         }
 
-        // ── the warps' sums, added in warp order ──
+        }  // rounds
+
+        // ── the warps' results, rescaled to the item's maximum and added in warp order ──
 #pragma unroll
         for (int o = 4; o < 32; o <<= 1) {
             l0 += __shfl_xor_sync(0xffffffffu, l0, o);
             l1 += __shfl_xor_sync(0xffffffffu, l1, o);
         }
         if (r == 0) {
+            rmx[warp * 8 + 2 * t] = m0;
+            rmx[warp * 8 + 2 * t + 1] = m1;
             rl[warp * 8 + 2 * t] = l0;
             rl[warp * 8 + 2 * t + 1] = l1;
         }
@@ -777,20 +791,26 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
         float* part = a.part + (((int64_t)row * a.hq + g * GA) * a.nch + c) * PART;
         for (int e = tid; e < GA * D; e += THREADS) {
             const int h = e / D, i = e - h * D;
+            float M = rmx[h];
+#pragma unroll
+            for (int w = 1; w < NWARPS; ++w) M = fmaxf(M, rmx[w * 8 + h]);
             float v = 0.0f;
 #pragma unroll
-            for (int w = 0; w < NWARPS; ++w) v += accs[(w * 8 + h) * D + i];
-            part[(int64_t)h * a.nch * PART + 2 + i] = v;
-        }
-        if (tid < GA) {
-            float m = rmx[tid], l = rl[tid];
-            for (int w = 1; w < NWARPS; ++w) {
-                m = fmaxf(m, rmx[w * 8 + tid]);
-                l += rl[w * 8 + tid];
+            for (int w = 0; w < NWARPS; ++w) {
+                const float mw = rmx[w * 8 + h];
+                if (mw > -INFINITY) v = fmaf(accs[(w * 8 + h) * D + i], __expf(mw - M), v);
             }
-            float* ph = part + (int64_t)tid * a.nch * PART;
-            ph[0] = m;
-            ph[1] = l;
+            part[(int64_t)h * a.nch * PART + 2 + i] = v;
+            if (i == 0) {
+                float l = 0.0f;
+#pragma unroll
+                for (int w = 0; w < NWARPS; ++w) {
+                    const float mw = rmx[w * 8 + h];
+                    if (mw > -INFINITY) l = fmaf(rl[w * 8 + h], __expf(mw - M), l);
+                }
+                part[(int64_t)h * a.nch * PART] = M;
+                part[(int64_t)h * a.nch * PART + 1] = l;
+            }
         }
         __syncthreads();  // the next item rewrites the maxima and sums
     }
