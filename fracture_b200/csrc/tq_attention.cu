@@ -501,7 +501,7 @@ __global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a) {
 // of an item the warps' results are rescaled to the item's maximum and added in warp order.
 
 namespace tc {
-constexpr int TILE = 16, TPW = 4, RND = 2, CHM = NWARPS * RND * TPW * TILE;  // 1024 positions per item
+constexpr int TILE = 16, TPW = 4, RND = 4, CHM = NWARPS * RND * TPW * TILE;  // 2048 positions per item
 
 template <int KB, int VB>
 struct Smem {
