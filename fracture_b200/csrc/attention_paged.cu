@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(128) kvp_combine(Args a) {
 // maximum and added in warp order.
 
 namespace tc {
-constexpr int TILE = 16, TPW = 4, CHM = NWARPS * TPW * TILE;  // 512 positions per item
+constexpr int TILE = 16, TPW = 4, RND = 4, CHM = NWARPS * RND * TPW * TILE;  // 2048 positions per item
 
 struct Smem {
     static constexpr int acc_off = 0;                                  // [NWARPS][8][D] f32
@@ -401,130 +401,134 @@ __global__ void __launch_bounds__(THREADS, 2) kvp_mma(Args a, Rows rw, int items
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
 
-        const int pw = p0 + warp * TPW * TILE;
-        const int lim = min(L, a.max_blocks * 16);
-        // the warp's tiles: block entry and positions in the cache (a prefix of the 16)
-        int32_t bk[TPW];
-        int nv[TPW];
+#pragma unroll 1
+        for (int rd = 0; rd < RND; ++rd) {  // rounds of four tiles, one running softmax
+            const int pw = p0 + (warp * RND + rd) * TPW * TILE;
+            const int lim = min(L, a.max_blocks * 16);
+            // the warp's tiles: block entry and positions in the cache (a prefix of the 16)
+            int32_t bk[TPW];
+            int nv[TPW];
 #pragma unroll
-        for (int i = 0; i < TPW; ++i) {
-            const int ps = pw + i * TILE;
-            const int32_t blk = ps < lim ? __ldg(a.block_tables + (int64_t)s * a.max_blocks + (ps >> 4)) : -1;
-            nv[i] = blk >= 0 ? min(min(TILE, L - ps), rw.block_rows(blk)) : 0;
-            bk[i] = blk;
-        }
-        // Tile i + 1's keys are requested as soon as tile i's scores are done with the key
-        // registers, its values as soon as tile i's values are done with the value registers.
-        uint32_t kw[2][16], vw[4][8];
-        auto load_k = [&](int i) {
-            const int n = nv[i];
-            const uint8_t *kb = nullptr, *vb = nullptr;
-            if (n > 0) rw.block_base(bk[i], g, a.hkv, (int)sizeof(T), kb, vb);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int off = r + 8 * h;
-                const uint4* p = (const uint4*)(kb + off * rst + 64 * t);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint4 u = off < n ? __ldg(p + j) : make_uint4(0, 0, 0, 0);
-                    kw[h][4 * j] = u.x;
-                    kw[h][4 * j + 1] = u.y;
-                    kw[h][4 * j + 2] = u.z;
-                    kw[h][4 * j + 3] = u.w;
-                }
+            for (int i = 0; i < TPW; ++i) {
+                const int ps = pw + i * TILE;
+                const int32_t blk = ps < lim ? __ldg(a.block_tables + (int64_t)s * a.max_blocks + (ps >> 4)) : -1;
+                nv[i] = blk >= 0 ? min(min(TILE, L - ps), rw.block_rows(blk)) : 0;
+                bk[i] = blk;
             }
-        };
-        auto load_v = [&](int i) {
-            const int n = nv[i];
-            const uint8_t *kb = nullptr, *vb = nullptr;
-            if (n > 0) rw.block_base(bk[i], g, a.hkv, (int)sizeof(T), kb, vb);
+            // Tile i + 1's keys are requested as soon as tile i's scores are done with the key
+            // registers, its values as soon as tile i's values are done with the value registers.
+            uint32_t kw[2][16], vw[4][8];
+            auto load_k = [&](int i) {
+                const int n = nv[i];
+                const uint8_t *kb = nullptr, *vb = nullptr;
+                if (n > 0) rw.block_base(bk[i], g, a.hkv, (int)sizeof(T), kb, vb);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int off = 2 * t + (u & 1) + 8 * (u >> 1);
-                const uint4* p = (const uint4*)(vb + off * rst + 32 * r);
+                for (int h = 0; h < 2; ++h) {
+                    const int off = r + 8 * h;
+                    const uint4* p = (const uint4*)(kb + off * rst + 64 * t);
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const uint4 x = off < n ? __ldg(p + j) : make_uint4(0, 0, 0, 0);
-                    vw[u][4 * j] = x.x;
-                    vw[u][4 * j + 1] = x.y;
-                    vw[u][4 * j + 2] = x.z;
-                    vw[u][4 * j + 3] = x.w;
+                    for (int j = 0; j < 4; ++j) {
+                        const uint4 u = off < n ? __ldg(p + j) : make_uint4(0, 0, 0, 0);
+                        kw[h][4 * j] = u.x;
+                        kw[h][4 * j + 1] = u.y;
+                        kw[h][4 * j + 2] = u.z;
+                        kw[h][4 * j + 3] = u.w;
+                    }
                 }
-            }
-        };
-        load_k(0);
-        load_v(0);
+            };
+            auto load_v = [&](int i) {
+                const int n = nv[i];
+                const uint8_t *kb = nullptr, *vb = nullptr;
+                if (n > 0) rw.block_base(bk[i], g, a.hkv, (int)sizeof(T), kb, vb);
 #pragma unroll
-        for (int i = 0; i < TPW; ++i) {
-            const int n = nv[i];
-            // scores of the tile
-            float c4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            if (n > 0) {
+                for (int u = 0; u < 4; ++u) {
+                    const int off = 2 * t + (u & 1) + 8 * (u >> 1);
+                    const uint4* p = (const uint4*)(vb + off * rst + 32 * r);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint2 b = qf[kk * 32 + lane];
-                    mma16816<T>(c4, kw[0][2 * kk], kw[1][2 * kk], kw[0][2 * kk + 1], kw[1][2 * kk + 1], b.x, b.y);
+                    for (int j = 0; j < 2; ++j) {
+                        const uint4 x = off < n ? __ldg(p + j) : make_uint4(0, 0, 0, 0);
+                        vw[u][4 * j] = x.x;
+                        vw[u][4 * j + 1] = x.y;
+                        vw[u][4 * j + 2] = x.z;
+                        vw[u][4 * j + 3] = x.w;
+                    }
                 }
-            }
-            if (i + 1 < TPW) load_k(i + 1);
-            if (n > 0) {
-                const float s0 = r < n ? c4[0] * scale : -INFINITY, s1 = r < n ? c4[1] * scale : -INFINITY;
-                const float s2 = r + 8 < n ? c4[2] * scale : -INFINITY, s3 = r + 8 < n ? c4[3] * scale : -INFINITY;
+            };
+            load_k(0);
+            load_v(0);
+#pragma unroll
+            for (int i = 0; i < TPW; ++i) {
+                const int n = nv[i];
+                // scores of the tile
+                float c4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (n > 0) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint2 b = qf[kk * 32 + lane];
+                        mma16816<T>(c4, kw[0][2 * kk], kw[1][2 * kk], kw[0][2 * kk + 1], kw[1][2 * kk + 1], b.x, b.y);
+                    }
+                }
+                if (i + 1 < TPW) load_k(i + 1);
+                if (n > 0) {
+                    const float s0 = r < n ? c4[0] * scale : -INFINITY, s1 = r < n ? c4[1] * scale : -INFINITY;
+                    const float s2 = r + 8 < n ? c4[2] * scale : -INFINITY, s3 = r + 8 < n ? c4[3] * scale : -INFINITY;
 
-                // running softmax: the tile's maximum per head (row 0 of the tile is in range)
-                float t0 = fmaxf(s0, s2), t1 = fmaxf(s1, s3);
+                    // running softmax: the tile's maximum per head (row 0 of the tile is in range)
+                    float t0 = fmaxf(s0, s2), t1 = fmaxf(s1, s3);
 #pragma unroll
-                for (int o = 4; o < 32; o <<= 1) {
-                    t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
-                    t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
-                }
-                if (t0 > m0 || t1 > m1) {
-                    const float f0 = t0 > m0 ? __expf(m0 - t0) : 1.0f, f1 = t1 > m1 ? __expf(m1 - t1) : 1.0f;
-                    m0 = fmaxf(m0, t0);
-                    m1 = fmaxf(m1, t1);
-                    l0 *= f0;
-                    l1 *= f1;
+                    for (int o = 4; o < 32; o <<= 1) {
+                        t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
+                        t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, o));
+                    }
+                    if (t0 > m0 || t1 > m1) {
+                        const float f0 = t0 > m0 ? __expf(m0 - t0) : 1.0f, f1 = t1 > m1 ? __expf(m1 - t1) : 1.0f;
+                        m0 = fmaxf(m0, t0);
+                        m1 = fmaxf(m1, t1);
+                        l0 *= f0;
+                        l1 *= f1;
+#pragma unroll
+                        for (int mt = 0; mt < 8; ++mt) {
+                            acc[mt][0] *= f0;
+                            acc[mt][2] *= f0;
+                            acc[mt][1] *= f1;
+                            acc[mt][3] *= f1;
+                        }
+                    }
+                    const float e0 = __expf(s0 - m0), e1 = __expf(s1 - m1), e2 = __expf(s2 - m0), e3 = __expf(s3 - m1);
+                    l0 += e0 + e2;
+                    l1 += e1 + e3;
+
+                    // weights -> B registers (transposed through shared memory)
+                    __syncwarp();
+                    {
+                        uint32_t* pr = (uint32_t*)(pb + r * 8 + 2 * t);
+                        float x0, x1, x2, x3;
+                        pr[0] = pack2<T>(e0, e1, x0, x1);
+                        pr[32] = pack2<T>(e2, e3, x2, x3);  // row r + 8
+                        if constexpr (SPLIT) {
+                            pr[64] = pack2<T>(x0, x1);  // the low parts, rows 16..31
+                            pr[96] = pack2<T>(x2, x3);
+                        }
+                    }
+                    __syncwarp();
+                    uint32_t b0, b1, b2 = 0u, b3 = 0u;
+                    ldsm_x2_trans(b0, b1, (uint32_t)__cvta_generic_to_shared(pb + (lane & 15) * 8));
+                    if constexpr (SPLIT) ldsm_x2_trans(b2, b3, (uint32_t)__cvta_generic_to_shared(pb + (16 + (lane & 15)) * 8));
+
+                    // values: A register = one coordinate at two adjacent positions
 #pragma unroll
                     for (int mt = 0; mt < 8; ++mt) {
-                        acc[mt][0] *= f0;
-                        acc[mt][2] *= f0;
-                        acc[mt][1] *= f1;
-                        acc[mt][3] *= f1;
+                        const uint32_t a0 = __byte_perm(vw[0][mt], vw[1][mt], 0x5410u);
+                        const uint32_t a1 = __byte_perm(vw[0][mt], vw[1][mt], 0x7632u);
+                        const uint32_t a2 = __byte_perm(vw[2][mt], vw[3][mt], 0x5410u);
+                        const uint32_t a3 = __byte_perm(vw[2][mt], vw[3][mt], 0x7632u);
+                        mma16816<T>(acc[mt], a0, a1, a2, a3, b0, b1);
+                        if constexpr (SPLIT) mma16816<T>(acc[mt], a0, a1, a2, a3, b2, b3);
                     }
                 }
-                const float e0 = __expf(s0 - m0), e1 = __expf(s1 - m1), e2 = __expf(s2 - m0), e3 = __expf(s3 - m1);
-                l0 += e0 + e2;
-                l1 += e1 + e3;
-
-                // weights -> B registers (transposed through shared memory)
-                __syncwarp();
-                {
-                    uint32_t* pr = (uint32_t*)(pb + r * 8 + 2 * t);
-                    float x0, x1, x2, x3;
-                    pr[0] = pack2<T>(e0, e1, x0, x1);
-                    pr[32] = pack2<T>(e2, e3, x2, x3);  // row r + 8
-                    if constexpr (SPLIT) {
-                        pr[64] = pack2<T>(x0, x1);  // the low parts, rows 16..31
-                        pr[96] = pack2<T>(x2, x3);
-                    }
-                }
-                __syncwarp();
-                uint32_t b0, b1, b2 = 0u, b3 = 0u;
-                ldsm_x2_trans(b0, b1, (uint32_t)__cvta_generic_to_shared(pb + (lane & 15) * 8));
-                if constexpr (SPLIT) ldsm_x2_trans(b2, b3, (uint32_t)__cvta_generic_to_shared(pb + (16 + (lane & 15)) * 8));
-
-                // values: A register = one coordinate at two adjacent positions
-#pragma unroll
-                for (int mt = 0; mt < 8; ++mt) {
-                    const uint32_t a0 = __byte_perm(vw[0][mt], vw[1][mt], 0x5410u);
-                    const uint32_t a1 = __byte_perm(vw[0][mt], vw[1][mt], 0x7632u);
-                    const uint32_t a2 = __byte_perm(vw[2][mt], vw[3][mt], 0x5410u);
-                    const uint32_t a3 = __byte_perm(vw[2][mt], vw[3][mt], 0x7632u);
-                    mma16816<T>(acc[mt], a0, a1, a2, a3, b0, b1);
-                    if constexpr (SPLIT) mma16816<T>(acc[mt], a0, a1, a2, a3, b2, b3);
-                }
+                if (i + 1 < TPW) load_v(i + 1);
             }
-            if (i + 1 < TPW) load_v(i + 1);
+
         }
 
         // ── the warps' results, rescaled to the item's maximum and added in warp order ──
