@@ -48,7 +48,8 @@ struct Args {
     int kv_len, start;
     float* part;  // [rows, hq, nch, PART]
     int nch;
-    int ch;  // positions per chunk
+    int ch;   // positions per chunk
+    int rnd;  // tensor-core kernel: rounds of four 16-position tiles per warp and item
     void* out;
 };
 
@@ -309,7 +310,7 @@ __global__ void __launch_bounds__(128) kvp_combine(Args a) {
 // maximum and added in warp order.
 
 namespace tc {
-constexpr int TILE = 16, TPW = 4, RND = 4, CHM = NWARPS * RND * TPW * TILE;  // 2048 positions per item
+constexpr int TILE = 16, TPW = 4, MAX_RND = 4;  // an item: NWARPS * rnd * TPW * TILE positions, rnd <= MAX_RND
 
 struct Smem {
     static constexpr int acc_off = 0;                                  // [NWARPS][8][D] f32
@@ -383,7 +384,7 @@ __global__ void __launch_bounds__(THREADS, 2) kvp_mma(Args a, Rows rw, int items
         const int c = item % a.nch, rest = item / a.nch, g = rest % a.hkv, row = rest / a.hkv;
         const int s = row / a.q_per_seq, tq = row - s * a.q_per_seq;
         const int L = causal_len(a, s, tq);
-        const int p0 = c * CHM;
+        const int p0 = c * a.ch;
         if (p0 >= L) continue;  // the whole CTA
 
         // B registers of the score MMA, step kk, lane (r, t): the query of head r (zeros past
@@ -402,8 +403,8 @@ __global__ void __launch_bounds__(THREADS, 2) kvp_mma(Args a, Rows rw, int items
         for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
 
 #pragma unroll 1
-        for (int rd = 0; rd < RND; ++rd) {  // rounds of four tiles, one running softmax
-            const int pw = p0 + (warp * RND + rd) * TPW * TILE;
+        for (int rd = 0; rd < a.rnd; ++rd) {  // rounds of four tiles, one running softmax
+            const int pw = p0 + (warp * a.rnd + rd) * TPW * TILE;
             const int lim = min(L, a.max_blocks * 16);
             // the warp's tiles: block entry and positions in the cache (a prefix of the 16)
             int32_t bk[TPW];
@@ -640,16 +641,27 @@ int launch_tc(const Args& a, const Rows& rw, cudaStream_t s) {
     return (int)cudaGetLastError();
 }
 
+// Items of the tensor-core kernel as long as they stay at least six per CTA slot (two CTAs per
+// SM): long items pay the per-item cost (query staging, the warps' reduction, one partial) over
+// more positions, short ones keep small batches spread over the SMs.
+inline void tc_chunks(Args& a, int64_t positions, int64_t rows) {
+    int rnd = tc::MAX_RND;
+    const int64_t per_round = (int64_t)NWARPS * tc::TPW * tc::TILE;
+    while (rnd > 1 && (positions + per_round * rnd - 1) / (per_round * rnd) * a.hkv * rows < 12LL * num_sms()) rnd /= 2;
+    a.rnd = rnd;
+    a.ch = (int)(per_round * rnd);
+    a.nch = (int)((positions + a.ch - 1) / a.ch);
+}
+
 template <typename T, typename Rows>
 int run_t(Args a, const Rows& rw, cudaStream_t s) {
     const int rows = a.num_seqs * a.q_per_seq;
     if (rows == 0) return 0;
     a.ch = CH;
     // the tensor-core kernel reads the queries 16 bytes at a time; a.nch counts CH-position
-    // chunks (the workspace is sized for them), the tensor-core kernel takes CHM-position ones
+    // chunks (the workspace is sized for them), the tensor-core kernel takes larger ones
     if (aligned16(a.q)) {
-        a.ch = tc::CHM;
-        a.nch = (int)(((int64_t)a.nch * CH + tc::CHM - 1) / tc::CHM);
+        tc_chunks(a, (int64_t)a.nch * CH, rows);
         if (a.nch > 0) {
             const int rc = launch_tc<T>(a, rw, s);
             if (rc) return rc;

@@ -63,7 +63,8 @@ struct AttnArgs {
     float* qrot;  // [rows, hq, D]
     float* part;  // [rows, hq, nch, PART]
     int nch;
-    int ch;  // positions per chunk
+    int ch;   // positions per chunk
+    int rnd;  // tensor-core kernel: rounds of four 16-position tiles per warp and item
     sm100::DivU32 dnch, dhkv, dqps;  // nch, hkv, q_per_seq as multiply-high divisors (tensor-core kernel)
     void* out;
 };
@@ -501,7 +502,7 @@ __global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a) {
 // of an item the warps' results are rescaled to the item's maximum and added in warp order.
 
 namespace tc {
-constexpr int TILE = 16, TPW = 4, RND = 4, CHM = NWARPS * RND * TPW * TILE;  // 2048 positions per item
+constexpr int TILE = 16, TPW = 4, MAX_RND = 4;  // an item: NWARPS * rnd * TPW * TILE positions, rnd <= MAX_RND
 
 template <int KB, int VB>
 struct Smem {
@@ -576,7 +577,7 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
         const int c = item - (int)rest * a.nch, g = (int)rest - (int)rw_ * a.hkv, row = (int)rw_;
         const int s = (int)sm100::divu32(rw_, a.dqps), tq = row - s * a.q_per_seq;
         const int L = causal_len(a, s, tq);
-        const int p0 = c * CHM;
+        const int p0 = c * a.ch;
         if (p0 >= L) continue;  // the whole CTA
 
         // B registers of the score MMA, step kk, lane (r, t): q_rot of head r (zeros past the
@@ -595,9 +596,9 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
 #pragma unroll 1
-        for (int rd = 0; rd < RND; ++rd) {
+        for (int rd = 0; rd < a.rnd; ++rd) {
         // codes and norms of the round's four tiles of the warp, all requested before any is used
-        const int pw = p0 + (warp * RND + rd) * TPW * TILE;
+        const int pw = p0 + (warp * a.rnd + rd) * TPW * TILE;
         uint32_t kw[TPW][2][KW], vw[TPW][4][VW];
         float kn[TPW][2], vn[TPW][2];
         int nv[TPW];
@@ -886,6 +887,18 @@ int dispatch_tc(const AttnArgs& a, int vb, const Addr& ad, cudaStream_t s) {
 
 bool tc_ok(int kb, int vb) { return (kb == 2 || kb == 4) && (vb == 2 || vb == 4); }
 
+// Items of the tensor-core kernel as long as they stay at least six per CTA slot (two CTAs per
+// SM): long items pay the per-item cost (query staging, the warps' reduction, one partial) over
+// more positions, short ones keep small batches spread over the SMs.
+inline void tc_chunks(AttnArgs& a, int64_t positions, int64_t rows) {
+    int rnd = tc::MAX_RND;
+    const int64_t per_round = (int64_t)NWARPS * tc::TPW * tc::TILE;
+    while (rnd > 1 && (positions + per_round * rnd - 1) / (per_round * rnd) * a.hkv * rows < 12LL * num_sms()) rnd /= 2;
+    a.rnd = rnd;
+    a.ch = (int)(per_round * rnd);
+    a.nch = (int)((positions + a.ch - 1) / a.ch);
+}
+
 template <typename Addr>
 int run(AttnArgs a, int kb, int vb, const Addr& ad, cudaStream_t s) {
     const int rows = a.num_seqs * a.q_per_seq;
@@ -894,11 +907,10 @@ int run(AttnArgs a, int kb, int vb, const Addr& ad, cudaStream_t s) {
     int rc = (int)cudaGetLastError();
     if (rc) return rc;
     // a.nch counts CH-position chunks (the workspace is sized for them); the tensor-core
-    // path takes CHM-position chunks, so it uses fewer of the same partial slots
+    // path takes larger chunks, so it uses fewer of the same partial slots
     a.ch = CH;
     if (tc_ok(kb, vb)) {
-        a.ch = tc::CHM;
-        a.nch = (int)(((int64_t)a.nch * CH + tc::CHM - 1) / tc::CHM);
+        tc_chunks(a, (int64_t)a.nch * CH, rows);
         if (a.nch > 0) {
             rc = kb == 2 ? dispatch_tc<2>(a, vb, ad, s) : dispatch_tc<4>(a, vb, ad, s);
             if (rc) return rc;

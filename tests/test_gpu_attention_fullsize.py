@@ -1,5 +1,6 @@
 """Both paged attention paths at the bench's decode size (64 sequences x 1 query token at the end
-of an 8192-token context, 32 Q / 8 KV heads x 128, shuffled block tables over one pool), through
+of an 8192-token context, 32 Q / 8 KV heads x 128, shuffled block tables over one pool), and at
+32 and 1 sequences (the tensor-core kernels pick 2048-, 1024- and 512-position items), through
 a size-independent identity instead of the float64 statement (which would take minutes here):
 
 * TurboQuant cache: the attention equals plain softmax attention over the cache as this
@@ -21,11 +22,12 @@ from oracle import ops
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
-S, L, HQ, HKV, D = 64, 8192, 32, 8, 128
+L, HQ, HKV, D = 8192, 32, 8, 128
 NB = L // 16
+BATCHES = [64, 32, 1]
 
 
-def _setup(seed):
+def _setup(seed, S):
     g = torch.Generator(device=DEV).manual_seed(seed)
     tables = torch.randperm(S * NB, generator=g, device=DEV).to(torch.int32).view(S, NB)
     q = torch.randn((S, 1, HQ, D), generator=g, device=DEV).half()
@@ -42,8 +44,9 @@ def _sdpa(q, k, v):
     return out.permute(1, 0, 2)
 
 
-def test_tq_attention_equals_attention_over_the_dequantized_cache():
-    g, tables, q, kv_lens, starts = _setup(21)
+@pytest.mark.parametrize("S", BATCHES)
+def test_tq_attention_equals_attention_over_the_dequantized_cache(S):
+    g, tables, q, kv_lens, starts = _setup(21, S)
     KB, VB = 4, 2
     rows = S * L
     kp = torch.empty((rows, HKV * D * KB // 8), dtype=torch.uint8, device=DEV)
@@ -68,11 +71,12 @@ def test_tq_attention_equals_attention_over_the_dequantized_cache():
         ref[s] = _sdpa(q[s], khat, vhat)[0]
     torch.cuda.synchronize()
     ops.assert_close_fp(out[:, 0].float().cpu().numpy(), ref.cpu().numpy(), rel=2e-3, min_cos=0.9999,
-                        label="TurboQuant attention, 64 x 8192", dtype="f16")
+                        label=f"TurboQuant attention, {S} x 8192", dtype="f16")
 
 
-def test_fp16_attention_equals_attention_over_the_addressed_rows():
-    g, tables, q, kv_lens, starts = _setup(22)
+@pytest.mark.parametrize("S", BATCHES)
+def test_fp16_attention_equals_attention_over_the_addressed_rows(S):
+    g, tables, q, kv_lens, starts = _setup(22, S)
     kpool = torch.empty((S * L, HKV, D), dtype=torch.float16, device=DEV)
     vpool = torch.empty_like(kpool)
     for s in range(S):
@@ -87,4 +91,4 @@ def test_fp16_attention_equals_attention_over_the_addressed_rows():
         ref[s] = _sdpa(q[s], kpool[rows], vpool[rows])[0]
     torch.cuda.synchronize()
     ops.assert_close_fp(out[:, 0].float().cpu().numpy(), ref.cpu().numpy(), rel=2e-3, min_cos=0.9999,
-                        label="FP16 attention, 64 x 8192", dtype="f16")
+                        label=f"FP16 attention, {S} x 8192", dtype="f16")

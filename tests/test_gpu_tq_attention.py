@@ -91,8 +91,9 @@ def make_q(S, Tq, Hq, dt, seed):
                                         (4, 2, 4, "bf16"), (8, 4, 2, "bf16"), (2, 2, 2, "f16"), (4, 3, 2, "f16")])
 def test_decode_matches_statement(G, kb, vb, dt):
     """One query token per sequence at the end of its context (decode), contexts of 1 to 777
-    positions (one to four 256-position chunks of the CUDA-core kernel, one 2048-position chunk of
-    the tensor-core kernel), GQA groups of 1 to 8."""
+    positions (one to four 256-position chunks of the CUDA-core kernel, one or two 512-position
+    chunks of the tensor-core kernel, which takes short items for small batches), GQA groups of
+    1 to 8."""
     Hkv = 2
     kv_lens = [1, 300, 777]
     c = build_cache(kv_lens, Hkv, kb, vb, seed=10 * G + kb)
@@ -190,10 +191,10 @@ def test_reference_kernel_meets_the_bar_against_the_statement(kb, vb):
 
 @pytest.mark.parametrize("kb,vb", [(4, 2), (2, 2)])
 def test_chunk_boundaries_and_more_items_than_ctas(kb, vb):
-    """Contexts crossing the 2048-position chunk edge of the tensor-core kernel and, inside a
-    chunk, the edges between its warps (256 positions) and their rounds (64), with 40 prefill
-    query tokens per sequence: more (chunk, KV head, token) items than the persistent grid has
-    CTAs, so CTAs take several each."""
+    """Contexts crossing several chunk edges of the tensor-core kernel (512-position items at this
+    batch size; the full-size tests cover the longer ones), with 40 prefill query tokens per
+    sequence: more (chunk, KV head, token) items than the persistent grid has CTAs, so CTAs take
+    several each."""
     kv_lens, Tq, Hkv, G = [513, 1040, 1064, 2100], 40, 2, 4
     c = build_cache(kv_lens, Hkv, kb, vb, seed=60 + kb + vb)
     qh, q = make_q(len(kv_lens), Tq, G * Hkv, "f16", seed=61)
