@@ -14,7 +14,8 @@
 //                value rows (lane l: coordinates 4l..4l+3, one coalesced 8-byte load per
 //                position) for every head; the chunk's (max, sum, acc) go to the workspace
 //   kvp_mma      (queries 16-byte aligned, i.e. always through the Python and backend layers)
-//                replaces kvp_chunk: tensor cores, persistent CTAs, 512-position chunks; see below
+//                replaces kvp_chunk: tensor cores, persistent CTAs, chunks of 512 to 2048
+//                positions; see below
 //   kvp_combine  rescales and sums the chunks of each query token and head and divides
 //   kvp_append   writes new key/value rows into the pool through the block table
 //
@@ -289,8 +290,9 @@ __global__ void __launch_bounds__(128) kvp_combine(Args a) {
 
 // ── tensor-core path ──
 //
-// One work item = (512-position chunk, KV head, query token); persistent CTAs take items in
-// turn. Warp w takes positions 64w..64w+63 of the chunk as four 16-position tiles, one after the
+// One work item = (chunk of 512 x rnd positions, KV head, query token), rnd = 1, 2 or 4 chosen
+// per call (tc_chunks); persistent CTAs take items in turn. Warp w takes its 64 rnd positions of
+// the chunk as rnd rounds of four 16-position tiles, one after the
 // other (the next tile's rows requested into the registers the current one has finished with)
 // with its own running softmax (maximum, sum, accumulator) per head, and does both
 // contractions with mma.sync m16n8k16 (16-bit operands, FP32 accumulators) on operands loaded

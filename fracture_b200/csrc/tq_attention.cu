@@ -22,7 +22,7 @@
 //                   head h, column i of Pi_v shared by the group's heads through L1)
 //
 // With 2- or 4-bit keys and values, tqa_mma (tensor cores, below) replaces tqa_chunk: same
-// split-K partials, 2048-position chunks. 3- and 8-bit codes take tqa_chunk.
+// split-K partials, chunks of 512 to 2048 positions. 3- and 8-bit codes take tqa_chunk.
 //
 // Each KV head's codes are read once per query token for its whole group of Q heads. A
 // position whose block-table entry is negative, or whose pool row is out of range, is left
@@ -477,9 +477,10 @@ __global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a) {
 
 // ── tensor-core path: 2- and 4-bit keys and values ──
 //
-// One work item = (2048-position chunk, KV head, query token); a persistent CTA takes items
-// in turn and builds its decoding tables once. Warp w takes positions 256w..256w+255 of the
-// chunk in four rounds of four 16-position tiles (a round's codes all requested before any is
+// One work item = (chunk of 512 x rnd positions, KV head, query token), rnd = 1, 2 or 4 chosen per
+// call (tc_chunks); a persistent CTA takes items in turn and builds its decoding tables once.
+// Warp w takes positions 64 rnd w .. 64 rnd (w + 1) - 1 of the chunk in rnd rounds of four
+// 16-position tiles (a round's codes all requested before any is
 // used), keeps a running softmax (maximum, sum, accumulator) per head across the rounds, and
 // does both contractions with mma.sync m16n8k16 (FP16 operands, FP32 accumulators), the
 // operands decoded in registers:
