@@ -725,7 +725,7 @@ def run_tq_attention(args, local_rank: int) -> dict:
     pk = peaks()
     return {"workload": "TurboQuant paged attention (decode): 64 sequences x 1 query token, context 8192, "
                         "32 Q / 8 KV heads x 128, K 4-bit / V 2-bit, FP16 queries and output",
-            "kernels": "tqa_rotate_q + tqa_mma (persistent CTAs, 512-position split-K, mma.sync m16n8k16 on FP16 operands decoded in registers, FP32 accumulators) + tqa_combine",
+            "kernels": "tqa_rotate_q + tqa_mma (persistent CTAs, split-K over 2048-position items at this shape, mma.sync m16n8k16 on FP16 operands decoded in registers, FP32 accumulators) + tqa_combine",
             "ms_per_step": round(ms, 4), "query_tokens_per_s": round(S / (ms / 1e3), 1),
             "kv_positions_per_s": round(S * L / (ms / 1e3), 1), "algorithmic_bytes_per_step": by,
             "achieved_gbs": round(gbs, 1), "frac_of_peak": round(gbs / pk["hbm_gbs"], 4),
@@ -776,7 +776,7 @@ def run_attention_fp16(args, local_rank: int) -> dict:
     pk = peaks()
     return {"workload": "paged attention (decode) over the FP16 cache: 64 sequences x 1 query token, context 8192, "
                         "32 Q / 8 KV heads x 128",
-            "kernels": "kvp_mma (persistent CTAs, 512-position split-K, mma.sync m16n8k16 on the cache rows loaded straight into fragment registers, FP32 accumulators) + kvp_combine",
+            "kernels": "kvp_mma (persistent CTAs, split-K over 2048-position items at this shape, mma.sync m16n8k16 on the cache rows loaded straight into fragment registers, FP32 accumulators) + kvp_combine",
             "ms_per_step": round(ms, 4), "query_tokens_per_s": round(S / (ms / 1e3), 1),
             "kv_positions_per_s": round(S * L / (ms / 1e3), 1), "algorithmic_bytes_per_step": by,
             "achieved_gbs": round(gbs, 1), "frac_of_peak": round(gbs / pk["hbm_gbs"], 4),
