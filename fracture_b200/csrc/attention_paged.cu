@@ -265,6 +265,7 @@ __global__ void __launch_bounds__(THREADS) kvp_chunk(Args a, Rows rw) {
 // out = (sum_c acc_c e^(m_c - M)) / (sum_c l_c e^(m_c - M)); thread i: coordinate i of every head.
 template <typename T>
 __global__ void __launch_bounds__(128) kvp_combine(Args a) {
+    pdl_begin();
     const int row = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
     const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
     const int L = causal_len(a, s, t);
@@ -369,6 +370,7 @@ __device__ __forceinline__ uint32_t pack2(float x, float y) {
 
 template <typename T, typename Rows>
 __global__ void __launch_bounds__(THREADS, 2) kvp_mma(Args a, Rows rw, int items) {
+    pdl_begin();
     using namespace tc;
     constexpr bool SPLIT = dtype_of<T>::value == FB_BF16;
     extern __shared__ __align__(16) uint8_t sm[];
@@ -639,7 +641,8 @@ int launch_tc(const Args& a, const Rows& rw, cudaStream_t s) {
     }
     const int64_t items = (int64_t)a.nch * a.hkv * a.num_seqs * a.q_per_seq;
     if (items > INT32_MAX) return (int)cudaErrorInvalidValue;
-    kern<<<(int)std::min<int64_t>(items, slots[dev]), THREADS, smem, s>>>(a, rw, (int)items);
+    launch_pdl_smem(kern, dim3((unsigned)std::min<int64_t>(items, slots[dev])), dim3(THREADS), (size_t)smem, s, a, rw,
+                    (int)items);
     return (int)cudaGetLastError();
 }
 
@@ -676,7 +679,7 @@ int run_t(Args a, const Rows& rw, cudaStream_t s) {
         const int rc = a.hq / a.hkv <= 4 ? launch_chunk<T, 4>(a, rw, s) : launch_chunk<T, 8>(a, rw, s);
         if (rc) return rc;
     }
-    kvp_combine<T><<<dim3(rows, a.hq), 128, 0, s>>>(a);
+    launch_pdl(kvp_combine<T>, dim3(rows, a.hq), dim3(128), s, a);
     return (int)cudaGetLastError();
 }
 

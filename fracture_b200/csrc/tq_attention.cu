@@ -142,6 +142,7 @@ __device__ __forceinline__ float load_q(const AttnArgs& a, int64_t i) {
 
 // q_rot[row][h][i] = sum_j Pi_k[i][j] q[row][h][j] for the heads of KV group blockIdx.y.
 __global__ void __launch_bounds__(128) tqa_rotate_q(AttnArgs a) {
+    pdl_begin();
     __shared__ float qs[MAXG][D];
     const int row = blockIdx.x, g = blockIdx.y, G = a.hq / a.hkv;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -437,6 +438,7 @@ __global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
 // out[row][h][i] = sum_j Pi_v[j][i] * (sum_c acc_c[j] e^(m_c - M)) / (sum_c l_c e^(m_c - M)):
 // thread (h, i), 128 per head of KV group blockIdx.y.
 __global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a) {
+    pdl_begin();
     __shared__ float accs[MAXG][D];
     const int row = blockIdx.x, g = blockIdx.y, G = a.hq / a.hkv;
     const int h = threadIdx.x / D, i = threadIdx.x - h * D;
@@ -560,6 +562,7 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
 #pragma unroll
         for (int k = 0; k < 8; ++k) row[(k + j) & 7] = make_uint4(w, w, w, w);
     }
+    pdl_begin();  // the tables above read only the codebooks; what follows reads the rotate kernel's output
     __syncthreads();
     auto lut = [&](uint32_t addr) { return *reinterpret_cast<const uint32_t*>(sm + addr); };
 
@@ -877,7 +880,7 @@ int launch_tc(const AttnArgs& a, const Addr& ad, cudaStream_t s) {
     b.dnch = sm100::make_divu32((uint32_t)a.nch);
     b.dhkv = sm100::make_divu32((uint32_t)a.hkv);
     b.dqps = sm100::make_divu32((uint32_t)a.q_per_seq);
-    kern<<<grid, THREADS, smem, s>>>(b, ad, (int)items);
+    launch_pdl_smem(kern, dim3(grid), dim3(THREADS), (size_t)smem, s, b, ad, (int)items);
     return (int)cudaGetLastError();
 }
 
@@ -908,7 +911,7 @@ template <typename Addr>
 int run(AttnArgs a, int kb, int vb, const Addr& ad, cudaStream_t s) {
     const int rows = a.num_seqs * a.q_per_seq;
     if (rows == 0) return 0;
-    tqa_rotate_q<<<dim3(rows, a.hkv), 128, 0, s>>>(a);
+    launch_pdl(tqa_rotate_q, dim3(rows, a.hkv), dim3(128), s, a);
     int rc = (int)cudaGetLastError();
     if (rc) return rc;
     // a.nch counts CH-position chunks (the workspace is sized for them); the tensor-core
@@ -929,7 +932,7 @@ int run(AttnArgs a, int kb, int vb, const Addr& ad, cudaStream_t s) {
         }
         if (rc) return rc;
     }
-    tqa_combine<<<dim3(rows, a.hkv), (a.hq / a.hkv) * D, 0, s>>>(a);
+    launch_pdl(tqa_combine, dim3(rows, a.hkv), dim3((a.hq / a.hkv) * D), s, a);
     return (int)cudaGetLastError();
 }
 
