@@ -26,8 +26,8 @@
  *     and the FP16/BF16 paged KV cache of paged_kv_cache.rs.
  *
  * Stream order: every call is ordered after the work already on its stream.
- * Decode-sized elementwise, RoPE and small TurboQuant launches are
- * programmatic dependent launches: they may be scheduled while the previous
+ * Decode-sized elementwise, RoPE, small TurboQuant and paged-attention launches
+ * are programmatic dependent launches: they may be scheduled while the previous
  * kernel on the stream drains, and wait for it to complete (its writes
  * visible) before they touch memory, so the ordering is the same.
  *
