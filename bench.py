@@ -12,12 +12,15 @@ feed the chain (o_proj, down_proj, q/k, gate/up) are synthetic tensors of their
 real shapes. Every tensor the chain streams is larger than L2, so no L2 flush
 is needed between steps.
 
-Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): each rank runs
-its own 16 x 2048-token batch (weak scaling, sequences are independent: no
-data-path collective); value = all ranks' tokens / max-over-ranks time.
+Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): the job's 16
+sequences are split over the ranks (16/N per GPU; sequences are independent, so
+there is no data-path collective); value = the job's 32768 tokens / the slowest
+rank's time ("strong" scaling). The line also carries ``weak_scaling``, where
+every rank runs its own 16 x 2048 tokens.
 
-With ``--pipeline`` the line also carries ``pipeline_config5``
-(70B shapes, 80 layers split into N pipeline stages, NCCL handoff between stages).
+At N > 1 (or with ``--pipeline``) the line also carries ``pipeline_config5``:
+BASELINE config 5 (70B shapes, 80 layers split into N pipeline stages, NCCL
+handoff between stages), with the stage compute and the handoff timed apart.
 
 The same line carries ``tq_config4``: BASELINE config 4 (TurboQuant K+V of
 65536 tokens x 8 KV heads x 128 quantized into a paged cache and dequantized
@@ -120,108 +123,125 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch.distributed as dist
 
     from fracture_b200 import kernels as K
+    from fracture_b200 import shards
     from fracture_b200.backend import FB_BF16, CudaBackend
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    T = T_SEQ * N_SEQ
     bf = torch.bfloat16
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
-
-    def act(shape):
-        x = torch.randn(shape, generator=g, device=dev)
-        cols = torch.rand(shape[-1], generator=g, device=dev) < 0.001  # outlier channels x20
-        return torch.where(cols, x * 20.0, x).to(bf)
-
-    table = (torch.randn((VOCAB, HID), generator=g, device=dev) * 0.02).to(bf)
-    ids = torch.randint(0, VOCAB, (T,), generator=g, device=dev, dtype=torch.int32)
-    positions = (torch.arange(T, device=dev, dtype=torch.int32) % T_SEQ).contiguous()
-    h = torch.empty((T, HID), device=dev, dtype=bf)
-    normed = torch.empty_like(h)
-    attn_proj, ffn_out = act((T, HID)), act((T, HID))
-    q, k = act((T, NQ, HD)), act((T, NKV, HD))
-    gate, up = act((T, INTER)), act((T, INTER))
-    mid = torch.empty_like(gate)
-    wa = (1 + 0.02 * torch.randn((LAYERS, HID), generator=g, device=dev)).to(bf)
-    wf = (1 + 0.02 * torch.randn((LAYERS + 1, HID), generator=g, device=dev)).to(bf)
-    freqs = torch.from_numpy(K.rope_freqs_llama3(HD, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"],
-                                                 ROPE["orig"])).to(dev)
     stream = torch.cuda.current_stream(dev)
     s = stream.cuda_stream
-
-    # algorithmic bytes (each input read once, each output written once; weight rows once per launch)
+    freqs = torch.from_numpy(K.rope_freqs_llama3(HD, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"],
+                                                 ROPE["orig"])).to(dev)
     B = 2
-    by_embed = T * HID * B * 2 + T * 4
-    by_norm = T * HID * B * 2 + HID * B
-    by_addnorm = T * HID * B * 4 + HID * B
-    by_rope = T * (NQ + NKV) * HD * B * 2 + T * 4 + HD // 2 * 4
-    by_silu = T * INTER * B * 3
-    step_bytes = by_embed + by_norm + (2 * LAYERS - 1) * by_addnorm + LAYERS * by_rope + LAYERS * by_silu + by_addnorm
-    launches_per_step = 1 + 1 + (2 * LAYERS - 1) + LAYERS + LAYERS + 1
-
-    silu_events = []
-
-    def step(record_silu: bool):
-        K.embedding(h, table, ids, stream=s)
-        for l in range(LAYERS):
-            if l == 0:
-                K.rmsnorm(normed, h, wa[0], EPS, stream=s)
-            else:
-                K.add_rmsnorm(h, ffn_out, wa[l], normed, EPS, stream=s)
-            K.rope(q, k, positions, freqs, stream=s)
-            K.add_rmsnorm(h, attn_proj, wf[l], normed, EPS, stream=s)
-            if record_silu:
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                K.silu_mul(mid, gate, up, stream=s)
-                e1.record(stream)
-                silu_events.append((e0, e1))
-            else:
-                K.silu_mul(mid, gate, up, stream=s)
-        K.add_rmsnorm(h, ffn_out, wf[LAYERS], normed, EPS, stream=s)
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    for _ in range(args.warmup):
-        step(False)
-    torch.cuda.synchronize(dev)
-    barrier()
-    torch.cuda.synchronize(dev)
+    def chain_data(n_seq: int) -> dict:
+        T = T_SEQ * n_seq
+        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+        def act(shape):
+            x = torch.randn(shape, generator=g, device=dev)
+            cols = torch.rand(shape[-1], generator=g, device=dev) < 0.001  # outlier channels x20
+            return torch.where(cols, x * 20.0, x).to(bf)
+
+        d = {"T": T, "n_seq": n_seq,
+             "table": (torch.randn((VOCAB, HID), generator=g, device=dev) * 0.02).to(bf),
+             "ids": torch.randint(0, VOCAB, (T,), generator=g, device=dev, dtype=torch.int32),
+             "positions": (torch.arange(T, device=dev, dtype=torch.int32) % T_SEQ).contiguous(),
+             "h": torch.empty((T, HID), device=dev, dtype=bf)}
+        d["normed"] = torch.empty_like(d["h"])
+        d["attn_proj"], d["ffn_out"] = act((T, HID)), act((T, HID))
+        d["q"], d["k"] = act((T, NQ, HD)), act((T, NKV, HD))
+        d["gate"], d["up"] = act((T, INTER)), act((T, INTER))
+        d["mid"] = torch.empty_like(d["gate"])
+        d["wa"] = (1 + 0.02 * torch.randn((LAYERS, HID), generator=g, device=dev)).to(bf)
+        d["wf"] = (1 + 0.02 * torch.randn((LAYERS + 1, HID), generator=g, device=dev)).to(bf)
+        return d
+
+    def step_bytes(T: int) -> dict:
+        # algorithmic bytes (each input read once, each output written once; weight rows once per launch)
+        by = {"embed": T * HID * B * 2 + T * 4, "norm": T * HID * B * 2 + HID * B,
+              "addnorm": T * HID * B * 4 + HID * B, "rope": T * (NQ + NKV) * HD * B * 2 + T * 4 + HD // 2 * 4,
+              "silu": T * INTER * B * 3}
+        by["step"] = by["embed"] + by["norm"] + (2 * LAYERS - 1) * by["addnorm"] + LAYERS * by["rope"] \
+            + LAYERS * by["silu"] + by["addnorm"]
+        return by
+
+    launches_per_step = 1 + 1 + (2 * LAYERS - 1) + LAYERS + LAYERS + 1
+
+    def step(d, silu_events=None):
+        h, normed = d["h"], d["normed"]
+        K.embedding(h, d["table"], d["ids"], stream=s)
+        for l in range(LAYERS):
+            if l == 0:
+                K.rmsnorm(normed, h, d["wa"][0], EPS, stream=s)
+            else:
+                K.add_rmsnorm(h, d["ffn_out"], d["wa"][l], normed, EPS, stream=s)
+            K.rope(d["q"], d["k"], d["positions"], freqs, stream=s)
+            K.add_rmsnorm(h, d["attn_proj"], d["wf"][l], normed, EPS, stream=s)
+            if silu_events is not None:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                K.silu_mul(d["mid"], d["gate"], d["up"], stream=s)
+                e1.record(stream)
+                silu_events.append((e0, e1))
+            else:
+                K.silu_mul(d["mid"], d["gate"], d["up"], stream=s)
+        K.add_rmsnorm(h, d["ffn_out"], d["wf"][LAYERS], normed, EPS, stream=s)
+
+    def timed_chain(d, clocks=None):
+        """W untimed steps, then K steps between events, barrier + sync on both sides; the
+        max over ranks of the elapsed time, and this rank's silu_mul launch times."""
+        for _ in range(args.warmup):
+            step(d)
+        torch.cuda.synchronize(dev)
+        barrier()
+        torch.cuda.synchronize(dev)
+        if clocks:
+            clocks.start()
+            time.sleep(0.3)
+        silu_events = []
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step(d, silu_events)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        clock = clocks.stop() if clocks else None
+        barrier()
+        torch.cuda.synchronize(dev)
+        ms = shards.max_over_ranks(t0.elapsed_time(t1), dev)
+        return ms, [a.elapsed_time(b) for a, b in silu_events], clock
+
+    # Headline: the configured job of 16 x 2048 tokens, its sequences split over the ranks
+    # (strong scaling: 16/N sequences per GPU, no collective on the data path).
+    my_seqs = shards.sequence_shard(N_SEQ, world, rank)
+    d = chain_data(len(my_seqs))
+    T = d["T"]
+    by = step_bytes(T)
     clocks = Clocks(local_rank)
-    clocks.start()
-    time.sleep(0.3)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(args.steps):
-        step(True)
-    t1.record(stream)
-    torch.cuda.synchronize(dev)
-    clock = clocks.stop()
-    barrier()
-    torch.cuda.synchronize(dev)
-    elapsed_ms = t0.elapsed_time(t1)
-    silu_ms = [a.elapsed_time(b) for a, b in silu_events]
-    if world > 1:
-        t = torch.tensor([elapsed_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
+    elapsed_ms, silu_ms, clock = timed_chain(d, clocks)
 
     # ── e2e through the reference-facing backend API (host buffers) ──
     be = CudaBackend(local_rank)
     be.precompute_rope_freqs_llama3(HD, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"], ROPE["orig"])
     reg = lambda t_, shape: be.register_external(t_.data_ptr(), shape, FB_BF16)
-    Th, Tn, Ta, Tf = reg(h, (T, HID)), reg(normed, (T, HID)), reg(attn_proj, (T, HID)), reg(ffn_out, (T, HID))
-    Tq, Tk = reg(q, (T, NQ, HD)), reg(k, (T, NKV, HD))
-    Tg, Tu, Tm = reg(gate, (T, INTER)), reg(up, (T, INTER)), reg(mid, (T, INTER))
-    Ttab = reg(table, (VOCAB, HID))
-    Twa = [reg(wa[l], (HID,)) for l in range(LAYERS)]
-    Twf = [reg(wf[l], (HID,)) for l in range(LAYERS + 1)]
-    last = be.alloc((N_SEQ, HID), FB_BF16)
+    Th, Tn = reg(d["h"], (T, HID)), reg(d["normed"], (T, HID))
+    Ta, Tf = reg(d["attn_proj"], (T, HID)), reg(d["ffn_out"], (T, HID))
+    Tq, Tk = reg(d["q"], (T, NQ, HD)), reg(d["k"], (T, NKV, HD))
+    Tg, Tu, Tm = reg(d["gate"], (T, INTER)), reg(d["up"], (T, INTER)), reg(d["mid"], (T, INTER))
+    Ttab = reg(d["table"], (VOCAB, HID))
+    Twa = [reg(d["wa"][l], (HID,)) for l in range(LAYERS)]
+    Twf = [reg(d["wf"][l], (HID,)) for l in range(LAYERS + 1)]
+    ns = d["n_seq"]
+    last = be.alloc((ns, HID), FB_BF16)
     host_ids = np.random.default_rng(rank).integers(0, VOCAB, T).astype(np.uint32)
-    pos_sets = [np.tile(np.arange(T_SEQ, dtype=np.uint32), N_SEQ), np.tile(np.arange(1, T_SEQ + 1, dtype=np.uint32), N_SEQ)]
-    out_host = np.empty(N_SEQ * HID * 2, dtype=np.uint8)
+    pos_sets = [np.tile(np.arange(T_SEQ, dtype=np.uint32), ns), np.tile(np.arange(1, T_SEQ + 1, dtype=np.uint32), ns)]
+    out_host = np.empty(ns * HID * 2, dtype=np.uint8)
 
     def e2e_step(i):
         pos = pos_sets[i % 2]  # a new forward: positions change, uploaded once, reused by all 32 layers
@@ -236,7 +256,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             be.silu_mul(Tg, Tu, Tm)
         be.add(Th, Tf, Th)
         be.rmsnorm(Th, Twf[LAYERS], EPS, Tn)
-        for sq in range(N_SEQ):
+        for sq in range(ns):
             be.copy_rows(Tn, last, sq * T_SEQ + T_SEQ - 1, sq, 1)
         be.copy_to_host(last, out_host)  # synchronous: the step's result is on the host
 
@@ -248,23 +268,32 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     w0 = time.perf_counter()
     for i in range(e2e_steps):
         e2e_step(i)
-    e2e_s = time.perf_counter() - w0
-    if world > 1:
-        t = torch.tensor([e2e_s], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = shards.max_over_ranks(time.perf_counter() - w0, dev)
     be.close()
+    del d
+
+    # The weak-scaling variant (every rank its own 16 x 2048 tokens), kept as a second figure.
+    weak = None
+    if world > 1:
+        dw = chain_data(N_SEQ)
+        ms_w, _, _ = timed_chain(dw)
+        del dw
+        ms_step_w = ms_w / args.steps
+        weak = {"tokens_per_gpu": T_SEQ * N_SEQ, "ms_per_step": round(ms_step_w, 4),
+                "value": round(world * T_SEQ * N_SEQ / (ms_step_w / 1e3), 1), "unit": "tokens/s",
+                "frac_of_peak_per_gpu": round(step_bytes(T_SEQ * N_SEQ)["step"] / (ms_step_w / 1e3) / 1e9
+                                              / peaks()["hbm_gbs"], 4)}
 
     if rank != 0:
         return None
     pk = peaks()
     ms_step = elapsed_ms / args.steps
-    value = world * T / (ms_step / 1e3)
+    value = T_SEQ * N_SEQ / (ms_step / 1e3)  # the whole job's tokens over the slowest rank's time
     silu_avg = statistics.mean(silu_ms)
-    achieved = by_silu / (silu_avg / 1e3) / 1e9
+    achieved = by["silu"] / (silu_avg / 1e3) / 1e9
     traffic = None  # DRAM bytes per launch from the committed ncu capture of this kernel at this size
     tf = ROOT / "profiles" / "silu_mul_bf16_config3.md"
-    if tf.exists():
+    if tf.exists() and world == 1:
         import re
 
         m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", tf.read_text())
@@ -278,25 +307,26 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "warmup": args.warmup,
         "ms_per_step": round(ms_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) activations, 0.1% channels x20; random-init norm weights and embedding table)",
-        "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "sequences_per_gpu": N_SEQ, "seq_len": T_SEQ,
+        "config": {"workload": WORKLOAD, "tokens": T_SEQ * N_SEQ, "sequences": N_SEQ, "tokens_per_gpu": T,
+                   "sequences_per_gpu": len(my_seqs), "seq_len": T_SEQ,
                    "hidden": HID, "heads": f"{NQ}/{NKV}x{HD}", "intermediate": INTER, "layers": LAYERS,
                    "vocab": VOCAB, "rope": "llama3 factor 8, low 1, high 4, original 8192, theta 5e5",
-                   "parallelism": f"dp{world} (sequence-sharded replicas, no collective on the data path)",
-                   "l2": "every streamed tensor > 126 MB L2 (no flush needed)"},
-        "hbm": {"algorithmic_bytes_per_step": step_bytes,
-                "achieved_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1),
-                "frac_of_peak": round(step_bytes / (ms_step / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+                   "parallelism": f"dp{world} (the 16 sequences split over the GPUs, no collective on the data path)",
+                   "l2": "each step streams far more than the 126 MB L2 (no flush needed)"},
+        "hbm": {"algorithmic_bytes_per_step_per_gpu": by["step"],
+                "achieved_gbs_per_gpu": round(by["step"] / (ms_step / 1e3) / 1e9, 1),
+                "frac_of_peak": round(by["step"] / (ms_step / 1e3) / 1e9 / pk["hbm_gbs"], 4),
                 "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"]},
         "roofline": {"kernel": "silu_mul_vec_kernel<bf16> (50% of the step's bytes)", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
-                     "algorithmic_bytes_per_launch": by_silu, "avg_launch_ms": round(silu_avg, 5),
+                     "algorithmic_bytes_per_launch": by["silu"], "avg_launch_ms": round(silu_avg, 5),
                      "peak_source": pk["source"]},
-        "e2e": {"value": round(world * T / (e2e_s / e2e_steps), 1) if e2e_steps else None, "unit": "tokens/s",
+        "e2e": {"value": round(T_SEQ * N_SEQ / (e2e_s / e2e_steps), 1) if e2e_steps else None, "unit": "tokens/s",
                 "h2d_bytes_per_step": int(host_ids.nbytes + pos_sets[0].nbytes),
                 "d2h_bytes_per_step": int(out_host.nbytes),
                 "path": "fracture_b200.backend.CudaBackend (C-ABI Backend mirror): embedding/add/rmsnorm/rope/silu_mul, "
@@ -304,6 +334,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clock,
     }
+    if weak is not None:
+        res["weak_scaling"] = weak
     return res
 
 
@@ -481,6 +513,7 @@ def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
     slot_base = torch.arange(c["seqs"], device=dev, dtype=torch.int64).view(G, gs) * seq_rows
     slots_dec = torch.empty((G, gs), device=dev, dtype=torch.int64)
     graphs = []
+    replay_events = []
 
     def group_body(gr):
         layers(hdec[gr], gs, pos_dec, slots_dec[gr])
@@ -507,7 +540,11 @@ def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
                 else:
                     link.irecv(h).wait()
                 if graphs:
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
                     graphs[gr].replay()
+                    e1.record()
+                    replay_events.append((e0, e1))
                 else:
                     group_body(gr)
                 if rank < world - 1:
@@ -551,10 +588,47 @@ def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     reps = max(1, min(args.steps, 2))
     ms_pre = timed(prefill, reps)
+
+    # Where the prefill time goes. (1) Stage compute alone: one micro-batch through this stage's
+    # layers, no handoff. (2) The handoff alone: every boundary moves one micro-batch at once
+    # (stage s -> s + 1), nothing else running. The pipelined prefill is compared with
+    # (micro-batches + stages - 1) x the slowest stage's compute, its bubble included.
+    def compute_only():
+        layers(rbuf[0], mb_tokens, pos_prefill, slots_prefill[0])
+
+    ms_compute = timed(compute_only, 4)
+    handoff = None
+    if world > 1:
+        import torch.distributed as dist
+
+        def boundary_exchange():
+            ops = []
+            if rank < world - 1:
+                ops.append(dist.P2POp(dist.isend, rbuf[1], rank + 1))
+            if rank > 0:
+                ops.append(dist.P2POp(dist.irecv, rbuf[2], rank - 1))
+            for w_ in dist.batch_isend_irecv(ops):
+                w_.wait()
+
+        ms_handoff = timed(boundary_exchange, 8)
+        mb_bytes = mb_tokens * H * 2
+        handoff = {"bytes_per_microbatch": mb_bytes, "ms_per_microbatch": round(ms_handoff, 4),
+                   "gbs_per_boundary": round(mb_bytes / (ms_handoff / 1e3) / 1e9, 1),
+                   "peer_copy_reference_gbs": 770.0,
+                   "all_microbatches_ms": round(ms_handoff * n_mb, 3),
+                   "bytes_per_boundary": n_mb * mb_bytes}
+    ideal_pre = (n_mb + world - 1) * ms_compute
+
     decode()  # eager pass: sizes every workspace before capture
     capture_decode_graphs()
+    replay_events.clear()
     ms_dec = timed(decode, 1)
     graphs.clear()
+    # the timed pass is the second decode() call inside timed(): the last n_replays events
+    n_replays = c["decode"] * G
+    replay_ms = sum(e0.elapsed_time(e1) for e0, e1 in replay_events[-n_replays:])
+    replay_events.clear()
+    replay_ms = shards.max_over_ranks(replay_ms, dev)
     # algorithmic bytes per token per layer (BF16 activations; 4-bit K and V into the pool)
     by_tok_layer = 2 * (4 * H * 2) + (NQ5 + NKV5) * HD5 * 2 * 2 + 4 + 3 * I5 * 2 \
         + 2 * (NKV5 * HD5 * 2 + NKV5 * (P + 2) + 8)
@@ -572,12 +646,27 @@ def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
             "handoff": "NCCL send/recv of BF16 hidden states between neighbouring stages (decode: next tokens "
                        "from the last stage back to stage 0)" if world > 1 else "none (one stage)",
             "prefill": {"ms": round(ms_pre, 3), "tokens_per_s": round(pre_tokens / (ms_pre / 1e3), 1),
+                        "micro_batches": n_mb,
                         "stage_algorithmic_bytes": stage_bytes_pre,
                         "stage_achieved_gbs": round(stage_bytes_pre / (ms_pre / 1e3) / 1e9, 1),
                         "stage_frac_of_peak": round(stage_bytes_pre / (ms_pre / 1e3) / 1e9 / pk["hbm_gbs"], 4),
-                        "handoff_bytes_per_boundary": pre_tokens * H * 2},
+                        "handoff_bytes_per_boundary": pre_tokens * H * 2,
+                        "breakdown": {
+                            "stage_compute_ms_per_microbatch": round(ms_compute, 4),
+                            "stage_compute_gbs": round(by_tok_layer * nl * mb_tokens / (ms_compute / 1e3) / 1e9, 1),
+                            "pipelined_ideal_ms": round(ideal_pre, 3),
+                            "pipeline_overhead_ms": round(ms_pre - ideal_pre, 3),
+                            "handoff_alone": handoff,
+                            "note": "ideal = (micro-batches + stages - 1) x the slowest stage's compute per "
+                                    "micro-batch (bubble included); overhead = measured - ideal is the exposed "
+                                    "cost of the handoffs and of stage imbalance"}},
             "decode": {"ms": round(ms_dec, 3), "tokens_per_s": round(dec_tokens / (ms_dec / 1e3), 1),
                        "groups": G, "group_sequences": gs,
+                       "breakdown": {"graph_replay_ms_busiest_stage": round(replay_ms, 3),
+                                     "outside_graphs_ms": round(ms_dec - replay_ms, 3),
+                                     "note": "graph replays = the stage's layers (device time between events "
+                                             "around each replay, summed); the rest of the decode time is the "
+                                             "handoff waits, embedding and launch gaps"},
                        "launch": "one CUDA graph per group and stage per step (layers of the stage); NCCL "
                                  "handoffs and the embedding outside the graphs"},
             "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"]}
@@ -784,49 +873,57 @@ def run_attention_fp16(args, local_rank: int) -> dict:
             "l2": "the 2.1 GB cache is larger than L2 (no flush)"}
 
 
-def cpu_baseline(tokens: int, layers: int, reps: int) -> dict:
+CPU_TOKENS, CPU_LAYERS = 1024, 8  # the CPU sample both arms time: a slice of the config-3 job
+
+
+def cpu_sample(warmup: int, reps: int) -> dict:
+    """The reference's CPU path (oracle/cpu_chain.py, torch on every host thread) on a bounded sample
+    of the config-3 workload: CPU_TOKENS tokens through CPU_LAYERS layers of the chain, with the
+    full 128,256-row embedding table. Both the GPU arm's ``cpu_baseline`` and ``--impl reference``
+    run this same function, so their numbers differ only by run-to-run noise."""
     import torch
 
     from oracle import cpu_chain, ops
 
     n = cpu_chain.set_threads()
     inv = ops.rope_freqs_llama3(HD, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"], ROPE["orig"])
-    data = cpu_chain.make_data(tokens, HID, NQ, NKV, HD, INTER, layers, 4096, torch.bfloat16)
-    cpu_chain.run_chain(data, inv)  # warm-up
-    secs = min(cpu_chain.run_chain(data, inv) for _ in range(reps))
-    tok_s = tokens / (secs * LAYERS / layers)
-    return {"value": round(tok_s, 2), "unit": "tokens/s", "cores": n, "kind": "port",
-            "sample": f"{tokens} tokens x {layers} layers of the config-3 chain (BF16 storage, f32 math, torch CPU, "
-                      f"4096-row embedding table), best of {reps}; tokens/s scaled to the 32-layer chain"}
+    data = cpu_chain.make_data(CPU_TOKENS, HID, NQ, NKV, HD, INTER, CPU_LAYERS, VOCAB, torch.bfloat16)
+    for _ in range(max(1, warmup)):
+        cpu_chain.run_chain(data, inv)
+    secs = [cpu_chain.run_chain(data, inv) for _ in range(reps)]
+    per_step = statistics.mean(secs) * LAYERS / CPU_LAYERS  # scaled to the 32-layer chain
+    value = CPU_TOKENS / per_step
+    return {"value": round(value, 2), "unit": "tokens/s", "cores": n, "kind": "port",
+            "seconds_per_step": per_step,
+            "sample": f"{CPU_TOKENS} tokens x {CPU_LAYERS} layers of the config-3 chain (BF16 storage, f32 math, "
+                      f"torch CPU on {n} threads, full {VOCAB}-row embedding table), mean of {reps} runs after "
+                      f"{max(1, warmup)} warm-up; tokens/s scaled to the 32-layer chain"}
+
+
+def cpu_baseline(reps: int = 3) -> dict:
+    r = cpu_sample(1, reps)
+    r.pop("seconds_per_step")
+    return r
 
 
 def run_reference(args, rank: int) -> dict | None:
     """The reference's CPU path on the host cores; rank 0 only (other ranks exit without work)."""
     if rank != 0:
         return None
-    tokens, layers = 1024, 8
-    import torch
-
-    from oracle import cpu_chain, ops
-
-    n = cpu_chain.set_threads()
-    inv = ops.rope_freqs_llama3(HD, ROPE["theta"], ROPE["factor"], ROPE["low"], ROPE["high"], ROPE["orig"])
-    data = cpu_chain.make_data(tokens, HID, NQ, NKV, HD, INTER, layers, 4096, torch.bfloat16)
-    for _ in range(args.warmup):
-        cpu_chain.run_chain(data, inv)
-    secs = [cpu_chain.run_chain(data, inv) for _ in range(args.steps)]
-    per_step = statistics.mean(secs) * LAYERS / layers  # scaled to the 32-layer chain
-    value = tokens / per_step
+    cb = cpu_sample(args.warmup, args.steps)
+    per_step = cb.pop("seconds_per_step")
+    value = cb["value"]
     return {
         "impl": "reference",
-        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": 0, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 0, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 2), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "tokens_per_step_sample": tokens, "layers_timed": layers},
-        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": n, "kind": "port",
-                         "sample": f"{tokens} tokens x {layers} layers per step (scaled to 32 layers); the "
-                                   "reference's PyTorch-CPU numerical path (oracle/cpu_chain.py)"},
-        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": {"workload": WORKLOAD, "tokens": T_SEQ * N_SEQ, "sequences": N_SEQ, "seq_len": T_SEQ,
+                   "hidden": HID, "heads": f"{NQ}/{NKV}x{HD}", "intermediate": INTER, "layers": LAYERS,
+                   "vocab": VOCAB, "rope": "llama3 factor 8, low 1, high 4, original 8192, theta 5e5",
+                   "tokens_per_step_sample": CPU_TOKENS, "layers_timed": CPU_LAYERS},
+        "cpu_baseline": cb,
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
@@ -909,7 +1006,8 @@ def main() -> None:
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode-shaped measurement")
     ap.add_argument("--no-attention", action="store_true", help="skip the TurboQuant paged-attention measurement")
     ap.add_argument("--pipeline", action="store_true",
-                    help="also run config 5 (70B-shaped pipeline over the ranks, NCCL stage handoff)")
+                    help="run config 5 (70B-shaped pipeline, NCCL stage handoff) at N=1 too (default: N > 1 only)")
+    ap.add_argument("--no-pipeline", action="store_true", help="skip config 5")
     ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding", "tq_compress",
                                                                    "tq_dequant", "tq_attention", "attention_fp16"],
                     help="run only this kernel at its config-3 size (W warm-up launches + 1), for ncu captures")
@@ -939,7 +1037,8 @@ def main() -> None:
                                 device_id=torch.device("cuda", local_rank))
     res = run_ours(args, rank, world, local_rank)
     tq = None if args.no_tq else run_tq_config4(args, rank, world, local_rank)
-    c5 = run_config5(args, rank, world, local_rank) if args.pipeline else None
+    c5 = run_config5(args, rank, world, local_rank) if (args.pipeline or world > 1) and not args.no_pipeline \
+        else None
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -954,7 +1053,7 @@ def main() -> None:
         res["attention_fp16"] = run_attention_fp16(args, local_rank)
     if res is not None:
         if world == 1 and not args.no_cpu_baseline:
-            res["cpu_baseline"] = cpu_baseline(tokens=2048, layers=16, reps=3)
+            res["cpu_baseline"] = cpu_baseline(reps=3)
         print(json.dumps(res), flush=True)
 
 

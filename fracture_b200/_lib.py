@@ -66,6 +66,7 @@ SIGNATURES = {
                                         C.c_size_t, vp, vp]),
     "fb_launch_kv_append_paged": (i32, [vp, vp, i32, i64, i32, i32, vp, i64, i64, vp, vp, vp, vp]),
     "fb_tq_timeouts": (C.c_uint, []),
+    "fb_tq_path_counts": (i32, [C.POINTER(C.c_ulonglong), i32]),
     "fb_rope_freqs": (i32, [i32, C.c_double, f32p]),
     "fb_rope_freqs_llama3": (i32, [i32, C.c_double, C.c_double, C.c_double, C.c_double, C.c_double, f32p]),
     "fb_tq_codebook": (i32, [i32, i32, f32p, f32p]),

@@ -24,6 +24,7 @@
 // token with no position gives zeros.
 
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 
@@ -623,12 +624,13 @@ template <typename T, typename Rows>
 int launch_tc(const Args& a, const Rows& rw, cudaStream_t s) {
     constexpr int smem = tc::Smem::bytes;
     auto kern = kvp_mma<T, Rows>;
-    static int slots[64];  // CTAs per device, found on the first launch on that device
+    static std::atomic<int> slots[64];  // CTAs per device, found on the first launch on that device
+    // (two threads making their first launch at once both compute the same value)
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
     if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-    if (slots[dev] == 0) {
+    if (slots[dev].load(std::memory_order_relaxed) == 0) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return (int)e;
         int per_sm = 0, sms = 0;
@@ -637,11 +639,11 @@ int launch_tc(const Args& a, const Rows& rw, cudaStream_t s) {
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return (int)e;
         if (per_sm < 1) return (int)cudaErrorInvalidConfiguration;
-        slots[dev] = per_sm * sms;
+        slots[dev].store(per_sm * sms, std::memory_order_relaxed);
     }
     const int64_t items = (int64_t)a.nch * a.hkv * a.num_seqs * a.q_per_seq;
     if (items > INT32_MAX) return (int)cudaErrorInvalidValue;
-    launch_pdl_smem(kern, dim3((unsigned)std::min<int64_t>(items, slots[dev])), dim3(THREADS), (size_t)smem, s, a, rw,
+    launch_pdl_smem(kern, dim3((unsigned)std::min<int64_t>(items, slots[dev].load(std::memory_order_relaxed))), dim3(THREADS), (size_t)smem, s, a, rw,
                     (int)items);
     return (int)cudaGetLastError();
 }

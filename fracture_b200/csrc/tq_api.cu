@@ -6,6 +6,8 @@
 
 #include <cstdio>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "tq_common.cuh"
 
@@ -16,6 +18,15 @@ void set_last_error(const char* msg);
 }
 
 using namespace fb;
+
+// Calls served per path since the library was loaded: compress small / tensor-core / exact, then
+// dequantize small / tensor-core / exact (fb_tq_path_counts).
+static std::atomic<unsigned long long> g_tq_path_calls[6];
+
+static int count_path(int which, int rc) {
+    if (rc == 0) g_tq_path_calls[which].fetch_add(1, std::memory_order_relaxed);
+    return rc;
+}
 
 static bool tq_bits_ok(int bits) { return bits == 2 || bits == 3 || bits == 4 || bits == 8; }
 
@@ -52,11 +63,11 @@ static int tq_compress_any(const void* input, int dtype, const float* rotation, 
     a.packed_pool = packed_pool;
     a.norms_pool = norms_pool;
     a.err_count = err_count;
-    if (tq_small_compress_call(a)) return tq_compress_small(a, (cudaStream_t)stream);
+    if (tq_small_compress_call(a)) return count_path(0, tq_compress_small(a, (cudaStream_t)stream));
     bool handled = false;
     rc = tq_compress_umma(a, (cudaStream_t)stream, &handled);
-    if (handled) return rc;
-    return tq_compress_exact(a, (cudaStream_t)stream);
+    if (handled) return count_path(1, rc);
+    return count_path(2, tq_compress_exact(a, (cudaStream_t)stream));
 }
 
 extern "C" int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotation, const float* centroids,
@@ -150,11 +161,11 @@ static int tq_dequant_any(const void* packed_pool, const void* norms_pool, const
     a.norms_pool = const_cast<void*>(norms_pool);
     a.output = output;
     a.out_dtype = dtype;
-    if (tq_small_dequant_call(a)) return tq_dequant_small(a, (cudaStream_t)stream);
+    if (tq_small_dequant_call(a)) return count_path(3, tq_dequant_small(a, (cudaStream_t)stream));
     bool handled = false;
     rc = tq_dequant_umma(a, (cudaStream_t)stream, &handled);
-    if (handled) return rc;
-    return tq_dequant_exact(a, (cudaStream_t)stream);
+    if (handled) return count_path(4, rc);
+    return count_path(5, tq_dequant_exact(a, (cudaStream_t)stream));
 }
 
 extern "C" int fb_launch_tq_dequant_paged(const void* packed_pool, const void* norms_pool, const float* rotation,
@@ -193,4 +204,10 @@ extern "C" int launch_turboquant_decompress(const void* packed_in, const void* n
         return (int)cudaErrorInvalidValue;
     return fb_launch_tq_dequant_paged(packed_in, norms_in, rotation, centroids, bits, num_tokens, num_kv_heads,
                                       head_dim, nullptr, 0, num_tokens, output, FB_FP16, stream);
+}
+
+extern "C" int fb_tq_path_counts(unsigned long long* counts, int n) {
+    if (!counts || n < 0) return (int)cudaErrorInvalidValue;
+    for (int i = 0; i < n && i < 6; ++i) counts[i] = g_tq_path_calls[i].load(std::memory_order_relaxed);
+    return 0;
 }

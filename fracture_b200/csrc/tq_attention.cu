@@ -29,6 +29,7 @@
 // out; a query token with no position gives zeros.
 
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "tq_sm100.cuh"
@@ -562,7 +563,11 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
 #pragma unroll
         for (int k = 0; k < 8; ++k) row[(k + j) & 7] = make_uint4(w, w, w, w);
     }
-    pdl_begin();  // the tables above read only the codebooks; what follows reads the rotate kernel's output
+    // The tables above read only the codebooks, before the wait: this is safe because run() always
+    // launches tqa_rotate_q (which waits for the work before it) right before this kernel, and
+    // nothing writes the codebooks in between. A chain that drops or reorders rotate_q must move
+    // the table build after pdl_begin().
+    pdl_begin();  // what follows reads the rotate kernel's output
     __syncthreads();
     auto lut = [&](uint32_t addr) { return *reinterpret_cast<const uint32_t*>(sm + addr); };
 
@@ -857,12 +862,13 @@ template <int KB, int VB, typename Addr>
 int launch_tc(const AttnArgs& a, const Addr& ad, cudaStream_t s) {
     constexpr int smem = tc::Smem<KB, VB>::bytes;
     auto kern = tqa_mma<KB, VB, Addr>;
-    static int slots[64];  // CTAs per device, found on the first launch on that device
+    static std::atomic<int> slots[64];  // CTAs per device, found on the first launch on that device
+    // (two threads making their first launch at once both compute the same value)
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
     if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-    if (slots[dev] == 0) {
+    if (slots[dev].load(std::memory_order_relaxed) == 0) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return (int)e;
         int per_sm = 0, sms = 0;
@@ -871,11 +877,11 @@ int launch_tc(const AttnArgs& a, const Addr& ad, cudaStream_t s) {
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return (int)e;
         if (per_sm < 1) return (int)cudaErrorInvalidConfiguration;
-        slots[dev] = per_sm * sms;
+        slots[dev].store(per_sm * sms, std::memory_order_relaxed);
     }
     const int64_t items = (int64_t)a.nch * a.hkv * a.num_seqs * a.q_per_seq;
     if (items > INT32_MAX) return (int)cudaErrorInvalidValue;
-    const int grid = (int)std::min<int64_t>(items, slots[dev]);
+    const int grid = (int)std::min<int64_t>(items, slots[dev].load(std::memory_order_relaxed));
     AttnArgs b = a;
     b.dnch = sm100::make_divu32((uint32_t)a.nch);
     b.dhkv = sm100::make_divu32((uint32_t)a.hkv);

@@ -5,7 +5,8 @@
 // sequential sums with separately rounded multiply and add (__fmul_rn /
 // __fadd_rn, so nothing is contracted to an FMA), true division by
 // (norm + 1e-8), nearest centroid with the first minimum winning. They serve
-// every head_dim up to 256 and any input alignment; the tensor-core kernel in
+// every head_dim up to 192 (the limit the entry points check) and any input
+// alignment; the tensor-core kernel in
 // tq_umma.cu takes head_dim 128 and reuses the per-coordinate routine here to
 // settle coordinates that fall near a decision boundary.
 //

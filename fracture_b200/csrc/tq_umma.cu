@@ -683,8 +683,7 @@ int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled) {
     if (!aligned16(a.input) || !aligned16(a.packed_pool) || (((uintptr_t)a.norms_pool) & 1)) return 0;
     if (((uintptr_t)a.rotation & 15) != 0) return 0;
     if (a.num_tokens * a.num_heads > ((int64_t)1 << 31) - umma::TILE) return 0;
-    static int sm100 = -1;
-    if (sm100 < 0) sm100 = device_is_sm100() ? 1 : 0;
+    static const bool sm100 = device_is_sm100();  // thread-safe one-time initialisation
     if (!sm100) return 0;
     *handled = true;
     if (a.in_dtype == FB_FP16) {

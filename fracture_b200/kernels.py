@@ -105,6 +105,17 @@ def tq_dequant_slots(packed_pool, norms_pool, rotation, centroids, bits, out, sl
         slot_map.data_ptr(), rows, out.data_ptr(), _dt(out), _stream(stream)), "tq_dequant_slots")
 
 
+TQ_PATHS = ("compress_small", "compress_tensor_core", "compress_exact", "dequant_small", "dequant_tensor_core",
+            "dequant_exact")
+
+
+def tq_path_counts() -> dict:
+    """Calls served so far by each TurboQuant kernel family (fb_tq_path_counts)."""
+    arr = (C.c_ulonglong * 6)()
+    _ok(_lib.load().fb_tq_path_counts(arr, 6), "fb_tq_path_counts")
+    return dict(zip(TQ_PATHS, (int(v) for v in arr)))
+
+
 def tq_attention_workspace_bytes(num_seqs, q_per_seq, num_q_heads, max_kv_len) -> int:
     return int(_lib.load().fb_tq_attention_workspace_bytes(num_seqs, q_per_seq, num_q_heads, max_kv_len))
 

@@ -90,7 +90,11 @@ int launch_turboquant_decompress(const void* packed_in, const void* norms_in, co
  * v_block_ptrs[b] (device arrays of device pointers, [16, Hkv, d] each). Token t attends positions
  * [0, min(start_pos + t + 1, kv_len)). head_dim 128, Hq/Hkv in {1, 2, 4, 8}; float32 math. Uses a
  * device workspace owned by this library, one per device and stream, grown to the largest call on
- * that stream and kept until exit (calls on different streams may run at the same time). */
+ * that stream and kept until exit (calls on different streams may run at the same time). Growing
+ * it calls cudaFree/cudaMalloc, which a stream being captured into a CUDA graph refuses: make a
+ * call of the largest size on the stream before capturing. The workspace is keyed by the stream
+ * handle, so do not call on a handle that was destroyed and reused while work queued on the old
+ * stream may still be running. */
 int launch_paged_attention(void* output, const void* q, const int* block_table, const void** k_block_ptrs,
                            const void** v_block_ptrs, int num_tokens, int num_q_heads, int num_kv_heads,
                            int head_dim, int kv_len, int start_pos, int num_blocks_in_seq, void* stream);
@@ -105,7 +109,9 @@ int launch_paged_attention(void* output, const void* q, const int* block_table, 
  * fp16 operands), 3- and 8-bit codes on CUDA cores in float32 with the 3-bit centroid values read
  * as fp16; all within the 2e-3 FP bar of the float32 statement. Uses a device workspace owned by
  * this library, one per device and stream, grown to the largest call on that stream and kept until
- * exit (calls on different streams may run at the same time). */
+ * exit (calls on different streams may run at the same time), with the same two caveats as
+ * launch_paged_attention: a warm-up call of the largest size before graph capture, and no call on
+ * a recycled stream handle while the old stream's work may still be running. */
 int launch_attention_paged_tq(void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
                               const void** k_norms_ptrs, const void** v_packed_ptrs, const void** v_norms_ptrs,
                               const float* k_rotation, const float* v_rotation, const float* k_centroids,
@@ -169,6 +175,12 @@ int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype, const floa
                                         int head_dim, const int32_t* block_table, int64_t start_pos,
                                         int64_t num_pool_rows, void* packed_pool, void* norms_pool,
                                         unsigned int* err_count, void* stream);
+
+/* Which TurboQuant kernels served the compress / dequantize calls made so far in this process (no
+ * reference counterpart; for tests and diagnostics): counts[0..2] = compress calls that took the
+ * small-call kernel (tq_small.cu), the tensor-core kernel (tq_umma.cu) and the exact CUDA-core
+ * kernel (tq_exact.cu); counts[3..5] the same for dequantize. Writes min(n, 6) counters. */
+int fb_tq_path_counts(unsigned long long* counts, int n);
 
 /* Batched append (no reference counterpart; the reference appends one sequence at a time,
  * quantized_paged_kv_cache.rs:404-500, called per sequence from batched.rs:324-350): as

@@ -303,32 +303,51 @@ def test_tensor_core_path_bit_exact_many_tiles(dt, bits):
     assert bad_rows.size == 0, f"{bad_rows.size} token rows differ, first {bad_rows[:5]}"
 
 
-def test_tensor_core_path_adversarial_vectors():
+SMALL_CALL_VECTORS = 1024  # kTqSmallCompressVectors: larger calls take the tensor-core kernel
+
+
+def _compress_on_path(x, dt, pi, c, bits, expect_tensor_core):
+    """Compresses x ([T, H, 128], values) and checks which kernel family served the call."""
+    T, H, d = x.shape
+    P = d * bits // 8
+    packed = torch.zeros((T, H * P), dtype=torch.uint8, device=DEV)
+    norms = torch.zeros((T, H), dtype=torch.float16, device=DEV)
+    before = K.tq_path_counts()
+    K.tq_compress_paged(dev(x, dt), torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed, norms)
+    torch.cuda.synchronize()
+    after = K.tq_path_counts()
+    path = "compress_tensor_core" if expect_tensor_core else "compress_small"
+    assert after[path] == before[path] + 1, (before, after)
+    return packed.cpu().numpy(), norms.cpu().numpy()
+
+
+@pytest.mark.parametrize("T", [40, 300])
+def test_tensor_core_path_adversarial_vectors(T):
     """Vectors aligned with rows of Pi (|y_i| = 1), zero vectors, tiny and huge fp16 values,
-    and vectors placed exactly on decision boundaries."""
-    T, H, d, bits = 40, 8, 128, 4
+    and vectors placed exactly on decision boundaries, at the start and in the middle of the
+    call: 40 tokens x 8 heads take the small-call kernel, 300 x 8 (2400 vectors) the tensor-core
+    kernel (the call asserts which one ran). Bit-exact against the exact statement."""
+    H, d, bits = 8, 128, 4
     pi, c = tables(d, bits, 42)
     rng = np.random.default_rng(5)
     x = rng.standard_normal((T, H, d)).astype(np.float32)
-    x[0, :] = pi[:H, :]            # x = row i of Pi  ->  y = e_i
-    x[1, :] = 0.0
-    x[2, :] = 6e-8                 # fp16 subnormal
-    x[3, :] = 60000.0
-    x[4, :, :] = 0.0
-    x[4, :, 0] = 1.0               # y = Pi[:, 0]
     mids = (c[:-1] + c[1:]) / 2
-    for h in range(H):             # y lands on a boundary (to fp16 rounding of x)
-        y = rng.choice(mids, d)
-        x[5, h] = pi.T.astype(np.float64) @ y
+    for r0 in sorted({0, T // 2 + 3}):
+        x[r0 + 0, :] = pi[:H, :]       # x = row i of Pi  ->  y = e_i
+        x[r0 + 1, :] = 0.0
+        x[r0 + 2, :] = 6e-8            # fp16 subnormal
+        x[r0 + 3, :] = 60000.0
+        x[r0 + 4, :, :] = 0.0
+        x[r0 + 4, :, 0] = 1.0          # y = Pi[:, 0]
+        for h in range(H):             # y lands on a boundary (to fp16 rounding of x)
+            y = rng.choice(mids, d)
+            x[r0 + 5, h] = pi.T.astype(np.float64) @ y
     x = ops.round_to(x, "f16")
     raw = ops.to_storage_bytes(x, "f16").reshape(x.shape)
-    packed = torch.zeros((T, H * 64), dtype=torch.uint8, device=DEV)
-    norms = torch.zeros((T, H), dtype=torch.float16, device=DEV)
-    K.tq_compress_paged(dev(x, "f16"), torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed, norms)
-    torch.cuda.synchronize()
-    pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits)
-    assert np.array_equal(packed.cpu().numpy(), pc)
-    assert np.array_equal(norms.cpu().numpy().view(np.uint16), nc)
+    got_p, got_n = _compress_on_path(x, "f16", pi, c, bits, T * H > SMALL_CALL_VECTORS)
+    pc, nc, _ = tq.compress_c(raw, tq.INPUT_F16, pi, c, bits, num_threads=4)
+    assert np.array_equal(got_p, pc)
+    assert np.array_equal(got_n.view(np.uint16), nc)
 
 
 def _boundary_codebook(values, n_levels):
@@ -376,31 +395,31 @@ def test_tensor_core_path_queue_overflow():
     assert np.array_equal(norms.cpu().numpy().view(np.uint16), nc)
 
 
+@pytest.mark.parametrize("T", [64, 260])
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
-def test_tensor_core_path_non_finite_rows(dt):
+def test_tensor_core_path_non_finite_rows(dt, T):
     """Rows holding NaN or +-inf (and, for BF16, values whose squares overflow float32) next to
-    ordinary rows of the same warp: the tensor-core path keeps every table index in range, and
-    every row equals the exact statement (NaN rows code to index 0; NaN norms compared as NaN)."""
-    T, H, d, bits = 64, 8, 128, 4
+    ordinary rows of the same warp, at the start and in the middle of the call: 64 x 8 vectors
+    take the small-call kernel, 260 x 8 the tensor-core kernel (asserted), which keeps every table
+    index in range. Every row equals the exact statement (NaN rows code to index 0; NaN norms
+    compared as NaN)."""
+    H, d, bits = 8, 128, 4
     x, _ = make_input(T, H, d, dt, seed=21)
-    x[0, 1, 5] = np.nan
-    x[1, 2, 0] = np.inf
-    x[2, 3, 7] = -np.inf
-    x[3, 4, 9], x[3, 4, 10] = np.inf, -np.inf
-    x[9, 0, :] = np.nan
-    if dt == "bf16":
-        x[5, 6, :] = 1e30  # |x|^2 overflows float32: norm = inf, y = 0
-        x[6, 7, 3] = -3e38
+    for r0 in sorted({0, T // 2 + 1}):
+        x[r0 + 0, 1, 5] = np.nan
+        x[r0 + 1, 2, 0] = np.inf
+        x[r0 + 2, 3, 7] = -np.inf
+        x[r0 + 3, 4, 9], x[r0 + 3, 4, 10] = np.inf, -np.inf
+        x[r0 + 9, 0, :] = np.nan
+        if dt == "bf16":
+            x[r0 + 5, 6, :] = 1e30  # |x|^2 overflows float32: norm = inf, y = 0
+            x[r0 + 6, 7, 3] = -3e38
     x = ops.round_to(x, dt)
     raw = ops.to_storage_bytes(x, dt).reshape(x.shape)
     pi, c = tables(d, bits, 42)
-    packed = torch.zeros((T, H * 64), dtype=torch.uint8, device=DEV)
-    norms = torch.zeros((T, H), dtype=torch.float16, device=DEV)
-    K.tq_compress_paged(dev(x, dt), torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV), bits, packed, norms)
-    torch.cuda.synchronize()
-    pc, nc, _ = tq.compress_c(raw, KIND[dt], pi, c, bits)
-    assert np.array_equal(packed.cpu().numpy(), pc)
-    got = norms.cpu().numpy()
+    got_p, got = _compress_on_path(x, dt, pi, c, bits, T * H > SMALL_CALL_VECTORS)
+    pc, nc, _ = tq.compress_c(raw, KIND[dt], pi, c, bits, num_threads=4)
+    assert np.array_equal(got_p, pc)
     exp = nc.view(np.float16)
     both_nan = np.isnan(got) & np.isnan(exp)
     assert np.array_equal(got.view(np.uint16)[~both_nan], nc[~both_nan])
