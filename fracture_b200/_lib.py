@@ -44,6 +44,7 @@ SIGNATURES = {
     "launch_turboquant_compress": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]),
     "launch_turboquant_decompress": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "launch_attention_paged_tq": (i32, [vp] * 11 + [i32] * 10 + [vp]),
+    "launch_attention_paged_tq_noalloc": (i32, [vp] * 11 + [i32] * 10 + [vp]),
     "launch_paged_attention": (i32, [vp] * 5 + [i32] * 7 + [vp]),
     # 2. new kernel entry points
     "fb_launch_embedding": (i32, [vp, vp, vp, i64, i64, i64, i32, vp]),
@@ -53,8 +54,6 @@ SIGNATURES = {
     "fb_launch_rope": (i32, [vp, vp, vp, vp, i64, i32, i32, i32, i32, vp]),
     "fb_launch_silu_mul": (i32, [vp, vp, vp, i64, i32, vp]),
     "fb_launch_tq_compress_paged": (i32, [vp, i32, vp, vp, i32, i64, i32, i32, vp, i64, i64, vp, vp, vp, vp]),
-    "fb_launch_tq_compress_paged_noalloc": (i32, [vp, i32, vp, vp, i32, i64, i32, i32, vp, i64, i64, vp, vp, vp,
-                                                  vp]),
     "fb_launch_tq_dequant_paged": (i32, [vp, vp, vp, vp, i32, i64, i32, i32, vp, i64, i64, vp, i32, vp]),
     "fb_launch_tq_compress_slots": (i32, [vp, i32, vp, vp, i32, i64, i32, i32, vp, i64, vp, vp, vp, vp]),
     "fb_launch_tq_dequant_slots": (i32, [vp, vp, vp, vp, i32, i64, i32, i32, vp, i64, vp, i32, vp]),

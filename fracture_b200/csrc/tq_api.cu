@@ -4,8 +4,6 @@
 // (backends/fracture-cuda/src/ffi.rs:220-247) write/read the compact
 // [T, Hkv * P] layout; they are the paged entry points with no block table.
 
-#include <cstdio>
-
 #include <atomic>
 
 #include "common.cuh"
@@ -14,7 +12,6 @@
 namespace fb {
 int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled);
 int tq_dequant_umma(const TqArgs& a, cudaStream_t s, bool* handled);
-void set_last_error(const char* msg);
 }
 
 using namespace fb;
@@ -87,52 +84,6 @@ extern "C" int fb_launch_tq_compress_slots(const void* input, int dtype, const f
     if (!slot_map && num_tokens > 0) return (int)cudaErrorInvalidValue;
     return tq_compress_any(input, dtype, rotation, centroids, bits, num_tokens, num_kv_heads, head_dim, nullptr,
                            slot_map, 0, num_pool_rows, packed_pool, norms_pool, err_count, stream);
-}
-
-// Same contract as fb_launch_tq_compress_paged, which allocates no device memory (the settle
-// queue of the tensor-core path is in shared memory), with a per-call limit of
-// kTqNoAllocMaxVectors vectors: larger calls are rejected before anything is launched.
-extern "C" int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype, const float* rotation,
-                                                   const float* centroids, int bits, int64_t num_tokens,
-                                                   int num_kv_heads, int head_dim, const int32_t* block_table,
-                                                   int64_t start_pos, int64_t num_pool_rows, void* packed_pool,
-                                                   void* norms_pool, unsigned int* err_count, void* stream) {
-    int rc = tq_check_common(bits, num_tokens, num_kv_heads, head_dim, num_pool_rows);
-    if (rc) return rc;
-    if (dtype != FB_FP16 && dtype != FB_BF16 && dtype != FB_FP32) return (int)cudaErrorInvalidValue;
-    if (start_pos < 0) return (int)cudaErrorInvalidValue;
-    if (num_tokens > kTqNoAllocMaxVectors / num_kv_heads) {
-        char msg[200];
-        snprintf(msg, sizeof msg,
-                 "fb_launch_tq_compress_paged_noalloc: %lld tokens x %d KV heads exceed the per-call "
-                 "limit of %lld vectors",
-                 (long long)num_tokens, num_kv_heads, (long long)kTqNoAllocMaxVectors);
-        set_last_error(msg);
-        return (int)cudaErrorInvalidValue;
-    }
-    if (num_tokens == 0) return 0;
-    if (!input || !rotation || !centroids || !packed_pool || !norms_pool) return (int)cudaErrorInvalidValue;
-    TqArgs a{};
-    a.input = input;
-    a.in_dtype = dtype;
-    a.rotation = rotation;
-    a.centroids = centroids;
-    a.bits = bits;
-    a.n_levels = 1 << bits;
-    a.num_tokens = num_tokens;
-    a.num_heads = num_kv_heads;
-    a.head_dim = head_dim;
-    a.block_table = block_table;
-    a.start_pos = start_pos;
-    a.pool_rows = num_pool_rows;
-    a.packed_pool = packed_pool;
-    a.norms_pool = norms_pool;
-    a.err_count = err_count;
-    if (tq_small_compress_call(a)) return tq_compress_small(a, (cudaStream_t)stream);
-    bool handled = false;
-    rc = tq_compress_umma(a, (cudaStream_t)stream, &handled);
-    if (handled) return rc;
-    return tq_compress_exact(a, (cudaStream_t)stream);
 }
 
 static int tq_dequant_any(const void* packed_pool, const void* norms_pool, const float* rotation,

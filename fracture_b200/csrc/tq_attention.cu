@@ -30,6 +30,8 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 #include "tq_sm100.cuh"
@@ -1060,15 +1062,17 @@ extern "C" int fb_launch_tq_attention_paged(const void* q, int dtype, int num_se
 }
 
 // The reference ABI (ffi.rs:251-274, attention_paged_tq.cu:261-309): one sequence, FP16, a
-// device block table and per-block pointer arrays. The workspace is this library's, one per
-// device and stream, grown to the largest call on that stream and kept.
-extern "C" int launch_attention_paged_tq(void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
-                                         const void** k_norms_ptrs, const void** v_packed_ptrs,
-                                         const void** v_norms_ptrs, const float* k_rotation, const float* v_rotation,
-                                         const float* k_centroids, const float* v_centroids, int num_tokens,
-                                         int num_q_heads, int num_kv_heads, int head_dim, int kv_len, int start_pos,
-                                         int key_bits, int value_bits, int k_packed_dim_per_head,
-                                         int v_packed_dim_per_head, void* stream) {
+// device block table and per-block pointer arrays. ref_abi_check validates a call and sizes its
+// workspace; ref_abi_run enqueues it on a given workspace.
+namespace {
+
+int ref_abi_check(const void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
+                  const void** k_norms_ptrs, const void** v_packed_ptrs, const void** v_norms_ptrs,
+                  const float* k_rotation, const float* v_rotation, const float* k_centroids,
+                  const float* v_centroids, int num_tokens, int num_q_heads, int num_kv_heads, int head_dim,
+                  int kv_len, int start_pos, int key_bits, int value_bits, int k_packed_dim_per_head,
+                  int v_packed_dim_per_head, size_t* need) {
+    *need = 0;
     if (!tqa::shape_ok(num_q_heads, num_kv_heads, head_dim) || !tqa::bits_ok(key_bits) || !tqa::bits_ok(value_bits))
         return (int)cudaErrorInvalidValue;
     if (k_packed_dim_per_head != (head_dim * key_bits + 7) / 8 ||
@@ -1081,29 +1085,133 @@ extern "C" int launch_attention_paged_tq(void* output, const void* q, const int*
     if (kv_len > 0 && (!block_table || !k_packed_ptrs || !k_norms_ptrs || !v_packed_ptrs || !v_norms_ptrs))
         return (int)cudaErrorInvalidValue;
     const int nch = (kv_len + tqa::CH - 1) / tqa::CH;
-    const size_t need = tqa::workspace_bytes(num_tokens, num_q_heads, nch);
+    *need = tqa::workspace_bytes(num_tokens, num_q_heads, nch);
+    return 0;
+}
+
+int ref_abi_run(void* ws, void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
+                const void** k_norms_ptrs, const void** v_packed_ptrs, const void** v_norms_ptrs,
+                const float* k_rotation, const float* v_rotation, const float* k_centroids, const float* v_centroids,
+                int num_tokens, int num_q_heads, int num_kv_heads, int kv_len, int start_pos, int key_bits,
+                int value_bits, void* stream) {
+    tqa::AttnArgs a{};
+    a.q = q;
+    a.dtype = FB_FP16;
+    a.num_seqs = 1;
+    a.q_per_seq = num_tokens;
+    a.hq = num_q_heads;
+    a.hkv = num_kv_heads;
+    a.block_tables = block_table;
+    a.max_blocks = (kv_len + 15) / 16;
+    a.kv_len = kv_len;
+    a.start = start_pos;
+    a.pik = k_rotation;
+    a.piv = v_rotation;
+    a.ck = k_centroids;
+    a.cv = v_centroids;
+    a.qrot = (float*)ws;
+    a.part = a.qrot + (int64_t)num_tokens * num_q_heads * tqa::D;
+    a.nch = (kv_len + tqa::CH - 1) / tqa::CH;
+    a.out = output;
+    tqa::BlockPtrAddr ad{(const uint8_t* const*)k_packed_ptrs, (const __half* const*)k_norms_ptrs,
+                         (const uint8_t* const*)v_packed_ptrs, (const __half* const*)v_norms_ptrs};
+    return tqa::run(a, key_bits, value_bits, ad, (cudaStream_t)stream);
+}
+
+}  // namespace
+
+// The workspace is this library's, one per device and stream, grown to the largest call on that
+// stream and kept.
+extern "C" int launch_attention_paged_tq(void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
+                                         const void** k_norms_ptrs, const void** v_packed_ptrs,
+                                         const void** v_norms_ptrs, const float* k_rotation, const float* v_rotation,
+                                         const float* k_centroids, const float* v_centroids, int num_tokens,
+                                         int num_q_heads, int num_kv_heads, int head_dim, int kv_len, int start_pos,
+                                         int key_bits, int value_bits, int k_packed_dim_per_head,
+                                         int v_packed_dim_per_head, void* stream) {
+    size_t need = 0;
+    const int rc = ref_abi_check(output, q, block_table, k_packed_ptrs, k_norms_ptrs, v_packed_ptrs, v_norms_ptrs,
+                                 k_rotation, v_rotation, k_centroids, v_centroids, num_tokens, num_q_heads,
+                                 num_kv_heads, head_dim, kv_len, start_pos, key_bits, value_bits,
+                                 k_packed_dim_per_head, v_packed_dim_per_head, &need);
+    if (rc || num_tokens == 0) return rc;
     return with_stream_workspace(stream, need, [&](void* ws) {
-        tqa::AttnArgs a{};
-        a.q = q;
-        a.dtype = FB_FP16;
-        a.num_seqs = 1;
-        a.q_per_seq = num_tokens;
-        a.hq = num_q_heads;
-        a.hkv = num_kv_heads;
-        a.block_tables = block_table;
-        a.max_blocks = (kv_len + 15) / 16;
-        a.kv_len = kv_len;
-        a.start = start_pos;
-        a.pik = k_rotation;
-        a.piv = v_rotation;
-        a.ck = k_centroids;
-        a.cv = v_centroids;
-        a.qrot = (float*)ws;
-        a.part = a.qrot + (int64_t)num_tokens * num_q_heads * tqa::D;
-        a.nch = nch;
-        a.out = output;
-        tqa::BlockPtrAddr ad{(const uint8_t* const*)k_packed_ptrs, (const __half* const*)k_norms_ptrs,
-                             (const uint8_t* const*)v_packed_ptrs, (const __half* const*)v_norms_ptrs};
-        return tqa::run(a, key_bits, value_bits, ad, (cudaStream_t)stream);
+        return ref_abi_run(ws, output, q, block_table, k_packed_ptrs, k_norms_ptrs, v_packed_ptrs, v_norms_ptrs,
+                           k_rotation, v_rotation, k_centroids, v_centroids, num_tokens, num_q_heads, num_kv_heads,
+                           kv_len, start_pos, key_bits, value_bits, stream);
     });
+}
+
+// ── launch_attention_paged_tq without any allocation ─────────────────────────
+//
+// Some callers cannot allocate device memory when they call attention: an engine whose KV pool
+// was sized to take all free memory at start-up (a cudaMalloc mid-step would fail), and a decode
+// loop that must not stall on the device-wide synchronisation cudaFree implies when the library
+// workspace of launch_attention_paged_tq grows. This variant keeps the rotated queries and the
+// split-K partials in a fixed array of device memory that is part of the library image instead.
+//
+// The array is a file-scope __device__ variable: every GPU on which the library's module is
+// loaded holds its kTqaNoAllocScratchBytes until the process exits. In host code its name is a
+// host-side stand-in, not a device address, so the address handed to the kernels comes from
+// cudaGetSymbolAddress, looked up once per device (with that device current) on the first call
+// made on it. All calls share the array and it keeps the last call's contents: nothing in it has
+// to start at zero (the kernels write every rotated query and every partial the combine step
+// reads before reading it), but two calls that can overlap on the GPU (on different streams, or
+// on different host threads without ordering) race on it.
+
+constexpr size_t kTqaNoAllocScratchBytes = FB_TQA_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_tqa_noalloc_scratch[kTqaNoAllocScratchBytes];
+
+namespace {
+
+std::mutex g_tqa_noalloc_mu;
+void* g_tqa_noalloc_addr[64];  // device address of g_tqa_noalloc_scratch, per device ordinal
+
+int tqa_noalloc_scratch(void** addr) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(g_tqa_noalloc_mu);
+    if (!g_tqa_noalloc_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_tqa_noalloc_scratch);
+        if (e != cudaSuccess) return (int)e;
+        g_tqa_noalloc_addr[dev] = p;
+    }
+    *addr = g_tqa_noalloc_addr[dev];
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int launch_attention_paged_tq_noalloc(void* output, const void* q, const int* block_table,
+                                                 const void** k_packed_ptrs, const void** k_norms_ptrs,
+                                                 const void** v_packed_ptrs, const void** v_norms_ptrs,
+                                                 const float* k_rotation, const float* v_rotation,
+                                                 const float* k_centroids, const float* v_centroids, int num_tokens,
+                                                 int num_q_heads, int num_kv_heads, int head_dim, int kv_len,
+                                                 int start_pos, int key_bits, int value_bits,
+                                                 int k_packed_dim_per_head, int v_packed_dim_per_head, void* stream) {
+    size_t need = 0;
+    int rc = ref_abi_check(output, q, block_table, k_packed_ptrs, k_norms_ptrs, v_packed_ptrs, v_norms_ptrs,
+                           k_rotation, v_rotation, k_centroids, v_centroids, num_tokens, num_q_heads, num_kv_heads,
+                           head_dim, kv_len, start_pos, key_bits, value_bits, k_packed_dim_per_head,
+                           v_packed_dim_per_head, &need);
+    if (rc || num_tokens == 0) return rc;
+    if (need > kTqaNoAllocScratchBytes) {
+        char msg[256];
+        snprintf(msg, sizeof msg,
+                 "launch_attention_paged_tq_noalloc: %d query tokens x %d heads over %d positions need %zu bytes "
+                 "of scratch, more than its fixed %zu",
+                 num_tokens, num_q_heads, kv_len, need, kTqaNoAllocScratchBytes);
+        set_last_error(msg);
+        return (int)cudaErrorInvalidValue;
+    }
+    void* ws = nullptr;
+    rc = tqa_noalloc_scratch(&ws);
+    if (rc) return rc;
+    return ref_abi_run(ws, output, q, block_table, k_packed_ptrs, k_norms_ptrs, v_packed_ptrs, v_norms_ptrs,
+                       k_rotation, v_rotation, k_centroids, v_centroids, num_tokens, num_q_heads, num_kv_heads, kv_len,
+                       start_pos, key_bits, value_bits, stream);
 }

@@ -6,9 +6,6 @@
 
 namespace fb {
 
-// Largest call (num_tokens * num_kv_heads) accepted by the no-allocation compress entry point.
-constexpr int64_t kTqNoAllocMaxVectors = (int64_t)1 << 19;
-
 // Calls of at most this many head vectors (num_tokens * num_kv_heads) take the small-call exact
 // kernels of tq_small.cu (a few vectors per CTA, none of the tensor-core kernels' set-up):
 // where they beat the tensor-core kernels on B200 (GPU time of graph-replayed calls, head_dim

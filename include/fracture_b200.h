@@ -119,6 +119,30 @@ int launch_attention_paged_tq(void* output, const void* q, const int* block_tabl
                               int head_dim, int kv_len, int start_pos, int key_bits, int value_bits,
                               int k_packed_dim_per_head, int v_packed_dim_per_head, void* stream);
 
+/* launch_attention_paged_tq for callers that cannot allocate device memory (no counterpart in the
+ * reference). An engine that sized its KV pool to take all free memory at start-up cannot have a
+ * cudaMalloc succeed mid-step, and a decode loop must not stall on the device-wide synchronisation
+ * of the cudaFree that growing launch_attention_paged_tq's workspace implies. This entry point
+ * allocates nothing: the rotated queries and split-K partials live in one fixed array of
+ * FB_TQA_NOALLOC_SCRATCH_BYTES (4 MiB) of device memory inside the library image, which every GPU
+ * that loads the library holds until the process exits. Same arguments, kernels and results as
+ * launch_attention_paged_tq (bit for bit). A call needs
+ *   num_tokens * num_q_heads * (512 + 520 * ceil(kv_len / 256)) bytes
+ * of it (one decode token with 32 Q heads: contexts up to 64,256 positions); a larger call returns
+ * cudaErrorInvalidValue, with the reason in fb_last_error(), before anything is enqueued. The
+ * first call on a device looks the array's device address up (cudaGetSymbolAddress), so make it
+ * before any stream capture. Every call shares the array and it keeps the last call's contents
+ * (nothing needs clearing: each call writes what it reads), so calls that can overlap on the GPU
+ * (on two streams, or from two threads without ordering) race; order them on one stream. */
+#define FB_TQA_NOALLOC_SCRATCH_BYTES ((size_t)4 << 20)
+int launch_attention_paged_tq_noalloc(void* output, const void* q, const int* block_table,
+                                      const void** k_packed_ptrs, const void** k_norms_ptrs,
+                                      const void** v_packed_ptrs, const void** v_norms_ptrs,
+                                      const float* k_rotation, const float* v_rotation, const float* k_centroids,
+                                      const float* v_centroids, int num_tokens, int num_q_heads, int num_kv_heads,
+                                      int head_dim, int kv_len, int start_pos, int key_bits, int value_bits,
+                                      int k_packed_dim_per_head, int v_packed_dim_per_head, void* stream);
+
 /* ======================================================================== */
 /* 2. New kernel entry points                                               */
 /* ======================================================================== */
@@ -162,19 +186,6 @@ int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotat
                                 int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
                                 const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
                                 void* packed_pool, void* norms_pool, unsigned int* err_count, void* stream);
-
-/* fb_launch_tq_compress_paged that allocates no device memory (no reference counterpart; the
- * reference allocates per call). Results are identical to fb_launch_tq_compress_paged, which
- * itself now allocates nothing either: the exact-settle queue of the tensor-core path lives in
- * each CTA's shared memory, so there is no device scratch and no state shared between calls.
- * This entry point keeps its per-call limit of 524288 vectors (num_tokens * num_kv_heads):
- * larger calls return cudaErrorInvalidValue with the reason in fb_last_error(), before anything
- * is launched. */
-int fb_launch_tq_compress_paged_noalloc(const void* input, int dtype, const float* rotation,
-                                        const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
-                                        int head_dim, const int32_t* block_table, int64_t start_pos,
-                                        int64_t num_pool_rows, void* packed_pool, void* norms_pool,
-                                        unsigned int* err_count, void* stream);
 
 /* Which TurboQuant kernels served the compress / dequantize calls made so far in this process (no
  * reference counterpart; for tests and diagnostics): counts[0..2] = compress calls that took the
