@@ -730,9 +730,9 @@ def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
         pools = [(torch.empty((T, H * P), dtype=torch.uint8, device=dev),
                   torch.empty((T, H), dtype=torch.float16, device=dev)) for _ in range(2)]
 
-        def quant():
-            for j in range(2):
-                K.tq_compress_paged(kv[j], rot[j], cen, bits, pools[j][0], pools[j][1], block_table=table)
+        def quant():  # K and V of the step in one call (one launch)
+            K.tq_compress_kv_paged(kv[0], kv[1], rot[0], rot[1], cen, cen, bits, bits, pools[0][0], pools[0][1],
+                                   pools[1][0], pools[1][1], block_table=table)
 
         def dequant():
             for j in range(2):
@@ -956,16 +956,21 @@ def profile_kernel(args) -> None:
                                                  ROPE["orig"])).to(dev)
         fn = lambda: K.rope(q, k, pos, f)
     elif args.profile_kernel == "tq_compress":
-        # K of 65536 tokens x 8 KV heads x 128, FP16, 4-bit, random block table
+        # K and V of 65536 tokens x 8 KV heads x 128, FP16, 4-bit, random block
+        # table, one launch for both (as the bench's quantize step)
         Tk = 65536
-        x = torch.randn((Tk, NKV, HD), generator=g, device=dev)
-        x = torch.where(torch.rand((Tk, NKV, HD), generator=g, device=dev) < 0.005, x * 10, x).to(torch.float16)
-        rot = torch.from_numpy(K.tq_rotation_matrix(HD, 42)).to(dev)
+        xs = []
+        for _ in range(2):
+            x = torch.randn((Tk, NKV, HD), generator=g, device=dev)
+            xs.append(torch.where(torch.rand((Tk, NKV, HD), generator=g, device=dev) < 0.005, x * 10, x)
+                      .to(torch.float16))
+        rots = [torch.from_numpy(K.tq_rotation_matrix(HD, sd)).to(dev) for sd in (42, 542)]
         cen = torch.from_numpy(K.tq_codebook(HD, 4)[0]).to(dev)
         table = torch.randperm(Tk // 16, generator=g, device=dev).to(torch.int32)
-        packed = torch.empty((Tk, NKV * 64), dtype=torch.uint8, device=dev)
-        norms = torch.empty((Tk, NKV), dtype=torch.float16, device=dev)
-        fn = lambda: K.tq_compress_paged(x, rot, cen, 4, packed, norms, block_table=table)
+        pools = [(torch.empty((Tk, NKV * 64), dtype=torch.uint8, device=dev),
+                  torch.empty((Tk, NKV), dtype=torch.float16, device=dev)) for _ in range(2)]
+        fn = lambda: K.tq_compress_kv_paged(xs[0], xs[1], rots[0], rots[1], cen, cen, 4, 4, pools[0][0], pools[0][1],
+                                            pools[1][0], pools[1][1], block_table=table)
     elif args.profile_kernel == "tq_dequant":
         # BASELINE config 4 dequantize: the K pool of 65536 tokens x 8 KV heads x 128 back to FP16
         Tk = 65536
@@ -1008,6 +1013,8 @@ def main() -> None:
     ap.add_argument("--pipeline", action="store_true",
                     help="run config 5 (70B-shaped pipeline, NCCL stage handoff) at N=1 too (default: N > 1 only)")
     ap.add_argument("--no-pipeline", action="store_true", help="skip config 5")
+    ap.add_argument("--only", default=None, choices=["tq", "decode", "attention"],
+                    help="run only this workload on one GPU and print its figures")
     ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding", "tq_compress",
                                                                    "tq_dequant", "tq_attention", "attention_fp16"],
                     help="run only this kernel at its config-3 size (W warm-up launches + 1), for ncu captures")
@@ -1019,6 +1026,12 @@ def main() -> None:
 
     if args.profile_kernel:
         profile_kernel(args)
+        return
+    if args.only:  # one workload on one GPU, printed alone (development runs; not the driver's line)
+        fn = {"tq": lambda: run_tq_config4(args, 0, 1, local_rank), "decode": lambda: run_config2(args, local_rank),
+              "attention": lambda: {"tq": run_tq_attention(args, local_rank),
+                                    "fp16": run_attention_fp16(args, local_rank)}}[args.only]
+        print(json.dumps({"only": args.only, **fn()}), flush=True)
         return
     if args.impl == "reference":
         res = run_reference(args, rank)

@@ -934,14 +934,15 @@ int fb_tq_cache_append_kv(fb_tq_cache* c, uint64_t handle, size_t layer, const f
     if ((rc = tq_sync_table(c, s))) return rc;
     const int64_t start = (int64_t)(s.len - num_new);
     const int64_t rows = (int64_t)c->num_blocks * 16;
-    for (int kv = 0; kv < 2; ++kv) {
-        const int bits = kv == 0 ? c->kbits[layer] : c->vbits[layer];
-        int e = fb_launch_tq_compress_paged(kv == 0 ? pk : pv, keys->dtype, (const float*)c->rot[kv][layer],
-                                            (const float*)c->centroids[bits], bits, (int64_t)num_new, (int)c->heads,
-                                            (int)c->head_dim, (const int32_t*)s.dev_table.ptr, start, rows,
-                                            c->packed[kv][layer], c->norms[kv][layer], nullptr, b->stream);
-        if (e) return cuda_fail((cudaError_t)e);
-    }
+    // K and V in one call (one launch where both take the tensor-core kernel)
+    const int kb = c->kbits[layer], vb = c->vbits[layer];
+    int e = fb_launch_tq_compress_kv_paged(pk, pv, keys->dtype, (const float*)c->rot[0][layer],
+                                           (const float*)c->rot[1][layer], (const float*)c->centroids[kb],
+                                           (const float*)c->centroids[vb], kb, vb, (int64_t)num_new, (int)c->heads,
+                                           (int)c->head_dim, (const int32_t*)s.dev_table.ptr, start, rows,
+                                           c->packed[0][layer], c->norms[0][layer], c->packed[1][layer],
+                                           c->norms[1][layer], nullptr, b->stream);
+    if (e) return cuda_fail((cudaError_t)e);
     return FB_OK;
 }
 

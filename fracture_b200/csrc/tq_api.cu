@@ -11,14 +11,17 @@
 
 namespace fb {
 int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled);
+int tq_compress_umma_pair(const TqArgs& k, const TqArgs& v, cudaStream_t s, bool* handled);
 int tq_dequant_umma(const TqArgs& a, cudaStream_t s, bool* handled);
 }
 
 using namespace fb;
 
 // Calls served per path since the library was loaded: compress small / tensor-core / exact, then
-// dequantize small / tensor-core / exact (fb_tq_path_counts).
-static std::atomic<unsigned long long> g_tq_path_calls[6];
+// dequantize small / tensor-core / exact, then K+V compress pairs served by one tensor-core launch
+// (fb_tq_path_counts).
+constexpr int kTqPaths = 7;
+static std::atomic<unsigned long long> g_tq_path_calls[kTqPaths];
 
 static int count_path(int which, int rc) {
     if (rc == 0) g_tq_path_calls[which].fetch_add(1, std::memory_order_relaxed);
@@ -33,17 +36,19 @@ static int tq_check_common(int bits, int64_t num_tokens, int num_kv_heads, int h
     return 0;
 }
 
-static int tq_compress_any(const void* input, int dtype, const float* rotation, const float* centroids, int bits,
-                           int64_t num_tokens, int num_kv_heads, int head_dim, const int32_t* block_table,
-                           const int64_t* slot_map, int64_t start_pos, int64_t num_pool_rows, void* packed_pool,
-                           void* norms_pool, unsigned int* err_count, void* stream) {
+// Checks one compress call and fills its argument block (a.num_tokens == 0: nothing to do).
+static int tq_compress_args(const void* input, int dtype, const float* rotation, const float* centroids, int bits,
+                            int64_t num_tokens, int num_kv_heads, int head_dim, const int32_t* block_table,
+                            const int64_t* slot_map, int64_t start_pos, int64_t num_pool_rows, void* packed_pool,
+                            void* norms_pool, unsigned int* err_count, TqArgs* out) {
+    *out = TqArgs{};
     int rc = tq_check_common(bits, num_tokens, num_kv_heads, head_dim, num_pool_rows);
     if (rc) return rc;
     if (dtype != FB_FP16 && dtype != FB_BF16 && dtype != FB_FP32) return (int)cudaErrorInvalidValue;
     if (start_pos < 0) return (int)cudaErrorInvalidValue;
     if (num_tokens == 0) return 0;
     if (!input || !rotation || !centroids || !packed_pool || !norms_pool) return (int)cudaErrorInvalidValue;
-    TqArgs a{};
+    TqArgs& a = *out;
     a.input = input;
     a.in_dtype = dtype;
     a.rotation = rotation;
@@ -60,11 +65,29 @@ static int tq_compress_any(const void* input, int dtype, const float* rotation, 
     a.packed_pool = packed_pool;
     a.norms_pool = norms_pool;
     a.err_count = err_count;
+    return 0;
+}
+
+// Small calls take the few-vectors-per-CTA kernels, the rest the tensor-core kernel where it
+// applies, else the exact CUDA-core kernel.
+static int tq_compress_dispatch(const TqArgs& a, void* stream) {
     if (tq_small_compress_call(a)) return count_path(0, tq_compress_small(a, (cudaStream_t)stream));
     bool handled = false;
-    rc = tq_compress_umma(a, (cudaStream_t)stream, &handled);
+    const int rc = tq_compress_umma(a, (cudaStream_t)stream, &handled);
     if (handled) return count_path(1, rc);
     return count_path(2, tq_compress_exact(a, (cudaStream_t)stream));
+}
+
+static int tq_compress_any(const void* input, int dtype, const float* rotation, const float* centroids, int bits,
+                           int64_t num_tokens, int num_kv_heads, int head_dim, const int32_t* block_table,
+                           const int64_t* slot_map, int64_t start_pos, int64_t num_pool_rows, void* packed_pool,
+                           void* norms_pool, unsigned int* err_count, void* stream) {
+    TqArgs a;
+    const int rc = tq_compress_args(input, dtype, rotation, centroids, bits, num_tokens, num_kv_heads, head_dim,
+                                    block_table, slot_map, start_pos, num_pool_rows, packed_pool, norms_pool,
+                                    err_count, &a);
+    if (rc || a.num_tokens == 0) return rc;
+    return tq_compress_dispatch(a, stream);
 }
 
 extern "C" int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotation, const float* centroids,
@@ -73,6 +96,32 @@ extern "C" int fb_launch_tq_compress_paged(const void* input, int dtype, const f
                                            void* packed_pool, void* norms_pool, unsigned int* err_count, void* stream) {
     return tq_compress_any(input, dtype, rotation, centroids, bits, num_tokens, num_kv_heads, head_dim, block_table,
                            nullptr, start_pos, num_pool_rows, packed_pool, norms_pool, err_count, stream);
+}
+
+// K and V of one append: one tensor-core launch for both where they qualify, else two calls.
+extern "C" int fb_launch_tq_compress_kv_paged(const void* k_input, const void* v_input, int dtype,
+                                              const float* k_rotation, const float* v_rotation,
+                                              const float* k_centroids, const float* v_centroids, int key_bits,
+                                              int value_bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                                              const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
+                                              void* k_packed_pool, void* k_norms_pool, void* v_packed_pool,
+                                              void* v_norms_pool, unsigned int* err_count, void* stream) {
+    TqArgs k, v;
+    int rc = tq_compress_args(k_input, dtype, k_rotation, k_centroids, key_bits, num_tokens, num_kv_heads, head_dim,
+                              block_table, nullptr, start_pos, num_pool_rows, k_packed_pool, k_norms_pool, err_count,
+                              &k);
+    if (rc) return rc;
+    rc = tq_compress_args(v_input, dtype, v_rotation, v_centroids, value_bits, num_tokens, num_kv_heads, head_dim,
+                          block_table, nullptr, start_pos, num_pool_rows, v_packed_pool, v_norms_pool, err_count, &v);
+    if (rc || num_tokens == 0) return rc;
+    if (!tq_small_compress_call(k)) {
+        bool handled = false;
+        rc = tq_compress_umma_pair(k, v, (cudaStream_t)stream, &handled);
+        if (handled) return count_path(6, rc);
+    }
+    rc = tq_compress_dispatch(k, stream);
+    if (rc) return rc;
+    return tq_compress_dispatch(v, stream);
 }
 
 // Batched append: token t of the call goes to pool row slot_map[t] (negative or out of range:
@@ -159,6 +208,6 @@ extern "C" int launch_turboquant_decompress(const void* packed_in, const void* n
 
 extern "C" int fb_tq_path_counts(unsigned long long* counts, int n) {
     if (!counts || n < 0) return (int)cudaErrorInvalidValue;
-    for (int i = 0; i < n && i < 6; ++i) counts[i] = g_tq_path_calls[i].load(std::memory_order_relaxed);
+    for (int i = 0; i < n && i < kTqPaths; ++i) counts[i] = g_tq_path_calls[i].load(std::memory_order_relaxed);
     return 0;
 }

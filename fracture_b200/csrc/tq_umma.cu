@@ -2,7 +2,10 @@
 //
 // Replaces backends/fracture-cuda/kernels/turboquant_compress.cu:27-222 for
 // head_dim 128 and 2/3/4-bit codes. One persistent CTA per SM streams tiles of
-// 128 head vectors:
+// 128 head vectors. A launch serves one compress call, or two (the K and V of an
+// append): the grid is split between the calls in proportion to their tiles, and
+// each CTA works for one of them only, so a step pays one pipeline fill and one
+// tail for both.
 //
 //   warp 0      TMA producer: [128 vectors x 128] fp16/bf16 tile -> smem (SW128)
 //   warp 1      MMA issuer:   acc[v][i] = sum_j x[v][j] * Pi[i][j] on tcgen05,
@@ -29,6 +32,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -44,7 +48,9 @@ namespace umma {
 
 using namespace sm100;
 
-constexpr int STAGES = 3;           // A-tile pipeline depth
+constexpr int MAX_STAGES = 4;       // A-tile pipeline depth: 4 with FP16 input, 3 with BF16 (its
+                                    // third operand part takes the fourth stage's shared memory)
+__host__ __device__ constexpr int stages_for(int nparts) { return nparts == 2 ? 4 : 3; }
 constexpr int NB = 128;             // decision-table bins; bin b covers y in [(b - kBin0 -+ 1/2) w]
 constexpr int kBin0 = 64;           // the bin centred on y = 0
 constexpr float kInvW = 63.5f / 1.02f;  // 1 / bin width: bins span [-1.036, 1.02), and |y| <= 1
@@ -75,8 +81,8 @@ struct FixEntry {
 constexpr uint32_t kHasCoord = 1u << 8, kFixNorm = 1u << 9, kFixAll = 1u << 10, kSkip = 1u << 11;
 
 struct Misc {
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
+    uint64_t full[MAX_STAGES];
+    uint64_t empty[MAX_STAGES];
     uint64_t tfull[EPI_WGS];
     uint64_t tempty[EPI_WGS];
     uint32_t tmem_base;
@@ -92,16 +98,30 @@ struct Misc {
 // Byte offsets from the 1024-aligned base of dynamic shared memory.
 struct Smem {
     static constexpr int a_off(int nparts) { return nparts * TILE_BYTES; }
-    static constexpr int lut_off(int nparts) { return a_off(nparts) + STAGES * TILE_BYTES; }
+    static constexpr int lut_off(int nparts) { return a_off(nparts) + stages_for(nparts) * TILE_BYTES; }
     static constexpr int misc_off(int nparts) { return lut_off(nparts) + NB * LUT_COPIES * 8; }
     static constexpr int bytes(int nparts) { return misc_off(nparts) + (int)sizeof(Misc) + 1024; }
 };
+
+// try_wait that may suspend the thread until the phase completes (or ~100 us pass), so a waiting
+// warp does not spin through issue slots the epilogue warps of its scheduler need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
+        : "memory");
+    return ok != 0;
+}
 
 // Bounded wait for the phase with parity `parity`; false (and a counted timeout) if it never completes.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity)) {
         if (clock64() - t0 > kTimeoutCycles) {
             atomicAdd(&g_tq_umma_timeouts, 1u);
             if (err) atomicAdd(err, 1u);
@@ -255,9 +275,27 @@ __device__ __forceinline__ void settle_entry(const TqArgs& a, const FixEntry& en
     }
 }
 
+// One compress call of a launch, served by CTAs [cta0, cta0 + ncta) of the grid.
+struct TqJob {
+    TqArgs a;
+    int num_tiles;
+    int cta0, ncta;
+};
+
+// The kernel's parameters: one or two calls (njobs) with their input tensor maps.
+struct TqLaunch {
+    CUtensorMap map[2];
+    TqJob job[2];
+    int njobs;
+};
+
+// The work of one CTA for job `jb`: CTA `cta` of the job's `ncta` takes tiles cta, cta + ncta, ...
 template <typename TIn, int NPARTS, int BITS>
-__global__ void __maxnreg__(MAX_REGS)
-    tq_compress_umma_kernel(const __grid_constant__ CUtensorMap tmap, TqArgs a, int num_tiles) {
+__device__ __forceinline__ void compress_cta(const CUtensorMap* tmap_p, const TqJob& jb) {
+    constexpr int STAGES = stages_for(NPARTS);
+    const TqArgs& a = jb.a;
+    const int num_tiles = jb.num_tiles;
+    const int cta = (int)blockIdx.x - jb.cta0, ncta = jb.ncta;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sB = base;
@@ -268,7 +306,7 @@ __global__ void __maxnreg__(MAX_REGS)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nlev = 1 << BITS;
 
-    const int ntiles_cta = num_tiles > (int)blockIdx.x ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int ntiles_cta = num_tiles > cta ? (num_tiles - 1 - cta) / ncta + 1 : 0;
     const int prefetched = ntiles_cta < STAGES ? ntiles_cta : STAGES;
 
     // ── prologue ─────────────────────────────────────────────────────────────
@@ -293,10 +331,10 @@ __global__ void __maxnreg__(MAX_REGS)
         misc->sq_tail = 0u;
         // The first tiles are requested now, so their loads overlap the set-up below.
         for (int i = 0; i < prefetched; ++i) {
-            const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+            const int tile = cta + i * ncta;
             mbar_expect_tx(&misc->full[i], TILE_BYTES);
-            tma_load_2d(sA + i * TILE_BYTES, &tmap, &misc->full[i], 0, tile * TILE);
-            tma_load_2d(sA + i * TILE_BYTES + KBLK_BYTES, &tmap, &misc->full[i], 64, tile * TILE);
+            tma_load_2d(sA + i * TILE_BYTES, tmap_p, &misc->full[i], 0, tile * TILE);
+            tma_load_2d(sA + i * TILE_BYTES + KBLK_BYTES, tmap_p, &misc->full[i], 64, tile * TILE);
         }
     }
     for (int e = threadIdx.x; e < nlev; e += THREADS) misc->cen[e] = __ldg(a.centroids + e);
@@ -377,10 +415,10 @@ __global__ void __maxnreg__(MAX_REGS)
             for (int i = prefetched; i < ntiles_cta; ++i) {
                 const int s = i % STAGES;
                 if (!mbar_wait(&misc->empty[s], ((i / STAGES) + 1) & 1, err)) break;
-                const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+                const int tile = cta + i * ncta;
                 mbar_expect_tx(&misc->full[s], TILE_BYTES);
-                tma_load_2d(sA + s * TILE_BYTES, &tmap, &misc->full[s], 0, tile * TILE);
-                tma_load_2d(sA + s * TILE_BYTES + KBLK_BYTES, &tmap, &misc->full[s], 64, tile * TILE);
+                tma_load_2d(sA + s * TILE_BYTES, tmap_p, &misc->full[s], 0, tile * TILE);
+                tma_load_2d(sA + s * TILE_BYTES + KBLK_BYTES, tmap_p, &misc->full[s], 64, tile * TILE);
                 ++issued;
             }
             // Loads still in flight land before the CTA exits.
@@ -434,7 +472,7 @@ __global__ void __maxnreg__(MAX_REGS)
         constexpr int CW = 16;                    // accumulator columns per TMEM load (one chunk)
         constexpr int NCH = D / CW;               // chunks per row
         for (int i = eg; i < ntiles_cta; i += EPI_WGS) {
-            const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+            const int tile = cta + i * ncta;
             const int64_t vi = (int64_t)tile * TILE + row;
             // Pool row: the block-table lookup is issued before the accumulator wait.
             int64_t slot = -1;
@@ -452,7 +490,7 @@ __global__ void __maxnreg__(MAX_REGS)
             // partial sums for ILP; the exact norm is settled later when needed). The last
             // chunk stays in registers.
             uint32_t ra[CW], rb[CW];
-            float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            float2 s2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};  // paired f32 sums (FFMA2)
             tmem_ld16_issue(taddr, ra);
 #pragma unroll
             for (int h = 0; h < NCH; ++h) {
@@ -461,17 +499,18 @@ __global__ void __maxnreg__(MAX_REGS)
                 tmem_wait_tie(cur);
                 if (h + 1 < NCH) tmem_ld16_issue(taddr + (h + 1) * CW, nxt);
 #pragma unroll
-                for (int j = 0; j < CW; ++j) {
-                    const float v = __uint_as_float(cur[j]);
-                    s4[j & 3] = fmaf(v, v, s4[j & 3]);
+                for (int j = 0; j < CW / 2; ++j) {
+                    const float2 v2 = make_float2(__uint_as_float(cur[2 * j]), __uint_as_float(cur[2 * j + 1]));
+                    s2[j & 1] = __ffma2_rn(v2, v2, s2[j & 1]);
                 }
             }
-            const float ss = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+            const float ss = (s2[0].x + s2[0].y) + (s2[1].x + s2[1].y);
             const bool zero = ss == 0.0f;  // zero vector: y = 0 for every coordinate in both statements
             const bool finite = ss <= 3.402823466e38f;  // NaN or inf: the row takes the exact path
             const float norm_f = sqrtf(ss);
             const float kr = finite ? __frcp_rn(norm_f + 1e-8f) : 0.0f;  // y = acc * kr
             const float ku = kr * kInvW;
+            const float2 ku2 = make_float2(ku, ku), ub2 = make_float2(ubias, ubias);
             const bool norm_amb =
                 __float2half_rn(norm_f * (1.0f - kNormBand)) != __float2half_rn(norm_f * (1.0f + kNormBand));
             // Pass 2, codes, chunks NCH-1..0 (the last one is still in registers; the next
@@ -508,23 +547,32 @@ __global__ void __maxnreg__(MAX_REGS)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&misc->tempty[eg]);
                 }
-                // four running minima and a pairwise packing tree keep the dependency chains short
-                float dm[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+                // two running minima (three-input min over a pair of coordinates) and a pairwise
+                // packing tree keep the dependency chains short; the table bins of a pair of
+                // coordinates come from one paired FMA
+                float dm[2] = {1.0f, 1.0f};
                 constexpr int WPC = CW / G;  // packing words per chunk
 #pragma unroll
                 for (int w2 = 0; w2 < WPC; ++w2) {
                     uint32_t code[G];
 #pragma unroll
-                    for (int q = 0; q < G; ++q) {
-                        const float v = (SAFE && !finite) ? 0.0f : __uint_as_float(cur[w2 * G + q]);
-                        const float u = fmaf(v, ku, ubias);
-                        const uint32_t addr = __float_as_uint(u) * (LUT_COPIES * 8u) + lut_lane;
-                        float mid;
-                        uint32_t base;
-                        asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
-                        const float dd = fmaf(-v, kr, mid);
-                        dm[q & 3] = fminf(dm[q & 3], fabsf(dd));
-                        code[q] = base + (__float_as_uint(dd) >> 31);
+                    for (int q = 0; q < G; q += 2) {
+                        const float2 v2 = (SAFE && !finite)
+                                              ? make_float2(0.0f, 0.0f)
+                                              : make_float2(__uint_as_float(cur[w2 * G + q]),
+                                                            __uint_as_float(cur[w2 * G + q + 1]));
+                        const float2 u2 = __ffma2_rn(v2, ku2, ub2);
+                        const uint32_t addr0 = __float_as_uint(u2.x) * (LUT_COPIES * 8u) + lut_lane;
+                        const uint32_t addr1 = __float_as_uint(u2.y) * (LUT_COPIES * 8u) + lut_lane;
+                        float mid0, mid1;
+                        uint32_t base0, base1;
+                        asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid0), "=r"(base0) : "r"(addr0));
+                        asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid1), "=r"(base1) : "r"(addr1));
+                        const float dd0 = fmaf(-v2.x, kr, mid0), dd1 = fmaf(-v2.y, kr, mid1);
+                        float& m = dm[(q >> 1) & 1];
+                        asm("min.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(m), "f"(fabsf(dd0)), "f"(fabsf(dd1)));
+                        code[q] = base0 + (__float_as_uint(dd0) >> 31);
+                        code[q + 1] = base1 + (__float_as_uint(dd1) >> 31);
                     }
                     // big-endian: code 0 in the top bits
 #pragma unroll
@@ -533,7 +581,7 @@ __global__ void __maxnreg__(MAX_REGS)
                         for (int q = 0; q < G; q += 2 * span) code[q] = code[q] * (1u << (BITS * span)) + code[q + span];
                     w[hc * WPC + w2] = zero ? zero_word : code[0];
                 }
-                const float dmin = fminf(fminf(dm[0], dm[1]), fminf(dm[2], dm[3]));
+                const float dmin = fminf(dm[0], dm[1]);
                 if (dmin < kRiskBand && !zero) {
                     // rare: list this chunk's coordinates within the band
                     uint32_t m = 0;
@@ -625,6 +673,18 @@ __global__ void __maxnreg__(MAX_REGS)
     }
 }
 
+// B0 / B1: code widths of job 0 / job 1 (equal for a single call, or for K and V of one width).
+template <typename TIn, int NPARTS, int B0, int B1>
+__global__ void __maxnreg__(MAX_REGS)
+    tq_compress_umma_kernel(const __grid_constant__ TqLaunch L) {
+    const int j = (L.njobs > 1 && (int)blockIdx.x >= L.job[1].cta0) ? 1 : 0;
+    if constexpr (B0 == B1) {
+        compress_cta<TIn, NPARTS, B0>(&L.map[j], L.job[j]);
+    } else {
+        if (j == 0) compress_cta<TIn, NPARTS, B0>(&L.map[0], L.job[0]);
+        else compress_cta<TIn, NPARTS, B1>(&L.map[1], L.job[1]);
+    }
+}
 
 }  // namespace umma
 
@@ -651,49 +711,98 @@ static bool device_is_sm100() {
     return major == 10 && minor == 0;
 }
 
-template <typename TIn, int NPARTS, int BITS>
-static int launch_umma(const TqArgs& a, cudaStream_t s) {
+static bool encode_input_map(CUtensorMap* map, const TqArgs& a, bool bf16) {
     auto encode = get_encode();
-    if (!encode) return (int)cudaErrorNotSupported;
+    if (!encode) return false;
     const int64_t nvec = a.num_tokens * a.num_heads;
-    CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)umma::D, (cuuint64_t)nvec};
-    const cuuint64_t strides[1] = {(cuuint64_t)umma::D * sizeof(TIn)};
+    const cuuint64_t strides[1] = {(cuuint64_t)umma::D * 2};
     const cuuint32_t box[2] = {64, (cuuint32_t)umma::TILE};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode(&map, dtype_of<TIn>::value == FB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        2, const_cast<void*>(a.input), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return (int)cudaErrorInvalidValue;
+    return encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(a.input), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Launches jobs[0..njobs) (njobs 1 or 2) as one grid of at most one CTA per SM, split between
+// the jobs in proportion to their tiles (each job at least one CTA, at most one per tile).
+template <typename TIn, int NPARTS, int B0, int B1>
+static int launch_umma(const TqArgs* jobs, int njobs, cudaStream_t s) {
+    umma::TqLaunch L;
+    memset(&L, 0, sizeof L);
+    L.njobs = njobs;
+    int64_t tiles[2] = {0, 0};
+    for (int j = 0; j < njobs; ++j) {
+        if (!encode_input_map(&L.map[j], jobs[j], dtype_of<TIn>::value == FB_BF16)) return (int)cudaErrorInvalidValue;
+        L.job[j].a = jobs[j];
+        tiles[j] = (jobs[j].num_tokens * jobs[j].num_heads + umma::TILE - 1) / umma::TILE;
+        L.job[j].num_tiles = (int)tiles[j];
+    }
+    const int sms = num_sms();
+    int n0 = (int)std::min<int64_t>(tiles[0], sms), n1 = 0;
+    if (njobs == 2) {
+        if (tiles[0] + tiles[1] <= sms) {
+            n0 = (int)tiles[0];
+            n1 = (int)tiles[1];
+        } else {
+            n0 = (int)((tiles[0] * sms + (tiles[0] + tiles[1]) / 2) / (tiles[0] + tiles[1]));
+            n0 = std::max(1, std::min(n0, sms - 1));
+            n1 = sms - n0;
+            n0 = (int)std::min<int64_t>(n0, tiles[0]);
+            n1 = (int)std::min<int64_t>(n1, tiles[1]);
+        }
+    }
+    L.job[0].cta0 = 0;
+    L.job[0].ncta = n0;
+    L.job[1].cta0 = n0;
+    L.job[1].ncta = n1;
     constexpr int smem = umma::Smem::bytes(NPARTS);
-    auto kern = umma::tq_compress_umma_kernel<TIn, NPARTS, BITS>;
+    auto kern = umma::tq_compress_umma_kernel<TIn, NPARTS, B0, B1>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
-    const int num_tiles = (int)((nvec + umma::TILE - 1) / umma::TILE);
-    const int grid = std::max(1, std::min(num_tiles, num_sms()));
-    kern<<<grid, umma::THREADS, smem, s>>>(map, a, num_tiles);
+    kern<<<std::max(1, n0 + n1), umma::THREADS, smem, s>>>(L);
     return (int)cudaGetLastError();
+}
+
+static bool umma_eligible(const TqArgs& a) {
+    if (a.head_dim != umma::D || !(a.bits == 2 || a.bits == 3 || a.bits == 4)) return false;
+    if (a.in_dtype != FB_FP16 && a.in_dtype != FB_BF16) return false;
+    if (!aligned16(a.input) || !aligned16(a.packed_pool) || (((uintptr_t)a.norms_pool) & 1)) return false;
+    if (((uintptr_t)a.rotation & 15) != 0) return false;
+    if (a.num_tokens * a.num_heads > ((int64_t)1 << 31) - umma::TILE) return false;
+    static const bool sm100 = device_is_sm100();  // thread-safe one-time initialisation
+    return sm100;
+}
+
+template <typename TIn, int NPARTS>
+static int launch_same_bits(const TqArgs* jobs, int njobs, int bits, cudaStream_t s) {
+    if (bits == 4) return launch_umma<TIn, NPARTS, 4, 4>(jobs, njobs, s);
+    if (bits == 3) return launch_umma<TIn, NPARTS, 3, 3>(jobs, njobs, s);
+    return launch_umma<TIn, NPARTS, 2, 2>(jobs, njobs, s);
 }
 
 int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled) {
     *handled = false;
-    if (a.head_dim != umma::D || !(a.bits == 2 || a.bits == 3 || a.bits == 4)) return 0;
-    if (a.in_dtype != FB_FP16 && a.in_dtype != FB_BF16) return 0;
-    if (!aligned16(a.input) || !aligned16(a.packed_pool) || (((uintptr_t)a.norms_pool) & 1)) return 0;
-    if (((uintptr_t)a.rotation & 15) != 0) return 0;
-    if (a.num_tokens * a.num_heads > ((int64_t)1 << 31) - umma::TILE) return 0;
-    static const bool sm100 = device_is_sm100();  // thread-safe one-time initialisation
-    if (!sm100) return 0;
+    if (!umma_eligible(a)) return 0;
     *handled = true;
-    if (a.in_dtype == FB_FP16) {
-        if (a.bits == 4) return launch_umma<__half, 2, 4>(a, s);
-        if (a.bits == 3) return launch_umma<__half, 2, 3>(a, s);
-        return launch_umma<__half, 2, 2>(a, s);
-    }
-    if (a.bits == 4) return launch_umma<__nv_bfloat16, 3, 4>(a, s);
-    if (a.bits == 3) return launch_umma<__nv_bfloat16, 3, 3>(a, s);
-    return launch_umma<__nv_bfloat16, 3, 2>(a, s);
+    if (a.in_dtype == FB_FP16) return launch_same_bits<__half, 2>(&a, 1, a.bits, s);
+    return launch_same_bits<__nv_bfloat16, 3>(&a, 1, a.bits, s);
+}
+
+// K and V of one append in one launch, when both take the tensor-core path with the same input
+// type and their widths are equal or 4/2 (the reference's default key/value widths).
+int tq_compress_umma_pair(const TqArgs& k, const TqArgs& v, cudaStream_t s, bool* handled) {
+    *handled = false;
+    if (!umma_eligible(k) || !umma_eligible(v) || k.in_dtype != v.in_dtype) return 0;
+    if (k.bits != v.bits && !(k.bits == 4 && v.bits == 2)) return 0;
+    *handled = true;
+    const TqArgs jobs[2] = {k, v};
+    const bool pair42 = k.bits != v.bits;
+    if (k.in_dtype == FB_FP16)
+        return pair42 ? launch_umma<__half, 2, 4, 2>(jobs, 2, s) : launch_same_bits<__half, 2>(jobs, 2, k.bits, s);
+    return pair42 ? launch_umma<__nv_bfloat16, 3, 4, 2>(jobs, 2, s)
+                  : launch_same_bits<__nv_bfloat16, 3>(jobs, 2, k.bits, s);
 }
 
 

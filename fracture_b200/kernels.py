@@ -76,6 +76,20 @@ def tq_compress_paged(x, rotation, centroids, bits, packed_pool, norms_pool, blo
         norms_pool.data_ptr(), err.data_ptr() if err is not None else None, _stream(stream)), "tq_compress_paged")
 
 
+def tq_compress_kv_paged(k, v, k_rotation, v_rotation, k_centroids, v_centroids, key_bits, value_bits, k_pool,
+                         k_norms, v_pool, v_norms, block_table=None, start_pos=0, err=None, stream=None):
+    """K and V of one append (``[T, H, d]`` each) into their pools, one launch where both qualify."""
+    T, H, d = k.shape
+    assert v.shape == k.shape and v.dtype == k.dtype and v_norms.shape[0] == k_norms.shape[0]
+    rows = k_norms.shape[0]
+    _ok(_lib.load().fb_launch_tq_compress_kv_paged(
+        k.data_ptr(), v.data_ptr(), _dt(k), k_rotation.data_ptr(), v_rotation.data_ptr(), k_centroids.data_ptr(),
+        v_centroids.data_ptr(), key_bits, value_bits, T, H, d,
+        block_table.data_ptr() if block_table is not None else None, start_pos, rows, k_pool.data_ptr(),
+        k_norms.data_ptr(), v_pool.data_ptr(), v_norms.data_ptr(), err.data_ptr() if err is not None else None,
+        _stream(stream)), "tq_compress_kv_paged")
+
+
 def tq_dequant_paged(packed_pool, norms_pool, rotation, centroids, bits, out, block_table=None, start_pos=0,
                      stream=None):
     T, H, d = out.shape
@@ -106,13 +120,13 @@ def tq_dequant_slots(packed_pool, norms_pool, rotation, centroids, bits, out, sl
 
 
 TQ_PATHS = ("compress_small", "compress_tensor_core", "compress_exact", "dequant_small", "dequant_tensor_core",
-            "dequant_exact")
+            "dequant_exact", "compress_kv_fused")
 
 
 def tq_path_counts() -> dict:
     """Calls served so far by each TurboQuant kernel family (fb_tq_path_counts)."""
-    arr = (C.c_ulonglong * 6)()
-    _ok(_lib.load().fb_tq_path_counts(arr, 6), "fb_tq_path_counts")
+    arr = (C.c_ulonglong * len(TQ_PATHS))()
+    _ok(_lib.load().fb_tq_path_counts(arr, len(TQ_PATHS)), "fb_tq_path_counts")
     return dict(zip(TQ_PATHS, (int(v) for v in arr)))
 
 

@@ -187,10 +187,24 @@ int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotat
                                 const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
                                 void* packed_pool, void* norms_pool, unsigned int* err_count, void* stream);
 
+/* K and V of one append in one call (no reference counterpart; replaces the two compress calls of
+ * quantized_paged_kv_cache.rs:417-438): fb_launch_tq_compress_paged for the keys (k_*, key_bits)
+ * and for the values (v_*, value_bits), same tokens, block table and pool rows. Where both take
+ * the tensor-core kernel (head_dim 128, FP16 or BF16, 2/3/4-bit codes of equal width, or 4-bit
+ * keys with 2-bit values) they run as one launch whose grid is split between K and V; otherwise
+ * as two calls. Results equal the two separate calls bit for bit. */
+int fb_launch_tq_compress_kv_paged(const void* k_input, const void* v_input, int dtype, const float* k_rotation,
+                                   const float* v_rotation, const float* k_centroids, const float* v_centroids,
+                                   int key_bits, int value_bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                                   const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
+                                   void* k_packed_pool, void* k_norms_pool, void* v_packed_pool, void* v_norms_pool,
+                                   unsigned int* err_count, void* stream);
+
 /* Which TurboQuant kernels served the compress / dequantize calls made so far in this process (no
  * reference counterpart; for tests and diagnostics): counts[0..2] = compress calls that took the
  * small-call kernel (tq_small.cu), the tensor-core kernel (tq_umma.cu) and the exact CUDA-core
- * kernel (tq_exact.cu); counts[3..5] the same for dequantize. Writes min(n, 6) counters. */
+ * kernel (tq_exact.cu); counts[3..5] the same for dequantize; counts[6] = K+V pairs of
+ * fb_launch_tq_compress_kv_paged served by one tensor-core launch. Writes min(n, 7) counters. */
 int fb_tq_path_counts(unsigned long long* counts, int n);
 
 /* Batched append (no reference counterpart; the reference appends one sequence at a time,

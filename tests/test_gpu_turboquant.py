@@ -426,6 +426,43 @@ def test_tensor_core_path_non_finite_rows(dt, T):
     assert np.array_equal(np.isnan(got), np.isnan(exp))
 
 
+@pytest.mark.parametrize("dt,kb,vb,T", [("f16", 4, 4, 4099), ("bf16", 4, 4, 1500), ("f16", 3, 3, 2053),
+                                         ("f16", 2, 2, 300), ("f16", 4, 2, 3001), ("bf16", 4, 2, 1200),
+                                         ("f16", 2, 4, 700), ("f16", 4, 4, 130), ("bf16", 3, 3, 20000)])
+def test_compress_kv_one_launch_equals_the_statement(dt, kb, vb, T):
+    """fb_launch_tq_compress_kv_paged: K and V of one append (shuffled block table, unaligned start)
+    in one tensor-core launch whose grid is split between them (or two calls where the widths have
+    no fused kernel, 2/4, or the call is small). Every packed byte and norm equals the exact
+    statement; the path counter shows which way it went. 20000 x 8 vectors (1250 tiles per job)
+    splits the SMs in proportion; 130 x 8 (9 tiles) gives each job fewer CTAs than SMs."""
+    H, d, start = 8, 128, 5
+    xk, rk = make_input(T, H, d, dt, seed=900 + T)
+    xv, rv = make_input(T, H, d, dt, seed=901 + T)
+    pik, ck = tables(d, kb, 42)
+    piv, cv = tables(d, vb, 542)
+    nblk = (start + T + 15) // 16
+    table = np.random.default_rng(T).permutation(nblk + 2)[:nblk].astype(np.int32)
+    rows = (nblk + 2) * 16
+    pools = [(torch.full((rows, H * d * b // 8), 0x5A, dtype=torch.uint8, device=DEV),
+              torch.zeros((rows, H), dtype=torch.float16, device=DEV)) for b in (kb, vb)]
+    before = K.tq_path_counts()
+    K.tq_compress_kv_paged(dev(xk, dt), dev(xv, dt), torch.from_numpy(pik).to(DEV), torch.from_numpy(piv).to(DEV),
+                           torch.from_numpy(ck).to(DEV), torch.from_numpy(cv).to(DEV), kb, vb, pools[0][0],
+                           pools[0][1], pools[1][0], pools[1][1], block_table=torch.from_numpy(table).to(DEV),
+                           start_pos=start)
+    torch.cuda.synchronize()
+    after = K.tq_path_counts()
+    fused = T * H > SMALL_CALL_VECTORS and (kb == vb or (kb, vb) == (4, 2))
+    assert after["compress_kv_fused"] - before["compress_kv_fused"] == (1 if fused else 0), (before, after)
+    pos = start + np.arange(T)
+    prow = table[pos // 16] * 16 + pos % 16
+    for (packed, norms), raw, pi, c, b in ((pools[0], rk, pik, ck, kb), (pools[1], rv, piv, cv, vb)):
+        pc, nc, _ = tq.compress_c(raw, KIND[dt], pi, c, b, num_threads=8)
+        got_p, got_n = packed.cpu().numpy()[prow], norms.cpu().numpy().view(np.uint16)[prow]
+        bad = np.nonzero(np.any(got_p != pc, axis=1) | np.any(got_n != nc, axis=1))[0]
+        assert bad.size == 0, f"{b}-bit: {bad.size} token rows differ, first {bad[:5]}"
+
+
 # ── tensor-core dequantize (head_dim 128, 2/3/4 bits, FP16/BF16 output) ──
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
