@@ -141,6 +141,22 @@ __device__ __forceinline__ void tmem_wait_tie(uint32_t (&r)[16]) {
                  : "memory");
 }
 
+// Waits until every TMEM load this thread issued is done; ties only r (the oldest of the loads in
+// flight when several are: tcgen05.wait::ld waits for all of them, so the others are complete too,
+// but their registers stay untied until their own wait).
+__device__ __forceinline__ void tmem_wait_one(uint32_t (&r)[16]) { tmem_wait_tie(r); }
+
+// 16-column TMEM store of this thread's accumulator row from r; complete after tmem_wait_st().
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Byte offset in the SW128 K-major image of element (row n, column k) of a
 // 128 x 128 tile stored as two 64-column K-blocks.
 __device__ __forceinline__ int sw128_offset(int n, int k) {

@@ -54,13 +54,12 @@ __host__ __device__ constexpr int stages_for(int nparts) { return nparts == 2 ? 
 constexpr int NB = 128;             // decision-table bins; bin b covers y in [(b - kBin0 -+ 1/2) w]
 constexpr int kBin0 = 64;           // the bin centred on y = 0
 constexpr float kInvW = 63.5f / 1.02f;  // 1 / bin width: bins span [-1.036, 1.02), and |y| <= 1
-constexpr int LUT_COPIES = 16;      // copies per bin; lanes l and l + 16 share one
+constexpr int LUT_COPIES = 32;      // copies per bin, one per lane: a warp's lookups hit 32 banks
 constexpr float kRiskBand = 1e-6f;   // |y - boundary| below this: settle with the exact sequence
 constexpr float kNormBand = 1e-6f;  // relative band around fp16 rounding ties of the norm
 constexpr float kWindowPad = 1e-4f; // a bin owns the boundaries within this distance of its edges
 constexpr int EPI_WGS = 4;                 // epilogue warpgroups, one TMEM accumulator each
 constexpr int THREADS = 64 + EPI_WGS * 128;  // warp 0 TMA, warp 1 MMA, then the epilogue
-constexpr int VCH = 32;                    // accumulator values per thread per TMEM load round
 constexpr int MAX_REGS = 96;               // 18 warps: up to 5 per scheduler, 16K registers each
 constexpr int SQ = 512;                    // settle queue entries per CTA (shared memory)
 static_assert(THREADS > NB, "one thread per table bin plus one for the checks");
@@ -87,7 +86,6 @@ struct Misc {
     uint64_t tempty[EPI_WGS];
     uint32_t tmem_base;
     int use_exact;  // table could not be built: every row takes the exact path
-    uint32_t zero_word; // packing word of a zero vector (every code = nearest centroid of 0)
     float cen[256];
     float bin_mid[NB];      // per-bin table entry before it is copied LUT_COPIES times
     uint32_t bin_base[NB];
@@ -99,7 +97,7 @@ struct Misc {
 struct Smem {
     static constexpr int a_off(int nparts) { return nparts * TILE_BYTES; }
     static constexpr int lut_off(int nparts) { return a_off(nparts) + stages_for(nparts) * TILE_BYTES; }
-    static constexpr int misc_off(int nparts) { return lut_off(nparts) + NB * LUT_COPIES * 8; }
+    static constexpr int misc_off(int nparts) { return lut_off(nparts) + NB * LUT_COPIES * 4; }
     static constexpr int bytes(int nparts) { return misc_off(nparts) + (int)sizeof(Misc) + 1024; }
 };
 
@@ -131,13 +129,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     return true;
 }
 
-// One table entry per (bin, copy). The 16 copies of a bin sit side by side, so the
-// 16 lanes of each half-warp read 16 different bank pairs with one 64-bit load.
-struct LutEntry {
-    float mid;      // the bin's decision boundary in y units (8.0: the bin holds none)
-    uint32_t base;  // code below the boundary (the code of the whole bin when it holds none)
-};
-
+// One 32-bit table entry per (bin, copy), the 32 copies of a bin side by side so that lane l
+// reads copy l: one shared-memory wavefront per warp lookup. An entry is the bin's decision
+// boundary m in y units (8.0: the bin holds none) with its low four mantissa bits replaced by
+// the code below the boundary. That moves m by at most 15 units in the last place (under 2.3e-7
+// for the |m| < 0.25 of 2- to 4-bit codebooks), far inside the settle band kRiskBand: a
+// coordinate whose fast decision against the stored value could differ from the exact one is
+// within the band of it and is settled exactly.
+constexpr uint32_t kLutCodeMask = 15u;
 
 // Correctly rounded x / den for fp16 x with |x| <= den, den in [1e-8, 2^20]: from the
 // correctly rounded reciprocal r, two FMA corrections of the quotient (P. Markstein,
@@ -275,11 +274,35 @@ __device__ __forceinline__ void settle_entry(const TqArgs& a, const FixEntry& en
     }
 }
 
+// One packing word of codes (16 for 2 bits, else 8) in stream order. 4-bit: 8 codes, byte k =
+// (c[2k] << 4) | c[2k+1] with bytes little-endian, so the word is stored as is; 2-bit: 16 codes,
+// byte k = c[4k] .. c[4k+3] MSB first; 3-bit: 8 codes as a 24-bit value, first code on top.
+template <int BITS>
+__device__ __forceinline__ uint32_t pack_codes(const uint32_t (&c)[BITS == 2 ? 16 : 8]) {
+    if constexpr (BITS == 4) {
+        uint32_t b[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) b[k] = c[2 * k] * 16u + c[2 * k + 1];
+        return ((b[3] * 256u + b[2]) * 256u + b[1]) * 256u + b[0];
+    } else if constexpr (BITS == 2) {
+        uint32_t b[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) b[k] = ((c[4 * k] * 4u + c[4 * k + 1]) * 4u + c[4 * k + 2]) * 4u + c[4 * k + 3];
+        return ((b[3] * 256u + b[2]) * 256u + b[1]) * 256u + b[0];
+    } else {
+        uint32_t v = c[0];
+#pragma unroll
+        for (int q = 1; q < 8; ++q) v = v * 8u + c[q];
+        return v;
+    }
+}
+
 // One compress call of a launch, served by CTAs [cta0, cta0 + ncta) of the grid.
 struct TqJob {
     TqArgs a;
     int num_tiles;
     int cta0, ncta;
+    DivU32 hdiv;  // division by num_heads
 };
 
 // The kernel's parameters: one or two calls (njobs) with their input tensor maps.
@@ -300,7 +323,7 @@ __device__ __forceinline__ void compress_cta(const CUtensorMap* tmap_p, const Tq
     uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sB = base;
     uint8_t* sA = base + Smem::a_off(NPARTS);
-    LutEntry* lut = (LutEntry*)(base + Smem::lut_off(NPARTS));
+    uint32_t* lut = (uint32_t*)(base + Smem::lut_off(NPARTS));
     Misc* misc = (Misc*)(base + Smem::misc_off(NPARTS));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -378,8 +401,6 @@ __device__ __forceinline__ void compress_cta(const CUtensorMap* tmap_p, const Tq
                 }
             }
             if (!ok) misc->use_exact = 1;
-            const uint32_t cz = (uint32_t)nearest_centroid(0.0f, misc->cen, nlev);
-            misc->zero_word = BITS == 4 ? cz * 0x11111111u : BITS == 2 ? cz * 0x55555555u : cz * 0x249249u;
         }
         if (threadIdx.x < NB) {
             const int bin = threadIdx.x;
@@ -394,18 +415,13 @@ __device__ __forceinline__ void compress_cta(const CUtensorMap* tmap_p, const Tq
             misc->bin_base[bin] = owner >= 0 ? (uint32_t)owner : (uint32_t)below;
         }
         __syncthreads();
-        for (int e = threadIdx.x; e < NB * LUT_COPIES; e += THREADS) {
-            LutEntry en;
-            en.mid = misc->bin_mid[e / LUT_COPIES];
-            en.base = misc->bin_base[e / LUT_COPIES];
-            lut[e] = en;
-        }
+        for (int e = threadIdx.x; e < NB * LUT_COPIES; e += THREADS)
+            lut[e] = (__float_as_uint(misc->bin_mid[e / LUT_COPIES]) & ~kLutCodeMask) | misc->bin_base[e / LUT_COPIES];
     }
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = misc->tmem_base;
     const int use_exact = misc->use_exact;
-    const uint32_t zero_word = misc->zero_word;
     unsigned int* err = a.err_count;
 
     if (warp == 0) {
@@ -464,149 +480,183 @@ __device__ __forceinline__ void compress_cta(const CUtensorMap* tmap_p, const Tq
         const int P = (D * BITS) >> 3;
         const float magic = 12582912.0f;  // 1.5 * 2^23: fma(y, 1/w, magic + kBin0) holds the bin in its low bits
         const float ubias = magic + (float)kBin0;
-        const uint32_t lut_lane =
-            smem_u32(lut) + (lane & (LUT_COPIES - 1)) * 8 - (uint32_t)__float_as_uint(magic) * (LUT_COPIES * 8u);
+        const uint32_t lut_lane = smem_u32(lut) + lane * 4u - (uint32_t)__float_as_uint(magic) * (LUT_COPIES * 4u);
         const int64_t nvec = a.num_tokens * a.num_heads;
         constexpr int G = (BITS == 2) ? 16 : 8;  // codes per packing word
-        constexpr int WPR = VCH / G;              // packing words per round
-        constexpr int CW = 16;                    // accumulator columns per TMEM load (one chunk)
+        constexpr int CW = 16;                    // accumulator columns per TMEM load in the coding pass
         constexpr int NCH = D / CW;               // chunks per row
+        constexpr int WPC = CW / G;               // packing words per chunk
+        // Pool rows in two steps so that no wait falls on a load: raw_of(i) issues the slot-map or
+        // block-table read for this thread's vector of tile i (kNoVec: no vector), a tile ahead of its
+        // use; prow_of applies the slot rule of tq_slot to it (-1: no row; err_count bumped for a
+        // slot out of range). Token and head by multiply-high division (the host keeps the vector
+        // count below 2^31).
+        constexpr int64_t kNoVec = INT64_MIN;  // a slot-map entry may itself be negative
+        auto raw_of = [&](int i) -> int64_t {
+            const int64_t v = (int64_t)(cta + i * ncta) * TILE + row;
+            if (i >= ntiles_cta || v >= nvec) return kNoVec;
+            const uint32_t t = divu32((uint32_t)v, jb.hdiv);
+            if (a.slot_map) return __ldg(a.slot_map + t);
+            if (a.block_table) return (int64_t)(uint32_t)__ldg(a.block_table + ((a.start_pos + t) >> 4));
+            return 0;
+        };
+        auto prow_of = [&](int i, int64_t raw) -> int64_t {
+            if (raw == kNoVec) return -1;
+            const uint32_t v = (uint32_t)((cta + i * ncta) * TILE + row);
+            const uint32_t t = divu32(v, jb.hdiv), head = v - t * (uint32_t)a.num_heads;
+            const int64_t pos = a.start_pos + t;
+            int64_t slot = pos;
+            if (a.slot_map) {
+                slot = raw;
+            } else if (a.block_table) {
+                const int32_t b = (int32_t)(uint32_t)raw;
+                slot = b < 0 ? -1 : (int64_t)b * 16 + (pos & 15);
+            }
+            if (slot < 0 || slot >= a.pool_rows) {
+                if (a.err_count) atomicAdd(a.err_count, 1u);
+                return -1;
+            }
+            return slot * a.num_heads + head;
+        };
+        int64_t raw_next = raw_of(eg);
         for (int i = eg; i < ntiles_cta; i += EPI_WGS) {
             const int tile = cta + i * ncta;
             const int64_t vi = (int64_t)tile * TILE + row;
-            // Pool row: the block-table lookup is issued before the accumulator wait.
-            int64_t slot = -1;
-            // 32-bit division: the host keeps the vector count below 2^31
-            const uint32_t tok = (uint32_t)vi / (uint32_t)a.num_heads;
-            const uint32_t head = (uint32_t)vi - tok * (uint32_t)a.num_heads;
-            if (vi < nvec) slot = tq_slot(a, (int64_t)tok);
-            const int64_t prow = slot >= 0 ? slot * a.num_heads + head : -1;
-            uint8_t* dst = prow >= 0 ? (uint8_t*)a.packed_pool + prow * P : nullptr;
+            const int64_t raw = raw_next;
+            raw_next = raw_of(i + EPI_WGS);
             if (!mbar_wait(&misc->tfull[eg], (i / EPI_WGS) & 1, err)) break;
             tc_fence_after();
             const uint32_t taddr = tmem_base + (uint32_t)(eg * D) + ((uint32_t)(quarter * 32) << 16);
-            // Pass 1: |Pi x|^2 = |x|^2 from the accumulator row, in 16-column chunks 0..NCH-1
-            // with the next chunk's load in flight while the current one is summed (four
-            // partial sums for ILP; the exact norm is settled later when needed). The last
-            // chunk stays in registers.
-            uint32_t ra[CW], rb[CW];
-            float2 s2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};  // paired f32 sums (FFMA2)
-            tmem_ld16_issue(taddr, ra);
+            // Pass 1: |Pi x|^2 = |x|^2 from the accumulator row, 16-column chunks with the next three
+            // loads in flight while one is summed (paired FMAs; the exact norm is settled where
+            // needed).
+            float2 s2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+            {
+                constexpr int NB1 = 4;  // load buffers
+                uint32_t xb[NB1][CW];
 #pragma unroll
-            for (int h = 0; h < NCH; ++h) {
-                uint32_t(&cur)[CW] = (h & 1) ? rb : ra;
-                uint32_t(&nxt)[CW] = (h & 1) ? ra : rb;
-                tmem_wait_tie(cur);
-                if (h + 1 < NCH) tmem_ld16_issue(taddr + (h + 1) * CW, nxt);
+                for (int h = 0; h < NB1 - 1; ++h) tmem_ld16_issue(taddr + h * CW, xb[h]);
 #pragma unroll
-                for (int j = 0; j < CW / 2; ++j) {
-                    const float2 v2 = make_float2(__uint_as_float(cur[2 * j]), __uint_as_float(cur[2 * j + 1]));
-                    s2[j & 1] = __ffma2_rn(v2, v2, s2[j & 1]);
+                for (int h = 0; h < NCH; ++h) {
+                    tmem_wait_one(xb[h % NB1]);
+                    if (h + NB1 - 1 < NCH) tmem_ld16_issue(taddr + (h + NB1 - 1) * CW, xb[(h + NB1 - 1) % NB1]);
+#pragma unroll
+                    for (int j = 0; j < CW / 2; ++j) {
+                        const float2 v2 = make_float2(__uint_as_float(xb[h % NB1][2 * j]), __uint_as_float(xb[h % NB1][2 * j + 1]));
+                        s2[j & 1] = __ffma2_rn(v2, v2, s2[j & 1]);
+                    }
                 }
             }
             const float ss = (s2[0].x + s2[0].y) + (s2[1].x + s2[1].y);
-            const bool zero = ss == 0.0f;  // zero vector: y = 0 for every coordinate in both statements
+            // zero vector: y = 0 exactly for every coordinate in both statements, so the table
+            // codes it exactly (the lower code at a boundary that is exactly 0, the statement's first
+            // minimum); no coordinate of it needs settling
+            const bool zero = ss == 0.0f;
             const bool finite = ss <= 3.402823466e38f;  // NaN or inf: the row takes the exact path
+            if (__any_sync(0xffffffffu, !finite)) {
+                // rare: a row of this warp holds NaN/inf (its accumulator values are not finite).
+                // Its accumulator row is overwritten with zeros so that every table index of the
+                // coding pass stays in range; the row is settled whole by the exact path below.
+                uint32_t z[CW];
+#pragma unroll 1
+                for (int c = 0; c < NCH; ++c) {
+                    tmem_ld16_issue(taddr + c * CW, z);
+                    tmem_wait_tie(z);
+#pragma unroll
+                    for (int j = 0; j < CW; ++j) z[j] = finite ? z[j] : 0u;
+                    tmem_st16(taddr + c * CW, z);
+                }
+                tmem_wait_st();
+            }
+            const int64_t prow = prow_of(i, raw);
+            uint8_t* dst = prow >= 0 ? (uint8_t*)a.packed_pool + prow * P : nullptr;
             const float norm_f = sqrtf(ss);
             const float kr = finite ? __frcp_rn(norm_f + 1e-8f) : 0.0f;  // y = acc * kr
             const float ku = kr * kInvW;
             const float2 ku2 = make_float2(ku, ku), ub2 = make_float2(ubias, ubias);
             const bool norm_amb =
                 __float2half_rn(norm_f * (1.0f - kNormBand)) != __float2half_rn(norm_f * (1.0f + kNormBand));
-            // Pass 2, codes, chunks NCH-1..0 (the last one is still in registers; the next
-            // load is in flight while a chunk is coded); a round of VCH coordinates (two
-            // chunks) is stored as soon as both are coded. Per coordinate: its table bin from
-            // the rounded fma(acc, ku, ubias), the bin's boundary m and lower code; dd = m - y;
-            // code = base + (y > m) from the sign of dd, packed big-endian by integer
-            // multiply-add (first code in the top bits). The accumulator goes back to the MMA
-            // warp once the last chunk is in registers.
+            // Pass 2, codes: chunks 0..NCH-1, the next load in flight while one is coded; two
+            // chunks (one 32-coordinate round) are coded and stored per loop iteration. Per coordinate: its table bin
+            // from the rounded fma(acc, ku, ubias) (two coordinates per paired FMA), the bin's
+            // entry (boundary m, lower code in its low bits), dd = m - y, code = lower + (y > m)
+            // from the sign of dd, packed big-endian (first code in the top bits) by integer
+            // multiply-add; the running minimum of |dd| flags the rare chunk to list for the exact
+            // settle. The accumulator goes back to the MMA warp once the last chunk is loaded.
             uint32_t mask[4] = {0u, 0u, 0u, 0u};
-            uint32_t w[WPR];
-            // SAFE: a row of this warp is not finite (NaN/inf in the input); its accumulator
-            // values are replaced by 0 so every table index stays in range (the row is
-            // settled whole by the exact path).
-            auto pass2 = [&](auto safe_tag) {
-            constexpr bool SAFE = decltype(safe_tag)::value;
-            // rounds g = NCH/2-1 .. 0 of two chunks each, kept rolled so the hot loop stays small
-            // in the instruction cache; within a round everything is unrolled
-#pragma unroll 1
-            for (int g = NCH / 2 - 1; g >= 0; --g)
-#pragma unroll
-            for (int hc = 1; hc >= 0; --hc) {
-                const int c = 2 * g + hc;
-                // chunk NCH-1 is in the buffer pass 1 used last; the chunks below alternate
-                constexpr bool last_in_b = ((NCH - 1) & 1) != 0;
-                const bool in_b = hc == 1 ? last_in_b : !last_in_b;
-                uint32_t(&cur)[CW] = in_b ? rb : ra;
-                uint32_t(&nxt)[CW] = in_b ? ra : rb;
-                if (c < NCH - 1) tmem_wait_tie(cur);
-                if (c > 0) {
-                    tmem_ld16_issue(taddr + (c - 1) * CW, nxt);
-                } else {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&misc->tempty[eg]);
-                }
-                // two running minima (three-input min over a pair of coordinates) and a pairwise
-                // packing tree keep the dependency chains short; the table bins of a pair of
-                // coordinates come from one paired FMA
+            uint32_t w[2 * WPC];
+            uint32_t ra[CW], rb[CW];
+            // one chunk: code its 16 coordinates into w[half * WPC ..], return whether a lane's
+            // coordinate lies within the settle band (and list those coordinates in mk)
+            auto code_chunk = [&](const uint32_t (&cur)[CW], int half, uint32_t& mk) {
                 float dm[2] = {1.0f, 1.0f};
-                constexpr int WPC = CW / G;  // packing words per chunk
 #pragma unroll
                 for (int w2 = 0; w2 < WPC; ++w2) {
                     uint32_t code[G];
 #pragma unroll
                     for (int q = 0; q < G; q += 2) {
-                        const float2 v2 = (SAFE && !finite)
-                                              ? make_float2(0.0f, 0.0f)
-                                              : make_float2(__uint_as_float(cur[w2 * G + q]),
-                                                            __uint_as_float(cur[w2 * G + q + 1]));
+                        const float2 v2 = make_float2(__uint_as_float(cur[w2 * G + q]), __uint_as_float(cur[w2 * G + q + 1]));
                         const float2 u2 = __ffma2_rn(v2, ku2, ub2);
-                        const uint32_t addr0 = __float_as_uint(u2.x) * (LUT_COPIES * 8u) + lut_lane;
-                        const uint32_t addr1 = __float_as_uint(u2.y) * (LUT_COPIES * 8u) + lut_lane;
-                        float mid0, mid1;
-                        uint32_t base0, base1;
-                        asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid0), "=r"(base0) : "r"(addr0));
-                        asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid1), "=r"(base1) : "r"(addr1));
-                        const float dd0 = fmaf(-v2.x, kr, mid0), dd1 = fmaf(-v2.y, kr, mid1);
+                        const uint32_t addr0 = __float_as_uint(u2.x) * (LUT_COPIES * 4u) + lut_lane;
+                        const uint32_t addr1 = __float_as_uint(u2.y) * (LUT_COPIES * 4u) + lut_lane;
+                        uint32_t e0, e1;
+                        asm("ld.shared.b32 %0, [%1];" : "=r"(e0) : "r"(addr0));
+                        asm("ld.shared.b32 %0, [%1];" : "=r"(e1) : "r"(addr1));
+                        const float dd0 = fmaf(-v2.x, kr, __uint_as_float(e0));
+                        const float dd1 = fmaf(-v2.y, kr, __uint_as_float(e1));
                         float& m = dm[(q >> 1) & 1];
                         asm("min.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(m), "f"(fabsf(dd0)), "f"(fabsf(dd1)));
-                        code[q] = base0 + (__float_as_uint(dd0) >> 31);
-                        code[q + 1] = base1 + (__float_as_uint(dd1) >> 31);
+                        code[q] = (e0 & kLutCodeMask) + (__float_as_uint(dd0) >> 31);
+                        code[q + 1] = (e1 & kLutCodeMask) + (__float_as_uint(dd1) >> 31);
                     }
-                    // big-endian: code 0 in the top bits
-#pragma unroll
-                    for (int span = 1; span < G; span *= 2)
-#pragma unroll
-                        for (int q = 0; q < G; q += 2 * span) code[q] = code[q] * (1u << (BITS * span)) + code[q + span];
-                    w[hc * WPC + w2] = zero ? zero_word : code[0];
+                    // the word as stored: byte k holds codes of stream order MSB first, bytes
+                    // little-endian (4-bit: byte k = c[2k] c[2k+1]; 2-bit: c[4k] .. c[4k+3];
+                    // 3-bit: a 24-bit big-endian group, laid out by the caller)
+                    w[half * WPC + w2] = pack_codes<BITS>(code);
                 }
-                const float dmin = fminf(dm[0], dm[1]);
-                if (dmin < kRiskBand && !zero) {
+                mk = 0;
+                if (fminf(dm[0], dm[1]) < kRiskBand && !zero) {
                     // rare: list this chunk's coordinates within the band
-                    uint32_t m = 0;
 #pragma unroll
                     for (int j = 0; j < CW; ++j) {
-                        const float v = (SAFE && !finite) ? 0.0f : __uint_as_float(cur[j]);
+                        const float v = __uint_as_float(cur[j]);
                         const float u = fmaf(v, ku, ubias);
-                        const uint32_t addr = __float_as_uint(u) * (LUT_COPIES * 8u) + lut_lane;
-                        float mid;
-                        uint32_t base;
-                        asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(mid), "=r"(base) : "r"(addr));
-                        if (fabsf(fmaf(-v, kr, mid)) < kRiskBand) m |= 1u << j;
+                        uint32_t e;
+                        asm("ld.shared.b32 %0, [%1];" : "=r"(e) : "r"(__float_as_uint(u) * (LUT_COPIES * 4u) + lut_lane));
+                        if (fabsf(fmaf(-v, kr, __uint_as_float(e))) < kRiskBand) mk |= 1u << j;
                     }
-                    const uint32_t mm = m << (hc * CW);
-                    if (g == 0) mask[0] |= mm;
-                    else if (g == 1) mask[1] |= mm;
-                    else if (g == 2) mask[2] |= mm;
-                    else mask[3] |= mm;
                 }
-                if (hc == 0 && dst) {  // both chunks of round g are coded
+            };
+            // rounds g = 0 .. NCH/2-1 of two chunks, rolled so the hot loop stays small in the
+            // instruction cache; chunk 2g is in ra, 2g + 1 in rb
+            tmem_ld16_issue(taddr, ra);
+#pragma unroll 1
+            for (int g = 0; g < NCH / 2; ++g) {
+                uint32_t mk0, mk1;
+                tmem_wait_tie(ra);
+                tmem_ld16_issue(taddr + (2 * g + 1) * CW, rb);
+                code_chunk(ra, 0, mk0);
+                tmem_wait_tie(rb);
+                if (g + 1 < NCH / 2) {
+                    tmem_ld16_issue(taddr + (2 * g + 2) * CW, ra);
+                } else {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&misc->tempty[eg]);
+                }
+                code_chunk(rb, 1, mk1);
+                const uint32_t mm = mk0 | (mk1 << CW);
+                if (mm) {
+                    if (g == 0) mask[0] = mm;
+                    else if (g == 1) mask[1] = mm;
+                    else if (g == 2) mask[2] = mm;
+                    else mask[3] = mm;
+                }
+                if (dst) {
                     if constexpr (BITS == 4) {
-                        *(uint4*)(dst + 16 * g) = make_uint4(__byte_perm(w[0], 0, 0x0123), __byte_perm(w[1], 0, 0x0123),
-                                                             __byte_perm(w[2], 0, 0x0123), __byte_perm(w[3], 0, 0x0123));
+                        *(uint4*)(dst + 16 * g) = make_uint4(w[0], w[1], w[2], w[3]);
                     } else if constexpr (BITS == 2) {
-                        *(uint2*)(dst + 8 * g) = make_uint2(__byte_perm(w[0], 0, 0x0123), __byte_perm(w[1], 0, 0x0123));
+                        *(uint2*)(dst + 8 * g) = make_uint2(w[0], w[1]);
                     } else {
                         // 3-bit: each word holds 24 stream bits (bits 23..0, first code on top)
                         uint32_t* d3 = (uint32_t*)(dst + 12 * g);
@@ -616,9 +666,6 @@ __device__ __forceinline__ void compress_cta(const CUtensorMap* tmap_p, const Tq
                     }
                 }
             }
-            };
-            if (__any_sync(0xffffffffu, !finite)) pass2(std::true_type{});
-            else pass2(std::false_type{});
             if (prow < 0) continue;
             ((__half*)a.norms_pool)[prow] = __float2half_rn(norm_f);
             const uint32_t flags = ((norm_amb && !zero) ? kFixNorm : 0u) |
@@ -645,9 +692,9 @@ __device__ __forceinline__ void compress_cta(const CUtensorMap* tmap_p, const Tq
                     for (int c4 = 0; c4 < 4; ++c4) {
                         uint32_t m = mask[c4];
                         while (m) {
-                            const uint32_t i = (uint32_t)(c4 * 32 + __ffs(m) - 1);
+                            const uint32_t ci = (uint32_t)(c4 * 32 + __ffs(m) - 1);
                             m &= m - 1;
-                            misc->sq[q0 + k] = FixEntry{(uint32_t)vi, i | kHasCoord | nf, prow};
+                            misc->sq[q0 + k] = FixEntry{(uint32_t)vi, ci | kHasCoord | nf, prow};
                             nf = 0;
                             ++k;
                         }
@@ -736,6 +783,7 @@ static int launch_umma(const TqArgs* jobs, int njobs, cudaStream_t s) {
     for (int j = 0; j < njobs; ++j) {
         if (!encode_input_map(&L.map[j], jobs[j], dtype_of<TIn>::value == FB_BF16)) return (int)cudaErrorInvalidValue;
         L.job[j].a = jobs[j];
+        L.job[j].hdiv = sm100::make_divu32((uint32_t)jobs[j].num_heads);
         tiles[j] = (jobs[j].num_tokens * jobs[j].num_heads + umma::TILE - 1) / umma::TILE;
         L.job[j].num_tiles = (int)tiles[j];
     }
