@@ -734,9 +734,9 @@ def run_tq_config4(args, rank: int, world: int, local_rank: int) -> dict | None:
             K.tq_compress_kv_paged(kv[0], kv[1], rot[0], rot[1], cen, cen, bits, bits, pools[0][0], pools[0][1],
                                    pools[1][0], pools[1][1], block_table=table)
 
-        def dequant():
-            for j in range(2):
-                K.tq_dequant_paged(pools[j][0], pools[j][1], rot[j], cen, bits, outs[j], block_table=table)
+        def dequant():  # K and V of the step in one call (one launch)
+            K.tq_dequant_kv_paged(pools[0][0], pools[0][1], pools[1][0], pools[1][1], rot[0], rot[1], cen, cen, bits,
+                                  bits, outs[0], outs[1], block_table=table)
 
         ms_q, ms_d = timed(quant), timed(dequant)
         vec = 2 * T_all * H  # K and V vectors of the whole job
@@ -972,18 +972,23 @@ def profile_kernel(args) -> None:
         fn = lambda: K.tq_compress_kv_paged(xs[0], xs[1], rots[0], rots[1], cen, cen, 4, 4, pools[0][0], pools[0][1],
                                             pools[1][0], pools[1][1], block_table=table)
     elif args.profile_kernel == "tq_dequant":
-        # BASELINE config 4 dequantize: the K pool of 65536 tokens x 8 KV heads x 128 back to FP16
+        # BASELINE config 4 dequantize: the K and V pools of 65536 tokens x 8 KV heads x 128 back
+        # to FP16, one launch for both (as the bench's dequantize step)
         Tk = 65536
-        x = torch.randn((Tk, NKV, HD), generator=g, device=dev)
-        x = torch.where(torch.rand((Tk, NKV, HD), generator=g, device=dev) < 0.005, x * 10, x).to(torch.float16)
-        rot = torch.from_numpy(K.tq_rotation_matrix(HD, 42)).to(dev)
+        rots = [torch.from_numpy(K.tq_rotation_matrix(HD, sd)).to(dev) for sd in (42, 542)]
         cen = torch.from_numpy(K.tq_codebook(HD, 4)[0]).to(dev)
         table = torch.randperm(Tk // 16, generator=g, device=dev).to(torch.int32)
-        packed = torch.empty((Tk, NKV * 64), dtype=torch.uint8, device=dev)
-        norms = torch.empty((Tk, NKV), dtype=torch.float16, device=dev)
-        K.tq_compress_paged(x, rot, cen, 4, packed, norms, block_table=table)
-        out = torch.empty((Tk, NKV, HD), dtype=torch.float16, device=dev)
-        fn = lambda: K.tq_dequant_paged(packed, norms, rot, cen, 4, out, block_table=table)
+        pools = []
+        for j in range(2):
+            x = torch.randn((Tk, NKV, HD), generator=g, device=dev)
+            x = torch.where(torch.rand((Tk, NKV, HD), generator=g, device=dev) < 0.005, x * 10, x).to(torch.float16)
+            packed = torch.empty((Tk, NKV * 64), dtype=torch.uint8, device=dev)
+            norms = torch.empty((Tk, NKV), dtype=torch.float16, device=dev)
+            K.tq_compress_paged(x, rots[j], cen, 4, packed, norms, block_table=table)
+            pools.append((packed, norms))
+        outs = [torch.empty((Tk, NKV, HD), dtype=torch.float16, device=dev) for _ in range(2)]
+        fn = lambda: K.tq_dequant_kv_paged(pools[0][0], pools[0][1], pools[1][0], pools[1][1], rots[0], rots[1], cen,
+                                           cen, 4, 4, outs[0], outs[1], block_table=table)
     else:
         tab = rnd(VOCAB, HID)
         ids = torch.randint(0, VOCAB, (T,), generator=g, device=dev, dtype=torch.int32)

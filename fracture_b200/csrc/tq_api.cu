@@ -13,14 +13,15 @@ namespace fb {
 int tq_compress_umma(const TqArgs& a, cudaStream_t s, bool* handled);
 int tq_compress_umma_pair(const TqArgs& k, const TqArgs& v, cudaStream_t s, bool* handled);
 int tq_dequant_umma(const TqArgs& a, cudaStream_t s, bool* handled);
+int tq_dequant_umma_pair(const TqArgs& k, const TqArgs& v, cudaStream_t s, bool* handled);
 }
 
 using namespace fb;
 
 // Calls served per path since the library was loaded: compress small / tensor-core / exact, then
-// dequantize small / tensor-core / exact, then K+V compress pairs served by one tensor-core launch
-// (fb_tq_path_counts).
-constexpr int kTqPaths = 7;
+// dequantize small / tensor-core / exact, then K+V compress and K+V dequantize pairs served by one
+// tensor-core launch (fb_tq_path_counts).
+constexpr int kTqPaths = 8;
 static std::atomic<unsigned long long> g_tq_path_calls[kTqPaths];
 
 static int count_path(int which, int rc) {
@@ -135,17 +136,19 @@ extern "C" int fb_launch_tq_compress_slots(const void* input, int dtype, const f
                            slot_map, 0, num_pool_rows, packed_pool, norms_pool, err_count, stream);
 }
 
-static int tq_dequant_any(const void* packed_pool, const void* norms_pool, const float* rotation,
-                          const float* centroids, int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
-                          const int32_t* block_table, const int64_t* slot_map, int64_t start_pos,
-                          int64_t num_pool_rows, void* output, int dtype, void* stream) {
+// Checks one dequantize call and fills its argument block (a.num_tokens == 0: nothing to do).
+static int tq_dequant_args(const void* packed_pool, const void* norms_pool, const float* rotation,
+                           const float* centroids, int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                           const int32_t* block_table, const int64_t* slot_map, int64_t start_pos,
+                           int64_t num_pool_rows, void* output, int dtype, TqArgs* out) {
+    *out = TqArgs{};
     int rc = tq_check_common(bits, num_tokens, num_kv_heads, head_dim, num_pool_rows);
     if (rc) return rc;
     if (dtype != FB_FP16 && dtype != FB_BF16 && dtype != FB_FP32) return (int)cudaErrorInvalidValue;
     if (start_pos < 0) return (int)cudaErrorInvalidValue;
     if (num_tokens == 0) return 0;
     if (!packed_pool || !norms_pool || !rotation || !centroids || !output) return (int)cudaErrorInvalidValue;
-    TqArgs a{};
+    TqArgs& a = *out;
     a.rotation = rotation;
     a.centroids = centroids;
     a.bits = bits;
@@ -161,11 +164,51 @@ static int tq_dequant_any(const void* packed_pool, const void* norms_pool, const
     a.norms_pool = const_cast<void*>(norms_pool);
     a.output = output;
     a.out_dtype = dtype;
+    return 0;
+}
+
+static int tq_dequant_dispatch(const TqArgs& a, void* stream) {
     if (tq_small_dequant_call(a)) return count_path(3, tq_dequant_small(a, (cudaStream_t)stream));
     bool handled = false;
-    rc = tq_dequant_umma(a, (cudaStream_t)stream, &handled);
+    const int rc = tq_dequant_umma(a, (cudaStream_t)stream, &handled);
     if (handled) return count_path(4, rc);
     return count_path(5, tq_dequant_exact(a, (cudaStream_t)stream));
+}
+
+static int tq_dequant_any(const void* packed_pool, const void* norms_pool, const float* rotation,
+                          const float* centroids, int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                          const int32_t* block_table, const int64_t* slot_map, int64_t start_pos,
+                          int64_t num_pool_rows, void* output, int dtype, void* stream) {
+    TqArgs a;
+    const int rc = tq_dequant_args(packed_pool, norms_pool, rotation, centroids, bits, num_tokens, num_kv_heads,
+                                   head_dim, block_table, slot_map, start_pos, num_pool_rows, output, dtype, &a);
+    if (rc || a.num_tokens == 0) return rc;
+    return tq_dequant_dispatch(a, stream);
+}
+
+// K and V of one cache read: one tensor-core launch for both where they qualify, else two calls.
+extern "C" int fb_launch_tq_dequant_kv_paged(const void* k_packed_pool, const void* k_norms_pool,
+                                             const void* v_packed_pool, const void* v_norms_pool,
+                                             const float* k_rotation, const float* v_rotation,
+                                             const float* k_centroids, const float* v_centroids, int key_bits,
+                                             int value_bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                                             const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
+                                             void* k_output, void* v_output, int dtype, void* stream) {
+    TqArgs k, v;
+    int rc = tq_dequant_args(k_packed_pool, k_norms_pool, k_rotation, k_centroids, key_bits, num_tokens, num_kv_heads,
+                             head_dim, block_table, nullptr, start_pos, num_pool_rows, k_output, dtype, &k);
+    if (rc) return rc;
+    rc = tq_dequant_args(v_packed_pool, v_norms_pool, v_rotation, v_centroids, value_bits, num_tokens, num_kv_heads,
+                         head_dim, block_table, nullptr, start_pos, num_pool_rows, v_output, dtype, &v);
+    if (rc || num_tokens == 0) return rc;
+    if (!tq_small_dequant_call(k)) {
+        bool handled = false;
+        rc = tq_dequant_umma_pair(k, v, (cudaStream_t)stream, &handled);
+        if (handled) return count_path(7, rc);
+    }
+    rc = tq_dequant_dispatch(k, stream);
+    if (rc) return rc;
+    return tq_dequant_dispatch(v, stream);
 }
 
 extern "C" int fb_launch_tq_dequant_paged(const void* packed_pool, const void* norms_pool, const float* rotation,

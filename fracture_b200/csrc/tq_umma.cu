@@ -320,7 +320,9 @@ __device__ __forceinline__ void compress_cta(const CUtensorMap* tmap_p, const Tq
     const int num_tiles = jb.num_tiles;
     const int cta = (int)blockIdx.x - jb.cta0, ncta = jb.ncta;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    // 1024-byte aligned by pointer arithmetic on the shared array, so that the compiler still
+    // knows every pointer derived from it addresses shared memory (plain ld/st.shared)
+    uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sB = base;
     uint8_t* sA = base + Smem::a_off(NPARTS);
     uint32_t* lut = (uint32_t*)(base + Smem::lut_off(NPARTS));

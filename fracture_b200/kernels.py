@@ -100,6 +100,19 @@ def tq_dequant_paged(packed_pool, norms_pool, rotation, centroids, bits, out, bl
         _stream(stream)), "tq_dequant_paged")
 
 
+def tq_dequant_kv_paged(k_pool, k_norms, v_pool, v_norms, k_rotation, v_rotation, k_centroids, v_centroids,
+                        key_bits, value_bits, k_out, v_out, block_table=None, start_pos=0, stream=None):
+    """K and V of one cache read into ``k_out``/``v_out`` (``[T, H, d]``), one launch where both qualify."""
+    T, H, d = k_out.shape
+    assert v_out.shape == k_out.shape and v_out.dtype == k_out.dtype
+    rows = k_norms.shape[0]
+    _ok(_lib.load().fb_launch_tq_dequant_kv_paged(
+        k_pool.data_ptr(), k_norms.data_ptr(), v_pool.data_ptr(), v_norms.data_ptr(), k_rotation.data_ptr(),
+        v_rotation.data_ptr(), k_centroids.data_ptr(), v_centroids.data_ptr(), key_bits, value_bits, T, H, d,
+        block_table.data_ptr() if block_table is not None else None, start_pos, rows, k_out.data_ptr(),
+        v_out.data_ptr(), _dt(k_out), _stream(stream)), "tq_dequant_kv_paged")
+
+
 def tq_compress_slots(x, rotation, centroids, bits, packed_pool, norms_pool, slot_map, err=None, stream=None):
     """Batched append: token t of ``x [T, H, d]`` into pool row ``slot_map[t]`` (int64 tensor)."""
     T, H, d = x.shape
@@ -120,7 +133,7 @@ def tq_dequant_slots(packed_pool, norms_pool, rotation, centroids, bits, out, sl
 
 
 TQ_PATHS = ("compress_small", "compress_tensor_core", "compress_exact", "dequant_small", "dequant_tensor_core",
-            "dequant_exact", "compress_kv_fused")
+            "dequant_exact", "compress_kv_fused", "dequant_kv_fused")
 
 
 def tq_path_counts() -> dict:

@@ -204,7 +204,8 @@ int fb_launch_tq_compress_kv_paged(const void* k_input, const void* v_input, int
  * reference counterpart; for tests and diagnostics): counts[0..2] = compress calls that took the
  * small-call kernel (tq_small.cu), the tensor-core kernel (tq_umma.cu) and the exact CUDA-core
  * kernel (tq_exact.cu); counts[3..5] the same for dequantize; counts[6] = K+V pairs of
- * fb_launch_tq_compress_kv_paged served by one tensor-core launch. Writes min(n, 7) counters. */
+ * fb_launch_tq_compress_kv_paged served by one tensor-core launch; counts[7] the same for
+ * fb_launch_tq_dequant_kv_paged. Writes min(n, 8) counters. */
 int fb_tq_path_counts(unsigned long long* counts, int n);
 
 /* Batched append (no reference counterpart; the reference appends one sequence at a time,
@@ -226,6 +227,20 @@ int fb_launch_tq_dequant_paged(const void* packed_pool, const void* norms_pool, 
                                const float* centroids, int bits, int64_t num_tokens, int num_kv_heads,
                                int head_dim, const int32_t* block_table, int64_t start_pos,
                                int64_t num_pool_rows, void* output, int dtype, void* stream);
+
+/* K and V of one cache read in one call (no reference counterpart): fb_launch_tq_dequant_paged for
+ * the keys (k_*, key_bits) and the values (v_*, value_bits), same tokens, block table and pool
+ * rows, outputs of one `dtype`. Where both take the tensor-core kernel with whole-token tiles
+ * (head_dim 128, FP16/BF16 output, 2/3/4-bit codes of equal width or 4-bit keys with 2-bit
+ * values, KV head count a multiple of 8 dividing 128, 16-byte aligned pools) they run as one
+ * launch whose grid is split between K and V; otherwise as two calls. Results equal the two
+ * separate calls bit for bit. */
+int fb_launch_tq_dequant_kv_paged(const void* k_packed_pool, const void* k_norms_pool, const void* v_packed_pool,
+                                  const void* v_norms_pool, const float* k_rotation, const float* v_rotation,
+                                  const float* k_centroids, const float* v_centroids, int key_bits, int value_bits,
+                                  int64_t num_tokens, int num_kv_heads, int head_dim, const int32_t* block_table,
+                                  int64_t start_pos, int64_t num_pool_rows, void* k_output, void* v_output, int dtype,
+                                  void* stream);
 
 /* Gather counterpart of fb_launch_tq_compress_slots (no reference counterpart): output token t is
  * dequantized from pool row slot_map[t] (no row: zeros). Same kernels and tolerance as

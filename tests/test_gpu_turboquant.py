@@ -497,6 +497,66 @@ def test_tensor_core_dequant_paged_many_tiles(dt, bits):
     assert (num / den).min() > 0.9999
 
 
+@pytest.mark.parametrize("dt,kb,vb,T,H,start", [("f16", 4, 4, 4099, 8, 21), ("bf16", 4, 2, 2000, 8, 0),
+                                               ("f16", 3, 3, 1500, 16, 5), ("f16", 2, 2, 700, 32, 13),
+                                               ("bf16", 4, 4, 300, 64, 3), ("f16", 2, 4, 900, 8, 7)])
+def test_dequant_kv_one_launch_with_missing_blocks(dt, kb, vb, T, H, start):
+    """fb_launch_tq_dequant_kv_paged: K and V from shuffled pools in one launch (widths with a fused
+    kernel; 2/4 goes as two calls), with two block-table entries negative and the pool ending 5 rows
+    into the last block, so whole tiles, parts of tiles and parts of blocks have no pool row. Every
+    token with a row equals the float32 statement (3e-4 of magnitude beyond the output rounding,
+    cosine 0.9999 per vector); tokens without one are zero; the fused call equals the two separate
+    calls bit for bit."""
+    d = 128
+    nblk = (start + T + 15) // 16
+    table = np.random.default_rng(T + H).permutation(nblk).astype(np.int32)
+    table[nblk // 3] = -1
+    table[(2 * nblk) // 3] = -7
+    rows = int(table.max()) * 16 + 5  # the highest block keeps only its first 5 rows
+    tt = torch.from_numpy(table).to(DEV)
+    pos = start + np.arange(T)
+    slot = table[pos // 16].astype(np.int64) * 16 + pos % 16
+    has_row = (table[pos // 16] >= 0) & (slot < rows)
+    assert has_row.sum() < T and has_row.sum() > T // 2
+    jobs = []
+    for j, b in enumerate((kb, vb)):
+        x, raw = make_input(T, H, d, "f16", seed=60 + 7 * j + T)
+        pi, c = tables(d, b, 31 + j)
+        P = d * b // 8
+        packed = torch.zeros((rows, H * P), dtype=torch.uint8, device=DEV)
+        norms = torch.zeros((rows, H), dtype=torch.float16, device=DEV)
+        tpi, tc = torch.from_numpy(pi).to(DEV), torch.from_numpy(c).to(DEV)
+        # write only the tokens that have a row (the others would be refused and counted)
+        err = torch.zeros(1, dtype=torch.int32, device=DEV)
+        K.tq_compress_paged(dev(x, "f16"), tpi, tc, b, packed, norms, block_table=tt, start_pos=start, err=err)
+        torch.cuda.synchronize()
+        assert err.item() == (T - has_row.sum()) * H
+        jobs.append(dict(x=x, raw=raw, pi=pi, c=c, b=b, packed=packed, norms=norms, tpi=tpi, tc=tc))
+    outs = [torch.full((T, H, d), 7.0, dtype=TDT[dt], device=DEV) for _ in range(2)]
+    before = K.tq_path_counts()
+    K.tq_dequant_kv_paged(jobs[0]["packed"], jobs[0]["norms"], jobs[1]["packed"], jobs[1]["norms"], jobs[0]["tpi"],
+                          jobs[1]["tpi"], jobs[0]["tc"], jobs[1]["tc"], kb, vb, outs[0], outs[1], block_table=tt,
+                          start_pos=start)
+    torch.cuda.synchronize()
+    after = K.tq_path_counts()
+    fused = kb == vb or (kb, vb) == (4, 2)
+    assert after["dequant_kv_fused"] - before["dequant_kv_fused"] == (1 if fused else 0), (before, after)
+    for j, jb in enumerate(jobs):
+        sep = torch.full((T, H, d), 7.0, dtype=TDT[dt], device=DEV)
+        K.tq_dequant_paged(jb["packed"], jb["norms"], jb["tpi"], jb["tc"], jb["b"], sep, block_table=tt,
+                           start_pos=start)
+        torch.cuda.synchronize()
+        assert torch.equal(sep.view(torch.int16), outs[j].view(torch.int16)), f"job {j}: fused differs from separate"
+        got = outs[j].float().cpu().numpy()
+        assert not np.any(got[~has_row]), f"job {j}: a token without a pool row is not zero"
+        pc, nc, _ = tq.compress_c(jb["raw"][has_row], tq.INPUT_F16, jb["pi"], jb["c"], jb["b"], num_threads=8)
+        ref = tq.decompress_c(pc, nc, jb["pi"], jb["c"], jb["b"], H, d).reshape(-1, H, d)
+        g = got[has_row]
+        ops.assert_close_fp(g, ref, rel=3e-4, min_cos=0.9999, label=f"job {j} {dt}/{jb['b']}", dtype=dt)
+        cos = (g * ref).sum(-1) / (np.linalg.norm(g, axis=-1) * np.linalg.norm(ref, axis=-1) + 1e-30)
+        assert cos.min() > 0.9999
+
+
 @pytest.mark.parametrize("H", [1, 3, 5, 7])
 def test_tensor_core_dequant_odd_head_counts(H):
     """Token and head of each vector come from a division by the head count done by
