@@ -989,6 +989,23 @@ def profile_kernel(args) -> None:
         outs = [torch.empty((Tk, NKV, HD), dtype=torch.float16, device=dev) for _ in range(2)]
         fn = lambda: K.tq_dequant_kv_paged(pools[0][0], pools[0][1], pools[1][0], pools[1][1], rots[0], rots[1], cen,
                                            cen, 4, 4, outs[0], outs[1], block_table=table)
+    elif args.profile_kernel in ("tq_small_compress", "tq_small_dequant"):
+        # decode-sized TurboQuant write / read (config 5 decode: the new tokens of a group of 32
+        # sequences, 8 KV heads, into slot-mapped pool rows): 256 vectors compressed, 192 read back
+        n_tok = 32 if args.profile_kernel == "tq_small_compress" else 24
+        rows = 256 * 1152
+        rot = torch.from_numpy(K.tq_rotation_matrix(HD, 42)).to(dev)
+        cen = torch.from_numpy(K.tq_codebook(HD, 4)[0]).to(dev)
+        pool = torch.zeros((rows, NKV * 64), dtype=torch.uint8, device=dev)
+        norms = torch.zeros((rows, NKV), dtype=torch.float16, device=dev)
+        slots = (torch.randperm(256, generator=g, device=dev)[:n_tok].to(torch.int64) * 1152 + 1030).contiguous()
+        x = torch.randn((n_tok, NKV, HD), generator=g, device=dev).to(torch.float16)
+        K.tq_compress_slots(x, rot, cen, 4, pool, norms, slots)
+        out = torch.empty_like(x)
+        if args.profile_kernel == "tq_small_compress":
+            fn = lambda: K.tq_compress_slots(x, rot, cen, 4, pool, norms, slots)
+        else:
+            fn = lambda: K.tq_dequant_slots(pool, norms, rot, cen, 4, out, slots)
     else:
         tab = rnd(VOCAB, HID)
         ids = torch.randint(0, VOCAB, (T,), generator=g, device=dev, dtype=torch.int32)
@@ -1021,7 +1038,8 @@ def main() -> None:
     ap.add_argument("--only", default=None, choices=["tq", "decode", "attention"],
                     help="run only this workload on one GPU and print its figures")
     ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding", "tq_compress",
-                                                                   "tq_dequant", "tq_attention", "attention_fp16"],
+                                                                   "tq_dequant", "tq_attention", "attention_fp16",
+                                                                   "tq_small_compress", "tq_small_dequant"],
                     help="run only this kernel at its config-3 size (W warm-up launches + 1), for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
