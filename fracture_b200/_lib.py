@@ -31,6 +31,14 @@ class FbTqConfig(C.Structure):
                 ("seed", C.c_uint64)]
 
 
+class FbRopeParams(C.Structure):
+    _fields_ = [("theta", C.c_double), ("factor", C.c_double), ("original_context", C.c_double),
+                ("low_freq_factor", C.c_double), ("high_freq_factor", C.c_double), ("scaling", C.c_int32),
+                ("head_dim", C.c_int32), ("num_freq_factors", C.c_int32), ("pad0", C.c_int32)]
+
+
+FB_ROPE_SCALING = {0: "none", 1: "linear", 2: "llama3", 3: "factors"}
+
 TP = C.POINTER(FbTensor)
 
 # name -> (restype, argtypes)
@@ -74,6 +82,9 @@ SIGNATURES = {
     "fb_rope_freqs_llama3": (i32, [i32, C.c_double, C.c_double, C.c_double, C.c_double, C.c_double, f32p]),
     "fb_tq_codebook": (i32, [i32, i32, f32p, f32p]),
     "fb_tq_rotation_matrix": (i32, [i32, C.c_uint64, f32p]),
+    "fb_gguf_rope_params": (i32, [C.c_char_p, C.POINTER(FbRopeParams)]),
+    "fb_rope_freqs_from_gguf": (i32, [C.c_char_p, i32, f32p]),
+    "fb_gguf_last_error": (C.c_char_p, []),
     # 3. backend object
     "fb_last_error": (C.c_char_p, []),
     "fb_backend_create": (i32, [i32, C.POINTER(vp)]),
@@ -98,6 +109,7 @@ SIGNATURES = {
     "fb_synchronize": (i32, [vp]),
     "fb_precompute_rope_freqs": (i32, [vp, szt, C.c_double]),
     "fb_precompute_rope_freqs_llama3": (i32, [vp, szt, C.c_double, C.c_double, C.c_double, C.c_double, C.c_double]),
+    "fb_precompute_rope_freqs_gguf": (i32, [vp, szt, C.c_char_p]),
     "fb_create_timer": (i32, [vp, C.POINTER(C.c_uint64)]),
     "fb_start_timer": (i32, [vp, C.c_uint64]),
     "fb_stop_timer": (i32, [vp, C.c_uint64, C.POINTER(C.c_float)]),

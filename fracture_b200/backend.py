@@ -218,6 +218,11 @@ class CudaBackend:
                                                          float(low_freq_factor), float(high_freq_factor),
                                                          float(original_max_position)))
 
+    def precompute_rope_freqs_gguf(self, head_dim: int, gguf_path) -> None:
+        """The RoPE table a GGUF model file calls for (llama3 scaling from its metadata or its
+        rope_freqs tensor); replaces precompute_rope_freqs(head_dim, theta) at the server's start."""
+        _check(self._lib.fb_precompute_rope_freqs_gguf(self._h, head_dim, str(gguf_path).encode()))
+
     # timers ------------------------------------------------------------------
     def create_timer(self) -> int:
         t = C.c_uint64()

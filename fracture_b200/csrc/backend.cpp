@@ -607,6 +607,21 @@ int fb_precompute_rope_freqs_llama3(fb_backend* b, size_t head_dim, double theta
     return FB_OK;
 }
 
+int fb_precompute_rope_freqs_gguf(fb_backend* b, size_t head_dim, const char* gguf_path) {
+    if (!b || !gguf_path) return fail(FB_ERR_BACKEND, "null argument");
+    std::vector<float> f(head_dim / 2);
+    if (head_dim == 0 || fb_rope_freqs_from_gguf(gguf_path, (int)head_dim, f.data()))
+        return fail(FB_ERR_MODEL_CONFIG, std::string("rope frequencies from GGUF: ") + fb_gguf_last_error());
+    std::lock_guard<std::recursive_mutex> g(b->mu);
+    int rc;
+    if ((rc = b->flush())) return rc;
+    FB_CUDA(b->freq.ensure(f.size() * sizeof(float), b->stream));
+    FB_CUDA(cudaMemcpyAsync(b->freq.ptr, f.data(), f.size() * sizeof(float), cudaMemcpyHostToDevice, b->stream));
+    FB_CUDA(cudaStreamSynchronize(b->stream));
+    b->freq_half = (int)f.size();
+    return FB_OK;
+}
+
 int fb_rope(fb_backend* b, const fb_tensor* q, const fb_tensor* k, const uint32_t* positions, size_t num_positions,
             double theta, size_t head_dim) {
     (void)theta;  // the table comes from precompute_rope_freqs, as in the reference (backend.rs:161-172)

@@ -214,6 +214,26 @@ def rope_freqs_llama3(head_dim, theta, factor, low, high, original_max_position)
     return out
 
 
+def gguf_rope_params(path) -> dict:
+    """The rope metadata of a GGUF file (fb_gguf_rope_params)."""
+    p = _lib.FbRopeParams()
+    lib = _lib.load()
+    if lib.fb_gguf_rope_params(str(path).encode(), C.byref(p)) != 0:
+        raise ValueError(lib.fb_gguf_last_error().decode())
+    d = {n: getattr(p, n) for n, _ in p._fields_ if n != "pad0"}
+    d["scaling"] = _lib.FB_ROPE_SCALING[d["scaling"]]
+    return d
+
+
+def rope_freqs_from_gguf(path, head_dim: int) -> np.ndarray:
+    """The RoPE frequency table a GGUF model file calls for (fb_rope_freqs_from_gguf)."""
+    out = np.empty(head_dim // 2, dtype=np.float32)
+    lib = _lib.load()
+    if lib.fb_rope_freqs_from_gguf(str(path).encode(), head_dim, out.ctypes.data_as(_lib.f32p)) != 0:
+        raise ValueError(lib.fb_gguf_last_error().decode())
+    return out
+
+
 def tq_codebook(dim: int, bits: int):
     c = np.zeros(1 << bits, dtype=np.float32)
     b = np.zeros((1 << bits) - 1, dtype=np.float32)

@@ -313,6 +313,31 @@ int fb_tq_codebook(int dim, int bits, float* centroids, float* boundaries);
 /* generate_rotation_matrix (turboquant.rs:306-338): out[d*d] row-major f32. */
 int fb_tq_rotation_matrix(int d, uint64_t seed, float* out);
 
+/* RoPE frequencies from a GGUF model file (no reference counterpart: the reference reads only
+ * `{arch}.rope.freq_base`, crates/fracture-gguf/src/parser.rs:482, and calls
+ * precompute_rope_freqs(head_dim, theta) at bins/fracture-server-cuda/src/main.rs:104, so Llama
+ * 3.1 runs with unscaled frequencies). fb_gguf_rope_params reads the file's rope metadata:
+ * theta (`{arch}.rope.freq_base`, default 500000 as in the reference), `rope.dimension_count`,
+ * `rope.scaling.{type,factor,original_context_length,low_freq_factor,high_freq_factor}`
+ * (defaults 1, 8192, 1, 4) and whether a `rope_freqs.weight` F32 tensor of per-pair divisors is
+ * present (what llama.cpp's converter writes for Llama 3.1). fb_rope_freqs_from_gguf builds the
+ * head_dim/2 table the RoPE kernels take: base / divisors when the tensor is there, else the llama3
+ * rule (fb_rope_freqs_llama3) for scaling type "llama3", base / factor for "linear", else the
+ * reference's table (fb_rope_freqs). Host only; returns 0, or non-zero with the reason in
+ * fb_gguf_last_error(). */
+enum fb_rope_scaling { FB_ROPE_SCALING_NONE = 0, FB_ROPE_SCALING_LINEAR = 1, FB_ROPE_SCALING_LLAMA3 = 2,
+                       FB_ROPE_SCALING_FACTORS = 3 };
+typedef struct fb_rope_params {
+    double theta, factor, original_context, low_freq_factor, high_freq_factor;
+    int32_t scaling;           /* enum fb_rope_scaling */
+    int32_t head_dim;          /* rope.dimension_count, 0 when absent */
+    int32_t num_freq_factors;  /* entries of rope_freqs.weight, 0 when absent */
+    int32_t pad0;
+} fb_rope_params;
+int fb_gguf_rope_params(const char* path, fb_rope_params* out);
+int fb_rope_freqs_from_gguf(const char* path, int head_dim, float* out);
+const char* fb_gguf_last_error(void);
+
 /* ======================================================================== */
 /* 3. Backend object (mirror of trait Backend)                              */
 /* ======================================================================== */
@@ -379,6 +404,9 @@ int fb_synchronize(fb_backend* b);
 int fb_precompute_rope_freqs(fb_backend* b, size_t head_dim, double theta);
 int fb_precompute_rope_freqs_llama3(fb_backend* b, size_t head_dim, double theta, double factor,
                                     double low_freq_factor, double high_freq_factor, double original_max_position);
+/* precompute_rope_freqs from a GGUF model file: the table of fb_rope_freqs_from_gguf uploaded as
+ * the backend's RoPE table (the call-site change for bins/fracture-server-cuda/src/main.rs:104). */
+int fb_precompute_rope_freqs_gguf(fb_backend* b, size_t head_dim, const char* gguf_path);
 
 /* Timers (backend.rs:132-143; src/timers.rs). */
 int fb_create_timer(fb_backend* b, uint64_t* timer);

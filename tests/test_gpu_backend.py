@@ -149,6 +149,45 @@ def test_rope_requires_freq_table_then_matches_oracle():
     b.close()
 
 
+def test_rope_table_from_a_gguf_file(tmp_path):
+    """precompute_rope_freqs_gguf: a GGUF file whose metadata says llama3 scaling gives the same
+    rotated Q/K bytes as precompute_rope_freqs_llama3 with those parameters (the call-site change
+    for bins/fracture-server-cuda/src/main.rs:104)."""
+    gguf = pytest.importorskip("gguf")
+    path = tmp_path / "llama31.gguf"
+    w = gguf.GGUFWriter(str(path), "llama")
+    w.add_float32("llama.rope.freq_base", 5e5)
+    w.add_string("llama.rope.scaling.type", "llama3")
+    w.add_float32("llama.rope.scaling.factor", 8.0)
+    w.add_uint32("llama.rope.scaling.original_context_length", 8192)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    rng = np.random.default_rng(5)
+    qx = ops.round_to(rng.standard_normal((16, 32, 128)), "f16")
+    kx = ops.round_to(rng.standard_normal((16, 8, 128)), "f16")
+    pos = rng.integers(0, 8192, 16).astype(np.uint32)
+    outs = []
+    for how in ("gguf", "params"):
+        b = CudaBackend(0)
+        if how == "gguf":
+            b.precompute_rope_freqs_gguf(128, path)
+        else:
+            b.precompute_rope_freqs_llama3(128, 5e5, 8.0, 1.0, 4.0, 8192)
+        tq_, tk = upload(b, qx), upload(b, kx)
+        b.rope(tq_, tk, pos, 5e5, 128)
+        outs.append((download(b, tq_), download(b, tk)))
+        b.close()
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+    with pytest.raises(BackendError, match="rope frequencies from GGUF"):
+        b = CudaBackend(0)
+        try:
+            b.precompute_rope_freqs_gguf(128, tmp_path / "missing.gguf")
+        finally:
+            b.close()
+
+
 def test_embedding_through_backend(be):
     table = np.random.default_rng(2).standard_normal((256, 64)).astype(np.float32) * 0.02
     tt = upload(be, table, FB_BF16)
