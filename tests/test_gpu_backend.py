@@ -7,6 +7,7 @@ import numpy as np
 import pytest
 
 from fracture_b200.backend import (FB_BF16, FB_FP16, FB_FP32, FB_INT8, BackendError, CudaBackend, InvalidShape,
+                                   ModelConfigError,
                                    KvCacheError, OutOfMemory, PagedKvCache, QuantizedKvCache, TensorNotFound, TurboQuantConfig)
 from fracture_b200 import kernels as K
 from oracle import ops, turboquant as tq
@@ -180,7 +181,7 @@ def test_rope_table_from_a_gguf_file(tmp_path):
         outs.append((download(b, tq_), download(b, tk)))
         b.close()
     assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
-    with pytest.raises(BackendError, match="rope frequencies from GGUF"):
+    with pytest.raises(ModelConfigError, match="rope frequencies from GGUF"):
         b = CudaBackend(0)
         try:
             b.precompute_rope_freqs_gguf(128, tmp_path / "missing.gguf")
