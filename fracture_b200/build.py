@@ -73,7 +73,21 @@ def build(verbose: bool = False, jobs: int | None = None) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed\n{r.stdout}\n{r.stderr}")
+        _check_defined(LIB)
     return LIB
+
+
+def _check_defined(lib: Path) -> None:
+    """A shared library links with undefined symbols; fail the build if one of this library's own
+    (namespace fb or an fb_/launch_ entry point) is left undefined, instead of at first call."""
+    r = subprocess.run(["nm", "-D", "--undefined-only", str(lib)], capture_output=True, text=True)
+    if r.returncode != 0:
+        return  # no nm: nothing to check with
+    missing = [ln.split()[-1] for ln in r.stdout.splitlines()
+               if ln.split() and ln.split()[-1].startswith(("_ZN2fb", "fb_", "launch_"))]
+    if missing:
+        lib.unlink()
+        raise RuntimeError("undefined library symbols: " + ", ".join(missing))
 
 
 if __name__ == "__main__":

@@ -20,13 +20,18 @@ using namespace fb;
 
 // Calls served per path since the library was loaded: compress small / tensor-core / exact, then
 // dequantize small / tensor-core / exact, then K+V compress and K+V dequantize pairs served by one
-// tensor-core launch (fb_tq_path_counts).
-constexpr int kTqPaths = 8;
+// tensor-core launch, then paged attention calls served by the CUDA-core, the per-head
+// tensor-core and the streamed tensor-core kernel (fb_tq_path_counts).
+constexpr int kTqPaths = 11;
 static std::atomic<unsigned long long> g_tq_path_calls[kTqPaths];
 
 static int count_path(int which, int rc) {
     if (rc == 0) g_tq_path_calls[which].fetch_add(1, std::memory_order_relaxed);
     return rc;
+}
+
+namespace fb {
+int tq_count_path(int which, int rc) { return count_path(which, rc); }
 }
 
 static bool tq_bits_ok(int bits) { return bits == 2 || bits == 3 || bits == 4 || bits == 8; }

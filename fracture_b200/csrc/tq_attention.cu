@@ -8,8 +8,8 @@
 // Pi_v^T acc. Here, with the centroid values read as fp16 (2^-11 relative) and everything else
 // in float32:
 //
-//   tqa_rotate_q    q_rot = Pi_k q for every query token and Q head (one warp per 32 rows
-//                   of Pi_k, lanes along the row), into the workspace
+//   tqa_rotate_q    q_rot = Pi_k q for every query token and Q head (thread i: row i of Pi_k
+//                   for all heads of a KV group), into the workspace
 //   tqa_chunk       one CTA per (256-position chunk, KV head, query token): thread p scores
 //                   position p for all Q heads of the group from the position's packed K
 //                   row (pair-of-codes lookup tables, lane-private), the CTA takes the
@@ -32,142 +32,69 @@
 #include <atomic>
 #include <cstdio>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "tq_sm100.cuh"
 #include "tq_common.cuh"
+#include "tq_attention.cuh"
 
 namespace fb {
 
+// tq_api.cu: counts a served call of path `which` when rc is 0 (fb_tq_path_counts); returns rc.
+int tq_count_path(int which, int rc);
+
 namespace tqa {
-
-constexpr int D = 128;
-constexpr int CH = 256;       // positions per chunk: one per thread of tqa_chunk
-constexpr int THREADS = 256;
-constexpr int NWARPS = THREADS / 32;
-constexpr int MAXG = 8;
-constexpr int PART = D + 2;   // floats per chunk partial: max, sum, acc[D]
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-struct AttnArgs {
-    const void* q;
-    int dtype;  // of q and out: FB_FP16 or FB_BF16
-    int num_seqs, q_per_seq, hq, hkv;
-    const int32_t* block_tables;  // [num_seqs, max_blocks]
-    int max_blocks;
-    const int32_t* kv_lens;    // [num_seqs] (null: kv_len for every sequence)
-    const int32_t* start_pos;  // [num_seqs] (null: start for every sequence)
-    int kv_len, start;
-    const float* pik;
-    const float* piv;
-    const float* ck;
-    const float* cv;
-    float* qrot;  // [rows, hq, D]
-    float* part;  // [rows, hq, nch, PART]
-    int nch;
-    int ch;   // positions per chunk
-    int rnd;  // tensor-core kernel: rounds of four 16-position tiles per warp and item
-    sm100::DivU32 dnch, dhkv, dqps;  // nch, hkv, q_per_seq as multiply-high divisors (tensor-core kernel)
-    void* out;
-};
-
-// K/V rows in this library's contiguous pools: pool row = block * 16 + offset, head g at
-// g * P within it.
-struct PoolAddr {
-    const uint8_t* kp;
-    const __half* kn;
-    const uint8_t* vp;
-    const __half* vn;
-    int64_t pool_rows;
-    __device__ bool locate(int32_t blk, int off, int g, int hkv, int pk, int pv, const uint8_t*& krow,
-                           const uint8_t*& vrow, float& knorm, float& vnorm) const {
-        const int64_t row = (int64_t)blk * 16 + off;
-        if (row >= pool_rows) return false;
-        const int64_t hr = row * hkv + g;
-        krow = kp + hr * pk;
-        vrow = vp + hr * pv;
-        knorm = __half2float(kn[hr]);
-        vnorm = __half2float(vn[hr]);
-        return true;
-    }
-    // Rows of block blk that lie inside the pool (16 unless the pool ends inside the block).
-    __device__ int block_rows(int32_t blk) const {
-        return (int)max((int64_t)0, min((int64_t)16, pool_rows - (int64_t)blk * 16));
-    }
-    // KV head g of row `off` of block blk: K codes at kb + off * hkv * pk, its norm at
-    // knb[off * hkv]; the same for V.
-    __device__ void block_base(int32_t blk, int g, int hkv, int pk, int pv, const uint8_t*& kb, const uint8_t*& vb,
-                               const __half*& knb, const __half*& vnb) const {
-        const int64_t hr = (int64_t)blk * 16 * hkv + g;
-        kb = kp + hr * pk;
-        vb = vp + hr * pv;
-        knb = kn + hr;
-        vnb = vn + hr;
-    }
-};
-
-// The reference's per-block tensors (attention_paged_tq.cu:123-129): block b's packed K rows
-// at kp[b] ([16, hkv * P]), its norms at kn[b] ([16, hkv]); the same for V.
-struct BlockPtrAddr {
-    const uint8_t* const* kp;
-    const __half* const* kn;
-    const uint8_t* const* vp;
-    const __half* const* vn;
-    __device__ bool locate(int32_t blk, int off, int g, int hkv, int pk, int pv, const uint8_t*& krow,
-                           const uint8_t*& vrow, float& knorm, float& vnorm) const {
-        const int hr = off * hkv + g;
-        krow = kp[blk] + hr * pk;
-        vrow = vp[blk] + hr * pv;
-        knorm = __half2float(kn[blk][hr]);
-        vnorm = __half2float(vn[blk][hr]);
-        return true;
-    }
-    __device__ int block_rows(int32_t) const { return 16; }
-    __device__ void block_base(int32_t blk, int g, int hkv, int pk, int pv, const uint8_t*& kb, const uint8_t*& vb,
-                               const __half*& knb, const __half*& vnb) const {
-        kb = kp[blk] + g * pk;
-        vb = vp[blk] + g * pv;
-        knb = kn[blk] + g;
-        vnb = vn[blk] + g;
-    }
-};
-
-__device__ __forceinline__ int causal_len(const AttnArgs& a, int s, int t) {
-    const int kv = a.kv_lens ? a.kv_lens[s] : a.kv_len;
-    const int st = a.start_pos ? a.start_pos[s] : a.start;
-    return max(0, min(st + t + 1, kv));
-}
 
 __device__ __forceinline__ float load_q(const AttnArgs& a, int64_t i) {
     return a.dtype == FB_BF16 ? __bfloat162float(((const __nv_bfloat16*)a.q)[i]) : __half2float(((const __half*)a.q)[i]);
 }
 
-// q_rot[row][h][i] = sum_j Pi_k[i][j] q[row][h][j] for the heads of KV group blockIdx.y.
-__global__ void __launch_bounds__(128) tqa_rotate_q(AttnArgs a) {
+// q_rot[row][h][i] = sum_j Pi_k[i][j] q[row][h][j] for the heads of KV group blockIdx.y: thread i
+// reads row i of Pi_k (through L1, 16 bytes at a time, eight loads in flight) once for all the
+// group's heads, whose queries are broadcast from shared memory.
+__global__ void __launch_bounds__(D) tqa_rotate_q(AttnArgs a) {
     pdl_begin();
-    __shared__ float qs[MAXG][D];
-    const int row = blockIdx.x, g = blockIdx.y, G = a.hq / a.hkv;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int e = threadIdx.x; e < G * D; e += blockDim.x)
-        qs[e / D][e % D] = load_q(a, ((int64_t)row * a.hq + g * G) * D + e);
+    __shared__ float4 qs[MAXG][D / 4];
+    const int row = blockIdx.x, g = blockIdx.y, G = a.hq / a.hkv, i = threadIdx.x;
+    for (int e = threadIdx.x; e < G * D; e += D)
+        ((float*)qs)[e] = load_q(a, ((int64_t)row * a.hq + g * G) * D + e);
     __syncthreads();
-    // warp w: rows w, w + 4, ...; eight rows' loads in flight at a time
-    for (int i0 = warp; i0 < D; i0 += 32) {
+    float acc[MAXG];
+#pragma unroll
+    for (int h = 0; h < MAXG; ++h) acc[h] = 0.0f;
+    const float4* prow = (const float4*)(a.pik + (int64_t)i * D);
+#pragma unroll 1
+    for (int j0 = 0; j0 < D / 4; j0 += 8) {
         float4 p[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) p[k] = __ldg((const float4*)(a.pik + (i0 + 4 * k) * D) + lane);
-        for (int h = 0; h < G; ++h) {
-            const float4 x = *(const float4*)&qs[h][4 * lane];
+        for (int k = 0; k < 8; ++k) p[k] = __ldg(prow + j0 + k);
+#pragma unroll
+        for (int h = 0; h < MAXG; ++h) {
+            if (h >= G) break;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-                float v = p[k].x * x.x + p[k].y * x.y + p[k].z * x.z + p[k].w * x.w;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == 0) a.qrot[((int64_t)row * a.hq + g * G + h) * D + i0 + 4 * k] = v;
+                const float4 x = qs[h][j0 + k];
+                acc[h] = fmaf(p[k].x, x.x, acc[h]);
+                acc[h] = fmaf(p[k].y, x.y, acc[h]);
+                acc[h] = fmaf(p[k].z, x.z, acc[h]);
+                acc[h] = fmaf(p[k].w, x.w, acc[h]);
             }
         }
     }
+#pragma unroll
+    for (int h = 0; h < MAXG; ++h) {
+        if (h >= G) break;
+        const int64_t o = ((int64_t)row * a.hq + g * G + h) * D + i;
+        if (a.qrot_f16) ((__half*)a.qrot)[o] = __float2half_rn(acc[h]);
+        else a.qrot[o] = acc[h];
+    }
+}
+
+// One launch of tqa_rotate_q for the call's rows.
+inline int launch_rotate(const AttnArgs& a, int rows, cudaStream_t s) {
+    launch_pdl(tqa_rotate_q, dim3(rows, a.hkv), dim3(D), s, a);
+    return (int)cudaGetLastError();
 }
 
 // Decoding tables, 32 lane-private copies side by side (a warp's lookups hit 32 banks). Pair
@@ -447,7 +374,7 @@ __global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a) {
     const int h = threadIdx.x / D, i = threadIdx.x - h * D;
     const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
     const int L = causal_len(a, s, t);
-    const int nc = min((L + a.ch - 1) / a.ch, a.nch);  // kv_lens past max_kv_len: the chunks computed
+    const int nc = min((L + a.ch - 1) / a.ch * a.spc, a.nch);  // kv_lens past max_kv_len: the chunks computed
     {
         const float* ph = a.part + ((int64_t)row * a.hq + g * G + h) * a.nch * PART;
         float M = -INFINITY;
@@ -478,6 +405,12 @@ __global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a) {
     const int64_t e = ((int64_t)row * a.hq + g * G + h) * D + i;
     if (a.dtype == FB_BF16) ((__nv_bfloat16*)a.out)[e] = __float2bfloat16_rn(o);
     else ((__half*)a.out)[e] = __float2half_rn(o);
+}
+
+// One launch of tqa_combine for the call's rows.
+inline int launch_combine(const AttnArgs& a, int rows, cudaStream_t s) {
+    launch_pdl(tqa_combine, dim3(rows, a.hkv), dim3((a.hq / a.hkv) * D), s, a);
+    return (int)cudaGetLastError();
 }
 
 // ── tensor-core path: 2- and 4-bit keys and values ──
@@ -521,28 +454,6 @@ struct Smem {
     static constexpr int q_off = l_off + NWARPS * 8 * 4;              // [8 steps][32 lanes] uint2
     static constexpr int bytes = q_off + 8 * 32 * 8;
 };
-
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void ldsm_x2_trans(uint32_t& r0, uint32_t& r1, uint32_t addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr)
-                 : "memory");
-}
-
-__device__ __forceinline__ uint32_t pack_half2(float x, float y) {
-    const __half2 h = __floats2half2_rn(x, y);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-// Table address of the code byte b of word w: (byte << 8) | off, off = lane offset (< 256).
-__device__ __forceinline__ uint32_t taddr(uint32_t w, uint32_t off, int b) {
-    return __byte_perm(w, off, 0x5504u | ((uint32_t)b << 4));
-}
 
 }  // namespace tc
 
@@ -915,20 +826,34 @@ inline void tc_chunks(AttnArgs& a, int64_t positions, int64_t rows) {
     a.nch = (int)((positions + a.ch - 1) / a.ch);
 }
 
+// tq_attention_stream.cu: the streamed tensor-core kernel for pool-backed caches.
+bool stream_ok(const AttnArgs& a, int kb, int vb, const PoolAddr& ad);
+int stream_launch(AttnArgs& a, int kb, int vb, const PoolAddr& ad, cudaStream_t s);
+
 template <typename Addr>
 int run(AttnArgs a, int kb, int vb, const Addr& ad, cudaStream_t s) {
     const int rows = a.num_seqs * a.q_per_seq;
     if (rows == 0) return 0;
-    launch_pdl(tqa_rotate_q, dim3(rows, a.hkv), dim3(128), s, a);
-    int rc = (int)cudaGetLastError();
+    a.spc = 1;
+    bool streamed = false;
+    if constexpr (std::is_same<Addr, PoolAddr>::value) streamed = a.nch > 0 && stream_ok(a, kb, vb, ad);
+    a.qrot_f16 = streamed ? 1 : 0;
+    int rc = launch_rotate(a, rows, s);
     if (rc) return rc;
     // a.nch counts CH-position chunks (the workspace is sized for them); the tensor-core
-    // path takes larger chunks, so it uses fewer of the same partial slots
+    // paths take larger chunks, so they use fewer of the same partial slots
     a.ch = CH;
+    if constexpr (std::is_same<Addr, PoolAddr>::value) {
+        if (streamed) {
+            rc = tq_count_path(10, stream_launch(a, kb, vb, ad, s));  // sets a.ch, a.spc, a.nch
+            if (rc) return rc;
+            return launch_combine(a, rows, s);
+        }
+    }
     if (tc_ok(kb, vb)) {
         tc_chunks(a, (int64_t)a.nch * CH, rows);
         if (a.nch > 0) {
-            rc = kb == 2 ? dispatch_tc<2>(a, vb, ad, s) : dispatch_tc<4>(a, vb, ad, s);
+            rc = tq_count_path(9, kb == 2 ? dispatch_tc<2>(a, vb, ad, s) : dispatch_tc<4>(a, vb, ad, s));
             if (rc) return rc;
         }
     } else if (a.nch > 0) {
@@ -938,10 +863,9 @@ int run(AttnArgs a, int kb, int vb, const Addr& ad, cudaStream_t s) {
             case 4: rc = dispatch_vb<4>(a, vb, ad, s); break;
             default: rc = dispatch_vb<8>(a, vb, ad, s); break;
         }
-        if (rc) return rc;
+        if (tq_count_path(8, rc)) return rc;
     }
-    launch_pdl(tqa_combine, dim3(rows, a.hkv), dim3((a.hq / a.hkv) * D), s, a);
-    return (int)cudaGetLastError();
+    return launch_combine(a, rows, s);
 }
 
 bool bits_ok(int b) { return b == 2 || b == 3 || b == 4 || b == 8; }

@@ -860,10 +860,11 @@ int tq_compress_umma_pair(const TqArgs& k, const TqArgs& v, cudaStream_t s, bool
 
 namespace fb {
 unsigned int tq_dequant_timeouts();
+unsigned int tqa_stream_timeouts();
 }
 
 extern "C" unsigned int fb_tq_timeouts(void) {
     unsigned int v = 0;
     cudaMemcpyFromSymbol(&v, fb::g_tq_umma_timeouts, sizeof(v));
-    return v + fb::tq_dequant_timeouts();
+    return v + fb::tq_dequant_timeouts() + fb::tqa_stream_timeouts();
 }

@@ -133,7 +133,8 @@ def tq_dequant_slots(packed_pool, norms_pool, rotation, centroids, bits, out, sl
 
 
 TQ_PATHS = ("compress_small", "compress_tensor_core", "compress_exact", "dequant_small", "dequant_tensor_core",
-            "dequant_exact", "compress_kv_fused", "dequant_kv_fused")
+            "dequant_exact", "compress_kv_fused", "dequant_kv_fused", "attention_cuda_core", "attention_per_head",
+            "attention_streamed")
 
 
 def tq_path_counts() -> dict:

@@ -205,7 +205,9 @@ int fb_launch_tq_compress_kv_paged(const void* k_input, const void* v_input, int
  * small-call kernel (tq_small.cu), the tensor-core kernel (tq_umma.cu) and the exact CUDA-core
  * kernel (tq_exact.cu); counts[3..5] the same for dequantize; counts[6] = K+V pairs of
  * fb_launch_tq_compress_kv_paged served by one tensor-core launch; counts[7] the same for
- * fb_launch_tq_dequant_kv_paged. Writes min(n, 8) counters. */
+ * fb_launch_tq_dequant_kv_paged; counts[8..10] = paged-attention calls (every TurboQuant attention
+ * entry point) whose main kernel was the CUDA-core one, the per-head tensor-core one and the
+ * streamed tensor-core one. Writes min(n, 11) counters. */
 int fb_tq_path_counts(unsigned long long* counts, int n);
 
 /* Batched append (no reference counterpart; the reference appends one sequence at a time,
@@ -295,9 +297,9 @@ int fb_launch_kv_append_paged(const void* keys, const void* values, int dtype, i
                               int head_dim, const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
                               void* k_pool, void* v_pool, unsigned int* err_count, void* stream);
 
-/* Number of bounded waits that timed out inside the tensor-core TurboQuant kernels (compress and
- * dequantize) since the library was loaded (0 in normal operation; a timeout abandons the launch's
- * remaining tiles). */
+/* Number of bounded waits that timed out inside the tensor-core TurboQuant kernels (compress,
+ * dequantize and the streamed paged attention) since the library was loaded (0 in normal
+ * operation; a timeout abandons the launch's remaining work). */
 unsigned int fb_tq_timeouts(void);
 
 /* Host tables. */

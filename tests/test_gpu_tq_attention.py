@@ -272,3 +272,135 @@ def test_reference_abi_calls_on_two_streams_at_once():
     torch.cuda.synchronize()
     for o, r in zip(outs, ref):
         assert torch.equal(o, r)
+
+
+# ── the streamed tensor-core kernel (pool-backed caches, KV heads a multiple of 8) ──
+
+def _run_counted(path, fn):
+    """fn() and whether exactly one call of it was served by the named attention path."""
+    before = K.tq_path_counts()[path]
+    out = fn()
+    return out, K.tq_path_counts()[path] - before
+
+
+@pytest.mark.parametrize("G,kb,vb,dt", [(4, 4, 2, "f16"), (1, 4, 4, "f16"), (2, 2, 2, "bf16"), (8, 2, 4, "f16"),
+                                        (4, 4, 4, "bf16")])
+def test_streamed_kernel_decode_matches_statement(G, kb, vb, dt):
+    """Eight KV heads (one head group): decode at contexts that end inside a 32-position stage,
+    cross 512-position chunks and take an item to its last stage, for each bit-width pair, group
+    size and query dtype."""
+    kv_lens, Hkv = [300, 777, 1500, 2049], 8
+    c = build_cache(kv_lens, Hkv, kb, vb, seed=100 + 10 * G + kb + vb)
+    qh, q = make_q(len(kv_lens), 1, G * Hkv, dt, seed=101 + G)
+    starts = [L - 1 for L in kv_lens]
+    got, served = _run_counted("attention_streamed", lambda: run_ours(c, q, kv_lens, starts, dt))
+    assert served == 1
+    got = got.float().cpu().numpy()
+    for s, L in enumerate(kv_lens):
+        ops.assert_close_fp(got[s], statement(c, qh[s], s, L, starts[s]), rel=2e-3, min_cos=0.9999,
+                            label=f"seq {s} (kv {L})", dtype=dt)
+
+
+def test_streamed_kernel_prefill_chunk_causal_and_many_items():
+    """40 query tokens per sequence with their own causal ranges (the token of a sequence share
+    a chunk's codes), more items than the persistent grid has CTAs."""
+    kv_lens, Tq, Hkv, G = [60, 600, 1100, 2100], 40, 8, 4
+    c = build_cache(kv_lens, Hkv, 4, 2, seed=110)
+    qh, q = make_q(len(kv_lens), Tq, G * Hkv, "f16", seed=111)
+    starts = [L - Tq for L in kv_lens]
+    got, served = _run_counted("attention_streamed", lambda: run_ours(c, q, kv_lens, starts, "f16"))
+    assert served == 1
+    got = got.float().cpu().numpy()
+    for s, L in enumerate(kv_lens):
+        ops.assert_close_fp(got[s], statement(c, qh[s], s, L, starts[s]), rel=2e-3, min_cos=0.9999,
+                            label=f"seq {s} (kv {L})", dtype="f16")
+
+
+def test_streamed_kernel_missing_blocks_and_empty_sequence():
+    """Negative block-table entries (one in each block slot of a stage, and a first block) leave
+    their positions out; an empty sequence gives zeros."""
+    kv_lens, Hkv, G = [0, 90, 513, 1029], 8, 4
+    c = build_cache(kv_lens, Hkv, 2, 2, seed=120)
+    c["tables"][1, 0] = -1
+    c["tables"][2, 3] = -1
+    c["tables"][3, 10] = -1
+    c["tables"][3, 11] = -1
+    c["tables"][3, 40] = -1
+    qh, q = make_q(len(kv_lens), 1, G * Hkv, "f16", seed=121)
+    starts = [max(L - 1, 0) for L in kv_lens]
+    got, served = _run_counted("attention_streamed", lambda: run_ours(c, q, kv_lens, starts, "f16"))
+    assert served == 1
+    got = got.float().cpu().numpy()
+    assert not np.any(got[0])
+    for s in (1, 2, 3):
+        ops.assert_close_fp(got[s], statement(c, qh[s], s, kv_lens[s], starts[s]), rel=2e-3, min_cos=0.9999,
+                            label=f"seq {s}", dtype="f16")
+
+
+def test_streamed_kernel_pool_ending_inside_a_block():
+    """A pool cut 5 rows into the last block the sequence uses: the kernel's copies read zeros
+    past the pool's end, and the positions there are left out."""
+    kv_len, Hkv, G, kb, vb = 700, 8, 4, 4, 2
+    c = build_cache([kv_len], Hkv, kb, vb, seed=130)
+    table = c["tables"][0]
+    cut = int(table.max()) * 16 + 11
+    qh, q = make_q(1, 1, G * Hkv, "f16", seed=131)
+    pos = np.arange(kv_len)
+    rows = table[pos // 16] * 16 + pos % 16
+    keep = rows < cut
+    assert 0 < (~keep).sum() < kv_len
+    Pk, Pv = D * kb // 8, D * vb // 8
+    n = int(keep.sum())
+    nb = (n + 15) // 16
+    pad = nb * 16 - n
+    kp = np.concatenate([c["kp"].cpu().numpy().reshape(-1, Hkv, Pk)[rows[keep]],
+                         np.zeros((pad, Hkv, Pk), np.uint8)]).reshape(nb * 16, Hkv * Pk)
+    vp = np.concatenate([c["vp"].cpu().numpy().reshape(-1, Hkv, Pv)[rows[keep]],
+                         np.zeros((pad, Hkv, Pv), np.uint8)]).reshape(nb * 16, Hkv * Pv)
+    kn = np.concatenate([c["kn"].float().cpu().numpy()[rows[keep]], np.zeros((pad, Hkv))])
+    vn = np.concatenate([c["vn"].float().cpu().numpy()[rows[keep]], np.zeros((pad, Hkv))])
+    exp = tq.attention_paged_tq(qh[0], kp, kn, vp, vn, np.arange(nb), n, n - 1, c["pik_h"], c["piv_h"], c["ck_h"],
+                                c["cv_h"], kb, vb, Hkv)
+    out = torch.full(q.shape, 7.0, dtype=torch.float16, device=DEV)
+
+    def call():
+        K.tq_attention_paged(q, c["kp"][:cut], c["kn"][:cut], c["vp"][:cut], c["vn"][:cut],
+                             torch.from_numpy(c["tables"]).to(DEV),
+                             torch.tensor([kv_len], dtype=torch.int32, device=DEV),
+                             torch.tensor([kv_len - 1], dtype=torch.int32, device=DEV), c["pik"], c["piv"], c["ck"],
+                             c["cv"], kb, vb, out)
+        torch.cuda.synchronize()
+
+    _, served = _run_counted("attention_streamed", call)
+    assert served == 1
+    ops.assert_close_fp(out[0].float().cpu().numpy(), exp, rel=2e-3, min_cos=0.9999, label="cut pool", dtype="f16")
+
+
+def test_streamed_kernel_two_head_groups():
+    """Sixteen KV heads: two items per (chunk, token), one per group of eight, each reading its
+    half of every pool row."""
+    kv_lens, Tq, Hkv, G = [700, 1300], 3, 16, 2
+    c = build_cache(kv_lens, Hkv, 4, 4, seed=140)
+    qh, q = make_q(len(kv_lens), Tq, G * Hkv, "f16", seed=141)
+    starts = [L - Tq for L in kv_lens]
+    got, served = _run_counted("attention_streamed", lambda: run_ours(c, q, kv_lens, starts, "f16"))
+    assert served == 1
+    got = got.float().cpu().numpy()
+    for s, L in enumerate(kv_lens):
+        ops.assert_close_fp(got[s], statement(c, qh[s], s, L, starts[s]), rel=2e-3, min_cos=0.9999,
+                            label=f"seq {s} (kv {L})", dtype="f16")
+
+
+def test_short_contexts_stream_and_few_kv_heads_keep_the_per_head_kernel():
+    """Contexts of at most 256 positions (one chunk) take the streamed kernel with 8 KV heads;
+    KV-head counts that are not a multiple of 8 take the per-head tensor-core kernel."""
+    for kv_lens, Hkv, path in (([200, 256, 17], 8, "attention_streamed"), ([900], 2, "attention_per_head")):
+        c = build_cache(kv_lens, Hkv, 4, 2, seed=150 + Hkv)
+        qh, q = make_q(len(kv_lens), 1, 4 * Hkv, "f16", seed=151)
+        starts = [L - 1 for L in kv_lens]
+        got, served = _run_counted(path, lambda: run_ours(c, q, kv_lens, starts, "f16"))
+        assert served == 1
+        got = got.float().cpu().numpy()
+        for s, L in enumerate(kv_lens):
+            ops.assert_close_fp(got[s], statement(c, qh[s], s, L, starts[s]), rel=2e-3, min_cos=0.9999,
+                                label=f"Hkv {Hkv} seq {s}", dtype="f16")
