@@ -8,8 +8,8 @@
 // Pi_v^T acc. Here, with the centroid values read as fp16 (2^-11 relative) and everything else
 // in float32:
 //
-//   tqa_rotate_q    q_rot = Pi_k q for every query token and Q head (thread i: row i of Pi_k
-//                   for all heads of a KV group), into the workspace
+//   tqa_rotate_q    q_rot = Pi_k q for every query token and Q head (a CTA per up to four
+//                   query tokens and KV group, Pi_k staged by TMA), into the workspace
 //   tqa_chunk       one CTA per (256-position chunk, KV head, query token): thread p scores
 //                   position p for all Q heads of the group from the position's packed K
 //                   row (pair-of-codes lookup tables, lane-private), the CTA takes the
@@ -18,8 +18,9 @@
 //                   group) from the V rows staged in shared memory; the chunk's (max, sum,
 //                   acc) go to the workspace (split-K over the causal range)
 //   tqa_combine     rescales and sums the chunks of each query token and head, divides by
-//                   the softmax sum and rotates back with Pi_v^T (thread (h, i): output i of
-//                   head h, column i of Pi_v shared by the group's heads through L1)
+//                   the softmax sum and rotates back with Pi_v^T (a CTA per up to four query
+//                   tokens and KV group, Pi_v staged by one bulk copy; thread (h, i): output i
+//                   of head h)
 //
 // With 2- or 4-bit keys and values, tqa_mma (tensor cores, below) replaces tqa_chunk: same
 // split-K partials, chunks of 512 to 2048 positions. 3- and 8-bit codes take tqa_chunk.
@@ -31,6 +32,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -41,6 +43,9 @@
 
 namespace fb {
 
+// Bounded waits of the rotate and combine kernels' staging copies that ran out (fb_tq_timeouts).
+__device__ unsigned int g_tqa_timeouts = 0;
+
 // tq_api.cu: counts a served call of path `which` when rc is 0 (fb_tq_path_counts); returns rc.
 int tq_count_path(int which, int rc);
 
@@ -50,50 +55,115 @@ __device__ __forceinline__ float load_q(const AttnArgs& a, int64_t i) {
     return a.dtype == FB_BF16 ? __bfloat162float(((const __nv_bfloat16*)a.q)[i]) : __half2float(((const __half*)a.q)[i]);
 }
 
-// q_rot[row][h][i] = sum_j Pi_k[i][j] q[row][h][j] for the heads of KV group blockIdx.y: thread i
-// reads row i of Pi_k (through L1, 16 bytes at a time, eight loads in flight) once for all the
-// group's heads, whose queries are broadcast from shared memory.
-__global__ void __launch_bounds__(D) tqa_rotate_q(AttnArgs a) {
-    pdl_begin();
-    __shared__ float4 qs[MAXG][D / 4];
-    const int row = blockIdx.x, g = blockIdx.y, G = a.hq / a.hkv, i = threadIdx.x;
-    for (int e = threadIdx.x; e < G * D; e += D)
-        ((float*)qs)[e] = load_q(a, ((int64_t)row * a.hq + g * G) * D + e);
+constexpr int RQ = 4;  // query rows per rotate / combine CTA
+
+// Bounded wait for a one-shot staging barrier (phase 0); a wait that runs out is counted.
+__device__ __forceinline__ bool stage_wait(uint64_t* bar) {
+    const long long t0 = clock64();
+    while (!sm100::mbar_try_wait(bar, 0))
+        if (clock64() - t0 > 4000000000LL) {
+            atomicAdd(&g_tqa_timeouts, 1u);
+            return false;
+        }
+    return true;
+}
+
+struct RotateParams {
+    CUtensorMap pimap;  // Pi_k: f32 [128][128], box 32 columns x 128 rows, 128-byte swizzle
+    AttnArgs a;
+    int rows;
+};
+
+// Query rows per rotate / combine CTA: RQ when that still gives a CTA to every SM, else fewer.
+inline int rows_per_cta(int rows, int hkv) {
+    int rq = RQ;
+    while (rq > 1 && (int64_t)((rows + rq - 1) / rq) * hkv < num_sms()) rq /= 2;
+    return rq;
+}
+
+// q_rot[row][h][i] = sum_j Pi_k[i][j] q[row][h][j] for NR query rows and the G heads of KV group
+// blockIdx.y. Pi_k arrives by four TMA boxes of 32 columns with the 128-byte swizzle, so thread i
+// reads its row 16 bytes at a time without bank conflicts while every thread reads the same query
+// words (broadcast); thread i computes coordinate i of all NR * G vectors.
+template <int G, int NR>
+__global__ void __launch_bounds__(D) tqa_rotate_q(const __grid_constant__ RotateParams R) {
+    extern __shared__ uint8_t rsm_raw[];
+    uint8_t* rsm = rsm_raw + ((1024u - (smem_addr(rsm_raw) & 1023u)) & 1023u);
+    float* pis = (float*)rsm;               // 4 x [128 rows][32 columns], swizzled
+    float* qs = (float*)(rsm + D * D * 4);  // [NR * G][D]
+    uint64_t* bar = (uint64_t*)(qs + NR * G * D);
+    const AttnArgs& a = R.a;
+    const int r0 = blockIdx.x * NR, g = blockIdx.y, i = threadIdx.x;
+    const int nr = min(NR, R.rows - r0);
+    if (i == 0) {
+        sm100::mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
     __syncthreads();
-    float acc[MAXG];
+    pdl_begin();
+    if (i == 0) {
+        sm100::mbar_expect_tx(bar, D * D * 4);
+        for (int c = 0; c < 4; ++c) sm100::tma_load_2d(pis + c * 32 * D, &R.pimap, bar, 32 * c, 0);
+    }
+    for (int e = i; e < NR * G * D; e += D) {
+        const int rr = e / (G * D);
+        qs[e] = rr < nr ? load_q(a, ((int64_t)(r0 + rr) * a.hq + g * G) * D + (e - rr * G * D)) : 0.0f;
+    }
+    __syncthreads();
+    if (!stage_wait(bar)) return;
+    float acc[NR * G];
 #pragma unroll
-    for (int h = 0; h < MAXG; ++h) acc[h] = 0.0f;
-    const float4* prow = (const float4*)(a.pik + (int64_t)i * D);
-#pragma unroll 1
-    for (int j0 = 0; j0 < D / 4; j0 += 8) {
-        float4 p[8];
+    for (int v = 0; v < NR * G; ++v) acc[v] = 0.0f;
+#pragma unroll 2
+    for (int m = 0; m < D / 4; ++m) {  // columns 4m .. 4m + 3
+        const float4 p = *(const float4*)(pis + (m >> 3) * 32 * D + i * 32 + (((m & 7) ^ (i & 7)) << 2));
 #pragma unroll
-        for (int k = 0; k < 8; ++k) p[k] = __ldg(prow + j0 + k);
-#pragma unroll
-        for (int h = 0; h < MAXG; ++h) {
-            if (h >= G) break;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float4 x = qs[h][j0 + k];
-                acc[h] = fmaf(p[k].x, x.x, acc[h]);
-                acc[h] = fmaf(p[k].y, x.y, acc[h]);
-                acc[h] = fmaf(p[k].z, x.z, acc[h]);
-                acc[h] = fmaf(p[k].w, x.w, acc[h]);
-            }
+        for (int v = 0; v < NR * G; ++v) {
+            const float4 x = *(const float4*)(qs + v * D + 4 * m);
+            acc[v] = fmaf(p.x, x.x, acc[v]);
+            acc[v] = fmaf(p.y, x.y, acc[v]);
+            acc[v] = fmaf(p.z, x.z, acc[v]);
+            acc[v] = fmaf(p.w, x.w, acc[v]);
         }
     }
 #pragma unroll
-    for (int h = 0; h < MAXG; ++h) {
-        if (h >= G) break;
-        const int64_t o = ((int64_t)row * a.hq + g * G + h) * D + i;
-        if (a.qrot_f16) ((__half*)a.qrot)[o] = __float2half_rn(acc[h]);
-        else a.qrot[o] = acc[h];
+    for (int v = 0; v < NR * G; ++v) {
+        const int rr = v / G;
+        if (rr < nr) {
+            const int64_t o = ((int64_t)(r0 + rr) * a.hq + g * G + (v - rr * G)) * D + i;
+            if (a.qrot_f16) ((__half*)a.qrot)[o] = __float2half_rn(acc[v]);
+            else a.qrot[o] = acc[v];
+        }
     }
 }
 
-// One launch of tqa_rotate_q for the call's rows.
+// One launch of tqa_rotate_q for the call's rows (Pi_k 16-byte aligned, as every entry point checks).
 inline int launch_rotate(const AttnArgs& a, int rows, cudaStream_t s) {
-    launch_pdl(tqa_rotate_q, dim3(rows, a.hkv), dim3(D), s, a);
+    auto encode = sm100::tensor_map_encoder();
+    if (!encode) return (int)cudaErrorNotSupported;
+    RotateParams R;
+    memset(&R, 0, sizeof R);
+    const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)D};
+    const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+    const cuuint32_t box[2] = {32, (cuuint32_t)D};
+    const cuuint32_t estr[2] = {1, 1};
+    if (encode(&R.pimap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(a.pik), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return (int)cudaErrorInvalidValue;
+    R.a = a;
+    R.rows = rows;
+    const int G = a.hq / a.hkv, rq = rows_per_cta(rows, a.hkv);
+    const size_t smem = 1024 + (size_t)D * D * 4 + (size_t)rq * G * D * 4 + 16;
+    using Kern = void (*)(RotateParams);
+    static const Kern kerns[4][3] = {{tqa_rotate_q<1, 1>, tqa_rotate_q<1, 2>, tqa_rotate_q<1, 4>},
+                                     {tqa_rotate_q<2, 1>, tqa_rotate_q<2, 2>, tqa_rotate_q<2, 4>},
+                                     {tqa_rotate_q<4, 1>, tqa_rotate_q<4, 2>, tqa_rotate_q<4, 4>},
+                                     {tqa_rotate_q<8, 1>, tqa_rotate_q<8, 2>, tqa_rotate_q<8, 4>}};
+    const Kern kern = kerns[G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3][rq == 1 ? 0 : rq == 2 ? 1 : 2];
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    launch_pdl_smem(kern, dim3((rows + rq - 1) / rq, a.hkv), dim3(D), smem, s, R);
     return (int)cudaGetLastError();
 }
 
@@ -365,51 +435,95 @@ __global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
     }
 }
 
-// out[row][h][i] = sum_j Pi_v[j][i] * (sum_c acc_c[j] e^(m_c - M)) / (sum_c l_c e^(m_c - M)):
-// thread (h, i), 128 per head of KV group blockIdx.y.
-__global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a) {
-    pdl_begin();
-    __shared__ float accs[MAXG][D];
-    const int row = blockIdx.x, g = blockIdx.y, G = a.hq / a.hkv;
-    const int h = threadIdx.x / D, i = threadIdx.x - h * D;
-    const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
-    const int L = causal_len(a, s, t);
-    const int nc = min((L + a.ch - 1) / a.ch * a.spc, a.nch);  // kv_lens past max_kv_len: the chunks computed
-    {
-        const float* ph = a.part + ((int64_t)row * a.hq + g * G + h) * a.nch * PART;
-        float M = -INFINITY;
-#pragma unroll 8
-        for (int c = 0; c < nc; ++c) M = fmaxf(M, ph[c * PART]);
-        float l = 0.0f, v = 0.0f;
-        if (M > -INFINITY) {
-#pragma unroll 4
-            for (int c = 0; c < nc; ++c) {
-                const float m = ph[c * PART];
-                if (m == -INFINITY) continue;
-                const float f = expf(m - M);
-                l = fmaf(ph[c * PART + 1], f, l);
-                v = fmaf(ph[c * PART + 2 + i], f, v);
-            }
-        }
-        accs[h][i] = l > 0.0f ? v / l : 0.0f;
+// out[row][h][i] = sum_j Pi_v[j][i] * (sum_c acc_c[j] e^(m_c - M)) / (sum_c l_c e^(m_c - M)) for rq
+// query rows: thread (h, i) of KV group blockIdx.y sums the chunks of output i of head h in one
+// pass (the running maximum rescales what it has summed when it grows), eight chunks' loads in
+// flight at a time, while one bulk copy brings Pi_v into shared memory; the rotation back reads
+// column i of Pi_v (consecutive words across threads) once for the CTA's rows.
+__global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a, int rows, int rq) {
+    extern __shared__ __align__(16) float csm[];
+    float* pvs = csm;           // [D][D]
+    float* accs = csm + D * D;  // [RQ][G][D]
+    const int G = a.hq / a.hkv;
+    uint64_t* bar = (uint64_t*)(accs + RQ * G * D);
+    const int r0 = blockIdx.x * rq, g = blockIdx.y, tid = threadIdx.x;
+    const int h = tid / D, i = tid - h * D;
+    const int nr = min(rq, rows - r0);
+    const bool bulk = ((uintptr_t)a.piv & 15) == 0;
+    if (tid == 0) {
+        sm100::mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    float o = 0.0f;
-    for (int j0 = 0; j0 < D; j0 += 16) {  // sixteen loads of column i in flight at a time
-        float p[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) p[k] = __ldg(a.piv + (j0 + k) * D + i);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) o = fmaf(p[k], accs[h][j0 + k], o);
+    pdl_begin();
+    if (bulk) {
+        if (tid == 0) {
+            sm100::mbar_expect_tx(bar, D * D * 4);
+            sm100::bulk_load(pvs, a.piv, D * D * 4, bar);
+        }
+    } else {
+        for (int e = tid; e < D * D; e += G * D) pvs[e] = __ldg(a.piv + e);
     }
-    const int64_t e = ((int64_t)row * a.hq + g * G + h) * D + i;
-    if (a.dtype == FB_BF16) ((__nv_bfloat16*)a.out)[e] = __float2bfloat16_rn(o);
-    else ((__half*)a.out)[e] = __float2half_rn(o);
+    for (int rr = 0; rr < nr; ++rr) {
+        const int row = r0 + rr;
+        const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
+        const int L = causal_len(a, s, t);
+        const int nc = min((L + a.ch - 1) / a.ch * a.spc, a.nch);  // kv_lens past max_kv_len: the chunks computed
+        const float* ph = a.part + ((int64_t)row * a.hq + g * G + h) * a.nch * PART;
+        float M = -INFINITY, l = 0.0f, v = 0.0f;
+        for (int c0 = 0; c0 < nc; c0 += 8) {
+            float m8[8], l8[8], v8[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int c = c0 + k;
+                m8[k] = c < nc ? ph[c * PART] : -INFINITY;
+                l8[k] = c < nc ? ph[c * PART + 1] : 0.0f;
+                v8[k] = c < nc ? ph[c * PART + 2 + i] : 0.0f;
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                if (m8[k] == -INFINITY) continue;
+                if (m8[k] > M) {
+                    const float sc = expf(M - m8[k]);
+                    l *= sc;
+                    v *= sc;
+                    M = m8[k];
+                }
+                const float f = expf(m8[k] - M);
+                l = fmaf(l8[k], f, l);
+                v = fmaf(v8[k], f, v);
+            }
+        }
+        accs[(rr * G + h) * D + i] = l > 0.0f ? v / l : 0.0f;
+    }
+    __syncthreads();
+    if (bulk && !stage_wait(bar)) return;
+    float o[RQ];
+#pragma unroll
+    for (int rr = 0; rr < RQ; ++rr) o[rr] = 0.0f;
+#pragma unroll 4
+    for (int j = 0; j < D; ++j) {
+        const float p = pvs[j * D + i];
+#pragma unroll
+        for (int rr = 0; rr < RQ; ++rr) o[rr] = fmaf(p, accs[(rr * G + h) * D + j], o[rr]);
+    }
+#pragma unroll
+    for (int rr = 0; rr < RQ; ++rr) {
+        if (rr >= nr) break;
+        const int64_t e = ((int64_t)(r0 + rr) * a.hq + g * G + h) * D + i;
+        if (a.dtype == FB_BF16) ((__nv_bfloat16*)a.out)[e] = __float2bfloat16_rn(o[rr]);
+        else ((__half*)a.out)[e] = __float2half_rn(o[rr]);
+    }
 }
 
 // One launch of tqa_combine for the call's rows.
 inline int launch_combine(const AttnArgs& a, int rows, cudaStream_t s) {
-    launch_pdl(tqa_combine, dim3(rows, a.hkv), dim3((a.hq / a.hkv) * D), s, a);
+    const int G = a.hq / a.hkv;
+    const size_t smem = (size_t)D * D * 4 + (size_t)RQ * G * D * 4 + 16;
+    cudaError_t e = cudaFuncSetAttribute(tqa_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    const int rq = rows_per_cta(rows, a.hkv);
+    launch_pdl_smem(tqa_combine, dim3((rows + rq - 1) / rq, a.hkv), dim3(G * D), smem, s, a, rows, rq);
     return (int)cudaGetLastError();
 }
 
@@ -1139,3 +1253,11 @@ extern "C" int launch_attention_paged_tq_noalloc(void* output, const void* q, co
                        k_rotation, v_rotation, k_centroids, v_centroids, num_tokens, num_q_heads, num_kv_heads, kv_len,
                        start_pos, key_bits, value_bits, stream);
 }
+
+namespace fb {
+unsigned int tqa_timeouts() {
+    unsigned int v = 0;
+    cudaMemcpyFromSymbol(&v, g_tqa_timeouts, sizeof(v));
+    return v;
+}
+}  // namespace fb

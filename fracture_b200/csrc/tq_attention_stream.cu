@@ -628,22 +628,9 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
 
 // ── host side ──
 
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
-    });
-    return fn;
-}
-
 // Norms: f16 [rows, hkv], box of HC heads x 16 rows.
 static bool encode_norms(CUtensorMap* map, const void* base, uint64_t hkv, uint64_t rows) {
-    auto encode = get_encode();
+    auto encode = sm100::tensor_map_encoder();
     if (!encode) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)hkv, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)(hkv * 2)};
@@ -657,7 +644,7 @@ static bool encode_norms(CUtensorMap* map, const void* base, uint64_t hkv, uint6
 // Codes: uint8 [rows, hkv * P] seen as [rows][hkv * P / 128 lines][128 bytes]; box of `lines`
 // lines (one head group) x 16 rows, 128-byte swizzle.
 static bool encode_codes(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t lines) {
-    auto encode = get_encode();
+    auto encode = sm100::tensor_map_encoder();
     if (!encode) return false;
     const cuuint64_t dims[3] = {128, (cuuint64_t)(row_bytes / 128), (cuuint64_t)rows};
     const cuuint64_t strides[2] = {128, (cuuint64_t)row_bytes};

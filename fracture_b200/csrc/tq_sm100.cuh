@@ -3,11 +3,28 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 namespace fb {
 namespace sm100 {
+
+// cuTensorMapEncodeTiled from the driver, looked up once (null if the driver lacks it).
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    });
+    return fn;
+}
 
 constexpr int D = 128;                      // head_dim of the tensor-core kernels
 constexpr int TILE = 128;                   // vectors per tile (MMA M)

@@ -739,19 +739,6 @@ __global__ void __maxnreg__(MAX_REGS)
 
 // ── host side ───────────────────────────────────────────────────────────────
 
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
-    });
-    return fn;
-}
-
 static bool device_is_sm100() {
     int dev = 0, major = 0, minor = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return false;
@@ -761,7 +748,7 @@ static bool device_is_sm100() {
 }
 
 static bool encode_input_map(CUtensorMap* map, const TqArgs& a, bool bf16) {
-    auto encode = get_encode();
+    auto encode = sm100::tensor_map_encoder();
     if (!encode) return false;
     const int64_t nvec = a.num_tokens * a.num_heads;
     const cuuint64_t dims[2] = {(cuuint64_t)umma::D, (cuuint64_t)nvec};
@@ -861,10 +848,11 @@ int tq_compress_umma_pair(const TqArgs& k, const TqArgs& v, cudaStream_t s, bool
 namespace fb {
 unsigned int tq_dequant_timeouts();
 unsigned int tqa_stream_timeouts();
+unsigned int tqa_timeouts();
 }
 
 extern "C" unsigned int fb_tq_timeouts(void) {
     unsigned int v = 0;
     cudaMemcpyFromSymbol(&v, fb::g_tq_umma_timeouts, sizeof(v));
-    return v + fb::tq_dequant_timeouts() + fb::tqa_stream_timeouts();
+    return v + fb::tq_dequant_timeouts() + fb::tqa_stream_timeouts() + fb::tqa_timeouts();
 }

@@ -297,9 +297,10 @@ int fb_launch_kv_append_paged(const void* keys, const void* values, int dtype, i
                               int head_dim, const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
                               void* k_pool, void* v_pool, unsigned int* err_count, void* stream);
 
-/* Number of bounded waits that timed out inside the tensor-core TurboQuant kernels (compress,
- * dequantize and the streamed paged attention) since the library was loaded (0 in normal
- * operation; a timeout abandons the launch's remaining work). */
+/* Number of bounded waits that timed out inside the TurboQuant kernels that stage data
+ * asynchronously (tensor-core compress and dequantize; paged attention's rotate, streamed and
+ * combine kernels) since the library was loaded (0 in normal operation; a timeout abandons the
+ * launch's remaining work). */
 unsigned int fb_tq_timeouts(void);
 
 /* Host tables. */
