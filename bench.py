@@ -814,7 +814,7 @@ def run_tq_attention(args, local_rank: int) -> dict:
     pk = peaks()
     return {"workload": "TurboQuant paged attention (decode): 64 sequences x 1 query token, context 8192, "
                         "32 Q / 8 KV heads x 128, K 4-bit / V 2-bit, FP16 queries and output",
-            "kernels": "tqa_rotate_q + tqa_mma (persistent CTAs, split-K over 2048-position items at this shape, mma.sync m16n8k16 on FP16 operands decoded in registers, FP32 accumulators) + tqa_combine",
+            "kernels": "tqa_rotate_q + tqa_stream (persistent CTAs; 4 producer warps feed a ring of stages by TMA, two 16-position blocks x 8 KV heads per stage; 8 consumer warps decode codes through 64 KB-aligned lane-private tables into mma.sync m16n8k16 FP16 operands, FP32 accumulators; split-K over 512-position items at this shape) + tqa_combine",
             "ms_per_step": round(ms, 4), "query_tokens_per_s": round(S / (ms / 1e3), 1),
             "kv_positions_per_s": round(S * L / (ms / 1e3), 1), "algorithmic_bytes_per_step": by,
             "achieved_gbs": round(gbs, 1), "frac_of_peak": round(gbs / pk["hbm_gbs"], 4),

@@ -1,7 +1,7 @@
-// Streamed tensor-core attention over the TurboQuant paged cache (2- and 4-bit codes), sm_100a.
+// Streamed tensor-core attention over the TurboQuant paged cache (2-, 4- and 8-bit codes), sm_100a.
 //
-// Replaces the per-head items of tqa_mma for caches in this library's contiguous pools with a
-// KV-head count that is a multiple of 8. The math is the same split-K statement
+// Replaces tqa_mma (2- and 4-bit codes) and tqa_chunk (8-bit codes) for caches in this library's
+// contiguous pools with a KV-head count that is a multiple of 8. The math is the same split-K statement
 // (attention_paged_tq.cu:12-17 of the reference: scores in K's rotated space, softmax, values
 // summed in V's rotated space; tqa_combine adds the partials and rotates back), the operands
 // decoded the same way (lane-private lookup tables feeding mma.sync m16n8k16 with FP16
@@ -11,13 +11,14 @@
 //     of a block hold all KV heads of a position side by side, so one block's K codes for the
 //     group are one rectangle of the pool, fetched with one TMA box; the V codes likewise; the
 //     norms of a block are one contiguous run (one bulk copy) when the pool holds 8 KV heads,
-//     else a TMA box. A stage holds two blocks; the ring of stages runs ahead across items.
-//   * Four producer warps issue a stage's copies in parallel (block slot 0 / 1 x K / V side:
+//     else a TMA box. A stage holds two blocks (one with 8-bit codes); the ring of stages runs
+//     ahead across items.
+//   * Two producer warps per block slot issue a stage's copies in parallel (K side / V side:
 //     the issue of one copy takes long enough that one thread would not keep up), each first
 //     planning the item's blocks from the block table (32 entries per load, the next item's
 //     entries requested before this item's copies).
-//   * Eight consumer warps: warp w takes KV head w of the group in both tiles of every stage
-//     (its two tiles are independent work for the scheduler), keeps a running softmax for the
+//   * Eight consumer warps: warp w takes KV head w of the group in every tile of a stage (two
+//     tiles are independent work for the scheduler), keeps a running softmax for the
 //     head's Q heads over the item, and writes one partial (maximum, sum, accumulator). The
 //     item's rotated queries are loaded into registers one item ahead.
 //   * A block's codes land as [16 rows][128-byte lines] with the 128-byte swizzle, and the value
@@ -27,7 +28,7 @@
 //   * The decoding tables sit at shared address 0x10000 (64 KB aligned): one byte permute of a
 //     code byte and the lane's copy offset is the whole lookup address. 2-bit codes decode four
 //     at a time (one 8-byte lookup, 16 lane copies), 4-bit codes two at a time (one 4-byte
-//     lookup, 32 copies). Scores carry log2(e) so the softmax uses exp2; the partial's maximum
+//     lookup, 32 copies), 8-bit codes one at a time (two lookups and a byte permute per register). Scores carry log2(e) so the softmax uses exp2; the partial's maximum
 //     is converted back to natural units.
 //
 // Every wait is bounded: a wait that runs out counts itself in g_tqa_stream_timeouts, raises the
@@ -55,17 +56,23 @@ namespace stream {
 using namespace sm100;
 
 constexpr int HC = 8;                    // KV heads per item
-constexpr int BPS = 2;                   // 16-position blocks per stage
-constexpr int NCW = 8;                   // consumer warps: warp w takes KV head w, both blocks
-constexpr int NPW = 4;                   // producer warps: block slot p & 1, side p >> 1 (K / V)
-constexpr int THREADS = (NCW + NPW) * 32;
+constexpr int NCW = 8;                   // consumer warps: warp w takes KV head w in every block of a stage
 constexpr int MAX_NST = 8;
+constexpr int MAX_SPI = 128;             // stages per item (2048 positions at one block per stage)
 constexpr uint32_t TAB = 0x10000;        // shared address of the decoding tables (64 KB)
 constexpr uint32_t DYN_BYTES = 232448;   // dynamic shared memory requested (the sm_100 maximum)
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
+// A stage holds BPS 16-position blocks: two, or one when a side has 8-bit codes (its blocks are
+// 16 KB). Producer warp p copies block slot p % BPS, side p / BPS (0: K codes and norms, 1: V).
+// 8-bit codes sit line-major ([lines][16 rows][128]) so that the 128-byte swizzle phase follows
+// the row; 2- and 4-bit codes row-major ([16 rows][lines][128]).
 template <int KB, int VB>
 struct Layout {
+    static constexpr bool K8 = KB == 8, V8 = VB == 8;
+    static constexpr int BPS = K8 || V8 ? 1 : 2;
+    static constexpr int NPW = 2 * BPS;
+    static constexpr int THREADS = (NCW + NPW) * 32;
     static constexpr int PK = D * KB / 8, PV = D * VB / 8;
     static constexpr int KBOX = HC * PK / 128, VBOX = HC * PV / 128;  // 128-byte lines per block row
     static constexpr int k_off = 0;
@@ -78,17 +85,19 @@ struct Layout {
 
 // Shared memory other than the tables and stages: barriers, the producers' plans, the
 // consumers' weight tiles.
+template <int BPS>
 struct Small {
-    static constexpr int bar_off = 0;                      // full[MAX_NST], empty[MAX_NST], abort flag
-    static constexpr int plan_off = 256;                   // [NPW][64] int2
-    static constexpr int p_off = plan_off + NPW * 64 * 8;  // [NCW][BPS][16 x 8] f16
+    static constexpr int NPW = 2 * BPS;
+    static constexpr int bar_off = 0;                           // full[MAX_NST], empty[MAX_NST], abort flag
+    static constexpr int plan_off = 256;                        // [NPW][MAX_SPI] int2
+    static constexpr int p_off = plan_off + NPW * MAX_SPI * 8;  // [NCW][BPS][16 x 8] f16
     static constexpr int bytes = (p_off + NCW * BPS * 256 + 1023) / 1024 * 1024;
 };
 
 struct Params {
     CUtensorMap kmap, vmap, knmap, vnmap;  // codes: uint8 [pool_rows][hkv * P / 128][128]; norms: f16 [pool_rows, hkv]
     AttnArgs a;
-    int items, spi;                // spi: stages per item (ch = spi * BPS * 16)
+    int items, spi;                // spi: stages per item (ch = spi * blocks per stage * 16)
     int nchi, ng;                  // chunks per sequence, KV-head groups
     DivU32 dng, dqps, dnchi;
     int64_t pool_rows;
@@ -191,6 +200,7 @@ __device__ __forceinline__ uint32_t tab_addr(uint32_t w, uint32_t off, int b) {
 struct Item {
     int s, c, t, hg, row, L, p0, nstg;
 };
+template <int BPS>
 __device__ __forceinline__ Item decode_item(const Params& P, int item) {
     Item it;
     const uint32_t r1 = divu32((uint32_t)item, P.dng);
@@ -215,11 +225,12 @@ struct Places {
     int n_lo, nst;
     __device__ uint32_t stage(int i, int sb) const { return i < n_lo ? lo + i * sb : hi + (i - n_lo) * sb; }
 };
+template <int BPS>
 __device__ __forceinline__ Places places(uint32_t base, int sb) {
     Places pl;
     pl.lo = (base + 1023u) & ~1023u;
     pl.hi = TAB + 0x10000u;
-    pl.small = ((base + DYN_BYTES) & ~1023u) - Small::bytes;
+    pl.small = ((base + DYN_BYTES) & ~1023u) - Small<BPS>::bytes;
     pl.n_lo = pl.lo + sb <= TAB ? (int)((TAB - pl.lo) / sb) : 0;
     const int n_hi = pl.small >= pl.hi + sb ? (int)((pl.small - pl.hi) / sb) : 0;
     pl.nst = min(MAX_NST, pl.n_lo + n_hi);
@@ -227,13 +238,15 @@ __device__ __forceinline__ Places places(uint32_t base, int sb) {
 }
 
 template <int KB, int VB>
-__global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(Layout<KB, VB>::THREADS, 1) tqa_stream(const __grid_constant__ Params P) {
     using Ly = Layout<KB, VB>;
     constexpr int PK = Ly::PK, PV = Ly::PV;
     constexpr int SB = Ly::stage_bytes;
+    constexpr int BPS = Ly::BPS, NPW = Ly::NPW, THREADS = Ly::THREADS;
+    using Sm = Small<BPS>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base = smem_u32(smem_raw);
-    const Places pl = places(base, SB);
+    const Places pl = places<BPS>(base, SB);
     const AttnArgs& a = P.a;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = a.hq / a.hkv;
@@ -244,7 +257,7 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
         return;
     }
     uint8_t* gsmall = smem_raw + (pl.small - base);  // generic pointer to the small region
-    uint64_t* full = (uint64_t*)(gsmall + Small::bar_off);
+    uint64_t* full = (uint64_t*)(gsmall + Sm::bar_off);
     uint64_t* empty = full + MAX_NST;
     volatile int* abort = (volatile int*)(empty + MAX_NST);
 
@@ -257,10 +270,10 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     // Decoding tables (codes MSB first: the first code of a byte is its high bits). Entry e at
-    // TAB + 256e. K part (+0): 4-bit, 32 copies of half2(c[e >> 4], c[e & 15]); 2-bit, 16 copies
-    // of half2(c[e >> 6], c[(e >> 4) & 3]), half2(c[(e >> 2) & 3], c[e & 3]) (four coordinates of
-    // one row). V part (+128): 4-bit as for K (the two codes are one coordinate at two
-    // positions); 2-bit, 16 copies of half2(c[e >> 6], c[(e >> 2) & 3]), half2(c[(e >> 4) & 3],
+    // TAB + 256e. K part (+0): 8-bit, 32 copies of half2(c[e], c[e]); 4-bit, 32 copies of
+    // half2(c[e >> 4], c[e & 15]); 2-bit, 16 copies of half2(c[e >> 6], c[(e >> 4) & 3]),
+    // half2(c[(e >> 2) & 3], c[e & 3]) (four coordinates of one row). V part (+128): 8-bit and
+    // 4-bit as for K (a 4-bit pair is one coordinate at two positions); 2-bit, 16 copies of half2(c[e >> 6], c[(e >> 2) & 3]), half2(c[(e >> 4) & 3],
     // c[e & 3]) (two coordinates, each at two positions; the index interleaves two positions'
     // code bytes).
     for (int j = threadIdx.x; j < 512; j += THREADS) {
@@ -269,7 +282,10 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
         const int bits = key ? KB : VB;
         const float* cen = key ? a.ck : a.cv;
         uint4 v;
-        if (bits == 4) {
+        if (bits == 8) {  // one code: half2(c[e], c[e])
+            const uint32_t w = pack_half2(__ldg(cen + e), __ldg(cen + e));
+            v = make_uint4(w, w, w, w);
+        } else if (bits == 4) {
             const uint32_t w = pack_half2(__ldg(cen + (e >> 4)), __ldg(cen + (e & 15)));
             v = make_uint4(w, w, w, w);
         } else if (key) {
@@ -290,39 +306,42 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
     __syncthreads();
 
     if (warp >= NCW) {
-        // ── producers: warp NCW + p copies block slot p & 1, side p >> 1 (0: K codes and norms,
+        // ── producers: warp NCW + p copies block slot p % BPS, side p / BPS (0: K codes and norms,
         // 1: V codes and norms) of every stage ──
-        const int p = warp - NCW, slot = p & 1, side = p >> 1;
-        int2* plan = (int2*)(gsmall + Small::plan_off) + p * 64;  // per stage: (pool row, valid rows)
+        const int p = warp - NCW, slot = p % BPS, side = p / BPS;
+        int2* plan = (int2*)(gsmall + Sm::plan_off) + p * MAX_SPI;  // per stage: (pool row, valid rows)
         int sidx = 0;
         uint32_t sph = 0;
         long long issued = 0;
         bool ok = true;
-        // block-table entries of an item for this slot: lane l holds stages l and l + 32
-        auto fetch = [&](int item, int32_t (&bt)[2]) {
+        // block-table entries of an item for this slot: lane l holds stages l, l + 32, ...
+        constexpr int NBT = MAX_SPI / BPS / 32;
+        auto fetch = [&](int item, int32_t (&bt)[NBT]) {
             Item it{};
-            if (item < P.items) it = decode_item(P, item);
+            if (item < P.items) it = decode_item<BPS>(P, item);
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int st = lane + 32 * i, b = (it.p0 >> 4) + 2 * st + slot;
+            for (int i = 0; i < NBT; ++i) {
+                const int st = lane + 32 * i, b = (it.p0 >> 4) + BPS * st + slot;
                 bt[i] = it.nstg > 0 && st < it.nstg && b < a.max_blocks
                             ? __ldg(a.block_tables + (int64_t)it.s * a.max_blocks + b)
                             : -1;
             }
         };
-        int32_t bt_next[2];
+        int32_t bt_next[NBT];
         fetch(blockIdx.x, bt_next);
         for (int item = blockIdx.x; item < P.items && ok; item += gridDim.x) {
-            const int32_t bt0 = bt_next[0], bt1 = bt_next[1];
-            const Item it = decode_item(P, item);
+            int32_t bt[NBT];
+#pragma unroll
+            for (int i = 0; i < NBT; ++i) bt[i] = bt_next[i];
+            const Item it = decode_item<BPS>(P, item);
             fetch(item + gridDim.x, bt_next);
             if (it.nstg == 0) continue;
             // valid rows of each block from row 0: causal range, missing blocks, pool end
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
+            for (int i = 0; i < NBT; ++i) {
                 const int st = lane + 32 * i;
-                const int32_t blk = i ? bt1 : bt0;
-                const int pos = it.p0 + (2 * st + slot) * 16;
+                const int32_t blk = bt[i];
+                const int pos = it.p0 + (BPS * st + slot) * 16;
                 const int64_t first = (int64_t)blk * 16;
                 int n = 0;
                 if (blk >= 0 && pos < it.L && first < P.pool_rows)
@@ -345,12 +364,16 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
                     mbar_expect_tx(&full[sidx], tx);
                     if (pn.y > 0) {
                         const uint32_t nd = stg + (side ? Ly::vn_off : Ly::kn_off) + slot * 16 * HC * 2;
-                        if (side == 0)
+                        // row-major maps take (line, row), line-major ones (8-bit codes) (row, line)
+                        if (side == 0) {
+                            const int l0 = it.hg * Ly::KBOX;
                             tma_load_3d(stg + Ly::k_off + slot * Ly::KBOX * 2048, &P.kmap, &full[sidx], 0,
-                                        it.hg * Ly::KBOX, pn.x);
-                        else
+                                        Ly::K8 ? pn.x : l0, Ly::K8 ? l0 : pn.x);
+                        } else {
+                            const int l0 = it.hg * Ly::VBOX;
                             tma_load_3d(stg + Ly::v_off + slot * Ly::VBOX * 2048, &P.vmap, &full[sidx], 0,
-                                        it.hg * Ly::VBOX, pn.x);
+                                        Ly::V8 ? pn.x : l0, Ly::V8 ? l0 : pn.x);
+                        }
                         if (P.norms_bulk)
                             bulk_load_u(nd, (side ? P.vn : P.kn) + (int64_t)pn.x * HC, nb, &full[sidx]);
                         else
@@ -387,26 +410,37 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
         return;
     }
 
-    // ── consumers: warp hl takes KV head hl of the group in both block slots ──
+    // ── consumers: warp hl takes KV head hl of the group in every block slot ──
     const int r = lane >> 2, t = lane & 3;
     const int hl = warp;
-    // This lane's byte offsets inside a stage's block slot 0 (slot 1: + the slot's size). A
-    // block's K codes sit as [16 rows][KBOX 128-byte lines][128], the 16-byte chunk j of line L at
-    // j ^ (L & 7); the same for V with VBOX. Fragment row r of the score MMA is tile row r. The
-    // value MMA's k index 2t + e (+8) stands for position t + 4e (+8), so that the four lanes t
-    // of one row read positions whose swizzle phases differ.
-    uint32_t koff, voff0, voff1;
+    // This lane's byte offsets inside a stage's block slot 0 (other slots: + the slot's size).
+    // Row-major codes (2-, 4-bit): [16 rows][lines][128], the 16-byte chunk j of line L at
+    // j ^ (L & 7). Line-major codes (8-bit): [lines][16 rows][128], chunk j of (line, row) at
+    // j ^ (row & 7); KV head hl owns line hl. Fragment row r of the score MMA is tile row r. The
+    // value MMA's k index 2t + e (+8) stands for position t + 4e (+8) with 2- and 4-bit values
+    // and for position 2t + e (+8) with 8-bit ones, so that the lanes of one wavefront read
+    // chunks whose swizzle phases differ. koff2 / voff2 / voff3: the second 16 bytes of a K row
+    // and the other two V rows of an 8-bit lane.
+    uint32_t koff, koff2 = 0, voff0, voff1;
     {
         constexpr int KL = Ly::KBOX, VL = Ly::VBOX;
         const int kc = (hl * PK) >> 7, kj = ((hl * PK) & 127) >> 4;
-        if constexpr (KB == 4)
+        if constexpr (KB == 8) {
+            koff = Ly::k_off + hl * 2048 + r * 128 + (((2 * t) ^ (r & 7)) << 4);
+            koff2 = Ly::k_off + hl * 2048 + r * 128 + (((2 * t + 1) ^ (r & 7)) << 4);
+        } else if constexpr (KB == 4) {
             koff = Ly::k_off + r * KL * 128 + kc * 128 + (((kj + t) ^ ((r * KL + kc) & 7)) << 4);
-        else
+        } else {
             koff = Ly::k_off + r * KL * 128 + kc * 128 + (((kj + (t >> 1)) ^ ((r * KL + kc) & 7)) << 4) + 8 * (t & 1);
+        }
         const int vc = (hl * PV) >> 7, vj = ((hl * PV) & 127) >> 4;
         const int q0 = t, q1 = t + 4;
         const int vbase = Ly::v_off + vc * 128;
-        if constexpr (VB == 2) {
+        if constexpr (VB == 8) {
+            const int p0 = 2 * t, p1 = 2 * t + 1;
+            voff0 = Ly::v_off + hl * 2048 + p0 * 128 + ((r ^ (p0 & 7)) << 4);
+            voff1 = Ly::v_off + hl * 2048 + p1 * 128 + ((r ^ (p1 & 7)) << 4);
+        } else if constexpr (VB == 2) {
             voff0 = vbase + q0 * VL * 128 + (((vj + (r >> 2)) ^ ((q0 * VL + vc) & 7)) << 4) + 4 * (r & 3);
             voff1 = vbase + q1 * VL * 128 + (((vj + (r >> 2)) ^ ((q1 * VL + vc) & 7)) << 4) + 4 * (r & 3);
         } else {
@@ -415,13 +449,14 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
         }
     }
     constexpr uint32_t KSLOT = Ly::KBOX * 2048, VSLOT = Ly::VBOX * 2048, NSLOT = 16 * HC * 2;
-    constexpr uint32_t KROW8 = 8 * Ly::KBOX * 128, VROW8 = 8 * Ly::VBOX * 128;  // 8 rows further
+    // 8 rows further: row-major, 8 rows of lines; line-major, 8 rows of 128 bytes
+    constexpr uint32_t KROW8 = Ly::K8 ? 8 * 128 : 8 * Ly::KBOX * 128, VROW8 = Ly::V8 ? 8 * 128 : 8 * Ly::VBOX * 128;
     const uint32_t knoff = Ly::kn_off + (r * HC + hl) * 2;
     const uint32_t vnoff = Ly::vn_off + (r * HC + hl) * 2;
-    const int kr = 2 * (r & 3) + (r >> 2);  // the value MMA's k index of tile row r (r + 8: kr + 8)
-    const uint32_t kof = TAB | (KB == 4 ? 4u * lane : 8u * (lane & 15));
-    const uint32_t vof = TAB | (VB == 4 ? 128u + 4u * lane : 128u + 8u * (lane & 15));
-    const uint32_t pbuf = pl.small + Small::p_off + warp * BPS * 256;  // this warp's two weight tiles
+    const int kr = Ly::V8 ? r : 2 * (r & 3) + (r >> 2);  // the value MMA's k index of tile row r (r + 8: kr + 8)
+    const uint32_t kof = TAB | (KB != 2 ? 4u * lane : 8u * (lane & 15));
+    const uint32_t vof = TAB | (VB != 2 ? 128u + 4u * lane : 128u + 8u * (lane & 15));
+    const uint32_t pbuf = pl.small + Sm::p_off + warp * BPS * 256;  // this warp's weight tiles
     const uint32_t pw0 = pbuf + (kr * 8 + 2 * t) * 2, pw1 = pw0 + 8 * 8 * 2;  // rows kr, kr + 8
     const uint32_t pld = pbuf + (lane & 15) * 16;                              // ldmatrix row address
     const float kscale = rsqrtf((float)D) * 1.4426950408889634f;  // 1/sqrt(d) and log2(e)
@@ -430,7 +465,7 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
     // score MMA's B registers (zeros past the group)
     auto load_q = [&](int item, uint2 (&q)[8]) {
         Item it{};
-        if (item < P.items) it = decode_item(P, item);
+        if (item < P.items) it = decode_item<BPS>(P, item);
         const bool live = it.nstg > 0 && r < G;
         const __half* qh = (const __half*)a.qrot + ((int64_t)it.row * a.hq + (it.hg * HC + hl) * G + r) * D + 32 * t;
 #pragma unroll
@@ -442,7 +477,7 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
     int sidx = 0;
     uint32_t sph = 0;
     for (int item = blockIdx.x; item < P.items; item += gridDim.x) {
-        const Item it = decode_item(P, item);
+        const Item it = decode_item<BPS>(P, item);
         if (it.nstg == 0) {
             load_q(item + gridDim.x, qn);
             continue;
@@ -471,7 +506,14 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
                 const int n = j ? nn.y : nn.x;
                 const uint32_t ks = sb + j * KSLOT, ns = sb + j * NSLOT;
                 uint32_t kw[2][PK / 16];
-                if constexpr (KB == 4) {
+                if constexpr (KB == 8) {  // 32 bytes of rows r and r + 8
+                    const uint4 x0 = lds128(ks + koff), x1 = lds128(ks + koff2);
+                    const uint4 y0 = lds128(ks + koff + KROW8), y1 = lds128(ks + koff2 + KROW8);
+                    kw[0][0] = x0.x; kw[0][1] = x0.y; kw[0][2] = x0.z; kw[0][3] = x0.w;
+                    kw[0][4] = x1.x; kw[0][5] = x1.y; kw[0][6] = x1.z; kw[0][7] = x1.w;
+                    kw[1][0] = y0.x; kw[1][1] = y0.y; kw[1][2] = y0.z; kw[1][3] = y0.w;
+                    kw[1][4] = y1.x; kw[1][5] = y1.y; kw[1][6] = y1.z; kw[1][7] = y1.w;
+                } else if constexpr (KB == 4) {
                     const uint4 x = lds128(ks + koff), y = lds128(ks + koff + KROW8);
                     kw[0][0] = x.x; kw[0][1] = x.y; kw[0][2] = x.z; kw[0][3] = x.w;
                     kw[1][0] = y.x; kw[1][1] = y.y; kw[1][2] = y.z; kw[1][3] = y.w;
@@ -489,7 +531,13 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     uint32_t a0, a1, a2, a3;
-                    if constexpr (KB == 4) {  // byte 2kk: coordinates 32t + 4kk, +1; byte 2kk + 1: +2, +3
+                    if constexpr (KB == 8) {  // bytes 4kk .. 4kk + 3: coordinates 32t + 4kk .. +3, one code each
+                        const uint32_t w0 = kw[0][kk], w1 = kw[1][kk];
+                        a0 = __byte_perm(lds32(tab_addr(w0, kof, 0)), lds32(tab_addr(w0, kof, 1)), 0x7610u);
+                        a2 = __byte_perm(lds32(tab_addr(w0, kof, 2)), lds32(tab_addr(w0, kof, 3)), 0x7610u);
+                        a1 = __byte_perm(lds32(tab_addr(w1, kof, 0)), lds32(tab_addr(w1, kof, 1)), 0x7610u);
+                        a3 = __byte_perm(lds32(tab_addr(w1, kof, 2)), lds32(tab_addr(w1, kof, 3)), 0x7610u);
+                    } else if constexpr (KB == 4) {  // byte 2kk: coordinates 32t + 4kk, +1; byte 2kk + 1: +2, +3
                         const uint32_t w0 = kw[0][kk >> 1], w1 = kw[1][kk >> 1];
                         const int b = 2 * (kk & 1);
                         a0 = lds32(tab_addr(w0, kof, b));
@@ -514,9 +562,13 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
                 sc[j][3] = ok1 ? (c4[0][3] + c4[1][3]) * f1 : -INFINITY;
             }
 
-            // ── running softmax over both tiles: the stage's maximum per head ──
-            float t0 = fmaxf(fmaxf(sc[0][0], sc[0][2]), fmaxf(sc[1][0], sc[1][2]));
-            float t1 = fmaxf(fmaxf(sc[0][1], sc[0][3]), fmaxf(sc[1][1], sc[1][3]));
+            // ── running softmax over the stage's tiles: their maximum per head ──
+            float t0 = fmaxf(sc[0][0], sc[0][2]), t1 = fmaxf(sc[0][1], sc[0][3]);
+#pragma unroll
+            for (int j = 1; j < BPS; ++j) {
+                t0 = fmaxf(t0, fmaxf(sc[j][0], sc[j][2]));
+                t1 = fmaxf(t1, fmaxf(sc[j][1], sc[j][3]));
+            }
 #pragma unroll
             for (int o = 4; o < 32; o <<= 1) {
                 t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, o));
@@ -557,7 +609,23 @@ __global__ void __launch_bounds__(THREADS, 1) tqa_stream(const __grid_constant__
                 uint32_t b0, b1;
                 ldsm_x2_trans(b0, b1, pld + j * 256);
                 const uint32_t vs = sb + j * VSLOT;
-                if constexpr (VB == 2) {
+                if constexpr (VB == 8) {
+                    // 16 bytes (dims 16r .. 16r + 15) of positions 2t, 2t + 1, 2t + 8, 2t + 9; MMA mt:
+                    // dims 16r + 2mt (row r) and + 1 (row r + 8), one code per byte
+                    const uint4 x0 = lds128(vs + voff0), x1 = lds128(vs + voff1);
+                    const uint4 x2 = lds128(vs + voff0 + VROW8), x3 = lds128(vs + voff1 + VROW8);
+                    const uint32_t v0[4] = {x0.x, x0.y, x0.z, x0.w}, v1[4] = {x1.x, x1.y, x1.z, x1.w};
+                    const uint32_t v2[4] = {x2.x, x2.y, x2.z, x2.w}, v3[4] = {x3.x, x3.y, x3.z, x3.w};
+#pragma unroll
+                    for (int mt = 0; mt < 8; ++mt) {
+                        const int wd = mt >> 1, b = 2 * (mt & 1);
+                        const uint32_t a0 = __byte_perm(lds32(tab_addr(v0[wd], vof, b)), lds32(tab_addr(v1[wd], vof, b)), 0x7610u);
+                        const uint32_t a1 = __byte_perm(lds32(tab_addr(v0[wd], vof, b + 1)), lds32(tab_addr(v1[wd], vof, b + 1)), 0x7610u);
+                        const uint32_t a2 = __byte_perm(lds32(tab_addr(v2[wd], vof, b)), lds32(tab_addr(v3[wd], vof, b)), 0x7610u);
+                        const uint32_t a3 = __byte_perm(lds32(tab_addr(v2[wd], vof, b + 1)), lds32(tab_addr(v3[wd], vof, b + 1)), 0x7610u);
+                        mma16816(acc[mt], a0, a1, a2, a3, b0, b1);
+                    }
+                } else if constexpr (VB == 2) {
                     // words: bytes 4r..4r+3 (dims 16r..16r+15) of positions t, t + 4 (and + 8); X
                     // byte q: dims 16r + 4q, +1 at both positions of the pair; Xb: dims +2, +3
                     const uint32_t w0 = lds32(vs + voff0), w1 = lds32(vs + voff1);
@@ -642,13 +710,16 @@ static bool encode_norms(CUtensorMap* map, const void* base, uint64_t hkv, uint6
 }
 
 // Codes: uint8 [rows, hkv * P] seen as [rows][hkv * P / 128 lines][128 bytes]; box of `lines`
-// lines (one head group) x 16 rows, 128-byte swizzle.
-static bool encode_codes(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t lines) {
+// lines (one head group) x 16 rows, 128-byte swizzle. Line-major (8-bit codes): the same bytes
+// seen as [lines][rows][128] (dimension order 128, rows, lines), so the box lands line by line.
+static bool encode_codes(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t lines,
+                         bool line_major) {
     auto encode = sm100::tensor_map_encoder();
     if (!encode) return false;
-    const cuuint64_t dims[3] = {128, (cuuint64_t)(row_bytes / 128), (cuuint64_t)rows};
-    const cuuint64_t strides[2] = {128, (cuuint64_t)row_bytes};
-    const cuuint32_t box[3] = {128, lines, 16};
+    const cuuint64_t nl = row_bytes / 128;
+    const cuuint64_t dims[3] = {128, line_major ? (cuuint64_t)rows : nl, line_major ? nl : (cuuint64_t)rows};
+    const cuuint64_t strides[2] = {line_major ? (cuuint64_t)row_bytes : 128, line_major ? 128 : (cuuint64_t)row_bytes};
+    const cuuint32_t box[3] = {128, line_major ? 16u : lines, line_major ? lines : 16u};
     const cuuint32_t estr[3] = {1, 1, 1};
     return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -675,10 +746,11 @@ static int stream_chunk(int64_t positions, int64_t rows, int ng, int sms) {
     return best;
 }
 
-// Whether the streamed kernel takes this call: 2- or 4-bit codes, KV heads a multiple of 8,
+// Whether the streamed kernel takes this call: 2-, 4- or 8-bit codes, KV heads a multiple of 8,
 // 16-byte aligned pools whose rows a TMA coordinate can reach.
 bool stream_ok(const AttnArgs& a, int kb, int vb, const PoolAddr& ad) {
-    if (!((kb == 2 || kb == 4) && (vb == 2 || vb == 4))) return false;
+    const auto bits = [](int b) { return b == 2 || b == 4 || b == 8; };
+    if (!bits(kb) || !bits(vb)) return false;
     if (a.hkv % stream::HC != 0 || a.hq / a.hkv > MAXG) return false;
     if (!aligned16(ad.kp) || !aligned16(ad.vp) || !aligned16(ad.kn) || !aligned16(ad.vn)) return false;
     return ad.pool_rows > 0 && ad.pool_rows <= INT32_MAX;
@@ -695,8 +767,8 @@ static int stream_launch_t(AttnArgs& a, const PoolAddr& ad, cudaStream_t s) {
     stream::Params P;
     memset(&P, 0, sizeof P);
     const uint64_t prow = (uint64_t)ad.pool_rows;
-    if (!stream::encode_codes(&P.kmap, ad.kp, (uint64_t)a.hkv * Ly::PK, prow, Ly::KBOX) ||
-        !stream::encode_codes(&P.vmap, ad.vp, (uint64_t)a.hkv * Ly::PV, prow, Ly::VBOX) ||
+    if (!stream::encode_codes(&P.kmap, ad.kp, (uint64_t)a.hkv * Ly::PK, prow, Ly::KBOX, Ly::K8) ||
+        !stream::encode_codes(&P.vmap, ad.vp, (uint64_t)a.hkv * Ly::PV, prow, Ly::VBOX, Ly::V8) ||
         !stream::encode_norms(&P.knmap, ad.kn, (uint64_t)a.hkv, prow) ||
         !stream::encode_norms(&P.vnmap, ad.vn, (uint64_t)a.hkv, prow))
         return (int)cudaErrorInvalidValue;
@@ -709,7 +781,7 @@ static int stream_launch_t(AttnArgs& a, const PoolAddr& ad, cudaStream_t s) {
     P.kn = ad.kn;
     P.vn = ad.vn;
     P.norms_bulk = a.hkv == stream::HC ? 1 : 0;
-    P.spi = ch / (stream::BPS * 16);
+    P.spi = ch / (Ly::BPS * 16);
     P.nchi = nchi;
     P.ng = ng;
     P.dng = sm100::make_divu32((uint32_t)ng);
@@ -722,15 +794,24 @@ static int stream_launch_t(AttnArgs& a, const PoolAddr& ad, cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stream::DYN_BYTES);
     if (e != cudaSuccess) return (int)e;
     const int grid = (int)std::min<int64_t>(items, sms);
-    launch_pdl_smem(kern, dim3(grid), dim3(stream::THREADS), (size_t)stream::DYN_BYTES, s, P);
+    launch_pdl_smem(kern, dim3(grid), dim3(Ly::THREADS), (size_t)stream::DYN_BYTES, s, P);
     return (int)cudaGetLastError();
 }
 
 // Launches the streamed kernel for a call stream_ok() accepted.
 int stream_launch(AttnArgs& a, int kb, int vb, const PoolAddr& ad, cudaStream_t s) {
     if (!stream_ok(a, kb, vb, ad)) return (int)cudaErrorInvalidValue;
-    if (kb == 4) return vb == 2 ? stream_launch_t<4, 2>(a, ad, s) : stream_launch_t<4, 4>(a, ad, s);
-    return vb == 2 ? stream_launch_t<2, 2>(a, ad, s) : stream_launch_t<2, 4>(a, ad, s);
+    switch (kb * 10 + vb) {
+        case 22: return stream_launch_t<2, 2>(a, ad, s);
+        case 24: return stream_launch_t<2, 4>(a, ad, s);
+        case 28: return stream_launch_t<2, 8>(a, ad, s);
+        case 42: return stream_launch_t<4, 2>(a, ad, s);
+        case 44: return stream_launch_t<4, 4>(a, ad, s);
+        case 48: return stream_launch_t<4, 8>(a, ad, s);
+        case 82: return stream_launch_t<8, 2>(a, ad, s);
+        case 84: return stream_launch_t<8, 4>(a, ad, s);
+        default: return stream_launch_t<8, 8>(a, ad, s);
+    }
 }
 
 }  // namespace tqa

@@ -284,11 +284,12 @@ def _run_counted(path, fn):
 
 
 @pytest.mark.parametrize("G,kb,vb,dt", [(4, 4, 2, "f16"), (1, 4, 4, "f16"), (2, 2, 2, "bf16"), (8, 2, 4, "f16"),
-                                        (4, 4, 4, "bf16")])
+                                        (4, 4, 4, "bf16"), (4, 8, 8, "f16"), (2, 8, 4, "bf16"), (4, 2, 8, "f16"),
+                                        (8, 8, 2, "f16")])
 def test_streamed_kernel_decode_matches_statement(G, kb, vb, dt):
-    """Eight KV heads (one head group): decode at contexts that end inside a 32-position stage,
-    cross 512-position chunks and take an item to its last stage, for each bit-width pair, group
-    size and query dtype."""
+    """Eight KV heads (one head group): decode at contexts that end inside a stage, cross chunk
+    edges and take an item to its last stage, for each bit-width pair (8-bit codes included: the
+    reference's protected layers), group size and query dtype."""
     kv_lens, Hkv = [300, 777, 1500, 2049], 8
     c = build_cache(kv_lens, Hkv, kb, vb, seed=100 + 10 * G + kb + vb)
     qh, q = make_q(len(kv_lens), 1, G * Hkv, dt, seed=101 + G)
@@ -301,11 +302,12 @@ def test_streamed_kernel_decode_matches_statement(G, kb, vb, dt):
                             label=f"seq {s} (kv {L})", dtype=dt)
 
 
-def test_streamed_kernel_prefill_chunk_causal_and_many_items():
-    """40 query tokens per sequence with their own causal ranges (the token of a sequence share
+@pytest.mark.parametrize("kb,vb", [(4, 2), (8, 8)])
+def test_streamed_kernel_prefill_chunk_causal_and_many_items(kb, vb):
+    """40 query tokens per sequence with their own causal ranges (the tokens of a sequence share
     a chunk's codes), more items than the persistent grid has CTAs."""
     kv_lens, Tq, Hkv, G = [60, 600, 1100, 2100], 40, 8, 4
-    c = build_cache(kv_lens, Hkv, 4, 2, seed=110)
+    c = build_cache(kv_lens, Hkv, kb, vb, seed=110 + kb)
     qh, q = make_q(len(kv_lens), Tq, G * Hkv, "f16", seed=111)
     starts = [L - Tq for L in kv_lens]
     got, served = _run_counted("attention_streamed", lambda: run_ours(c, q, kv_lens, starts, "f16"))
@@ -337,11 +339,12 @@ def test_streamed_kernel_missing_blocks_and_empty_sequence():
                             label=f"seq {s}", dtype="f16")
 
 
-def test_streamed_kernel_pool_ending_inside_a_block():
+@pytest.mark.parametrize("kb,vb", [(4, 2), (8, 8)])
+def test_streamed_kernel_pool_ending_inside_a_block(kb, vb):
     """A pool cut 5 rows into the last block the sequence uses: the kernel's copies read zeros
     past the pool's end, and the positions there are left out."""
-    kv_len, Hkv, G, kb, vb = 700, 8, 4, 4, 2
-    c = build_cache([kv_len], Hkv, kb, vb, seed=130)
+    kv_len, Hkv, G = 700, 8, 4
+    c = build_cache([kv_len], Hkv, kb, vb, seed=130 + kb)
     table = c["tables"][0]
     cut = int(table.max()) * 16 + 11
     qh, q = make_q(1, 1, G * Hkv, "f16", seed=131)
