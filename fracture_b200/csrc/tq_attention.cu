@@ -105,9 +105,15 @@ __global__ void __launch_bounds__(D) tqa_rotate_q(const __grid_constant__ Rotate
         sm100::mbar_expect_tx(bar, D * D * 4);
         for (int c = 0; c < 4; ++c) sm100::tma_load_2d(pis + c * 32 * D, &R.pimap, bar, 32 * c, 0);
     }
-    for (int e = i; e < NR * G * D; e += D) {
-        const int rr = e / (G * D);
-        qs[e] = rr < nr ? load_q(a, ((int64_t)(r0 + rr) * a.hq + g * G) * D + (e - rr * G * D)) : 0.0f;
+    {
+        float qv[NR * G];  // every query load in flight before the first store
+#pragma unroll
+        for (int k = 0; k < NR * G; ++k) {
+            const int e = i + k * D, rr = e / (G * D);
+            qv[k] = rr < nr ? load_q(a, ((int64_t)(r0 + rr) * a.hq + g * G) * D + (e - rr * G * D)) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < NR * G; ++k) qs[i + k * D] = qv[k];
     }
     __syncthreads();
     if (!stage_wait(bar)) return;
@@ -435,20 +441,21 @@ __global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
     }
 }
 
-// out[row][h][i] = sum_j Pi_v[j][i] * (sum_c acc_c[j] e^(m_c - M)) / (sum_c l_c e^(m_c - M)) for rq
-// query rows: thread (h, i) of KV group blockIdx.y sums the chunks of output i of head h in one
-// pass (the running maximum rescales what it has summed when it grows), eight chunks' loads in
-// flight at a time, while one bulk copy brings Pi_v into shared memory; the rotation back reads
-// column i of Pi_v (consecutive words across threads) once for the CTA's rows.
-__global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a, int rows, int rq) {
+// out[row][h][i] = sum_j Pi_v[j][i] * (sum_c acc_c[j] e^(m_c - M)) / (sum_c l_c e^(m_c - M)) for NR
+// query rows: thread (h, i) of KV group blockIdx.y sums the chunks of output i of head h, eight
+// chunks' loads in flight at a time, while one bulk copy brings Pi_v into shared memory; the
+// rotation back reads column i of Pi_v (consecutive words across threads) once for the CTA's
+// rows.
+template <int NR>
+__global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a, int rows) {
     extern __shared__ __align__(16) float csm[];
     float* pvs = csm;           // [D][D]
     float* accs = csm + D * D;  // [RQ][G][D]
     const int G = a.hq / a.hkv;
     uint64_t* bar = (uint64_t*)(accs + RQ * G * D);
-    const int r0 = blockIdx.x * rq, g = blockIdx.y, tid = threadIdx.x;
+    const int r0 = blockIdx.x * NR, g = blockIdx.y, tid = threadIdx.x;
     const int h = tid / D, i = tid - h * D;
-    const int nr = min(rq, rows - r0);
+    const int nr = min(NR, rows - r0);
     const bool bulk = ((uintptr_t)a.piv & 15) == 0;
     if (tid == 0) {
         sm100::mbar_init(bar, 1);
@@ -470,45 +477,50 @@ __global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a, int rows, in
         const int L = causal_len(a, s, t);
         const int nc = min((L + a.ch - 1) / a.ch * a.spc, a.nch);  // kv_lens past max_kv_len: the chunks computed
         const float* ph = a.part + ((int64_t)row * a.hq + g * G + h) * a.nch * PART;
-        float M = -INFINITY, l = 0.0f, v = 0.0f;
+        // the maxima first (eight loads in flight), then the weights e^(m_c - M) as exp2 of
+        // log2(e)-scaled differences (ex2.approx, 2 ulp) for the sums
+        float M = -INFINITY;
         for (int c0 = 0; c0 < nc; c0 += 8) {
-            float m8[8], l8[8], v8[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const int c = c0 + k;
-                m8[k] = c < nc ? ph[c * PART] : -INFINITY;
-                l8[k] = c < nc ? ph[c * PART + 1] : 0.0f;
-                v8[k] = c < nc ? ph[c * PART + 2 + i] : 0.0f;
-            }
+            for (int k = 0; k < 8; ++k)
+                if (c0 + k < nc) M = fmaxf(M, ph[(c0 + k) * PART]);
+        }
+        float l = 0.0f, v = 0.0f;
+        if (M > -INFINITY) {
+            const float Ml = M * 1.4426950408889634f;
+            for (int c0 = 0; c0 < nc; c0 += 8) {
+                float m8[8], l8[8], v8[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                if (m8[k] == -INFINITY) continue;
-                if (m8[k] > M) {
-                    const float sc = expf(M - m8[k]);
-                    l *= sc;
-                    v *= sc;
-                    M = m8[k];
+                for (int k = 0; k < 8; ++k) {
+                    const int c = c0 + k;
+                    m8[k] = c < nc ? ph[c * PART] : -INFINITY;
+                    l8[k] = c < nc ? ph[c * PART + 1] : 0.0f;
+                    v8[k] = c < nc ? ph[c * PART + 2 + i] : 0.0f;
                 }
-                const float f = expf(m8[k] - M);
-                l = fmaf(l8[k], f, l);
-                v = fmaf(v8[k], f, v);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    float f;
+                    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(f) : "f"(fmaf(m8[k], 1.4426950408889634f, -Ml)));
+                    l = fmaf(l8[k], f, l);  // a chunk with no position: m = -inf, f = 0
+                    v = fmaf(v8[k], f, v);
+                }
             }
         }
         accs[(rr * G + h) * D + i] = l > 0.0f ? v / l : 0.0f;
     }
     __syncthreads();
     if (bulk && !stage_wait(bar)) return;
-    float o[RQ];
+    float o[NR];
 #pragma unroll
-    for (int rr = 0; rr < RQ; ++rr) o[rr] = 0.0f;
+    for (int rr = 0; rr < NR; ++rr) o[rr] = 0.0f;
 #pragma unroll 4
     for (int j = 0; j < D; ++j) {
         const float p = pvs[j * D + i];
 #pragma unroll
-        for (int rr = 0; rr < RQ; ++rr) o[rr] = fmaf(p, accs[(rr * G + h) * D + j], o[rr]);
+        for (int rr = 0; rr < NR; ++rr) o[rr] = fmaf(p, accs[(rr * G + h) * D + j], o[rr]);
     }
 #pragma unroll
-    for (int rr = 0; rr < RQ; ++rr) {
+    for (int rr = 0; rr < NR; ++rr) {
         if (rr >= nr) break;
         const int64_t e = ((int64_t)(r0 + rr) * a.hq + g * G + h) * D + i;
         if (a.dtype == FB_BF16) ((__nv_bfloat16*)a.out)[e] = __float2bfloat16_rn(o[rr]);
@@ -520,10 +532,11 @@ __global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a, int rows, in
 inline int launch_combine(const AttnArgs& a, int rows, cudaStream_t s) {
     const int G = a.hq / a.hkv;
     const size_t smem = (size_t)D * D * 4 + (size_t)RQ * G * D * 4 + 16;
-    cudaError_t e = cudaFuncSetAttribute(tqa_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return (int)e;
     const int rq = rows_per_cta(rows, a.hkv);
-    launch_pdl_smem(tqa_combine, dim3((rows + rq - 1) / rq, a.hkv), dim3(G * D), smem, s, a, rows, rq);
+    void (*kern)(AttnArgs, int) = rq == 1 ? tqa_combine<1> : rq == 2 ? tqa_combine<2> : tqa_combine<4>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    launch_pdl_smem(kern, dim3((rows + rq - 1) / rq, a.hkv), dim3(G * D), smem, s, a, rows);
     return (int)cudaGetLastError();
 }
 
