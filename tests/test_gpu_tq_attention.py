@@ -407,3 +407,20 @@ def test_short_contexts_stream_and_few_kv_heads_keep_the_per_head_kernel():
         for s, L in enumerate(kv_lens):
             ops.assert_close_fp(got[s], statement(c, qh[s], s, L, starts[s]), rel=2e-3, min_cos=0.9999,
                                 label=f"Hkv {Hkv} seq {s}", dtype="f16")
+
+
+def test_streamed_kernel_many_items_per_cta_and_ragged_lengths():
+    """Forty sequences of 1000-3000 positions: several hundred items of different lengths, so
+    every persistent CTA takes several (its stage ring and query prefetch run across them)."""
+    rng = np.random.default_rng(160)
+    kv_lens = [int(x) for x in rng.integers(1000, 3001, size=40)]
+    Hkv, G = 8, 4
+    c = build_cache(kv_lens, Hkv, 4, 2, seed=161)
+    qh, q = make_q(len(kv_lens), 1, G * Hkv, "f16", seed=162)
+    starts = [L - 1 for L in kv_lens]
+    got, served = _run_counted("attention_streamed", lambda: run_ours(c, q, kv_lens, starts, "f16"))
+    assert served == 1
+    got = got.float().cpu().numpy()
+    for s, L in enumerate(kv_lens):
+        ops.assert_close_fp(got[s], statement(c, qh[s], s, L, starts[s]), rel=2e-3, min_cos=0.9999,
+                            label=f"seq {s} (kv {L})", dtype="f16")
