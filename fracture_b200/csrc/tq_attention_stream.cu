@@ -730,11 +730,13 @@ static bool encode_codes(CUtensorMap* map, const void* base, uint64_t row_bytes,
 
 // Positions per chunk for the streamed kernel: of 256, 512, 1024 and 2048, the one whose items
 // fill the persistent grid's waves best, the longer on a tie (one partial slot per chunk: at
-// most the workspace's one per 256 positions).
+// most the workspace's one per 256 positions). Chunks that would leave a query row more than 32
+// partials are skipped while a longer chunk exists: the combine reads every partial of a row.
 static int stream_chunk(int64_t positions, int64_t rows, int ng, int sms) {
     int best = 0;
     double best_eff = -1.0;
     for (int ch = 256; ch <= 2048; ch *= 2) {
+        if (ch < 2048 && (positions + ch - 1) / ch > 32) continue;
         const int64_t items = (positions + ch - 1) / ch * rows * ng;
         const int64_t waves = (items + sms - 1) / sms;
         const double eff = (double)items / (double)(waves * sms) + 1e-3 * (ch / 256);
