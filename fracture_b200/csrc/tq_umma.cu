@@ -363,23 +363,37 @@ __device__ __forceinline__ void compress_cta(const CUtensorMap* tmap_p, const Tq
         }
     }
     for (int e = threadIdx.x; e < nlev; e += THREADS) misc->cen[e] = __ldg(a.centroids + e);
-    // B operand: Pi split into NPARTS parts (hi + lo [+ lo2]) in the SW128 K-major image.
-    for (int c = threadIdx.x; c < D * D / 8; c += THREADS) {
-        const int n = c >> 4, k0 = (c & 15) << 3;
-        float rem[8];
-        const float4 p0 = __ldg((const float4*)(a.rotation + n * D + k0));
-        const float4 p1 = __ldg((const float4*)(a.rotation + n * D + k0 + 4));
-        rem[0] = p0.x; rem[1] = p0.y; rem[2] = p0.z; rem[3] = p0.w;
-        rem[4] = p1.x; rem[5] = p1.y; rem[6] = p1.z; rem[7] = p1.w;
+    // B operand: Pi split into NPARTS parts (hi + lo [+ lo2]) in the SW128 K-major image. A
+    // thread's loads of Pi (four pairs of 16 bytes at most) are all in flight before it splits.
+    {
+        constexpr int PER = (D * D / 8 + THREADS - 1) / THREADS;
+        float4 pv[PER][2];
 #pragma unroll
-        for (int p = 0; p < NPARTS; ++p) {
-            Vec16<TIn> v;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                v.e[e] = from_f32<TIn>(rem[e]);
-                rem[e] = rem[e] - to_f32(v.e[e]);
+        for (int q = 0; q < PER; ++q) {
+            const int c = threadIdx.x + q * THREADS;
+            if (c < D * D / 8) {
+                const int n = c >> 4, k0 = (c & 15) << 3;
+                pv[q][0] = __ldg((const float4*)(a.rotation + n * D + k0));
+                pv[q][1] = __ldg((const float4*)(a.rotation + n * D + k0 + 4));
             }
-            *(uint4*)(sB + p * TILE_BYTES + sw128_offset(n, k0)) = v.u;
+        }
+#pragma unroll
+        for (int q = 0; q < PER; ++q) {
+            const int c = threadIdx.x + q * THREADS;
+            if (c >= D * D / 8) break;
+            const int n = c >> 4, k0 = (c & 15) << 3;
+            float rem[8] = {pv[q][0].x, pv[q][0].y, pv[q][0].z, pv[q][0].w,
+                            pv[q][1].x, pv[q][1].y, pv[q][1].z, pv[q][1].w};
+#pragma unroll
+            for (int p = 0; p < NPARTS; ++p) {
+                Vec16<TIn> v;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    v.e[e] = from_f32<TIn>(rem[e]);
+                    rem[e] = rem[e] - to_f32(v.e[e]);
+                }
+                *(uint4*)(sB + p * TILE_BYTES + sw128_offset(n, k0)) = v.u;
+            }
         }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
