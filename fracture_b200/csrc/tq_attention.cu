@@ -442,19 +442,18 @@ __global__ void __launch_bounds__(THREADS) tqa_chunk(AttnArgs a, Addr ad) {
 }
 
 // out[row][h][i] = sum_j Pi_v[j][i] * (sum_c acc_c[j] e^(m_c - M)) / (sum_c l_c e^(m_c - M)) for NR
-// query rows: thread (h, i) of KV group blockIdx.y sums the chunks of output i of head h, eight
-// chunks' loads in flight at a time, while one bulk copy brings Pi_v into shared memory; the
-// rotation back reads column i of Pi_v (consecutive words across threads) once for the CTA's
-// rows.
+// query rows of KV group blockIdx.y: the chunks' partials are summed while one bulk copy brings
+// Pi_v into shared memory; the rotation back reads column i of Pi_v (consecutive words across
+// threads) once for the CTA's rows.
 template <int NR>
-__global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a, int rows) {
+__global__ void __launch_bounds__(4 * D) tqa_combine(AttnArgs a, int rows) {
     extern __shared__ __align__(16) float csm[];
     float* pvs = csm;           // [D][D]
-    float* accs = csm + D * D;  // [RQ][G][D]
-    const int G = a.hq / a.hkv;
+    float* accs = csm + D * D;  // [NR][G][D]
+    const int G = a.hq / a.hkv, GT = min(G, 4);  // heads per KV group; head lanes of the CTA
     uint64_t* bar = (uint64_t*)(accs + RQ * G * D);
     const int r0 = blockIdx.x * NR, g = blockIdx.y, tid = threadIdx.x;
-    const int h = tid / D, i = tid - h * D;
+    const int hh = tid / D, i = tid - hh * D;
     const int nr = min(NR, rows - r0);
     const bool bulk = ((uintptr_t)a.piv & 15) == 0;
     if (tid == 0) {
@@ -469,62 +468,97 @@ __global__ void __launch_bounds__(MAXG * D) tqa_combine(AttnArgs a, int rows) {
             sm100::bulk_load(pvs, a.piv, D * D * 4, bar);
         }
     } else {
-        for (int e = tid; e < D * D; e += G * D) pvs[e] = __ldg(a.piv + e);
+        for (int e = tid; e < D * D; e += GT * D) pvs[e] = __ldg(a.piv + e);
     }
+    // weights e^(m_c - M) as exp2 of log2(e)-scaled differences (ex2.approx, 2 ulp); a chunk
+    // with no position has m = -inf and weight 0
+    auto weight = [](float m, float Ml) {
+        float f;
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(f) : "f"(fmaf(m, 1.4426950408889634f, -Ml)));
+        return f;
+    };
+    // Thread (hh, i) sums output i of heads hh, hh + 4 of each row. With at most CMAX chunks, a
+    // row's maxima, sums and accumulator values are requested at once (one round trip to L2);
+    // else two passes (the maxima, then the weighted sums), eight chunks' loads at a time.
+    constexpr int CMAX = 16;
     for (int rr = 0; rr < nr; ++rr) {
         const int row = r0 + rr;
         const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
         const int L = causal_len(a, s, t);
         const int nc = min((L + a.ch - 1) / a.ch * a.spc, a.nch);  // kv_lens past max_kv_len: the chunks computed
-        const float* ph = a.part + ((int64_t)row * a.hq + g * G + h) * a.nch * PART;
-        // the maxima first (eight loads in flight), then the weights e^(m_c - M) as exp2 of
-        // log2(e)-scaled differences (ex2.approx, 2 ulp) for the sums
-        float M = -INFINITY;
-        for (int c0 = 0; c0 < nc; c0 += 8) {
+        for (int h = hh; h < G; h += 4) {
+            const float* ph = a.part + ((int64_t)row * a.hq + g * G + h) * a.nch * PART;
+            float l = 0.0f, v = 0.0f;
+            if (nc <= CMAX) {
+                float mm[CMAX], ll[CMAX], vv[CMAX];
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-                if (c0 + k < nc) M = fmaxf(M, ph[(c0 + k) * PART]);
-        }
-        float l = 0.0f, v = 0.0f;
-        if (M > -INFINITY) {
-            const float Ml = M * 1.4426950408889634f;
-            for (int c0 = 0; c0 < nc; c0 += 8) {
-                float m8[8], l8[8], v8[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const int c = c0 + k;
-                    m8[k] = c < nc ? ph[c * PART] : -INFINITY;
-                    l8[k] = c < nc ? ph[c * PART + 1] : 0.0f;
-                    v8[k] = c < nc ? ph[c * PART + 2 + i] : 0.0f;
+                for (int c = 0; c < CMAX; ++c) {
+                    const bool in = c < nc;
+                    mm[c] = in ? ph[c * PART] : -INFINITY;
+                    ll[c] = in ? ph[c * PART + 1] : 0.0f;
+                    vv[c] = in ? ph[c * PART + 2 + i] : 0.0f;
                 }
+                float M = -INFINITY;
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    float f;
-                    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(f) : "f"(fmaf(m8[k], 1.4426950408889634f, -Ml)));
-                    l = fmaf(l8[k], f, l);  // a chunk with no position: m = -inf, f = 0
-                    v = fmaf(v8[k], f, v);
+                for (int c = 0; c < CMAX; ++c) M = fmaxf(M, mm[c]);
+                if (M > -INFINITY) {
+                    const float Ml = M * 1.4426950408889634f;
+#pragma unroll
+                    for (int c = 0; c < CMAX; ++c) {
+                        const float f = weight(mm[c], Ml);
+                        l = fmaf(ll[c], f, l);
+                        v = fmaf(vv[c], f, v);
+                    }
+                }
+            } else {
+                float M = -INFINITY;
+                for (int c0 = 0; c0 < nc; c0 += 8) {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (c0 + k < nc) M = fmaxf(M, ph[(c0 + k) * PART]);
+                }
+                if (M > -INFINITY) {
+                    const float Ml = M * 1.4426950408889634f;
+                    for (int c0 = 0; c0 < nc; c0 += 8) {
+                        float m8[8], l8[8], v8[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const int c = c0 + k;
+                            m8[k] = c < nc ? ph[c * PART] : -INFINITY;
+                            l8[k] = c < nc ? ph[c * PART + 1] : 0.0f;
+                            v8[k] = c < nc ? ph[c * PART + 2 + i] : 0.0f;
+                        }
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const float f = weight(m8[k], Ml);
+                            l = fmaf(l8[k], f, l);
+                            v = fmaf(v8[k], f, v);
+                        }
+                    }
                 }
             }
+            accs[(rr * G + h) * D + i] = l > 0.0f ? v / l : 0.0f;
         }
-        accs[(rr * G + h) * D + i] = l > 0.0f ? v / l : 0.0f;
     }
     __syncthreads();
     if (bulk && !stage_wait(bar)) return;
-    float o[NR];
+    for (int h = hh; h < G; h += 4) {
+        float o[NR];
 #pragma unroll
-    for (int rr = 0; rr < NR; ++rr) o[rr] = 0.0f;
+        for (int rr = 0; rr < NR; ++rr) o[rr] = 0.0f;
 #pragma unroll 4
-    for (int j = 0; j < D; ++j) {
-        const float p = pvs[j * D + i];
+        for (int j = 0; j < D; ++j) {
+            const float p = pvs[j * D + i];
 #pragma unroll
-        for (int rr = 0; rr < NR; ++rr) o[rr] = fmaf(p, accs[(rr * G + h) * D + j], o[rr]);
-    }
+            for (int rr = 0; rr < NR; ++rr) o[rr] = fmaf(p, accs[(rr * G + h) * D + j], o[rr]);
+        }
 #pragma unroll
-    for (int rr = 0; rr < NR; ++rr) {
-        if (rr >= nr) break;
-        const int64_t e = ((int64_t)(r0 + rr) * a.hq + g * G + h) * D + i;
-        if (a.dtype == FB_BF16) ((__nv_bfloat16*)a.out)[e] = __float2bfloat16_rn(o[rr]);
-        else ((__half*)a.out)[e] = __float2half_rn(o[rr]);
+        for (int rr = 0; rr < NR; ++rr) {
+            if (rr >= nr) break;
+            const int64_t e = ((int64_t)(r0 + rr) * a.hq + g * G + h) * D + i;
+            if (a.dtype == FB_BF16) ((__nv_bfloat16*)a.out)[e] = __float2bfloat16_rn(o[rr]);
+            else ((__half*)a.out)[e] = __float2half_rn(o[rr]);
+        }
     }
 }
 
@@ -536,7 +570,7 @@ inline int launch_combine(const AttnArgs& a, int rows, cudaStream_t s) {
     void (*kern)(AttnArgs, int) = rq == 1 ? tqa_combine<1> : rq == 2 ? tqa_combine<2> : tqa_combine<4>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;
-    launch_pdl_smem(kern, dim3((rows + rq - 1) / rq, a.hkv), dim3(G * D), smem, s, a, rows);
+    launch_pdl_smem(kern, dim3((rows + rq - 1) / rq, a.hkv), dim3(std::min(G, 4) * D), smem, s, a, rows);
     return (int)cudaGetLastError();
 }
 
