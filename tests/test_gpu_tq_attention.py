@@ -424,3 +424,17 @@ def test_streamed_kernel_many_items_per_cta_and_ragged_lengths():
     for s, L in enumerate(kv_lens):
         ops.assert_close_fp(got[s], statement(c, qh[s], s, L, starts[s]), rel=2e-3, min_cos=0.9999,
                             label=f"seq {s} (kv {L})", dtype="f16")
+
+
+@pytest.mark.parametrize("kv_len,kb,vb", [(12000, 4, 2), (20000, 4, 2), (33000, 4, 2), (33000, 8, 8)])
+def test_streamed_kernel_every_chunk_length(kv_len, kb, vb):
+    """One long sequence: a row may have at most 32 partials, so these contexts take 512-, 1024-
+    and 2048-position chunks (the last with 8-bit codes: 128 one-block stages per item), each
+    ending inside a chunk and inside a stage."""
+    Hkv, G = 8, 4
+    c = build_cache([kv_len], Hkv, kb, vb, seed=170 + kv_len % 97 + kb)
+    qh, q = make_q(1, 1, G * Hkv, "f16", seed=171)
+    got, served = _run_counted("attention_streamed", lambda: run_ours(c, q, [kv_len], [kv_len - 1], "f16"))
+    assert served == 1
+    ops.assert_close_fp(got.float().cpu().numpy()[0], statement(c, qh[0], 0, kv_len, kv_len - 1), rel=2e-3,
+                        min_cos=0.9999, label=f"kv {kv_len}", dtype="f16")
