@@ -241,7 +241,7 @@ int fb_launch_kv_append_paged(const void* keys, const void* values, int dtype, i
 }
 
 namespace fb {
-size_t tq_attention_ws_bytes(int64_t rows, int hq, int max_kv_len);
+size_t tq_attention_ws_bytes_full(int64_t rows, int hq, int max_kv_len);
 int tq_attention_one_seq(const void* q, int dtype, int num_tokens, int hq, int hkv, int head_dim, const void* kp,
                          const void* kn, const void* vp, const void* vn, int64_t pool_rows, const int32_t* block_table,
                          int num_blocks, int kv_len, int start_pos, const float* pik, const float* piv,
@@ -1273,7 +1273,7 @@ int fb_tq_cache_attention(fb_tq_cache* c, uint64_t handle, size_t layer, const f
         return fail(FB_ERR_UNSUPPORTED_DTYPE, "attention: q and out must be FP16 or BF16 of one type");
     if ((rc = b->flush())) return rc;
     if ((rc = tq_sync_table(c, it->second))) return rc;
-    const size_t ws = fb::tq_attention_ws_bytes(q->shape[0], (int)q->shape[1], (int)kv_len);
+    const size_t ws = fb::tq_attention_ws_bytes_full(q->shape[0], (int)q->shape[1], (int)kv_len);
     FB_CUDA(c->attn_ws.ensure(std::max<size_t>(ws, 16), b->stream));
     const int kb = c->kbits[layer], vb = c->vbits[layer];
     int e = fb::tq_attention_one_seq(pq, q->dtype, (int)q->shape[0], (int)q->shape[1], (int)c->heads, (int)c->head_dim,

@@ -68,6 +68,13 @@ __device__ __forceinline__ bool stage_wait(uint64_t* bar) {
     return true;
 }
 
+// 2^x (ex2.approx, 2 ulp; 2^-inf = 0)
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 struct RotateParams {
     CUtensorMap pimap;  // Pi_k: f32 [128][128], box 32 columns x 128 rows, 128-byte swizzle
     AttnArgs a;
@@ -461,15 +468,17 @@ __global__ void __launch_bounds__(4 * D) tqa_combine(AttnArgs a, int rows) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    pdl_begin();
-    if (bulk) {
-        if (tid == 0) {
-            sm100::mbar_expect_tx(bar, D * D * 4);
-            sm100::bulk_load(pvs, a.piv, D * D * 4, bar);
-        }
-    } else {
-        for (int e = tid; e < D * D; e += GT * D) pvs[e] = __ldg(a.piv + e);
+    // Pi_v is read before the wait for the chunk kernel: run() launches this kernel right after
+    // one of this file's chunk kernels (tqa_stream, tqa_mma, tqa_chunk), none of which writes the
+    // rotation, so the copy overlaps that kernel's tail. A chain that puts another kernel in
+    // between must move the copy after pdl_begin().
+    if (bulk && tid == 0) {
+        sm100::mbar_expect_tx(bar, D * D * 4);
+        sm100::bulk_load(pvs, a.piv, D * D * 4, bar);
     }
+    pdl_begin();
+    if (!bulk)
+        for (int e = tid; e < D * D; e += GT * D) pvs[e] = __ldg(a.piv + e);
     // weights e^(m_c - M) as exp2 of log2(e)-scaled differences (ex2.approx, 2 ulp); a chunk
     // with no position has m = -inf and weight 0
     auto weight = [](float m, float Ml) {
@@ -562,9 +571,125 @@ __global__ void __launch_bounds__(4 * D) tqa_combine(AttnArgs a, int rows) {
     }
 }
 
-// One launch of tqa_combine for the call's rows.
+// The combine for calls with few rows: one CTA per (query row, HPC Q heads), so that a call of
+// one or a few rows still spreads over many SMs, and the partials of a head split over the four
+// 128-thread chunk lanes (lane k takes chunks k, k + 4, ...), each keeping a running maximum, sum
+// and accumulator (eight chunks' loads in flight at a time), merged through shared memory. Then
+// as tqa_combine: divide by the sum, rotate back by Pi_v (the four lanes each take 32 of the 128
+// terms), convert.
+__global__ void __launch_bounds__(4 * D) tqa_combine_deep(AttnArgs a, int hpc) {
+    extern __shared__ __align__(16) float csm[];
+    float* pvs = csm;                  // [D][D]
+    float* mv = csm + D * D;           // [4][D] lane accumulators, then [4][D] rotation partials
+    float* ms = mv + 4 * D;            // [4] lane maxima (log2 units)
+    float* ls = ms + 4;                // [4] lane sums
+    float* acc = ls + 4;               // [D] the head's normalised accumulator
+    uint64_t* bar = (uint64_t*)(acc + D);
+    const int row = blockIdx.x, tid = threadIdx.x;
+    const int cl = tid / D, i = tid - cl * D;
+    const bool bulk = ((uintptr_t)a.piv & 15) == 0;
+    if (tid == 0) {
+        sm100::mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    // Pi_v before the wait, as in tqa_combine (same launch order, same invariant)
+    if (bulk && tid == 0) {
+        sm100::mbar_expect_tx(bar, D * D * 4);
+        sm100::bulk_load(pvs, a.piv, D * D * 4, bar);
+    }
+    pdl_begin();
+    if (!bulk)
+        for (int e = tid; e < D * D; e += 4 * D) pvs[e] = __ldg(a.piv + e);
+    const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
+    const int L = causal_len(a, s, t);
+    const int nc = min((L + a.ch - 1) / a.ch * a.spc, a.nch);
+    bool have_pv = !bulk;
+    for (int hk = 0; hk < hpc; ++hk) {
+        const int h = blockIdx.y * hpc + hk;
+        const float* ph = a.part + ((int64_t)row * a.hq + h) * a.nch * PART;
+        float m = -INFINITY, l = 0.0f, v = 0.0f;
+        for (int k0 = 0; cl + 4 * k0 < nc; k0 += 8) {
+            float m8[8], l8[8], v8[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int c = cl + 4 * (k0 + k);
+                const bool in = c < nc;
+                m8[k] = in ? ph[c * PART] * 1.4426950408889634f : -INFINITY;
+                l8[k] = in ? ph[c * PART + 1] : 0.0f;
+                v8[k] = in ? ph[c * PART + 2 + i] : 0.0f;
+            }
+            float bm = m8[0];
+#pragma unroll
+            for (int k = 1; k < 8; ++k) bm = fmaxf(bm, m8[k]);
+            if (bm > m) {  // m = -inf before: l and v are 0 and stay 0
+                const float f = ex2f(m - bm);
+                l *= f;
+                v *= f;
+                m = bm;
+            }
+            if (m > -INFINITY) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const float f = ex2f(m8[k] - m);
+                    l = fmaf(l8[k], f, l);
+                    v = fmaf(v8[k], f, v);
+                }
+            }
+        }
+        mv[cl * D + i] = v;
+        if (i == 0) {
+            ms[cl] = m;
+            ls[cl] = l;
+        }
+        __syncthreads();
+        if (cl == 0) {
+            const float M = fmaxf(fmaxf(ms[0], ms[1]), fmaxf(ms[2], ms[3]));
+            float lt = 0.0f, vt = 0.0f;
+            if (M > -INFINITY) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float f = ex2f(ms[k] - M);
+                    lt = fmaf(ls[k], f, lt);
+                    vt = fmaf(mv[k * D + i], f, vt);
+                }
+            }
+            acc[i] = lt > 0.0f ? vt / lt : 0.0f;
+        }
+        __syncthreads();
+        if (!have_pv) {
+            if (!stage_wait(bar)) return;
+            have_pv = true;
+        }
+        float o = 0.0f;
+#pragma unroll 8
+        for (int j = 32 * cl; j < 32 * cl + 32; ++j) o = fmaf(pvs[j * D + i], acc[j], o);
+        mv[cl * D + i] = o;
+        __syncthreads();
+        if (cl == 0) {
+            o = (mv[i] + mv[D + i]) + (mv[2 * D + i] + mv[3 * D + i]);
+            const int64_t e = ((int64_t)row * a.hq + h) * D + i;
+            if (a.dtype == FB_BF16) ((__nv_bfloat16*)a.out)[e] = __float2bfloat16_rn(o);
+            else ((__half*)a.out)[e] = __float2half_rn(o);
+        }
+        __syncthreads();  // mv, ms, ls and acc are reused by the next head
+    }
+}
+
+// One launch of the combine for the call's rows: tqa_combine_deep when one CTA per (row group,
+// KV head) would leave SMs idle and a row has more partials than tqa_combine requests at once
+// (its threads would wait on one round trip to memory after another), else tqa_combine.
 inline int launch_combine(const AttnArgs& a, int rows, cudaStream_t s) {
     const int G = a.hq / a.hkv;
+    if ((int64_t)rows * a.hkv < num_sms() && a.nch > 16) {
+        int hpc = 1;  // heads per CTA: at most two CTAs per SM
+        while ((int64_t)rows * a.hq / hpc > 2LL * num_sms() && hpc < G) hpc *= 2;
+        const size_t smem = (size_t)D * D * 4 + (4 * D + 8 + D) * 4 + 16;
+        cudaError_t e = cudaFuncSetAttribute(tqa_combine_deep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return (int)e;
+        launch_pdl_smem(tqa_combine_deep, dim3(rows, a.hq / hpc), dim3(4 * D), smem, s, a, hpc);
+        return (int)cudaGetLastError();
+    }
     const size_t smem = (size_t)D * D * 4 + (size_t)RQ * G * D * 4 + 16;
     const int rq = rows_per_cta(rows, a.hkv);
     void (*kern)(AttnArgs, int) = rq == 1 ? tqa_combine<1> : rq == 2 ? tqa_combine<2> : tqa_combine<4>;
@@ -900,8 +1025,28 @@ __global__ void __launch_bounds__(THREADS, 2) tqa_mma(AttnArgs a, Addr ad, int i
     }
 }
 
-size_t workspace_bytes(int64_t rows, int hq, int nch) {
+size_t workspace_bytes(int64_t rows, int hq, int64_t nch) {
     return (size_t)rows * hq * D * 4 + (size_t)rows * hq * nch * PART * 4;
+}
+
+// Partial slots per (row, head) a workspace is sized for: one per CH positions (the least any
+// call needs), and for calls with few query rows up to one per 32 positions, at most 160 over
+// the rows: the streamed kernel then splits a context into more, shorter chunks to give every
+// SM an item.
+int64_t partial_slots(int64_t rows, int max_kv_len) {
+    const int64_t nch = (max_kv_len + CH - 1) / CH;
+    if (rows <= 0) return nch;
+    return std::max<int64_t>(nch, std::min<int64_t>((max_kv_len + 31) / 32, 160 / rows));
+}
+
+// The slots a call uses: what a workspace of `bytes` holds past the rotated queries, capped at
+// partial_slots() so that the choice of chunks (and so the result) does not depend on how much
+// larger than that the caller made the workspace; at least nch (the entry points check that).
+int call_slots(size_t bytes, int64_t rows, int hq, int max_kv_len) {
+    const int64_t nch = (max_kv_len + CH - 1) / CH;
+    const size_t q = (size_t)rows * hq * D * 4, per = (size_t)rows * hq * PART * 4;
+    const int64_t held = bytes > q && per > 0 ? (int64_t)((bytes - q) / per) : 0;
+    return (int)std::max<int64_t>(nch, std::min<int64_t>(held, partial_slots(rows, max_kv_len)));
 }
 
 template <int KB, int VB, int G, typename Addr>
@@ -987,29 +1132,28 @@ inline void tc_chunks(AttnArgs& a, int64_t positions, int64_t rows) {
     a.nch = (int)((positions + a.ch - 1) / a.ch);
 }
 
-// tq_attention_stream.cu: the streamed tensor-core kernel for pool-backed caches.
+// tq_attention_stream.cu: the streamed tensor-core kernel (pools or per-block buffers).
 bool stream_ok(const AttnArgs& a, int kb, int vb, const PoolAddr& ad);
+bool stream_ok(const AttnArgs& a, int kb, int vb, const BlockPtrAddr& ad);
 int stream_launch(AttnArgs& a, int kb, int vb, const PoolAddr& ad, cudaStream_t s);
+int stream_launch(AttnArgs& a, int kb, int vb, const BlockPtrAddr& ad, cudaStream_t s);
 
 template <typename Addr>
 int run(AttnArgs a, int kb, int vb, const Addr& ad, cudaStream_t s) {
     const int rows = a.num_seqs * a.q_per_seq;
     if (rows == 0) return 0;
     a.spc = 1;
-    bool streamed = false;
-    if constexpr (std::is_same<Addr, PoolAddr>::value) streamed = a.nch > 0 && stream_ok(a, kb, vb, ad);
+    const bool streamed = a.nch > 0 && stream_ok(a, kb, vb, ad);
     a.qrot_f16 = streamed ? 1 : 0;
     int rc = launch_rotate(a, rows, s);
     if (rc) return rc;
     // a.nch counts CH-position chunks (the workspace is sized for them); the tensor-core
     // paths take larger chunks, so they use fewer of the same partial slots
     a.ch = CH;
-    if constexpr (std::is_same<Addr, PoolAddr>::value) {
-        if (streamed) {
-            rc = tq_count_path(10, stream_launch(a, kb, vb, ad, s));  // sets a.ch, a.spc, a.nch
-            if (rc) return rc;
-            return launch_combine(a, rows, s);
-        }
+    if (streamed) {
+        rc = tq_count_path(10, stream_launch(a, kb, vb, ad, s));  // sets a.ch, a.spc, a.nch
+        if (rc) return rc;
+        return launch_combine(a, rows, s);
     }
     if (tc_ok(kb, vb)) {
         tc_chunks(a, (int64_t)a.nch * CH, rows);
@@ -1041,8 +1185,12 @@ bool shape_ok(int hq, int hkv, int head_dim) {
 
 void set_last_error(const char* msg);
 
+// The least workspace a call takes, and the size that lets it use every partial slot it may.
 size_t tq_attention_ws_bytes(int64_t rows, int hq, int max_kv_len) {
     return tqa::workspace_bytes(rows, hq, (max_kv_len + tqa::CH - 1) / tqa::CH);
+}
+size_t tq_attention_ws_bytes_full(int64_t rows, int hq, int max_kv_len) {
+    return tqa::workspace_bytes(rows, hq, tqa::partial_slots(rows, max_kv_len));
 }
 
 // One sequence over the contiguous pools, with host scalars for its length and start (the
@@ -1077,6 +1225,7 @@ int tq_attention_one_seq(const void* q, int dtype, int num_tokens, int hq, int h
     a.qrot = (float*)workspace;
     a.part = a.qrot + (int64_t)num_tokens * hq * tqa::D;
     a.nch = (kv_len + tqa::CH - 1) / tqa::CH;
+    a.slots = tqa::call_slots(ws_bytes, num_tokens, hq, kv_len);
     a.out = out;
     tqa::PoolAddr ad{(const uint8_t*)kp, (const __half*)kn, (const uint8_t*)vp, (const __half*)vn, pool_rows};
     return tqa::run(a, kb, vb, ad, s);
@@ -1088,8 +1237,7 @@ using namespace fb;
 
 extern "C" size_t fb_tq_attention_workspace_bytes(int num_seqs, int q_per_seq, int num_q_heads, int max_kv_len) {
     if (num_seqs < 0 || q_per_seq < 0 || num_q_heads <= 0 || max_kv_len < 0) return 0;
-    const int nch = (max_kv_len + tqa::CH - 1) / tqa::CH;
-    return tqa::workspace_bytes((int64_t)num_seqs * q_per_seq, num_q_heads, nch);
+    return tq_attention_ws_bytes_full((int64_t)num_seqs * q_per_seq, num_q_heads, max_kv_len);
 }
 
 extern "C" int fb_launch_tq_attention_paged(const void* q, int dtype, int num_seqs, int q_per_seq, int num_q_heads,
@@ -1118,8 +1266,8 @@ extern "C" int fb_launch_tq_attention_paged(const void* q, int dtype, int num_se
     const int64_t rows = (int64_t)num_seqs * q_per_seq;
     if (rows > 65535 || nch > (1 << 30) || !workspace ||
         workspace_bytes < tqa::workspace_bytes(rows, num_q_heads, nch)) {
-        set_last_error("fb_launch_tq_attention_paged: workspace missing or smaller than "
-                       "fb_tq_attention_workspace_bytes(), or more than 65535 query rows");
+        set_last_error("fb_launch_tq_attention_paged: workspace missing or smaller than rows x heads x "
+                       "(512 + 520 x ceil(max_kv_len / 256)) bytes, or more than 65535 query rows");
         return (int)cudaErrorInvalidValue;
     }
     tqa::AttnArgs a{};
@@ -1140,6 +1288,7 @@ extern "C" int fb_launch_tq_attention_paged(const void* q, int dtype, int num_se
     a.qrot = (float*)workspace;
     a.part = a.qrot + rows * num_q_heads * tqa::D;
     a.nch = nch;
+    a.slots = tqa::call_slots(workspace_bytes, rows, num_q_heads, max_kv_len);
     a.out = output;
     tqa::PoolAddr ad{(const uint8_t*)k_packed_pool, (const __half*)k_norms_pool, (const uint8_t*)v_packed_pool,
                      (const __half*)v_norms_pool, num_pool_rows};
@@ -1156,8 +1305,8 @@ int ref_abi_check(const void* output, const void* q, const int* block_table, con
                   const float* k_rotation, const float* v_rotation, const float* k_centroids,
                   const float* v_centroids, int num_tokens, int num_q_heads, int num_kv_heads, int head_dim,
                   int kv_len, int start_pos, int key_bits, int value_bits, int k_packed_dim_per_head,
-                  int v_packed_dim_per_head, size_t* need) {
-    *need = 0;
+                  int v_packed_dim_per_head, size_t* need, size_t* want) {
+    *need = *want = 0;
     if (!tqa::shape_ok(num_q_heads, num_kv_heads, head_dim) || !tqa::bits_ok(key_bits) || !tqa::bits_ok(value_bits))
         return (int)cudaErrorInvalidValue;
     if (k_packed_dim_per_head != (head_dim * key_bits + 7) / 8 ||
@@ -1171,10 +1320,15 @@ int ref_abi_check(const void* output, const void* q, const int* block_table, con
         return (int)cudaErrorInvalidValue;
     const int nch = (kv_len + tqa::CH - 1) / tqa::CH;
     *need = tqa::workspace_bytes(num_tokens, num_q_heads, nch);
+    // the workspace for all the call's partial slots, but no larger than the no-allocation
+    // variant's scratch (unless the call needs more): both entry points then split a context into
+    // the same chunks and agree bit for bit
+    *want = std::max(*need, std::min(tq_attention_ws_bytes_full(num_tokens, num_q_heads, kv_len),
+                                     (size_t)FB_TQA_NOALLOC_SCRATCH_BYTES));
     return 0;
 }
 
-int ref_abi_run(void* ws, void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
+int ref_abi_run(void* ws, size_t ws_bytes, void* output, const void* q, const int* block_table, const void** k_packed_ptrs,
                 const void** k_norms_ptrs, const void** v_packed_ptrs, const void** v_norms_ptrs,
                 const float* k_rotation, const float* v_rotation, const float* k_centroids, const float* v_centroids,
                 int num_tokens, int num_q_heads, int num_kv_heads, int kv_len, int start_pos, int key_bits,
@@ -1197,6 +1351,7 @@ int ref_abi_run(void* ws, void* output, const void* q, const int* block_table, c
     a.qrot = (float*)ws;
     a.part = a.qrot + (int64_t)num_tokens * num_q_heads * tqa::D;
     a.nch = (kv_len + tqa::CH - 1) / tqa::CH;
+    a.slots = tqa::call_slots(ws_bytes, num_tokens, num_q_heads, kv_len);
     a.out = output;
     tqa::BlockPtrAddr ad{(const uint8_t* const*)k_packed_ptrs, (const __half* const*)k_norms_ptrs,
                          (const uint8_t* const*)v_packed_ptrs, (const __half* const*)v_norms_ptrs};
@@ -1214,14 +1369,14 @@ extern "C" int launch_attention_paged_tq(void* output, const void* q, const int*
                                          int num_q_heads, int num_kv_heads, int head_dim, int kv_len, int start_pos,
                                          int key_bits, int value_bits, int k_packed_dim_per_head,
                                          int v_packed_dim_per_head, void* stream) {
-    size_t need = 0;
+    size_t need = 0, want = 0;
     const int rc = ref_abi_check(output, q, block_table, k_packed_ptrs, k_norms_ptrs, v_packed_ptrs, v_norms_ptrs,
                                  k_rotation, v_rotation, k_centroids, v_centroids, num_tokens, num_q_heads,
                                  num_kv_heads, head_dim, kv_len, start_pos, key_bits, value_bits,
-                                 k_packed_dim_per_head, v_packed_dim_per_head, &need);
+                                 k_packed_dim_per_head, v_packed_dim_per_head, &need, &want);
     if (rc || num_tokens == 0) return rc;
-    return with_stream_workspace(stream, need, [&](void* ws) {
-        return ref_abi_run(ws, output, q, block_table, k_packed_ptrs, k_norms_ptrs, v_packed_ptrs, v_norms_ptrs,
+    return with_stream_workspace(stream, want, [&](void* ws) {
+        return ref_abi_run(ws, want, output, q, block_table, k_packed_ptrs, k_norms_ptrs, v_packed_ptrs, v_norms_ptrs,
                            k_rotation, v_rotation, k_centroids, v_centroids, num_tokens, num_q_heads, num_kv_heads,
                            kv_len, start_pos, key_bits, value_bits, stream);
     });
@@ -1278,11 +1433,11 @@ extern "C" int launch_attention_paged_tq_noalloc(void* output, const void* q, co
                                                  int num_q_heads, int num_kv_heads, int head_dim, int kv_len,
                                                  int start_pos, int key_bits, int value_bits,
                                                  int k_packed_dim_per_head, int v_packed_dim_per_head, void* stream) {
-    size_t need = 0;
+    size_t need = 0, want = 0;
     int rc = ref_abi_check(output, q, block_table, k_packed_ptrs, k_norms_ptrs, v_packed_ptrs, v_norms_ptrs,
                            k_rotation, v_rotation, k_centroids, v_centroids, num_tokens, num_q_heads, num_kv_heads,
                            head_dim, kv_len, start_pos, key_bits, value_bits, k_packed_dim_per_head,
-                           v_packed_dim_per_head, &need);
+                           v_packed_dim_per_head, &need, &want);
     if (rc || num_tokens == 0) return rc;
     if (need > kTqaNoAllocScratchBytes) {
         char msg[256];
@@ -1296,7 +1451,7 @@ extern "C" int launch_attention_paged_tq_noalloc(void* output, const void* q, co
     void* ws = nullptr;
     rc = tqa_noalloc_scratch(&ws);
     if (rc) return rc;
-    return ref_abi_run(ws, output, q, block_table, k_packed_ptrs, k_norms_ptrs, v_packed_ptrs, v_norms_ptrs,
+    return ref_abi_run(ws, kTqaNoAllocScratchBytes, output, q, block_table, k_packed_ptrs, k_norms_ptrs, v_packed_ptrs, v_norms_ptrs,
                        k_rotation, v_rotation, k_centroids, v_centroids, num_tokens, num_q_heads, num_kv_heads, kv_len,
                        start_pos, key_bits, value_bits, stream);
 }

@@ -39,7 +39,8 @@ struct AttnArgs {
     float* qrot;   // [rows, hq, D] f32, or f16 when qrot_f16 is set
     int qrot_f16;  // the rotate kernel writes q_rot as fp16 (the streamed kernel's input)
     float* part;   // [rows, hq, nch, PART]
-    int nch;       // partial slots per (row, head)
+    int nch;       // partial slots per (row, head): the layout's stride (CH-position chunks until a kernel sets its own)
+    int slots;     // partial slots per (row, head) the workspace holds (>= nch; the streamed kernel may use more chunks)
     int spc;       // partial slots per chunk (the streamed kernel writes one per block slot)
     int ch;        // positions per chunk
     int rnd;  // tensor-core kernel: rounds of four 16-position tiles per warp and item

@@ -1,7 +1,8 @@
 // Streamed tensor-core attention over the TurboQuant paged cache (2-, 4- and 8-bit codes), sm_100a.
 //
-// Replaces tqa_mma (2- and 4-bit codes) and tqa_chunk (8-bit codes) for caches in this library's
-// contiguous pools with a KV-head count that is a multiple of 8. The math is the same split-K statement
+// Replaces tqa_mma (2- and 4-bit codes) and tqa_chunk (8-bit codes) for caches with a KV-head count
+// that is a multiple of 8, in this library's contiguous pools or in the reference ABI's per-block
+// buffers (template PTRS: copied block by block with bulk copies). The math is the same split-K statement
 // (attention_paged_tq.cu:12-17 of the reference: scores in K's rotated space, softmax, values
 // summed in V's rotated space; tqa_combine adds the partials and rotates back), the operands
 // decoded the same way (lane-private lookup tables feeding mma.sync m16n8k16 with FP16
@@ -84,14 +85,15 @@ struct Layout {
 };
 
 // Shared memory other than the tables and stages: barriers, the producers' plans, the
-// consumers' weight tiles.
-template <int BPS>
+// consumers' weight tiles and, with per-block buffers (PTRS), the producers' block pointers.
+template <int BPS, bool PTRS>
 struct Small {
     static constexpr int NPW = 2 * BPS;
     static constexpr int bar_off = 0;                           // full[MAX_NST], empty[MAX_NST], abort flag
     static constexpr int plan_off = 256;                        // [NPW][MAX_SPI] int2
     static constexpr int p_off = plan_off + NPW * MAX_SPI * 8;  // [NCW][BPS][16 x 8] f16
-    static constexpr int bytes = (p_off + NCW * BPS * 256 + 1023) / 1024 * 1024;
+    static constexpr int ptr_off = p_off + NCW * BPS * 256;     // [NPW][MAX_SPI / BPS] (codes, norms) pointers
+    static constexpr int bytes = (ptr_off + (PTRS ? NPW * (MAX_SPI / BPS) * 16 : 0) + 1023) / 1024 * 1024;
 };
 
 struct Params {
@@ -104,6 +106,10 @@ struct Params {
     const __half* kn;              // norm pools (bulk copies when norms_bulk)
     const __half* vn;
     int norms_bulk;                // hkv == HC: a block's norms are contiguous
+    // per-block buffers (kernel template PTRS, the reference ABI's cache): block b's codes
+    // [16, hkv * P] at codes[side][b], its norms [16, hkv] at norms[side][b]; side 0 K, 1 V
+    const uint8_t* const* codes[2];
+    const __half* const* norms[2];
 };
 
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort) {
@@ -225,28 +231,31 @@ struct Places {
     int n_lo, nst;
     __device__ uint32_t stage(int i, int sb) const { return i < n_lo ? lo + i * sb : hi + (i - n_lo) * sb; }
 };
-template <int BPS>
+template <int SMALL_BYTES>
 __device__ __forceinline__ Places places(uint32_t base, int sb) {
     Places pl;
     pl.lo = (base + 1023u) & ~1023u;
     pl.hi = TAB + 0x10000u;
-    pl.small = ((base + DYN_BYTES) & ~1023u) - Small<BPS>::bytes;
+    pl.small = ((base + DYN_BYTES) & ~1023u) - SMALL_BYTES;
     pl.n_lo = pl.lo + sb <= TAB ? (int)((TAB - pl.lo) / sb) : 0;
     const int n_hi = pl.small >= pl.hi + sb ? (int)((pl.small - pl.hi) / sb) : 0;
     pl.nst = min(MAX_NST, pl.n_lo + n_hi);
     return pl;
 }
 
-template <int KB, int VB>
+// PTRS: the cache is the reference ABI's per-block buffers, a block's rows of one head group
+// copied by bulk copies into unswizzled stage rows; else the pools, copied by TMA boxes that land
+// with the 128-byte swizzle.
+template <int KB, int VB, bool PTRS>
 __global__ void __launch_bounds__(Layout<KB, VB>::THREADS, 1) tqa_stream(const __grid_constant__ Params P) {
     using Ly = Layout<KB, VB>;
     constexpr int PK = Ly::PK, PV = Ly::PV;
     constexpr int SB = Ly::stage_bytes;
     constexpr int BPS = Ly::BPS, NPW = Ly::NPW, THREADS = Ly::THREADS;
-    using Sm = Small<BPS>;
+    using Sm = Small<BPS, PTRS>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base = smem_u32(smem_raw);
-    const Places pl = places<BPS>(base, SB);
+    const Places pl = places<Sm::bytes>(base, SB);
     const AttnArgs& a = P.a;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = a.hq / a.hkv;
@@ -314,8 +323,11 @@ __global__ void __launch_bounds__(Layout<KB, VB>::THREADS, 1) tqa_stream(const _
         uint32_t sph = 0;
         long long issued = 0;
         bool ok = true;
-        // block-table entries of an item for this slot: lane l holds stages l, l + 32, ...
+        // block-table entries of an item for this slot: lane l holds stages l, l + 32, ... (with
+        // per-block buffers, also the blocks' code and norm pointers of this side)
         constexpr int NBT = MAX_SPI / BPS / 32;
+        constexpr int NBP = PTRS ? NBT : 1;
+        unsigned long long cp_next[NBP], np_next[NBP];
         auto fetch = [&](int item, int32_t (&bt)[NBT]) {
             Item it{};
             if (item < P.items) it = decode_item<BPS>(P, item);
@@ -326,13 +338,28 @@ __global__ void __launch_bounds__(Layout<KB, VB>::THREADS, 1) tqa_stream(const _
                             ? __ldg(a.block_tables + (int64_t)it.s * a.max_blocks + b)
                             : -1;
             }
+            if constexpr (PTRS) {
+#pragma unroll
+                for (int i = 0; i < NBT; ++i) {
+                    cp_next[i] = bt[i] >= 0 ? __ldg((const unsigned long long*)P.codes[side] + bt[i]) : 0ull;
+                    np_next[i] = bt[i] >= 0 ? __ldg((const unsigned long long*)P.norms[side] + bt[i]) : 0ull;
+                }
+            }
         };
         int32_t bt_next[NBT];
         fetch(blockIdx.x, bt_next);
         for (int item = blockIdx.x; item < P.items && ok; item += gridDim.x) {
             int32_t bt[NBT];
+            unsigned long long cps[NBP], nps[NBP];
 #pragma unroll
             for (int i = 0; i < NBT; ++i) bt[i] = bt_next[i];
+            if constexpr (PTRS) {
+#pragma unroll
+                for (int i = 0; i < NBT; ++i) {
+                    cps[i] = cp_next[i];
+                    nps[i] = np_next[i];
+                }
+            }
             const Item it = decode_item<BPS>(P, item);
             fetch(item + gridDim.x, bt_next);
             if (it.nstg == 0) continue;
@@ -347,9 +374,66 @@ __global__ void __launch_bounds__(Layout<KB, VB>::THREADS, 1) tqa_stream(const _
                 if (blk >= 0 && pos < it.L && first < P.pool_rows)
                     n = (int)min((int64_t)min(16, it.L - pos), P.pool_rows - first);
                 plan[st] = make_int2(n > 0 ? (int)first : 0, n);
+                if constexpr (PTRS)
+                    ((ulonglong2*)(gsmall + Sm::ptr_off))[p * (MAX_SPI / BPS) + st] = make_ulonglong2(cps[i], nps[i]);
             }
             __syncwarp();
-            if (lane == 0) {
+            if constexpr (PTRS) {
+                // The group's rows of a block: with 8 KV heads the whole buffers (one bulk copy for
+                // the codes, one for the norms), else 16 code rows and 16 norm rows, one copy per
+                // lane. A block whose buffers are not 16-byte aligned is copied by the lanes with
+                // byte loads and shared stores into the same unswizzled rows.
+                const ulonglong2* pp = (const ulonglong2*)(gsmall + Sm::ptr_off) + p * (MAX_SPI / BPS);
+                const uint32_t rb = HC * (side ? PV : PK);       // a stage row: the group's codes of a position
+                const uint32_t cb = 16u * rb;
+                const int64_t rs = (int64_t)a.hkv * (side ? PV : PK);  // a buffer row
+                const int64_t ns = (int64_t)a.hkv * 2;
+                const uint32_t cd0 = side ? Ly::v_off + slot * Ly::VBOX * 2048 : Ly::k_off + slot * Ly::KBOX * 2048;
+                const uint32_t nd0 = (side ? Ly::vn_off : Ly::kn_off) + slot * 16 * HC * 2;
+                for (int st = 0; st < it.nstg; ++st) {
+                    const int2 pn = plan[st];
+                    const ulonglong2 ptr = pp[st];
+                    if (lane == 0) ok = wait_bar(&empty[sidx], sph ^ 1u, abort);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) break;
+                    __syncwarp();  // every lane's writes into the stage come after lane 0's wait
+                    const uint32_t stg = pl.stage(sidx, SB);
+                    const uint32_t cd = stg + cd0, nd = stg + nd0;
+                    const uint8_t* cs = (const uint8_t*)ptr.x + (int64_t)it.hg * rb;
+                    const uint8_t* nsrc = (const uint8_t*)ptr.y + it.hg * HC * 2;
+                    const bool bulk = ((ptr.x | ptr.y) & 15ull) == 0;
+                    if (pn.y > 0 && !bulk) {
+                        for (uint32_t e = lane; e < cb; e += 32)
+                            asm volatile("st.shared.u8 [%0], %1;" ::"r"(cd + e), "h"((unsigned short)__ldg(cs + (e / rb) * rs + e % rb))
+                                         : "memory");
+                        for (uint32_t e = lane; e < 16u * HC * 2u; e += 32)
+                            asm volatile("st.shared.u8 [%0], %1;" ::"r"(nd + e), "h"((unsigned short)__ldg(nsrc + (e >> 4) * ns + (e & 15)))
+                                         : "memory");
+                        fence_async_smem();  // later bulk copies into these bytes come after the stores
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (side == 0) *(int*)(smem_raw + (stg - base) + Ly::hdr_off + 4 * slot) = pn.y;
+                        mbar_expect_tx(&full[sidx], pn.y > 0 && bulk ? cb + 16u * HC * 2u : 0u);
+                    }
+                    __syncwarp();
+                    if (pn.y > 0 && bulk) {
+                        if (a.hkv == HC) {
+                            if (lane == 0) bulk_load_u(cd, cs, cb, &full[sidx]);
+                            if (lane == 16) bulk_load_u(nd, nsrc, 16u * HC * 2u, &full[sidx]);
+                        } else if (lane < 16) {
+                            bulk_load_u(cd + lane * rb, cs + lane * rs, rb, &full[sidx]);
+                        } else {
+                            bulk_load_u(nd + (lane - 16) * 16, nsrc + (lane - 16) * ns, 16u, &full[sidx]);
+                        }
+                    }
+                    ++issued;
+                    if (++sidx == pl.nst) {
+                        sidx = 0;
+                        sph ^= 1u;
+                    }
+                }
+            } else if (lane == 0) {
                 for (int st = 0; st < it.nstg; ++st) {
                     const int2 pn = plan[st];
                     ok = wait_bar(&empty[sidx], sph ^ 1u, abort);
@@ -422,7 +506,15 @@ __global__ void __launch_bounds__(Layout<KB, VB>::THREADS, 1) tqa_stream(const _
     // chunks whose swizzle phases differ. koff2 / voff2 / voff3: the second 16 bytes of a K row
     // and the other two V rows of an 8-bit lane.
     uint32_t koff, koff2 = 0, voff0, voff1;
-    {
+    if constexpr (PTRS) {
+        // unswizzled rows of the group: K [16 positions][8 heads x PK], V [16][8 x PV]; the same
+        // bytes of a head as the swizzled layouts below give each lane
+        koff = Ly::k_off + r * HC * PK + hl * PK + (PK / 4) * t;
+        koff2 = koff + 16;
+        const int p0 = VB == 8 ? 2 * t : t, p1 = VB == 8 ? 2 * t + 1 : t + 4;
+        voff0 = Ly::v_off + p0 * HC * PV + hl * PV + (PV / 8) * r;
+        voff1 = Ly::v_off + p1 * HC * PV + hl * PV + (PV / 8) * r;
+    } else {
         constexpr int KL = Ly::KBOX, VL = Ly::VBOX;
         const int kc = (hl * PK) >> 7, kj = ((hl * PK) & 127) >> 4;
         if constexpr (KB == 8) {
@@ -449,8 +541,9 @@ __global__ void __launch_bounds__(Layout<KB, VB>::THREADS, 1) tqa_stream(const _
         }
     }
     constexpr uint32_t KSLOT = Ly::KBOX * 2048, VSLOT = Ly::VBOX * 2048, NSLOT = 16 * HC * 2;
-    // 8 rows further: row-major, 8 rows of lines; line-major, 8 rows of 128 bytes
-    constexpr uint32_t KROW8 = Ly::K8 ? 8 * 128 : 8 * Ly::KBOX * 128, VROW8 = Ly::V8 ? 8 * 128 : 8 * Ly::VBOX * 128;
+    // 8 rows further: row-major (swizzled or not), 8 rows of lines; line-major, 8 rows of 128 bytes
+    constexpr uint32_t KROW8 = Ly::K8 && !PTRS ? 8 * 128 : 8 * Ly::KBOX * 128;
+    constexpr uint32_t VROW8 = Ly::V8 && !PTRS ? 8 * 128 : 8 * Ly::VBOX * 128;
     const uint32_t knoff = Ly::kn_off + (r * HC + hl) * 2;
     const uint32_t vnoff = Ly::vn_off + (r * HC + hl) * 2;
     const int kr = Ly::V8 ? r : 2 * (r & 3) + (r >> 2);  // the value MMA's k index of tile row r (r + 8: kr + 8)
@@ -728,11 +821,15 @@ static bool encode_codes(CUtensorMap* map, const void* base, uint64_t row_bytes,
 
 }  // namespace stream
 
-// Positions per chunk for the streamed kernel: of 256, 512, 1024 and 2048, the one whose items
-// fill the persistent grid's waves best, the longer on a tie (one partial slot per chunk: at
-// most the workspace's one per 256 positions). Chunks that would leave a query row more than 32
-// partials are skipped while a longer chunk exists: the combine reads every partial of a row.
-static int stream_chunk(int64_t positions, int64_t rows, int ng, int sms) {
+// Positions per chunk for the streamed kernel. Of 256, 512, 1024 and 2048, the one whose items
+// fill the persistent grid's waves best, the longer on a tie (chunks that would leave a query row
+// more than 32 partials are skipped while a longer chunk exists: the combine reads every partial
+// of a row). When that leaves SMs without an item (few query rows over a context that is short, or
+// long and cut in few chunks), every power of two from 32 to 2048 whose chunk count the
+// workspace's slots hold is weighed instead by an estimate of its time: waves of items, each
+// taking its positions at a per-position cost plus a fixed cost (pipeline fill, partial write),
+// and the partials written and read again by the combine.
+static int stream_chunk(int64_t positions, int64_t rows, int ng, int hq, int sms, int64_t slots, int kb, int vb) {
     int best = 0;
     double best_eff = -1.0;
     for (int ch = 256; ch <= 2048; ch *= 2) {
@@ -745,44 +842,76 @@ static int stream_chunk(int64_t positions, int64_t rows, int ng, int sms) {
             best = ch;
         }
     }
+    if ((positions + best - 1) / best * rows * ng >= sms) return best;
+    const double tpos = (0.5 + (kb + vb) / 12.0) / 32.0;  // us per position of an item (8 KV heads)
+    const double fixed = 2.0;                            // us per item
+    const double part = 2.0 * PART * 4 / 3.0e6;          // us per partial (written, read; ~3 TB/s)
+    double best_t = 0.0;
+    best = 0;
+    for (int ch = 2048; ch >= 32; ch /= 2) {
+        const int64_t nchi = (positions + ch - 1) / ch;
+        if (nchi > slots) break;  // shorter chunks have more
+        const int64_t waves = (nchi * rows * ng + sms - 1) / sms;
+        const double t = (double)waves * (ch * tpos + fixed) + (double)(nchi * rows * hq) * part;
+        if (best == 0 || t < 0.98 * best_t) {  // a shorter chunk has to win by 2 %
+            best = ch;
+            best_t = t;
+        }
+    }
     return best;
 }
 
-// Whether the streamed kernel takes this call: 2-, 4- or 8-bit codes, KV heads a multiple of 8,
-// 16-byte aligned pools whose rows a TMA coordinate can reach.
-bool stream_ok(const AttnArgs& a, int kb, int vb, const PoolAddr& ad) {
+// Whether the streamed kernel takes this call: 2-, 4- or 8-bit codes, KV heads a multiple of 8;
+// with pools, 16-byte aligned ones whose rows a TMA coordinate can reach. (Per-block buffers are
+// checked block by block in the kernel: a block whose buffers are not 16-byte aligned is copied
+// without the bulk copies.)
+static bool stream_shape_ok(const AttnArgs& a, int kb, int vb) {
     const auto bits = [](int b) { return b == 2 || b == 4 || b == 8; };
     if (!bits(kb) || !bits(vb)) return false;
-    if (a.hkv % stream::HC != 0 || a.hq / a.hkv > MAXG) return false;
+    return a.hkv % stream::HC == 0 && a.hq / a.hkv <= MAXG;
+}
+bool stream_ok(const AttnArgs& a, int kb, int vb, const PoolAddr& ad) {
+    if (!stream_shape_ok(a, kb, vb)) return false;
     if (!aligned16(ad.kp) || !aligned16(ad.vp) || !aligned16(ad.kn) || !aligned16(ad.vn)) return false;
     return ad.pool_rows > 0 && ad.pool_rows <= INT32_MAX;
 }
+bool stream_ok(const AttnArgs& a, int kb, int vb, const BlockPtrAddr&) { return stream_shape_ok(a, kb, vb); }
 
-template <int KB, int VB>
-static int stream_launch_t(AttnArgs& a, const PoolAddr& ad, cudaStream_t s) {
+// One of pool / ptrs is given (PTRS selects which).
+template <int KB, int VB, bool PTRS>
+static int stream_launch_t(AttnArgs& a, const PoolAddr* pool, const BlockPtrAddr* ptrs, cudaStream_t s) {
     using Ly = stream::Layout<KB, VB>;
     const int rows = a.num_seqs * a.q_per_seq;
     const int ng = a.hkv / stream::HC;
     const int sms = num_sms();
-    const int64_t positions = (int64_t)a.nch * CH;  // the workspace holds a.nch slots, chunks of >= CH need no more
-    const int ch = stream_chunk(positions, rows, ng, sms);
+    const int64_t positions = (int64_t)a.nch * CH;  // the context rounded up to CH
+    const int ch = stream_chunk(positions, rows, ng, a.hq, sms, std::max(a.slots, a.nch), KB, VB);
     stream::Params P;
     memset(&P, 0, sizeof P);
-    const uint64_t prow = (uint64_t)ad.pool_rows;
-    if (!stream::encode_codes(&P.kmap, ad.kp, (uint64_t)a.hkv * Ly::PK, prow, Ly::KBOX, Ly::K8) ||
-        !stream::encode_codes(&P.vmap, ad.vp, (uint64_t)a.hkv * Ly::PV, prow, Ly::VBOX, Ly::V8) ||
-        !stream::encode_norms(&P.knmap, ad.kn, (uint64_t)a.hkv, prow) ||
-        !stream::encode_norms(&P.vnmap, ad.vn, (uint64_t)a.hkv, prow))
-        return (int)cudaErrorInvalidValue;
+    if constexpr (PTRS) {
+        P.codes[0] = ptrs->kp;
+        P.codes[1] = ptrs->vp;
+        P.norms[0] = ptrs->kn;
+        P.norms[1] = ptrs->vn;
+        P.pool_rows = INT64_MAX;  // every row of a listed block exists
+    } else {
+        const PoolAddr& ad = *pool;
+        const uint64_t prow = (uint64_t)ad.pool_rows;
+        if (!stream::encode_codes(&P.kmap, ad.kp, (uint64_t)a.hkv * Ly::PK, prow, Ly::KBOX, Ly::K8) ||
+            !stream::encode_codes(&P.vmap, ad.vp, (uint64_t)a.hkv * Ly::PV, prow, Ly::VBOX, Ly::V8) ||
+            !stream::encode_norms(&P.knmap, ad.kn, (uint64_t)a.hkv, prow) ||
+            !stream::encode_norms(&P.vnmap, ad.vn, (uint64_t)a.hkv, prow))
+            return (int)cudaErrorInvalidValue;
+        P.pool_rows = ad.pool_rows;
+        P.kn = ad.kn;
+        P.vn = ad.vn;
+        P.norms_bulk = a.hkv == stream::HC ? 1 : 0;
+    }
     const int nchi = (int)((positions + ch - 1) / ch);
     a.ch = ch;
     a.spc = 1;
     a.nch = nchi;
     P.a = a;
-    P.pool_rows = ad.pool_rows;
-    P.kn = ad.kn;
-    P.vn = ad.vn;
-    P.norms_bulk = a.hkv == stream::HC ? 1 : 0;
     P.spi = ch / (Ly::BPS * 16);
     P.nchi = nchi;
     P.ng = ng;
@@ -792,7 +921,7 @@ static int stream_launch_t(AttnArgs& a, const PoolAddr& ad, cudaStream_t s) {
     const int64_t items = (int64_t)a.num_seqs * nchi * a.q_per_seq * ng;
     if (items > INT32_MAX) return (int)cudaErrorInvalidValue;
     P.items = (int)items;
-    auto kern = stream::tqa_stream<KB, VB>;
+    auto kern = stream::tqa_stream<KB, VB, PTRS>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stream::DYN_BYTES);
     if (e != cudaSuccess) return (int)e;
     const int grid = (int)std::min<int64_t>(items, sms);
@@ -800,20 +929,30 @@ static int stream_launch_t(AttnArgs& a, const PoolAddr& ad, cudaStream_t s) {
     return (int)cudaGetLastError();
 }
 
+template <bool PTRS>
+static int stream_dispatch(AttnArgs& a, int kb, int vb, const PoolAddr* pool, const BlockPtrAddr* ptrs,
+                           cudaStream_t s) {
+    switch (kb * 10 + vb) {
+        case 22: return stream_launch_t<2, 2, PTRS>(a, pool, ptrs, s);
+        case 24: return stream_launch_t<2, 4, PTRS>(a, pool, ptrs, s);
+        case 28: return stream_launch_t<2, 8, PTRS>(a, pool, ptrs, s);
+        case 42: return stream_launch_t<4, 2, PTRS>(a, pool, ptrs, s);
+        case 44: return stream_launch_t<4, 4, PTRS>(a, pool, ptrs, s);
+        case 48: return stream_launch_t<4, 8, PTRS>(a, pool, ptrs, s);
+        case 82: return stream_launch_t<8, 2, PTRS>(a, pool, ptrs, s);
+        case 84: return stream_launch_t<8, 4, PTRS>(a, pool, ptrs, s);
+        default: return stream_launch_t<8, 8, PTRS>(a, pool, ptrs, s);
+    }
+}
+
 // Launches the streamed kernel for a call stream_ok() accepted.
 int stream_launch(AttnArgs& a, int kb, int vb, const PoolAddr& ad, cudaStream_t s) {
     if (!stream_ok(a, kb, vb, ad)) return (int)cudaErrorInvalidValue;
-    switch (kb * 10 + vb) {
-        case 22: return stream_launch_t<2, 2>(a, ad, s);
-        case 24: return stream_launch_t<2, 4>(a, ad, s);
-        case 28: return stream_launch_t<2, 8>(a, ad, s);
-        case 42: return stream_launch_t<4, 2>(a, ad, s);
-        case 44: return stream_launch_t<4, 4>(a, ad, s);
-        case 48: return stream_launch_t<4, 8>(a, ad, s);
-        case 82: return stream_launch_t<8, 2>(a, ad, s);
-        case 84: return stream_launch_t<8, 4>(a, ad, s);
-        default: return stream_launch_t<8, 8>(a, ad, s);
-    }
+    return stream_dispatch<false>(a, kb, vb, &ad, nullptr, s);
+}
+int stream_launch(AttnArgs& a, int kb, int vb, const BlockPtrAddr& ad, cudaStream_t s) {
+    if (!stream_ok(a, kb, vb, ad)) return (int)cudaErrorInvalidValue;
+    return stream_dispatch<true>(a, kb, vb, nullptr, &ad, s);
 }
 
 }  // namespace tqa

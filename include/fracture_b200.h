@@ -260,8 +260,12 @@ int fb_launch_tq_dequant_slots(const void* packed_pool, const void* norms_pool, 
  * fb_launch_tq_compress_paged writes them; query t of sequence s attends positions
  * [0, min(start_pos[s] + t + 1, kv_lens[s])) (device int32 arrays; max_kv_len bounds kv_lens).
  * Hq/Hkv in {1, 2, 4, 8}; key_bits/value_bits 2, 3, 4 or 8. `workspace` (16-byte aligned, at
- * least fb_tq_attention_workspace_bytes(num_seqs, q_per_seq, num_q_heads, max_kv_len) bytes)
- * holds the rotated queries and the split-K partial results (sized for 256-position chunks).
+ * least num_seqs * q_per_seq * num_q_heads * (512 + 520 * ceil(max_kv_len / 256)) bytes) holds the
+ * rotated queries and the split-K partial results, one per chunk of at least 256 positions.
+ * fb_tq_attention_workspace_bytes returns that, or more for calls with few query rows: room for
+ * up to one partial per 32 positions (at most 160 per head over the rows), with which the
+ * streamed kernel splits a short or sparsely batched context into more chunks to give every SM
+ * work. A workspace between the two sizes uses the slots it holds.
  * k_rotation 16-byte aligned. Numerics as for launch_attention_paged_tq. */
 size_t fb_tq_attention_workspace_bytes(int num_seqs, int q_per_seq, int num_q_heads, int max_kv_len);
 int fb_launch_tq_attention_paged(const void* q, int dtype, int num_seqs, int q_per_seq, int num_q_heads,

@@ -438,3 +438,130 @@ def test_streamed_kernel_every_chunk_length(kv_len, kb, vb):
     assert served == 1
     ops.assert_close_fp(got.float().cpu().numpy()[0], statement(c, qh[0], 0, kv_len, kv_len - 1), rel=2e-3,
                         min_cos=0.9999, label=f"kv {kv_len}", dtype="f16")
+
+
+# ── the streamed kernel through the reference ABI (per-block buffers, ffi.rs:251-274) ──
+
+def _scattered_block_buffers(c, nblocks, misalign):
+    """Each block's code and norm rows copied to its own place in one buffer per tensor, as a
+    cache of separate per-block allocations would hold them; with `misalign`, the odd blocks'
+    codes start 1 byte and their norms 2 bytes past a 16-byte boundary. Returns the buffers
+    (kept alive by the caller) and the four pointer arrays."""
+    keep, arrays = [], []
+    for name, shift in (("kp", 1), ("kn", 2), ("vp", 1), ("vn", 2)):
+        flat = c[name].view(torch.uint8).reshape(-1)
+        blk = flat.numel() // (c[name].shape[0] // 16)
+        stride = (blk + 31) // 32 * 32 + 32
+        buf = torch.zeros(nblocks * stride + 64, dtype=torch.uint8, device=DEV)
+        ptrs = []
+        for b in range(nblocks):
+            off = b * stride + (shift if misalign and b % 2 else 0)
+            buf[off:off + blk] = flat[b * blk:(b + 1) * blk]
+            ptrs.append(buf.data_ptr() + off)
+        keep.append(buf)
+        arrays.append(torch.tensor(ptrs, dtype=torch.int64, device=DEV))
+    return keep, arrays
+
+
+def _abi_call(c, q, kv_len, start, arrays, table):
+    """launch_attention_paged_tq on the given pointer arrays and block table (one sequence)."""
+    lib = _lib.load()
+    Tq, Hq, _ = q.shape
+    kp, kn, vp, vn = arrays
+    bt = torch.from_numpy(np.ascontiguousarray(table)).to(DEV)
+    out = torch.full((Tq, Hq, D), 7.0, dtype=torch.float16, device=DEV)
+    Pk, Pv = D * c["kb"] // 8, D * c["vb"] // 8
+    rc = lib.launch_attention_paged_tq(out.data_ptr(), q.data_ptr(), bt.data_ptr(), kp.data_ptr(), kn.data_ptr(),
+                                       vp.data_ptr(), vn.data_ptr(), c["pik"].data_ptr(), c["piv"].data_ptr(),
+                                       c["ck"].data_ptr(), c["cv"].data_ptr(), Tq, Hq, c["Hkv"], D, kv_len, start,
+                                       c["kb"], c["vb"], Pk, Pv, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == 0
+    return out
+
+
+@pytest.mark.parametrize("kb,vb,Hkv,Tq", [(4, 2, 8, 1), (8, 8, 8, 3), (2, 4, 8, 1), (4, 8, 8, 2), (8, 2, 8, 1),
+                                          (4, 4, 16, 2), (2, 2, 16, 1)])
+def test_reference_abi_streams_per_block_buffers(kb, vb, Hkv, Tq):
+    """With a multiple of 8 KV heads the reference ABI takes the streamed kernel, its blocks'
+    rows brought in by bulk copies from the per-block buffers (one per buffer with 8 KV heads,
+    one per row with 16): the batched pool entry's result bit for bit (the same chunks and
+    arithmetic), within the bar of the statement, over a context that ends inside a block."""
+    kv_len, G = 1500, 4
+    c = build_cache([kv_len], Hkv, kb, vb, seed=200 + kb + 3 * vb + Hkv)
+    qh, q = make_q(1, Tq, G * Hkv, "f16", seed=201)
+    ours = run_ours(c, q, [kv_len], [kv_len - Tq], "f16")
+    arrays = _block_pointer_arrays(c, int(c["tables"].max()) + 1)
+    abi, served = _run_counted("attention_streamed", lambda: _abi_call(c, q[0], kv_len, kv_len - Tq, arrays,
+                                                                         c["tables"][0]))
+    assert served == 1
+    assert torch.equal(abi, ours[0])
+    ops.assert_close_fp(abi.float().cpu().numpy(), statement(c, qh[0], 0, kv_len, kv_len - Tq), rel=2e-3,
+                        min_cos=0.9999, label="reference ABI, streamed", dtype="f16")
+
+
+@pytest.mark.parametrize("kb,vb,Hkv", [(4, 2, 8), (8, 8, 8), (4, 4, 16)])
+def test_reference_abi_streams_misaligned_block_buffers(kb, vb, Hkv):
+    """Per-block buffers in separate places, every other one not 16-byte aligned (codes 1 byte,
+    norms 2 bytes off): those blocks are copied by the producer lanes without bulk copies, the
+    others by bulk copies, within one call; a missing block (-1) is left out. Equal bit for bit
+    to the pool entry on the same cache and table."""
+    kv_len, Tq, G = 1100, 2, 4
+    c = build_cache([kv_len], Hkv, kb, vb, seed=210 + kb + vb + Hkv)
+    c["tables"][0, 5] = -1
+    qh, q = make_q(1, Tq, G * Hkv, "f16", seed=211)
+    ours = run_ours(c, q, [kv_len], [kv_len - Tq], "f16")
+    keep, arrays = _scattered_block_buffers(c, c["kp"].shape[0] // 16, misalign=True)
+    abi, served = _run_counted("attention_streamed", lambda: _abi_call(c, q[0], kv_len, kv_len - Tq, arrays,
+                                                                         c["tables"][0]))
+    assert served == 1
+    assert torch.equal(abi, ours[0])
+    ops.assert_close_fp(abi.float().cpu().numpy(), statement(c, qh[0], 0, kv_len, kv_len - Tq), rel=2e-3,
+                        min_cos=0.9999, label="misaligned per-block buffers", dtype="f16")
+    del keep
+
+
+def _least_workspace(S, Tq, Hq, max_kv_len):
+    """The least workspace the batched entry accepts: rotated queries and one partial per
+    256-position chunk (fb_tq_attention_workspace_bytes gives more to calls with few rows)."""
+    return S * Tq * Hq * (D * 4 + (D + 2) * 4 * ((max_kv_len + 255) // 256))
+
+
+def test_workspace_sizing_gives_few_rows_finer_chunks():
+    """fb_tq_attention_workspace_bytes: the least size for many rows, and up to one partial per
+    32 positions (at most 160 per head over the rows) for few."""
+    Hq = 32
+    assert K.tq_attention_workspace_bytes(64, 1, Hq, 8192) == _least_workspace(64, 1, Hq, 8192)
+    assert K.tq_attention_workspace_bytes(1, 1, Hq, 8192) == Hq * (D * 4 + (D + 2) * 4 * 160)
+    assert K.tq_attention_workspace_bytes(1, 1, Hq, 1000) == Hq * (D * 4 + (D + 2) * 4 * 32)
+    assert K.tq_attention_workspace_bytes(2, 1, Hq, 100000) == _least_workspace(2, 1, Hq, 100000)
+
+
+@pytest.mark.parametrize("kv_lens,Tq,kb,vb", [([8192], 1, 4, 2), ([1000], 1, 2, 4), ([3000, 77], 2, 8, 8),
+                                               ([20000], 1, 4, 4)])
+def test_streamed_kernel_few_rows_split_finer(kv_lens, Tq, kb, vb):
+    """Few query rows: the streamed kernel cuts the context into chunks as short as 32 positions
+    (one stage) so that every SM has an item, up to 160 partials per head; the same call with the
+    least workspace keeps 256-position or longer chunks. Both meet the bar against the statement."""
+    Hkv, G = 8, 4
+    c = build_cache(kv_lens, Hkv, kb, vb, seed=220 + kb + vb + len(kv_lens))
+    qh, q = make_q(len(kv_lens), Tq, G * Hkv, "f16", seed=221)
+    starts = [L - Tq for L in kv_lens]
+    S, Hq, L = len(kv_lens), G * Hkv, max(kv_lens)
+    for ws_bytes in (K.tq_attention_workspace_bytes(S, Tq, Hq, L), _least_workspace(S, Tq, Hq, L)):
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=DEV)
+        out = torch.full(q.shape, 7.0, dtype=torch.float16, device=DEV)
+
+        def call():
+            K.tq_attention_paged(q, c["kp"], c["kn"], c["vp"], c["vn"], torch.from_numpy(c["tables"]).to(DEV),
+                                 torch.tensor(kv_lens, dtype=torch.int32, device=DEV),
+                                 torch.tensor(starts, dtype=torch.int32, device=DEV), c["pik"], c["piv"], c["ck"],
+                                 c["cv"], kb, vb, out, max_kv_len=L, workspace=ws)
+            torch.cuda.synchronize()
+
+        _, served = _run_counted("attention_streamed", call)
+        assert served == 1
+        got = out.float().cpu().numpy()
+        for s, Ls in enumerate(kv_lens):
+            ops.assert_close_fp(got[s], statement(c, qh[s], s, Ls, starts[s]), rel=2e-3, min_cos=0.9999,
+                                label=f"ws {ws_bytes} seq {s} (kv {Ls})", dtype="f16")
