@@ -822,6 +822,91 @@ def run_tq_attention(args, local_rank: int) -> dict:
             "l2": "the 420 MB cache is larger than L2 (no flush)"}
 
 
+def run_tq_attention_abi(args, local_rank: int, steps: int = 0) -> dict:
+    """The reference ABI's call (launch_attention_paged_tq, ffi.rs:251-274: one sequence, FP16,
+    per-block pointer arrays), as CudaBackend::attention_paged_tq makes it once per sequence and
+    layer: one decode token at the end of a 32768-token context, 32 Q / 8 KV heads x 128, K 4-bit /
+    V 2-bit. Twenty layers' caches (26 MB each, 529 MB in all: more than L2) sit in one pool, their
+    blocks shuffled and addressed through per-layer pointer arrays; one step = one call, and
+    consecutive calls go to consecutive layers, as a decode step's do. Timed as twenty calls (one
+    per layer) captured in a CUDA graph and replayed, so that no host time sits between calls (the
+    figure is GPU time per call). Codes and norms are random bytes and values: the kernels' work
+    does not depend on them."""
+    import torch
+
+    from fracture_b200 import _lib
+    from fracture_b200 import kernels as K
+
+    dev = torch.device("cuda", local_rank)
+    L, HQ, HKV, D, KB, VB, NL = 32768, NQ, NKV, HD, 4, 2, 20
+    nblk = L // 16
+    Pk, Pv = D * KB // 8, D * VB // 8
+    g = torch.Generator(device=dev).manual_seed(11)
+    rows = NL * L
+    kp = torch.randint(0, 256, (rows, HKV * Pk), dtype=torch.uint8, device=dev, generator=g)
+    vp = torch.randint(0, 256, (rows, HKV * Pv), dtype=torch.uint8, device=dev, generator=g)
+    kn = (torch.rand((rows, HKV), generator=g, device=dev) + 0.5).half()
+    vn = (torch.rand((rows, HKV), generator=g, device=dev) + 0.5).half()
+    perm = torch.randperm(NL * nblk, generator=g, device=dev).to(torch.int64)
+    pik, piv = (torch.from_numpy(K.tq_rotation_matrix(D, sd)).to(dev) for sd in (42, 542))
+    ck, cv = (torch.from_numpy(K.tq_codebook(D, b)[0]).to(dev) for b in (KB, VB))
+    layers = []
+    for layer in range(NL):  # layer l: its own blocks, block b at entry b of its pointer arrays
+        blocks = perm[layer * nblk:(layer + 1) * nblk]
+        arr = lambda t, row: t.data_ptr() + blocks * (16 * row)
+        layers.append((arr(kp, HKV * Pk), arr(kn, HKV * 2), arr(vp, HKV * Pv), arr(vn, HKV * 2)))
+    table = torch.arange(nblk, dtype=torch.int32, device=dev)
+    q = torch.randn((1, HQ, D), generator=g, device=dev).half()
+    out = torch.empty_like(q)
+    lib = _lib.load()
+    side = torch.cuda.Stream(dev)
+
+    def call(layer):
+        kpa, kna, vpa, vna = layers[layer]
+        rc = lib.launch_attention_paged_tq(out.data_ptr(), q.data_ptr(), table.data_ptr(), kpa.data_ptr(),
+                                           kna.data_ptr(), vpa.data_ptr(), vna.data_ptr(), pik.data_ptr(),
+                                           piv.data_ptr(), ck.data_ptr(), cv.data_ptr(), 1, HQ, HKV, D, L, L - 1,
+                                           KB, VB, Pk, Pv, torch.cuda.current_stream(dev).cuda_stream)
+        if rc:
+            raise RuntimeError(f"launch_attention_paged_tq: {rc}")
+
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(max(args.warmup, 3)):  # the first call sizes the library workspace
+            call(i % NL)
+    torch.cuda.synchronize(dev)
+    if steps:  # profile mode: eager calls only
+        for i in range(steps):
+            call(i % NL)
+        torch.cuda.synchronize(dev)
+        return {}
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for layer in range(NL):
+            call(layer)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    cur = torch.cuda.current_stream(dev)  # replays run on the current stream
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record(cur)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(cur)
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1000.0 / (reps * NL)
+    by = L * HKV * (Pk + Pv + 4) + 2 * HQ * D * 2 + nblk * (4 + 4 * 8) + 2 * D * D * 4
+    del graph
+    pk = peaks()
+    return {"workload": "reference ABI call (launch_attention_paged_tq): 1 sequence x 1 decode token, context 32768, "
+                        "32 Q / 8 KV heads x 128, K 4-bit / V 2-bit, per-block pointer arrays; 20 layers' caches, "
+                        "one call per layer in turn",
+            "us_per_call": round(us, 2), "algorithmic_bytes_per_call": by,
+            "achieved_gbs": round(by / us / 1e3, 1), "frac_of_peak": round(by / us / 1e3 / pk["hbm_gbs"], 4),
+            "timing": "20 calls (one per layer, 529 MB of caches: more than L2) in one CUDA graph, 10 replays; "
+                      "GPU time per call"}
+
+
 def run_attention_fp16(args, local_rank: int) -> dict:
     """The same decode attention over the uncompressed FP16 paged cache (PagedKvCacheManager's
     path): 64 sequences x 1 query token at the end of an 8192-token context, 32 Q / 8 KV heads x
@@ -933,6 +1018,10 @@ def profile_kernel(args) -> None:
 
     from fracture_b200 import kernels as K
 
+    if args.profile_kernel == "tq_attention_abi":  # W warm-up calls + 1, eager
+        run_tq_attention_abi(args, 0, steps=1)
+        print(json.dumps({"kernel": args.profile_kernel}))
+        return
     if args.profile_kernel in ("tq_attention", "attention_fp16"):  # the bench's workload, W warm-ups + 1
         args.steps = 1
         fn = run_tq_attention if args.profile_kernel == "tq_attention" else run_attention_fp16
@@ -1038,7 +1127,8 @@ def main() -> None:
     ap.add_argument("--only", default=None, choices=["tq", "decode", "attention"],
                     help="run only this workload on one GPU and print its figures")
     ap.add_argument("--profile-kernel", default=None, choices=["silu_mul", "add_rmsnorm", "rope", "embedding", "tq_compress",
-                                                                   "tq_dequant", "tq_attention", "attention_fp16",
+                                                                   "tq_dequant", "tq_attention", "tq_attention_abi",
+                                                                   "attention_fp16",
                                                                    "tq_small_compress", "tq_small_dequant"],
                     help="run only this kernel at its config-3 size (W warm-up launches + 1), for ncu captures")
     args = ap.parse_args()
@@ -1053,6 +1143,7 @@ def main() -> None:
     if args.only:  # one workload on one GPU, printed alone (development runs; not the driver's line)
         fn = {"tq": lambda: run_tq_config4(args, 0, 1, local_rank), "decode": lambda: run_config2(args, local_rank),
               "attention": lambda: {"tq": run_tq_attention(args, local_rank),
+                                    "tq_abi": run_tq_attention_abi(args, local_rank),
                                     "fp16": run_attention_fp16(args, local_rank)}}[args.only]
         print(json.dumps({"only": args.only, **fn()}), flush=True)
         return
@@ -1086,6 +1177,7 @@ def main() -> None:
         res["decode_config2"] = run_config2(args, local_rank)
     if res is not None and world == 1 and not args.no_attention:
         res["tq_attention"] = run_tq_attention(args, local_rank)
+        res["tq_attention_abi"] = run_tq_attention_abi(args, local_rank)
         res["attention_fp16"] = run_attention_fp16(args, local_rank)
     if res is not None:
         if world == 1 and not args.no_cpu_baseline:
