@@ -574,7 +574,7 @@ __global__ void __launch_bounds__(4 * D) tqa_combine(AttnArgs a, int rows) {
 // The combine for calls with few rows: one CTA per (query row, HPC Q heads), so that a call of
 // one or a few rows still spreads over many SMs, and the partials of a head split over the four
 // 128-thread chunk lanes (lane k takes chunks k, k + 4, ...), each keeping a running maximum, sum
-// and accumulator (eight chunks' loads in flight at a time), merged through shared memory. Then
+// and accumulator (eight or sixteen chunks' loads in flight at a time), merged through shared memory. Then
 // as tqa_combine: divide by the sum, rotate back by Pi_v (the four lanes each take 32 of the 128
 // terms), convert.
 __global__ void __launch_bounds__(4 * D) tqa_combine_deep(AttnArgs a, int hpc) {
@@ -605,14 +605,14 @@ __global__ void __launch_bounds__(4 * D) tqa_combine_deep(AttnArgs a, int hpc) {
     const int L = causal_len(a, s, t);
     const int nc = min((L + a.ch - 1) / a.ch * a.spc, a.nch);
     bool have_pv = !bulk;
-    for (int hk = 0; hk < hpc; ++hk) {
-        const int h = blockIdx.y * hpc + hk;
-        const float* ph = a.part + ((int64_t)row * a.hq + h) * a.nch * PART;
-        float m = -INFINITY, l = 0.0f, v = 0.0f;
-        for (int k0 = 0; cl + 4 * k0 < nc; k0 += 8) {
-            float m8[8], l8[8], v8[8];
+    // a lane's chunks, DB at a time with their loads in flight together: 16 when a lane has more
+    // than 8 (fewer round trips), else 8 (no loads masked off)
+    auto merge = [&](auto dbc, const float* ph, float& m, float& l, float& v) {
+        constexpr int DB = decltype(dbc)::value;
+        for (int k0 = 0; cl + 4 * k0 < nc; k0 += DB) {
+            float m8[DB], l8[DB], v8[DB];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
+            for (int k = 0; k < DB; ++k) {
                 const int c = cl + 4 * (k0 + k);
                 const bool in = c < nc;
                 m8[k] = in ? ph[c * PART] * 1.4426950408889634f : -INFINITY;
@@ -621,7 +621,7 @@ __global__ void __launch_bounds__(4 * D) tqa_combine_deep(AttnArgs a, int hpc) {
             }
             float bm = m8[0];
 #pragma unroll
-            for (int k = 1; k < 8; ++k) bm = fmaxf(bm, m8[k]);
+            for (int k = 1; k < DB; ++k) bm = fmaxf(bm, m8[k]);
             if (bm > m) {  // m = -inf before: l and v are 0 and stay 0
                 const float f = ex2f(m - bm);
                 l *= f;
@@ -630,13 +630,20 @@ __global__ void __launch_bounds__(4 * D) tqa_combine_deep(AttnArgs a, int hpc) {
             }
             if (m > -INFINITY) {
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
+                for (int k = 0; k < DB; ++k) {
                     const float f = ex2f(m8[k] - m);
                     l = fmaf(l8[k], f, l);
                     v = fmaf(v8[k], f, v);
                 }
             }
         }
+    };
+    for (int hk = 0; hk < hpc; ++hk) {
+        const int h = blockIdx.y * hpc + hk;
+        const float* ph = a.part + ((int64_t)row * a.hq + h) * a.nch * PART;
+        float m = -INFINITY, l = 0.0f, v = 0.0f;
+        if (nc > 32) merge(std::integral_constant<int, 16>{}, ph, m, l, v);
+        else merge(std::integral_constant<int, 8>{}, ph, m, l, v);
         mv[cl * D + i] = v;
         if (i == 0) {
             ms[cl] = m;
