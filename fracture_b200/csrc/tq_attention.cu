@@ -150,8 +150,50 @@ __global__ void __launch_bounds__(D) tqa_rotate_q(const __grid_constant__ Rotate
     }
 }
 
+// For calls with few rows: CTA (row, group g, slice z) computes coordinates 32z .. 32z + 31 of the
+// G heads of KV group g, so that the launch spreads over four times as many SMs and each CTA
+// reads a quarter of Pi_k. Thread (h, i) = (tid / 32, tid % 32) computes coordinate 32z + i of
+// head h; its Pi_k row sits in shared memory at a stride of D + 4 floats (the 16-byte reads of
+// a quarter-warp fall in different banks), the head's query is read by the whole warp at once.
+__global__ void __launch_bounds__(8 * 32) tqa_rotate_q_slice(AttnArgs a) {
+    __shared__ __align__(16) float pis[32][D + 4];
+    __shared__ __align__(16) float qs[MAXG][D];
+    const int row = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
+    const int G = a.hq / a.hkv, tid = threadIdx.x, h = tid >> 5, i = tid & 31;
+    pdl_begin();
+    // the slice of Pi_k: 32 rows of 512 bytes, 16 bytes per thread and step
+    for (int e = tid; e < 32 * D / 4; e += blockDim.x) {
+        const int r = e / (D / 4), c = e - r * (D / 4);
+        const uint32_t dst = smem_addr(&pis[r][4 * c]);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(a.pik + (int64_t)(32 * z + r) * D + 4 * c)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int e = tid; e < G * D; e += blockDim.x)
+        qs[e / D][e % D] = load_q(a, ((int64_t)row * a.hq + g * G) * D + e);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int m = 0; m < D / 4; ++m) {
+        const float4 p = *(const float4*)&pis[i][4 * m];
+        const float4 x = *(const float4*)&qs[h][4 * m];
+        acc = fmaf(p.x, x.x, acc);
+        acc = fmaf(p.y, x.y, acc);
+        acc = fmaf(p.z, x.z, acc);
+        acc = fmaf(p.w, x.w, acc);
+    }
+    const int64_t o = ((int64_t)row * a.hq + g * G + h) * D + 32 * z + i;
+    if (a.qrot_f16) ((__half*)a.qrot)[o] = __float2half_rn(acc);
+    else a.qrot[o] = acc;
+}
+
 // One launch of tqa_rotate_q for the call's rows (Pi_k 16-byte aligned, as every entry point checks).
 inline int launch_rotate(const AttnArgs& a, int rows, cudaStream_t s) {
+    if ((int64_t)rows * a.hkv * 4 <= 2LL * num_sms()) {  // few rows: four slices per (row, group)
+        launch_pdl_smem(tqa_rotate_q_slice, dim3(rows, a.hkv, 4), dim3(32 * (a.hq / a.hkv)), 0, s, a);
+        return (int)cudaGetLastError();
+    }
     auto encode = sm100::tensor_map_encoder();
     if (!encode) return (int)cudaErrorNotSupported;
     RotateParams R;
