@@ -614,18 +614,19 @@ __global__ void __launch_bounds__(4 * D) tqa_combine(AttnArgs a, int rows) {
 }
 
 // The combine for calls with few rows: one CTA per (query row, HPC Q heads), so that a call of
-// one or a few rows still spreads over many SMs, and the partials of a head split over the four
-// 128-thread chunk lanes (lane k takes chunks k, k + 4, ...), each keeping a running maximum, sum
+// one or a few rows still spreads over many SMs, and the partials of a head split over the CL
+// (4 or 8) 128-thread chunk lanes (lane k takes chunks k, k + CL, ...), each keeping a running maximum, sum
 // and accumulator (eight or sixteen chunks' loads in flight at a time), merged through shared memory. Then
-// as tqa_combine: divide by the sum, rotate back by Pi_v (the four lanes each take 32 of the 128
+// as tqa_combine: divide by the sum, rotate back by Pi_v (the CL lanes each take 128 / CL of the 128
 // terms), convert.
-__global__ void __launch_bounds__(4 * D) tqa_combine_deep(AttnArgs a, int hpc) {
+template <int CL>
+__global__ void __launch_bounds__(CL * D) tqa_combine_deep(AttnArgs a, int hpc) {
     extern __shared__ __align__(16) float csm[];
     float* pvs = csm;                  // [D][D]
-    float* mv = csm + D * D;           // [4][D] lane accumulators, then [4][D] rotation partials
-    float* ms = mv + 4 * D;            // [4] lane maxima (log2 units)
-    float* ls = ms + 4;                // [4] lane sums
-    float* acc = ls + 4;               // [D] the head's normalised accumulator
+    float* mv = csm + D * D;           // [CL][D] lane accumulators, then [CL][D] rotation partials
+    float* ms = mv + CL * D;           // [CL] lane maxima (log2 units)
+    float* ls = ms + CL;               // [CL] lane sums
+    float* acc = ls + CL;              // [D] the head's normalised accumulator
     uint64_t* bar = (uint64_t*)(acc + D);
     const int row = blockIdx.x, tid = threadIdx.x;
     const int cl = tid / D, i = tid - cl * D;
@@ -642,7 +643,7 @@ __global__ void __launch_bounds__(4 * D) tqa_combine_deep(AttnArgs a, int hpc) {
     }
     pdl_begin();
     if (!bulk)
-        for (int e = tid; e < D * D; e += 4 * D) pvs[e] = __ldg(a.piv + e);
+        for (int e = tid; e < D * D; e += CL * D) pvs[e] = __ldg(a.piv + e);
     const int s = row / a.q_per_seq, t = row - s * a.q_per_seq;
     const int L = causal_len(a, s, t);
     const int nc = min((L + a.ch - 1) / a.ch * a.spc, a.nch);
@@ -651,11 +652,11 @@ __global__ void __launch_bounds__(4 * D) tqa_combine_deep(AttnArgs a, int hpc) {
     // than 8 (fewer round trips), else 8 (no loads masked off)
     auto merge = [&](auto dbc, const float* ph, float& m, float& l, float& v) {
         constexpr int DB = decltype(dbc)::value;
-        for (int k0 = 0; cl + 4 * k0 < nc; k0 += DB) {
+        for (int k0 = 0; cl + CL * k0 < nc; k0 += DB) {
             float m8[DB], l8[DB], v8[DB];
 #pragma unroll
             for (int k = 0; k < DB; ++k) {
-                const int c = cl + 4 * (k0 + k);
+                const int c = cl + CL * (k0 + k);
                 const bool in = c < nc;
                 m8[k] = in ? ph[c * PART] * 1.4426950408889634f : -INFINITY;
                 l8[k] = in ? ph[c * PART + 1] : 0.0f;
@@ -684,7 +685,7 @@ __global__ void __launch_bounds__(4 * D) tqa_combine_deep(AttnArgs a, int hpc) {
         const int h = blockIdx.y * hpc + hk;
         const float* ph = a.part + ((int64_t)row * a.hq + h) * a.nch * PART;
         float m = -INFINITY, l = 0.0f, v = 0.0f;
-        if (nc > 32) merge(std::integral_constant<int, 16>{}, ph, m, l, v);
+        if (nc > 8 * CL) merge(std::integral_constant<int, 16>{}, ph, m, l, v);
         else merge(std::integral_constant<int, 8>{}, ph, m, l, v);
         mv[cl * D + i] = v;
         if (i == 0) {
@@ -693,11 +694,13 @@ __global__ void __launch_bounds__(4 * D) tqa_combine_deep(AttnArgs a, int hpc) {
         }
         __syncthreads();
         if (cl == 0) {
-            const float M = fmaxf(fmaxf(ms[0], ms[1]), fmaxf(ms[2], ms[3]));
+            float M = ms[0];
+#pragma unroll
+            for (int k = 1; k < CL; ++k) M = fmaxf(M, ms[k]);
             float lt = 0.0f, vt = 0.0f;
             if (M > -INFINITY) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < CL; ++k) {
                     const float f = ex2f(ms[k] - M);
                     lt = fmaf(ls[k], f, lt);
                     vt = fmaf(mv[k * D + i], f, vt);
@@ -711,12 +714,15 @@ __global__ void __launch_bounds__(4 * D) tqa_combine_deep(AttnArgs a, int hpc) {
             have_pv = true;
         }
         float o = 0.0f;
+        constexpr int JL = D / CL;  // terms of the rotation per lane
 #pragma unroll 8
-        for (int j = 32 * cl; j < 32 * cl + 32; ++j) o = fmaf(pvs[j * D + i], acc[j], o);
+        for (int j = JL * cl; j < JL * cl + JL; ++j) o = fmaf(pvs[j * D + i], acc[j], o);
         mv[cl * D + i] = o;
         __syncthreads();
         if (cl == 0) {
-            o = (mv[i] + mv[D + i]) + (mv[2 * D + i] + mv[3 * D + i]);
+            o = mv[i];
+#pragma unroll
+            for (int k = 1; k < CL; ++k) o += mv[k * D + i];
             const int64_t e = ((int64_t)row * a.hq + h) * D + i;
             if (a.dtype == FB_BF16) ((__nv_bfloat16*)a.out)[e] = __float2bfloat16_rn(o);
             else ((__half*)a.out)[e] = __float2half_rn(o);
@@ -733,10 +739,15 @@ inline int launch_combine(const AttnArgs& a, int rows, cudaStream_t s) {
     if ((int64_t)rows * a.hkv < num_sms() && a.nch > 16) {
         int hpc = 1;  // heads per CTA: at most two CTAs per SM
         while ((int64_t)rows * a.hq / hpc > 2LL * num_sms() && hpc < G) hpc *= 2;
-        const size_t smem = (size_t)D * D * 4 + (4 * D + 8 + D) * 4 + 16;
-        cudaError_t e = cudaFuncSetAttribute(tqa_combine_deep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        // eight chunk lanes when the CTAs fill at most half the SMs and a row has 64 chunks or
+        // more (one round of loads per lane), else four
+        const bool wide = (int64_t)rows * a.hq / hpc * 2 <= num_sms() && a.nch >= 64;
+        const int cl = wide ? 8 : 4;
+        auto kern = wide ? tqa_combine_deep<8> : tqa_combine_deep<4>;
+        const size_t smem = (size_t)D * D * 4 + (size_t)(cl * D + 2 * cl + D) * 4 + 16;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return (int)e;
-        launch_pdl_smem(tqa_combine_deep, dim3(rows, a.hq / hpc), dim3(4 * D), smem, s, a, hpc);
+        launch_pdl_smem(kern, dim3(rows, a.hq / hpc), dim3(cl * D), smem, s, a, hpc);
         return (int)cudaGetLastError();
     }
     const size_t smem = (size_t)D * D * 4 + (size_t)RQ * G * D * 4 + 16;
