@@ -10,7 +10,9 @@ residual-add+RMSNorm, SwiGLU silu*mul; a final fused add+norm. Activations are
 synthetic N(0,1) with 0.1% of the channels scaled x20; the GEMM outputs that
 feed the chain (o_proj, down_proj, q/k, gate/up) are synthetic tensors of their
 real shapes. Every tensor the chain streams is larger than L2, so no L2 flush
-is needed between steps.
+is needed between steps. A timed step is one replay of the step's 130 launches
+captured as one CUDA graph; the same steps launched one kernel at a time from
+the host are in the line as ``eager``.
 
 Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): the job's 16
 sequences are split over the ranks (16/N per GPU; sequences are independent, so
@@ -173,49 +175,75 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     launches_per_step = 1 + 1 + (2 * LAYERS - 1) + LAYERS + LAYERS + 1
 
-    def step(d, silu_events=None):
+    def step(d, st, silu_events=None):
+        """One step of the chain on the raw stream handle ``st``; with ``silu_events`` (a list of
+        LAYERS event pairs), each silu_mul launch is bracketed by its pair."""
         h, normed = d["h"], d["normed"]
-        K.embedding(h, d["table"], d["ids"], stream=s)
+        K.embedding(h, d["table"], d["ids"], stream=st)
         for l in range(LAYERS):
             if l == 0:
-                K.rmsnorm(normed, h, d["wa"][0], EPS, stream=s)
+                K.rmsnorm(normed, h, d["wa"][0], EPS, stream=st)
             else:
-                K.add_rmsnorm(h, d["ffn_out"], d["wa"][l], normed, EPS, stream=s)
-            K.rope(d["q"], d["k"], d["positions"], freqs, stream=s)
-            K.add_rmsnorm(h, d["attn_proj"], d["wf"][l], normed, EPS, stream=s)
+                K.add_rmsnorm(h, d["ffn_out"], d["wa"][l], normed, EPS, stream=st)
+            K.rope(d["q"], d["k"], d["positions"], freqs, stream=st)
+            K.add_rmsnorm(h, d["attn_proj"], d["wf"][l], normed, EPS, stream=st)
             if silu_events is not None:
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                K.silu_mul(d["mid"], d["gate"], d["up"], stream=s)
-                e1.record(stream)
-                silu_events.append((e0, e1))
+                silu_events[l][0].record()
+                K.silu_mul(d["mid"], d["gate"], d["up"], stream=st)
+                silu_events[l][1].record()
             else:
-                K.silu_mul(d["mid"], d["gate"], d["up"], stream=s)
-        K.add_rmsnorm(h, d["ffn_out"], d["wf"][LAYERS], normed, EPS, stream=s)
+                K.silu_mul(d["mid"], d["gate"], d["up"], stream=st)
+        K.add_rmsnorm(h, d["ffn_out"], d["wf"][LAYERS], normed, EPS, stream=st)
+
+    def capture(d):
+        """One step captured as a CUDA graph (its 130 launches replay with no host work between
+        them), with external timing events around each silu_mul launch that record on every
+        replay."""
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            step(d, side.cuda_stream)  # one eager pass on the capture stream before capture
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        ev = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+              for _ in range(LAYERS)]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            step(d, side.cuda_stream, ev)
+        return g, ev
 
     def timed_chain(d, clocks=None):
-        """W untimed steps, then K steps between events, barrier + sync on both sides; the
-        max over ranks of the elapsed time, and this rank's silu_mul launch times."""
-        for _ in range(args.warmup):
-            step(d)
-        torch.cuda.synchronize(dev)
-        barrier()
-        torch.cuda.synchronize(dev)
-        if clocks:
-            clocks.start()
-            time.sleep(0.3)
-        silu_events = []
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        for _ in range(args.steps):
-            step(d, silu_events)
-        t1.record(stream)
-        torch.cuda.synchronize(dev)
-        clock = clocks.stop() if clocks else None
-        barrier()
-        torch.cuda.synchronize(dev)
-        ms = shards.max_over_ranks(t0.elapsed_time(t1), dev)
-        return ms, [a.elapsed_time(b) for a, b in silu_events], clock
+        """W untimed steps, then K steps between events, barrier + sync on both sides; the max over
+        ranks of the elapsed time and the silu_mul launch times of the last timed step. A step is
+        one replay of the captured graph; the same K steps launched one kernel at a time from the
+        host (eager) are timed after it for comparison."""
+        g, ev = capture(d)
+
+        def run(fn, clk=None):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize(dev)
+            barrier()
+            torch.cuda.synchronize(dev)
+            if clk:
+                clk.start()
+                time.sleep(0.3)
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            t1.record(stream)
+            torch.cuda.synchronize(dev)
+            clock = clk.stop() if clk else None
+            barrier()
+            torch.cuda.synchronize(dev)
+            return shards.max_over_ranks(t0.elapsed_time(t1), dev), clock
+
+        ms, clock = run(g.replay, clocks)
+        silu = [a.elapsed_time(b) for a, b in ev]
+        del g
+        ms_eager, _ = run(lambda: step(d, s))
+        return ms, silu, clock, ms_eager
 
     # Headline: the configured job of 16 x 2048 tokens, its sequences split over the ranks
     # (strong scaling: 16/N sequences per GPU, no collective on the data path).
@@ -224,7 +252,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     T = d["T"]
     by = step_bytes(T)
     clocks = Clocks(local_rank)
-    elapsed_ms, silu_ms, clock = timed_chain(d, clocks)
+    elapsed_ms, silu_ms, clock, eager_ms = timed_chain(d, clocks)
 
     # ── e2e through the reference-facing backend API (host buffers) ──
     be = CudaBackend(local_rank)
@@ -276,7 +304,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     weak = None
     if world > 1:
         dw = chain_data(N_SEQ)
-        ms_w, _, _ = timed_chain(dw)
+        ms_w, _, _, _ = timed_chain(dw)
         del dw
         ms_step_w = ms_w / args.steps
         weak = {"tokens_per_gpu": T_SEQ * N_SEQ, "ms_per_step": round(ms_step_w, 4),
@@ -333,6 +361,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                         "host token ids + positions uploaded each step, last-token rows read back"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clock,
+        "timing": "a step is one replay of the step's 130 launches captured as one CUDA graph; the silu_mul times "
+                  "come from external events inside the graph (last timed step, 32 launches)",
+        "eager": {"ms_per_step": round(eager_ms / args.steps, 4),
+                  "value": round(T_SEQ * N_SEQ / (eager_ms / args.steps / 1e3), 1), "unit": "tokens/s",
+                  "note": "the same K steps launched one kernel at a time from the host"},
     }
     if weak is not None:
         res["weak_scaling"] = weak
