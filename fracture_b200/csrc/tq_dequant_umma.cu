@@ -18,8 +18,9 @@
 //                per lookup)
 //   warps 17-24  epilogue, two warpgroups taking tiles in turn: one thread per vector scales
 //                its accumulator row (one of four TMEM accumulators) by the stored fp16
-//                norm, converts, stages the tile in its warpgroup's swizzled staging tile,
-//                and one thread writes it out with two TMA tensor stores
+//                norm, converts, and stages it in its warp's swizzled staging area, one
+//                64-column half of the warp's 32 rows at a time, each half written with one
+//                TMA tensor store
 //   warp 25      producer (staged calls): copies each tile's packed codes and norms into a
 //                ring of shared-memory stages with bulk asynchronous copies, three tiles
 //                ahead of the decoders
@@ -54,9 +55,11 @@ namespace dq {
 
 using namespace sm100;
 
-constexpr int A_STAGES = 2;  // decoded A tiles in flight
+constexpr int A_STAGES = 3;  // decoded A tiles in flight
 constexpr int NACC = 4;      // TMEM accumulators (4 x 128 columns: all of TMEM)
-constexpr int STG = 2;       // output staging tiles (one per epilogue warpgroup)
+constexpr int STG = 2;       // output staging areas (one per epilogue warpgroup)
+constexpr int STG_WARP = 32 * 128;        // a warp's staging: 32 rows x 64 columns (one half), SW128
+constexpr int STG_BYTES = 4 * STG_WARP;   // a warpgroup's staging area
 constexpr int CSTAGES = 3;   // code stages of a staged call (tiles the producer runs ahead)
 constexpr int DEC_WARPS = 16;
 constexpr int TPR = DEC_WARPS * 32 / TILE;  // decoder threads per vector
@@ -76,8 +79,6 @@ struct Misc {
     uint64_t a_empty[A_STAGES];
     uint64_t tfull[NACC];
     uint64_t tempty[NACC];
-    uint64_t st_free[STG];  // staging tile may be overwritten (its last TMA store has read it)
-    uint64_t st_full[STG];  // staging tile written by all four warps of the warpgroup
     uint64_t pi_full;        // Pi (fp32) copied into the staging area for the set-up
     uint64_t code_full[CSTAGES];   // a tile's codes and norms have landed in the code stage
     uint64_t code_empty[CSTAGES];  // every decoder warp has read the code stage
@@ -103,8 +104,8 @@ struct Smem {
     static constexpr int P = D * BITS / 8;                            // packed bytes per vector
     static constexpr int b_off = 0;                                   // Pi^T, fp16, SW128
     static constexpr int a_off = TILE_BYTES;                          // A_STAGES decoded tiles
-    static constexpr int st_off = a_off + A_STAGES * TILE_BYTES;      // STG output staging tiles
-    static constexpr int tab_off = st_off + STG * TILE_BYTES;
+    static constexpr int st_off = a_off + A_STAGES * TILE_BYTES;      // STG output staging areas
+    static constexpr int tab_off = st_off + STG * STG_BYTES;
     static constexpr int code_off = tab_off + Table<BITS>::bytes;     // CSTAGES x (codes, norms)
     static constexpr int code_stage = TILE * P + TILE * 2;
     static constexpr int misc_off = code_off + CSTAGES * code_stage;
@@ -202,10 +203,6 @@ __device__ __forceinline__ void dequant_cta(const CUtensorMap* omap, const DqJob
             mbar_init(&misc->tfull[b], 1);
             mbar_init(&misc->tempty[b], 4);
         }
-        for (int b = 0; b < STG; ++b) {
-            mbar_init(&misc->st_free[b], 1);
-            mbar_init(&misc->st_full[b], 4);
-        }
         for (int c = 0; c < CSTAGES; ++c) {
             mbar_init(&misc->code_full[c], 1);
             mbar_init(&misc->code_empty[c], DEC_WARPS);
@@ -213,42 +210,48 @@ __device__ __forceinline__ void dequant_cta(const CUtensorMap* omap, const DqJob
         mbar_init(&misc->pi_full, 1);
         for (int k = 0; k < NORM_BUF; ++k) mbar_init(&misc->norm_full[k], DEC_WARPS);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        // Pi (64 KB fp32) lands in the output staging area, which is free until the first tile
+        // Pi (64 KB fp32) lands in the A stages, which are free until the first tile
         mbar_expect_tx(&misc->pi_full, D * D * 4);
-        bulk_load(sST, a.rotation, D * D * 4, &misc->pi_full);
+        bulk_load(sA, a.rotation, D * D * 4, &misc->pi_full);
     }
     if (threadIdx.x < nlev) misc->cen[threadIdx.x] = __ldg(a.centroids + threadIdx.x);
     __syncthreads();
-    // Decode tables (codes in MSB-first order: the first code of a byte is its high bits).
-    for (int e = threadIdx.x; e < TB::entries * TB::copies; e += THREADS) {
-        const int ent = e / TB::copies;
-        const float* cen = misc->cen;
-        if constexpr (BITS == 4) {
-            ((uint32_t*)tab)[e] = h2_bits(__floats2half2_rn(cen[ent >> 4], cen[ent & 15]));
-        } else if constexpr (BITS == 3) {
-            ((uint32_t*)tab)[e] = h2_bits(__floats2half2_rn(cen[ent >> 3], cen[ent & 7]));
-        } else {
-            const __half2 h0 = __floats2half2_rn(cen[ent >> 6], cen[(ent >> 4) & 3]);
-            const __half2 h1 = __floats2half2_rn(cen[(ent >> 2) & 3], cen[ent & 3]);
-            ((uint2*)tab)[e] = make_uint2(h2_bits(h0), h2_bits(h1));
+    // In staged calls the producer warp (the last warp) starts copying codes right away, while
+    // the other warps build the tables and the B operand and meet on named barrier 1.
+    constexpr int PRO_THREADS = STAGED ? THREADS - 32 : THREADS;
+    if (!STAGED || warp != PROD_WARP) {
+        // Decode tables (codes in MSB-first order: the first code of a byte is its high bits).
+        for (int e = threadIdx.x; e < TB::entries * TB::copies; e += PRO_THREADS) {
+            const int ent = e / TB::copies;
+            const float* cen = misc->cen;
+            if constexpr (BITS == 4) {
+                ((uint32_t*)tab)[e] = h2_bits(__floats2half2_rn(cen[ent >> 4], cen[ent & 15]));
+            } else if constexpr (BITS == 3) {
+                ((uint32_t*)tab)[e] = h2_bits(__floats2half2_rn(cen[ent >> 3], cen[ent & 7]));
+            } else {
+                const __half2 h0 = __floats2half2_rn(cen[ent >> 6], cen[(ent >> 4) & 3]);
+                const __half2 h1 = __floats2half2_rn(cen[(ent >> 2) & 3], cen[ent & 3]);
+                ((uint2*)tab)[e] = make_uint2(h2_bits(h0), h2_bits(h1));
+            }
         }
-    }
-    // B operand: B[i][j] = Pi[j][i] in fp16 (K-major: the contraction index j is contiguous);
-    // item (i, j0) packs Pi[j0..j0+7][i] into one 16-byte chunk.
-    mbar_wait(&misc->pi_full, 0);  // a timeout is counted (B would then be garbage)
-    {
-        const float* pis = (const float*)sST;
-        for (int it = threadIdx.x; it < D * D / 8; it += THREADS) {
-            const int i = it & (D - 1), j0 = (it >> 7) * 8;
-            uint32_t o[4];
+        // B operand: B[i][j] = Pi[j][i] in fp16 (K-major: the contraction index j is contiguous);
+        // item (i, j0) packs Pi[j0..j0+7][i] into one 16-byte chunk.
+        mbar_wait(&misc->pi_full, 0);  // a timeout is counted (B would then be garbage)
+        {
+            const float* pis = (const float*)sA;
+            for (int it = threadIdx.x; it < D * D / 8; it += PRO_THREADS) {
+                const int i = it & (D - 1), j0 = (it >> 7) * 8;
+                uint32_t o[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                o[k] = h2_bits(__floats2half2_rn(pis[(j0 + 2 * k) * D + i], pis[(j0 + 2 * k + 1) * D + i]));
-            *(uint4*)(sB + sw128_offset(i, j0)) = make_uint4(o[0], o[1], o[2], o[3]);
+                for (int k = 0; k < 4; ++k)
+                    o[k] = h2_bits(__floats2half2_rn(pis[(j0 + 2 * k) * D + i], pis[(j0 + 2 * k + 1) * D + i]));
+                *(uint4*)(sB + sw128_offset(i, j0)) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
         }
+        fence_async_smem();
+        if constexpr (STAGED) asm volatile("bar.sync 1, %0;" ::"r"(PRO_THREADS) : "memory");
+        else __syncthreads();
     }
-    fence_async_smem();
-    __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = misc->tmem_base;
 
@@ -464,33 +467,33 @@ __device__ __forceinline__ void dequant_cta(const CUtensorMap* omap, const DqJob
             }
         }
     } else if (warp < PROD_WARP) {
-        // ── epilogue: warpgroup e takes the tiles i with i % EPI_WGS == e (accumulator i % NACC)
-        // and stages them in its own staging tile for two TMA tensor stores ──
-        static_assert(EPI_WGS == STG, "one warpgroup per staging tile");
+        // ── epilogue: warpgroup e takes the tiles i with i % EPI_WGS == e (accumulator i % NACC).
+        // Each warp stages its own 32 rows one 64-column half at a time in its own 4 KB of the
+        // warpgroup's staging area and writes the half with one TMA tensor store; before it stages
+        // the next half its lane 0 waits until that store has read the area. No barrier joins the
+        // four warps. ──
         const int e = (warp - 1 - DEC_WARPS) >> 2;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
-        const bool leader = ((warp - 1 - DEC_WARPS) & 3) == 0 && lane == 0;
-        uint8_t* st = sST + e * TILE_BYTES;
-        for (int i = e, n = 0; i < ntiles_cta; i += EPI_WGS, ++n) {
+        // 4 KB-aligned, so the SW128 pattern of the 32 x 64 box follows (lane & 7) = (row & 7)
+        uint8_t* st_w = sST + e * STG_BYTES + quarter * STG_WARP;
+        for (int i = e; i < ntiles_cta; i += EPI_WGS) {
             const int tile = cta + i * ncta;
-            if (leader) {
-                // the store that last read this staging tile is done with it
-                bulk_wait_read_all();
-                mbar_arrive(&misc->st_free[e]);
-            }
             const int acc = i % NACC;
             if (!mbar_wait(&misc->tfull[acc], (i / NACC) & 1)) break;
-            if (!mbar_wait(&misc->st_free[e], n & 1)) break;
             tc_fence_after();
             if (!mbar_wait(&misc->norm_full[i % NORM_BUF], (i / NORM_BUF) & 1)) break;
             const float nrm = misc->norm[i % NORM_BUF][row];
             const uint32_t taddr = tmem_base + (uint32_t)(acc * D) + ((uint32_t)(quarter * 32) << 16);
-            // 16-column chunks, the next two loads in flight while the current chunk is stored
-            constexpr int NBE = 3;  // load buffers
+            // the first of this warp's rows exists (the last tile may end inside the warp's rows;
+            // the store box is clipped at the tensor's end, and no store starts past it)
+            const bool has_rows = (int64_t)tile * TILE + quarter * 32 < nvec;
+            // 16-column chunks, the next chunk's load in flight while the current chunk is stored
+            // (tcgen05.wait::ld waits for every load in flight, so a third buffer would hide no more)
+            constexpr int NBE = 2;  // load buffers
             uint32_t vbuf[NBE][16];
-            tmem_ld16_issue(taddr, vbuf[0]);
-            tmem_ld16_issue(taddr + 16, vbuf[1]);
+#pragma unroll
+            for (int h = 0; h < NBE - 1; ++h) tmem_ld16_issue(taddr + 16 * h, vbuf[h]);
 #pragma unroll
             for (int cchunk = 0; cchunk < D / 16; ++cchunk) {
                 uint32_t(&v)[16] = vbuf[cchunk % NBE];
@@ -502,6 +505,11 @@ __device__ __forceinline__ void dequant_cta(const CUtensorMap* omap, const DqJob
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&misc->tempty[acc]);
                 }
+                if ((cchunk & 3) == 0) {
+                    // the store of the previous half has read the staging area
+                    if (lane == 0) bulk_wait_read_all();
+                    __syncwarp();
+                }
 #pragma unroll
                 for (int g = 0; g < 2; ++g) {
                     uint32_t o[4];
@@ -509,20 +517,19 @@ __device__ __forceinline__ void dequant_cta(const CUtensorMap* omap, const DqJob
                     for (int k2 = 0; k2 < 4; ++k2)
                         o[k2] = pack_out<TOut>(__uint_as_float(v[8 * g + 2 * k2]) * nrm,
                                                __uint_as_float(v[8 * g + 2 * k2 + 1]) * nrm);
-                    *(uint4*)(st + sw128_offset(row, 16 * cchunk + 8 * g)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    *(uint4*)(st_w + sw128_offset(lane, (16 * cchunk + 8 * g) & 63)) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+                if ((cchunk & 3) == 3) {
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && has_rows) {
+                        tma_store_2d(omap, st_w, 64 * (cchunk >> 2), tile * TILE + quarter * 32);
+                        bulk_commit();
+                    }
                 }
             }
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&misc->st_full[e]);
-            if (leader) {
-                if (!mbar_wait(&misc->st_full[e], n & 1)) break;
-                tma_store_2d(omap, st, 0, tile * TILE);
-                tma_store_2d(omap, st + KBLK_BYTES, 64, tile * TILE);
-                bulk_commit();
-            }
         }
-        if (leader) bulk_wait_all();
+        if (lane == 0) bulk_wait_all();
     } else if constexpr (STAGED) {
         // ── producer: one lane copies tile i's codes and norms into code stage i % CSTAGES ──
         // A tile is TPT = 128 / H whole tokens (H a multiple of 8 dividing 128), at most two
@@ -668,7 +675,7 @@ static bool encode_output_map(CUtensorMap* map, const TqArgs& a) {
     const int64_t nvec = a.num_tokens * a.num_heads;
     const cuuint64_t dims[2] = {(cuuint64_t)dq::D, (cuuint64_t)nvec};
     const cuuint64_t strides[1] = {(cuuint64_t)dq::D * 2};
-    const cuuint32_t box[2] = {64, (cuuint32_t)dq::TILE};
+    const cuuint32_t box[2] = {64, 32};  // one epilogue warp's rows of one 64-column half
     const cuuint32_t estr[2] = {1, 1};
     return encode(map, a.out_dtype == FB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                   a.output, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
