@@ -515,8 +515,8 @@ def run_config5(args, rank: int, world: int, local_rank: int) -> dict | None:
         for j in range(nl):
             K.add_rmsnorm(h, attn_out[:T], wa[j], normed[:T], EPS)
             K.rope(q[:T], k[:T], pos, freqs)
-            for kv, src in ((0, k), (1, v)):
-                K.tq_compress_slots(src[:T], rots[kv], cen, bits, pools[j][kv][0], pools[j][kv][1], slots)
+            K.tq_compress_kv_slots(k[:T], v[:T], rots[0], rots[1], cen, cen, bits, bits, pools[j][0][0],
+                                   pools[j][0][1], pools[j][1][0], pools[j][1][1], slots)
             K.add_rmsnorm(h, ffn_out[:T], wf[j], normed[:T], EPS)
             K.silu_mul(mid[:T], gate[:T], up[:T])
 

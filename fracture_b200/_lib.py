@@ -68,6 +68,8 @@ SIGNATURES = {
                                             vp, vp, i32, vp]),
     "fb_launch_tq_dequant_paged": (i32, [vp, vp, vp, vp, i32, i64, i32, i32, vp, i64, i64, vp, i32, vp]),
     "fb_launch_tq_compress_slots": (i32, [vp, i32, vp, vp, i32, i64, i32, i32, vp, i64, vp, vp, vp, vp]),
+    "fb_launch_tq_compress_kv_slots": (i32, [vp, vp, i32, vp, vp, vp, vp, i32, i32, i64, i32, i32, vp, i64,
+                                             vp, vp, vp, vp, vp, vp]),
     "fb_launch_tq_dequant_slots": (i32, [vp, vp, vp, vp, i32, i64, i32, i32, vp, i64, vp, i32, vp]),
     "fb_tq_attention_workspace_bytes": (C.c_size_t, [i32, i32, i32, i32]),
     "fb_launch_tq_attention_paged": (i32, [vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, i64, vp, i32, vp, vp,

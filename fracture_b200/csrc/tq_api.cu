@@ -22,7 +22,7 @@ using namespace fb;
 // dequantize small / tensor-core / exact, then K+V compress and K+V dequantize pairs served by one
 // tensor-core launch, then paged attention calls served by the CUDA-core, the per-head
 // tensor-core and the streamed tensor-core kernel (fb_tq_path_counts).
-constexpr int kTqPaths = 11;
+constexpr int kTqPaths = 12;
 static std::atomic<unsigned long long> g_tq_path_calls[kTqPaths];
 
 static int count_path(int which, int rc) {
@@ -96,6 +96,18 @@ static int tq_compress_any(const void* input, int dtype, const float* rotation, 
     return tq_compress_dispatch(a, stream);
 }
 
+// K and V of one append (same tokens, heads and pool rows): small calls take one small-call launch
+// for both, larger ones one tensor-core launch where the widths allow it, else two calls.
+static int tq_compress_kv_dispatch(const TqArgs& k, const TqArgs& v, void* stream) {
+    if (tq_small_compress_call(k)) return count_path(11, tq_compress_small_pair(k, v, (cudaStream_t)stream));
+    bool handled = false;
+    const int rc = tq_compress_umma_pair(k, v, (cudaStream_t)stream, &handled);
+    if (handled) return count_path(6, rc);
+    const int rk = tq_compress_dispatch(k, stream);
+    if (rk) return rk;
+    return tq_compress_dispatch(v, stream);
+}
+
 extern "C" int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotation, const float* centroids,
                                            int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
                                            const int32_t* block_table, int64_t start_pos, int64_t num_pool_rows,
@@ -120,14 +132,26 @@ extern "C" int fb_launch_tq_compress_kv_paged(const void* k_input, const void* v
     rc = tq_compress_args(v_input, dtype, v_rotation, v_centroids, value_bits, num_tokens, num_kv_heads, head_dim,
                           block_table, nullptr, start_pos, num_pool_rows, v_packed_pool, v_norms_pool, err_count, &v);
     if (rc || num_tokens == 0) return rc;
-    if (!tq_small_compress_call(k)) {
-        bool handled = false;
-        rc = tq_compress_umma_pair(k, v, (cudaStream_t)stream, &handled);
-        if (handled) return count_path(6, rc);
-    }
-    rc = tq_compress_dispatch(k, stream);
+    return tq_compress_kv_dispatch(k, v, stream);
+}
+
+// K and V of a batched append through one slot map (one launch for both where they qualify).
+extern "C" int fb_launch_tq_compress_kv_slots(const void* k_input, const void* v_input, int dtype,
+                                              const float* k_rotation, const float* v_rotation,
+                                              const float* k_centroids, const float* v_centroids, int key_bits,
+                                              int value_bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                                              const int64_t* slot_map, int64_t num_pool_rows, void* k_packed_pool,
+                                              void* k_norms_pool, void* v_packed_pool, void* v_norms_pool,
+                                              unsigned int* err_count, void* stream) {
+    if (!slot_map && num_tokens > 0) return (int)cudaErrorInvalidValue;
+    TqArgs k, v;
+    int rc = tq_compress_args(k_input, dtype, k_rotation, k_centroids, key_bits, num_tokens, num_kv_heads, head_dim,
+                              nullptr, slot_map, 0, num_pool_rows, k_packed_pool, k_norms_pool, err_count, &k);
     if (rc) return rc;
-    return tq_compress_dispatch(v, stream);
+    rc = tq_compress_args(v_input, dtype, v_rotation, v_centroids, value_bits, num_tokens, num_kv_heads, head_dim,
+                          nullptr, slot_map, 0, num_pool_rows, v_packed_pool, v_norms_pool, err_count, &v);
+    if (rc || num_tokens == 0) return rc;
+    return tq_compress_kv_dispatch(k, v, stream);
 }
 
 // Batched append: token t of the call goes to pool row slot_map[t] (negative or out of range:

@@ -108,6 +108,7 @@ int tq_dequant_exact(const TqArgs& a, cudaStream_t s);
 bool tq_small_compress_call(const TqArgs& a);
 bool tq_small_dequant_call(const TqArgs& a);
 int tq_compress_small(const TqArgs& a, cudaStream_t s);
+int tq_compress_small_pair(const TqArgs& k, const TqArgs& v, cudaStream_t s);
 int tq_dequant_small(const TqArgs& a, cudaStream_t s);
 
 }  // namespace fb

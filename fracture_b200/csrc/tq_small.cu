@@ -67,10 +67,21 @@ __device__ __forceinline__ float norm_seq(const float* x, int d) {
     return __fsqrt_rn(s);
 }
 
+// One launch serves one compress call, or two (the K and V of an append, equal in vector count
+// and head_dim): CTAs [0, nblk0) take job 0, the rest job 1.
+struct SmallJobs {
+    TqArgs a[2];
+    unsigned nblk0;
+    int njobs;
+};
+
 template <int V>
-__global__ void __launch_bounds__(256) tq_compress_small_kernel(TqArgs a) {
+__global__ void __launch_bounds__(256) tq_compress_small_kernel(const __grid_constant__ SmallJobs J) {
     pdl_begin();
     extern __shared__ __align__(16) float sm[];
+    const int jb = (J.njobs > 1 && blockIdx.x >= J.nblk0) ? 1 : 0;
+    const TqArgs& a = J.a[jb];
+    const int64_t blk = (int64_t)blockIdx.x - (jb ? (int64_t)J.nblk0 : 0);
     const int d = a.head_dim, ld = d + 4, i = threadIdx.x;
     float* pis = sm;                 // pis[r * ld + j] = Pi[r][j]
     float* xs = pis + d * ld;        // [V][d]: x, then x / (norm + 1e-8)
@@ -79,7 +90,7 @@ __global__ void __launch_bounds__(256) tq_compress_small_kernel(TqArgs a) {
     long long* prow_s = (long long*)(((uintptr_t)(den + V) + 7) & ~(uintptr_t)7);  // [V]
     uint8_t* idx = (uint8_t*)(prow_s + V);  // [V][d]
     const int64_t nvec = a.num_tokens * a.num_heads;
-    const int64_t v0 = (int64_t)blockIdx.x * V;
+    const int64_t v0 = blk * V;
     const int nv = (int)std::min<int64_t>(V, nvec - v0);
 
     stage_pi(pis, a.rotation, d);  // in flight while the norms are summed
@@ -226,13 +237,44 @@ bool tq_small_dequant_call(const TqArgs& a) {
     return a.head_dim <= 192 && a.num_tokens * a.num_heads <= kTqSmallDequantVectors;
 }
 
-int tq_compress_small(const TqArgs& a, cudaStream_t s) {
-    if (a.num_tokens * a.num_heads == 0) return 0;
-    const int V = small_v(a.num_tokens * a.num_heads);
-    if (V == 1) return launch_small(tq_compress_small_kernel<1>, a, 1, s);
-    if (V == 2) return launch_small(tq_compress_small_kernel<2>, a, 2, s);
-    if (V == 4) return launch_small(tq_compress_small_kernel<4>, a, 4, s);
-    return launch_small(tq_compress_small_kernel<8>, a, 8, s);
+// jobs[0..njobs) (njobs 1 or 2, equal head_dim) in one launch of V-vector CTAs.
+template <int V>
+int launch_compress_small(const TqArgs* jobs, int njobs, cudaStream_t s) {
+    SmallJobs J{};
+    int64_t blocks = 0;
+    for (int j = 0; j < njobs; ++j) {
+        J.a[j] = jobs[j];
+        const int64_t nb = (jobs[j].num_tokens * jobs[j].num_heads + V - 1) / V;
+        if (j == 0) J.nblk0 = (unsigned)nb;
+        blocks += nb;
+    }
+    J.njobs = njobs;
+    if (blocks == 0) return 0;
+    auto kern = tq_compress_small_kernel<V>;
+    const size_t smem = small_smem(jobs[0].head_dim, V);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    launch_pdl_smem(kern, dim3((unsigned)blocks), dim3(small_threads(jobs[0].head_dim)), smem, s, J);
+    return (int)cudaGetLastError();
+}
+
+int compress_small_jobs(const TqArgs* jobs, int njobs, cudaStream_t s) {
+    int64_t nvec = 0;
+    for (int j = 0; j < njobs; ++j) nvec += jobs[j].num_tokens * jobs[j].num_heads;
+    if (nvec == 0) return 0;
+    const int V = small_v(nvec);
+    if (V == 1) return launch_compress_small<1>(jobs, njobs, s);
+    if (V == 2) return launch_compress_small<2>(jobs, njobs, s);
+    if (V == 4) return launch_compress_small<4>(jobs, njobs, s);
+    return launch_compress_small<8>(jobs, njobs, s);
+}
+
+int tq_compress_small(const TqArgs& a, cudaStream_t s) { return compress_small_jobs(&a, 1, s); }
+
+// The K and V of one append (the same tokens and head layout) in one launch.
+int tq_compress_small_pair(const TqArgs& k, const TqArgs& v, cudaStream_t s) {
+    const TqArgs jobs[2] = {k, v};
+    return compress_small_jobs(jobs, 2, s);
 }
 
 int tq_dequant_small(const TqArgs& a, cudaStream_t s) {

@@ -123,6 +123,19 @@ def tq_compress_slots(x, rotation, centroids, bits, packed_pool, norms_pool, slo
         "tq_compress_slots")
 
 
+def tq_compress_kv_slots(k, v, k_rotation, v_rotation, k_centroids, v_centroids, key_bits, value_bits, k_pool,
+                         k_norms, v_pool, v_norms, slot_map, err=None, stream=None):
+    """K and V of one batched append (``[T, H, d]`` each) through one slot map, one launch where both qualify."""
+    T, H, d = k.shape
+    assert v.shape == k.shape and v.dtype == k.dtype and v_norms.shape[0] == k_norms.shape[0]
+    rows = k_norms.shape[0]
+    _ok(_lib.load().fb_launch_tq_compress_kv_slots(
+        k.data_ptr(), v.data_ptr(), _dt(k), k_rotation.data_ptr(), v_rotation.data_ptr(), k_centroids.data_ptr(),
+        v_centroids.data_ptr(), key_bits, value_bits, T, H, d, slot_map.data_ptr(), rows, k_pool.data_ptr(),
+        k_norms.data_ptr(), v_pool.data_ptr(), v_norms.data_ptr(), err.data_ptr() if err is not None else None,
+        _stream(stream)), "tq_compress_kv_slots")
+
+
 def tq_dequant_slots(packed_pool, norms_pool, rotation, centroids, bits, out, slot_map, stream=None):
     """Gather: ``out[t]`` dequantized from pool row ``slot_map[t]`` (int64 tensor)."""
     T, H, d = out.shape
@@ -134,7 +147,7 @@ def tq_dequant_slots(packed_pool, norms_pool, rotation, centroids, bits, out, sl
 
 TQ_PATHS = ("compress_small", "compress_tensor_core", "compress_exact", "dequant_small", "dequant_tensor_core",
             "dequant_exact", "compress_kv_fused", "dequant_kv_fused", "attention_cuda_core", "attention_per_head",
-            "attention_streamed")
+            "attention_streamed", "compress_kv_small")
 
 
 def tq_path_counts() -> dict:

@@ -191,8 +191,10 @@ int fb_launch_tq_compress_paged(const void* input, int dtype, const float* rotat
  * quantized_paged_kv_cache.rs:417-438): fb_launch_tq_compress_paged for the keys (k_*, key_bits)
  * and for the values (v_*, value_bits), same tokens, block table and pool rows. Where both take
  * the tensor-core kernel (head_dim 128, FP16 or BF16, 2/3/4-bit codes of equal width, or 4-bit
- * keys with 2-bit values) they run as one launch whose grid is split between K and V; otherwise
- * as two calls. Results equal the two separate calls bit for bit. */
+ * keys with 2-bit values) they run as one launch whose grid is split between K and V; calls small
+ * enough for the small-call kernel (decode steps: at most 1024 head vectors each) also run as one
+ * launch of that kernel for both; otherwise as two calls. Results equal the two separate calls bit
+ * for bit. */
 int fb_launch_tq_compress_kv_paged(const void* k_input, const void* v_input, int dtype, const float* k_rotation,
                                    const float* v_rotation, const float* k_centroids, const float* v_centroids,
                                    int key_bits, int value_bits, int64_t num_tokens, int num_kv_heads, int head_dim,
@@ -207,7 +209,8 @@ int fb_launch_tq_compress_kv_paged(const void* k_input, const void* v_input, int
  * fb_launch_tq_compress_kv_paged served by one tensor-core launch; counts[7] the same for
  * fb_launch_tq_dequant_kv_paged; counts[8..10] = paged-attention calls (every TurboQuant attention
  * entry point) whose main kernel was the CUDA-core one, the per-head tensor-core one and the
- * streamed tensor-core one. Writes min(n, 11) counters. */
+ * streamed tensor-core one; counts[11] = K+V pairs of fb_launch_tq_compress_kv_paged or
+ * fb_launch_tq_compress_kv_slots served by one small-call launch. Writes min(n, 12) counters. */
 int fb_tq_path_counts(unsigned long long* counts, int n);
 
 /* Batched append (no reference counterpart; the reference appends one sequence at a time,
@@ -219,6 +222,18 @@ int fb_launch_tq_compress_slots(const void* input, int dtype, const float* rotat
                                 int bits, int64_t num_tokens, int num_kv_heads, int head_dim,
                                 const int64_t* slot_map, int64_t num_pool_rows, void* packed_pool,
                                 void* norms_pool, unsigned int* err_count, void* stream);
+
+/* K and V of one batched append in one call (no reference counterpart; the reference compresses K
+ * and V separately, quantized_paged_kv_cache.rs:417-438): fb_launch_tq_compress_slots for the keys
+ * (k_*, key_bits) and for the values (v_*, value_bits) through the same slot map, with the launch
+ * sharing of fb_launch_tq_compress_kv_paged (one small-call launch for both at decode sizes, one
+ * tensor-core launch where both qualify). Results equal the two separate calls bit for bit. */
+int fb_launch_tq_compress_kv_slots(const void* k_input, const void* v_input, int dtype, const float* k_rotation,
+                                   const float* v_rotation, const float* k_centroids, const float* v_centroids,
+                                   int key_bits, int value_bits, int64_t num_tokens, int num_kv_heads, int head_dim,
+                                   const int64_t* slot_map, int64_t num_pool_rows, void* k_packed_pool,
+                                   void* k_norms_pool, void* v_packed_pool, void* v_norms_pool,
+                                   unsigned int* err_count, void* stream);
 
 /* TurboQuant dequantize from a paged pool into [num_tokens, Hkv, d] (`dtype` FP16/BF16/FP32):
  * x = (Pi^T @ centroids[idx]) * norm (replaces turboquant_decompress.cu:21-94). Same slot rule; a

@@ -177,6 +177,63 @@ def test_small_call_compress_bit_exact(dt, T, H, d, bits):
     assert err.item() == int((~have).sum()) * H
 
 
+@pytest.mark.parametrize("entry", ["paged", "slots"])
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("T,H,d,kb,vb", [(1, 8, 128, 4, 2), (32, 8, 128, 4, 4), (128, 8, 128, 4, 2),
+                                         (77, 8, 128, 3, 3), (9, 3, 64, 8, 2), (5, 3, 33, 2, 4)])
+def test_small_call_compress_kv_one_launch(entry, dt, T, H, d, kb, vb):
+    """K and V of a decode-sized append in one small-call launch (its CTAs split between K and V,
+    the vectors per CTA chosen from both calls' vectors; 128 x 8 is 1024 vectors each, the
+    small-call limit), through the block-table entry point (unaligned start) and the slot-map one
+    (one token without a pool row): pool bytes and norms bit-exact against the oracle, rows not
+    written left as they were, the skipped token counted once per head vector of K and of V, and
+    one launch counted for the pair."""
+    xk, rk = make_input(T, H, d, dt, seed=1300 + T * H + d)
+    xv, rv = make_input(T, H, d, dt, seed=1301 + T * H + d)
+    pik, ck = tables(d, kb, 42)
+    piv, cv = tables(d, vb, 542)
+    rng = np.random.default_rng(T + d)
+    start = 3
+    nblk = (start + T + 15) // 16 + 2
+    rows = nblk * 16
+    if entry == "paged":
+        table = rng.permutation(nblk).astype(np.int32)
+        pos = start + np.arange(T)
+        slots = (table[pos // 16] * 16 + pos % 16).astype(np.int64)
+    else:
+        slots = rng.permutation(rows)[:T].astype(np.int64)
+        if T > 4:
+            slots[T // 2] = -1
+    have = slots >= 0
+    pools = []
+    for b in (kb, vb):
+        P = (d * b + 7) // 8
+        pools.append((torch.full((rows, H * P), 0xAB, dtype=torch.uint8, device=DEV),
+                      torch.full((rows, H), 0x5555, dtype=torch.int16, device=DEV)))
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    args = (dev(xk, dt), dev(xv, dt), torch.from_numpy(pik).to(DEV), torch.from_numpy(piv).to(DEV),
+            torch.from_numpy(ck).to(DEV), torch.from_numpy(cv).to(DEV), kb, vb, pools[0][0], pools[0][1],
+            pools[1][0], pools[1][1])
+    before = K.tq_path_counts()
+    if entry == "paged":
+        K.tq_compress_kv_paged(*args, block_table=torch.from_numpy(table).to(DEV), start_pos=start, err=err)
+    else:
+        K.tq_compress_kv_slots(*args, torch.from_numpy(slots).to(DEV), err=err)
+    torch.cuda.synchronize()
+    after = K.tq_path_counts()
+    assert after["compress_kv_small"] - before["compress_kv_small"] == 1, (before, after)
+    assert after["compress_small"] == before["compress_small"], (before, after)
+    assert err.item() == int((~have).sum()) * H * 2
+    for (packed, norms), raw, pi, c, b in ((pools[0], rk, pik, ck, kb), (pools[1], rv, piv, cv, vb)):
+        pc, nc, _ = tq.compress_c(raw, KIND[dt], pi, c, b)
+        exp_p = np.full((rows, H * ((d * b + 7) // 8)), 0xAB, np.uint8)
+        exp_n = np.full((rows, H), 0x5555, np.uint16)
+        exp_p[slots[have]] = pc[have]
+        exp_n[slots[have]] = nc[have]
+        assert np.array_equal(packed.cpu().numpy(), exp_p), f"{b}-bit codes"
+        assert np.array_equal(norms.cpu().numpy().view(np.uint16), exp_n), f"{b}-bit norms"
+
+
 @pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
 @pytest.mark.parametrize("T,H,d,bits", [(1, 8, 128, 4), (24, 8, 128, 4), (19, 3, 64, 3), (7, 3, 33, 2)])
 def test_small_call_dequant_bit_exact(dt, T, H, d, bits):
