@@ -75,7 +75,9 @@ struct SmallJobs {
     int njobs;
 };
 
-template <int V>
+// NH = 2 splits the CTA's vectors between two halves of the threads (each half one thread per
+// coordinate), so that a CTA runs twice the warps on the sequential sums.
+template <int V, int NH>
 __global__ void __launch_bounds__(256) tq_compress_small_kernel(const __grid_constant__ SmallJobs J) {
     pdl_begin();
     extern __shared__ __align__(16) float sm[];
@@ -113,19 +115,22 @@ __global__ void __launch_bounds__(256) tq_compress_small_kernel(const __grid_con
     __syncthreads();
     for (int e = i; e < nv * d; e += blockDim.x) xs[e] = __fdiv_rn(xs[e], den[e / d]);
     __syncthreads();
-    if (i < d) {
-        float acc[V];
+    constexpr int VH = V / NH;  // vectors per thread
+    const int tph = (int)blockDim.x / NH, half = i / tph, c = i - half * tph;  // coordinate c of half `half`
+    if (c < d) {
+        float acc[VH];
 #pragma unroll
-        for (int v = 0; v < V; ++v) acc[v] = 0.0f;
-        const float* row = pis + i * ld;
+        for (int v = 0; v < VH; ++v) acc[v] = 0.0f;
+        const float* row = pis + c * ld;
+        const float* xh = xs + half * VH * d;
         if ((d & 3) == 0) {
-            // row i four floats at a time (16-byte aligned: ld is a multiple of 4)
+            // row c four floats at a time (16-byte aligned: ld is a multiple of 4)
 #pragma unroll 2
             for (int j = 0; j < d; j += 4) {
                 const float4 p = *(const float4*)(row + j);
 #pragma unroll
-                for (int v = 0; v < V; ++v) {
-                    const float4 x = *(const float4*)(xs + v * d + j);
+                for (int v = 0; v < VH; ++v) {
+                    const float4 x = *(const float4*)(xh + v * d + j);
                     acc[v] = __fadd_rn(acc[v], __fmul_rn(p.x, x.x));
                     acc[v] = __fadd_rn(acc[v], __fmul_rn(p.y, x.y));
                     acc[v] = __fadd_rn(acc[v], __fmul_rn(p.z, x.z));
@@ -136,12 +141,14 @@ __global__ void __launch_bounds__(256) tq_compress_small_kernel(const __grid_con
             for (int j = 0; j < d; ++j) {
                 const float p = row[j];
 #pragma unroll
-                for (int v = 0; v < V; ++v) acc[v] = __fadd_rn(acc[v], __fmul_rn(p, xs[v * d + j]));
+                for (int v = 0; v < VH; ++v) acc[v] = __fadd_rn(acc[v], __fmul_rn(p, xh[v * d + j]));
             }
         }
 #pragma unroll
-        for (int v = 0; v < V; ++v)
-            if (v < nv) idx[v * d + i] = (uint8_t)nearest_centroid(acc[v], cen, a.n_levels);
+        for (int v = 0; v < VH; ++v) {
+            const int vv = half * VH + v;
+            if (vv < nv) idx[vv * d + c] = (uint8_t)nearest_centroid(acc[v], cen, a.n_levels);
+        }
     }
     __syncthreads();
     const int P = (d * a.bits + 7) >> 3;
@@ -250,11 +257,15 @@ int launch_compress_small(const TqArgs* jobs, int njobs, cudaStream_t s) {
     }
     J.njobs = njobs;
     if (blocks == 0) return 0;
-    auto kern = tq_compress_small_kernel<V>;
+    // two thread halves (each one thread per coordinate) when the CTA has vectors to split and
+    // room for twice the threads
+    const int th = small_threads(jobs[0].head_dim);
+    const bool split = V >= 2 && 2 * th <= 256;
+    auto kern = split ? tq_compress_small_kernel<V, (V >= 2 ? 2 : 1)> : tq_compress_small_kernel<V, 1>;
     const size_t smem = small_smem(jobs[0].head_dim, V);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (int)e;
-    launch_pdl_smem(kern, dim3((unsigned)blocks), dim3(small_threads(jobs[0].head_dim)), smem, s, J);
+    launch_pdl_smem(kern, dim3((unsigned)blocks), dim3(split ? 2 * th : th), smem, s, J);
     return (int)cudaGetLastError();
 }
 
