@@ -89,6 +89,11 @@ __device__ __forceinline__ void pdl_begin() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// Lets the next programmatic dependent launch on the stream be scheduled before this kernel's CTAs
+// exit (its CTAs then take SMs as they free up and run up to their own pdl_begin()). Used by the
+// TurboQuant attention chain, whose kernels do set-up that needs no predecessor output.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Host-side helpers ----------------------------------------------------------
 
 int num_sms();  // SM count of the current device (cached per device)

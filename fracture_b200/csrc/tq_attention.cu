@@ -94,6 +94,7 @@ inline int rows_per_cta(int rows, int hkv) {
 // words (broadcast); thread i computes coordinate i of all NR * G vectors.
 template <int G, int NR>
 __global__ void __launch_bounds__(D) tqa_rotate_q(const __grid_constant__ RotateParams R) {
+    pdl_trigger();  // the attention kernel's CTAs may start their table set-up meanwhile
     extern __shared__ uint8_t rsm_raw[];
     uint8_t* rsm = rsm_raw + ((1024u - (smem_addr(rsm_raw) & 1023u)) & 1023u);
     float* pis = (float*)rsm;               // 4 x [128 rows][32 columns], swizzled
@@ -156,6 +157,7 @@ __global__ void __launch_bounds__(D) tqa_rotate_q(const __grid_constant__ Rotate
 // head h; its Pi_k row sits in shared memory at a stride of D + 4 floats (the 16-byte reads of
 // a quarter-warp fall in different banks), the head's query is read by the whole warp at once.
 __global__ void __launch_bounds__(8 * 32) tqa_rotate_q_slice(AttnArgs a) {
+    pdl_trigger();  // the attention kernel's CTAs may start their table set-up meanwhile
     __shared__ __align__(16) float pis[32][D + 4];
     __shared__ __align__(16) float qs[MAXG][D];
     const int row = blockIdx.x, g = blockIdx.y, z = blockIdx.z;

@@ -248,6 +248,7 @@ __device__ __forceinline__ Places places(uint32_t base, int sb) {
 // with the 128-byte swizzle.
 template <int KB, int VB, bool PTRS>
 __global__ void __launch_bounds__(Layout<KB, VB>::THREADS, 1) tqa_stream(const __grid_constant__ Params P) {
+    pdl_trigger();  // the combine's CTAs may take SMs this grid has left and stage Pi_v meanwhile
     using Ly = Layout<KB, VB>;
     constexpr int PK = Ly::PK, PV = Ly::PV;
     constexpr int SB = Ly::stage_bytes;
