@@ -82,9 +82,9 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // First statement of a kernel that launch_pdl may start early: waits until the previous kernel
 // on the stream has completed and its writes are visible (a no-op for an ordinary launch). The
-// kernel does not trigger its own dependents early: they are scheduled as its CTAs exit, which
-// measured faster under CUDA-graph replay than an early trigger (0.293 vs 0.368 ms for the
-// 130-launch decode chain).
+// elementwise kernels do not trigger their dependents early: they are scheduled as its CTAs exit,
+// which measured faster under CUDA-graph replay than an early trigger (0.293 vs 0.368 ms for the
+// 130-launch decode chain); the TurboQuant attention chain does (pdl_trigger below).
 __device__ __forceinline__ void pdl_begin() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
