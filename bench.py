@@ -1113,7 +1113,8 @@ def profile_kernel(args) -> None:
                                            cen, 4, 4, outs[0], outs[1], block_table=table)
     elif args.profile_kernel in ("tq_small_compress", "tq_small_dequant"):
         # decode-sized TurboQuant write / read (config 5 decode: the new tokens of a group of 32
-        # sequences, 8 KV heads, into slot-mapped pool rows): 256 vectors compressed, 192 read back
+        # sequences, 8 KV heads, into slot-mapped pool rows): K and V of 256 vectors each compressed
+        # in one launch, 192 vectors read back
         n_tok = 32 if args.profile_kernel == "tq_small_compress" else 24
         rows = 256 * 1152
         rot = torch.from_numpy(K.tq_rotation_matrix(HD, 42)).to(dev)
@@ -1125,7 +1126,10 @@ def profile_kernel(args) -> None:
         K.tq_compress_slots(x, rot, cen, 4, pool, norms, slots)
         out = torch.empty_like(x)
         if args.profile_kernel == "tq_small_compress":
-            fn = lambda: K.tq_compress_slots(x, rot, cen, 4, pool, norms, slots)
+            xv = torch.randn((n_tok, NKV, HD), generator=g, device=dev).to(torch.float16)
+            rot_v = torch.from_numpy(K.tq_rotation_matrix(HD, 542)).to(dev)
+            pool_v, norms_v = torch.zeros_like(pool), torch.zeros_like(norms)
+            fn = lambda: K.tq_compress_kv_slots(x, xv, rot, rot_v, cen, cen, 4, 4, pool, norms, pool_v, norms_v, slots)
         else:
             fn = lambda: K.tq_dequant_slots(pool, norms, rot, cen, 4, out, slots)
     else:
