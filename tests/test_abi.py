@@ -72,6 +72,16 @@ def test_argument_checks_reject_before_launch():
     assert lib.launch_turboquant_compress(None, None, None, None, None, 1, 1, 128, 8, 4, 64, None) == 1
     assert lib.launch_turboquant_decompress(None, None, None, None, None, 1, 1, 128, 6, 96, None) == 1
     assert lib.fb_launch_tq_compress_paged(None, 0, None, None, 4, 4, 8, 256, None, 0, 16, None, None, None, None) == 1
+    # K+V in one call: a slot map is required when there are tokens; widths are checked per side
+    kv = lambda kb, vb, n, slots: lib.fb_launch_tq_compress_kv_slots(None, None, 0, None, None, None, None, kb, vb,
+                                                                     n, 8, 128, slots, 16, None, None, None, None,
+                                                                     None, None)
+    assert kv(4, 4, 4, None) == 1
+    assert kv(4, 5, 4, None) == 1
+    assert kv(4, 2, 0, None) == 0  # empty: nothing to do
+    assert kv(5, 4, 0, None) == 1  # a bad width is rejected even when empty
+    assert lib.fb_launch_tq_compress_kv_paged(None, None, 0, None, None, None, None, 4, 4, 4, 8, 128, None, 0, 16,
+                                              None, None, None, None, None, None) == 1
     # empty inputs are a no-op success
     assert lib.launch_add(None, None, None, 0, None) == 0
     assert lib.fb_launch_tq_compress_paged(None, 0, None, None, 4, 0, 8, 128, None, 0, 0, None, None, None, None) == 0
