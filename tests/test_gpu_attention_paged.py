@@ -172,6 +172,42 @@ def test_chunk_boundaries_and_more_items_than_ctas():
         ops.assert_close_fp(got[s], ref, rel=2e-3, min_cos=0.9999, label=f"seq {s} (kv {L})", dtype="bf16")
 
 
+def _rounds(max_kv_len, hkv, rows, sms):
+    """Rounds of four 16-position tiles per warp and work item that the tensor-core attention
+    kernels pick for a call (tc_chunks): 4, halved while the call's items would fill less than
+    three quarters of a wave of two CTAs per SM."""
+    positions = -(-max_kv_len // 256) * 256
+    rnd = 4
+    while rnd > 1 and -(-positions // (512 * rnd)) * hkv * rows * 4 < 6 * sms:
+        rnd //= 2
+    return rnd
+
+
+def _queries_for_rounds(target, kv_lens, hkv):
+    """A query count per sequence for which this GPU's SM count makes the kernel take `target` rounds."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    for tq in range(1, min(kv_lens) + 1):
+        if _rounds(max(kv_lens), hkv, len(kv_lens) * tq, sms) == target:
+            return tq
+    pytest.skip(f"no query count gives {target} rounds on {sms} SMs")
+
+
+@pytest.mark.parametrize("rnd", [1, 2, 4])
+def test_ragged_contexts_at_every_item_length(rnd):
+    """Ragged contexts around tile and item edges (513, 1040, 1064, 2100 positions), with the query
+    count per sequence chosen from this GPU's SM count so that the tensor-core kernel takes items
+    of 1, 2 and 4 rounds (512, 1024 and 2048 positions): every item length ends in a partial item
+    whose later rounds are empty for some warps."""
+    kv_lens, Hkv, G = [513, 1040, 1064, 2100], 2, 4
+    Tq = _queries_for_rounds(rnd, kv_lens, Hkv)
+    c = build_cache(kv_lens, Hkv, "f16", seed=70 + rnd)
+    qh, q = make_q(len(kv_lens), Tq, G * Hkv, "f16", seed=71 + rnd)
+    starts = [L - Tq for L in kv_lens]
+    got = run_ours(c, q, kv_lens, starts).float().cpu().numpy()
+    for s, L in enumerate(kv_lens):
+        ref = ops.attention_paged(qh[s], c["hk"], c["hv"], c["tables"][s], L, starts[s])
+        ops.assert_close_fp(got[s], ref, rel=2e-3, min_cos=0.9999, label=f"rnd {rnd}, seq {s} (kv {L})", dtype="f16")
+
 def test_unaligned_queries_take_the_cuda_core_kernel():
     """Queries that do not start on a 16-byte boundary go through the CUDA-core kernel (the
     tensor-core kernel reads them 16 bytes at a time); both meet the bar."""

@@ -205,6 +205,44 @@ def test_chunk_boundaries_and_more_items_than_ctas(kb, vb):
                             label=f"seq {s} (kv {L})", dtype="f16")
 
 
+def _rounds(max_kv_len, hkv, rows, sms):
+    """Rounds of four 16-position tiles per warp and work item that the tensor-core attention
+    kernels pick for a call (tc_chunks): 4, halved while the call's items would fill less than
+    three quarters of a wave of two CTAs per SM."""
+    positions = -(-max_kv_len // 256) * 256
+    rnd = 4
+    while rnd > 1 and -(-positions // (512 * rnd)) * hkv * rows * 4 < 6 * sms:
+        rnd //= 2
+    return rnd
+
+
+def _queries_for_rounds(target, kv_lens, hkv):
+    """A query count per sequence for which this GPU's SM count makes the kernel take `target` rounds."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    for tq in range(1, min(kv_lens) + 1):
+        if _rounds(max(kv_lens), hkv, len(kv_lens) * tq, sms) == target:
+            return tq
+    pytest.skip(f"no query count gives {target} rounds on {sms} SMs")
+
+
+@pytest.mark.parametrize("rnd", [1, 2, 4])
+def test_per_head_kernel_ragged_contexts_at_every_item_length(rnd):
+    """The per-head tensor-core kernel (2 KV heads, 4-bit keys, 2-bit values) on ragged contexts
+    (513, 1040, 1064, 2100 positions), with the query count per sequence chosen from this GPU's SM
+    count so that it takes items of 1, 2 and 4 rounds (512, 1024 and 2048 positions): every item
+    length ends in a partial item."""
+    kv_lens, Hkv, G, kb, vb = [513, 1040, 1064, 2100], 2, 4, 4, 2
+    Tq = _queries_for_rounds(rnd, kv_lens, Hkv)
+    c = build_cache(kv_lens, Hkv, kb, vb, seed=80 + rnd)
+    qh, q = make_q(len(kv_lens), Tq, G * Hkv, "f16", seed=81 + rnd)
+    starts = [L - Tq for L in kv_lens]
+    before = K.tq_path_counts()["attention_per_head"]
+    got = run_ours(c, q, kv_lens, starts, "f16").float().cpu().numpy()
+    assert K.tq_path_counts()["attention_per_head"] == before + 1
+    for s, L in enumerate(kv_lens):
+        ops.assert_close_fp(got[s], statement(c, qh[s], s, L, starts[s]), rel=2e-3, min_cos=0.9999,
+                            label=f"rnd {rnd}, seq {s} (kv {L})", dtype="f16")
+
 @pytest.mark.parametrize("kb,vb", [(4, 2), (3, 3)])
 def test_pool_ending_inside_a_block_leaves_the_missing_rows_out(kb, vb):
     """Pools cut 5 rows into the last block the sequence uses: positions whose pool row lies past
