@@ -233,17 +233,6 @@ int launch_small(K kern, const TqArgs& a, int V, cudaStream_t s) {
     return (int)cudaGetLastError();
 }
 
-}  // namespace
-
-// head_dim <= 192 (the entry points' limit): Pi and the vectors fit in shared memory.
-bool tq_small_compress_call(const TqArgs& a) {
-    return a.head_dim <= 192 && a.num_tokens * a.num_heads <= kTqSmallCompressVectors;
-}
-
-bool tq_small_dequant_call(const TqArgs& a) {
-    return a.head_dim <= 192 && a.num_tokens * a.num_heads <= kTqSmallDequantVectors;
-}
-
 // jobs[0..njobs) (njobs 1 or 2, equal head_dim) in one launch of V-vector CTAs.
 template <int V>
 int launch_compress_small(const TqArgs* jobs, int njobs, cudaStream_t s) {
@@ -278,6 +267,17 @@ int compress_small_jobs(const TqArgs* jobs, int njobs, cudaStream_t s) {
     if (V == 2) return launch_compress_small<2>(jobs, njobs, s);
     if (V == 4) return launch_compress_small<4>(jobs, njobs, s);
     return launch_compress_small<8>(jobs, njobs, s);
+}
+
+}  // namespace
+
+// head_dim <= 192 (the entry points' limit): Pi and the vectors fit in shared memory.
+bool tq_small_compress_call(const TqArgs& a) {
+    return a.head_dim <= 192 && a.num_tokens * a.num_heads <= kTqSmallCompressVectors;
+}
+
+bool tq_small_dequant_call(const TqArgs& a) {
+    return a.head_dim <= 192 && a.num_tokens * a.num_heads <= kTqSmallDequantVectors;
 }
 
 int tq_compress_small(const TqArgs& a, cudaStream_t s) { return compress_small_jobs(&a, 1, s); }
