@@ -87,6 +87,18 @@ def test_argument_checks_reject_before_launch():
     assert lib.fb_launch_tq_compress_paged(None, 0, None, None, 4, 0, 8, 128, None, 0, 0, None, None, None, None) == 0
 
 
+def test_path_counters_match_the_python_names():
+    """fb_tq_path_counts fills exactly one counter per name in kernels.TQ_PATHS (a host call, no GPU)."""
+    import ctypes as C
+
+    lib = _lib.load()
+    n = len(K.TQ_PATHS)
+    arr = (C.c_ulonglong * (n + 4))(*([0xDEAD] * (n + 4)))
+    assert lib.fb_tq_path_counts(arr, n + 4) == 0
+    assert all(v != 0xDEAD for v in arr[:n]) and all(v == 0xDEAD for v in arr[n:])
+    assert lib.fb_tq_path_counts(None, n) == 1
+
+
 def test_invalid_table_arguments():
     lib = _lib.load()
     out = np.zeros(64, dtype=np.float32)
