@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -43,7 +44,9 @@ LAYER_FILES = [
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("FRACTURE_REFERENCE", str(HERE.parents[2] / "reference")),
+                    help="the Fracture checkout (default: $FRACTURE_REFERENCE, or a checkout named `reference` "
+                         "beside this repository)")
     ap.add_argument("--out", default=str(HERE))
     args = ap.parse_args()
     ref = Path(args.reference)
