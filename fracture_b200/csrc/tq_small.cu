@@ -6,8 +6,10 @@
 // V vectors (V chosen so the call spreads over the SMs), copies Pi into shared memory with
 // asynchronous 16-byte copies (rows padded to d + 4 floats, so that thread i reading row i
 // four floats at a time, and thread i reading column i, are both free of bank conflicts),
-// and thread i computes coordinate i of all V vectors with the V sequential sums
-// interleaved. Results are the exact statement
+// and thread i computes coordinate i of the CTA's vectors with their sequential sums
+// interleaved (compress: two thread halves with half the vectors each where head_dim allows; a
+// launch may serve the K and V of one append, its CTAs split between them). Results are the
+// exact statement
 // (crates/fracture-core/src/turboquant.rs:1225-1290), like tq_exact.cu, with the same slot
 // rule and error counting.
 
